@@ -1,0 +1,170 @@
+/*
+ * st_b200.h -- C ABI of scratchtape-b200, the B200 (sm_100a) implementation
+ * of scratchtape's matmul family, batched causal attention and 2-bit kNN
+ * scoring.
+ *
+ * Conventions
+ *  - Every call enqueues on the handle's CUDA stream and returns at once; no
+ *    call aborts across the FFI: failures come back as st_status, with text
+ *    from st_last_error().  Device-side waits are bounded; a wait that runs
+ *    out sets a device status word that st_sync() reports as ST_TIMEOUT.
+ *  - Pointers marked "device" are caller-owned device memory.  The library
+ *    owns only its scratch pool (grown on demand, reused afterwards, so a
+ *    call repeated with the same shapes allocates nothing).
+ *  - One handle per host thread; handles are not internally locked.
+ *  - Results are deterministic: no float atomics; split-k partial sums are
+ *    added in a fixed order.
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * the scratchtape crate).
+ */
+#ifndef ST_B200_H
+#define ST_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ST_API __attribute__((visibility("default")))
+#else
+#define ST_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    ST_OK = 0,
+    ST_INVALID_ARG = 1,
+    ST_UNSUPPORTED_SHAPE = 2,
+    ST_CUDA_ERROR = 3,
+    ST_NCCL_ERROR = 4,
+    ST_TIMEOUT = 5,
+    ST_NO_MEMORY = 6,
+    ST_NOT_FOUND = 7
+} st_status;
+
+typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2 } st_dtype;
+
+/* Arithmetic of st_gemm.
+ * F32_EXACT: SIMT, each output a k-ascending sequence of f32 multiply then
+ *            add from 0 -- bit-identical to NdArray::matmul (src/tensor.rs:248-276).
+ * TF32:      tcgen05 kind::tf32 tensor cores, f32 accumulate in TMEM. */
+typedef enum { ST_PREC_F32_EXACT = 0, ST_PREC_TF32 = 1 } st_precision;
+
+typedef struct st_handle st_handle;
+
+/* A matrix inside a device buffer -- mirrors MatRef (src/gpu_step/matmul.rs:31-60).
+ * Matrix z starts at element off + (z / group) * stride + (z % group) * inner
+ * of ptr; its stored rows are ld elements apart (0: packed).  trans: a
+ * logical [r, c] operand stored as [c, r].  stride 0 reuses one matrix for
+ * every batch.  group 0 is read as 1. */
+typedef struct {
+    void *ptr;
+    int64_t off;
+    int64_t stride;
+    int64_t inner;
+    int64_t ld;
+    int32_t group;
+    int32_t trans;
+    int32_t dtype; /* st_dtype; st_gemm takes ST_F32 */
+    int32_t reserved;
+} st_mat;
+
+/* Per-element epilogue in this order -- mirrors Epilogue
+ * (src/gpu_step/matmul.rs:66-79): + bias[bias_off + z*bias_stride + col],
+ * ReLU, zero where mask (out's layout, at mask_off) is not positive,
+ * + residual (out's layout, at residual_off), + the value already in out.
+ * col_sum: also add the column sums of b[z] over k into
+ * col_sum[col_sum_off + z*col_sum_stride + col] (always +=).
+ * Every pointer may be NULL. */
+typedef struct {
+    const float *bias;
+    int64_t bias_off;
+    int64_t bias_stride;
+    const float *mask;
+    int64_t mask_off;
+    const float *residual;
+    int64_t residual_off;
+    float *col_sum;
+    int64_t col_sum_off;
+    int64_t col_sum_stride;
+    int32_t relu;
+    int32_t accumulate;
+} st_epilogue;
+
+/* ---- handle -------------------------------------------------------------- */
+
+/* Creates a handle on CUDA device `device` that enqueues on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream).  Replaces the
+ * cubecl client setup of src/gpu_step/mod.rs:78-97. */
+ST_API st_status st_create(int device, void *stream, st_handle **out);
+ST_API st_status st_destroy(st_handle *h);
+ST_API st_status st_set_stream(st_handle *h, void *stream);
+/* Text of the last failure on this handle (valid until the next call). */
+ST_API const char *st_last_error(const st_handle *h);
+/* Waits for the handle's stream, then reports a device-side status
+ * (ST_TIMEOUT if a bounded wait ran out) and clears it. */
+ST_API st_status st_sync(st_handle *h);
+/* Kernels this library has launched on the handle since creation. */
+ST_API int64_t st_launch_count(const st_handle *h);
+/* Name of the last kernel this handle launched ("" before the first). */
+ST_API const char *st_last_kernel(const st_handle *h);
+/* Bytes currently held by the handle's scratch pool. */
+ST_API int64_t st_scratch_bytes(const st_handle *h);
+
+/* ---- matmul family --------------------------------------------------------- */
+
+/* out[z] (+)= epilogue(a[z] . b[z]) for z < batch, a[z] logically [m, k],
+ * b[z] [k, n], out[z] row-major [m, n] (out->trans must be 0).  NN, NT and
+ * TN come from the operands' trans flags (transpose by descriptor, no
+ * copy).  Replaces gpu_step::matmul::{matmul, matmul_f32, matmul_with}
+ * (src/gpu_step/matmul.rs:86-192) and, with batch > 1, Tape::batched_matmul
+ * (src/tape.rs:73-112).  TF32 needs 16-byte aligned rows (ld*4 % 16 == 0,
+ * 16-byte aligned matrix starts); other layouts run the F32_EXACT kernel. */
+ST_API st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch, int64_t m,
+                  int64_t k, int64_t n, const st_epilogue *epi, st_precision prec);
+
+/* NdArray::matmul with host buffers (src/tensor.rs:241 and the drop-in
+ * gpu_matmul, src/gpu.rs:98-169): out[m, n] = op(a) . op(b), row-major host
+ * f32, ta: a stored [k, m], tb: b stored [n, k].  Copies in, computes,
+ * copies out, and waits.  Device buffers come from the scratch pool. */
+ST_API st_status st_matmul_host(st_handle *h, const float *a, const float *b, float *out, int64_t m, int64_t k, int64_t n,
+                         int32_t ta, int32_t tb, st_precision prec);
+
+/* ---- rows ------------------------------------------------------------------ */
+
+/* Row softmax of scale*x over x [rows, n] (device f32); causal: row r sees
+ * columns 0..=r%t and the rest are exactly 0; one: softmax1 with a phantom
+ * 0 logit, shifted by max(row max, 0).  y may alias x.  Replaces
+ * rows::softmax (src/gpu_step/rows.rs:106-112). */
+ST_API st_status st_softmax_rows(st_handle *h, const float *x, float *y, int64_t rows, int64_t n, int64_t t, float scale,
+                          int32_t causal, int32_t one);
+/* dx = scale * y * (dy - sum(dy*y)) per row (rows.rs:117-123). */
+ST_API st_status st_softmax_rows_bwd(st_handle *h, const float *dy, const float *y, float *dx, int64_t rows, int64_t n,
+                              float scale);
+
+/* ---- fused causal attention ----------------------------------------------- */
+
+/* Flash-style fused attention over bh independent heads, f16 storage with f32
+ * accumulation on tcgen05 (kind::f16).  q, k, v, o: device f16 [bh, t, d]
+ * (head z at z*t*d); lse: device f32 [bh, t] (natural-log sum of exp of the
+ * scaled, masked row, for the backward).  Replaces the chain
+ * batched_matmul(q,k,T) -> scale -> +mask -> softmax -> batched_matmul(w,v)
+ * of TransformerBlock::forward_full (src/nn.rs:657-671) and of
+ * DeviceTape::block_forward (src/gpu_step/tape.rs:481-484).
+ * Shapes: t <= 128, d in {64} for the tensor-core kernel. */
+ST_API st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse, int64_t bh,
+                      int64_t t, int64_t d, float scale, int32_t causal);
+/* Backward: dq, dk, dv (device f16 [bh, t, d]) from q, k, v, o, do (f16) and
+ * lse (f32).  Replaces batched_matmul_backward + the softmax backward
+ * (src/tape.rs:90-112, src/gpu_step/tape.rs:363-375). */
+ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o, const void *dout,
+                      const float *lse, void *dq, void *dk, void *dv, int64_t bh, int64_t t, int64_t d, float scale,
+                      int32_t causal);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ST_B200_H */

@@ -1,0 +1,81 @@
+"""ctypes binding of libst_b200.so (declared in include/st_b200.h).
+
+The library is required: importing this module without the built .so raises
+ImportError with the build command, and there is no fallback path.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libst_b200.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError("scratchtape_b200: native library %s is missing; build it with "
+                      "`python -c 'import __graft_entry__ as g; g.build()'` or `python scratchtape_b200/build.py`"
+                      % LIB_PATH)
+
+lib = ctypes.CDLL(LIB_PATH)
+
+ST_OK, ST_INVALID_ARG, ST_UNSUPPORTED_SHAPE, ST_CUDA_ERROR, ST_NCCL_ERROR, ST_TIMEOUT, ST_NO_MEMORY, ST_NOT_FOUND = \
+    range(8)
+STATUS_NAMES = ["OK", "INVALID_ARG", "UNSUPPORTED_SHAPE", "CUDA_ERROR", "NCCL_ERROR", "TIMEOUT", "NO_MEMORY",
+                "NOT_FOUND"]
+ST_F32, ST_F16, ST_BF16 = 0, 1, 2
+PREC_F32_EXACT, PREC_TF32 = 0, 1
+
+
+class StMat(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("off", ctypes.c_int64), ("stride", ctypes.c_int64),
+                ("inner", ctypes.c_int64), ("ld", ctypes.c_int64), ("group", ctypes.c_int32),
+                ("trans", ctypes.c_int32), ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class StEpilogue(ctypes.Structure):
+    _fields_ = [("bias", ctypes.c_void_p), ("bias_off", ctypes.c_int64), ("bias_stride", ctypes.c_int64),
+                ("mask", ctypes.c_void_p), ("mask_off", ctypes.c_int64), ("residual", ctypes.c_void_p),
+                ("residual_off", ctypes.c_int64), ("col_sum", ctypes.c_void_p), ("col_sum_off", ctypes.c_int64),
+                ("col_sum_stride", ctypes.c_int64), ("relu", ctypes.c_int32), ("accumulate", ctypes.c_int32)]
+
+
+_h = ctypes.c_void_p
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_f32 = ctypes.c_float
+_st = ctypes.c_int
+
+# name -> (restype, argtypes); every name here is declared in include/st_b200.h
+SIGNATURES = {
+    "st_create": (_st, [ctypes.c_int, _vp, ctypes.POINTER(_h)]),
+    "st_destroy": (_st, [_h]),
+    "st_set_stream": (_st, [_h, _vp]),
+    "st_last_error": (ctypes.c_char_p, [_h]),
+    "st_sync": (_st, [_h]),
+    "st_launch_count": (_i64, [_h]),
+    "st_scratch_bytes": (_i64, [_h]),
+    "st_last_kernel": (ctypes.c_char_p, [_h]),
+    "st_gemm": (_st, [_h, ctypes.POINTER(StMat), ctypes.POINTER(StMat), ctypes.POINTER(StMat), _i64, _i64, _i64, _i64,
+                      ctypes.POINTER(StEpilogue), ctypes.c_int]),
+    "st_matmul_host": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_int]),
+    "st_softmax_rows": (_st, [_h, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
+    "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class StError(RuntimeError):
+    def __init__(self, status, text):
+        self.status = status
+        name = STATUS_NAMES[status] if 0 <= status < len(STATUS_NAMES) else str(status)
+        super().__init__("ST_%s: %s" % (name, text))
+
+
+def check(handle_ptr, status):
+    if status != ST_OK:
+        txt = lib.st_last_error(handle_ptr)
+        raise StError(status, txt.decode() if txt else "")
+    return status

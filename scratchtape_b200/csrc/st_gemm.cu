@@ -1,0 +1,483 @@
+// st_gemm.cu -- the matmul family: NN / NT / TN, batched, head views,
+// epilogue, deterministic split-k.
+//
+// Reference: gpu_step::matmul (src/gpu_step/matmul.rs:86-299): MatRef
+// addressing (:31-60), Epilogue (:66-79), split-k summed in a fixed order
+// (:246-299); CPU semantics of NdArray::matmul (src/tensor.rs:248-276).
+//
+// Two kernels:
+//  * k_gemm_tf32: tcgen05 kind::tf32.  One 128 x BN output tile per CTA,
+//    operands streamed by TMA into 128-byte-swizzled shared memory, a
+//    STAGES-deep mbarrier ring, the accumulator in TMEM, one thread issuing
+//    the MMAs.  NT/TN need no transpose: a stored-transposed operand is
+//    loaded as it lies and described to the tensor core as MN-major.
+//  * k_gemm_exact: SIMT, each output a k-ascending chain of f32 multiply then
+//    add starting from 0 (no FMA) -- the same bits as NdArray::matmul.
+#include <algorithm>
+
+#include "st_internal.h"
+#include "st_ptx.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // f32 elements per k block = one 128-byte swizzle row
+
+struct Operand {  // element (z, r, c) of a logical [rows, cols] matrix
+    const float *ptr;
+    int64_t off, stride, inner, ld;
+    int grp, trans;
+};
+
+struct GemmArgs {
+    int M, N, K;
+    int batch, splits, kb_per_split;
+    int a_grp, a_outer, b_grp, b_outer;  // TMA batch coordinates: z%grp (if grp>1), z/grp (if outer)
+    float *c;
+    int64_t c_off, c_stride, c_inner, c_ld;
+    int c_grp;
+    const float *bias;
+    int64_t bias_off, bias_stride;
+    const float *mask;
+    int64_t mask_off;
+    const float *residual;
+    int64_t residual_off;
+    int relu, accumulate;
+    float *partial;  // split-k partials, [batch*splits][M][N]
+    int *status;
+};
+
+__device__ __forceinline__ int64_t out_index(const GemmArgs &g, int z, int row, int col) {
+    return g.c_off + static_cast<int64_t>(z / g.c_grp) * g.c_stride + static_cast<int64_t>(z % g.c_grp) * g.c_inner +
+           static_cast<int64_t>(row) * g.c_ld + col;
+}
+
+// Epilogue order of the reference: + bias, ReLU, mask, + residual, + out.
+// mask and residual share out's layout relative to their own offsets
+// (src/gpu_step/matmul.rs:925-931).
+__device__ __forceinline__ float epilogue(const GemmArgs &g, int z, int64_t oi, int col, float v) {
+    if (g.bias) v = v + g.bias[g.bias_off + static_cast<int64_t>(z) * g.bias_stride + col];
+    if (g.relu) v = fmaxf(v, 0.0f);
+    if (g.mask && !(g.mask[g.mask_off + oi - g.c_off] > 0.0f)) v = 0.0f;
+    if (g.residual) v = v + g.residual[g.residual_off + oi - g.c_off];
+    if (g.accumulate) v = v + g.c[oi];
+    return v;
+}
+
+template <int BN, int STAGES>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 4;
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int TMEM_COLS = BN;  // f32 accumulator, one column per output column
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    using C = Cfg<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *acc_full = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int z = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
+    const int kb_total = (g.K + BK - 1) / BK;
+    const int kb_begin = split * g.kb_per_split;
+    const int nkb = max(0, min(kb_total, kb_begin + g.kb_per_split) - kb_begin);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            st::mbar_init(&full[s], 1);
+            st::mbar_init(&empty[s], 1);
+        }
+        st::mbar_init(acc_full, 1);
+        st::fence_mbar_init();
+    }
+    if (warp == 1) {
+        st::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            st::tma_prefetch_desc(&tmA);
+            st::tma_prefetch_desc(&tmB);
+            const int ca2 = g.a_grp > 1 ? z % g.a_grp : 0, ca3 = g.a_outer ? z / g.a_grp : 0;
+            const int cb2 = g.b_grp > 1 ? z % g.b_grp : 0, cb3 = g.b_outer ? z / g.b_grp : 0;
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !st::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, g.status, st::DEV_TIMEOUT_EMPTY))
+                    break;
+                st::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                const int kc = (kb_begin + i) * BK;
+                uint8_t *sa = smem + s * C::STAGE_BYTES;
+                uint8_t *sb = sa + C::A_BYTES;
+                if (!A_MN) {
+                    st::tma_load_4d(sa, &tmA, &full[s], kc, m0, ca2, ca3);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BM / 32; j++) st::tma_load_4d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, kc, ca2, ca3);
+                }
+                if (!B_MN) {
+                    st::tma_load_4d(sb, &tmB, &full[s], kc, n0, cb2, cb3);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BN / 32; j++) st::tma_load_4d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, kc, cb2, cb3);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = st::idesc_make(1, 2, A_MN, B_MN, BM, BN);
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (!st::mbar_wait(&full[s], (i / STAGES) & 1, g.status, st::DEV_TIMEOUT_FULL)) break;
+                st::tc_fence_after();
+                const uint32_t sa = st::smem_u32(smem + s * C::STAGE_BYTES);
+                const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; kk++) {
+                    // K-major (128B swizzle): advance 32 bytes (8 tf32) along the
+                    // swizzled row; 8-row groups 1024 bytes apart.
+                    // MN-major (128B swizzle on a 32B base): advance 8 k rows
+                    // (1024 bytes); 4-row atoms 512 bytes apart; 32-wide MN
+                    // chunks (one TMA box each) 4096 bytes apart.
+                    const uint64_t ad = A_MN ? st::sdesc_make(sa + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
+                                             : st::sdesc_sw128(sa + kk * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? st::sdesc_make(sb + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
+                                             : st::sdesc_sw128(sb + kk * 32, 16, 1024);
+                    st::umma_tf32(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                st::umma_commit(&empty[s]);
+            }
+            st::umma_commit(acc_full);
+        }
+    } else {  // warps 2..5: epilogue; warp w reads TMEM lanes 32*(w%4) ..
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        const bool ok = st::mbar_wait(acc_full, 0, g.status, st::DEV_TIMEOUT_ACC);
+        st::tc_fence_after();
+        const bool split_out = g.splits > 1;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+            st::tmem_ld_wait();
+            if (!ok || nkb == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j++) r[j] = 0u;
+            }
+            if (row < g.M) {
+                if (split_out) {
+                    float *dst = g.partial + (static_cast<int64_t>(blockIdx.z) * g.M + row) * g.N;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int col = n0 + c0 + j;
+                        if (col < g.N) dst[col] = __uint_as_float(r[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int col = n0 + c0 + j;
+                        if (col < g.N) {
+                            const int64_t oi = out_index(g, z, row, col);
+                            g.c[oi] = epilogue(g, z, oi, col, __uint_as_float(r[j]));
+                        }
+                    }
+                }
+            }
+        }
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        st::tc_fence_after();
+        st::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// Sums split-k partials in split order, then applies the epilogue.
+__global__ void k_splitk_reduce(const GemmArgs g) {
+    const int64_t mn = static_cast<int64_t>(g.M) * g.N;
+    const int64_t total = mn * g.batch;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int z = static_cast<int>(i / mn);
+        const int64_t rem = i - static_cast<int64_t>(z) * mn;
+        const int row = static_cast<int>(rem / g.N), col = static_cast<int>(rem % g.N);
+        const float *p = g.partial + static_cast<int64_t>(z) * g.splits * mn + rem;
+        float s = 0.0f;
+        for (int sp = 0; sp < g.splits; sp++) s = __fadd_rn(s, p[sp * mn]);
+        const int64_t oi = out_index(g, z, row, col);
+        g.c[oi] = epilogue(g, z, oi, col, s);
+    }
+}
+
+__device__ __forceinline__ float load_op(const Operand &o, int z, int r, int c) {
+    const int64_t base = o.off + static_cast<int64_t>(z / o.grp) * o.stride + static_cast<int64_t>(z % o.grp) * o.inner;
+    return o.trans ? o.ptr[base + static_cast<int64_t>(c) * o.ld + r] : o.ptr[base + static_cast<int64_t>(r) * o.ld + c];
+}
+
+// Bit-exact SIMT matmul: 64x64 tile per 256 threads, 4x4 outputs per thread,
+// each output accumulated as acc = acc + a*b (separately rounded) over k
+// ascending, from +0.
+constexpr int EX_T = 64, EX_K = 16;
+__global__ void __launch_bounds__(256) k_gemm_exact(const Operand A, const Operand B, const GemmArgs g) {
+    __shared__ float As[EX_K][EX_T + 4];
+    __shared__ float Bs[EX_K][EX_T + 4];
+    const int z = blockIdx.z;
+    const int m0 = blockIdx.y * EX_T, n0 = blockIdx.x * EX_T;
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < g.K; k0 += EX_K) {
+        for (int e = threadIdx.x; e < EX_K * EX_T; e += 256) {
+            const int kk = e / EX_T, mm = e % EX_T;
+            const int kg = k0 + kk;
+            As[kk][mm] = (m0 + mm < g.M && kg < g.K) ? load_op(A, z, m0 + mm, kg) : 0.0f;
+            Bs[kk][mm] = (n0 + mm < g.N && kg < g.K) ? load_op(B, z, kg, n0 + mm) : 0.0f;
+        }
+        __syncthreads();
+        const int kmax = min(EX_K, g.K - k0);
+        for (int kk = 0; kk < kmax; kk++) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], b[j]));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int row = m0 + ty * 4 + i;
+        if (row >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int col = n0 + tx * 4 + j;
+            if (col >= g.N) continue;
+            const int64_t oi = out_index(g, z, row, col);
+            g.c[oi] = epilogue(g, z, oi, col, acc[i][j]);
+        }
+    }
+}
+
+// Column sums of b[z] (logical [k, n]) over k, added into col_sum: the
+// Epilogue::col_sum bias gradient (src/gpu_step/matmul.rs:75-78), k ascending.
+__global__ void k_col_sum(const Operand B, int K, int N, int batch, float *dst, int64_t off, int64_t stride) {
+    const int64_t total = static_cast<int64_t>(batch) * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int z = static_cast<int>(i / N), col = static_cast<int>(i % N);
+        float s = 0.0f;
+        for (int k = 0; k < K; k++) s = __fadd_rn(s, load_op(B, z, k, col));
+        float *d = dst + off + static_cast<int64_t>(z) * stride + col;
+        *d = __fadd_rn(*d, s);
+    }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, dim3 grid) {
+    using C = Cfg<BN, STAGES>;
+    auto kern = k_gemm_tf32<BN, STAGES, A_MN, B_MN>;
+    static bool attr_done = false;  // per instantiation
+    if (!attr_done) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_done = true;
+    }
+    kern<<<grid, 192, C::SMEM, h->stream>>>(ma, mb, g);
+    return st_after_launch(h, "k_gemm_tf32");
+}
+
+template <int BN, int STAGES>
+st_status dispatch_tf32(st_handle *h, bool a_mn, bool b_mn, const CUtensorMap &ma, const CUtensorMap &mb,
+                        const GemmArgs &g, dim3 grid) {
+    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, g, grid);
+    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, g, grid);
+    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, g, grid);
+    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, g, grid);
+}
+
+Operand to_operand(const st_mat *m, int64_t packed_ld) {
+    Operand o;
+    o.ptr = static_cast<const float *>(m->ptr);
+    o.off = m->off;
+    o.stride = m->stride;
+    o.inner = m->inner;
+    o.ld = m->ld ? m->ld : packed_ld;
+    o.grp = m->group > 0 ? m->group : 1;
+    o.trans = m->trans;
+    return o;
+}
+
+// Tensor map for an operand stored as [srows, scols] (scols contiguous).
+bool operand_map(CUtensorMap *map, const Operand &o, int64_t batch, int64_t srows, int64_t scols, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapSwizzle swz, std::string *why) {
+    const float *base = o.ptr + o.off;
+    const int64_t outer = (o.stride != 0) ? (batch + o.grp - 1) / o.grp : 1;
+    const int64_t grp = o.grp > 1 ? std::min<int64_t>(o.grp, batch) : 1;
+    const uint64_t filler = static_cast<uint64_t>(o.ld) * srows;  // any valid stride for extent-1 dims
+    const uint64_t inner = grp > 1 ? static_cast<uint64_t>(o.inner) : filler;
+    const uint64_t stride = o.stride != 0 ? static_cast<uint64_t>(o.stride) : filler;
+    return st_make_map_4d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, scols, srows, grp, outer, o.ld, inner, stride,
+                          box_cols, box_rows, swz, why);
+}
+
+}  // namespace
+
+static bool fits_i32(int64_t v) { return v >= 0 && v < (1ll << 31); }
+
+extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch,
+                             int64_t m, int64_t k, int64_t n, const st_epilogue *epi, st_precision prec) {
+    if (!h) return ST_INVALID_ARG;
+    if (!a || !b || !out || !a->ptr || !b->ptr || !out->ptr) return h->fail(ST_INVALID_ARG, "st_gemm: null operand");
+    if (batch < 1 || m < 1 || n < 1 || k < 0 || !fits_i32(m) || !fits_i32(n) || !fits_i32(k) || batch > 65535)
+        return h->fail(ST_INVALID_ARG, "st_gemm: bad shape batch=%lld m=%lld k=%lld n=%lld", (long long)batch,
+                       (long long)m, (long long)k, (long long)n);
+    if (out->trans) return h->fail(ST_INVALID_ARG, "st_gemm: out must be stored row-major (trans = 0)");
+    if (a->dtype != ST_F32 || b->dtype != ST_F32 || out->dtype != ST_F32)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: operands must be f32");
+    if (a->off < 0 || b->off < 0 || out->off < 0 || a->ld < 0 || b->ld < 0 || out->ld < 0)
+        return h->fail(ST_INVALID_ARG, "st_gemm: negative offset or ld");
+    if (prec != ST_PREC_F32_EXACT && prec != ST_PREC_TF32) return h->fail(ST_INVALID_ARG, "st_gemm: unknown precision");
+    cudaSetDevice(h->device);
+
+    const Operand A = to_operand(a, a->trans ? m : k);
+    const Operand B = to_operand(b, b->trans ? k : n);
+    st_epilogue e{};
+    if (epi) e = *epi;
+
+    GemmArgs g{};
+    g.M = static_cast<int>(m);
+    g.N = static_cast<int>(n);
+    g.K = static_cast<int>(k);
+    g.batch = static_cast<int>(batch);
+    g.splits = 1;
+    g.c = static_cast<float *>(out->ptr);
+    g.c_off = out->off;
+    g.c_stride = out->stride;
+    g.c_inner = out->inner;
+    g.c_ld = out->ld ? out->ld : n;
+    g.c_grp = out->group > 0 ? out->group : 1;
+    g.bias = e.bias;
+    g.bias_off = e.bias_off;
+    g.bias_stride = e.bias_stride;
+    g.mask = e.mask;
+    g.mask_off = e.mask_off;
+    g.residual = e.residual;
+    g.residual_off = e.residual_off;
+    g.relu = e.relu;
+    g.accumulate = e.accumulate;
+    g.status = h->d_status;
+
+    if (e.col_sum) {
+        const int64_t total = batch * n;
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+        k_col_sum<<<blocks, 256, 0, h->stream>>>(B, g.K, g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
+        st_status s = st_after_launch(h, "k_col_sum");
+        if (s != ST_OK) return s;
+    }
+
+    bool use_tc = (prec == ST_PREC_TF32) && k >= 1;
+    CUtensorMap ma, mb;
+    std::string why;
+    const bool a_mn = a->trans != 0, b_mn = b->trans == 0;
+    int BN = 128;
+    const int64_t m_tiles = (m + BM - 1) / BM;
+    if (n <= 64 || m_tiles * ((n + 127) / 128) * batch < h->num_sms / 2) BN = 64;
+    if (use_tc) {
+        // A: logical [m, k]; stored [m, k] (K-major) or [k, m] (MN-major).
+        // K-major tiles: 128-byte swizzle.  MN-major tf32 tiles: 128-byte
+        // swizzle of 32-byte chunks (the layout the tensor core reads for
+        // 32-bit MN-major operands).
+        const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        bool okA = a_mn ? operand_map(&ma, A, batch, k, m, 32, 32, mnmaj, &why)
+                        : operand_map(&ma, A, batch, m, k, 32, BM, kmaj, &why);
+        bool okB = okA && (b_mn ? operand_map(&mb, B, batch, k, n, 32, 32, mnmaj, &why)
+                                : operand_map(&mb, B, batch, n, k, 32, static_cast<uint32_t>(BN), kmaj, &why));
+        use_tc = okA && okB;
+    }
+    if (use_tc) {
+        g.a_grp = A.grp > 1 ? static_cast<int>(std::min<int64_t>(A.grp, batch)) : 1;
+        g.a_outer = A.stride != 0;
+        g.b_grp = B.grp > 1 ? static_cast<int>(std::min<int64_t>(B.grp, batch)) : 1;
+        g.b_outer = B.stride != 0;
+        if (A.grp > 1) g.a_grp = A.grp;
+        if (B.grp > 1) g.b_grp = B.grp;
+        const int kb_total = static_cast<int>((k + BK - 1) / BK);
+        const int64_t tiles = m_tiles * ((n + BN - 1) / BN) * batch;
+        int splits = 1;
+        if (tiles < h->num_sms && kb_total >= 4) {
+            splits = static_cast<int>(std::min<int64_t>((h->num_sms + tiles - 1) / tiles, kb_total / 2));
+            splits = std::max(splits, 1);
+        }
+        int kbps = (kb_total + splits - 1) / splits;
+        splits = (kb_total + kbps - 1) / kbps;
+        if (batch * splits > 65535) {
+            splits = 1;
+            kbps = kb_total;
+        }
+        g.splits = splits;
+        g.kb_per_split = kbps;
+        if (splits > 1) {
+            g.partial = static_cast<float *>(st_scratch(h, SLOT_SPLITK, sizeof(float) * batch * splits * m * n));
+            if (!g.partial) return ST_NO_MEMORY;
+        }
+        dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
+                  static_cast<unsigned>(batch * splits));
+        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, g, grid)
+                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, g, grid);
+        if (s != ST_OK) return s;
+        if (splits > 1) {
+            const int64_t total = batch * m * n;
+            const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * h->num_sms));
+            k_splitk_reduce<<<blocks, 256, 0, h->stream>>>(g);
+            return st_after_launch(h, "k_splitk_reduce");
+        }
+        return ST_OK;
+    }
+    dim3 grid(static_cast<unsigned>((n + EX_T - 1) / EX_T), static_cast<unsigned>((m + EX_T - 1) / EX_T),
+              static_cast<unsigned>(batch));
+    if (grid.y > 65535) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: m too large for the exact kernel");
+    k_gemm_exact<<<grid, 256, 0, h->stream>>>(A, B, g);
+    return st_after_launch(h, "k_gemm_exact");
+}
+
+extern "C" st_status st_matmul_host(st_handle *h, const float *a, const float *b, float *out, int64_t m, int64_t k,
+                                    int64_t n, int32_t ta, int32_t tb, st_precision prec) {
+    if (!h) return ST_INVALID_ARG;
+    if (!a || !b || !out) return h->fail(ST_INVALID_ARG, "st_matmul_host: null buffer");
+    if (m < 1 || n < 1 || k < 0) return h->fail(ST_INVALID_ARG, "st_matmul_host: bad shape");
+    cudaSetDevice(h->device);
+    const size_t ab = sizeof(float) * m * k, bb = sizeof(float) * k * n, cb = sizeof(float) * m * n;
+    float *da = static_cast<float *>(st_scratch(h, SLOT_HOST_A, ab));
+    float *db = static_cast<float *>(st_scratch(h, SLOT_HOST_B, bb));
+    float *dc = static_cast<float *>(st_scratch(h, SLOT_HOST_C, cb));
+    if (!da || !db || !dc) return ST_NO_MEMORY;
+    if (ab) ST_CHECK_CUDA(h, cudaMemcpyAsync(da, a, ab, cudaMemcpyHostToDevice, h->stream));
+    if (bb) ST_CHECK_CUDA(h, cudaMemcpyAsync(db, b, bb, cudaMemcpyHostToDevice, h->stream));
+    st_mat A{da, 0, 0, 0, 0, 1, ta, ST_F32, 0};
+    st_mat B{db, 0, 0, 0, 0, 1, tb, ST_F32, 0};
+    st_mat C{dc, 0, 0, 0, 0, 1, 0, ST_F32, 0};
+    st_status s = st_gemm(h, &A, &B, &C, 1, m, k, n, nullptr, prec);
+    if (s != ST_OK) return s;
+    ST_CHECK_CUDA(h, cudaMemcpyAsync(out, dc, cb, cudaMemcpyDeviceToHost, h->stream));
+    return st_sync(h);
+}

@@ -1,0 +1,71 @@
+// st_internal.h -- handle state and host helpers shared by the .cu files.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/st_b200.h"
+
+// Scratch slots of the handle's pool (one buffer each, grown on demand).
+enum StScratchSlot {
+    SLOT_SPLITK = 0,  // split-k partial sums
+    SLOT_HOST_A,      // device copies for the host-buffer entry points
+    SLOT_HOST_B,
+    SLOT_HOST_C,
+    SLOT_KNN_CAND,    // kNN candidate lists
+    SLOT_KNN_PART,    // kNN per-split partial top-k lists
+    SLOT_KNN_Q,       // kNN quantised queries
+    SLOT_KNN_MISC,
+    SLOT_COUNT
+};
+
+struct st_handle {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    int *d_status = nullptr;  // device status word written by bounded waits
+    void *slot_ptr[SLOT_COUNT] = {};
+    size_t slot_bytes[SLOT_COUNT] = {};
+    int64_t launches = 0;
+    const char *last_kernel = "";
+    int num_sms = 148;
+
+    st_status fail(st_status s, const char *fmt, ...) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        err = buf;
+        return s;
+    }
+};
+
+#define ST_CHECK_CUDA(h, call)                                                                           \
+    do {                                                                                                 \
+        cudaError_t e_ = (call);                                                                         \
+        if (e_ != cudaSuccess) return (h)->fail(ST_CUDA_ERROR, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+// Checks the launch that was just enqueued and counts it.
+st_status st_after_launch(st_handle *h, const char *what);
+
+// Returns a device buffer of at least `bytes` for `slot` (grows the slot;
+// growth synchronises the stream).  nullptr on failure (h->err set).
+void *st_scratch(st_handle *h, int slot, size_t bytes);
+
+// cuTensorMapEncodeTiled, resolved through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 st_encode_fn();
+
+// A 4-D tiled tensor map over fp32/f16/... rows: dims {cols, rows, grp, outer},
+// byte strides {ld, inner, stride}, box {box_cols, box_rows, 1, 1}, 128-byte
+// swizzle, zero fill out of bounds.
+bool st_make_map_4d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes, const void *base, uint64_t cols,
+                    uint64_t rows, uint64_t grp, uint64_t outer, uint64_t ld_elems, uint64_t inner_elems,
+                    uint64_t stride_elems, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz,
+                    std::string *why);
