@@ -1,0 +1,377 @@
+#!/usr/bin/env python
+"""Benchmark of scratchtape-b200's hot path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3|c5] [--impl ours|reference]
+
+Default workload ("C2"): one byte-level-transformer MLP
+layer forward + backward as six f32 GEMMs -- tokens M = 32 x 128 = 4096,
+d_model 128, d_ff 512; X ~ N(0,1), W1/W2 Xavier-uniform, dY ~ N(0, 1e-2) --
+run on the tcgen05 TF32 tensor cores.  A step is those six GEMMs (NN
+forward, NT dX, TN dW) over one batch.  The inputs (25 MB) fit in L2, so L2
+is flushed (a 256 MiB write) before every timed step, outside its events.
+
+``value``: TFLOP/s of the whole job with inputs resident in HBM, the step
+replayed from a CUDA graph, timed by CUDA events per step (flush excluded),
+max over ranks.  ``e2e``: the same metric through the public host-array API
+(scratchtape_b200.mlp.forward_backward_host): pinned host inputs copied in,
+six GEMMs, gradients copied out, every step.  ``roofline``: the TF32 GEMM
+kernel's algorithmic bytes per launch over its CUDA-event duration (cold L2),
+against the measured HBM copy bandwidth.  ``cpu_baseline``: the CPU oracle
+(restated tensor.rs matmul, one thread like the reference) on one full step.
+
+``--impl reference`` times that CPU restatement of the reference's path with
+all host threads on the same workload (rank 0 only under torchrun).
+
+Multi-GPU: the GEMMs of one layer do not shard (replicas only); with N ranks
+each GPU runs its own replica and value is the sum over GPUs.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMM TFLOP/s & % of B200 peak per layout; kNN keys/s vs HBM; vs CPU tensor.rs"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+C2 = dict(m=32 * 128, d=128, dff=512)
+# dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the C2
+# step, averaged over its launches, from profiles/gemm_tf32_c2.md (ncu, 1 pass).
+C2_TRAFFIC_PER_LAUNCH = None
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--config", default="c2", choices=["c2"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index, period=0.005):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def mlp_inputs(torch, device, seed=0):
+    """C2 synthetic inputs; seeded torch generator."""
+    m, d, dff = C2["m"], C2["d"], C2["dff"]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 1)
+    x = torch.randn((m, d), generator=g, device=device)
+    lim1 = (6.0 / (d + dff)) ** 0.5
+    w1 = (torch.rand((d, dff), generator=g, device=device) * 2 - 1) * lim1
+    w2 = (torch.rand((dff, d), generator=g, device=device) * 2 - 1) * lim1
+    dy = torch.randn((m, d), generator=g, device=device) * 0.1
+    return x, w1, w2, dy
+
+
+def c2_flops():
+    return 6 * 2 * C2["m"] * C2["d"] * C2["dff"]
+
+
+def cpu_step_c2(x, w1, w2, dy, threads):
+    """One C2 step on the CPU oracle: the tape's six matmuls (NT/TN through
+    explicit transposes, src/tape.rs:505-510), ReLU and its mask."""
+    import oracle
+    pre = oracle.matmul_layout(x, w1, threads=threads)
+    h = np.maximum(pre, np.float32(0))
+    oracle.matmul_layout(h, w2, threads=threads)
+    dh = oracle.matmul_layout(dy, oracle.transpose(w2), threads=threads)
+    dh = np.where(pre > 0, dh, np.float32(0)).astype(np.float32)
+    oracle.matmul_layout(oracle.transpose(h), dy, threads=threads)
+    oracle.matmul_layout(dh, oracle.transpose(w1), threads=threads)
+    oracle.matmul_layout(oracle.transpose(x), dh, threads=threads)
+
+
+def host_c2_inputs(seed=0):
+    rng = np.random.default_rng(seed + 1)
+    m, d, dff = C2["m"], C2["d"], C2["dff"]
+    lim = (6.0 / (d + dff)) ** 0.5
+    x = rng.standard_normal((m, d)).astype(np.float32)
+    w1 = rng.uniform(-lim, lim, (d, dff)).astype(np.float32)
+    w2 = rng.uniform(-lim, lim, (dff, d)).astype(np.float32)
+    dy = (rng.standard_normal((m, d)) * 0.1).astype(np.float32)
+    return x, w1, w2, dy
+
+
+def cpu_baseline_c2():
+    x, w1, w2, dy = host_c2_inputs()
+    times = []
+    t_end = time.perf_counter() + 20.0
+    while len(times) < 3 and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        cpu_step_c2(x, w1, w2, dy, threads=1)
+        times.append(time.perf_counter() - t0)
+    t = float(np.median(times))
+    return {"value": c2_flops() / t / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": "%d full C2 steps (6 GEMMs, tape transposes, ReLU mask) on the oracle's restated "
+                      "tensor.rs matmul, 1 thread as the reference runs; median" % len(times),
+            "ms_per_step": t * 1e3}
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    x, w1, w2, dy = host_c2_inputs()
+    for _ in range(args.warmup):
+        cpu_step_c2(x, w1, w2, dy, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step_c2(x, w1, w2, dy, threads)
+    el = time.perf_counter() - t0
+    v = c2_flops() * args.steps / el / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2 MLP layer fwd+bwd GEMMs, M=4096 (32x128), d_model 128, d_ff 512, f32",
+                   "global_batch": 32, "seq_len": 128, "parallelism": "replicas only (CPU, rank 0)"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": "full C2 steps on the oracle's restated tensor.rs matmul (row-parallel over %d "
+                                   "threads; the reference itself is single threaded)" % threads},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import scratchtape_b200 as st
+    from scratchtape_b200 import mlp
+
+    peaks, peak_src = load_peaks()
+    h = st.handle()
+    m, d, dff = C2["m"], C2["d"], C2["dff"]
+    bufs = mlp.MlpBuffers.allocate(m, d, dff, device)
+    x, w1, w2, dy = mlp_inputs(torch, device, seed=rank)
+    bufs.x.copy_(x)
+    bufs.w1.copy_(w1)
+    bufs.w2.copy_(w2)
+    bufs.dy.copy_(dy)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    # eager warm-up: grows scratch, sets kernel attributes, counts launches
+    n0 = h.launches
+    mlp.forward_backward(bufs)
+    torch.cuda.synchronize()
+    launches_per_step = h.launches - n0
+
+    stream = torch.cuda.Stream(device)
+    sides = mlp.StepStreams(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        mlp.forward_backward(bufs, streams=sides)  # warm on the capture streams
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        mlp.forward_backward(bufs, streams=sides)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        graph.replay()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            graph.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = float(sum(step_ms))
+    if world > 1:
+        t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = c2_flops() * args.steps * world / (total_ms / 1e3) / 1e12
+
+    # per-launch roofline of the TF32 GEMM kernel: each of the six GEMMs timed
+    # alone with cold L2, algorithmic bytes / duration
+    per_bytes = mlp.gemm_bytes(m, d, dff)
+    gl = mlp.gemm_list(bufs)
+    reps = 20
+    gemm_ms = []
+    for (a_, b_, o_, mm_, kk_, nn_, epi), nb in zip(gl, per_bytes):
+        gg = torch.cuda.CUDAGraph()  # one GEMM (and its split-k reduce) per graph: no host gaps
+        with torch.cuda.graph(gg, stream=stream):
+            st.matmul_with(a_, b_, o_, 1, mm_, kk_, nn_, epi, st.TF32)
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gg.replay()
+            e1.record()
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        gemm_ms.append(float(np.mean([a.elapsed_time(b) for a, b in ts])))
+        del gg
+    bytes_total = float(sum(per_bytes))
+    achieved = bytes_total / (sum(gemm_ms) / 1e3) / 1e9
+    hbm = float(peaks["hbm_gbs"])
+
+    # e2e through the host-array API
+    hx, hw1, hw2, hdy = (t.cpu().pin_memory() for t in (x, w1, w2, dy))
+    outs = tuple(torch.empty(t.shape, dtype=torch.float32, pin_memory=True) for t in (bufs.y, bufs.dx, bufs.dw1,
+                                                                                      bufs.dw2))
+    for _ in range(max(3, args.warmup // 4)):
+        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides)
+    e2e_steps = max(10, min(args.steps, 200))
+    e_ms = []
+    for _ in range(e2e_steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides)
+        e1.record()
+        e1.synchronize()
+        e_ms.append(e0.elapsed_time(e1))
+    e_total = float(sum(e_ms))
+    if world > 1:
+        t = torch.tensor([e_total], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_total = float(t.item())
+    e2e_value = c2_flops() * e2e_steps * world / (e_total / 1e3) / 1e12
+    h2d = sum(t.numel() * 4 for t in (hx, hw1, hw2, hdy))
+    d2h = sum(t.numel() * 4 for t in outs)
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_c2()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "tf32", "data": "synthetic",
+            "config": {"workload": "C2 MLP layer fwd+bwd GEMMs (BASELINE configs[1]): M=4096 (batch 32 x seq 128), "
+                                   "d_model 128, d_ff 512, f32 in/out, TF32 tensor cores; NN fwd, NT dX/dH, TN dW",
+                       "global_batch": 32 * world, "seq_len": 128,
+                       "parallelism": "replicas only" if world > 1 else "single GPU",
+                       "l2": "flushed (256 MiB write) before every timed step, outside its events",
+                       "graph": "step replayed from one CUDA graph"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": C2_TRAFFIC_PER_LAUNCH, "peak_source": peak_src,
+                         "kernel": "k_gemm_tf32 (+k_splitk_reduce)",
+                         "per_gemm_us": [round(t * 1e3, 2) for t in gemm_ms],
+                         "per_gemm_bytes": per_bytes,
+                         "tensor_frac_of_bf16_peak": c2_flops() / (sum(gemm_ms) / 1e3) / 1e12 /
+                         float(peaks["bf16_tflops"])},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e_total / e2e_steps, "steps": e2e_steps,
+                    "api": "scratchtape_b200.mlp.forward_backward_host (pinned host arrays)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

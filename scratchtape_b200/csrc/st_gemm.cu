@@ -43,6 +43,7 @@ struct GemmArgs {
     const float *residual;
     int64_t residual_off;
     int relu, accumulate;
+    int vec;  // out/mask/residual rows 16-byte aligned with N % 4 == 0: float4 epilogue
     float *partial;  // split-k partials, [batch*splits][M][N]
     int *status;
 };
@@ -73,8 +74,127 @@ struct Cfg {
     static constexpr int TMEM_COLS = BN;  // f32 accumulator, one column per output column
 };
 
+// Epilogue of one CTA tile, run by 4 warps; warp q owns TMEM lanes (tile
+// rows) 32q..32q+31.  Each 32x32 TMEM chunk (thread = row after tcgen05.ld)
+// is transposed through shared memory so that global traffic is row-major
+// and coalesced.  The staging tile reuses the operand ring: once acc_full
+// has fired every stage has been consumed by the tensor core.
+
+// float4 path: 32 x 32 tile, 16-byte chunks XOR-swizzled by row so both the
+// row-wise writes and the 4-rows-per-pass reads are free of bank conflicts;
+// lane = (row within pass, 4-column chunk); all extra loads are issued before
+// any arithmetic so their latencies overlap.
+template <int BN>
+__device__ __forceinline__ void epilogue_vec(const GemmArgs &g, uint8_t *smem, uint32_t tmem, int q, int lane, int m0,
+                                             int n0, int z, bool have) {
+    float *tile = reinterpret_cast<float *>(smem) + q * 1024;
+    const int sub = lane >> 3, ch = lane & 7;
+    const bool split_out = g.splits > 1;
+    const int64_t zbase = g.c_off + static_cast<int64_t>(z / g.c_grp) * g.c_stride +
+                          static_cast<int64_t>(z % g.c_grp) * g.c_inner;
+    const float *bias_z = g.bias ? g.bias + g.bias_off + static_cast<int64_t>(z) * g.bias_stride : nullptr;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+        st::tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            float4 w = have ? make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                                          __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(tile + lane * 32 + ((c ^ (lane & 7)) << 2)) = w;
+        }
+        __syncwarp();
+        float4 v[8];
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int rr = it * 4 + sub;
+            v[it] = *reinterpret_cast<const float4 *>(tile + rr * 32 + ((ch ^ (rr & 7)) << 2));
+        }
+        __syncwarp();
+        const int col = n0 + c0 + ch * 4;
+        if (col >= g.N) continue;  // N % 4 == 0: a chunk is all in or all out
+        const int row0 = m0 + q * 32 + sub;
+        if (split_out) {
+            float *dst = g.partial + (static_cast<int64_t>(blockIdx.z) * g.M + row0) * g.N + col;
+#pragma unroll
+            for (int it = 0; it < 8; it++)
+                if (row0 + it * 4 < g.M) *reinterpret_cast<float4 *>(dst + static_cast<int64_t>(it) * 4 * g.N) = v[it];
+            continue;
+        }
+        float4 mk[8], rs[8], ac[8];
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int row = row0 + it * 4;
+            const int64_t rel = static_cast<int64_t>(row) * g.c_ld + col + (zbase - g.c_off);
+            const bool in = row < g.M;
+            mk[it] = (g.mask && in) ? __ldg(reinterpret_cast<const float4 *>(g.mask + g.mask_off + rel)) : make_float4(1.f, 1.f, 1.f, 1.f);
+            rs[it] = (g.residual && in) ? __ldg(reinterpret_cast<const float4 *>(g.residual + g.residual_off + rel)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            ac[it] = (g.accumulate && in) ? *reinterpret_cast<const float4 *>(g.c + g.c_off + rel) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float4 bz = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (bias_z) bz = make_float4(bias_z[col], bias_z[col + 1], bias_z[col + 2], bias_z[col + 3]);
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+            const int row = row0 + it * 4;
+            if (row >= g.M) break;
+            float o[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+            const float b4[4] = {bz.x, bz.y, bz.z, bz.w};
+            const float m4[4] = {mk[it].x, mk[it].y, mk[it].z, mk[it].w};
+            const float r4[4] = {rs[it].x, rs[it].y, rs[it].z, rs[it].w};
+            const float a4[4] = {ac[it].x, ac[it].y, ac[it].z, ac[it].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float x = o[j];
+                if (bias_z) x = x + b4[j];
+                if (g.relu) x = fmaxf(x, 0.0f);
+                if (g.mask && !(m4[j] > 0.0f)) x = 0.0f;
+                if (g.residual) x = x + r4[j];
+                if (g.accumulate) x = x + a4[j];
+                o[j] = x;
+            }
+            *reinterpret_cast<float4 *>(g.c + zbase + static_cast<int64_t>(row) * g.c_ld + col) =
+                make_float4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+// Scalar path for layouts that are not 16-byte aligned: lane = column.
+template <int BN>
+__device__ __forceinline__ void epilogue_scalar(const GemmArgs &g, uint8_t *smem, uint32_t tmem, int q, int lane,
+                                                int m0, int n0, int z, bool have) {
+    float *tile = reinterpret_cast<float *>(smem) + q * (32 * 33);
+    const bool split_out = g.splits > 1;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+        st::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j++) tile[lane * 33 + j] = have ? __uint_as_float(r[j]) : 0.0f;
+        __syncwarp();
+        const int col = n0 + c0 + lane;
+        if (col < g.N) {
+#pragma unroll 4
+            for (int rr = 0; rr < 32; rr++) {
+                const int row = m0 + q * 32 + rr;
+                if (row >= g.M) break;
+                const float v = tile[rr * 33 + lane];
+                if (split_out) {
+                    g.partial[(static_cast<int64_t>(blockIdx.z) * g.M + row) * g.N + col] = v;
+                } else {
+                    const int64_t oi = out_index(g, z, row, col);
+                    g.c[oi] = epilogue(g, z, oi, col, v);
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
@@ -164,38 +284,12 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {  // warps 2..5: epilogue; warp w reads TMEM lanes 32*(w%4) ..
         const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
         const bool ok = st::mbar_wait(acc_full, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
-        const bool split_out = g.splits > 1;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-            st::tmem_ld_wait();
-            if (!ok || nkb == 0) {
-#pragma unroll
-                for (int j = 0; j < 32; j++) r[j] = 0u;
-            }
-            if (row < g.M) {
-                if (split_out) {
-                    float *dst = g.partial + (static_cast<int64_t>(blockIdx.z) * g.M + row) * g.N;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int col = n0 + c0 + j;
-                        if (col < g.N) dst[col] = __uint_as_float(r[j]);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int col = n0 + c0 + j;
-                        if (col < g.N) {
-                            const int64_t oi = out_index(g, z, row, col);
-                            g.c[oi] = epilogue(g, z, oi, col, __uint_as_float(r[j]));
-                        }
-                    }
-                }
-            }
+        if (g.vec) {
+            epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
+        } else {
+            epilogue_scalar<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         }
     }
     st::tc_fence_before();
@@ -206,20 +300,48 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-// Sums split-k partials in split order, then applies the epilogue.
+// Sums split-k partials in split order, then applies the epilogue.  Thread
+// (z, row, 4-column group); coalesced along the row.  Partials are fetched
+// eight splits at a time before any addition, so their latencies overlap;
+// the additions stay in split order.
 __global__ void k_splitk_reduce(const GemmArgs g) {
+    const int groups = (g.N + 3) / 4;
+    const int z = blockIdx.z;
     const int64_t mn = static_cast<int64_t>(g.M) * g.N;
-    const int64_t total = mn * g.batch;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int z = static_cast<int>(i / mn);
-        const int64_t rem = i - static_cast<int64_t>(z) * mn;
-        const int row = static_cast<int>(rem / g.N), col = static_cast<int>(rem % g.N);
-        const float *p = g.partial + static_cast<int64_t>(z) * g.splits * mn + rem;
-        float s = 0.0f;
-        for (int sp = 0; sp < g.splits; sp++) s = __fadd_rn(s, p[sp * mn]);
-        const int64_t oi = out_index(g, z, row, col);
-        g.c[oi] = epilogue(g, z, oi, col, s);
+    const bool vec = (g.N % 4 == 0);
+    for (int row = blockIdx.y; row < g.M; row += gridDim.y) {
+        for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += gridDim.x * blockDim.x) {
+            const int col0 = gi * 4;
+            const float *p = g.partial + static_cast<int64_t>(z) * g.splits * mn + static_cast<int64_t>(row) * g.N + col0;
+            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (vec) {
+                for (int sp0 = 0; sp0 < g.splits; sp0 += 8) {
+                    float4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        v[j] = (sp0 + j < g.splits) ? __ldcg(reinterpret_cast<const float4 *>(p + (sp0 + j) * mn))
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        if (sp0 + j >= g.splits) break;
+                        s[0] = __fadd_rn(s[0], v[j].x);
+                        s[1] = __fadd_rn(s[1], v[j].y);
+                        s[2] = __fadd_rn(s[2], v[j].z);
+                        s[3] = __fadd_rn(s[3], v[j].w);
+                    }
+                }
+            } else {
+                for (int sp = 0; sp < g.splits; sp++)
+                    for (int j = 0; j < 4; j++)
+                        if (col0 + j < g.N) s[j] = __fadd_rn(s[j], p[sp * mn + j]);
+            }
+            for (int j = 0; j < 4; j++) {
+                const int col = col0 + j;
+                if (col >= g.N) break;
+                const int64_t oi = out_index(g, z, row, col);
+                g.c[oi] = epilogue(g, z, oi, col, s[j]);
+            }
+        }
     }
 }
 
@@ -386,6 +508,16 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     g.relu = e.relu;
     g.accumulate = e.accumulate;
     g.status = h->d_status;
+    {
+        auto al16 = [](const void *p, int64_t off) {
+            return (reinterpret_cast<uintptr_t>(p) + static_cast<uintptr_t>(off) * 4) % 16 == 0;
+        };
+        bool v = (n % 4 == 0) && (g.c_ld % 4 == 0) && al16(g.c, g.c_off);
+        if (batch > 1) v = v && (g.c_stride % 4 == 0) && (g.c_grp == 1 || g.c_inner % 4 == 0);
+        if (g.mask) v = v && al16(g.mask, g.mask_off);
+        if (g.residual) v = v && al16(g.residual, g.residual_off);
+        g.vec = v ? 1 : 0;
+    }
 
     if (e.col_sum) {
         const int64_t total = batch * n;
@@ -399,9 +531,12 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     CUtensorMap ma, mb;
     std::string why;
     const bool a_mn = a->trans != 0, b_mn = b->trans == 0;
-    int BN = 128;
+    // Tile width: 128 when the grid already fills the GPU, or when it is so
+    // small that split-k carries the parallelism (fewer re-reads of A);
+    // otherwise 64, which doubles the CTAs.
     const int64_t m_tiles = (m + BM - 1) / BM;
-    if (n <= 64 || m_tiles * ((n + 127) / 128) * batch < h->num_sms / 2) BN = 64;
+    const int64_t tiles128 = m_tiles * ((n + 127) / 128) * batch;
+    int BN = (n > 64 && (tiles128 >= h->num_sms || tiles128 * 8 <= h->num_sms)) ? 128 : 64;
     if (use_tc) {
         // A: logical [m, k]; stored [m, k] (K-major) or [k, m] (MN-major).
         // K-major tiles: 128-byte swizzle.  MN-major tf32 tiles: 128-byte
@@ -414,6 +549,7 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
                                 : operand_map(&mb, B, batch, n, k, 32, static_cast<uint32_t>(BN), kmaj, &why));
         use_tc = okA && okB;
     }
+    if (use_tc && m_tiles > 65535) use_tc = false;
     if (use_tc) {
         g.a_grp = A.grp > 1 ? static_cast<int>(std::min<int64_t>(A.grp, batch)) : 1;
         g.a_outer = A.stride != 0;
@@ -423,9 +559,11 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         if (B.grp > 1) g.b_grp = B.grp;
         const int kb_total = static_cast<int>((k + BK - 1) / BK);
         const int64_t tiles = m_tiles * ((n + BN - 1) / BN) * batch;
+        // Split k only when the tiles fill less than half the GPU, keeping
+        // at least 4 k blocks (128) per split.
         int splits = 1;
-        if (tiles < h->num_sms && kb_total >= 4) {
-            splits = static_cast<int>(std::min<int64_t>((h->num_sms + tiles - 1) / tiles, kb_total / 2));
+        if (tiles * 2 <= h->num_sms && kb_total >= 8) {
+            splits = static_cast<int>(std::min<int64_t>(std::min<int64_t>(h->num_sms / tiles, kb_total / 4), 16));
             splits = std::max(splits, 1);
         }
         int kbps = (kb_total + splits - 1) / splits;
@@ -446,9 +584,11 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
                                : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, g, grid);
         if (s != ST_OK) return s;
         if (splits > 1) {
-            const int64_t total = batch * m * n;
-            const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * h->num_sms));
-            k_splitk_reduce<<<blocks, 256, 0, h->stream>>>(g);
+            const int groups = static_cast<int>((n + 3) / 4);
+            const int threads = groups >= 128 ? 128 : 32 * ((groups + 31) / 32);
+            dim3 rgrid(static_cast<unsigned>((groups + threads - 1) / threads), static_cast<unsigned>(std::min<int64_t>(m, 65535)),
+                       static_cast<unsigned>(batch));
+            k_splitk_reduce<<<rgrid, threads, 0, h->stream>>>(g);
             return st_after_launch(h, "k_splitk_reduce");
         }
         return ST_OK;

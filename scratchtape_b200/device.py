@@ -68,6 +68,22 @@ def handle(device=None):
         return h
 
 
+_stream_handles = {}
+
+
+def handle_for_stream(stream):
+    """A handle of its own for `stream` (own scratch pool), for GEMMs that run
+    concurrently with others on side streams."""
+    key = (stream.device.index, stream.cuda_stream)
+    with _lock:
+        h = _stream_handles.get(key)
+        if h is None:
+            with torch.cuda.stream(stream):
+                h = Handle(stream.device.index)
+            _stream_handles[key] = h
+        return h
+
+
 def ptr(t):
     """Raw data pointer of a tensor (None -> NULL)."""
     return None if t is None else ctypes.c_void_p(t.data_ptr())

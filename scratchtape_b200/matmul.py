@@ -86,10 +86,13 @@ class Epilogue:
         return e
 
 
-def matmul_with(a: MatRef, b: MatRef, out: MatRef, batch, m, k, n, epi: Optional[Epilogue] = None, precision=TF32):
+def matmul_with(a: MatRef, b: MatRef, out: MatRef, batch, m, k, n, epi: Optional[Epilogue] = None, precision=TF32,
+                h=None):
     """out[z] (+)= epi(a[z] @ b[z]) for z < batch; one or two launches, enqueued
-    on torch's current stream (matmul.rs:106-192)."""
-    h = handle(out.h.device)
+    on torch's current stream (matmul.rs:106-192).  ``h``: the handle to use
+    (default: the device's); GEMMs running concurrently need distinct handles."""
+    if h is None:
+        h = handle(out.h.device)
     ca, cb, co = a._c(), b._c(), out._c()
     ce = epi._c(out.h) if epi is not None else None
     h.call("st_gemm", ctypes.byref(ca), ctypes.byref(cb), ctypes.byref(co), batch, m, k, n,

@@ -1,0 +1,123 @@
+"""One MLP layer forward + backward on the device: the six GEMMs the tape emits.
+
+Forward  H = ReLU(X W1) (NN), Y = H W2 (NN); backward dH = (dY W2^T) masked by
+H > 0 (NT, ReLU's backward as a GEMM epilogue), dW2 = H^T dY (TN),
+dX = dH W1^T (NT), dW1 = X^T dH (TN) -- the layouts Tape::backward's MatMul
+arm produces (src/tape.rs:505-510) for Linear layers without bias
+(src/nn.rs:110-114), with ReLU's mask as in the Relu arm (src/tape.rs:530-534).
+"""
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .matmul import MatRef, Epilogue, matmul_with, TF32
+
+
+@dataclass
+class MlpBuffers:
+    """Device tensors of one layer: inputs x, w1, w2, dy; outputs h, y, dh, dx, dw1, dw2."""
+    x: torch.Tensor
+    w1: torch.Tensor
+    w2: torch.Tensor
+    dy: torch.Tensor
+    h: torch.Tensor
+    y: torch.Tensor
+    dh: torch.Tensor
+    dx: torch.Tensor
+    dw1: torch.Tensor
+    dw2: torch.Tensor
+
+    @staticmethod
+    def allocate(m, d, dff, device):
+        f = lambda *s: torch.empty(s, dtype=torch.float32, device=device)
+        return MlpBuffers(f(m, d), f(d, dff), f(dff, d), f(m, d), f(m, dff), f(m, d), f(m, dff), f(m, d), f(d, dff),
+                          f(dff, d))
+
+
+def gemm_list(b: MlpBuffers):
+    """The six (a, b, out, m, k, n, epilogue) GEMMs of the step, in order."""
+    m, d = b.x.shape
+    dff = b.w1.shape[1]
+    return [
+        (MatRef(b.x), MatRef(b.w1), MatRef(b.h), m, d, dff, Epilogue(relu=True)),                # H = relu(X W1)
+        (MatRef(b.h), MatRef(b.w2), MatRef(b.y), m, dff, d, None),                               # Y = H W2
+        (MatRef(b.dy), MatRef(b.w2, trans=True), MatRef(b.dh), m, d, dff, Epilogue(mask=(b.h, 0))),  # dH
+        (MatRef(b.h, trans=True), MatRef(b.dy), MatRef(b.dw2), dff, m, d, None),                 # dW2 = H^T dY
+        (MatRef(b.dh), MatRef(b.w1, trans=True), MatRef(b.dx), m, dff, d, None),                 # dX = dH W1^T
+        (MatRef(b.x, trans=True), MatRef(b.dh), MatRef(b.dw1), d, m, dff, None),                 # dW1 = X^T dH
+    ]
+
+
+def gemm_bytes(m, d, dff):
+    """Algorithmic f32 bytes each GEMM must move (read A, B, mask; write C)."""
+    x, w, hh = m * d * 4, d * dff * 4, m * dff * 4
+    return [x + w + hh, hh + w + x, x + w + hh + hh, hh + x + w, hh + w + x, x + hh + w]
+
+
+class StepStreams:
+    """Two side streams (with their own library handles) so the step's
+    independent GEMMs overlap: after H, {Y, dH, dW2} run concurrently; after
+    dH, {dX, dW1}."""
+
+    def __init__(self, device):
+        from .device import handle_for_stream
+        self.s1 = torch.cuda.Stream(device)
+        self.s2 = torch.cuda.Stream(device)
+        self.h1 = handle_for_stream(self.s1)
+        self.h2 = handle_for_stream(self.s2)
+
+
+def forward_backward(b: MlpBuffers, precision=TF32, streams: StepStreams = None):
+    """Enqueues the six GEMMs on torch's current stream (and, with `streams`,
+    overlaps the independent ones on two side streams)."""
+    g = gemm_list(b)
+    if streams is None:
+        for a_, b_, o_, m, k, n, epi in g:
+            matmul_with(a_, b_, o_, 1, m, k, n, epi, precision)
+        return b
+    main = torch.cuda.current_stream()
+    run = lambda i, h=None: matmul_with(*g[i][:3], 1, *g[i][3:6], g[i][6], precision, h)
+    run(0)                                   # H = relu(X W1)
+    e_h = torch.cuda.Event()
+    e_h.record(main)
+    for s in (streams.s1, streams.s2):
+        s.wait_event(e_h)
+    with torch.cuda.stream(streams.s1):
+        run(1, streams.h1)                   # Y = H W2
+    with torch.cuda.stream(streams.s2):
+        run(3, streams.h2)                   # dW2 = H^T dY
+    run(2)                                   # dH
+    e_dh = torch.cuda.Event()
+    e_dh.record(main)
+    streams.s1.wait_event(e_dh)
+    with torch.cuda.stream(streams.s1):
+        run(5, streams.h1)                   # dW1 = X^T dH
+    run(4)                                   # dX = dH W1^T
+    for s in (streams.s1, streams.s2):
+        e = torch.cuda.Event()
+        e.record(s)
+        main.wait_event(e)
+    return b
+
+
+def forward_backward_host(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, dy: np.ndarray, bufs: MlpBuffers = None,
+                          outs=None, precision=TF32, streams: StepStreams = None):
+    """Host arrays in, host gradients out: copies x, w1, w2, dy to the device,
+    runs the layer forward and backward, and reads back (y, dx, dw1, dw2).
+    ``outs`` may hold preallocated (pinned) host tensors for the results."""
+    m, d = x.shape
+    dff = w1.shape[1]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if bufs is None:
+        bufs = MlpBuffers.allocate(m, d, dff, dev)
+    for dst, src in ((bufs.x, x), (bufs.w1, w1), (bufs.w2, w2), (bufs.dy, dy)):
+        dst.copy_(torch.as_tensor(src), non_blocking=True)
+    forward_backward(bufs, precision, streams)
+    if outs is None:
+        outs = tuple(torch.empty(t.shape, dtype=torch.float32, pin_memory=True) for t in (bufs.y, bufs.dx, bufs.dw1,
+                                                                                          bufs.dw2))
+    for dst, src in zip(outs, (bufs.y, bufs.dx, bufs.dw1, bufs.dw2)):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    return outs
