@@ -144,25 +144,6 @@ ST_API st_status st_softmax_rows(st_handle *h, const float *x, float *y, int64_t
 ST_API st_status st_softmax_rows_bwd(st_handle *h, const float *dy, const float *y, float *dx, int64_t rows, int64_t n,
                               float scale);
 
-/* ---- fused causal attention ----------------------------------------------- */
-
-/* Flash-style fused attention over bh independent heads, f16 storage with f32
- * accumulation on tcgen05 (kind::f16).  q, k, v, o: device f16 [bh, t, d]
- * (head z at z*t*d); lse: device f32 [bh, t] (natural-log sum of exp of the
- * scaled, masked row, for the backward).  Replaces the chain
- * batched_matmul(q,k,T) -> scale -> +mask -> softmax -> batched_matmul(w,v)
- * of TransformerBlock::forward_full (src/nn.rs:657-671) and of
- * DeviceTape::block_forward (src/gpu_step/tape.rs:481-484).
- * Shapes: t <= 128, d in {64} for the tensor-core kernel. */
-ST_API st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse, int64_t bh,
-                      int64_t t, int64_t d, float scale, int32_t causal);
-/* Backward: dq, dk, dv (device f16 [bh, t, d]) from q, k, v, o, do (f16) and
- * lse (f32).  Replaces batched_matmul_backward + the softmax backward
- * (src/tape.rs:90-112, src/gpu_step/tape.rs:363-375). */
-ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o, const void *dout,
-                      const float *lse, void *dq, void *dk, void *dv, int64_t bh, int64_t t, int64_t d, float scale,
-                      int32_t causal);
-
 #ifdef __cplusplus
 }
 #endif
