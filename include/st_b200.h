@@ -125,6 +125,27 @@ ST_API int64_t st_scratch_bytes(const st_handle *h);
 ST_API st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch, int64_t m,
                   int64_t k, int64_t n, const st_epilogue *epi, st_precision prec);
 
+/* st_gemm with ST_PREC_TF32 for callers that cannot let this library call
+ * cudaMalloc: a host program that has already divided the GPU's memory among
+ * its own pools and lends none to plug-ins, or a latency-critical loop where
+ * a cudaMalloc / cudaFree (which may synchronise the whole device) would
+ * stall it.  Split-k partial sums go to one 8 MiB array compiled into the
+ * library (every GPU that loads the library holds it until the process
+ * exits) instead of the handle's growable scratch pool, so the call calls no
+ * cudaMalloc / cudaFree and no allocating library routine.
+ * Limits: batch * m * n <= 1,048,576 output elements, k >= 1, f32 operands
+ * that TMA can describe (16-byte aligned starts and rows); beyond them the
+ * call returns ST_UNSUPPORTED_SHAPE (bad arguments: ST_INVALID_ARG) and
+ * launches nothing.  Errors are reported by the return value only
+ * (st_last_error is not updated).  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the one array and it keeps the last
+ * call's contents: calls that overlap on the GPU (other streams, other host
+ * threads) race on it.
+ * This entry point has no counterpart in the reference. */
+ST_API st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out,
+                                            int64_t batch, int64_t m, int64_t k, int64_t n, const st_epilogue *epi);
+
 /* NdArray::matmul with host buffers (src/tensor.rs:241 and the drop-in
  * gpu_matmul, src/gpu.rs:98-169): out[m, n] = op(a) . op(b), row-major host
  * f32, ta: a stored [k, m], tb: b stored [n, k].  Copies in, computes,

@@ -14,6 +14,7 @@
 //  * k_gemm_exact: SIMT, each output a k-ascending chain of f32 multiply then
 //    add starting from 0 (no FMA) -- the same bits as NdArray::matmul.
 #include <algorithm>
+#include <mutex>
 
 #include "st_internal.h"
 #include "st_ptx.cuh"
@@ -620,4 +621,160 @@ extern "C" st_status st_matmul_host(st_handle *h, const float *a, const float *b
     if (s != ST_OK) return s;
     ST_CHECK_CUDA(h, cudaMemcpyAsync(out, dc, cb, cudaMemcpyDeviceToHost, h->stream));
     return st_sync(h);
+}
+
+// ---------------------------------------------------------------------------
+// st_gemm_tf32_fixed_scratch: the TF32 GEMM for callers that cannot let this
+// library allocate device memory.
+//
+// st_gemm keeps its split-k partial sums in the handle's scratch pool, which
+// grows with cudaMalloc the first time a larger problem comes along.  Some
+// callers cannot accept that: a host program that has already carved the
+// GPU's memory into its own pools and lends none to plug-ins, or a
+// latency-critical loop in which a cudaMalloc / cudaFree (which may
+// synchronise the whole device) would stall it.  This entry point computes the
+// same result as st_gemm with ST_PREC_TF32 but takes its partial sums from one
+// array compiled into the library, so the call itself never allocates.
+//
+// The array is FIXED_SCRATCH_FLOATS floats (8 MiB); every GPU that loads the
+// library holds it until the process exits.  All calls share it, and it keeps
+// whatever the last call left in it, so two calls that overlap on the GPU (on
+// different streams, or from different host threads) race on it.  Nothing in
+// it has to start at zero: every split writes each element of its partial
+// before the reduction reads it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t FIXED_SCRATCH_FLOATS = 2 * 1024 * 1024;      // 8 MiB of f32 partial sums
+constexpr int64_t FIXED_MAX_OUTPUT = FIXED_SCRATCH_FLOATS / 2;  // room for at least two splits
+
+static __device__ __align__(256) float g_fixed_partials[FIXED_SCRATCH_FLOATS];
+
+constexpr int FIXED_MAX_DEVICES = 64;
+float *g_fixed_ptr[FIXED_MAX_DEVICES] = {};
+std::mutex g_fixed_mu;
+
+// The device address of g_fixed_partials on `device` (which must be current).
+// Looked up once per device; in host code the symbol itself is only a host
+// stand-in and must never be handed to a kernel.
+float *fixed_scratch(int device) {
+    if (device < 0 || device >= FIXED_MAX_DEVICES) return nullptr;
+    std::lock_guard<std::mutex> lock(g_fixed_mu);
+    if (!g_fixed_ptr[device]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_fixed_partials) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        g_fixed_ptr[device] = static_cast<float *>(p);
+    }
+    return g_fixed_ptr[device];
+}
+
+}  // namespace
+
+extern "C" st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out,
+                                                int64_t batch, int64_t m, int64_t k, int64_t n,
+                                                const st_epilogue *epi) {
+    if (!h || !a || !b || !out || !a->ptr || !b->ptr || !out->ptr) return ST_INVALID_ARG;
+    if (batch < 1 || m < 1 || n < 1 || k < 1 || !fits_i32(m) || !fits_i32(n) || !fits_i32(k) || batch > 65535)
+        return ST_INVALID_ARG;
+    if (out->trans || a->off < 0 || b->off < 0 || out->off < 0 || a->ld < 0 || b->ld < 0 || out->ld < 0)
+        return ST_INVALID_ARG;
+    if (a->dtype != ST_F32 || b->dtype != ST_F32 || out->dtype != ST_F32) return ST_UNSUPPORTED_SHAPE;
+    if (batch * m * n > FIXED_MAX_OUTPUT) return ST_UNSUPPORTED_SHAPE;  // output beyond the fixed scratch
+    if (cudaSetDevice(h->device) != cudaSuccess) return ST_CUDA_ERROR;
+    float *scratch = fixed_scratch(h->device);
+    if (!scratch) return ST_CUDA_ERROR;
+
+    const Operand A = to_operand(a, a->trans ? m : k);
+    const Operand B = to_operand(b, b->trans ? k : n);
+    st_epilogue e{};
+    if (epi) e = *epi;
+    GemmArgs g{};
+    g.M = static_cast<int>(m);
+    g.N = static_cast<int>(n);
+    g.K = static_cast<int>(k);
+    g.batch = static_cast<int>(batch);
+    g.c = static_cast<float *>(out->ptr);
+    g.c_off = out->off;
+    g.c_stride = out->stride;
+    g.c_inner = out->inner;
+    g.c_ld = out->ld ? out->ld : n;
+    g.c_grp = out->group > 0 ? out->group : 1;
+    g.bias = e.bias;
+    g.bias_off = e.bias_off;
+    g.bias_stride = e.bias_stride;
+    g.mask = e.mask;
+    g.mask_off = e.mask_off;
+    g.residual = e.residual;
+    g.residual_off = e.residual_off;
+    g.relu = e.relu;
+    g.accumulate = e.accumulate;
+    g.status = h->d_status;
+    {
+        auto al16 = [](const void *p, int64_t off) {
+            return (reinterpret_cast<uintptr_t>(p) + static_cast<uintptr_t>(off) * 4) % 16 == 0;
+        };
+        bool v = (n % 4 == 0) && (g.c_ld % 4 == 0) && al16(g.c, g.c_off);
+        if (batch > 1) v = v && (g.c_stride % 4 == 0) && (g.c_grp == 1 || g.c_inner % 4 == 0);
+        if (g.mask) v = v && al16(g.mask, g.mask_off);
+        if (g.residual) v = v && al16(g.residual, g.residual_off);
+        g.vec = v ? 1 : 0;
+    }
+
+    const int64_t m_tiles = (m + BM - 1) / BM;
+    if (m_tiles > 65535) return ST_UNSUPPORTED_SHAPE;
+    const int64_t tiles128 = m_tiles * ((n + 127) / 128) * batch;
+    const int BN = (n > 64 && (tiles128 >= h->num_sms || tiles128 * 8 <= h->num_sms)) ? 128 : 64;
+    const bool a_mn = a->trans != 0, b_mn = b->trans == 0;
+    CUtensorMap ma, mb;
+    const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    const bool okA = a_mn ? operand_map(&ma, A, batch, k, m, 32, 32, mnmaj, nullptr)
+                          : operand_map(&ma, A, batch, m, k, 32, BM, kmaj, nullptr);
+    const bool okB = okA && (b_mn ? operand_map(&mb, B, batch, k, n, 32, 32, mnmaj, nullptr)
+                                  : operand_map(&mb, B, batch, n, k, 32, static_cast<uint32_t>(BN), kmaj, nullptr));
+    if (!okA || !okB) return ST_UNSUPPORTED_SHAPE;  // needs TMA-describable (16-byte aligned) operands
+    g.a_grp = A.grp > 1 ? A.grp : 1;
+    g.a_outer = A.stride != 0;
+    g.b_grp = B.grp > 1 ? B.grp : 1;
+    g.b_outer = B.stride != 0;
+
+    // The split plan of st_gemm, capped so the partials fit the fixed array.
+    const int kb_total = static_cast<int>((k + BK - 1) / BK);
+    const int64_t tiles = m_tiles * ((n + BN - 1) / BN) * batch;
+    int splits = 1;
+    if (tiles * 2 <= h->num_sms && kb_total >= 8)
+        splits = static_cast<int>(std::min<int64_t>(std::min<int64_t>(h->num_sms / tiles, kb_total / 4), 16));
+    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, FIXED_SCRATCH_FLOATS / (batch * m * n))));
+    int kbps = (kb_total + splits - 1) / splits;
+    splits = (kb_total + kbps - 1) / kbps;
+    if (batch * splits > 65535) {
+        splits = 1;
+        kbps = kb_total;
+    }
+    g.splits = splits;
+    g.kb_per_split = kbps;
+    g.partial = splits > 1 ? scratch : nullptr;
+
+    if (e.col_sum) {
+        const int64_t total = batch * n;
+        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+        k_col_sum<<<blocks, 256, 0, h->stream>>>(B, g.K, g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
+        if (cudaGetLastError() != cudaSuccess) return ST_CUDA_ERROR;
+    }
+    dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
+              static_cast<unsigned>(batch * splits));
+    const st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, g, grid)
+                                 : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, g, grid);
+    if (s != ST_OK) return s;
+    if (splits > 1) {
+        const int groups = static_cast<int>((n + 3) / 4);
+        const int threads = groups >= 128 ? 128 : 32 * ((groups + 31) / 32);
+        dim3 rgrid(static_cast<unsigned>((groups + threads - 1) / threads),
+                   static_cast<unsigned>(std::min<int64_t>(m, 65535)), static_cast<unsigned>(batch));
+        k_splitk_reduce<<<rgrid, threads, 0, h->stream>>>(g);
+        if (cudaGetLastError() != cudaSuccess) return ST_CUDA_ERROR;
+    }
+    return ST_OK;
 }
