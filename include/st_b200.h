@@ -165,6 +165,61 @@ ST_API st_status st_softmax_rows(st_handle *h, const float *x, float *y, int64_t
 ST_API st_status st_softmax_rows_bwd(st_handle *h, const float *dy, const float *y, float *dx, int64_t rows, int64_t n,
                               float scale);
 
+/* ---- kNN memory: 2-bit key scan fused with top-k ------------------------- */
+
+/* Ranking modes (src/gpu_step/knn.rs:5, :522-532, :855).
+ * DOT: q.k, largest first.  L2: |k|^2 - 2 q.k + |q|^2 clamped at 0,
+ * smallest first.  Ties go to the lower key index. */
+typedef enum { ST_KNN_DOT = 0, ST_KNN_L2 = 1 } st_knn_mode;
+/* Arithmetic.  EXACT: the query is split into two f16 parts (power-of-two
+ * prescaled), the codes c = 2u - 3 are exact, f32 accumulation on tcgen05:
+ * error about 2^-22 of sum_i |q_i k_i|.  F16REF: the reference's numerics --
+ * query and dequantised key (u - 1.5) * scale rounded to f16 before the
+ * product (knn.rs:403-411, :630-643). */
+typedef enum { ST_KNN_EXACT = 0, ST_KNN_F16REF = 1 } st_knn_prec;
+
+/* The best k (1..128) keys per query.  codes: device [n_keys, dim/4] bytes,
+ * 2-bit codes packed low bits first (16-byte aligned); scales: device f32
+ * [n_keys]; queries: device f32 [nq, dim] (16-byte aligned); dim in {64, 128,
+ * 192, 256}.  out_scores: device f32 [nq, k] (DOT: q.k; L2: distance);
+ * out_ids: device int64 [nq, k] = index_base + key row, best first; missing
+ * entries (fewer than k keys) are (-inf or +inf, -1).  index_base + n_keys
+ * must stay below 2^32 - 1.  Replaces KnnStore::search / search_tagged and
+ * the search_from / search_block path (src/gpu_step/knn.rs:264-331,
+ * :401-535), with indices returned instead of values. */
+ST_API st_status st_knn_search(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
+                               const float *queries, int64_t nq, int32_t k, int32_t mode, int32_t prec,
+                               int64_t index_base, float *out_scores, int64_t *out_ids);
+/* The same scan, stopping before decoding: out_keys, device u64 [nq, 128],
+ * holds each query's best 128 as sortable 64-bit keys (score bits << 32 |
+ * 0xFFFFFFFF - index), best first, 0 = empty.  Keys of different shards (each
+ * with its own index_base) merge with st_knn_merge_keys -- the multi-GPU path
+ * gathers them over NCCL first.  Replaces k_sort_lists + k_merge_parts
+ * (src/gpu_step/knn.rs:661-715) across shards. */
+ST_API st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                  int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
+                                  int64_t index_base, uint64_t *out_keys);
+/* out_keys[q] = best 128 of lists[l * list_stride + q * 128 + r] over
+ * l < n_lists (device u64), best first. */
+ST_API st_status st_knn_merge_keys(st_handle *h, const uint64_t *lists, int64_t n_lists, int64_t list_stride,
+                                   int64_t nq, uint64_t *out_keys);
+/* Keys [nq, 128] -> out_scores [nq, k], out_ids [nq, k] as st_knn_search
+ * returns them (queries as given to the scan). */
+ST_API st_status st_knn_decode(st_handle *h, const uint64_t *keys, const float *queries, int64_t nq, int32_t dim,
+                               int32_t k, int32_t mode, int32_t prec, float *out_scores, int64_t *out_ids);
+/* The 2-bit quantiser of KnnStore::add (tile_of, src/gpu_step/knn.rs:190-221,
+ * quant_step :647-653) on the device, bit-identical to the reference's f32
+ * arithmetic: keys device f32 [n, dim] -> codes [n, dim/4], scales [n],
+ * norms [n] (sum of f16-rounded squares; may be NULL). */
+ST_API st_status st_knn_quantize(st_handle *h, const float *keys, int64_t n, int32_t dim, uint8_t *codes,
+                                 float *scales, float *norms);
+/* Synthetic keys (benchmark and tests): codes uniform on 0..3 and scale =
+ * |N(0,1)|, from a counter-based hash of (seed, first_key + row), so each
+ * shard makes its own rows independently.  No reference counterpart (the
+ * reference builds keys from trained hidden states). */
+ST_API st_status st_knn_synth_keys(st_handle *h, uint8_t *codes, float *scales, int64_t n, int32_t dim, uint64_t seed,
+                                   int64_t first_key);
+
 #ifdef __cplusplus
 }
 #endif

@@ -22,6 +22,9 @@ STATUS_NAMES = ["OK", "INVALID_ARG", "UNSUPPORTED_SHAPE", "CUDA_ERROR", "NCCL_ER
                 "NOT_FOUND"]
 ST_F32, ST_F16, ST_BF16 = 0, 1, 2
 PREC_F32_EXACT, PREC_TF32 = 0, 1
+KNN_DOT, KNN_L2 = 0, 1
+KNN_EXACT, KNN_F16REF = 0, 1
+KNN_KMAX = 128
 
 
 class StMat(ctypes.Structure):
@@ -61,6 +64,12 @@ SIGNATURES = {
     "st_matmul_host": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_int]),
     "st_softmax_rows": (_st, [_h, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),
+    "st_knn_search": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp]),
+    "st_knn_topk_keys": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i64, _vp]),
+    "st_knn_merge_keys": (_st, [_h, _vp, _i64, _i64, _i64, _vp]),
+    "st_knn_decode": (_st, [_h, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "st_knn_quantize": (_st, [_h, _vp, _i64, _i32, _vp, _vp, _vp]),
+    "st_knn_synth_keys": (_st, [_h, _vp, _vp, _i64, _i32, ctypes.c_uint64, _i64]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

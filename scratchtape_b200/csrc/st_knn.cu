@@ -1,0 +1,871 @@
+// st_knn.cu -- the kNN memory's 2-bit key scan, fused with top-k selection.
+//
+// Reference: KnnStore (src/gpu_step/knn.rs).  Keys are stored as the
+// reference stores them (knn.rs:190-221): per key, d/4 bytes of 2-bit codes u
+// packed low bits first, and one f32 scale; the dequantised key is
+// k[i] = (u_i - 1.5) * scale (k_dequant, knn.rs:630-643).  A search returns,
+// per query, the k best keys by
+//   DOT: q.k, largest first, or
+//   L2:  |k|^2 - 2 q.k + |q|^2 clamped at 0, smallest first (knn.rs:5,
+//        :522-532, :855),
+// ties broken by the lower key index.  Two arithmetics:
+//   EXACT:  c_i = 2u_i - 3 in {-3,-1,1,3} is exact in f16.  Each query is
+//           scaled by a power of two 2^e (max|q| into [2^14, 2^15)) and split
+//           into f16 hi + lo parts (~22 significant bits); the tensor core
+//           accumulates hi.c + lo.c in f32 and the epilogue multiplies by
+//           scale/2.  Error ~2^-22 of sum|q_i||k_i|.
+//   F16REF: the reference's numerics: query and dequantised key rounded to
+//           f16 (knn.rs:403-411, :630-643), products accumulated in f32.
+//
+// k_knn_scan is one persistent CTA per SM.  A unit of work is (block of 128
+// queries, contiguous key split); a CTA loops over units round-robin, so the
+// 32-odd CTAs that share a key split run together and share it through L2.
+// Per CTA:
+//   warps 5-8 (producers): load the unit's queries (f32 -> f16 hi/lo,
+//     128-byte swizzled, K-major) once; then per 256-key tile load the 2-bit
+//     codes from HBM and expand them in registers (byte -> prmt selector LUT)
+//     into f16 K-major swizzled shared memory, 64 dims per stage; per-key
+//     factors (scale/2, |k|^2) go to a small double buffer.
+//   warp 4 (one thread): tcgen05.mma kind::f16, M=128 queries x N=256 keys
+//     x K=16, accumulating in TMEM; two 256-column accumulators (all 512
+//     columns) so the epilogue of tile t overlaps the MMAs of tile t+1.
+//   warps 0-3 (epilogue): thread = query = TMEM lane.  tcgen05.ld 32 columns
+//     at a time, score = f(dot, key factors), and a running threshold: a key
+//     enters the query's candidate buffer (global, 1024 entries) only when it
+//     is at least as good as the current 128th best.  A full buffer is cut
+//     back to its best 128 by a warp-cooperative exact select (bitwise
+//     radix over 64-bit keys); at the end of a unit the best 128 are written
+//     out.  Inserts are rare after the first tiles, so the scan runs at the
+//     tensor core's pace.
+// k_knn_merge then merges the per-split lists of each query (exact: the
+// global best k is inside the union of the per-split best k), and
+// k_knn_decode turns 64-bit keys back into scores and indices.
+//
+// A candidate is one 64-bit key: (order-preserving bits of the score << 32)
+// | (0xFFFFFFFF - key index), so "larger key" = better score, then lower index.
+// Scores inside the kernel are "larger is better" in every mode; L2 uses
+// 2 q.k - |k|^2 and adds |q|^2 only when decoding.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "st_internal.h"
+#include "st_ptx.cuh"
+
+namespace {
+
+constexpr int KQ = 128;          // queries per unit (MMA M = TMEM lanes)
+constexpr int KT = 256;          // keys per tile (MMA N)
+constexpr int KSTAGES = 2;       // 64-dim key stages in flight
+constexpr int KTOP = 128;        // best entries kept per query and unit
+constexpr int KCAP = 1024;       // candidate buffer entries per query
+constexpr int KMAXD = 256;
+constexpr int QCH_BYTES = KQ * 128;  // one 64-dim chunk of 128 queries, f16
+constexpr int KCH_BYTES = KT * 128;  // one 64-dim chunk of 256 keys, f16
+constexpr int Q_BYTES = 2 * (KMAXD / 64) * QCH_BYTES;  // hi and lo limbs
+constexpr int OFF_K = Q_BYTES;
+constexpr int OFF_KF = OFF_K + KSTAGES * KCH_BYTES;        // [2][256] f32: scale/2
+constexpr int OFF_KN = OFF_KF + 2 * KT * 4;                // [2][256] f32: |k|^2
+constexpr int OFF_LUT = OFF_KN + 2 * KT * 4;               // [256] u32 prmt selectors
+constexpr int OFF_BAR = OFF_LUT + 256 * 4;
+constexpr int NBARS = 2 * KSTAGES + 2 + 2 + 2 + 3;        // full, empty, accf, acce, kfr, qfull, qfree, fin
+constexpr int OFF_MISC = OFF_BAR + NBARS * 8;              // tmem slot, abort flag
+constexpr int KNN_SMEM = OFF_MISC + 16 + 1024;             // + alignment slack
+constexpr int KNN_THREADS = 288;                           // 9 warps
+constexpr uint32_t TMEM_COLS = 512;
+
+static_assert(KNN_SMEM <= 232448, "kNN scan shared memory exceeds the sm_100 limit");
+
+enum { MODE_DOT = 0, MODE_L2 = 1 };
+enum { PREC_EXACT = 0, PREC_F16REF = 1 };
+
+struct ScanArgs {
+    const uint8_t *codes;  // [n_keys, d/4]
+    const float *scales;   // [n_keys]
+    const float *q;        // [nq, d]
+    int64_t n_keys;
+    int d, nq, nq_pad, nqb, splits;
+    int64_t tiles_per_split;
+    uint32_t index_base;
+    uint64_t *cbuf;      // [gridDim.x * 128][KCAP]
+    uint64_t *unit_out;  // [splits][nq_pad][KTOP]
+    int *status;
+};
+
+__device__ __forceinline__ uint32_t ord_f32(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unord_f32(uint32_t o) {
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+__device__ __forceinline__ uint64_t make_key(float s, uint32_t idx) {
+    return (static_cast<uint64_t>(ord_f32(s)) << 32) | static_cast<uint64_t>(0xffffffffu - idx);
+}
+
+// Power-of-two exponent e with max|q| * 2^e in [2^14, 2^15) (0 for an all-zero
+// query), clamped so that 2^e and 2^(e-1) are normal floats.
+__device__ __forceinline__ int query_exp(float maxabs) {
+    if (!(maxabs > 0.0f)) return 0;
+    const int biased = static_cast<int>((__float_as_uint(maxabs) >> 23) & 0xff);
+    const int ex = biased == 0 ? -126 : biased - 126;  // maxabs < 2^ex
+    return max(-100, min(100, 15 - ex));
+}
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Bounded mbarrier wait shared by every role of the scan: gives up after the
+// time limit, or at once when another thread of the CTA has given up.
+__device__ __forceinline__ bool kwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                      int code) {
+    if (st::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = st::globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (st::mbar_try_wait(bar, parity)) return true;
+        if ((i & 127u) == 0) {
+            if (*abort_flag) return false;
+            if (st::globaltimer() - t0 > st::WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                st::set_status(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Exact k-th largest of the warp's 1024 keys (v[i] of lane l is entry
+// i*32+l; absent entries are 0 and never counted): the largest value T with
+// #{v >= T} >= k, found bit by bit from the top.
+__device__ __forceinline__ uint64_t warp_kth_largest(const uint64_t (&v)[32], int k) {
+    uint64_t prefix = 0;
+#pragma unroll 1
+    for (int bit = 63; bit >= 0; --bit) {
+        const uint64_t cand = prefix | (1ull << bit);
+        int c = 0;
+#pragma unroll
+        for (int i = 0; i < 32; i++) c += v[i] >= cand ? 1 : 0;
+        if (warp_sum(c) >= k) prefix = cand;
+    }
+    return prefix;
+}
+
+// For every lane of this warp flagged in `need`: load its candidate buffer
+// (cnt entries), keep its best KTOP (all, if fewer), and write them either
+// back to the buffer front (dst_rows == nullptr) or to the lane's output row.
+// Updates the lane's count and threshold.
+__device__ void warp_compact(unsigned need, uint64_t *my_buf, int &cnt, float &thr, uint64_t *my_out, bool final) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();  // every lane's buffer writes are visible to the others
+    while (need) {
+        const int L = __ffs(need) - 1;
+        need &= need - 1;
+        const int n = __shfl_sync(0xffffffffu, cnt, L);
+        const uint64_t *src = reinterpret_cast<const uint64_t *>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_buf), L));
+        uint64_t *dst = final ? reinterpret_cast<uint64_t *>(
+                                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_out), L))
+                              : const_cast<uint64_t *>(src);
+        uint64_t v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int idx = i * 32 + lane;
+            v[i] = idx < n ? __ldcg(src + idx) : 0ull;
+        }
+        const uint64_t T = n > KTOP ? warp_kth_largest(v, KTOP) : 0ull;
+        __syncwarp();
+        int base = 0;
+        const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const bool keep = v[i] != 0ull && v[i] >= T;
+            const unsigned m = __ballot_sync(0xffffffffu, keep);
+            if (keep) dst[base + __popc(m & lt)] = v[i];
+            base += __popc(m);
+        }
+        if (final)
+            for (int p = base + lane; p < KTOP; p += 32) dst[p] = 0ull;
+        __syncwarp();
+        if (lane == L) {
+            cnt = base;
+            if (n > KTOP) thr = unord_f32(static_cast<uint32_t>(T >> 32));
+        }
+    }
+}
+
+__device__ __forceinline__ void key_tile_range(const ScanArgs &g, int split, int64_t &k0, int64_t &k1) {
+    k0 = static_cast<int64_t>(split) * g.tiles_per_split * KT;
+    k1 = min(g.n_keys, k0 + g.tiles_per_split * KT);
+}
+
+// Codes (d/4 bytes, zero-padded to 64) and scale of keys tb+pt and tb+pt+128
+// when they lie below k1; zeros otherwise.
+__device__ __forceinline__ void load_key_codes(const ScanArgs &g, int64_t tb, int64_t k1, int pt, int nchunks,
+                                               uint4 (&cw)[2][4], float (&sk)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int64_t key = tb + pt + 128 * h;
+        const bool in = key < k1;
+        const uint4 *src = reinterpret_cast<const uint4 *>(g.codes + key * (g.d / 4));
+#pragma unroll
+        for (int j = 0; j < 4; j++) cw[h][j] = (in && j < nchunks) ? __ldg(src + j) : make_uint4(0u, 0u, 0u, 0u);
+        sk[h] = in ? __ldg(g.scales + key) : 0.0f;
+    }
+}
+
+template <int MODE, int PREC>
+__global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *kf = reinterpret_cast<float *>(smem + OFF_KF);
+    float *kn = reinterpret_cast<float *>(smem + OFF_KN);
+    uint32_t *lut = reinterpret_cast<uint32_t *>(smem + OFF_LUT);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint64_t *full = bars, *empty = bars + KSTAGES, *accf = bars + 2 * KSTAGES, *acce = accf + 2, *kfr = acce + 2;
+    uint64_t *qfull = kfr + 2, *qfree = qfull + 1, *fin = qfree + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nchunks = g.d / 64;
+    const int units = g.nqb * g.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KSTAGES; s++) {
+            st::mbar_init(&full[s], 128);
+            st::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            st::mbar_init(&accf[b], 1);
+            st::mbar_init(&acce[b], 128);
+            st::mbar_init(&kfr[b], 128);
+        }
+        st::mbar_init(qfull, 128);
+        st::mbar_init(qfree, 1);
+        st::mbar_init(fin, 1);
+        *abort_flag = 0;
+        st::fence_mbar_init();
+    }
+    if (warp == 4) {
+        st::tmem_alloc(tmem_slot, TMEM_COLS);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= 5) {
+        // ------------------------------------------------------------ producers
+        const int pt = threadIdx.x - 160;  // 0..127
+        const int pw = pt >> 5;
+        // byte of four codes -> two prmt selectors (codes 0,1 | codes 2,3)
+        for (int x = pt; x < 256; x += 128) {
+            uint32_t sel[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t u0 = (x >> (4 * h)) & 3u, u1 = (x >> (4 * h + 2)) & 3u;
+                sel[h] = (2u * u0) | ((2u * u0 + 1u) << 4) | ((2u * u1) << 8) | ((2u * u1 + 1u) << 12);
+            }
+            lut[x] = sel[0] | (sel[1] << 16);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        uint32_t lc = 0, gt = 0, ui = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ui) {
+            const int qb = unit % g.nqb, split = unit / g.nqb;
+            // queries of this unit: row r, lane = 8 dims
+            if (ui > 0 && !kwait(qfree, (ui - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+            for (int r = pw; r < KQ; r += 4) {
+                const int qi = qb * KQ + r;
+                float x[8];
+                const bool live = qi < g.nq && lane * 8 < g.d;
+                if (live) {
+                    const float4 *src = reinterpret_cast<const float4 *>(g.q + static_cast<int64_t>(qi) * g.d + lane * 8);
+                    const float4 a = __ldg(src), b = __ldg(src + 1);
+                    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+                    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) x[i] = 0.0f;
+                }
+                float m = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(x[i]));
+                m = warp_max(m);
+                const float sc = PREC == PREC_EXACT ? pow2f(query_exp(m)) : 1.0f;
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float a = x[2 * i] * sc, b = x[2 * i + 1] * sc;
+                    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+                    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+                    hi[i] = static_cast<uint32_t>(__half_as_ushort(ha)) | (static_cast<uint32_t>(__half_as_ushort(hb)) << 16);
+                    lo[i] = static_cast<uint32_t>(__half_as_ushort(la)) | (static_cast<uint32_t>(__half_as_ushort(lb)) << 16);
+                }
+                if (lane * 8 < g.d) {
+                    const int j = lane >> 3, c = lane & 7;
+                    const uint32_t off = st::sw128_offset(r, c);
+                    *reinterpret_cast<uint4 *>(smem + j * QCH_BYTES + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    if (PREC == PREC_EXACT)
+                        *reinterpret_cast<uint4 *>(smem + (nchunks + j) * QCH_BYTES + off) =
+                            make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                }
+            }
+            st::fence_proxy_async_smem();
+            st::mbar_arrive(qfull);
+
+            int64_t k0, k1;
+            key_tile_range(g, split, k0, k1);
+            uint4 nx_cw[2][4];
+            float nx_sk[2];
+            load_key_codes(g, k0, k1, pt, nchunks, nx_cw, nx_sk);
+            for (int64_t tb = k0; tb < k1 && ok; tb += KT, ++gt) {
+                const uint32_t b = gt & 1u, use = gt >> 1;
+                // the codes of this thread's two keys (rows pt and pt+128);
+                // the next tile's are loaded now, so their latency hides
+                // behind this tile's expansion
+                uint4 cw[2][4];
+                float sk[2];
+                int n3[2];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) cw[h][j] = nx_cw[h][j];
+                    sk[h] = nx_sk[h];
+                }
+                load_key_codes(g, tb + KT, k1, pt, nchunks, nx_cw, nx_sk);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    int c3 = 0;  // codes with |2u-3| = 3: the two bits of u are equal
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const uint32_t w[4] = {cw[h][j].x, cw[h][j].y, cw[h][j].z, cw[h][j].w};
+#pragma unroll
+                        for (int t = 0; t < 4; t++) c3 += __popc(~(w[t] ^ (w[t] >> 1)) & 0x55555555u);
+                    }
+                    // zero-filled words (absent keys or dims) count as equal bits:
+                    // take them back out
+                    n3[h] = tb + pt + 128 * h < k1 ? c3 - 64 * (4 - nchunks) : 0;
+                }
+                // per-key factors, once the epilogue is done with buffer b
+                if (use > 0 && !kwait(&acce[b], (use - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int row = pt + 128 * h;
+                    const float s = sk[h];
+                    float f, nrm;
+                    if (PREC == PREC_EXACT) {
+                        f = 0.5f * s;
+                        nrm = f * f * static_cast<float>(g.d + 8 * n3[h]);
+                    } else {
+                        const float h1 = __half2float(__float2half_rn(0.5f * s));
+                        const float h3 = __half2float(__float2half_rn(1.5f * s));
+                        f = 1.0f;
+                        nrm = static_cast<float>(g.d - n3[h]) * (h1 * h1) + static_cast<float>(n3[h]) * (h3 * h3);
+                    }
+                    kf[b * KT + row] = f;
+                    kn[b * KT + row] = nrm;
+                }
+                st::mbar_arrive(&kfr[b]);
+                // value table: f16 of code u at bytes 2u, 2u+1 of {thi:tlo}
+                uint32_t tlo[2], thi[2];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    if (PREC == PREC_EXACT) {
+                        tlo[h] = 0xBC00C200u;  // -1.0 | -3.0
+                        thi[h] = 0x42003C00u;  // 3.0 | 1.0
+                    } else {
+                        const float s = sk[h];
+                        const uint32_t v0 = __half_as_ushort(__float2half_rn(-1.5f * s));
+                        const uint32_t v1 = __half_as_ushort(__float2half_rn(-0.5f * s));
+                        const uint32_t v2 = __half_as_ushort(__float2half_rn(0.5f * s));
+                        const uint32_t v3 = __half_as_ushort(__float2half_rn(1.5f * s));
+                        tlo[h] = v0 | (v1 << 16);
+                        thi[h] = v2 | (v3 << 16);
+                    }
+                }
+                for (int j = 0; j < nchunks; j++, ++lc) {
+                    const uint32_t s = lc % KSTAGES;
+                    if (lc >= KSTAGES &&
+                        !kwait(&empty[s], ((lc / KSTAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *stage = smem + OFF_K + s * KCH_BYTES;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int row = pt + 128 * h;
+                        uint4 cj = cw[h][0];
+                        if (j == 1) cj = cw[h][1];
+                        if (j == 2) cj = cw[h][2];
+                        if (j == 3) cj = cw[h][3];
+                        const uint32_t w[4] = {cj.x, cj.y, cj.z, cj.w};
+#pragma unroll
+                        for (int c = 0; c < 8; c++) {
+                            const uint32_t half16 = (w[c >> 1] >> (16 * (c & 1))) & 0xffffu;
+                            const uint32_t s0 = lut[half16 & 0xffu], s1 = lut[half16 >> 8];
+                            uint4 o;
+                            o.x = __byte_perm(tlo[h], thi[h], s0 & 0xffffu);
+                            o.y = __byte_perm(tlo[h], thi[h], s0 >> 16);
+                            o.z = __byte_perm(tlo[h], thi[h], s1 & 0xffffu);
+                            o.w = __byte_perm(tlo[h], thi[h], s1 >> 16);
+                            *reinterpret_cast<uint4 *>(stage + st::sw128_offset(row, c)) = o;
+                        }
+                    }
+                    st::fence_proxy_async_smem();
+                    st::mbar_arrive(&full[s]);
+                }
+            }
+        }
+    } else if (warp == 4) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, KQ, KT);
+            uint32_t lc = 0, gt = 0, ui = 0;
+            bool ok = true;
+            for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ui) {
+                const int split = unit / g.nqb;
+                if (!kwait(qfull, ui & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+                st::tc_fence_after();
+                int64_t k0, k1;
+                key_tile_range(g, split, k0, k1);
+                for (int64_t tb = k0; tb < k1 && ok; tb += KT, ++gt) {
+                    const uint32_t b = gt & 1u, use = gt >> 1;
+                    if (use > 0 && !kwait(&acce[b], (use - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    st::tc_fence_after();
+                    const uint32_t acc = tmem + b * KT;
+                    for (int j = 0; j < nchunks; j++, ++lc) {
+                        const uint32_t s = lc % KSTAGES;
+                        if (!kwait(&full[s], (lc / KSTAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
+                            ok = false;
+                            break;
+                        }
+                        st::tc_fence_after();
+                        const uint32_t sb = st::smem_u32(smem + OFF_K + s * KCH_BYTES);
+                        const uint32_t sq = st::smem_u32(smem + j * QCH_BYTES);
+                        const uint32_t sl = st::smem_u32(smem + (nchunks + j) * QCH_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++) {
+                            const uint64_t bd = st::sdesc_sw128(sb + kk * 32, 16, 1024);
+                            st::umma_f16(acc, st::sdesc_sw128(sq + kk * 32, 16, 1024), bd, idesc,
+                                         (j > 0 || kk > 0) ? 1u : 0u);
+                            if (PREC == PREC_EXACT) st::umma_f16(acc, st::sdesc_sw128(sl + kk * 32, 16, 1024), bd, idesc, 1u);
+                        }
+                        st::umma_commit(&empty[s]);
+                    }
+                    if (!ok) break;
+                    st::umma_commit(&accf[b]);
+                }
+                st::umma_commit(qfree);
+            }
+            // wait for every MMA issued above before the TMEM is released
+            st::umma_commit(fin);
+            kwait(fin, 0, abort_flag, g.status, st::DEV_TIMEOUT_ACC);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int row = threadIdx.x;  // TMEM lane = query row within the unit
+        uint64_t *my_buf = g.cbuf + (static_cast<int64_t>(blockIdx.x) * KQ + row) * KCAP;
+        uint32_t gt = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+            const int qb = unit % g.nqb, split = unit / g.nqb;
+            const int qi = qb * KQ + row;
+            const bool qlive = qi < g.nq;
+            float qf = 0.0f;  // 2^(e-1): L2's |k|^2 term in the query's scaled units
+            if (MODE == MODE_L2 && PREC == PREC_EXACT && qlive) {
+                const float4 *src = reinterpret_cast<const float4 *>(g.q + static_cast<int64_t>(qi) * g.d);
+                float m = 0.0f;
+                for (int i = 0; i < g.d / 4; i++) {
+                    const float4 a = __ldg(src + i);
+                    m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+                }
+                qf = pow2f(query_exp(m) - 1);
+            }
+            int cnt = 0;
+            float thr = -INFINITY;
+            int64_t k0, k1;
+            key_tile_range(g, split, k0, k1);
+            for (int64_t tb = k0; tb < k1; tb += KT, ++gt) {
+                const uint32_t b = gt & 1u, use = gt >> 1;
+                if (!kwait(&accf[b], use & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
+                    !kwait(&kfr[b], use & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+                    ok = false;
+                    break;
+                }
+                st::tc_fence_after();
+                const int ncols = static_cast<int>(k1 - tb < KT ? k1 - tb : KT);
+                const uint32_t base_idx = g.index_base + static_cast<uint32_t>(tb);
+                const float *kfb = kf + b * KT, *knb = kn + b * KT;
+#pragma unroll 1
+                for (int c0 = 0; c0 < ncols; c0 += 32) {
+                    uint32_t r[32];
+                    st::tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + b * KT + c0, r);
+                    st::tmem_ld_wait();
+                    const int lim = min(32, ncols - c0);
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++) {
+                        const int col = c0 + jj;
+                        const float dot = __uint_as_float(r[jj]);
+                        float s;
+                        if (MODE == MODE_DOT) {
+                            s = PREC == PREC_EXACT ? dot * kfb[col] : dot;
+                        } else {
+                            s = PREC == PREC_EXACT ? fmaf(-knb[col], qf, dot * kfb[col]) : fmaf(2.0f, dot, -knb[col]);
+                        }
+                        if (jj < lim && qlive && s >= thr) {
+                            my_buf[cnt] = make_key(s, base_idx + static_cast<uint32_t>(col));
+                            cnt++;
+                        }
+                    }
+                }
+                st::tc_fence_before();
+                st::mbar_arrive(&acce[b]);
+                const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - KT);
+                if (need) warp_compact(need, my_buf, cnt, thr, nullptr, false);
+            }
+            if (!ok) break;
+            uint64_t *my_out = g.unit_out + (static_cast<int64_t>(split) * g.nq_pad + qi) * KTOP;
+            const unsigned need = __ballot_sync(0xffffffffu, qlive);
+            if (need) warp_compact(need, my_buf, cnt, thr, my_out, true);
+        }
+    }
+
+    st::tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        st::tc_fence_after();
+        st::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Merge: out[q] = the best KTOP of lists l < n_lists, entries
+// lists[l * list_stride + q * KTOP + r], sorted best first (0 = empty).
+// One 256-thread CTA per query: an exact 8-bit-digit radix select of the
+// KTOP-th largest key, a gather of the keys at or above it, a rank sort.
+__global__ void __launch_bounds__(256) k_knn_merge(const uint64_t *lists, int64_t n_lists, int64_t list_stride,
+                                                   uint64_t *out) {
+    __shared__ int hist[256];
+    __shared__ uint64_t sel[KTOP];
+    __shared__ int s_digit, s_need, s_count;
+    const int64_t q = blockIdx.x;
+    const int64_t total = n_lists * KTOP;
+    auto at = [&](int64_t i) { return __ldg(lists + (i / KTOP) * list_stride + q * KTOP + (i % KTOP)); };
+    uint64_t prefix = 0, mask = 0;
+    int need = KTOP;
+    bool all = false;
+    for (int pass = 7; pass >= 0; --pass) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+            const uint64_t v = at(i);
+            if (v != 0ull && (v & mask) == prefix) atomicAdd(&hist[(v >> (8 * pass)) & 0xff], 1);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int acc = 0, d = -1;
+            for (int b = 255; b >= 0; --b) {
+                if (acc + hist[b] >= need) {
+                    d = b;
+                    break;
+                }
+                acc += hist[b];
+            }
+            s_digit = d;
+            s_need = d >= 0 ? need - acc : need;
+        }
+        __syncthreads();
+        if (s_digit < 0) {  // fewer than `need` candidates left: keep every nonzero key at or above the prefix
+            all = true;
+            break;
+        }
+        prefix |= static_cast<uint64_t>(s_digit) << (8 * pass);
+        mask |= 0xffull << (8 * pass);
+        need = s_need;
+        __syncthreads();
+    }
+    // T: the KTOP-th largest (or, with fewer candidates, the smallest admissible prefix)
+    const uint64_t T = all ? (prefix == 0 ? 1ull : prefix) : prefix;
+    if (threadIdx.x == 0) s_count = 0;
+    for (int i = threadIdx.x; i < KTOP; i += blockDim.x) sel[i] = 0ull;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+        const uint64_t v = at(i);
+        if (v != 0ull && v >= T) {
+            const int p = atomicAdd(&s_count, 1);
+            if (p < KTOP) sel[p] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < KTOP) {
+        const uint64_t v = sel[threadIdx.x];
+        int rank = 0;
+        for (int j = 0; j < KTOP; j++) rank += sel[j] > v ? 1 : 0;
+        // zeros all have the same rank; place them after the real keys
+        if (v == 0ull) {
+            int zeros_before = 0;
+            for (int j = 0; j < threadIdx.x; j++) zeros_before += sel[j] == 0ull ? 1 : 0;
+            rank += zeros_before;
+        }
+        out[q * KTOP + rank] = v;
+    }
+}
+
+// Keys -> (score, index).  DOT: q.k (EXACT divides out the query's 2^e);
+// L2: |q|^2 - (2 q.k - |k|^2), clamped at 0.  Empty slots: (-inf | +inf, -1).
+template <int MODE, int PREC>
+__global__ void __launch_bounds__(128) k_knn_decode(const uint64_t *keys, const float *qs, int d, int k,
+                                                    float *out_scores, int64_t *out_ids) {
+    const int64_t q = blockIdx.x;
+    __shared__ float s_qn, s_inv;
+    if (threadIdx.x < 32) {
+        const float *src = qs + q * d;
+        float m = 0.0f, ss = 0.0f;
+        for (int i = threadIdx.x; i < d; i += 32) {
+            m = fmaxf(m, fabsf(src[i]));
+            ss = fmaf(src[i], src[i], ss);
+        }
+        m = warp_max(m);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (threadIdx.x == 0) {
+            const int e = PREC == PREC_EXACT ? query_exp(m) : 0;
+            s_inv = MODE == MODE_DOT ? pow2f(-e) : pow2f(1 - e);
+            s_qn = ss;
+        }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < k; r += blockDim.x) {
+        const uint64_t key = keys[q * KTOP + r];
+        float sc;
+        int64_t id;
+        if (key == 0ull) {
+            sc = MODE == MODE_DOT ? -INFINITY : INFINITY;
+            id = -1;
+        } else {
+            id = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
+            const float s = unord_f32(static_cast<uint32_t>(key >> 32));
+            if (MODE == MODE_DOT) {
+                sc = PREC == PREC_EXACT ? s * s_inv : s;
+            } else {
+                const float t = PREC == PREC_EXACT ? s * s_inv : s;
+                sc = fmaxf(0.0f, s_qn - t);
+            }
+        }
+        out_scores[q * k + r] = sc;
+        out_ids[q * k + r] = id;
+    }
+}
+
+// tile_of's 2-bit quantiser (knn.rs:190-221, quant_step :647-653), one thread
+// per key, in the reference's f32 operation order: scale =
+// max(0.9957 * sqrt(sum(x*x) / d), 1e-30); u = clamp(round(x/scale + 1.5), 0, 3)
+// with round half away from zero; norm = sum of f16((u - 1.5) * scale)^2.
+__global__ void k_knn_quantize(const float *keys, int64_t n, int d, uint8_t *codes, float *scales, float *norms) {
+    for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float *x = keys + r * d;
+        float ss = 0.0f;
+        for (int i = 0; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+        float scale = __fmul_rn(0.9957f, __fsqrt_rn(__fdiv_rn(ss, static_cast<float>(d))));
+        if (!(scale >= 1e-30f)) scale = 1e-30f;
+        float nrm = 0.0f;
+        uint8_t *row = codes + r * (d / 4);
+        for (int i0 = 0; i0 < d; i0 += 4) {
+            uint32_t byte = 0;
+            for (int t = 0; t < 4; t++) {
+                float u = roundf(__fadd_rn(__fdiv_rn(x[i0 + t], scale), 1.5f));
+                u = fminf(fmaxf(u, 0.0f), 3.0f);
+                byte |= static_cast<uint32_t>(u) << (2 * t);
+                const float h = __half2float(__float2half_rn(__fmul_rn(__fsub_rn(u, 1.5f), scale)));
+                nrm = __fadd_rn(nrm, __fmul_rn(h, h));
+            }
+            row[i0 / 4] = static_cast<uint8_t>(byte);
+        }
+        scales[r] = scale;
+        if (norms) norms[r] = nrm;
+    }
+}
+
+// Synthetic keys for the benchmark and tests: codes uniform over 0..3 and
+// scale = |N(0,1)|, both from a counter-based hash of (seed, key), so any
+// shard can make its keys without the others.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+__global__ void k_knn_synth(uint8_t *codes, float *scales, int64_t n, int d, uint64_t seed, int64_t first) {
+    const int words = d / 32;  // 8-byte words of codes per key
+    for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < n;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t key = static_cast<uint64_t>(first + r);
+        const uint64_t base = mix64(seed ^ mix64(key));
+        uint64_t *dst = reinterpret_cast<uint64_t *>(codes + r * (d / 4));
+        for (int w = 0; w < words; w++) dst[w] = mix64(base + 1 + w);
+        const uint64_t h = mix64(base ^ 0x5bd1e995ull);
+        const float u1 = fmaxf(static_cast<float>((h >> 40) & 0xffffff) * (1.0f / 16777216.0f), 1e-9f);
+        const float u2 = static_cast<float>((h >> 16) & 0xffffff) * (1.0f / 16777216.0f);
+        scales[r] = fabsf(sqrtf(-2.0f * logf(u1)) * cosf(6.2831853f * u2));
+    }
+}
+
+template <int MODE, int PREC>
+st_status launch_scan(st_handle *h, const ScanArgs &g, int grid) {
+    auto kern = k_knn_scan<MODE, PREC>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KNN_SMEM));
+        attr_done = true;
+    }
+    kern<<<grid, KNN_THREADS, KNN_SMEM, h->stream>>>(g);
+    return st_after_launch(h, "k_knn_scan");
+}
+
+template <int MODE, int PREC>
+st_status launch_decode(st_handle *h, const uint64_t *keys, const float *q, int64_t nq, int d, int k, float *scores,
+                        int64_t *ids) {
+    k_knn_decode<MODE, PREC><<<static_cast<unsigned>(nq), 128, 0, h->stream>>>(keys, q, d, k, scores, ids);
+    return st_after_launch(h, "k_knn_decode");
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+st_status check_common(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
+                       const float *queries, int64_t nq, int32_t mode, int32_t prec, int64_t index_base,
+                       const char *who) {
+    if (!codes || !scales || !queries) return h->fail(ST_INVALID_ARG, "%s: null buffer", who);
+    if (dim < 64 || dim > KMAXD || dim % 64 != 0)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "%s: dim must be 64, 128, 192 or 256 (got %d)", who, dim);
+    if (n_keys < 1 || nq < 1 || nq > (1 << 24)) return h->fail(ST_INVALID_ARG, "%s: bad n_keys / nq", who);
+    if (index_base < 0 || index_base + n_keys >= 0xffffffffll)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "%s: key indices must stay below 2^32 - 1", who);
+    if ((mode != 0 && mode != 1) || (prec != 0 && prec != 1)) return h->fail(ST_INVALID_ARG, "%s: bad mode/prec", who);
+    if (!aligned16(codes) || !aligned16(queries))
+        return h->fail(ST_INVALID_ARG, "%s: codes and queries must be 16-byte aligned", who);
+    return ST_OK;
+}
+
+}  // namespace
+
+extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                      int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
+                                      int64_t index_base, uint64_t *out_keys) {
+    if (!h) return ST_INVALID_ARG;
+    st_status s = check_common(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, "st_knn_topk_keys");
+    if (s != ST_OK) return s;
+    if (!out_keys) return h->fail(ST_INVALID_ARG, "st_knn_topk_keys: null output");
+    cudaSetDevice(h->device);
+    const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
+    const int64_t tiles = (n_keys + KT - 1) / KT;
+    // about eight units per SM, every split non-empty
+    int64_t splits = std::max<int64_t>(1, (8LL * h->num_sms + nqb - 1) / nqb);
+    splits = std::min(splits, tiles);
+    const int64_t tps = (tiles + splits - 1) / splits;
+    splits = (tiles + tps - 1) / tps;
+    const int64_t units = splits * nqb;
+    const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
+    const int64_t nq_pad = static_cast<int64_t>(nqb) * KQ;
+
+    uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * KQ * KCAP));
+    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, sizeof(uint64_t) * splits * nq_pad * KTOP));
+    if (!cbuf || !unit_out) return ST_NO_MEMORY;
+
+    ScanArgs g{};
+    g.codes = codes;
+    g.scales = scales;
+    g.q = queries;
+    g.n_keys = n_keys;
+    g.d = dim;
+    g.nq = static_cast<int>(nq);
+    g.nq_pad = static_cast<int>(nq_pad);
+    g.nqb = nqb;
+    g.splits = static_cast<int>(splits);
+    g.tiles_per_split = tps;
+    g.index_base = static_cast<uint32_t>(index_base);
+    g.cbuf = cbuf;
+    g.unit_out = unit_out;
+    g.status = h->d_status;
+    if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT>(h, g, grid);
+    else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF>(h, g, grid);
+    else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT>(h, g, grid);
+    else s = launch_scan<MODE_L2, PREC_F16REF>(h, g, grid);
+    if (s != ST_OK) return s;
+    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, splits, nq_pad * KTOP, out_keys);
+    return st_after_launch(h, "k_knn_merge");
+}
+
+extern "C" st_status st_knn_merge_keys(st_handle *h, const uint64_t *lists, int64_t n_lists, int64_t list_stride,
+                                       int64_t nq, uint64_t *out_keys) {
+    if (!h) return ST_INVALID_ARG;
+    if (!lists || !out_keys || n_lists < 1 || nq < 1 || list_stride < nq * KTOP)
+        return h->fail(ST_INVALID_ARG, "st_knn_merge_keys: bad arguments");
+    cudaSetDevice(h->device);
+    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(lists, n_lists, list_stride, out_keys);
+    return st_after_launch(h, "k_knn_merge");
+}
+
+extern "C" st_status st_knn_decode(st_handle *h, const uint64_t *keys, const float *queries, int64_t nq, int32_t dim,
+                                   int32_t k, int32_t mode, int32_t prec, float *out_scores, int64_t *out_ids) {
+    if (!h) return ST_INVALID_ARG;
+    if (!keys || !queries || !out_scores || !out_ids || nq < 1 || dim < 1 || k < 1 || k > KTOP ||
+        (mode != 0 && mode != 1) || (prec != 0 && prec != 1))
+        return h->fail(ST_INVALID_ARG, "st_knn_decode: bad arguments (k must be 1..%d)", KTOP);
+    cudaSetDevice(h->device);
+    if (mode == 0 && prec == 0) return launch_decode<MODE_DOT, PREC_EXACT>(h, keys, queries, nq, dim, k, out_scores, out_ids);
+    if (mode == 0) return launch_decode<MODE_DOT, PREC_F16REF>(h, keys, queries, nq, dim, k, out_scores, out_ids);
+    if (prec == 0) return launch_decode<MODE_L2, PREC_EXACT>(h, keys, queries, nq, dim, k, out_scores, out_ids);
+    return launch_decode<MODE_L2, PREC_F16REF>(h, keys, queries, nq, dim, k, out_scores, out_ids);
+}
+
+extern "C" st_status st_knn_search(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                   int32_t dim, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                                   int32_t prec, int64_t index_base, float *out_scores, int64_t *out_ids) {
+    if (!h) return ST_INVALID_ARG;
+    if (k < 1 || k > KTOP) return h->fail(ST_INVALID_ARG, "st_knn_search: k must be 1..%d", KTOP);
+    if (!out_scores || !out_ids) return h->fail(ST_INVALID_ARG, "st_knn_search: null output");
+    uint64_t *keys = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_MISC, sizeof(uint64_t) * std::max<int64_t>(nq, 1) * KTOP));
+    if (!keys) return ST_NO_MEMORY;
+    st_status s = st_knn_topk_keys(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, keys);
+    if (s != ST_OK) return s;
+    return st_knn_decode(h, keys, queries, nq, dim, k, mode, prec, out_scores, out_ids);
+}
+
+extern "C" st_status st_knn_quantize(st_handle *h, const float *keys, int64_t n, int32_t dim, uint8_t *codes,
+                                     float *scales, float *norms) {
+    if (!h) return ST_INVALID_ARG;
+    if (!keys || !codes || !scales || n < 1 || dim < 4 || dim % 4 != 0)
+        return h->fail(ST_INVALID_ARG, "st_knn_quantize: bad arguments");
+    cudaSetDevice(h->device);
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 127) / 128, 65535));
+    k_knn_quantize<<<blocks, 128, 0, h->stream>>>(keys, n, dim, codes, scales, norms);
+    return st_after_launch(h, "k_knn_quantize");
+}
+
+extern "C" st_status st_knn_synth_keys(st_handle *h, uint8_t *codes, float *scales, int64_t n, int32_t dim,
+                                       uint64_t seed, int64_t first_key) {
+    if (!h) return ST_INVALID_ARG;
+    if (!codes || !scales || n < 1 || dim < 32 || dim % 32 != 0 || !aligned16(codes))
+        return h->fail(ST_INVALID_ARG, "st_knn_synth_keys: bad arguments");
+    cudaSetDevice(h->device);
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8 * 148 * 4));
+    k_knn_synth<<<blocks, 256, 0, h->stream>>>(codes, scales, n, dim, seed, first_key);
+    return st_after_launch(h, "k_knn_synth");
+}

@@ -1,0 +1,174 @@
+"""kNN memory over 2-bit keys on the device: the host mirror of KnnStore
+(src/gpu_step/knn.rs:114-331).
+
+Keys are held as the reference holds 2-bit keys (set_key_bits(2),
+knn.rs:142-145): per key d/4 bytes of codes u (low bits first) and one f32
+scale, dequantised as (u - 1.5) * scale.  Quantisation (tile_of,
+knn.rs:190-221) runs on the device with the reference's f32 arithmetic.  A
+search is one call of the fused scan + top-k kernel; results come back best
+first as (score, key index) -- and, when values were stored, the values.
+
+There is no CPU path: every method calls libst_b200.so.
+"""
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .device import handle, ptr
+
+MODES = {"dot": N.KNN_DOT, "l2": N.KNN_L2}
+PRECS = {"exact": N.KNN_EXACT, "f16": N.KNN_F16REF}
+KMAX = N.KNN_KMAX
+
+
+def _dev(device):
+    if device is None:
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device(device)
+
+
+def quantize(keys: torch.Tensor):
+    """tile_of's 2-bit quantiser on the device: keys f32 [n, d] ->
+    (codes u8 [n, d/4], scales f32 [n], norms f32 [n])."""
+    keys = keys.contiguous().float()
+    n, d = keys.shape
+    codes = torch.empty((n, d // 4), dtype=torch.uint8, device=keys.device)
+    scales = torch.empty(n, dtype=torch.float32, device=keys.device)
+    norms = torch.empty(n, dtype=torch.float32, device=keys.device)
+    handle(keys.device).call("st_knn_quantize", ptr(keys), n, d, ptr(codes), ptr(scales), ptr(norms))
+    return codes, scales, norms
+
+
+def synth_keys(n: int, d: int, seed: int, first_key: int = 0, device=None):
+    """Synthetic 2-bit keys: codes uniform on 0..3, scales |N(0,1)|, from a
+    counter hash of (seed, first_key + row)."""
+    device = _dev(device)
+    codes = torch.empty((n, d // 4), dtype=torch.uint8, device=device)
+    scales = torch.empty(n, dtype=torch.float32, device=device)
+    handle(device).call("st_knn_synth_keys", ptr(codes), ptr(scales), n, d, seed, first_key)
+    return codes, scales
+
+
+def search(codes: torch.Tensor, scales: torch.Tensor, queries: torch.Tensor, k: int = KMAX, mode: str = "l2",
+           prec: str = "exact", index_base: int = 0, out=None):
+    """The fused scan: best k keys per query.  Returns (scores f32 [nq, k],
+    ids int64 [nq, k]) on the device, best first (DOT: q.k; L2: distance)."""
+    queries = queries.contiguous().float()
+    nq, d = queries.shape
+    assert codes.shape[1] * 4 == d, "codes hold d/4 bytes per key"
+    if out is None:
+        out = (torch.empty((nq, k), dtype=torch.float32, device=queries.device),
+               torch.empty((nq, k), dtype=torch.int64, device=queries.device))
+    handle(queries.device).call("st_knn_search", ptr(codes), ptr(scales), codes.shape[0], d, ptr(queries), nq, k,
+                                MODES[mode], PRECS[prec], index_base, ptr(out[0]), ptr(out[1]))
+    return out
+
+
+def topk_keys(codes, scales, queries, mode="l2", prec="exact", index_base=0, out=None):
+    """The scan without decoding: sortable u64 keys [nq, 128] (as int64)."""
+    queries = queries.contiguous().float()
+    nq, d = queries.shape
+    if out is None:
+        out = torch.empty((nq, KMAX), dtype=torch.int64, device=queries.device)
+    handle(queries.device).call("st_knn_topk_keys", ptr(codes), ptr(scales), codes.shape[0], d, ptr(queries), nq,
+                                MODES[mode], PRECS[prec], index_base, ptr(out))
+    return out
+
+
+def merge_keys(lists: torch.Tensor, nq: int, out=None):
+    """Best 128 per query over lists [L, nq, 128] of sortable keys."""
+    lists = lists.contiguous()
+    n_lists = lists.shape[0]
+    if out is None:
+        out = torch.empty((nq, KMAX), dtype=torch.int64, device=lists.device)
+    handle(lists.device).call("st_knn_merge_keys", ptr(lists), n_lists, nq * KMAX, nq, ptr(out))
+    return out
+
+
+def decode(keys, queries, k=KMAX, mode="l2", prec="exact", out=None):
+    queries = queries.contiguous().float()
+    nq, d = queries.shape
+    if out is None:
+        out = (torch.empty((nq, k), dtype=torch.float32, device=queries.device),
+               torch.empty((nq, k), dtype=torch.int64, device=queries.device))
+    handle(queries.device).call("st_knn_decode", ptr(keys), ptr(queries), nq, d, k, MODES[mode], PRECS[prec],
+                                ptr(out[0]), ptr(out[1]))
+    return out
+
+
+class KnnStore:
+    """KnnStore (src/gpu_step/knn.rs:114-331) for 2-bit keys.
+
+    ``add(keys, vals)`` appends keys (row-major [n, d]) and their values;
+    ``finish()`` quantises pending keys on the device; ``search(queries, rows)``
+    returns, per query, the 128 nearest keys as (distance, value) sorted
+    ascending, like the reference (L2 with |q|^2 added, clamped at 0).
+    ``search_ids`` returns key indices instead, and ``mode="dot"`` ranks by
+    the dot product.
+    """
+
+    def __init__(self, d: int, tile: int = 16384, device=None):
+        if d % 64 != 0 or not 64 <= d <= 256:
+            raise ValueError("2-bit key scan supports d in {64, 128, 192, 256}")
+        self.d, self.tile = d, tile
+        self.device = _dev(device)
+        self.kbits = 2
+        self.codes = torch.empty((0, d // 4), dtype=torch.uint8, device=self.device)
+        self.scales = torch.empty(0, dtype=torch.float32, device=self.device)
+        self.norms = torch.empty(0, dtype=torch.float32, device=self.device)
+        self.vals = torch.empty(0, dtype=torch.int32, device=self.device)
+        self._pending = []
+        self._pending_vals = []
+
+    def set_key_bits(self, bits: int):
+        """Only 2-bit keys run on the fused scan (knn.rs:142-145)."""
+        if bits != 2 or len(self) != 0:
+            raise ValueError("this store holds 2-bit keys; set_key_bits(2) before the first add")
+        self.kbits = bits
+
+    def __len__(self):
+        return int(self.scales.shape[0]) + sum(int(p.shape[0]) for p in self._pending)
+
+    def add(self, keys, vals=None):
+        keys = torch.as_tensor(keys, dtype=torch.float32).reshape(-1, self.d)
+        self._pending.append(keys)
+        v = torch.zeros(keys.shape[0], dtype=torch.int32) if vals is None else torch.as_tensor(
+            np.asarray(vals), dtype=torch.int32).reshape(-1)
+        self._pending_vals.append(v)
+
+    def add_codes(self, codes: torch.Tensor, scales: torch.Tensor, vals=None):
+        """Appends already-quantised keys (codes [n, d/4], scales [n])."""
+        self.finish()
+        n = codes.shape[0]
+        norms = torch.zeros(n, dtype=torch.float32, device=self.device)
+        self.codes = torch.cat([self.codes, codes.to(self.device)])
+        self.scales = torch.cat([self.scales, scales.to(self.device)])
+        self.norms = torch.cat([self.norms, norms])
+        v = torch.zeros(n, dtype=torch.int32) if vals is None else torch.as_tensor(np.asarray(vals), dtype=torch.int32)
+        self.vals = torch.cat([self.vals, v.to(self.device)])
+
+    def finish(self):
+        if not self._pending:
+            return
+        keys = torch.cat(self._pending).to(self.device)
+        codes, scales, norms = quantize(keys)
+        self.codes = torch.cat([self.codes, codes])
+        self.scales = torch.cat([self.scales, scales])
+        self.norms = torch.cat([self.norms, norms])
+        self.vals = torch.cat([self.vals, torch.cat(self._pending_vals).to(self.device)])
+        self._pending, self._pending_vals = [], []
+
+    def search_ids(self, queries, rows: Optional[int] = None, k: int = KMAX, mode: str = "l2", prec: str = "exact"):
+        self.finish()
+        q = torch.as_tensor(queries, dtype=torch.float32).reshape(-1, self.d).to(self.device)
+        if rows is not None:
+            q = q[:rows]
+        return search(self.codes, self.scales, q, k=k, mode=mode, prec=prec)
+
+    def search(self, queries, rows: Optional[int] = None, mode: str = "l2", prec: str = "exact"):
+        """(distance or score, value) pairs, [rows, 128] each, best first."""
+        scores, ids = self.search_ids(queries, rows, KMAX, mode, prec)
+        vals = torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
+        return scores, vals
