@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "GEMM TFLOP/s & % of B200 peak per layout; kNN keys/s vs HBM; vs CPU tensor.rs"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 C2 = dict(m=32 * 128, d=128, dff=512)
+C5 = dict(keys=1 << 27, d=256, nq=4096, k=128)
 # dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the C2
 # step, averaged over its launches, from profiles/gemm_tf32_c2.md (ncu, 1 pass).
 C2_TRAFFIC_PER_LAUNCH = None
@@ -49,12 +50,19 @@ C2_TRAFFIC_PER_LAUNCH = None
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
-    p.add_argument("--warmup", type=int, default=20)
-    p.add_argument("--config", default="c2", choices=["c2"])
+    p.add_argument("--steps", type=int, default=None, help="timed steps (c2: 200, c5: 5)")
+    p.add_argument("--warmup", type=int, default=None, help="warm-up steps (c2: 20, c5: 3)")
+    p.add_argument("--config", default="c2", choices=["c2", "c5"])
+    p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
+    p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.steps is None:
+        a.steps = 5 if a.config == "c5" else 200
+    if a.warmup is None:
+        a.warmup = 3 if a.config == "c5" else 20
+    return a
 
 
 def load_peaks():
@@ -365,9 +373,222 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C5: kNN memory scoring, 4096 f32 queries (dim 256) against 2^27 2-bit keys,
+# top-128 per query.
+# ---------------------------------------------------------------------------
+C5_METRIC_UNIT = "keys/s"
+
+
+def c5_queries(n, d, seed=0):
+    rng = np.random.default_rng(seed + 1)
+    return rng.standard_normal((n, d)).astype(np.float32)
+
+
+def cpu_baseline_c5(prec, threads, sample_q=64, sample_keys=1 << 20):
+    """The oracle's brute force (f64, all given threads) on a sample: sample_q
+    queries against sample_keys synthetic keys; scaled to keys/s for a
+    4096-query batch."""
+    import oracle
+    rng = np.random.default_rng(7)
+    codes = rng.integers(0, 256, (sample_keys, C5["d"] // 4), dtype=np.uint8)
+    scales = np.abs(rng.standard_normal(sample_keys)).astype(np.float32)
+    q = c5_queries(sample_q, C5["d"])
+    t0 = time.perf_counter()
+    oracle.knn_topk(codes, scales, q, C5["k"], mode="dot", prec=prec, threads=threads)
+    el = time.perf_counter() - t0
+    return el, sample_keys * sample_q / C5["nq"] / el
+
+
+def run_reference_c5(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_baseline_c5(args.prec, threads, sample_q=8, sample_keys=1 << 16)
+    vals = []
+    for _ in range(args.steps):
+        _, v = cpu_baseline_c5(args.prec, threads, sample_q=32, sample_keys=1 << 18)
+        vals.append(v)
+    v = float(np.median(vals))
+    sample = ("per step 32 queries x 2^18 synthetic 2-bit keys, dim 256, top-128 by exact f64 dot product "
+              "(oracle brute force, %d threads); keys/s scaled to a 4096-query batch" % threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": C5_METRIC_UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": C5["keys"] / v * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "C5 kNN scoring: 4096 f32 queries x 2^27 2-bit keys, dim 256, top-128 (sampled)",
+                   "parallelism": "CPU, rank 0"},
+        "cpu_baseline": {"value": v, "unit": C5_METRIC_UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": C5_METRIC_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours_c5(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import scratchtape_b200 as st
+    import scratchtape_b200.knn as K
+
+    peaks, peak_src = load_peaks()
+    h = st.handle()
+    d, nq, k = C5["d"], C5["nq"], C5["k"]
+    n_total = args.keys
+    per = (n_total + world - 1) // world
+    first = rank * per
+    n_local = max(0, min(n_total, first + per) - first)
+    codes, scales = K.synth_keys(n_local, d, seed=1, first_key=first, device=device)
+    qh = c5_queries(nq, d)
+    q = torch.from_numpy(qh).to(device)
+    keys_local = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
+    gathered = torch.empty((world, nq, K.KMAX), dtype=torch.int64, device=device)
+    merged = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
+    out_s = torch.empty((nq, k), dtype=torch.float32, device=device)
+    out_i = torch.empty((nq, k), dtype=torch.int64, device=device)
+
+    def step(q_dev):
+        # local scan of this rank's shard -> exchange of the local top-128s -> merge -> decode
+        K.topk_keys(codes, scales, q_dev, mode="dot", prec=args.prec, index_base=first, out=keys_local)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, keys_local)
+            K.merge_keys(gathered, nq, out=merged)
+            K.decode(merged, q_dev, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+        else:
+            K.decode(keys_local, q_dev, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    n0 = h.launches
+    step(q)
+    torch.cuda.synchronize()
+    launches_per_step = h.launches - n0
+    for _ in range(max(0, args.warmup - 1)):
+        step(q)
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    scan_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local if world > 1 else torch.cuda.current_device(), period=0.05)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for i in range(args.steps):
+            starts[i].record()
+            scan_ev[i][0].record()
+            K.topk_keys(codes, scales, q, mode="dot", prec=args.prec, index_base=first, out=keys_local)
+            scan_ev[i][1].record()
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, keys_local)
+                K.merge_keys(gathered, nq, out=merged)
+                K.decode(merged, q, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+            else:
+                K.decode(keys_local, q, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in zip(starts, ends)))
+    scan_ms = float(np.mean([a.elapsed_time(b) for a, b in scan_ev]))
+    if world > 1:
+        t = torch.tensor([total_ms, scan_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, scan_ms = float(t[0].item()), float(t[1].item())
+    ms_per_step = total_ms / args.steps
+    value = n_total / (ms_per_step / 1e3)
+
+    # e2e through the public API: host queries in, host results out, every step
+    hq = torch.from_numpy(qh).pin_memory()
+    hs = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    hi = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    q2 = torch.empty_like(q)
+    e_ms = []
+    e2e_steps = max(2, min(args.steps, 5))
+    barrier()
+    for _ in range(e2e_steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        q2.copy_(hq, non_blocking=True)
+        step(q2)
+        hs.copy_(out_s, non_blocking=True)
+        hi.copy_(out_i, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        e_ms.append(e0.elapsed_time(e1))
+    e_total = float(sum(e_ms))
+    if world > 1:
+        t = torch.tensor([e_total], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_total = float(t.item())
+    e2e_value = n_total / (e_total / e2e_steps / 1e3)
+
+    flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
+    achieved = flops_alg / (scan_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    passes = 2 if args.prec == "exact" else 1
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": C5_METRIC_UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16x2-split (exact) / f32 accumulate" if passes == 2 else "f16",
+            "data": "synthetic",
+            "config": {"workload": "C5 kNN scoring (BASELINE configs[4]): 4096 f32 queries x 2^27 keys, dim 256, "
+                                   "2-bit codes {-3,-1,1,3} x per-key scale, exact dot-product scores, top-128 per "
+                                   "query; keys sharded evenly over GPUs, local top-128 all-gathered over NCCL and "
+                                   "merged",
+                       "keys": n_total, "queries": nq, "dim": d, "k": k, "prec": args.prec,
+                       "parallelism": "key-sharded x%d" % world if world > 1 else "single GPU",
+                       "l2": "inputs (%.1f GB of codes + scales) far larger than L2; no flush needed"
+                             % (n_total * (d / 4 + 4) / 1e9)},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": n_local * (d / 4 + 4) + nq * d * 4,
+                         "traffic_note": "algorithmic bytes per scan launch (codes + scales + queries); ncu DRAM "
+                                         "figures in profiles/knn_scan_c5.md",
+                         "peak_source": peak_src + " (bf16 dense, sustained)", "kernel": "k_knn_scan (+k_knn_merge)",
+                         "scan_ms": scan_ms, "tensor_passes": passes,
+                         "executed_tflops": achieved * passes,
+                         "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9},
+            "e2e": {"value": e2e_value, "unit": C5_METRIC_UNIT, "h2d_bytes_per_step": int(hq.numel() * 4),
+                    "d2h_bytes_per_step": int(hs.numel() * 4 + hi.numel() * 8), "ms_per_step": e_total / e2e_steps,
+                    "steps": e2e_steps,
+                    "api": "scratchtape_b200.knn.topk_keys/decode (st_knn_topk_keys/st_knn_decode) with the index "
+                           "resident in HBM; pinned host queries in, host scores/ids out"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            el, v = cpu_baseline_c5(args.prec if args.prec == "exact" else "f16", threads)
+            line["cpu_baseline"] = {"value": v, "unit": C5_METRIC_UNIT, "cores": threads, "kind": "port",
+                                    "sample": "64 queries x 2^20 synthetic keys, exact f64 brute force top-128 "
+                                              "(oracle, %d threads), %.1f s; keys/s scaled to a 4096-query batch"
+                                              % (threads, el)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.config == "c5":
+        if args.impl == "reference":
+            run_reference_c5(args)
+        else:
+            run_ours_c5(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

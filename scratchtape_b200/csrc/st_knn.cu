@@ -67,11 +67,15 @@ constexpr int OFF_K = Q_BYTES;
 constexpr int OFF_KF = OFF_K + KSTAGES * KCH_BYTES;        // [2][256] f32: scale/2
 constexpr int OFF_KN = OFF_KF + 2 * KT * 4;                // [2][256] f32: |k|^2
 constexpr int OFF_LUT = OFF_KN + 2 * KT * 4;               // [256] u32 prmt selectors
-constexpr int OFF_BAR = OFF_LUT + 256 * 4;
+constexpr int OFF_SLOT = OFF_LUT + 256 * 4;                // [NEPI][16] f32: scores of a step with hits
+constexpr int OFF_BAR = OFF_SLOT + 256 * 16 * 4;
 constexpr int NBARS = 2 * KSTAGES + 2 + 2 + 2 + 3;        // full, empty, accf, acce, kfr, qfull, qfree, fin
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;              // tmem slot, abort flag
 constexpr int KNN_SMEM = OFF_MISC + 16 + 1024;             // + alignment slack
-constexpr int KNN_THREADS = 288;                           // 9 warps
+constexpr int NEPI = 256;                                  // epilogue threads: warps 0-7
+constexpr int NPROD = 256;                                 // producer threads: warps 8-15, one key row each
+constexpr int MMA_WARP = (NEPI + NPROD) / 32;              // warp 16: TMEM owner, MMA issuer
+constexpr int KNN_THREADS = NEPI + NPROD + 32;             // 17 warps
 constexpr uint32_t TMEM_COLS = 512;
 
 static_assert(KNN_SMEM <= 232448, "kNN scan shared memory exceeds the sm_100 limit");
@@ -87,8 +91,8 @@ struct ScanArgs {
     int d, nq, nq_pad, nqb, splits;
     int64_t tiles_per_split;
     uint32_t index_base;
-    uint64_t *cbuf;      // [gridDim.x * 128][KCAP]
-    uint64_t *unit_out;  // [splits][nq_pad][KTOP]
+    uint64_t *cbuf;      // [gridDim.x * NEPI][KCAP]
+    uint64_t *unit_out;  // [splits * 2][nq_pad][KTOP]: one list per (split, column half)
     int *status;
 };
 
@@ -131,8 +135,8 @@ __device__ __forceinline__ bool kwait(uint64_t *bar, uint32_t parity, volatile i
     if (st::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = st::globaltimer();
     for (uint32_t i = 1;; ++i) {
-        if (st::mbar_try_wait(bar, parity)) return true;
-        if ((i & 127u) == 0) {
+        if (st::mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 7u) == 0) {
             if (*abort_flag) return false;
             if (st::globaltimer() - t0 > st::WAIT_LIMIT_NS) {
                 *abort_flag = 1;
@@ -143,10 +147,21 @@ __device__ __forceinline__ bool kwait(uint64_t *bar, uint32_t parity, volatile i
     }
 }
 
-// Exact k-th largest of the warp's 1024 keys (v[i] of lane l is entry
-// i*32+l; absent entries are 0 and never counted): the largest value T with
-// #{v >= T} >= k, found bit by bit from the top.
-__device__ __forceinline__ uint64_t warp_kth_largest(const uint64_t (&v)[32], int k) {
+// 16 consecutive f32 from shared memory (16-byte aligned address).
+__device__ __forceinline__ void lds_f32x16(uint32_t addr, float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v[4 * i]), "=f"(v[4 * i + 1]), "=f"(v[4 * i + 2]), "=f"(v[4 * i + 3])
+                     : "r"(addr + 16 * i));
+}
+
+// A threshold T over the warp's 1024 keys (v[i] of lane l is entry i*32+l;
+// absent entries are 0 and never counted) with exactly k keys >= T: the
+// largest prefix with #{v >= prefix} >= k, found bit by bit from the top and
+// stopped as soon as the count is exactly k (keys are distinct, so the full
+// 64-bit search ends at the k-th largest key, where the count is k).
+__device__ __forceinline__ uint64_t warp_select_threshold(const uint64_t (&v)[32], int k) {
     uint64_t prefix = 0;
 #pragma unroll 1
     for (int bit = 63; bit >= 0; --bit) {
@@ -154,7 +169,11 @@ __device__ __forceinline__ uint64_t warp_kth_largest(const uint64_t (&v)[32], in
         int c = 0;
 #pragma unroll
         for (int i = 0; i < 32; i++) c += v[i] >= cand ? 1 : 0;
-        if (warp_sum(c) >= k) prefix = cand;
+        c = warp_sum(c);
+        if (c >= k) {
+            prefix = cand;
+            if (c == k) break;
+        }
     }
     return prefix;
 }
@@ -181,7 +200,7 @@ __device__ void warp_compact(unsigned need, uint64_t *my_buf, int &cnt, float &t
             const int idx = i * 32 + lane;
             v[i] = idx < n ? __ldcg(src + idx) : 0ull;
         }
-        const uint64_t T = n > KTOP ? warp_kth_largest(v, KTOP) : 0ull;
+        const uint64_t T = n > KTOP ? warp_select_threshold(v, KTOP) : 0ull;
         __syncwarp();
         int base = 0;
         const unsigned lt = (1u << lane) - 1u;
@@ -207,19 +226,15 @@ __device__ __forceinline__ void key_tile_range(const ScanArgs &g, int split, int
     k1 = min(g.n_keys, k0 + g.tiles_per_split * KT);
 }
 
-// Codes (d/4 bytes, zero-padded to 64) and scale of keys tb+pt and tb+pt+128
-// when they lie below k1; zeros otherwise.
-__device__ __forceinline__ void load_key_codes(const ScanArgs &g, int64_t tb, int64_t k1, int pt, int nchunks,
-                                               uint4 (&cw)[2][4], float (&sk)[2]) {
+// Codes (d/4 bytes, zero-padded to 64) and scale of key `key` when it lies
+// below k1; zeros otherwise.
+__device__ __forceinline__ void load_key_codes(const ScanArgs &g, int64_t key, int64_t k1, int nchunks, uint4 (&cw)[4],
+                                               float &sk) {
+    const bool in = key < k1;
+    const uint4 *src = reinterpret_cast<const uint4 *>(g.codes + key * (g.d / 4));
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int64_t key = tb + pt + 128 * h;
-        const bool in = key < k1;
-        const uint4 *src = reinterpret_cast<const uint4 *>(g.codes + key * (g.d / 4));
-#pragma unroll
-        for (int j = 0; j < 4; j++) cw[h][j] = (in && j < nchunks) ? __ldg(src + j) : make_uint4(0u, 0u, 0u, 0u);
-        sk[h] = in ? __ldg(g.scales + key) : 0.0f;
-    }
+    for (int j = 0; j < 4; j++) cw[j] = (in && j < nchunks) ? __ldg(src + j) : make_uint4(0u, 0u, 0u, 0u);
+    sk = in ? __ldg(g.scales + key) : 0.0f;
 }
 
 template <int MODE, int PREC>
@@ -241,21 +256,21 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < KSTAGES; s++) {
-            st::mbar_init(&full[s], 128);
+            st::mbar_init(&full[s], NPROD);
             st::mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
             st::mbar_init(&accf[b], 1);
-            st::mbar_init(&acce[b], 128);
-            st::mbar_init(&kfr[b], 128);
+            st::mbar_init(&acce[b], NEPI);
+            st::mbar_init(&kfr[b], NPROD);
         }
-        st::mbar_init(qfull, 128);
+        st::mbar_init(qfull, NPROD);
         st::mbar_init(qfree, 1);
         st::mbar_init(fin, 1);
         *abort_flag = 0;
         st::fence_mbar_init();
     }
-    if (warp == 4) {
+    if (warp == MMA_WARP) {
         st::tmem_alloc(tmem_slot, TMEM_COLS);
         st::tmem_relinquish();
     }
@@ -264,12 +279,12 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
     st::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= 5) {
+    if (warp >= NEPI / 32 && warp < MMA_WARP) {
         // ------------------------------------------------------------ producers
-        const int pt = threadIdx.x - 160;  // 0..127
+        const int pt = threadIdx.x - NEPI;  // 0..255: key row of every tile
         const int pw = pt >> 5;
-        // byte of four codes -> two prmt selectors (codes 0,1 | codes 2,3)
-        for (int x = pt; x < 256; x += 128) {
+        {  // byte of four codes -> two prmt selectors (codes 0,1 | codes 2,3)
+            const int x = pt;
             uint32_t sel[2];
 #pragma unroll
             for (int h = 0; h < 2; h++) {
@@ -278,14 +293,14 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             }
             lut[x] = sel[0] | (sel[1] << 16);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(NPROD) : "memory");
         uint32_t lc = 0, gt = 0, ui = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ui) {
             const int qb = unit % g.nqb, split = unit / g.nqb;
             // queries of this unit: row r, lane = 8 dims
             if (ui > 0 && !kwait(qfree, (ui - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
-            for (int r = pw; r < KQ; r += 4) {
+            for (int r = pw; r < KQ; r += NPROD / 32) {
                 const int qi = qb * KQ + r;
                 float x[8];
                 const bool live = qi < g.nq && lane * 8 < g.d;
@@ -326,76 +341,40 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
 
             int64_t k0, k1;
             key_tile_range(g, split, k0, k1);
-            uint4 nx_cw[2][4];
-            float nx_sk[2];
-            load_key_codes(g, k0, k1, pt, nchunks, nx_cw, nx_sk);
+            uint4 nx_cw[4];
+            float nx_sk;
+            load_key_codes(g, k0 + pt, k1, nchunks, nx_cw, nx_sk);
             for (int64_t tb = k0; tb < k1 && ok; tb += KT, ++gt) {
                 const uint32_t b = gt & 1u, use = gt >> 1;
-                // the codes of this thread's two keys (rows pt and pt+128);
-                // the next tile's are loaded now, so their latency hides
-                // behind this tile's expansion
-                uint4 cw[2][4];
-                float sk[2];
-                int n3[2];
+                // this thread's key (row pt); the next tile's codes are loaded
+                // now, so their latency hides behind this tile
+                uint4 cw[4];
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
+                for (int j = 0; j < 4; j++) cw[j] = nx_cw[j];
+                const float sk = nx_sk;
+                const bool kin = tb + pt < k1;
+                load_key_codes(g, tb + KT + pt, k1, nchunks, nx_cw, nx_sk);
+                int c3 = 0;  // codes with |2u-3| = 3: the two bits of u are equal
 #pragma unroll
-                    for (int j = 0; j < 4; j++) cw[h][j] = nx_cw[h][j];
-                    sk[h] = nx_sk[h];
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t w[4] = {cw[j].x, cw[j].y, cw[j].z, cw[j].w};
+#pragma unroll
+                    for (int t = 0; t < 4; t++) c3 += __popc(~(w[t] ^ (w[t] >> 1)) & 0x55555555u);
                 }
-                load_key_codes(g, tb + KT, k1, pt, nchunks, nx_cw, nx_sk);
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    int c3 = 0;  // codes with |2u-3| = 3: the two bits of u are equal
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const uint32_t w[4] = {cw[h][j].x, cw[h][j].y, cw[h][j].z, cw[h][j].w};
-#pragma unroll
-                        for (int t = 0; t < 4; t++) c3 += __popc(~(w[t] ^ (w[t] >> 1)) & 0x55555555u);
-                    }
-                    // zero-filled words (absent keys or dims) count as equal bits:
-                    // take them back out
-                    n3[h] = tb + pt + 128 * h < k1 ? c3 - 64 * (4 - nchunks) : 0;
-                }
-                // per-key factors, once the epilogue is done with buffer b
-                if (use > 0 && !kwait(&acce[b], (use - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
-                    ok = false;
-                    break;
-                }
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int row = pt + 128 * h;
-                    const float s = sk[h];
-                    float f, nrm;
-                    if (PREC == PREC_EXACT) {
-                        f = 0.5f * s;
-                        nrm = f * f * static_cast<float>(g.d + 8 * n3[h]);
-                    } else {
-                        const float h1 = __half2float(__float2half_rn(0.5f * s));
-                        const float h3 = __half2float(__float2half_rn(1.5f * s));
-                        f = 1.0f;
-                        nrm = static_cast<float>(g.d - n3[h]) * (h1 * h1) + static_cast<float>(n3[h]) * (h3 * h3);
-                    }
-                    kf[b * KT + row] = f;
-                    kn[b * KT + row] = nrm;
-                }
-                st::mbar_arrive(&kfr[b]);
+                // zero-filled words (absent dims) count as equal bits: take them out
+                const int n3 = kin ? c3 - 64 * (4 - nchunks) : 0;
                 // value table: f16 of code u at bytes 2u, 2u+1 of {thi:tlo}
-                uint32_t tlo[2], thi[2];
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    if (PREC == PREC_EXACT) {
-                        tlo[h] = 0xBC00C200u;  // -1.0 | -3.0
-                        thi[h] = 0x42003C00u;  // 3.0 | 1.0
-                    } else {
-                        const float s = sk[h];
-                        const uint32_t v0 = __half_as_ushort(__float2half_rn(-1.5f * s));
-                        const uint32_t v1 = __half_as_ushort(__float2half_rn(-0.5f * s));
-                        const uint32_t v2 = __half_as_ushort(__float2half_rn(0.5f * s));
-                        const uint32_t v3 = __half_as_ushort(__float2half_rn(1.5f * s));
-                        tlo[h] = v0 | (v1 << 16);
-                        thi[h] = v2 | (v3 << 16);
-                    }
+                uint32_t tlo, thi;
+                if (PREC == PREC_EXACT) {
+                    tlo = 0xBC00C200u;  // -1.0 | -3.0
+                    thi = 0x42003C00u;  // 3.0 | 1.0
+                } else {
+                    const uint32_t v0 = __half_as_ushort(__float2half_rn(-1.5f * sk));
+                    const uint32_t v1 = __half_as_ushort(__float2half_rn(-0.5f * sk));
+                    const uint32_t v2 = __half_as_ushort(__float2half_rn(0.5f * sk));
+                    const uint32_t v3 = __half_as_ushort(__float2half_rn(1.5f * sk));
+                    tlo = v0 | (v1 << 16);
+                    thi = v2 | (v3 << 16);
                 }
                 for (int j = 0; j < nchunks; j++, ++lc) {
                     const uint32_t s = lc % KSTAGES;
@@ -405,32 +384,47 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                         break;
                     }
                     uint8_t *stage = smem + OFF_K + s * KCH_BYTES;
+                    uint4 cj = cw[0];
+                    if (j == 1) cj = cw[1];
+                    if (j == 2) cj = cw[2];
+                    if (j == 3) cj = cw[3];
+                    const uint32_t w[4] = {cj.x, cj.y, cj.z, cj.w};
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int row = pt + 128 * h;
-                        uint4 cj = cw[h][0];
-                        if (j == 1) cj = cw[h][1];
-                        if (j == 2) cj = cw[h][2];
-                        if (j == 3) cj = cw[h][3];
-                        const uint32_t w[4] = {cj.x, cj.y, cj.z, cj.w};
-#pragma unroll
-                        for (int c = 0; c < 8; c++) {
-                            const uint32_t half16 = (w[c >> 1] >> (16 * (c & 1))) & 0xffffu;
-                            const uint32_t s0 = lut[half16 & 0xffu], s1 = lut[half16 >> 8];
-                            uint4 o;
-                            o.x = __byte_perm(tlo[h], thi[h], s0 & 0xffffu);
-                            o.y = __byte_perm(tlo[h], thi[h], s0 >> 16);
-                            o.z = __byte_perm(tlo[h], thi[h], s1 & 0xffffu);
-                            o.w = __byte_perm(tlo[h], thi[h], s1 >> 16);
-                            *reinterpret_cast<uint4 *>(stage + st::sw128_offset(row, c)) = o;
-                        }
+                    for (int c = 0; c < 8; c++) {
+                        const uint32_t half16 = (w[c >> 1] >> (16 * (c & 1))) & 0xffffu;
+                        const uint32_t s0 = lut[half16 & 0xffu], s1 = lut[half16 >> 8];
+                        uint4 o;
+                        o.x = __byte_perm(tlo, thi, s0 & 0xffffu);
+                        o.y = __byte_perm(tlo, thi, s0 >> 16);
+                        o.z = __byte_perm(tlo, thi, s1 & 0xffffu);
+                        o.w = __byte_perm(tlo, thi, s1 >> 16);
+                        *reinterpret_cast<uint4 *>(stage + st::sw128_offset(pt, c)) = o;
                     }
                     st::fence_proxy_async_smem();
                     st::mbar_arrive(&full[s]);
                 }
+                if (!ok) break;
+                // per-key factors of this tile, once the epilogue is done with buffer b
+                if (use > 0 && !kwait(&acce[b], (use - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                float f, nrm;
+                if (PREC == PREC_EXACT) {
+                    f = 0.5f * sk;
+                    nrm = f * f * static_cast<float>(g.d + 8 * n3);
+                } else {
+                    const float h1 = __half2float(__float2half_rn(0.5f * sk));
+                    const float h3 = __half2float(__float2half_rn(1.5f * sk));
+                    f = 1.0f;
+                    nrm = static_cast<float>(g.d - n3) * (h1 * h1) + static_cast<float>(n3) * (h3 * h3);
+                }
+                kf[b * KT + pt] = f;
+                kn[b * KT + pt] = nrm;
+                st::mbar_arrive(&kfr[b]);
             }
         }
-    } else if (warp == 4) {
+    } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, KQ, KT);
@@ -478,10 +472,16 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             st::umma_commit(fin);
             kwait(fin, 0, abort_flag, g.status, st::DEV_TIMEOUT_ACC);
         }
-    } else {
+    } else if (warp < NEPI / 32) {
         // ------------------------------------------------------------ epilogue
-        const int row = threadIdx.x;  // TMEM lane = query row within the unit
-        uint64_t *my_buf = g.cbuf + (static_cast<int64_t>(blockIdx.x) * KQ + row) * KCAP;
+        // Warp w reads TMEM lanes 32*(w%4).. (its 32 queries) and owns half
+        // w/4 of every tile's columns; each (query, half) keeps its own
+        // candidate buffer, threshold and output list.
+        const int row = (warp & 3) * 32 + lane;  // TMEM lane = query row within the unit
+        const int half = warp >> 2;
+        uint64_t *my_buf = g.cbuf + (static_cast<int64_t>(blockIdx.x) * NEPI + threadIdx.x) * KCAP;
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        float *my_slot = reinterpret_cast<float *>(smem + OFF_SLOT) + threadIdx.x * 16;
         uint32_t gt = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
@@ -510,38 +510,58 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                     break;
                 }
                 st::tc_fence_after();
-                const int ncols = static_cast<int>(k1 - tb < KT ? k1 - tb : KT);
-                const uint32_t base_idx = g.index_base + static_cast<uint32_t>(tb);
-                const float *kfb = kf + b * KT, *knb = kn + b * KT;
+                const int col_lo = half * (KT / 2);
+                const int ncols = static_cast<int>(k1 - tb < KT ? k1 - tb : KT) - col_lo;  // may be <= 0
+                const uint32_t kfb = st::smem_u32(kf + b * KT), knb = st::smem_u32(kn + b * KT);
+                // 16 columns at a time: scores into registers, one pass mask,
+                // and the (rare) inserts only when this lane has a hit -- no
+                // per-key branch on the common path
 #pragma unroll 1
-                for (int c0 = 0; c0 < ncols; c0 += 32) {
-                    uint32_t r[32];
-                    st::tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + b * KT + c0, r);
+                for (int c0 = 0; c0 < ncols && c0 < KT / 2; c0 += 16) {
+                    const int col = col_lo + c0;
+                    uint32_t r[16];
+                    st::tmem_ld16(tmem + lane_base + b * KT + col, r);
+                    float f[16], nk[16];
+                    if (PREC == PREC_EXACT) lds_f32x16(kfb + 4 * col, f);
+                    if (MODE == MODE_L2) lds_f32x16(knb + 4 * col, nk);
                     st::tmem_ld_wait();
-                    const int lim = min(32, ncols - c0);
+                    float sc[16];
+                    uint32_t pass = 0;
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj++) {
-                        const int col = c0 + jj;
+                    for (int jj = 0; jj < 16; jj++) {
                         const float dot = __uint_as_float(r[jj]);
-                        float s;
                         if (MODE == MODE_DOT) {
-                            s = PREC == PREC_EXACT ? dot * kfb[col] : dot;
+                            sc[jj] = PREC == PREC_EXACT ? dot * f[jj] : dot;
                         } else {
-                            s = PREC == PREC_EXACT ? fmaf(-knb[col], qf, dot * kfb[col]) : fmaf(2.0f, dot, -knb[col]);
+                            sc[jj] = PREC == PREC_EXACT ? fmaf(-nk[jj], qf, dot * f[jj]) : fmaf(2.0f, dot, -nk[jj]);
                         }
-                        if (jj < lim && qlive && s >= thr) {
-                            my_buf[cnt] = make_key(s, base_idx + static_cast<uint32_t>(col));
+                        pass |= (sc[jj] >= thr ? 1u : 0u) << jj;
+                    }
+                    const int lim = ncols - c0;
+                    if (lim < 16) pass &= (1u << lim) - 1u;
+                    if (!qlive) pass = 0;
+                    if (pass) {
+                        // stage the 16 scores in this thread's slot, then visit only the hits
+                        const uint32_t idx0 = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(col);
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            *reinterpret_cast<float4 *>(my_slot + 4 * i) =
+                                make_float4(sc[4 * i], sc[4 * i + 1], sc[4 * i + 2], sc[4 * i + 3]);
+                        do {
+                            const int jj = __ffs(pass) - 1;
+                            pass &= pass - 1;
+                            my_buf[cnt] = make_key(my_slot[jj], idx0 + static_cast<uint32_t>(jj));
                             cnt++;
-                        }
+                        } while (pass);
                     }
                 }
                 st::tc_fence_before();
                 st::mbar_arrive(&acce[b]);
-                const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - KT);
+                const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - KT / 2);
                 if (need) warp_compact(need, my_buf, cnt, thr, nullptr, false);
             }
             if (!ok) break;
-            uint64_t *my_out = g.unit_out + (static_cast<int64_t>(split) * g.nq_pad + qi) * KTOP;
+            uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(split) * 2 + half) * g.nq_pad + qi) * KTOP;
             const unsigned need = __ballot_sync(0xffffffffu, qlive);
             if (need) warp_compact(need, my_buf, cnt, thr, my_out, true);
         }
@@ -549,7 +569,7 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
 
     st::tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == MMA_WARP) {
         st::tc_fence_after();
         st::tmem_dealloc(tmem, TMEM_COLS);
     }
@@ -784,8 +804,8 @@ extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const 
     const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
     const int64_t nq_pad = static_cast<int64_t>(nqb) * KQ;
 
-    uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * KQ * KCAP));
-    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, sizeof(uint64_t) * splits * nq_pad * KTOP));
+    uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * NEPI * KCAP));
+    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, sizeof(uint64_t) * 2 * splits * nq_pad * KTOP));
     if (!cbuf || !unit_out) return ST_NO_MEMORY;
 
     ScanArgs g{};
@@ -808,7 +828,7 @@ extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const 
     else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT>(h, g, grid);
     else s = launch_scan<MODE_L2, PREC_F16REF>(h, g, grid);
     if (s != ST_OK) return s;
-    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, splits, nq_pad * KTOP, out_keys);
+    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, 2 * splits, nq_pad * KTOP, out_keys);
     return st_after_launch(h, "k_knn_merge");
 }
 
