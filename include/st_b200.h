@@ -165,6 +165,27 @@ ST_API st_status st_softmax_rows(st_handle *h, const float *x, float *y, int64_t
 ST_API st_status st_softmax_rows_bwd(st_handle *h, const float *dy, const float *y, float *dx, int64_t rows, int64_t n,
                               float scale);
 
+/* ---- fused causal attention ----------------------------------------------- */
+
+/* Fused attention over bh independent heads, f16 storage with f32
+ * accumulation on tcgen05 (kind::f16): per head S = scale * Q K^T, causal
+ * mask (column j visible to row i iff j <= i), P = softmax(S), O = P V.
+ * q, k, v, o: device f16 [bh, t, d], head z at z*t*d (16-byte aligned);
+ * lse: device f32 [bh, t], the natural-log sum of exp of each scaled, masked
+ * row (for the backward).  t <= 128, d = 64.  Replaces the chain
+ * batched_matmul(q, k, transpose_b) -> scale -> + mask -> softmax ->
+ * batched_matmul(w, v) of TransformerBlock::forward_full (src/nn.rs:646-671)
+ * and of DeviceTape::block_forward (src/gpu_step/tape.rs:481-484). */
+ST_API st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse, int64_t bh,
+                             int64_t t, int64_t d, float scale, int32_t causal);
+/* Backward: dq, dk, dv (device f16 [bh, t, d]) from q, k, v, o, dout (f16)
+ * and lse (f32) of st_attn_fwd.  Replaces batched_matmul_backward
+ * (src/tape.rs:90-112) and the softmax backward (src/gpu_step/rows.rs:117-123,
+ * src/gpu_step/tape.rs:363-375). */
+ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o, const void *dout,
+                             const float *lse, void *dq, void *dk, void *dv, int64_t bh, int64_t t, int64_t d, float scale,
+                             int32_t causal);
+
 /* ---- kNN memory: 2-bit key scan fused with top-k ------------------------- */
 
 /* Ranking modes (src/gpu_step/knn.rs:5, :522-532, :855).

@@ -64,6 +64,8 @@ SIGNATURES = {
     "st_matmul_host": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_int]),
     "st_softmax_rows": (_st, [_h, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),
+    "st_attn_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
+    "st_attn_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
     "st_knn_search": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp]),
     "st_knn_topk_keys": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i64, _vp]),
     "st_knn_merge_keys": (_st, [_h, _vp, _i64, _i64, _i64, _vp]),

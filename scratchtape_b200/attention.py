@@ -1,0 +1,33 @@
+"""Fused causal attention on the device (f16 storage, f32 accumulation).
+
+Mirrors the attention of TransformerBlock::forward_full (src/nn.rs:646-671)
+and DeviceTape (src/gpu_step/tape.rs:481-484, :349-375): per head,
+O = softmax(scale * Q K^T + causal mask) V, and its backward.  One kernel
+launch per direction for all heads (st_attn_fwd / st_attn_bwd); there is no
+CPU path.
+"""
+import torch
+
+from .device import handle, ptr
+
+
+def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = True, out=None):
+    """q, k, v: f16 [bh, t, d] (d = 64, t <= 128) -> (o f16 [bh, t, d], lse f32 [bh, t])."""
+    q, k, v = (x.contiguous() for x in (q, k, v))
+    bh, t, d = q.shape
+    if out is None:
+        out = (torch.empty_like(q), torch.empty((bh, t), dtype=torch.float32, device=q.device))
+    handle(q.device).call("st_attn_fwd", ptr(q), ptr(k), ptr(v), ptr(out[0]), ptr(out[1]), bh, t, d, float(scale),
+                          int(causal))
+    return out
+
+
+def attention_bwd(q, k, v, o, dout, lse, scale: float, causal: bool = True, out=None):
+    """-> (dq, dk, dv), f16 [bh, t, d]."""
+    q, k, v, o, dout = (x.contiguous() for x in (q, k, v, o, dout))
+    bh, t, d = q.shape
+    if out is None:
+        out = (torch.empty_like(q), torch.empty_like(q), torch.empty_like(q))
+    handle(q.device).call("st_attn_bwd", ptr(q), ptr(k), ptr(v), ptr(o), ptr(dout), ptr(lse), ptr(out[0]),
+                          ptr(out[1]), ptr(out[2]), bh, t, d, float(scale), int(causal))
+    return out
