@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (c2: 200, c5: 5)")
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (c2: 20, c5: 3)")
-    p.add_argument("--config", default="c2", choices=["c2", "c5"])
+    p.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
     p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
     p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -581,6 +581,195 @@ def run_ours_c5(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C3: batched causal attention, f16 storage / f32 accumulation: batch 32,
+# 4 heads, head_dim 64, seq 128; forward + backward.
+# ---------------------------------------------------------------------------
+C3 = dict(b=32, h=4, t=128, d=64)
+
+
+def c3_flops():
+    """Causal count, as BASELINE states it: fwd 2 GEMMs, bwd 4, over the
+    t(t+1)/2 visible pairs of each head."""
+    bh, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
+    pairs = t * (t + 1) // 2
+    return 6 * 2 * bh * pairs * d
+
+
+def c3_bytes():
+    bh, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
+    tile = bh * t * d * 2
+    return {"fwd": 4 * tile + bh * t * 4, "bwd": 8 * tile + bh * t * 4}
+
+
+def c3_host_inputs(bh, seed=0):
+    rng = np.random.default_rng(seed + 3)
+    t, d = C3["t"], C3["d"]
+    q, k, v = ((rng.standard_normal((bh, t, d)) / 8.0).astype(np.float16) for _ in range(3))
+    dout = rng.standard_normal((bh, t, d)).astype(np.float16)
+    return q, k, v, dout
+
+
+def cpu_attn_sample(heads, threads=None):
+    import oracle
+    q, k, v, dout = (x.astype(np.float32) for x in c3_host_inputs(heads))
+    t0 = time.perf_counter()
+    oracle.attention_fwd(q, k, v, 0.125)
+    oracle.attention_bwd(q, k, v, dout, 0.125)
+    return time.perf_counter() - t0
+
+
+def run_reference_c3(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    heads = 16
+    for _ in range(args.warmup):
+        cpu_attn_sample(2)
+    ts = [cpu_attn_sample(heads) for _ in range(args.steps)]
+    el = float(np.median(ts)) * (C3["b"] * C3["h"]) / heads
+    v = c3_flops() / el / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C3 causal attention fwd+bwd, B32 H4 T128 D64 (sampled: 16 heads per step)",
+                       "parallelism": "CPU, rank 0"},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                             "sample": "16 heads of fwd+bwd on the oracle's restated tape attention (f32, 1 thread), "
+                                       "scaled to 128 heads"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours_c3(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import scratchtape_b200 as st
+    from scratchtape_b200.attention import attention_bwd, attention_fwd
+    peaks, peak_src = load_peaks()
+    h = st.handle()
+    bh_all, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
+    per = (bh_all + world - 1) // world
+    lo, hi = rank * per, min(bh_all, (rank + 1) * per)
+    bh = max(0, hi - lo)
+    hq, hk, hv, hdo = (torch.from_numpy(x[lo:hi]).pin_memory() for x in c3_host_inputs(bh_all))
+    q, k, v, dout = (x.to(device) for x in (hq, hk, hv, hdo))
+    o = torch.empty_like(q)
+    lse = torch.empty((bh, t), dtype=torch.float32, device=device)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    scale = 1.0 / 8.0
+
+    def step():
+        attention_fwd(q, k, v, scale, True, out=(o, lse))
+        attention_bwd(q, k, v, o, dout, lse, scale, True, out=(dq, dk, dv))
+
+    n0 = h.launches
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = h.launches - n0
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record()
+            attention_fwd(q, k, v, scale, True, out=(o, lse))
+            ev[i][1].record()
+            attention_bwd(q, k, v, o, dout, lse, scale, True, out=(dq, dk, dv))
+            ev[i][2].record()
+        torch.cuda.synchronize()
+    barrier()
+    fwd_ms = float(np.mean([a.elapsed_time(b) for a, b, _ in ev]))
+    bwd_ms = float(np.mean([b.elapsed_time(c) for _, b, c in ev]))
+    total_ms = float(sum(a.elapsed_time(c) for a, _, c in ev))
+    if world > 1:
+        tt = torch.tensor([total_ms, fwd_ms, bwd_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms, fwd_ms, bwd_ms = (float(x) for x in tt.tolist())
+    value = c3_flops() * args.steps / (total_ms / 1e3) / 1e12
+
+    # e2e through the public API with host tensors: copy in, fwd + bwd, copy out
+    outs = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (q, q, q, q)]
+    e_ms = []
+    e2e_steps = max(10, min(args.steps, 100))
+    barrier()
+    for _ in range(e2e_steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for src, dst in zip((hq, hk, hv, hdo), (q, k, v, dout)):
+            dst.copy_(src, non_blocking=True)
+        step()
+        for src, dst in zip((o, dq, dk, dv), outs):
+            dst.copy_(src, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        e_ms.append(e0.elapsed_time(e1))
+    e_total = float(sum(e_ms))
+    if world > 1:
+        tt = torch.tensor([e_total], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_total = float(tt.item())
+    e2e_value = c3_flops() * e2e_steps / (e_total / 1e3) / 1e12
+    by = c3_bytes()
+    frac_b = bh / bh_all
+    achieved = (by["fwd"] + by["bwd"]) * frac_b / ((fwd_ms + bwd_ms) / 1e3) / 1e9
+    hbm = float(peaks["hbm_gbs"])
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 storage / f32 accumulate", "data": "synthetic",
+            "config": {"workload": "C3 batched causal attention (BASELINE configs[2]): batch 32, 4 heads, head_dim 64, "
+                                   "seq 128, Q/K/V ~ N(0,1)/8 in f16, fwd + bwd (dQ, dK, dV); flops counted over the "
+                                   "causal pairs", "global_batch": 32, "seq_len": 128,
+                       "parallelism": "heads sharded x%d (no collective)" % world if world > 1 else "single GPU",
+                       "l2": "flushed (256 MiB write) before every timed step, outside its events"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "peak_source": peak_src, "kernel": "k_attn_fwd + k_attn_bwd",
+                         "fwd_us": fwd_ms * 1e3, "bwd_us": bwd_ms * 1e3,
+                         "bytes": {k2: int(v2 * frac_b) for k2, v2 in by.items()},
+                         "tensor_frac_of_bf16_peak": c3_flops() * frac_b / ((fwd_ms + bwd_ms) / 1e3) / 1e12 /
+                         float(peaks["bf16_tflops"])},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(4 * q.numel() * 2),
+                    "d2h_bytes_per_step": int(4 * q.numel() * 2), "ms_per_step": e_total / e2e_steps,
+                    "steps": e2e_steps, "api": "scratchtape_b200.attention.attention_fwd/attention_bwd (pinned host "
+                                               "f16 tensors copied in and out every step)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            el = cpu_attn_sample(16) * bh_all / 16
+            line["cpu_baseline"] = {"value": c3_flops() / el / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                    "sample": "16 heads of fwd+bwd on the oracle's restated tape attention (f32, 1 "
+                                              "thread, as the reference), scaled to 128 heads"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.config == "c5":
@@ -588,6 +777,11 @@ def main():
             run_reference_c5(args)
         else:
             run_ours_c5(args)
+    elif args.config == "c3":
+        if args.impl == "reference":
+            run_reference_c3(args)
+        else:
+            run_ours_c3(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

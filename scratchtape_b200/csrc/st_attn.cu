@@ -11,8 +11,8 @@
 //   dV = P^T dO, dP = dO V^T, dS = P * (dP - rowsum(dO * O)) * scale,
 //   dQ = dS K, dK = dS^T Q.
 //
-// B200 design.  A head of up to 128 rows fits one tile, so one CTA (4 warps,
-// thread = row) does a whole head with no online rescaling: Q, K, V (and
+// B200 design.  A head of up to 128 rows fits one tile, so one CTA (8 warps,
+// two threads per row) does a whole head with no online rescaling: Q, K, V (and
 // dO) are staged once in 128-byte-swizzled shared memory (16 KB each at
 // d = 64), every contraction is a tcgen05 kind::f16 MMA with f32
 // accumulation in TMEM, and every transposed operand (K^T, V as an N-major
@@ -32,7 +32,7 @@ constexpr int AT = 128;               // rows per head tile (max t)
 constexpr int AD = 64;                // head width
 constexpr int TILE = AT * AD * 2;     // one [128 x 64] f16 operand: 16 KB
 constexpr int PT = AT * AT * 2;       // one [128 x 128] f16 operand: 32 KB
-constexpr int ATHREADS = 128;
+constexpr int ATHREADS = 256;  // two threads per row
 
 struct AttnArgs {
     const __half *q, *k, *v, *o, *dout;
@@ -57,11 +57,12 @@ __device__ __forceinline__ bool await(uint64_t *bar, uint32_t parity, int *statu
     }
 }
 
-// Row r (< t, else zeros) of a [t, 64] f16 head into a swizzled 16 KB tile.
-__device__ __forceinline__ void stage_rows(uint8_t *dst, const __half *src, int r, int t) {
+// Half `half` (32 of the 64 columns) of row r (< t, else zeros) of a [t, 64]
+// f16 head into a swizzled 16 KB tile.
+__device__ __forceinline__ void stage_half_rows(uint8_t *dst, const __half *src, int r, int half, int t) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src + static_cast<int64_t>(r) * AD);
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
+    for (int c = 4 * half; c < 4 * half + 4; c++) {
         const uint4 v = r < t ? __ldg(s + c) : make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, c)) = v;
     }
@@ -97,16 +98,25 @@ __device__ __forceinline__ uint64_t mnmaj(uint32_t base, int kk, uint32_t mn_str
     return st::sdesc_make(base + kk * 2048, mn_stride, 1024, st::LAYOUT_SW128);
 }
 
+// e^x for the softmax numerators, as 2^(x * log2 e) on the SFU: P is rounded
+// to f16 right after, so its ~2 ulp f32 error is far below what is kept.
+__device__ __forceinline__ float fast_exp(float x) { return exp2f(x * 1.4426950408889634f); }
+
+// Threads r and r + 128 share row r % 128: thread r < 128 owns columns
+// [0, 64) of the row, thread r + 128 columns [64, 128) (warps w and w + 4 read
+// the same TMEM lanes).  Row reductions combine the two halves through `red`.
 __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem, *sK = smem + TILE, *sV = smem + 2 * TILE, *sP = smem + 3 * TILE;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sP + PT);
+    float *red = reinterpret_cast<float *>(sP + PT);  // [2][128]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 2 * AT);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
-    const int r = threadIdx.x, warp = r >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & (AT - 1), half = tid >> 7;
     const int64_t head = static_cast<int64_t>(blockIdx.x) * g.t * AD;
 
-    if (r == 0) {
+    if (tid == 0) {
         st::mbar_init(&bar[0], 1);
         st::mbar_init(&bar[1], 1);
         st::fence_mbar_init();
@@ -115,17 +125,17 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
         st::tmem_alloc(tslot, 256);
         st::tmem_relinquish();
     }
-    stage_rows(sQ, g.q + head, r, g.t);
-    stage_rows(sK, g.k + head, r, g.t);
-    stage_rows(sV, g.v + head, r, g.t);
+    stage_half_rows(sQ, g.q + head, r, half, g.t);
+    stage_half_rows(sK, g.k + head, r, half, g.t);
+    stage_half_rows(sV, g.v + head, r, half, g.t);
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
     const uint32_t tmem = *tslot, tS = tmem, tO = tmem + 128;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
-    if (r == 0) {  // S = Q K^T
+    if (tid == 0) {  // S = Q K^T
         constexpr uint32_t id = st::idesc_make(1, 0, false, false, AT, AT);
         const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK);
 #pragma unroll
@@ -135,45 +145,45 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     bool ok = await(&bar[0], 0, g.status);
     st::tc_fence_after();
 
-    // softmax of row r: masked max, then p = exp(s - max) as f16 into sP
+    // softmax of row r over this thread's 64 columns: masked max, exchange,
+    // p = exp(s - max) as f16 into sP, partial sums, exchange
     const int lim = r < g.t ? (g.causal ? r + 1 : g.t) : 0;  // columns < lim are visible
+    const int cbase = half * 64;
+    uint32_t x[64];
+    st::tmem_ld32(tS + lane_base + cbase, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+    st::tmem_ld32(tS + lane_base + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+    st::tmem_ld_wait();
     float m = -INFINITY;
-#pragma unroll 1
-    for (int c0 = 0; c0 < AT; c0 += 32) {
-        uint32_t x[32];
-        st::tmem_ld32(tS + lane_base + c0, x);
-        st::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (c0 + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
-    }
+    for (int j = 0; j < 64; j++)
+        if (cbase + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
+    red[half * AT + r] = m;
+    __syncthreads();
+    m = fmaxf(m, red[(half ^ 1) * AT + r]);
     float l = 0.0f;
-#pragma unroll 1
-    for (int c0 = 0; c0 < AT; c0 += 32) {
-        uint32_t x[32];
-        st::tmem_ld32(tS + lane_base + c0, x);
-        st::tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            float p[16];
+    for (int c = 0; c < 4; c++) {
+        float p[16];
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                const int col = c0 + 16 * h + j;
-                p[j] = col < lim ? expf(__uint_as_float(x[16 * h + j]) * g.scale - m) : 0.0f;
-                l += p[j];
-            }
-            uint32_t o[8];
-            pack16(p, o);
-            put16(sP, r, c0 + 16 * h, o);
+        for (int j = 0; j < 16; j++) {
+            const int col = cbase + 16 * c + j;
+            p[j] = col < lim ? fast_exp(__uint_as_float(x[16 * c + j]) * g.scale - m) : 0.0f;
+            l += p[j];
         }
+        uint32_t o[8];
+        pack16(p, o);
+        put16(sP, r, cbase + 16 * c, o);
     }
-    if (r < g.t) g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] = lim > 0 ? m + logf(l) : -INFINITY;
+    __syncthreads();  // every thread has read red (max) before it is reused for sums
+    red[half * AT + r] = l;
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
+    l += red[(half ^ 1) * AT + r];
+    if (half == 0 && r < g.t) g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] = lim > 0 ? m + logf(l) : -INFINITY;
 
-    if (r == 0) {  // O = P V   (V: B operand, N = d contiguous -> MN-major)
+    if (tid == 0) {  // O = P V   (V: B operand, N = d contiguous -> MN-major)
         constexpr uint32_t id = st::idesc_make(1, 0, false, true, AT, AD);
         const uint32_t p = st::smem_u32(sP), v = st::smem_u32(sV);
 #pragma unroll
@@ -184,13 +194,13 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     st::tc_fence_after();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll 1
-    for (int c0 = 0; c0 < AD; c0 += 16) {
-        uint32_t x[16];
-        st::tmem_ld16(tO + lane_base + c0, x);
+    for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+        uint32_t y16[16];
+        st::tmem_ld16(tO + lane_base + c0, y16);
         st::tmem_ld_wait();
         float y[16];
 #pragma unroll
-        for (int j = 0; j < 16; j++) y[j] = __uint_as_float(x[j]) * inv;
+        for (int j = 0; j < 16; j++) y[j] = __uint_as_float(y16[j]) * inv;
         uint32_t o[8];
         pack16(y, o);
         if (r < g.t && ok) {
@@ -212,12 +222,14 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem, *sK = smem + TILE, *sV = smem + 2 * TILE, *sO = smem + 3 * TILE;  // sO holds dO
     uint8_t *sP = smem + 4 * TILE, *sS = sP + PT;                                          // P, dS
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sS + PT);
+    float *red = reinterpret_cast<float *>(sS + PT);                                       // [2][128]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 2 * AT);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
-    const int r = threadIdx.x, warp = r >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & (AT - 1), half = tid >> 7;
     const int64_t head = static_cast<int64_t>(blockIdx.x) * g.t * AD;
 
-    if (r == 0) {
+    if (tid == 0) {
         st::mbar_init(&bar[0], 1);
         st::mbar_init(&bar[1], 1);
         st::fence_mbar_init();
@@ -226,17 +238,17 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
         st::tmem_alloc(tslot, 512);
         st::tmem_relinquish();
     }
-    stage_rows(sQ, g.q + head, r, g.t);
-    stage_rows(sK, g.k + head, r, g.t);
-    stage_rows(sV, g.v + head, r, g.t);
-    stage_rows(sO, g.dout + head, r, g.t);
-    // D_r = sum_d dO[r,d] * O[r,d]
+    stage_half_rows(sQ, g.q + head, r, half, g.t);
+    stage_half_rows(sK, g.k + head, r, half, g.t);
+    stage_half_rows(sV, g.v + head, r, half, g.t);
+    stage_half_rows(sO, g.dout + head, r, half, g.t);
+    // D_r = sum_d dO[r,d] * O[r,d], this thread's 32 of the 64 d, then exchanged
     float dsum = 0.0f;
     if (r < g.t) {
-        const uint4 *po = reinterpret_cast<const uint4 *>(g.o + head + static_cast<int64_t>(r) * AD);
-        const uint4 *pd = reinterpret_cast<const uint4 *>(g.dout + head + static_cast<int64_t>(r) * AD);
+        const uint4 *po = reinterpret_cast<const uint4 *>(g.o + head + static_cast<int64_t>(r) * AD) + 4 * half;
+        const uint4 *pd = reinterpret_cast<const uint4 *>(g.dout + head + static_cast<int64_t>(r) * AD) + 4 * half;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int c = 0; c < 4; c++) {
             const uint4 a = __ldg(po + c), b = __ldg(pd + c);
             const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -248,16 +260,18 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
             }
         }
     }
+    red[half * AT + r] = dsum;
     const float lse = r < g.t ? g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] : 0.0f;
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
+    dsum = red[0 * AT + r] + red[1 * AT + r];  // same order in both halves
     const uint32_t tmem = *tslot;
     const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
-    if (r == 0) {  // S = Q K^T, dP = dO V^T
+    if (tid == 0) {  // S = Q K^T, dP = dO V^T
         constexpr uint32_t id = st::idesc_make(1, 0, false, false, AT, AT);
         const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK), v = st::smem_u32(sV), d = st::smem_u32(sO);
 #pragma unroll
@@ -273,7 +287,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     // P = exp(scale*S - lse) (masked: 0) and dS = scale * P * (dP - D), both f16
     const int lim = r < g.t ? (g.causal ? r + 1 : g.t) : 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < AT; c0 += 16) {
+    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
         uint32_t xs[16], xd[16];
         st::tmem_ld16(tS + lane_base + c0, xs);
         st::tmem_ld16(tdP + lane_base + c0, xd);
@@ -282,7 +296,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
             const bool vis = c0 + j < lim;
-            p[j] = vis ? expf(__uint_as_float(xs[j]) * g.scale - lse) : 0.0f;
+            p[j] = vis ? fast_exp(__uint_as_float(xs[j]) * g.scale - lse) : 0.0f;
             ds[j] = p[j] * (__uint_as_float(xd[j]) - dsum) * g.scale;
         }
         uint32_t o[8];
@@ -296,7 +310,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     __syncthreads();
     st::tc_fence_after();
 
-    if (r == 0) {
+    if (tid == 0) {
         // dV = P^T dO and dK = dS^T Q: A = P^T / dS^T (stored [i][j]: MN-major, M = j),
         // B = dO / Q (stored [i][d]: MN-major, N = d), K = i
         constexpr uint32_t id_tt = st::idesc_make(1, 0, true, true, AT, AD);
@@ -314,15 +328,15 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     }
     ok = await(&bar[1], 0, g.status) && ok;
     st::tc_fence_after();
-    // row r of dV, dK (rows = keys) and dQ (rows = queries)
-    __half *outs[3] = {g.dv, g.dk, g.dq};
-    const uint32_t srcs[3] = {tdV, tdK, tdQ};
-#pragma unroll 1
+    // row r of dV, dK (rows = keys) and dQ (rows = queries), this thread's 32 columns
+#pragma unroll
     for (int w = 0; w < 3; w++) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < AD; c0 += 16) {
+        __half *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
+        const uint32_t src = w == 0 ? tdV : w == 1 ? tdK : tdQ;
+#pragma unroll
+        for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
             uint32_t x[16];
-            st::tmem_ld16(srcs[w] + lane_base + c0, x);
+            st::tmem_ld16(src + lane_base + c0, x);
             st::tmem_ld_wait();
             float y[16];
 #pragma unroll
@@ -330,7 +344,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
             uint32_t o[8];
             pack16(y, o);
             if (r < g.t && ok) {
-                uint4 *dst = reinterpret_cast<uint4 *>(outs[w] + head + static_cast<int64_t>(r) * AD + c0);
+                uint4 *dst = reinterpret_cast<uint4 *>(dst_t + head + static_cast<int64_t>(r) * AD + c0);
                 dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
                 dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
             }
@@ -344,8 +358,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     }
 }
 
-constexpr int FWD_SMEM = 3 * TILE + PT + 64 + 1024;
-constexpr int BWD_SMEM = 4 * TILE + 2 * PT + 64 + 1024;
+constexpr int FWD_SMEM = 3 * TILE + PT + 2 * AT * 4 + 64 + 1024;
+constexpr int BWD_SMEM = 4 * TILE + 2 * PT + 2 * AT * 4 + 64 + 1024;
 
 st_status check(st_handle *h, const void *q, const void *k, const void *v, int64_t bh, int64_t t, int64_t d,
                 const char *who) {
