@@ -444,10 +444,10 @@ def run_ours_c5(args):
     peaks, peak_src = load_peaks()
     h = st.handle()
     d, nq, k = C5["d"], C5["nq"], C5["k"]
+    from scratchtape_b200.shard import shard_range
     n_total = args.keys
-    per = (n_total + world - 1) // world
-    first = rank * per
-    n_local = max(0, min(n_total, first + per) - first)
+    first, last = shard_range(n_total, world, rank)
+    n_local = last - first
     codes, scales = K.synth_keys(n_local, d, seed=1, first_key=first, device=device)
     qh = c5_queries(nq, d)
     q = torch.from_numpy(qh).to(device)
@@ -658,9 +658,9 @@ def run_ours_c3(args):
     peaks, peak_src = load_peaks()
     h = st.handle()
     bh_all, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
-    per = (bh_all + world - 1) // world
-    lo, hi = rank * per, min(bh_all, (rank + 1) * per)
-    bh = max(0, hi - lo)
+    from scratchtape_b200.shard import shard_range
+    lo, hi = shard_range(bh_all, world, rank)
+    bh = hi - lo
     hq, hk, hv, hdo = (torch.from_numpy(x[lo:hi]).pin_memory() for x in c3_host_inputs(bh_all))
     q, k, v, dout = (x.to(device) for x in (hq, hk, hv, hdo))
     o = torch.empty_like(q)

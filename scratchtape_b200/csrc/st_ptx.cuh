@@ -1,5 +1,5 @@
 // st_ptx.cuh -- inline-PTX building blocks for sm_100a kernels: mbarriers
-// with bounded waits, TMA tile loads (never with cluster multicast), and the
+// with bounded waits, TMA tile loads into this CTA's own shared memory, and the
 // tcgen05 family (TMEM allocation, MMA issue, commit, TMEM loads).
 #pragma once
 #include <cuda.h>
@@ -86,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     }
 }
 
-// ---- TMA (tiled, no multicast) -----------------------------------------------
+// ---- TMA (tiled, one destination CTA) -------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
