@@ -186,6 +186,50 @@ ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const v
                              const float *lse, void *dq, void *dk, void *dv, int64_t bh, int64_t t, int64_t d, float scale,
                              int32_t causal);
 
+/* st_attn_fwd on the transformer step's packed f32 layouts, as DeviceTape
+ * addresses them through head views (MatRef::heads, src/gpu_step/matmul.rs:51-53;
+ * src/gpu_step/tape.rs:196-212, :481-484): qkv [batch*t, 3*heads*d] (Q, K, V
+ * column blocks of the fused QKV projection), o [batch*t, heads*d] (heads
+ * merged), lse [batch*heads, t].  Operands are rounded to f16 as they are
+ * staged (f32 accumulation); no split/merge copies. */
+ST_API st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o, float *lse, int64_t batch, int64_t heads,
+                                    int64_t t, int64_t d, float scale, int32_t causal);
+/* Backward on the same layouts: dqkv [batch*t, 3*heads*d] from qkv, o, dout
+ * [batch*t, heads*d] and lse. */
+ST_API st_status st_attn_bwd_packed(st_handle *h, const float *qkv, const float *o, const float *dout, const float *lse,
+                                    float *dqkv, int64_t batch, int64_t heads, int64_t t, int64_t d, float scale,
+                                    int32_t causal);
+
+/* ---- transformer step: embedding, LayerNorm, cross-entropy, Adam ---------- */
+
+/* x[r, :] = tok[ids[r], :] + pos[r % t, :] for r < batch*t (device f32 rows of d,
+ * ids int32).  Replaces tokens::embed / k_embed (src/gpu_step/tokens.rs:22-67, :125-135). */
+ST_API st_status st_embed_fwd(st_handle *h, const int32_t *ids, const float *tok, const float *pos, float *x,
+                              int64_t batch, int64_t t, int64_t d);
+/* dtok[v] (+)= sum of dx rows whose id is v, in row order; dpos[i] (+)= sum over
+ * the batch of dx[b*t + i], in batch order (no atomics).  Replaces k_embed_bwd_tok /
+ * k_embed_bwd_pos (src/gpu_step/tokens.rs:137-192).  d a multiple of 32, <= 1024. */
+ST_API st_status st_embed_bwd(st_handle *h, const int32_t *ids, const float *dx, float *dtok, float *dpos,
+                              int64_t batch, int64_t t, int64_t d, int64_t vocab, int32_t accumulate);
+/* y = (x - mean) / sqrt(var + eps) * gamma + beta per row (biased variance);
+ * saves mean and rstd per row.  Replaces rows::layer_norm (src/gpu_step/rows.rs:65-99). */
+ST_API st_status st_layernorm_fwd(st_handle *h, const float *x, const float *gamma, const float *beta, float *y,
+                                  float *mean, float *rstd, int64_t rows, int64_t d, float eps);
+/* dx (+)= the input gradient; dgamma, dbeta += the parameter gradients (fixed
+ * order).  Replaces rows::layer_norm_backward (src/gpu_step/rows.rs:100-293). */
+ST_API st_status st_layernorm_bwd(st_handle *h, const float *dy, const float *x, const float *gamma,
+                                  const float *mean, const float *rstd, float *dx, float *dgamma, float *dbeta,
+                                  int64_t rows, int64_t d, int32_t accumulate);
+/* loss[0] = mean over rows of -log softmax(logits)[target]; dlogits (may be
+ * NULL) = (softmax - onehot) / rows.  Replaces tokens::cross_entropy and its
+ * backward (src/gpu_step/tokens.rs:84-123, :194-253), without distillation. */
+ST_API st_status st_cross_entropy(st_handle *h, const float *logits, const int32_t *targets, float *loss,
+                                  float *dlogits, int64_t rows, int64_t vocab);
+/* One Adam step over n parameters (step = the 1-based step count), in the
+ * f32 operation order of Adam::step (src/optim.rs:42-57). */
+ST_API st_status st_adam(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t step, float lr,
+                         float beta1, float beta2, float eps);
+
 /* ---- kNN memory: 2-bit key scan fused with top-k ------------------------- */
 
 /* Ranking modes (src/gpu_step/knn.rs:5, :522-532, :855).

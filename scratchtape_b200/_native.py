@@ -66,6 +66,14 @@ SIGNATURES = {
     "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),
     "st_attn_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
     "st_attn_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
+    "st_attn_fwd_packed": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32]),
+    "st_attn_bwd_packed": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32]),
+    "st_embed_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i64, _i64]),
+    "st_embed_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32]),
+    "st_layernorm_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32]),
+    "st_layernorm_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32]),
+    "st_cross_entropy": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i64]),
+    "st_adam": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _f32, _f32]),
     "st_knn_search": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp]),
     "st_knn_topk_keys": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i64, _vp]),
     "st_knn_merge_keys": (_st, [_h, _vp, _i64, _i64, _i64, _vp]),

@@ -31,3 +31,27 @@ def attention_bwd(q, k, v, o, dout, lse, scale: float, causal: bool = True, out=
     handle(q.device).call("st_attn_bwd", ptr(q), ptr(k), ptr(v), ptr(o), ptr(dout), ptr(lse), ptr(out[0]),
                           ptr(out[1]), ptr(out[2]), bh, t, d, float(scale), int(causal))
     return out
+
+
+def attention_fwd_packed(qkv: torch.Tensor, batch: int, heads: int, t: int, scale: float, causal: bool = True,
+                         out=None):
+    """Fused attention on the packed f32 layout of the transformer step:
+    qkv [batch*t, 3*heads*64] -> (o [batch*t, heads*64] f32, lse [batch*heads, t])."""
+    d = 64
+    if out is None:
+        out = (torch.empty((batch * t, heads * d), dtype=torch.float32, device=qkv.device),
+               torch.empty((batch * heads, t), dtype=torch.float32, device=qkv.device))
+    handle(qkv.device).call("st_attn_fwd_packed", ptr(qkv), ptr(out[0]), ptr(out[1]), batch, heads, t, d,
+                            float(scale), int(causal))
+    return out
+
+
+def attention_bwd_packed(qkv, o, dout, lse, batch: int, heads: int, t: int, scale: float, causal: bool = True,
+                         out=None):
+    """-> dqkv [batch*t, 3*heads*64] f32."""
+    d = 64
+    if out is None:
+        out = torch.empty_like(qkv)
+    handle(qkv.device).call("st_attn_bwd_packed", ptr(qkv), ptr(o), ptr(dout), ptr(lse), ptr(out), batch, heads, t,
+                            d, float(scale), int(causal))
+    return out

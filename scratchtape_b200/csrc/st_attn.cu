@@ -34,11 +34,25 @@ constexpr int TILE = AT * AD * 2;     // one [128 x 64] f16 operand: 16 KB
 constexpr int PT = AT * AT * 2;       // one [128 x 128] f16 operand: 32 KB
 constexpr int ATHREADS = 256;  // two threads per row
 
+// Where row r of head z of a tensor lives: element (z / heads) * bstride +
+// (z % heads) * hstride + r * rstride of its base.  Per-head tensors
+// [bh, t, 64] use heads = 1, bstride = t * 64, rstride = 64; the packed
+// layouts of the transformer step (fused QKV [B*T, 3*H*64], merged O
+// [B*T, H*64]) use heads = H, hstride = 64, bstride = t * rstride.
+struct RowMap {
+    int64_t bstride, hstride, rstride;
+    __device__ __forceinline__ int64_t at(int z, int heads, int r) const {
+        return static_cast<int64_t>(z / heads) * bstride + static_cast<int64_t>(z % heads) * hstride +
+               static_cast<int64_t>(r) * rstride;
+    }
+};
+
 struct AttnArgs {
-    const __half *q, *k, *v, *o, *dout;
-    __half *out, *dq, *dk, *dv;
+    const void *q, *k, *v, *o, *dout;  // f16, or f32 when the kernel's F32 flag is set
+    void *out, *dq, *dk, *dv;
     float *lse;
-    int bh, t;
+    RowMap mq, mo;  // q/k/v/dq/dk/dv rows; o/dout/out rows
+    int bh, t, heads;
     float scale;
     int causal;
     int *status;
@@ -57,15 +71,87 @@ __device__ __forceinline__ bool await(uint64_t *bar, uint32_t parity, int *statu
     }
 }
 
-// Half `half` (32 of the 64 columns) of row r (< t, else zeros) of a [t, 64]
-// f16 head into a swizzled 16 KB tile.
-__device__ __forceinline__ void stage_half_rows(uint8_t *dst, const __half *src, int r, int half, int t) {
-    const uint4 *s = reinterpret_cast<const uint4 *>(src + static_cast<int64_t>(r) * AD);
+// Half `half` (32 of the 64 columns) of row r (zeros when !live) into a
+// swizzled 16 KB f16 tile; F32 sources are rounded to f16 on the way.
+template <bool F32>
+__device__ __forceinline__ void stage_half_rows(uint8_t *dst, const void *base, int64_t off, int r, int half,
+                                                bool live) {
+    if (F32) {
+        const float4 *s = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off) + 8 * half;
 #pragma unroll
-    for (int c = 4 * half; c < 4 * half + 4; c++) {
-        const uint4 v = r < t ? __ldg(s + c) : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, c)) = v;
+        for (int c = 0; c < 4; c++) {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (live) {
+                const float4 a = __ldg(s + 2 * c), b = __ldg(s + 2 * c + 1);
+                const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+                const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+                v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                               *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            }
+            *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, 4 * half + c)) = v;
+        }
+    } else {
+        const uint4 *s = reinterpret_cast<const uint4 *>(static_cast<const __half *>(base) + off) + 4 * half;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 v = live ? __ldg(s + c) : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, 4 * half + c)) = v;
+        }
     }
+}
+
+// 16 consecutive output values at element `off` of `base` (f16 or f32).
+template <bool F32>
+__device__ __forceinline__ void store16(void *base, int64_t off, const float (&y)[16]) {
+    if (F32) {
+        float4 *d = reinterpret_cast<float4 *>(static_cast<float *>(base) + off);
+#pragma unroll
+        for (int i = 0; i < 4; i++) d[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+    } else {
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const __half2 h = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+            o[i] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        uint4 *d = reinterpret_cast<uint4 *>(static_cast<__half *>(base) + off);
+        d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+// sum over this thread's 32 columns of a[i] * b[i] (f16 or f32 rows)
+template <bool F32>
+__device__ __forceinline__ float dot_half(const void *a, const void *b, int64_t off, int half) {
+    float acc = 0.0f;
+    if (F32) {
+        const float4 *pa = reinterpret_cast<const float4 *>(static_cast<const float *>(a) + off) + 8 * half;
+        const float4 *pb = reinterpret_cast<const float4 *>(static_cast<const float *>(b) + off) + 8 * half;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const float4 x = __ldg(pa + c), y = __ldg(pb + c);
+            acc = fmaf(x.x, y.x, acc);
+            acc = fmaf(x.y, y.y, acc);
+            acc = fmaf(x.z, y.z, acc);
+            acc = fmaf(x.w, y.w, acc);
+        }
+    } else {
+        const uint4 *pa = reinterpret_cast<const uint4 *>(static_cast<const __half *>(a) + off) + 4 * half;
+        const uint4 *pb = reinterpret_cast<const uint4 *>(static_cast<const __half *>(b) + off) + 4 * half;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 x = __ldg(pa + c), y = __ldg(pb + c);
+            const uint32_t xv[4] = {x.x, x.y, x.z, x.w}, yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&xv[i]));
+                const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&yv[i]));
+                acc = fmaf(fa.x, fb.x, acc);
+                acc = fmaf(fa.y, fb.y, acc);
+            }
+        }
+    }
+    return acc;
 }
 
 // 16 f32 values -> 8 packed f16 pairs.
@@ -105,6 +191,7 @@ __device__ __forceinline__ float fast_exp(float x) { return exp2f(x * 1.44269504
 // Threads r and r + 128 share row r % 128: thread r < 128 owns columns
 // [0, 64) of the row, thread r + 128 columns [64, 128) (warps w and w + 4 read
 // the same TMEM lanes).  Row reductions combine the two halves through `red`.
+template <bool F32>
 __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,7 +201,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
     const int tid = threadIdx.x, warp = tid >> 5;
     const int r = tid & (AT - 1), half = tid >> 7;
-    const int64_t head = static_cast<int64_t>(blockIdx.x) * g.t * AD;
+    const int64_t rq = g.mq.at(blockIdx.x, g.heads, r), ro = g.mo.at(blockIdx.x, g.heads, r);
+    const bool live = r < g.t;
 
     if (tid == 0) {
         st::mbar_init(&bar[0], 1);
@@ -125,9 +213,9 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
         st::tmem_alloc(tslot, 256);
         st::tmem_relinquish();
     }
-    stage_half_rows(sQ, g.q + head, r, half, g.t);
-    stage_half_rows(sK, g.k + head, r, half, g.t);
-    stage_half_rows(sV, g.v + head, r, half, g.t);
+    stage_half_rows<F32>(sQ, g.q, rq, r, half, live);
+    stage_half_rows<F32>(sK, g.k, rq, r, half, live);
+    stage_half_rows<F32>(sV, g.v, rq, r, half, live);
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
@@ -201,13 +289,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
         float y[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) y[j] = __uint_as_float(y16[j]) * inv;
-        uint32_t o[8];
-        pack16(y, o);
-        if (r < g.t && ok) {
-            uint4 *dst = reinterpret_cast<uint4 *>(g.out + head + static_cast<int64_t>(r) * AD + c0);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
+        if (live && ok) store16<F32>(g.out, ro + c0, y);
     }
     st::tc_fence_before();
     __syncthreads();
@@ -217,6 +299,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     }
 }
 
+template <bool F32>
 __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -227,7 +310,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
     const int tid = threadIdx.x, warp = tid >> 5;
     const int r = tid & (AT - 1), half = tid >> 7;
-    const int64_t head = static_cast<int64_t>(blockIdx.x) * g.t * AD;
+    const int64_t rq = g.mq.at(blockIdx.x, g.heads, r), ro = g.mo.at(blockIdx.x, g.heads, r);
+    const bool live = r < g.t;
 
     if (tid == 0) {
         st::mbar_init(&bar[0], 1);
@@ -238,28 +322,13 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
         st::tmem_alloc(tslot, 512);
         st::tmem_relinquish();
     }
-    stage_half_rows(sQ, g.q + head, r, half, g.t);
-    stage_half_rows(sK, g.k + head, r, half, g.t);
-    stage_half_rows(sV, g.v + head, r, half, g.t);
-    stage_half_rows(sO, g.dout + head, r, half, g.t);
+    stage_half_rows<F32>(sQ, g.q, rq, r, half, live);
+    stage_half_rows<F32>(sK, g.k, rq, r, half, live);
+    stage_half_rows<F32>(sV, g.v, rq, r, half, live);
+    stage_half_rows<F32>(sO, g.dout, ro, r, half, live);
     // D_r = sum_d dO[r,d] * O[r,d], this thread's 32 of the 64 d, then exchanged
-    float dsum = 0.0f;
-    if (r < g.t) {
-        const uint4 *po = reinterpret_cast<const uint4 *>(g.o + head + static_cast<int64_t>(r) * AD) + 4 * half;
-        const uint4 *pd = reinterpret_cast<const uint4 *>(g.dout + head + static_cast<int64_t>(r) * AD) + 4 * half;
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const uint4 a = __ldg(po + c), b = __ldg(pd + c);
-            const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&av[i]));
-                const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&bv[i]));
-                dsum = fmaf(fa.x, fb.x, dsum);
-                dsum = fmaf(fa.y, fb.y, dsum);
-            }
-        }
-    }
+    const float dsum_half = live ? dot_half<F32>(g.o, g.dout, ro, half) : 0.0f;
+    float dsum = dsum_half;
     red[half * AT + r] = dsum;
     const float lse = r < g.t ? g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] : 0.0f;
     st::fence_proxy_async_smem();
@@ -331,7 +400,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     // row r of dV, dK (rows = keys) and dQ (rows = queries), this thread's 32 columns
 #pragma unroll
     for (int w = 0; w < 3; w++) {
-        __half *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
+        void *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
         const uint32_t src = w == 0 ? tdV : w == 1 ? tdK : tdQ;
 #pragma unroll
         for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
@@ -341,13 +410,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
             float y[16];
 #pragma unroll
             for (int j = 0; j < 16; j++) y[j] = __uint_as_float(x[j]);
-            uint32_t o[8];
-            pack16(y, o);
-            if (r < g.t && ok) {
-                uint4 *dst = reinterpret_cast<uint4 *>(dst_t + head + static_cast<int64_t>(r) * AD + c0);
-                dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            }
+            if (live && ok) store16<F32>(dst_t, rq + c0, y);
         }
     }
     st::tc_fence_before();
@@ -373,6 +436,30 @@ st_status check(st_handle *h, const void *q, const void *k, const void *v, int64
     return ST_OK;
 }
 
+template <bool F32>
+st_status launch_fwd(st_handle *h, const AttnArgs &g) {
+    static bool attr = false;
+    if (!attr) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+        attr = true;
+    }
+    k_attn_fwd<F32><<<static_cast<unsigned>(g.bh), ATHREADS, FWD_SMEM, h->stream>>>(g);
+    return st_after_launch(h, "k_attn_fwd");
+}
+
+template <bool F32>
+st_status launch_bwd(st_handle *h, const AttnArgs &g) {
+    static bool attr = false;
+    if (!attr) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+        attr = true;
+    }
+    k_attn_bwd<F32><<<static_cast<unsigned>(g.bh), ATHREADS, BWD_SMEM, h->stream>>>(g);
+    return st_after_launch(h, "k_attn_bwd");
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 }  // namespace
 
 extern "C" st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse,
@@ -380,26 +467,23 @@ extern "C" st_status st_attn_fwd(st_handle *h, const void *q, const void *k, con
     if (!h) return ST_INVALID_ARG;
     st_status s = check(h, q, k, v, bh, t, d, "st_attn_fwd");
     if (s != ST_OK) return s;
-    if (!o || !lse || (reinterpret_cast<uintptr_t>(o) & 15u)) return h->fail(ST_INVALID_ARG, "st_attn_fwd: bad output");
+    if (!o || !lse || !al16(o)) return h->fail(ST_INVALID_ARG, "st_attn_fwd: bad output");
     cudaSetDevice(h->device);
-    static bool attr = false;
-    if (!attr) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
-        attr = true;
-    }
     AttnArgs g{};
-    g.q = static_cast<const __half *>(q);
-    g.k = static_cast<const __half *>(k);
-    g.v = static_cast<const __half *>(v);
-    g.out = static_cast<__half *>(o);
+    g.q = q;
+    g.k = k;
+    g.v = v;
+    g.out = o;
     g.lse = lse;
+    g.mq = RowMap{t * AD, 0, AD};
+    g.mo = g.mq;
     g.bh = static_cast<int>(bh);
     g.t = static_cast<int>(t);
+    g.heads = 1;
     g.scale = scale;
     g.causal = causal;
     g.status = h->d_status;
-    k_attn_fwd<<<static_cast<unsigned>(bh), ATHREADS, FWD_SMEM, h->stream>>>(g);
-    return st_after_launch(h, "k_attn_fwd");
+    return launch_fwd<false>(h, g);
 }
 
 extern "C" st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o,
@@ -408,31 +492,84 @@ extern "C" st_status st_attn_bwd(st_handle *h, const void *q, const void *k, con
     if (!h) return ST_INVALID_ARG;
     st_status s = check(h, q, k, v, bh, t, d, "st_attn_bwd");
     if (s != ST_OK) return s;
-    if (!o || !dout || !lse || !dq || !dk || !dv ||
-        ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout) | reinterpret_cast<uintptr_t>(dq) |
-          reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15u))
+    if (!o || !dout || !lse || !dq || !dk || !dv || !al16(o) || !al16(dout) || !al16(dq) || !al16(dk) || !al16(dv))
         return h->fail(ST_INVALID_ARG, "st_attn_bwd: null or unaligned buffer");
     cudaSetDevice(h->device);
-    static bool attr = false;
-    if (!attr) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
-        attr = true;
-    }
     AttnArgs g{};
-    g.q = static_cast<const __half *>(q);
-    g.k = static_cast<const __half *>(k);
-    g.v = static_cast<const __half *>(v);
-    g.o = static_cast<const __half *>(o);
-    g.dout = static_cast<const __half *>(dout);
-    g.dq = static_cast<__half *>(dq);
-    g.dk = static_cast<__half *>(dk);
-    g.dv = static_cast<__half *>(dv);
+    g.q = q;
+    g.k = k;
+    g.v = v;
+    g.o = o;
+    g.dout = dout;
+    g.dq = dq;
+    g.dk = dk;
+    g.dv = dv;
     g.lse = const_cast<float *>(lse);
+    g.mq = RowMap{t * AD, 0, AD};
+    g.mo = g.mq;
     g.bh = static_cast<int>(bh);
     g.t = static_cast<int>(t);
+    g.heads = 1;
     g.scale = scale;
     g.causal = causal;
     g.status = h->d_status;
-    k_attn_bwd<<<static_cast<unsigned>(bh), ATHREADS, BWD_SMEM, h->stream>>>(g);
-    return st_after_launch(h, "k_attn_bwd");
+    return launch_bwd<false>(h, g);
+}
+
+extern "C" st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o, float *lse, int64_t batch,
+                                        int64_t heads, int64_t t, int64_t d, float scale, int32_t causal) {
+    if (!h) return ST_INVALID_ARG;
+    if (batch < 1 || heads < 1 || batch * heads > (1 << 30)) return h->fail(ST_INVALID_ARG, "st_attn_fwd_packed: bad shape");
+    st_status s = check(h, qkv, qkv, qkv, batch * heads, t, d, "st_attn_fwd_packed");
+    if (s != ST_OK) return s;
+    if (!o || !lse || !al16(o)) return h->fail(ST_INVALID_ARG, "st_attn_fwd_packed: bad output");
+    cudaSetDevice(h->device);
+    const int64_t width = heads * AD;
+    AttnArgs g{};
+    g.q = qkv;
+    g.k = qkv + width;
+    g.v = qkv + 2 * width;
+    g.out = o;
+    g.lse = lse;
+    g.mq = RowMap{t * 3 * width, AD, 3 * width};
+    g.mo = RowMap{t * width, AD, width};
+    g.bh = static_cast<int>(batch * heads);
+    g.t = static_cast<int>(t);
+    g.heads = static_cast<int>(heads);
+    g.scale = scale;
+    g.causal = causal;
+    g.status = h->d_status;
+    return launch_fwd<true>(h, g);
+}
+
+extern "C" st_status st_attn_bwd_packed(st_handle *h, const float *qkv, const float *o, const float *dout,
+                                        const float *lse, float *dqkv, int64_t batch, int64_t heads, int64_t t,
+                                        int64_t d, float scale, int32_t causal) {
+    if (!h) return ST_INVALID_ARG;
+    if (batch < 1 || heads < 1 || batch * heads > (1 << 30)) return h->fail(ST_INVALID_ARG, "st_attn_bwd_packed: bad shape");
+    st_status s = check(h, qkv, qkv, qkv, batch * heads, t, d, "st_attn_bwd_packed");
+    if (s != ST_OK) return s;
+    if (!o || !dout || !lse || !dqkv || !al16(o) || !al16(dout) || !al16(dqkv))
+        return h->fail(ST_INVALID_ARG, "st_attn_bwd_packed: null or unaligned buffer");
+    cudaSetDevice(h->device);
+    const int64_t width = heads * AD;
+    AttnArgs g{};
+    g.q = qkv;
+    g.k = qkv + width;
+    g.v = qkv + 2 * width;
+    g.o = o;
+    g.dout = dout;
+    g.dq = dqkv;
+    g.dk = dqkv + width;
+    g.dv = dqkv + 2 * width;
+    g.lse = const_cast<float *>(lse);
+    g.mq = RowMap{t * 3 * width, AD, 3 * width};
+    g.mo = RowMap{t * width, AD, width};
+    g.bh = static_cast<int>(batch * heads);
+    g.t = static_cast<int>(t);
+    g.heads = static_cast<int>(heads);
+    g.scale = scale;
+    g.causal = causal;
+    g.status = h->d_status;
+    return launch_bwd<true>(h, g);
 }

@@ -21,6 +21,8 @@ enum StScratchSlot {
     SLOT_KNN_PART,    // kNN per-split partial top-k lists
     SLOT_KNN_Q,       // kNN quantised queries
     SLOT_KNN_MISC,
+    SLOT_STEP,        // LayerNorm parameter-gradient partials
+    SLOT_STEP_ROWS,   // per-row cross-entropy losses
     SLOT_COUNT
 };
 

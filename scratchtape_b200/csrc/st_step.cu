@@ -1,0 +1,360 @@
+// st_step.cu -- the row and elementwise kernels of the byte-level transformer
+// training step that surround its GEMMs and attention: token + position
+// embedding, LayerNorm, cross-entropy, Adam.
+//
+// Reference (src/gpu_step): k_embed / k_embed_bwd_tok / k_embed_bwd_pos
+// (tokens.rs:125-192), k_ln_fwd / k_ln_bwd_dx / k_ln_bwd_params
+// (rows.rs:177-293, biased variance), k_ce_rows / k_ce_bwd (tokens.rs:194-253),
+// and Adam (src/optim.rs:42-57; the reference runs it on the CPU).  As in the
+// reference, every reduction has a fixed order (no float atomics), so a step
+// is bit-reproducible.
+//
+// Layout: rows of d = 256 floats (one warp per row, 8 per lane), vocab 256.
+#include <algorithm>
+
+#include "st_internal.h"
+
+namespace {
+
+constexpr int MAXD = 1024;  // widest row the per-warp kernels take (32 lanes x 32)
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// x[r, :] = tok[ids[r], :] + pos[r % t, :]
+__global__ void k_embed_fwd(const int32_t *ids, const float *tok, const float *pos, float *x, int64_t rows, int t,
+                            int d) {
+    const int64_t n4 = rows * d / 4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = i * 4;
+        const int64_t r = e / d;
+        const int c = static_cast<int>(e % d);
+        const float4 a = *reinterpret_cast<const float4 *>(tok + static_cast<int64_t>(ids[r]) * d + c);
+        const float4 b = *reinterpret_cast<const float4 *>(pos + static_cast<int64_t>(r % t) * d + c);
+        *reinterpret_cast<float4 *>(x + e) = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    }
+}
+
+// dtok[v, :] (+)= sum over rows r with ids[r] == v, in row order, of dx[r, :].
+// One warp per vocabulary row; the warp scans the ids 32 at a time and adds
+// the matching rows in order (lane = 8 of the 256 columns... d/32 columns).
+__global__ void k_embed_bwd_tok(const int32_t *ids, const float *dx, float *dtok, int64_t rows, int d, int vocab,
+                                int accumulate) {
+    const int v = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (v >= vocab) return;
+    const int per = d / 32;  // columns per lane (d % 32 == 0)
+    float acc[MAXD / 32];
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++) acc[j] = 0.0f;
+    for (int64_t r0 = 0; r0 < rows; r0 += 32) {
+        const int64_t r = r0 + lane;
+        const bool hit = r < rows && ids[r] == v;
+        unsigned m = __ballot_sync(0xffffffffu, hit);
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const float *row = dx + (r0 + src) * d + lane * per;
+#pragma unroll
+            for (int j = 0; j < MAXD / 32; j++)
+                if (j < per) acc[j] += row[j];
+        }
+    }
+    float *out = dtok + static_cast<int64_t>(v) * d + lane * per;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) out[j] = accumulate ? out[j] + acc[j] : acc[j];
+}
+
+// dpos[i, c] (+)= sum over b ascending of dx[b*t + i, c]
+__global__ void k_embed_bwd_pos(const float *dx, float *dpos, int batch, int t, int d, int accumulate) {
+    const int64_t n = static_cast<int64_t>(t) * d;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float s = 0.0f;
+        for (int b = 0; b < batch; b++) s += dx[static_cast<int64_t>(b) * n + e];
+        dpos[e] = accumulate ? dpos[e] + s : s;
+    }
+}
+
+// y = (x - mean) * rstd * gamma + beta, rstd = 1 / sqrt(var + eps), biased var.
+__global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, float *y, float *mean, float *rstd,
+                         int64_t rows, int d, float eps) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int per = d / 32;
+    const float *xr = x + r * d + lane * per;
+    float v[MAXD / 32];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            v[j] = xr[j];
+            s += v[j];
+        }
+    const float mu = warp_sum_f(s) / static_cast<float>(d);
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            const float c = v[j] - mu;
+            q += c * c;
+        }
+    const float var = warp_sum_f(q) / static_cast<float>(d);
+    const float rs = 1.0f / sqrtf(var + eps);
+    float *yr = y + r * d + lane * per;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) yr[j] = (v[j] - mu) * rs * gamma[lane * per + j] + beta[lane * per + j];
+    if (lane == 0) {
+        mean[r] = mu;
+        rstd[r] = rs;
+    }
+}
+
+// dx (+)= rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma
+__global__ void k_ln_bwd_dx(const float *dy, const float *x, const float *gamma, const float *mean, const float *rstd,
+                            float *dx, int64_t rows, int d, int accumulate) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int per = d / 32;
+    const float mu = mean[r], rs = rstd[r];
+    float gv[MAXD / 32], xh[MAXD / 32];
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            const int c = lane * per + j;
+            xh[j] = (x[r * d + c] - mu) * rs;
+            gv[j] = dy[r * d + c] * gamma[c];
+            s1 += gv[j];
+            s2 += gv[j] * xh[j];
+        }
+    const float m1 = warp_sum_f(s1) / static_cast<float>(d), m2 = warp_sum_f(s2) / static_cast<float>(d);
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            const int64_t e = r * d + lane * per + j;
+            const float g = rs * (gv[j] - m1 - xh[j] * m2);
+            dx[e] = accumulate ? dx[e] + g : g;
+        }
+}
+
+// Per column, partial sums over a chunk of rows (row order), then the
+// partials in chunk order: dgamma += sum dy * xhat, dbeta += sum dy.
+__global__ void k_ln_bwd_params_part(const float *dy, const float *x, const float *mean, const float *rstd, float *part,
+                                     int64_t rows, int d, int64_t rows_per_chunk) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int chunk = blockIdx.y;
+    if (c >= d) return;
+    const int64_t r0 = chunk * rows_per_chunk, r1 = min(rows, r0 + rows_per_chunk);
+    float sg = 0.0f, sb = 0.0f;
+    for (int64_t r = r0; r < r1; r++) {
+        const float g = dy[r * d + c];
+        sg += g * ((x[r * d + c] - mean[r]) * rstd[r]);
+        sb += g;
+    }
+    part[(static_cast<int64_t>(chunk) * 2) * d + c] = sg;
+    part[(static_cast<int64_t>(chunk) * 2 + 1) * d + c] = sb;
+}
+__global__ void k_ln_bwd_params_sum(const float *part, float *dgamma, float *dbeta, int d, int chunks) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= d) return;
+    float sg = 0.0f, sb = 0.0f;
+    for (int k = 0; k < chunks; k++) {
+        sg += part[(static_cast<int64_t>(k) * 2) * d + c];
+        sb += part[(static_cast<int64_t>(k) * 2 + 1) * d + c];
+    }
+    dgamma[c] += sg;
+    dbeta[c] += sb;
+}
+
+// Per row: loss_r = log(sum exp(x - max)) + max - x[y];
+// dlogits = (softmax(x) - onehot(y)) * grad_scale.
+__global__ void k_ce(const float *logits, const int32_t *targets, float *loss_rows, float *dlogits, int64_t rows,
+                     int vocab, float grad_scale) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int per = vocab / 32;
+    const float *xr = logits + r * vocab + lane * per;
+    float v[MAXD / 32];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            v[j] = xr[j];
+            m = fmaxf(m, v[j]);
+        }
+    m = warp_max_f(m);
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < MAXD / 32; j++)
+        if (j < per) {
+            v[j] = expf(v[j] - m);
+            s += v[j];
+        }
+    s = warp_sum_f(s);
+    const int y = targets[r];
+    if (lane == 0) loss_rows[r] = logf(s) + m - logits[r * vocab + y];
+    const float inv = 1.0f / s;
+    if (dlogits) {
+        float *dr = dlogits + r * vocab + lane * per;
+#pragma unroll
+        for (int j = 0; j < MAXD / 32; j++)
+            if (j < per) dr[j] = (v[j] * inv - (lane * per + j == y ? 1.0f : 0.0f)) * grad_scale;
+    }
+}
+
+// out[0] = mean of x[0..n): per-thread strided sums, then a fixed tree.
+__global__ void k_mean(const float *x, int64_t n, float *out) {
+    __shared__ float sh[1024];
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+    sh[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[0] = sh[0] / static_cast<float>(n);
+}
+
+// Adam (src/optim.rs:42-57) in the reference's f32 operation order:
+// m = m*b1 + g*(1-b1); v = v*b2 + (g*g)*(1-b2); u = (m*i1 / (sqrt(v*i2) + eps)) * lr
+__global__ void k_adam(float *p, const float *g, float *m, float *v, int64_t n, float lr, float b1, float b2, float eps,
+                       float i1, float i2) {
+    const float c1 = __fsub_rn(1.0f, b1), c2 = __fsub_rn(1.0f, b2);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float gi = g[i];
+        const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, c1));
+        const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), c2));
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = __fmul_rn(mi, i1), vh = __fmul_rn(vi, i2);
+        const float u = __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), lr);
+        p[i] = __fsub_rn(p[i], u);
+    }
+}
+
+int blocks_for(int64_t n, int threads) {
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, 148 * 16)));
+}
+
+float powi_f32(float a, int b) {  // square-and-multiply, as Rust's f32::powi lowers
+    float r = 1.0f;
+    for (;;) {
+        if (b & 1) r *= a;
+        b /= 2;
+        if (b == 0) break;
+        a *= a;
+    }
+    return r;
+}
+
+}  // namespace
+
+extern "C" st_status st_embed_fwd(st_handle *h, const int32_t *ids, const float *tok, const float *pos, float *x,
+                                  int64_t batch, int64_t t, int64_t d) {
+    if (!h) return ST_INVALID_ARG;
+    if (!ids || !tok || !pos || !x || batch < 1 || t < 1 || d < 4 || d % 4 != 0)
+        return h->fail(ST_INVALID_ARG, "st_embed_fwd: bad arguments");
+    cudaSetDevice(h->device);
+    const int64_t rows = batch * t;
+    k_embed_fwd<<<blocks_for(rows * d / 4, 256), 256, 0, h->stream>>>(ids, tok, pos, x, rows, static_cast<int>(t),
+                                                                     static_cast<int>(d));
+    return st_after_launch(h, "k_embed_fwd");
+}
+
+extern "C" st_status st_embed_bwd(st_handle *h, const int32_t *ids, const float *dx, float *dtok, float *dpos,
+                                  int64_t batch, int64_t t, int64_t d, int64_t vocab, int32_t accumulate) {
+    if (!h) return ST_INVALID_ARG;
+    if (!ids || !dx || !dtok || !dpos || batch < 1 || t < 1 || d < 32 || d % 32 != 0 || d > MAXD || vocab < 1)
+        return h->fail(ST_INVALID_ARG, "st_embed_bwd: bad arguments");
+    cudaSetDevice(h->device);
+    const int wpb = 8;
+    k_embed_bwd_tok<<<static_cast<unsigned>((vocab + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
+        ids, dx, dtok, batch * t, static_cast<int>(d), static_cast<int>(vocab), accumulate);
+    st_status s = st_after_launch(h, "k_embed_bwd_tok");
+    if (s != ST_OK) return s;
+    k_embed_bwd_pos<<<blocks_for(t * d, 256), 256, 0, h->stream>>>(dx, dpos, static_cast<int>(batch),
+                                                                   static_cast<int>(t), static_cast<int>(d), accumulate);
+    return st_after_launch(h, "k_embed_bwd_pos");
+}
+
+extern "C" st_status st_layernorm_fwd(st_handle *h, const float *x, const float *gamma, const float *beta, float *y,
+                                      float *mean, float *rstd, int64_t rows, int64_t d, float eps) {
+    if (!h) return ST_INVALID_ARG;
+    if (!x || !gamma || !beta || !y || !mean || !rstd || rows < 1 || d < 32 || d % 32 != 0 || d > MAXD)
+        return h->fail(ST_INVALID_ARG, "st_layernorm_fwd: bad arguments (d a multiple of 32 up to %d)", MAXD);
+    cudaSetDevice(h->device);
+    const int wpb = 8;
+    k_ln_fwd<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(x, gamma, beta, y, mean, rstd,
+                                                                                        rows, static_cast<int>(d), eps);
+    return st_after_launch(h, "k_ln_fwd");
+}
+
+extern "C" st_status st_layernorm_bwd(st_handle *h, const float *dy, const float *x, const float *gamma,
+                                      const float *mean, const float *rstd, float *dx, float *dgamma, float *dbeta,
+                                      int64_t rows, int64_t d, int32_t accumulate) {
+    if (!h) return ST_INVALID_ARG;
+    if (!dy || !x || !gamma || !mean || !rstd || !dx || !dgamma || !dbeta || rows < 1 || d < 32 || d % 32 != 0 ||
+        d > MAXD)
+        return h->fail(ST_INVALID_ARG, "st_layernorm_bwd: bad arguments");
+    cudaSetDevice(h->device);
+    const int wpb = 8;
+    k_ln_bwd_dx<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
+        dy, x, gamma, mean, rstd, dx, rows, static_cast<int>(d), accumulate);
+    st_status s = st_after_launch(h, "k_ln_bwd_dx");
+    if (s != ST_OK) return s;
+    const int chunks = static_cast<int>(std::min<int64_t>(64, rows));
+    const int64_t rpc = (rows + chunks - 1) / chunks;
+    float *part = static_cast<float *>(st_scratch(h, SLOT_STEP, sizeof(float) * 2 * chunks * d));
+    if (!part) return ST_NO_MEMORY;
+    dim3 grid(static_cast<unsigned>((d + 127) / 128), static_cast<unsigned>(chunks));
+    k_ln_bwd_params_part<<<grid, 128, 0, h->stream>>>(dy, x, mean, rstd, part, rows, static_cast<int>(d), rpc);
+    s = st_after_launch(h, "k_ln_bwd_params_part");
+    if (s != ST_OK) return s;
+    k_ln_bwd_params_sum<<<static_cast<unsigned>((d + 127) / 128), 128, 0, h->stream>>>(part, dgamma, dbeta,
+                                                                                       static_cast<int>(d), chunks);
+    return st_after_launch(h, "k_ln_bwd_params_sum");
+}
+
+extern "C" st_status st_cross_entropy(st_handle *h, const float *logits, const int32_t *targets, float *loss,
+                                      float *dlogits, int64_t rows, int64_t vocab) {
+    if (!h) return ST_INVALID_ARG;
+    if (!logits || !targets || !loss || rows < 1 || vocab < 32 || vocab % 32 != 0 || vocab > MAXD)
+        return h->fail(ST_INVALID_ARG, "st_cross_entropy: bad arguments");
+    cudaSetDevice(h->device);
+    float *loss_rows = static_cast<float *>(st_scratch(h, SLOT_STEP_ROWS, sizeof(float) * rows));
+    if (!loss_rows) return ST_NO_MEMORY;
+    const int wpb = 8;
+    k_ce<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
+        logits, targets, loss_rows, dlogits, rows, static_cast<int>(vocab), 1.0f / static_cast<float>(rows));
+    st_status s = st_after_launch(h, "k_ce");
+    if (s != ST_OK) return s;
+    k_mean<<<1, 1024, 0, h->stream>>>(loss_rows, rows, loss);
+    return st_after_launch(h, "k_mean");
+}
+
+extern "C" st_status st_adam(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t step,
+                             float lr, float beta1, float beta2, float eps) {
+    if (!h) return ST_INVALID_ARG;
+    if (!p || !g || !m || !v || n < 1 || step < 1) return h->fail(ST_INVALID_ARG, "st_adam: bad arguments");
+    cudaSetDevice(h->device);
+    const float bc1 = 1.0f - powi_f32(beta1, step), bc2 = 1.0f - powi_f32(beta2, step);
+    k_adam<<<blocks_for(n, 256), 256, 0, h->stream>>>(p, g, m, v, n, lr, beta1, beta2, eps, 1.0f / bc1, 1.0f / bc2);
+    return st_after_launch(h, "k_adam");
+}
