@@ -52,16 +52,16 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (c2: 200, c5: 5)")
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (c2: 20, c5: 3)")
-    p.add_argument("--config", default="c2", choices=["c2", "c3", "c5"])
+    p.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"])
     p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
     p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     a = p.parse_args()
     if a.steps is None:
-        a.steps = 5 if a.config == "c5" else 200
+        a.steps = {"c5": 5, "c4": 24}.get(a.config, 200)
     if a.warmup is None:
-        a.warmup = 3 if a.config == "c5" else 20
+        a.warmup = {"c5": 3, "c4": 4}.get(a.config, 20)
     return a
 
 
@@ -770,6 +770,194 @@ def run_ours_c3(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C4: full byte-level transformer training step: vocab
+# 256, d 256, 4 layers, 4 heads, d_ff 1024, seq 128, batch 64 per GPU,
+# pre-LN, learned positions, tied embeddings, CE + Adam; data parallel with
+# local-SGD averaging every 8 steps.
+# ---------------------------------------------------------------------------
+def c4_batch(cfg, seed, step):
+    rng = np.random.default_rng(seed * 1000003 + step)
+    ids = rng.integers(0, 256, cfg.batch * cfg.t + 1, dtype=np.int32)
+    return ids[:-1].copy(), ids[1:].copy()
+
+
+def cpu_baseline_c4(cfg):
+    """The restated tensor.rs matmul on one thread over one step's GEMM shapes
+    at batch 1 (128 tokens), extrapolated x64 to the configured batch.  The
+    non-GEMM work (LN, softmax, CE, Adam) is not counted, so the figure flatters
+    the CPU."""
+    import oracle
+    rows = cfg.t
+    rng = np.random.default_rng(0)
+    shapes = []
+    for _ in range(cfg.layers):
+        for (k, n) in ((cfg.d, 3 * cfg.d), (cfg.d, cfg.d), (cfg.d, cfg.dff), (cfg.dff, cfg.d)):
+            shapes += [(rows, k, n), (rows, n, k), (k, rows, n)]  # fwd, dX, dW
+    shapes += [(rows, cfg.d, cfg.vocab), (rows, cfg.vocab, cfg.d), (cfg.vocab, rows, cfg.d)]
+    mats = [(rng.standard_normal((m, k)).astype(np.float32), rng.standard_normal((k, n)).astype(np.float32))
+            for m, k, n in shapes]
+    t0 = time.perf_counter()
+    for a, b in mats:
+        oracle.matmul_layout(a, b, threads=1)
+    el = (time.perf_counter() - t0) * cfg.batch
+    return el
+
+
+def run_reference_c4(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    cfg = _lm_config()
+    for _ in range(max(1, args.warmup // 4)):
+        cpu_baseline_c4(cfg)
+    ts = [cpu_baseline_c4(cfg) for _ in range(max(1, min(args.steps, 3)))]
+    el = float(np.median(ts))
+    v = cfg.flops_per_step() / el / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C4 training step GEMMs (sampled at batch 1, x64)", "parallelism": "CPU, rank 0"},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                             "sample": "one step's GEMM shapes at batch 1 on the restated tensor.rs matmul (1 thread), "
+                                       "extrapolated to batch 64; LN/softmax/CE/Adam not counted"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _lm_config():
+    """LmConfig without importing the package (the reference arm must not load the library)."""
+    class Cfg:
+        vocab, d, layers, heads, dff, t, batch = 256, 256, 4, 4, 1024, 128, 64
+
+        def flops_per_step(self):
+            rows = self.batch * self.t
+            lin = 2 * rows * (self.d * 3 * self.d + self.d * self.d + 2 * self.d * self.dff)
+            head = 2 * rows * self.d * self.vocab
+            attn = 4 * self.batch * self.heads * (self.t * (self.t + 1) // 2) * (self.d // self.heads)
+            return 3 * (self.layers * (lin + attn) + head)
+    return Cfg()
+
+
+def run_ours_c4(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    group = None
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import scratchtape_b200 as st
+    from scratchtape_b200.lm import LmConfig, TinyLM
+    peaks, peak_src = load_peaks()
+    h = st.handle()
+    cfg = LmConfig()
+    model = TinyLM(cfg, device, seed=0)  # same init on every rank
+    n_steps = args.warmup + args.steps
+    host = [c4_batch(cfg, rank, i) for i in range(n_steps + 8)]
+    ids_d = [torch.from_numpy(a).to(device) for a, _ in host]
+    tg_d = [torch.from_numpy(b).to(device) for _, b in host]
+
+    n0 = h.launches
+    model.train_step(ids_d[0], tg_d[0], group)
+    torch.cuda.synchronize()
+    launches_per_step = h.launches - n0
+    for i in range(1, args.warmup):
+        model.train_step(ids_d[i], tg_d[i], group)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    losses = []
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for i in range(args.steps):
+            ev[i][0].record()
+            loss = model.train_step(ids_d[args.warmup + i], tg_d[args.warmup + i], group)
+            ev[i][1].record()
+            losses.append(loss.clone())
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    if world > 1:
+        tt = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    ms = total_ms / args.steps
+    value = cfg.flops_per_step() * world / (ms / 1e3) / 1e12
+    tokens_s = cfg.batch * cfg.t * world / (ms / 1e3)
+
+    # e2e: host bytes in, loss out, every step, through TinyLM.train_step
+    hids = [torch.from_numpy(a).pin_memory() for a, _ in host[:8]]
+    htg = [torch.from_numpy(b).pin_memory() for _, b in host[:8]]
+    hloss = torch.empty(1, dtype=torch.float32).pin_memory()
+    ids_buf, tg_buf = torch.empty_like(ids_d[0]), torch.empty_like(tg_d[0])
+    e2e_steps = 8
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        ids_buf.copy_(hids[i], non_blocking=True)
+        tg_buf.copy_(htg[i], non_blocking=True)
+        loss = model.train_step(ids_buf, tg_buf, group)
+        hloss.copy_(loss, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    e2e_value = cfg.flops_per_step() * world * e2e_steps / (e_ms / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "tf32 GEMMs, f16-operand attention, f32 elsewhere", "data": "synthetic",
+            "config": {"workload": "C4 byte-level transformer training step (BASELINE configs[3]): vocab 256, d 256, "
+                                   "4 layers, 4 heads, d_ff 1024, seq 128, batch 64 per GPU, pre-LN, learned "
+                                   "positions, tied embeddings, CE + Adam, local-SGD average every 8 steps",
+                       "global_batch": cfg.batch * world, "seq_len": cfg.t,
+                       "parallelism": "dp%d local SGD (NCCL all-reduce every %d steps)" % (world, cfg.sync_every)
+                       if world > 1 else "single GPU",
+                       "tokens_per_s": tokens_s, "gemm_flops_per_step": cfg.flops_per_step(),
+                       "loss_first_last": [float(losses[0].item()), float(losses[-1].item())],
+                       "l2": "activations (~160 MB) exceed L2; no flush"},
+            "roofline": {"bound": "tensor", "achieved": cfg.flops_per_step() / (ms / 1e3) / 1e12,
+                         "peak": float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])), "unit": "TFLOP/s",
+                         "frac": cfg.flops_per_step() / (ms / 1e3) / 1e12 /
+                         float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])),
+                         "traffic": None, "peak_source": peak_src + " (bf16 dense, sustained; TF32 peak is lower)",
+                         "kernel": "whole step (TF32 GEMMs dominate)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(2 * 4 * cfg.batch * cfg.t),
+                    "d2h_bytes_per_step": 4, "ms_per_step": e_ms / e2e_steps, "steps": e2e_steps,
+                    "api": "scratchtape_b200.lm.TinyLM.train_step (pinned host bytes in, loss out)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            el = cpu_baseline_c4(cfg)
+            line["cpu_baseline"] = {"value": cfg.flops_per_step() / el / 1e12, "unit": "TFLOP/s", "cores": 1,
+                                    "kind": "port", "sample": "one step's GEMM shapes at batch 1 on the restated "
+                                    "tensor.rs matmul (1 thread), extrapolated to batch 64; LN/softmax/CE/Adam not "
+                                    "counted"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.config == "c5":
@@ -777,6 +965,11 @@ def main():
             run_reference_c5(args)
         else:
             run_ours_c5(args)
+    elif args.config == "c4":
+        if args.impl == "reference":
+            run_reference_c4(args)
+        else:
+            run_ours_c4(args)
     elif args.config == "c3":
         if args.impl == "reference":
             run_reference_c3(args)

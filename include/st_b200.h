@@ -216,7 +216,8 @@ ST_API st_status st_embed_bwd(st_handle *h, const int32_t *ids, const float *dx,
 ST_API st_status st_layernorm_fwd(st_handle *h, const float *x, const float *gamma, const float *beta, float *y,
                                   float *mean, float *rstd, int64_t rows, int64_t d, float eps);
 /* dx (+)= the input gradient; dgamma, dbeta += the parameter gradients (fixed
- * order).  Replaces rows::layer_norm_backward (src/gpu_step/rows.rs:100-293). */
+ * order).  d a multiple of 32, at most 512.  Replaces rows::layer_norm_backward
+ * (src/gpu_step/rows.rs:100-293). */
 ST_API st_status st_layernorm_bwd(st_handle *h, const float *dy, const float *x, const float *gamma,
                                   const float *mean, const float *rstd, float *dx, float *dgamma, float *dbeta,
                                   int64_t rows, int64_t d, int32_t accumulate);

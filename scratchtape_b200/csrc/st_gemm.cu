@@ -416,6 +416,37 @@ __global__ void k_col_sum(const Operand B, int K, int N, int batch, float *dst, 
     }
 }
 
+// Column sums in two fixed-order passes, for many rows: pass 1 sums rows
+// [chunk * rpc, (chunk + 1) * rpc) of each column of b[z] in k order; pass 2
+// adds the chunk sums in chunk order into col_sum.  Grid of pass 1:
+// (column blocks, chunks, batch).
+__global__ void k_col_sum_part(const Operand B, int K, int N, int64_t rpc, float *part) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    const int chunk = blockIdx.y, z = blockIdx.z;
+    if (col >= N) return;
+    const int64_t k0 = chunk * rpc, k1 = k0 + rpc < K ? k0 + rpc : static_cast<int64_t>(K);
+    float s = 0.0f;
+    for (int64_t k = k0; k < k1; k++) s = __fadd_rn(s, load_op(B, z, static_cast<int>(k), col));
+    part[(static_cast<int64_t>(z) * gridDim.y + chunk) * N + col] = s;
+}
+// one warp per (z, column): lanes take chunks lane, lane + 32, ..., then a
+// fixed butterfly
+__global__ void k_col_sum_fin(const float *part, int chunks, int N, int batch, float *dst, int64_t off,
+                              int64_t stride) {
+    const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (i >= static_cast<int64_t>(batch) * N) return;
+    const int z = static_cast<int>(i / N), col = static_cast<int>(i % N);
+    float s = 0.0f;
+    for (int c = lane; c < chunks; c += 32) s = __fadd_rn(s, part[(static_cast<int64_t>(z) * chunks + c) * N + col]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) {
+        float *d = dst + off + static_cast<int64_t>(z) * stride + col;
+        *d = __fadd_rn(*d, s);
+    }
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, dim3 grid) {
     using C = Cfg<BN, STAGES>;
@@ -521,10 +552,23 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     }
 
     if (e.col_sum) {
-        const int64_t total = batch * n;
-        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
-        k_col_sum<<<blocks, 256, 0, h->stream>>>(B, g.K, g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
-        st_status s = st_after_launch(h, "k_col_sum");
+        // chunks of >= 64 rows, so that batch * column blocks * chunks fills the GPU
+        const int64_t col_blocks = (n + 127) / 128;
+        int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((k + 63) / 64, (4LL * h->num_sms) / (col_blocks * batch) + 1));
+        chunks = std::min<int64_t>(chunks, 65535);
+        const int64_t rpc = std::max<int64_t>(1, (k + chunks - 1) / chunks);
+        chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
+        float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
+        if (!part) return ST_NO_MEMORY;
+        dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(chunks), static_cast<unsigned>(batch));
+        k_col_sum_part<<<grid, 128, 0, h->stream>>>(B, g.K, g.N, rpc, part);
+        st_status s = st_after_launch(h, "k_col_sum_part");
+        if (s != ST_OK) return s;
+        const int64_t fin_blocks = (batch * n + 7) / 8;
+        if (fin_blocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum too wide");
+        k_col_sum_fin<<<static_cast<unsigned>(fin_blocks), 256, 0, h->stream>>>(
+            part, static_cast<int>(chunks), g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
+        s = st_after_launch(h, "k_col_sum_fin");
         if (s != ST_OK) return s;
     }
 

@@ -23,6 +23,7 @@ enum StScratchSlot {
     SLOT_KNN_MISC,
     SLOT_STEP,        // LayerNorm parameter-gradient partials
     SLOT_STEP_ROWS,   // per-row cross-entropy losses
+    SLOT_COLSUM,      // column-sum partials of the GEMM epilogue
     SLOT_COUNT
 };
 

@@ -122,62 +122,84 @@ __global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, 
     }
 }
 
-// dx (+)= rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma
-__global__ void k_ln_bwd_dx(const float *dy, const float *x, const float *gamma, const float *mean, const float *rstd,
-                            float *dx, int64_t rows, int d, int accumulate) {
-    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
+// dx (+)= rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma.
+// Each block takes LN_ROWS consecutive rows (warp w: rows w, w + 8, ...) and
+// also writes its partial parameter gradients -- per column, sum over its rows
+// of dy * xhat and of dy, warps combined in warp order -- to
+// part[block][2][d]; k_ln_params_sum adds the blocks in block order.
+constexpr int LN_WARPS = 8, LN_ROWS = 32, LN_MAXD = 512;  // LN_MAXD: widest row of the backward
+__global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const float *x, const float *gamma,
+                                                          const float *mean, const float *rstd, float *dx, float *part,
+                                                          int64_t rows, int d, int accumulate) {
+    __shared__ float sh[LN_WARPS][2][LN_MAXD];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int per = d / 32;
-    const float mu = mean[r], rs = rstd[r];
-    float gv[MAXD / 32], xh[MAXD / 32];
-    float s1 = 0.0f, s2 = 0.0f;
+    float pg[LN_MAXD / 32], pb[LN_MAXD / 32];
 #pragma unroll
-    for (int j = 0; j < MAXD / 32; j++)
-        if (j < per) {
-            const int c = lane * per + j;
-            xh[j] = (x[r * d + c] - mu) * rs;
-            gv[j] = dy[r * d + c] * gamma[c];
-            s1 += gv[j];
-            s2 += gv[j] * xh[j];
-        }
-    const float m1 = warp_sum_f(s1) / static_cast<float>(d), m2 = warp_sum_f(s2) / static_cast<float>(d);
+    for (int j = 0; j < LN_MAXD / 32; j++) pg[j] = pb[j] = 0.0f;
+    for (int i = warp; i < LN_ROWS; i += LN_WARPS) {
+        const int64_t r = blockIdx.x * static_cast<int64_t>(LN_ROWS) + i;
+        if (r >= rows) break;
+        const float mu = mean[r], rs = rstd[r];
+        float gv[LN_MAXD / 32], xh[LN_MAXD / 32];
+        float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
-    for (int j = 0; j < MAXD / 32; j++)
+        for (int j = 0; j < LN_MAXD / 32; j++)
+            if (j < per) {
+                const int c = lane * per + j;
+                const float dyv = dy[r * d + c];
+                xh[j] = (x[r * d + c] - mu) * rs;
+                gv[j] = dyv * gamma[c];
+                s1 += gv[j];
+                s2 += gv[j] * xh[j];
+                pg[j] += dyv * xh[j];
+                pb[j] += dyv;
+            }
+        const float m1 = warp_sum_f(s1) / static_cast<float>(d), m2 = warp_sum_f(s2) / static_cast<float>(d);
+#pragma unroll
+        for (int j = 0; j < LN_MAXD / 32; j++)
+            if (j < per) {
+                const int64_t e = r * d + lane * per + j;
+                const float g = rs * (gv[j] - m1 - xh[j] * m2);
+                dx[e] = accumulate ? dx[e] + g : g;
+            }
+    }
+#pragma unroll
+    for (int j = 0; j < LN_MAXD / 32; j++)
         if (j < per) {
-            const int64_t e = r * d + lane * per + j;
-            const float g = rs * (gv[j] - m1 - xh[j] * m2);
-            dx[e] = accumulate ? dx[e] + g : g;
+            sh[warp][0][lane * per + j] = pg[j];
+            sh[warp][1][lane * per + j] = pb[j];
         }
+    __syncthreads();
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        float sg = 0.0f, sb = 0.0f;
+        for (int w = 0; w < LN_WARPS; w++) {
+            sg += sh[w][0][c];
+            sb += sh[w][1][c];
+        }
+        part[(static_cast<int64_t>(blockIdx.x) * 2) * d + c] = sg;
+        part[(static_cast<int64_t>(blockIdx.x) * 2 + 1) * d + c] = sb;
+    }
 }
 
-// Per column, partial sums over a chunk of rows (row order), then the
-// partials in chunk order: dgamma += sum dy * xhat, dbeta += sum dy.
-__global__ void k_ln_bwd_params_part(const float *dy, const float *x, const float *mean, const float *rstd, float *part,
-                                     int64_t rows, int d, int64_t rows_per_chunk) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    const int chunk = blockIdx.y;
-    if (c >= d) return;
-    const int64_t r0 = chunk * rows_per_chunk, r1 = min(rows, r0 + rows_per_chunk);
-    float sg = 0.0f, sb = 0.0f;
-    for (int64_t r = r0; r < r1; r++) {
-        const float g = dy[r * d + c];
-        sg += g * ((x[r * d + c] - mean[r]) * rstd[r]);
-        sb += g;
-    }
-    part[(static_cast<int64_t>(chunk) * 2) * d + c] = sg;
-    part[(static_cast<int64_t>(chunk) * 2 + 1) * d + c] = sb;
-}
-__global__ void k_ln_bwd_params_sum(const float *part, float *dgamma, float *dbeta, int d, int chunks) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// dgamma[c] += sum of part[b][0][c], dbeta[c] += sum of part[b][1][c] over
+// blocks b: one warp per column, lanes take blocks lane, lane + 32, ...,
+// then a fixed butterfly.
+__global__ void k_ln_params_sum(const float *part, float *dgamma, float *dbeta, int d, int nblocks) {
+    const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
     if (c >= d) return;
     float sg = 0.0f, sb = 0.0f;
-    for (int k = 0; k < chunks; k++) {
-        sg += part[(static_cast<int64_t>(k) * 2) * d + c];
-        sb += part[(static_cast<int64_t>(k) * 2 + 1) * d + c];
+    for (int b = lane; b < nblocks; b += 32) {
+        sg += part[(static_cast<int64_t>(b) * 2) * d + c];
+        sb += part[(static_cast<int64_t>(b) * 2 + 1) * d + c];
     }
-    dgamma[c] += sg;
-    dbeta[c] += sb;
+    sg = warp_sum_f(sg);
+    sb = warp_sum_f(sb);
+    if (lane == 0) {
+        dgamma[c] += sg;
+        dbeta[c] += sb;
+    }
 }
 
 // Per row: loss_r = log(sum exp(x - max)) + max - x[y];
@@ -311,25 +333,21 @@ extern "C" st_status st_layernorm_bwd(st_handle *h, const float *dy, const float
                                       int64_t rows, int64_t d, int32_t accumulate) {
     if (!h) return ST_INVALID_ARG;
     if (!dy || !x || !gamma || !mean || !rstd || !dx || !dgamma || !dbeta || rows < 1 || d < 32 || d % 32 != 0 ||
-        d > MAXD)
-        return h->fail(ST_INVALID_ARG, "st_layernorm_bwd: bad arguments");
+        d > LN_MAXD)
+        return h->fail(ST_INVALID_ARG, "st_layernorm_bwd: bad arguments (d a multiple of 32 up to %d)", LN_MAXD);
     cudaSetDevice(h->device);
-    const int wpb = 8;
-    k_ln_bwd_dx<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
-        dy, x, gamma, mean, rstd, dx, rows, static_cast<int>(d), accumulate);
-    st_status s = st_after_launch(h, "k_ln_bwd_dx");
-    if (s != ST_OK) return s;
-    const int chunks = static_cast<int>(std::min<int64_t>(64, rows));
-    const int64_t rpc = (rows + chunks - 1) / chunks;
-    float *part = static_cast<float *>(st_scratch(h, SLOT_STEP, sizeof(float) * 2 * chunks * d));
+    const int64_t nblocks = (rows + LN_ROWS - 1) / LN_ROWS;
+    if (nblocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_layernorm_bwd: too many rows");
+    float *part = static_cast<float *>(st_scratch(h, SLOT_STEP, sizeof(float) * 2 * nblocks * d));
     if (!part) return ST_NO_MEMORY;
-    dim3 grid(static_cast<unsigned>((d + 127) / 128), static_cast<unsigned>(chunks));
-    k_ln_bwd_params_part<<<grid, 128, 0, h->stream>>>(dy, x, mean, rstd, part, rows, static_cast<int>(d), rpc);
-    s = st_after_launch(h, "k_ln_bwd_params_part");
+    k_ln_bwd<<<static_cast<unsigned>(nblocks), LN_WARPS * 32, 0, h->stream>>>(dy, x, gamma, mean, rstd, dx, part, rows,
+                                                                            static_cast<int>(d), accumulate);
+    st_status s = st_after_launch(h, "k_ln_bwd");
     if (s != ST_OK) return s;
-    k_ln_bwd_params_sum<<<static_cast<unsigned>((d + 127) / 128), 128, 0, h->stream>>>(part, dgamma, dbeta,
-                                                                                       static_cast<int>(d), chunks);
-    return st_after_launch(h, "k_ln_bwd_params_sum");
+    k_ln_params_sum<<<static_cast<unsigned>((d + 7) / 8), 256, 0, h->stream>>>(part, dgamma, dbeta,
+                                                                              static_cast<int>(d),
+                                                                              static_cast<int>(nblocks));
+    return st_after_launch(h, "k_ln_params_sum");
 }
 
 extern "C" st_status st_cross_entropy(st_handle *h, const float *logits, const int32_t *targets, float *loss,
