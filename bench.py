@@ -868,8 +868,25 @@ def run_ours_c4(args):
     model.train_step(ids_d[0], tg_d[0], group)
     torch.cuda.synchronize()
     launches_per_step = h.launches - n0
-    for i in range(1, args.warmup):
-        model.train_step(ids_d[i], tg_d[i], group)
+    # the whole step (forward, backward, Adam) replays from one CUDA graph;
+    # the local-SGD average runs between replays every sync_every steps
+    ids_buf, tg_buf = torch.empty_like(ids_d[0]), torch.empty_like(tg_d[0])
+    ids_buf.copy_(ids_d[1])
+    tg_buf.copy_(tg_d[1])
+    graph = model.capture_step(ids_buf, tg_buf)
+
+    def one_step(i):
+        ids_buf.copy_(ids_d[i])
+        tg_buf.copy_(tg_d[i])
+        graph.replay()
+        model.step_count += 1
+        if group is not None and model.step_count % cfg.sync_every == 0:
+            from scratchtape_b200.shard import average_params
+            average_params(model.params, group)
+        return model.loss
+
+    for i in range(2, args.warmup):
+        one_step(i)
     torch.cuda.synchronize()
 
     def barrier():
@@ -884,7 +901,7 @@ def run_ours_c4(args):
     with sampler:
         for i in range(args.steps):
             ev[i][0].record()
-            loss = model.train_step(ids_d[args.warmup + i], tg_d[args.warmup + i], group)
+            loss = one_step(args.warmup + i)
             ev[i][1].record()
             losses.append(loss.clone())
         torch.cuda.synchronize()
@@ -902,7 +919,6 @@ def run_ours_c4(args):
     hids = [torch.from_numpy(a).pin_memory() for a, _ in host[:8]]
     htg = [torch.from_numpy(b).pin_memory() for _, b in host[:8]]
     hloss = torch.empty(1, dtype=torch.float32).pin_memory()
-    ids_buf, tg_buf = torch.empty_like(ids_d[0]), torch.empty_like(tg_d[0])
     e2e_steps = 8
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -910,8 +926,12 @@ def run_ours_c4(args):
     for i in range(e2e_steps):
         ids_buf.copy_(hids[i], non_blocking=True)
         tg_buf.copy_(htg[i], non_blocking=True)
-        loss = model.train_step(ids_buf, tg_buf, group)
-        hloss.copy_(loss, non_blocking=True)
+        graph.replay()
+        model.step_count += 1
+        if group is not None and model.step_count % cfg.sync_every == 0:
+            from scratchtape_b200.shard import average_params
+            average_params(model.params, group)
+        hloss.copy_(model.loss, non_blocking=True)
     e1.record()
     e1.synchronize()
     e_ms = e0.elapsed_time(e1)
@@ -942,7 +962,7 @@ def run_ours_c4(args):
                          "kernel": "whole step (TF32 GEMMs dominate)"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(2 * 4 * cfg.batch * cfg.t),
                     "d2h_bytes_per_step": 4, "ms_per_step": e_ms / e2e_steps, "steps": e2e_steps,
-                    "api": "scratchtape_b200.lm.TinyLM.train_step (pinned host bytes in, loss out)"},
+                    "api": "scratchtape_b200.lm.TinyLM.capture_step graph replay (pinned host bytes in, loss out)"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
         }

@@ -230,6 +230,10 @@ ST_API st_status st_cross_entropy(st_handle *h, const float *logits, const int32
  * f32 operation order of Adam::step (src/optim.rs:42-57). */
 ST_API st_status st_adam(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t step, float lr,
                          float beta1, float beta2, float eps);
+/* st_adam with the step count in device memory: increments *step (device
+ * int32), then updates with it -- the form a captured CUDA graph replays. */
+ST_API st_status st_adam_dev(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t *step,
+                             float lr, float beta1, float beta2, float eps);
 
 /* ---- kNN memory: 2-bit key scan fused with top-k ------------------------- */
 

@@ -271,6 +271,39 @@ __global__ void k_adam(float *p, const float *g, float *m, float *v, int64_t n, 
     }
 }
 
+// The step counter lives on the device, so a captured step replays correctly.
+__global__ void k_step_inc(int32_t *step) { step[0] += 1; }
+
+__device__ __forceinline__ float powi_dev(float a, int b) {  // the host powi_f32, op for op
+    float r = 1.0f;
+    for (;;) {
+        if (b & 1) r = __fmul_rn(r, a);
+        b /= 2;
+        if (b == 0) break;
+        a = __fmul_rn(a, a);
+    }
+    return r;
+}
+
+__global__ void k_adam_dev(float *p, const float *g, float *m, float *v, int64_t n, const int32_t *step, float lr,
+                           float b1, float b2, float eps) {
+    const int t = step[0];
+    const float i1 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b1, t)));
+    const float i2 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b2, t)));
+    const float c1 = __fsub_rn(1.0f, b1), c2 = __fsub_rn(1.0f, b2);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float gi = g[i];
+        const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, c1));
+        const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), c2));
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = __fmul_rn(mi, i1), vh = __fmul_rn(vi, i2);
+        const float u = __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), lr);
+        p[i] = __fsub_rn(p[i], u);
+    }
+}
+
 int blocks_for(int64_t n, int threads) {
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, 148 * 16)));
 }
@@ -375,4 +408,16 @@ extern "C" st_status st_adam(st_handle *h, float *p, const float *g, float *m, f
     const float bc1 = 1.0f - powi_f32(beta1, step), bc2 = 1.0f - powi_f32(beta2, step);
     k_adam<<<blocks_for(n, 256), 256, 0, h->stream>>>(p, g, m, v, n, lr, beta1, beta2, eps, 1.0f / bc1, 1.0f / bc2);
     return st_after_launch(h, "k_adam");
+}
+
+extern "C" st_status st_adam_dev(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t *step,
+                                 float lr, float beta1, float beta2, float eps) {
+    if (!h) return ST_INVALID_ARG;
+    if (!p || !g || !m || !v || !step || n < 1) return h->fail(ST_INVALID_ARG, "st_adam_dev: bad arguments");
+    cudaSetDevice(h->device);
+    k_step_inc<<<1, 1, 0, h->stream>>>(step);
+    st_status s = st_after_launch(h, "k_step_inc");
+    if (s != ST_OK) return s;
+    k_adam_dev<<<blocks_for(n, 256), 256, 0, h->stream>>>(p, g, m, v, n, step, lr, beta1, beta2, eps);
+    return st_after_launch(h, "k_adam_dev");
 }

@@ -82,6 +82,7 @@ class TinyLM:
         self.p = self._views(self.params)
         self.g = self._views(self.grads)
         self.step_count = 0
+        self.step_dev = torch.zeros(1, dtype=torch.int32, device=self.device)  # Adam's t, on the device
         self._init(seed)
         self._alloc()
 
@@ -206,8 +207,25 @@ class TinyLM:
     def adam_step(self):
         c = self.c
         self.step_count += 1
-        handle(self.device).call("st_adam", ptr(self.params), ptr(self.grads), ptr(self.m), ptr(self.v), self.n_params,
-                                 self.step_count, c.lr, c.beta1, c.beta2, c.adam_eps)
+        handle(self.device).call("st_adam_dev", ptr(self.params), ptr(self.grads), ptr(self.m), ptr(self.v),
+                                 self.n_params, ptr(self.step_dev), c.lr, c.beta1, c.beta2, c.adam_eps)
+
+    def capture_step(self, ids_buf: torch.Tensor, tg_buf: torch.Tensor):
+        """A CUDA graph of forward + backward + Adam reading the static buffers
+        ids_buf / tg_buf; each replay() is one optimiser step (the model
+        average of local SGD stays outside, between replays).  Runs one eager
+        step first, which sizes every scratch buffer."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.train_step(ids_buf, tg_buf)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            self.forward(ids_buf, tg_buf)
+            self.backward(ids_buf)
+            self.adam_step()
+        return graph
 
     def train_step(self, ids, targets, group=None):
         """forward + backward + Adam; every sync_every steps (distributed) the

@@ -105,3 +105,25 @@ def test_adam_bit_identical_to_oracle(dev):
     torch.cuda.synchronize()
     for got, want in ((tp, p), (tm, m), (tv, v)):
         assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_captured_step_replays_like_eager_steps(dev):
+    from scratchtape_b200.lm import LmConfig, TinyLM
+    c = LmConfig(d=128, heads=2, layers=2, dff=256, t=64, batch=4)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    batches = [(torch.randint(0, 256, (c.batch * c.t,), generator=g, device="cuda", dtype=torch.int32),
+                torch.randint(0, 256, (c.batch * c.t,), generator=g, device="cuda", dtype=torch.int32))
+               for _ in range(5)]
+    eager = TinyLM(c, "cuda", seed=2)
+    want = [eager.train_step(i, t).item() for i, t in batches]
+    model = TinyLM(c, "cuda", seed=2)
+    ids_buf, tg_buf = batches[0][0].clone(), batches[0][1].clone()
+    graph = model.capture_step(ids_buf, tg_buf)  # runs step 1 eagerly
+    got = [model.loss.item()]
+    for i, t in batches[1:]:
+        ids_buf.copy_(i)
+        tg_buf.copy_(t)
+        graph.replay()
+        got.append(model.loss.item())
+    assert got == want
+    assert torch.equal(model.params, eager.params)
