@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (c2: 200, c5: 5)")
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (c2: 20, c5: 3)")
-    p.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"])
+    p.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
     p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -978,6 +978,172 @@ def run_ours_c4(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C1: single f32 GEMMs of Tensor::matmul, 256 x 256 x 256, in the NN, NT and TN
+# layouts the tape's backward emits.  A step is the three
+# layouts once.
+# ---------------------------------------------------------------------------
+C1_N = 256
+
+
+def c1_host(seed=0):
+    rng = np.random.default_rng(seed + 1)
+    return [(rng.uniform(-1, 1, (C1_N, C1_N)).astype(np.float32), rng.uniform(-1, 1, (C1_N, C1_N)).astype(np.float32))
+            for _ in range(3)]
+
+
+def c1_flops():
+    return 3 * 2 * C1_N ** 3
+
+
+def cpu_c1(threads, reps=3):
+    import oracle
+    mats = c1_host()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for (a, b), (ta, tb) in zip(mats, ((False, False), (False, True), (True, False))):
+            # the tape's NT/TN go through an explicit transpose (src/tape.rs:505-510)
+            aa = oracle.transpose(a) if ta else a
+            bb = oracle.transpose(b) if tb else b
+            oracle.matmul_layout(aa, bb, threads=threads)
+        ts.append(time.perf_counter() - t0)
+    return float(np.median(ts))
+
+
+def run_reference_c1(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cpu_c1(threads, reps=max(1, args.warmup))
+    el = cpu_c1(threads, reps=max(3, min(args.steps, 21)))
+    v = c1_flops() / el / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C1 256^3 f32 GEMM x {NN, NT, TN} (tape transposes included)",
+                       "parallelism": "CPU, rank 0"},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": "the three layouts on the oracle's restated tensor.rs matmul, row-parallel over "
+                                       "%d threads, median" % threads},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours_c1(args):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+    import scratchtape_b200 as st
+    peaks, peak_src = load_peaks()
+    h = st.handle()
+    mats = c1_host(seed=rank)
+    layouts = ((False, False), (False, True), (True, False))
+    dev = [(torch.from_numpy(a).to(device), torch.from_numpy(b).to(device)) for a, b in mats]
+    outs = [torch.empty((C1_N, C1_N), dtype=torch.float32, device=device) for _ in range(3)]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step():
+        for (a, b), (ta, tb), o in zip(dev, layouts, outs):
+            st.mm(a, b, ta=ta, tb=tb, precision=st.TF32, out=o)
+
+    n0 = h.launches
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = h.launches - n0
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device)
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    for _ in range(args.warmup):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record()
+            graph.replay()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    if world > 1:
+        tt = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    ms = total_ms / args.steps
+    value = c1_flops() * world / (ms / 1e3) / 1e12
+    # e2e: the host-array drop-in (gpu_matmul -> st_matmul_host), copies in and out per GEMM
+    for _ in range(3):
+        for (a, b), (ta, tb) in zip(mats, layouts):
+            st.gpu_matmul(a, b, st.TF32, ta=ta, tb=tb)
+    e_steps = 20
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e_steps):
+        for (a, b), (ta, tb) in zip(mats, layouts):
+            st.gpu_matmul(a, b, st.TF32, ta=ta, tb=tb)
+    e_s = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([e_s], device=device, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_s = float(tt.item())
+    e2e_value = c1_flops() * world * e_steps / e_s / 1e12
+    byts = 3 * 3 * C1_N * C1_N * 4
+    achieved = byts / (ms / 1e3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "tf32", "data": "synthetic",
+            "config": {"workload": "C1 Tensor::matmul 256^3 f32 (BASELINE configs[0]) in the NN, NT and TN layouts, "
+                                   "TF32 tcgen05; NT/TN by descriptor (no transpose copy)",
+                       "parallelism": "replicas only" if world > 1 else "single GPU",
+                       "l2": "flushed (256 MiB write) before every timed step, outside its events",
+                       "graph": "the three GEMMs replayed from one CUDA graph"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                         "frac": achieved / float(peaks["hbm_gbs"]), "traffic": None, "peak_source": peak_src,
+                         "kernel": "k_gemm_tf32 (+k_splitk_reduce)", "us_per_gemm": ms * 1e3 / 3},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(3 * 2 * C1_N * C1_N * 4),
+                    "d2h_bytes_per_step": int(3 * C1_N * C1_N * 4), "ms_per_step": e_s / e_steps * 1e3,
+                    "steps": e_steps, "timing": "host wall clock (each call copies in, multiplies, copies out, syncs)",
+                    "api": "scratchtape_b200.gpu_matmul -> st_matmul_host (the NdArray::matmul drop-in)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            el = cpu_c1(1)
+            line["cpu_baseline"] = {"value": c1_flops() / el / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                    "sample": "the three layouts on the oracle's restated tensor.rs matmul (tape "
+                                              "transposes included), 1 thread as the reference runs, median of 3"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.config == "c5":
@@ -985,6 +1151,11 @@ def main():
             run_reference_c5(args)
         else:
             run_ours_c5(args)
+    elif args.config == "c1":
+        if args.impl == "reference":
+            run_reference_c1(args)
+        else:
+            run_ours_c1(args)
     elif args.config == "c4":
         if args.impl == "reference":
             run_reference_c4(args)

@@ -260,6 +260,14 @@ typedef enum { ST_KNN_EXACT = 0, ST_KNN_F16REF = 1 } st_knn_prec;
 ST_API st_status st_knn_search(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
                                const float *queries, int64_t nq, int32_t k, int32_t mode, int32_t prec,
                                int64_t index_base, float *out_scores, int64_t *out_ids);
+/* st_knn_search restricted per query: key j (global index) is visible to
+ * query q iff j < always or ranges[2q] <= j < ranges[2q+1] (ranges: device
+ * int64 [nq, 2]).  Replaces KnnStore::search_masked / search_tagged with a
+ * mask (src/gpu_step/knn.rs:280-299). */
+ST_API st_status st_knn_search_masked(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                      int32_t dim, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                                      int32_t prec, int64_t index_base, const int64_t *ranges, int64_t always,
+                                      float *out_scores, int64_t *out_ids);
 /* The same scan, stopping before decoding: out_keys, device u64 [nq, 128],
  * holds each query's best 128 as sortable 64-bit keys (score bits << 32 |
  * 0xFFFFFFFF - index), best first, 0 = empty.  Keys of different shards (each

@@ -76,6 +76,7 @@ SIGNATURES = {
     "st_adam": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i32, _f32, _f32, _f32, _f32]),
     "st_adam_dev": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _vp, _f32, _f32, _f32, _f32]),
     "st_knn_search": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp]),
+    "st_knn_search_masked": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _i64, _vp, _vp]),
     "st_knn_topk_keys": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i64, _vp]),
     "st_knn_merge_keys": (_st, [_h, _vp, _i64, _i64, _i64, _vp]),
     "st_knn_decode": (_st, [_h, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp]),

@@ -93,6 +93,8 @@ struct ScanArgs {
     uint32_t index_base;
     uint64_t *cbuf;      // [gridDim.x * NEPI][KCAP]
     uint64_t *unit_out;  // [splits * 2][nq_pad][KTOP]: one list per (split, column half)
+    const int64_t *ranges;  // masked scans: [nq][2] global key range [lo, hi) per query, or null
+    int64_t always;         // masked scans: keys below this global index are visible to every query
     int *status;
 };
 
@@ -237,7 +239,15 @@ __device__ __forceinline__ void load_key_codes(const ScanArgs &g, int64_t key, i
     sk = in ? __ldg(g.scales + key) : 0.0f;
 }
 
-template <int MODE, int PREC>
+// Bits of the 16 global key indices [i0, i0 + 16) that lie in [lo, hi).
+__device__ __forceinline__ uint32_t range_bits(int64_t i0, int64_t lo, int64_t hi) {
+    const int64_t a = lo > i0 ? lo : i0, b = hi < i0 + 16 ? hi : i0 + 16;
+    if (a >= b) return 0u;
+    const int n = static_cast<int>(b - a), s0 = static_cast<int>(a - i0);
+    return (n >= 32 ? 0xffffffffu : ((1u << n) - 1u)) << s0;
+}
+
+template <int MODE, int PREC, bool MASKED>
 __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -488,6 +498,13 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             const int qb = unit % g.nqb, split = unit / g.nqb;
             const int qi = qb * KQ + row;
             const bool qlive = qi < g.nq;
+            // search_masked (src/gpu_step/knn.rs:280-291): key j visible iff
+            // j < always or lo <= j < hi
+            int64_t mlo = 0, mhi = 0;
+            if (MASKED && qlive) {
+                mlo = g.ranges[2 * static_cast<int64_t>(qi)];
+                mhi = g.ranges[2 * static_cast<int64_t>(qi) + 1];
+            }
             float qf = 0.0f;  // 2^(e-1): L2's |k|^2 term in the query's scaled units
             if (MODE == MODE_L2 && PREC == PREC_EXACT && qlive) {
                 const float4 *src = reinterpret_cast<const float4 *>(g.q + static_cast<int64_t>(qi) * g.d);
@@ -540,6 +557,10 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                     const int lim = ncols - c0;
                     if (lim < 16) pass &= (1u << lim) - 1u;
                     if (!qlive) pass = 0;
+                    if (MASKED) {
+                        const int64_t i0 = static_cast<int64_t>(g.index_base) + tb + col;
+                        pass &= range_bits(i0, mlo, mhi) | range_bits(i0, 0, g.always);
+                    }
                     if (pass) {
                         // stage the 16 scores in this thread's slot, then visit only the hits
                         const uint32_t idx0 = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(col);
@@ -747,9 +768,9 @@ __global__ void k_knn_synth(uint8_t *codes, float *scales, int64_t n, int d, uin
     }
 }
 
-template <int MODE, int PREC>
+template <int MODE, int PREC, bool MASKED>
 st_status launch_scan(st_handle *h, const ScanArgs &g, int grid) {
-    auto kern = k_knn_scan<MODE, PREC>;
+    auto kern = k_knn_scan<MODE, PREC, MASKED>;
     static bool attr_done = false;
     if (!attr_done) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KNN_SMEM));
@@ -785,13 +806,13 @@ st_status check_common(st_handle *h, const uint8_t *codes, const float *scales, 
 
 }  // namespace
 
-extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
-                                      int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
-                                      int64_t index_base, uint64_t *out_keys) {
+static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
+                           const float *queries, int64_t nq, int32_t mode, int32_t prec, int64_t index_base,
+                           const int64_t *ranges, int64_t always, uint64_t *out_keys, const char *who) {
     if (!h) return ST_INVALID_ARG;
-    st_status s = check_common(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, "st_knn_topk_keys");
+    st_status s = check_common(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, who);
     if (s != ST_OK) return s;
-    if (!out_keys) return h->fail(ST_INVALID_ARG, "st_knn_topk_keys: null output");
+    if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
     const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
     const int64_t tiles = (n_keys + KT - 1) / KT;
@@ -822,14 +843,30 @@ extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const 
     g.index_base = static_cast<uint32_t>(index_base);
     g.cbuf = cbuf;
     g.unit_out = unit_out;
+    g.ranges = ranges;
+    g.always = always;
     g.status = h->d_status;
-    if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT>(h, g, grid);
-    else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF>(h, g, grid);
-    else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT>(h, g, grid);
-    else s = launch_scan<MODE_L2, PREC_F16REF>(h, g, grid);
+    if (ranges) {
+        if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT, true>(h, g, grid);
+        else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF, true>(h, g, grid);
+        else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT, true>(h, g, grid);
+        else s = launch_scan<MODE_L2, PREC_F16REF, true>(h, g, grid);
+    } else {
+        if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT, false>(h, g, grid);
+        else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF, false>(h, g, grid);
+        else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT, false>(h, g, grid);
+        else s = launch_scan<MODE_L2, PREC_F16REF, false>(h, g, grid);
+    }
     if (s != ST_OK) return s;
     k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, 2 * splits, nq_pad * KTOP, out_keys);
     return st_after_launch(h, "k_knn_merge");
+}
+
+extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                      int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
+                                      int64_t index_base, uint64_t *out_keys) {
+    return topk_keys(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, nullptr, 0, out_keys,
+                     "st_knn_topk_keys");
 }
 
 extern "C" st_status st_knn_merge_keys(st_handle *h, const uint64_t *lists, int64_t n_lists, int64_t list_stride,
@@ -888,4 +925,20 @@ extern "C" st_status st_knn_synth_keys(st_handle *h, uint8_t *codes, float *scal
     const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8 * 148 * 4));
     k_knn_synth<<<blocks, 256, 0, h->stream>>>(codes, scales, n, dim, seed, first_key);
     return st_after_launch(h, "k_knn_synth");
+}
+
+extern "C" st_status st_knn_search_masked(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                          int32_t dim, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                                          int32_t prec, int64_t index_base, const int64_t *ranges, int64_t always,
+                                          float *out_scores, int64_t *out_ids) {
+    if (!h) return ST_INVALID_ARG;
+    if (k < 1 || k > KTOP) return h->fail(ST_INVALID_ARG, "st_knn_search_masked: k must be 1..%d", KTOP);
+    if (!out_scores || !out_ids || !ranges || always < 0)
+        return h->fail(ST_INVALID_ARG, "st_knn_search_masked: null output or ranges, or negative always");
+    uint64_t *keys = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_MISC, sizeof(uint64_t) * std::max<int64_t>(nq, 1) * KTOP));
+    if (!keys) return ST_NO_MEMORY;
+    st_status s = topk_keys(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, ranges, always, keys,
+                            "st_knn_search_masked");
+    if (s != ST_OK) return s;
+    return st_knn_decode(h, keys, queries, nq, dim, k, mode, prec, out_scores, out_ids);
 }

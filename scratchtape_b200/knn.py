@@ -66,6 +66,20 @@ def search(codes: torch.Tensor, scales: torch.Tensor, queries: torch.Tensor, k: 
     return out
 
 
+def search_masked(codes: torch.Tensor, scales: torch.Tensor, queries: torch.Tensor, ranges: torch.Tensor,
+                  always: int = 0, k: int = KMAX, mode: str = "l2", prec: str = "exact", index_base: int = 0):
+    """search() where query q sees only keys j < always or ranges[q, 0] <= j < ranges[q, 1]
+    (KnnStore::search_masked, src/gpu_step/knn.rs:287-291)."""
+    queries = queries.contiguous().float()
+    nq, d = queries.shape
+    ranges = ranges.to(device=queries.device, dtype=torch.int64).contiguous()
+    out = (torch.empty((nq, k), dtype=torch.float32, device=queries.device),
+           torch.empty((nq, k), dtype=torch.int64, device=queries.device))
+    handle(queries.device).call("st_knn_search_masked", ptr(codes), ptr(scales), codes.shape[0], d, ptr(queries), nq, k,
+                                MODES[mode], PRECS[prec], index_base, ptr(ranges), always, ptr(out[0]), ptr(out[1]))
+    return out
+
+
 def topk_keys(codes, scales, queries, mode="l2", prec="exact", index_base=0, out=None):
     """The scan without decoding: sortable u64 keys [nq, 128] (as int64)."""
     queries = queries.contiguous().float()
@@ -166,6 +180,21 @@ class KnnStore:
         if rows is not None:
             q = q[:rows]
         return search(self.codes, self.scales, q, k=k, mode=mode, prec=prec)
+
+    def search_masked(self, queries, rows: Optional[int] = None, mask=None, mode: str = "l2", prec: str = "exact"):
+        """search() with mask = (ranges [rows, 2], always) as in knn.rs:287-291;
+        mask None searches every key."""
+        if mask is None:
+            return self.search(queries, rows, mode, prec)
+        self.finish()
+        q = torch.as_tensor(queries, dtype=torch.float32).reshape(-1, self.d).to(self.device)
+        if rows is not None:
+            q = q[:rows]
+        ranges, always = mask
+        scores, ids = search_masked(self.codes, self.scales, q, torch.as_tensor(np.asarray(ranges)), always,
+                                    mode=mode, prec=prec)
+        vals = torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
+        return scores, vals
 
     def search(self, queries, rows: Optional[int] = None, mode: str = "l2", prec: str = "exact"):
         """(distance or score, value) pairs, [rows, 128] each, best first."""

@@ -183,3 +183,31 @@ def test_bad_arguments_return_status(dev):
     with pytest.raises(N.StError) as e:
         K.search(codes, scales, torch.zeros(1, 64, device="cuda"), k=129)
     assert e.value.status == N.ST_INVALID_ARG
+
+
+@pytest.mark.parametrize("mode", ["dot", "l2"])
+def test_masked_search_matches_oracle(dev, mode):
+    """search_masked (src/gpu_step/knn.rs:280-291): query q sees keys j < always
+    or lo[q] <= j < hi[q]; ranges of every kind -- empty, inside one tile,
+    across tiles and splits, overlapping `always`, running past the end."""
+    import scratchtape_b200.knn as K
+    rng = np.random.default_rng(21)
+    n, d, nq, always = 30_000, 128, 9, 37
+    keys, codes, scales = _quantized(K, rng, n, d)
+    q = rng.standard_normal((nq, d)).astype(np.float32)
+    ranges = np.array([[0, 0], [5, 6], [100, 355], [255, 257], [1000, 29_000], [29_990, 40_000], [10, 60], [0, n],
+                       [12_345, 12_345 + 130]], np.int64)
+    s, i = K.search_masked(codes, scales, torch.from_numpy(q).cuda(), torch.from_numpy(ranges), always, k=64, mode=mode)
+    ws, wi = oracle.knn_topk(codes.cpu().numpy(), scales.cpu().numpy(), q, 64, mode=mode, ranges=ranges, always=always)
+    got = i.cpu().numpy()
+    for r in range(nq):
+        lo, hi = ranges[r]
+        ok = (got[r] < 0) | (got[r] < always) | ((got[r] >= lo) & (got[r] < hi))
+        assert ok.all(), "row %d returned a masked key" % r
+    tau = _tau(q, scales.cpu().numpy())
+    ws_g = s.cpu().numpy().astype(np.float64)
+    for r in range(nq):
+        valid = wi[r] >= 0
+        assert np.array_equal(got[r][~valid], wi[r][~valid])
+        t = tau[r] if mode == "dot" else 2 * tau[r] + 1e-3
+        assert np.all(np.abs(ws_g[r][valid] - ws[r][valid]) <= 2 * t + 1e-6 * np.abs(ws[r][valid]))
