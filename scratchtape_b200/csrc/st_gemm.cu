@@ -228,6 +228,9 @@ __global__ void __launch_bounds__(192, 2)
     __syncthreads();
     st::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // everything above overlaps the previous kernel's tail; no global memory
+    // is touched before it has completed
+    st::grid_dep_wait();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
@@ -287,6 +290,7 @@ __global__ void __launch_bounds__(192, 2)
         const int q = warp & 3;
         const bool ok = st::mbar_wait(acc_full, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
+        st::grid_dep_launch();  // the MMAs are done: let the next kernel start its prologue
         if (g.vec) {
             epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         } else {
@@ -306,6 +310,8 @@ __global__ void __launch_bounds__(192, 2)
 // eight splits at a time before any addition, so their latencies overlap;
 // the additions stay in split order.
 __global__ void k_splitk_reduce(const GemmArgs g) {
+    st::grid_dep_wait();
+    st::grid_dep_launch();
     const int groups = (g.N + 3) / 4;
     const int z = blockIdx.z;
     const int64_t mn = static_cast<int64_t>(g.M) * g.N;
@@ -447,6 +453,24 @@ __global__ void k_col_sum_fin(const float *part, int chunks, int N, int batch, f
     }
 }
 
+// Launches `kern` so that it may begin while the previous kernel on the
+// stream finishes (the kernel waits for it with grid_dep_wait).
+template <typename K, typename... Args>
+st_status launch_pdl(st_handle *h, K kern, dim3 grid, dim3 block, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = h->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, args...));
+    return ST_OK;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, dim3 grid) {
     using C = Cfg<BN, STAGES>;
@@ -456,7 +480,17 @@ st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_done = true;
     }
-    kern<<<grid, 192, C::SMEM, h->stream>>>(ma, mb, g);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = h->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // may start before the previous kernel ends
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, g));
     return st_after_launch(h, "k_gemm_tf32");
 }
 
@@ -633,7 +667,8 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             const int threads = groups >= 128 ? 128 : 32 * ((groups + 31) / 32);
             dim3 rgrid(static_cast<unsigned>((groups + threads - 1) / threads), static_cast<unsigned>(std::min<int64_t>(m, 65535)),
                        static_cast<unsigned>(batch));
-            k_splitk_reduce<<<rgrid, threads, 0, h->stream>>>(g);
+            st_status rs = launch_pdl(h, k_splitk_reduce, rgrid, dim3(threads), g);
+            if (rs != ST_OK) return rs;
             return st_after_launch(h, "k_splitk_reduce");
         }
         return ST_OK;

@@ -27,6 +27,14 @@ __device__ __forceinline__ void set_status(int *status, int code) {
     if (status) atomicCAS(status, 0, code);
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+
+// Waits until the grid this one programmatically depends on has completed and
+// its memory is visible (returns at once for an ordinary launch).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next programmatically dependent grid start launching.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- mbarrier ---------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
