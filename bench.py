@@ -127,6 +127,9 @@ class ClockSampler:
 
 
 def dist_setup():
+    # NCCL's own log lines (e.g. its version banner) go to stderr, so stdout
+    # carries only the one JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
