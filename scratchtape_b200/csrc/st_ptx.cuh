@@ -86,8 +86,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 7u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
             set_status(status, code);
             return false;
         }
