@@ -54,6 +54,21 @@ __device__ __forceinline__ int64_t out_index(const GemmArgs &g, int z, int row, 
            static_cast<int64_t>(row) * g.c_ld + col;
 }
 
+// A float4 read of the output buffer that the compiler may not hoist out of
+// its guarding branch: a plain load there is "safe" to speculate (the same
+// thread stores to the address later), and speculating it turned every
+// epilogue step into a wait on cold DRAM even when nothing accumulates.
+__device__ __forceinline__ float4 load_guarded(const float *p) {
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float load_guarded1(const float *p) {
+    float v;
+    asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 // Epilogue order of the reference: + bias, ReLU, mask, + residual, + out.
 // mask and residual share out's layout relative to their own offsets
 // (src/gpu_step/matmul.rs:925-931).
@@ -62,7 +77,7 @@ __device__ __forceinline__ float epilogue(const GemmArgs &g, int z, int64_t oi, 
     if (g.relu) v = fmaxf(v, 0.0f);
     if (g.mask && !(g.mask[g.mask_off + oi - g.c_off] > 0.0f)) v = 0.0f;
     if (g.residual) v = v + g.residual[g.residual_off + oi - g.c_off];
-    if (g.accumulate) v = v + g.c[oi];
+    if (g.accumulate) v = v + load_guarded1(g.c + oi);
     return v;
 }
 
@@ -127,12 +142,20 @@ __device__ __forceinline__ void epilogue_vec(const GemmArgs &g, uint8_t *smem, u
         float4 mk[8], rs[8], ac[8];
 #pragma unroll
         for (int it = 0; it < 8; it++) {
-            const int row = row0 + it * 4;
-            const int64_t rel = static_cast<int64_t>(row) * g.c_ld + col + (zbase - g.c_off);
-            const bool in = row < g.M;
-            mk[it] = (g.mask && in) ? __ldg(reinterpret_cast<const float4 *>(g.mask + g.mask_off + rel)) : make_float4(1.f, 1.f, 1.f, 1.f);
-            rs[it] = (g.residual && in) ? __ldg(reinterpret_cast<const float4 *>(g.residual + g.residual_off + rel)) : make_float4(0.f, 0.f, 0.f, 0.f);
-            ac[it] = (g.accumulate && in) ? *reinterpret_cast<const float4 *>(g.c + g.c_off + rel) : make_float4(0.f, 0.f, 0.f, 0.f);
+            mk[it] = make_float4(1.f, 1.f, 1.f, 1.f);
+            rs[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            ac[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (g.mask || g.residual || g.accumulate) {
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+                const int row = row0 + it * 4;
+                if (row >= g.M) break;
+                const int64_t rel = static_cast<int64_t>(row) * g.c_ld + col + (zbase - g.c_off);
+                if (g.mask) mk[it] = __ldg(reinterpret_cast<const float4 *>(g.mask + g.mask_off + rel));
+                if (g.residual) rs[it] = __ldg(reinterpret_cast<const float4 *>(g.residual + g.residual_off + rel));
+                if (g.accumulate) ac[it] = load_guarded(g.c + g.c_off + rel);
+            }
         }
         float4 bz = make_float4(0.f, 0.f, 0.f, 0.f);
         if (bias_z) bz = make_float4(bias_z[col], bias_z[col + 1], bias_z[col + 2], bias_z[col + 3]);
