@@ -14,6 +14,7 @@
 //  * k_gemm_exact: SIMT, each output a k-ascending chain of f32 multiply then
 //    add starting from 0 (no FMA) -- the same bits as NdArray::matmul.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "st_internal.h"
@@ -45,6 +46,8 @@ struct GemmArgs {
     int64_t residual_off;
     int relu, accumulate;
     int vec;  // out/mask/residual rows 16-byte aligned with N % 4 == 0: float4 epilogue
+    int tma_store;   // no split-k and a TMA-describable out: epilogue through TMA stores
+    int c_outer;     // out has a batch stride (TMA batch coordinate z / c_grp)
     float *partial;  // split-k partials, [batch*splits][M][N]
     int *status;
 };
@@ -184,6 +187,103 @@ __device__ __forceinline__ void epilogue_vec(const GemmArgs &g, uint8_t *smem, u
     }
 }
 
+// TMA-store path: thread = tile row (its TMEM lane); the epilogue runs in
+// registers on 32 columns at a time (bias broadcast, ReLU, and the thread's
+// own row of mask / residual / out), the result goes to a 128-byte-swizzled
+// 32x32 box in this warp's staging area (two boxes, alternating), and lane 0
+// hands the box to a TMA store.  The store engine clips rows and columns that
+// fall outside out.
+template <int BN>
+__device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMap *tmC, uint8_t *stage, uint32_t tmem,
+                                             int q, int lane, int m0, int n0, int z, bool have) {
+    const int row = m0 + q * 32 + lane;
+    const bool rin = row < g.M;
+    const int64_t zbase = g.c_off + static_cast<int64_t>(z / g.c_grp) * g.c_stride +
+                          static_cast<int64_t>(z % g.c_grp) * g.c_inner;
+    const float *bias_z = g.bias ? g.bias + g.bias_off + static_cast<int64_t>(z) * g.bias_stride : nullptr;
+    const int cz2 = g.c_grp > 1 ? z % g.c_grp : 0, cz3 = g.c_outer ? z / g.c_grp : 0;
+    const bool row_loads = rin && (g.mask || g.residual || g.accumulate);
+    int it = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32, ++it) {
+        if (n0 + c0 >= g.N) break;
+        uint32_t r[32];
+        st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+        st::tmem_ld_wait();
+        float x[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) x[j] = have ? __uint_as_float(r[j]) : 0.0f;
+        if (bias_z) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; j4++) {
+                const int col = n0 + c0 + 4 * j4;
+                if (col < g.N) {  // scalar loads: a batch's bias row need not be 16-byte aligned
+                    x[4 * j4] += __ldg(bias_z + col);
+                    x[4 * j4 + 1] += __ldg(bias_z + col + 1);
+                    x[4 * j4 + 2] += __ldg(bias_z + col + 2);
+                    x[4 * j4 + 3] += __ldg(bias_z + col + 3);
+                }
+            }
+        }
+        if (g.relu) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) x[j] = fmaxf(x[j], 0.0f);
+        }
+        if (row_loads) {
+            const int64_t rel0 = static_cast<int64_t>(row) * g.c_ld + (zbase - g.c_off);
+#pragma unroll
+            for (int j4 = 0; j4 < 8; j4++) {
+                const int col = n0 + c0 + 4 * j4;
+                if (col >= g.N) break;
+                const int64_t rel = rel0 + col;
+                float v[4] = {x[4 * j4], x[4 * j4 + 1], x[4 * j4 + 2], x[4 * j4 + 3]};
+                if (g.mask) {
+                    const float4 m = __ldg(reinterpret_cast<const float4 *>(g.mask + g.mask_off + rel));
+                    if (!(m.x > 0.0f)) v[0] = 0.0f;
+                    if (!(m.y > 0.0f)) v[1] = 0.0f;
+                    if (!(m.z > 0.0f)) v[2] = 0.0f;
+                    if (!(m.w > 0.0f)) v[3] = 0.0f;
+                }
+                if (g.residual) {
+                    const float4 rr = __ldg(reinterpret_cast<const float4 *>(g.residual + g.residual_off + rel));
+                    v[0] = v[0] + rr.x;
+                    v[1] = v[1] + rr.y;
+                    v[2] = v[2] + rr.z;
+                    v[3] = v[3] + rr.w;
+                }
+                if (g.accumulate) {
+                    const float4 a = load_guarded(g.c + g.c_off + rel);
+                    v[0] = v[0] + a.x;
+                    v[1] = v[1] + a.y;
+                    v[2] = v[2] + a.z;
+                    v[3] = v[3] + a.w;
+                }
+                x[4 * j4] = v[0];
+                x[4 * j4 + 1] = v[1];
+                x[4 * j4 + 2] = v[2];
+                x[4 * j4 + 3] = v[3];
+            }
+        }
+        uint8_t *buf = stage + (it & 1) * 4096;
+        if (it >= 2) {
+            if (lane == 0) st::bulk_wait_read<1>();  // the store that last used buf has read it
+            __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            *reinterpret_cast<float4 *>(buf + st::sw128_offset(lane, j)) =
+                make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+        st::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            st::tma_store_4d(tmC, buf, n0 + c0, m0 + q * 32, cz2, cz3);
+            st::bulk_commit();
+        }
+    }
+    if (lane == 0) st::bulk_wait_all();
+    __syncwarp();
+}
+
 // Scalar path for layouts that are not 16-byte aligned: lane = column.
 template <int BN>
 __device__ __forceinline__ void epilogue_scalar(const GemmArgs &g, uint8_t *smem, uint32_t tmem, int q, int lane,
@@ -219,7 +319,8 @@ __device__ __forceinline__ void epilogue_scalar(const GemmArgs &g, uint8_t *smem
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(192, 2)
-    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const GemmArgs g) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -314,7 +415,9 @@ __global__ void __launch_bounds__(192, 2)
         const bool ok = st::mbar_wait(acc_full, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
         st::grid_dep_launch();  // the MMAs are done: let the next kernel start its prologue
-        if (g.vec) {
+        if (g.tma_store) {
+            epilogue_tma<BN>(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0);
+        } else if (g.vec) {
             epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         } else {
             epilogue_scalar<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
@@ -495,7 +598,8 @@ st_status launch_pdl(st_handle *h, K kern, dim3 grid, dim3 block, Args... args) 
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, dim3 grid) {
+st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
+                      const GemmArgs &g, dim3 grid) {
     using C = Cfg<BN, STAGES>;
     auto kern = k_gemm_tf32<BN, STAGES, A_MN, B_MN>;
     static bool attr_done = false;  // per instantiation
@@ -513,17 +617,17 @@ st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, g));
+    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, g));
     return st_after_launch(h, "k_gemm_tf32");
 }
 
 template <int BN, int STAGES>
 st_status dispatch_tf32(st_handle *h, bool a_mn, bool b_mn, const CUtensorMap &ma, const CUtensorMap &mb,
-                        const GemmArgs &g, dim3 grid) {
-    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, g, grid);
-    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, g, grid);
-    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, g, grid);
-    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, g, grid);
+                        const CUtensorMap &mc, const GemmArgs &g, dim3 grid) {
+    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, mc, g, grid);
+    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, mc, g, grid);
+    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, mc, g, grid);
+    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, mc, g, grid);
 }
 
 Operand to_operand(const st_mat *m, int64_t packed_ld) {
@@ -680,10 +784,19 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             g.partial = static_cast<float *>(st_scratch(h, SLOT_SPLITK, sizeof(float) * batch * splits * m * n));
             if (!g.partial) return ST_NO_MEMORY;
         }
+        // epilogue through TMA stores when there is no split-k and out is
+        // TMA-describable (16-byte aligned start and rows)
+        CUtensorMap mc;
+        std::memset(&mc, 0, sizeof mc);
+        g.c_outer = out->stride != 0;
+        if (splits == 1 && g.vec && (batch == 1 || out->stride != 0)) {
+            const Operand Cm = to_operand(out, n);
+            g.tma_store = operand_map(&mc, Cm, batch, m, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, nullptr) ? 1 : 0;
+        }
         dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
                   static_cast<unsigned>(batch * splits));
-        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, g, grid)
-                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, g, grid);
+        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, g, grid)
+                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, g, grid);
         if (s != ST_OK) return s;
         if (splits > 1) {
             const int groups = static_cast<int>((n + 3) / 4);
@@ -867,8 +980,10 @@ extern "C" st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, c
     }
     dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
               static_cast<unsigned>(batch * splits));
-    const st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, g, grid)
-                                 : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, g, grid);
+    CUtensorMap mc;
+    std::memset(&mc, 0, sizeof mc);  // the fixed-scratch path keeps the register-staged epilogue (tma_store = 0)
+    const st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, g, grid)
+                                 : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, g, grid);
     if (s != ST_OK) return s;
     if (splits > 1) {
         const int groups = static_cast<int>((n + 3) / 4);
