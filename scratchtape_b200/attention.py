@@ -55,3 +55,36 @@ def attention_bwd_packed(qkv, o, dout, lse, batch: int, heads: int, t: int, scal
     handle(qkv.device).call("st_attn_bwd_packed", ptr(qkv), ptr(o), ptr(dout), ptr(lse), ptr(out), batch, heads, t,
                             d, float(scale), int(causal))
     return out
+
+
+class HostStream:
+    """Attention steps (forward + backward of every head) from host arrays,
+    pipelined: ``submit((q, k, v, dout), (o, dq, dk, dv))`` with pinned f16
+    host tensors [bh, t, 64]; uploads, the two kernels and downloads overlap
+    across consecutive steps (``pipeline.HostPipeline``)."""
+
+    def __init__(self, bh, t, scale, causal=True, device=None, depth=3):
+        from .pipeline import HostPipeline
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        f = lambda: torch.empty((bh, t, 64), dtype=torch.float16, device=dev)
+        self.sets = []
+        for _ in range(depth):
+            q, k, v, dout, o, dq, dk, dv = (f() for _ in range(8))
+            lse = torch.empty((bh, t), dtype=torch.float32, device=dev)
+            self.sets.append(((q, k, v, dout), (o, dq, dk, dv), lse))
+
+        def run(j):
+            (q, k, v, dout), (o, dq, dk, dv), lse = self.sets[j]
+            attention_fwd(q, k, v, scale, causal, out=(o, lse))
+            attention_bwd(q, k, v, o, dout, lse, scale, causal, out=(dq, dk, dv))
+
+        self.pipe = HostPipeline([(list(i), list(o)) for i, o, _ in self.sets], run, dev)
+
+    def submit(self, host_inputs, host_outputs):
+        return self.pipe.submit(host_inputs, host_outputs)
+
+    def wait(self, ticket):
+        self.pipe.wait(ticket)
+
+    def close(self):
+        self.pipe.close()

@@ -561,6 +561,92 @@ __global__ void k_col_sum_part(const Operand B, int K, int N, int64_t rpc, float
     for (int64_t k = k0; k < k1; k++) s = __fadd_rn(s, load_op(B, z, static_cast<int>(k), col));
     part[(static_cast<int64_t>(z) * gridDim.y + chunk) * N + col] = s;
 }
+// k_col_sum_part for a row-major B whose rows are 16-byte aligned.  Block
+// (64, COL_GROUPS): thread (q, g) sums column quad blockIdx.x * 64 + q over
+// rows k0 + g, k0 + g + COL_GROUPS, ... of the chunk (adjacent groups read
+// adjacent rows), COL_UNROLL 16-byte loads in flight, additions in row order;
+// the groups are then added in group order.
+constexpr int COL_QUADS = 64, COL_GROUPS = 4, COL_UNROLL = 8;
+__global__ void __launch_bounds__(COL_QUADS *COL_GROUPS)
+    k_col_sum_part4(const Operand B, int K, int N, int64_t rpc, float *part) {
+    __shared__ float4 red[COL_GROUPS][COL_QUADS];
+    const int q = blockIdx.x * COL_QUADS + threadIdx.x;  // column quad
+    const int g = threadIdx.y;
+    const int chunk = blockIdx.y, z = blockIdx.z;
+    const int64_t k0 = chunk * rpc, k1 = k0 + rpc < K ? k0 + rpc : static_cast<int64_t>(K);
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (4 * q < N) {
+        const int64_t base =
+            B.off + static_cast<int64_t>(z / B.grp) * B.stride + static_cast<int64_t>(z % B.grp) * B.inner;
+        const float *col = B.ptr + base + 4 * static_cast<int64_t>(q);
+        int64_t k = k0 + g;
+        for (; k + (COL_UNROLL - 1) * COL_GROUPS < k1; k += COL_UNROLL * COL_GROUPS) {
+            float4 v[COL_UNROLL];
+#pragma unroll
+            for (int u = 0; u < COL_UNROLL; u++)
+                v[u] = *reinterpret_cast<const float4 *>(col + (k + u * COL_GROUPS) * B.ld);
+#pragma unroll
+            for (int u = 0; u < COL_UNROLL; u++) {
+                s.x = __fadd_rn(s.x, v[u].x);
+                s.y = __fadd_rn(s.y, v[u].y);
+                s.z = __fadd_rn(s.z, v[u].z);
+                s.w = __fadd_rn(s.w, v[u].w);
+            }
+        }
+        for (; k < k1; k += COL_GROUPS) {
+            const float4 v = *reinterpret_cast<const float4 *>(col + k * B.ld);
+            s.x = __fadd_rn(s.x, v.x);
+            s.y = __fadd_rn(s.y, v.y);
+            s.z = __fadd_rn(s.z, v.z);
+            s.w = __fadd_rn(s.w, v.w);
+        }
+    }
+    red[g][threadIdx.x] = s;
+    __syncthreads();
+    if (g == 0 && 4 * q < N) {
+#pragma unroll
+        for (int j = 1; j < COL_GROUPS; j++) {
+            const float4 v = red[j][threadIdx.x];
+            s.x = __fadd_rn(s.x, v.x);
+            s.y = __fadd_rn(s.y, v.y);
+            s.z = __fadd_rn(s.z, v.z);
+            s.w = __fadd_rn(s.w, v.w);
+        }
+        *reinterpret_cast<float4 *>(part + (static_cast<int64_t>(z) * gridDim.y + chunk) * N + 4 * q) = s;
+    }
+}
+
+// k_col_sum_fin over many chunks: block of COLF_WARPS warps per 32 columns
+// (lane = column, coalesced), warp w adds chunks w, w + COLF_WARPS, ... in
+// order, then the warps' sums are added in warp order.
+constexpr int COLF_WARPS = 16;
+__global__ void __launch_bounds__(COLF_WARPS * 32)
+    k_col_sum_fin32(const float *part, int chunks, int N, float *dst, int64_t off, int64_t stride) {
+    __shared__ float red[COLF_WARPS][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x / 32;
+    const int col = blockIdx.x * 32 + lane, z = blockIdx.y;
+    float s = 0.0f;
+    if (col < N) {
+        const float *p = part + static_cast<int64_t>(z) * chunks * N + col;
+        int c = w;
+        for (; c + 7 * COLF_WARPS < chunks; c += 8 * COLF_WARPS) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = p[static_cast<int64_t>(c + u * COLF_WARPS) * N];
+#pragma unroll
+            for (int u = 0; u < 8; u++) s = __fadd_rn(s, v[u]);
+        }
+        for (; c < chunks; c += COLF_WARPS) s = __fadd_rn(s, p[static_cast<int64_t>(c) * N]);
+    }
+    red[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && col < N) {
+        for (int j = 1; j < COLF_WARPS; j++) s = __fadd_rn(s, red[j][lane]);
+        float *d = dst + off + static_cast<int64_t>(z) * stride + col;
+        *d = __fadd_rn(*d, s);
+    }
+}
+
 // one warp per (z, column): lanes take chunks lane, lane + 32, ..., then a
 // fixed butterfly
 __global__ void k_col_sum_fin(const float *part, int chunks, int N, int batch, float *dst, int64_t off,
@@ -713,24 +799,49 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     }
 
     if (e.col_sum) {
-        // chunks of >= 64 rows, so that batch * column blocks * chunks fills the GPU
-        const int64_t col_blocks = (n + 127) / 128;
-        int64_t chunks = std::max<int64_t>(1, std::min<int64_t>((k + 63) / 64, (4LL * h->num_sms) / (col_blocks * batch) + 1));
-        chunks = std::min<int64_t>(chunks, 65535);
-        const int64_t rpc = std::max<int64_t>(1, (k + chunks - 1) / chunks);
-        chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
-        float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
-        if (!part) return ST_NO_MEMORY;
-        dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(chunks), static_cast<unsigned>(batch));
-        k_col_sum_part<<<grid, 128, 0, h->stream>>>(B, g.K, g.N, rpc, part);
-        st_status s = st_after_launch(h, "k_col_sum_part");
-        if (s != ST_OK) return s;
-        const int64_t fin_blocks = (batch * n + 7) / 8;
-        if (fin_blocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum too wide");
-        k_col_sum_fin<<<static_cast<unsigned>(fin_blocks), 256, 0, h->stream>>>(
-            part, static_cast<int>(chunks), g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
-        s = st_after_launch(h, "k_col_sum_fin");
-        if (s != ST_OK) return s;
+        const bool quad = !B.trans && n % 4 == 0 && B.ld % 4 == 0 &&
+                          (reinterpret_cast<uintptr_t>(B.ptr + B.off) % 16) == 0 &&
+                          (batch == 1 || (B.stride % 4 == 0 && (B.grp == 1 || B.inner % 4 == 0)));
+        if (quad) {
+            // B's rows 16-byte aligned: chunks of 32 rows (one round of loads
+            // per thread), 64 column quads per block
+            int64_t rpc = 32;
+            if ((k + rpc - 1) / rpc > 65535) rpc = (k + 65534) / 65535;
+            const int64_t chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
+            float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
+            if (!part) return ST_NO_MEMORY;
+            dim3 grid(static_cast<unsigned>((n / 4 + COL_QUADS - 1) / COL_QUADS), static_cast<unsigned>(chunks),
+                      static_cast<unsigned>(batch));
+            k_col_sum_part4<<<grid, dim3(COL_QUADS, COL_GROUPS), 0, h->stream>>>(B, g.K, g.N, rpc, part);
+            st_status s = st_after_launch(h, "k_col_sum_part4");
+            if (s != ST_OK) return s;
+            k_col_sum_fin32<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(batch)),
+                              COLF_WARPS * 32, 0, h->stream>>>(part, static_cast<int>(chunks), g.N, e.col_sum,
+                                                               e.col_sum_off, e.col_sum_stride);
+            s = st_after_launch(h, "k_col_sum_fin32");
+            if (s != ST_OK) return s;
+        } else {
+            // one column per thread, chunks of >= 64 rows, so that batch * column
+            // blocks * chunks fills the GPU
+            const int64_t col_blocks = (n + 127) / 128;
+            int64_t chunks = std::max<int64_t>(
+                1, std::min<int64_t>((k + 63) / 64, (4LL * h->num_sms) / (col_blocks * batch) + 1));
+            chunks = std::min<int64_t>(chunks, 65535);
+            const int64_t rpc = std::max<int64_t>(1, (k + chunks - 1) / chunks);
+            chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
+            float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
+            if (!part) return ST_NO_MEMORY;
+            dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(chunks), static_cast<unsigned>(batch));
+            k_col_sum_part<<<grid, 128, 0, h->stream>>>(B, g.K, g.N, rpc, part);
+            st_status s = st_after_launch(h, "k_col_sum_part");
+            if (s != ST_OK) return s;
+            const int64_t fin_blocks = (batch * n + 7) / 8;
+            if (fin_blocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum too wide");
+            k_col_sum_fin<<<static_cast<unsigned>(fin_blocks), 256, 0, h->stream>>>(
+                part, static_cast<int>(chunks), g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
+            s = st_after_launch(h, "k_col_sum_fin");
+            if (s != ST_OK) return s;
+        }
     }
 
     bool use_tc = (prec == ST_PREC_TF32) && k >= 1;

@@ -9,7 +9,8 @@
 // reference, every reduction has a fixed order (no float atomics), so a step
 // is bit-reproducible.
 //
-// Layout: rows of d = 256 floats (one warp per row, 8 per lane), vocab 256.
+// Layout: rows of d = 256 floats (one warp per row, lane owning columns lane,
+// lane + 32, ... so that every load of the warp is one coalesced line), vocab 256.
 #include <algorithm>
 
 #include "st_internal.h"
@@ -45,34 +46,69 @@ __global__ void k_embed_fwd(const int32_t *ids, const float *tok, const float *p
 }
 
 // dtok[v, :] (+)= sum over rows r with ids[r] == v, in row order, of dx[r, :].
-// One warp per vocabulary row; the warp scans the ids 32 at a time and adds
-// the matching rows in order (lane = 8 of the 256 columns... d/32 columns).
-__global__ void k_embed_bwd_tok(const int32_t *ids, const float *dx, float *dtok, int64_t rows, int d, int vocab,
-                                int accumulate) {
-    const int v = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (v >= vocab) return;
-    const int per = d / 32;  // columns per lane (d % 32 == 0)
-    float acc[MAXD / 32];
+// One block per vocabulary row.  The block walks the ids in segments of
+// EMB_SEG, compacts the matching row numbers into shared memory in row order
+// (warp ballots, warp offsets from a prefix over the warps), then every
+// thread adds those rows for its columns, EMB_UNROLL loads in flight, the
+// additions still in row order.
+constexpr int EMB_THREADS = 256, EMB_SEG = 2048, EMB_UNROLL = 4;
+__global__ void __launch_bounds__(EMB_THREADS) k_embed_bwd_tok(const int32_t *ids, const float *dx, float *dtok,
+                                                               int64_t rows, int d, int vocab, int accumulate) {
+    __shared__ int64_t list[EMB_SEG];
+    __shared__ int warp_n[EMB_THREADS / 32];
+    const int v = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
+    constexpr int PER = MAXD / EMB_THREADS;
+    float acc[PER];
 #pragma unroll
-    for (int j = 0; j < MAXD / 32; j++) acc[j] = 0.0f;
-    for (int64_t r0 = 0; r0 < rows; r0 += 32) {
-        const int64_t r = r0 + lane;
-        const bool hit = r < rows && ids[r] == v;
-        unsigned m = __ballot_sync(0xffffffffu, hit);
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const float *row = dx + (r0 + src) * d + lane * per;
+    for (int j = 0; j < PER; j++) acc[j] = 0.0f;
+    for (int64_t s0 = 0; s0 < rows; s0 += EMB_SEG) {
+        int n = 0;  // rows listed so far in this segment (the same in every thread)
+        for (int i = 0; i < EMB_SEG; i += EMB_THREADS) {
+            const int64_t r = s0 + i + tid;
+            const bool hit = r < rows && ids[r] == v;
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) warp_n[warp] = __popc(m);
+            __syncthreads();
+            int off = n, tot = 0;
 #pragma unroll
-            for (int j = 0; j < MAXD / 32; j++)
-                if (j < per) acc[j] += row[j];
+            for (int w = 0; w < EMB_THREADS / 32; w++) {
+                if (w < warp) off += warp_n[w];
+                tot += warp_n[w];
+            }
+            if (hit) list[off + __popc(m & ((1u << lane) - 1u))] = r;
+            n += tot;
+            __syncthreads();
         }
-    }
-    float *out = dtok + static_cast<int64_t>(v) * d + lane * per;
+        int e = 0;
+        for (; e + EMB_UNROLL <= n; e += EMB_UNROLL) {
 #pragma unroll
-    for (int j = 0; j < MAXD / 32; j++)
-        if (j < per) out[j] = accumulate ? out[j] + acc[j] : acc[j];
+            for (int j = 0; j < PER; j++) {
+                const int c = tid + j * EMB_THREADS;
+                if (c < d) {
+                    float x[EMB_UNROLL];
+#pragma unroll
+                    for (int u = 0; u < EMB_UNROLL; u++) x[u] = dx[list[e + u] * d + c];
+#pragma unroll
+                    for (int u = 0; u < EMB_UNROLL; u++) acc[j] += x[u];
+                }
+            }
+        }
+        for (; e < n; e++) {
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const int c = tid + j * EMB_THREADS;
+                if (c < d) acc[j] += dx[list[e] * d + c];
+            }
+        }
+        __syncthreads();  // the list is rewritten by the next segment
+    }
+    float *out = dtok + static_cast<int64_t>(v) * d;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int c = tid + j * EMB_THREADS;
+        if (c < d) out[c] = accumulate ? out[c] + acc[j] : acc[j];
+    }
 }
 
 // dpos[i, c] (+)= sum over b ascending of dx[b*t + i, c]
@@ -87,19 +123,20 @@ __global__ void k_embed_bwd_pos(const float *dx, float *dpos, int batch, int t, 
 }
 
 // y = (x - mean) * rstd * gamma + beta, rstd = 1 / sqrt(var + eps), biased var.
+// One warp per row; lane owns columns lane, lane + 32, ... (coalesced).
 __global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, float *y, float *mean, float *rstd,
                          int64_t rows, int d, float eps) {
     const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
     const int per = d / 32;
-    const float *xr = x + r * d + lane * per;
+    const float *xr = x + r * d + lane;
     float v[MAXD / 32];
     float s = 0.0f;
 #pragma unroll
     for (int j = 0; j < MAXD / 32; j++)
         if (j < per) {
-            v[j] = xr[j];
+            v[j] = xr[32 * j];
             s += v[j];
         }
     const float mu = warp_sum_f(s) / static_cast<float>(d);
@@ -112,10 +149,10 @@ __global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, 
         }
     const float var = warp_sum_f(q) / static_cast<float>(d);
     const float rs = 1.0f / sqrtf(var + eps);
-    float *yr = y + r * d + lane * per;
+    float *yr = y + r * d + lane;
 #pragma unroll
     for (int j = 0; j < MAXD / 32; j++)
-        if (j < per) yr[j] = (v[j] - mu) * rs * gamma[lane * per + j] + beta[lane * per + j];
+        if (j < per) yr[32 * j] = (v[j] - mu) * rs * gamma[lane + 32 * j] + beta[lane + 32 * j];
     if (lane == 0) {
         mean[r] = mu;
         rstd[r] = rs;
@@ -146,7 +183,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const
 #pragma unroll
         for (int j = 0; j < LN_MAXD / 32; j++)
             if (j < per) {
-                const int c = lane * per + j;
+                const int c = lane + 32 * j;
                 const float dyv = dy[r * d + c];
                 xh[j] = (x[r * d + c] - mu) * rs;
                 gv[j] = dyv * gamma[c];
@@ -159,7 +196,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const
 #pragma unroll
         for (int j = 0; j < LN_MAXD / 32; j++)
             if (j < per) {
-                const int64_t e = r * d + lane * per + j;
+                const int64_t e = r * d + lane + 32 * j;
                 const float g = rs * (gv[j] - m1 - xh[j] * m2);
                 dx[e] = accumulate ? dx[e] + g : g;
             }
@@ -167,8 +204,8 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const
 #pragma unroll
     for (int j = 0; j < LN_MAXD / 32; j++)
         if (j < per) {
-            sh[warp][0][lane * per + j] = pg[j];
-            sh[warp][1][lane * per + j] = pb[j];
+            sh[warp][0][lane + 32 * j] = pg[j];
+            sh[warp][1][lane + 32 * j] = pb[j];
         }
     __syncthreads();
     for (int c = threadIdx.x; c < d; c += blockDim.x) {
@@ -210,13 +247,13 @@ __global__ void k_ce(const float *logits, const int32_t *targets, float *loss_ro
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
     const int per = vocab / 32;
-    const float *xr = logits + r * vocab + lane * per;
+    const float *xr = logits + r * vocab + lane;
     float v[MAXD / 32];
     float m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < MAXD / 32; j++)
         if (j < per) {
-            v[j] = xr[j];
+            v[j] = xr[32 * j];
             m = fmaxf(m, v[j]);
         }
     m = warp_max_f(m);
@@ -232,10 +269,10 @@ __global__ void k_ce(const float *logits, const int32_t *targets, float *loss_ro
     if (lane == 0) loss_rows[r] = logf(s) + m - logits[r * vocab + y];
     const float inv = 1.0f / s;
     if (dlogits) {
-        float *dr = dlogits + r * vocab + lane * per;
+        float *dr = dlogits + r * vocab + lane;
 #pragma unroll
         for (int j = 0; j < MAXD / 32; j++)
-            if (j < per) dr[j] = (v[j] * inv - (lane * per + j == y ? 1.0f : 0.0f)) * grad_scale;
+            if (j < per) dr[32 * j] = (v[j] * inv - (lane + 32 * j == y ? 1.0f : 0.0f)) * grad_scale;
     }
 }
 
@@ -336,11 +373,11 @@ extern "C" st_status st_embed_fwd(st_handle *h, const int32_t *ids, const float 
 extern "C" st_status st_embed_bwd(st_handle *h, const int32_t *ids, const float *dx, float *dtok, float *dpos,
                                   int64_t batch, int64_t t, int64_t d, int64_t vocab, int32_t accumulate) {
     if (!h) return ST_INVALID_ARG;
-    if (!ids || !dx || !dtok || !dpos || batch < 1 || t < 1 || d < 32 || d % 32 != 0 || d > MAXD || vocab < 1)
+    if (!ids || !dx || !dtok || !dpos || batch < 1 || t < 1 || d < 32 || d % 32 != 0 || d > MAXD || vocab < 1 ||
+        vocab > (1LL << 30))
         return h->fail(ST_INVALID_ARG, "st_embed_bwd: bad arguments");
     cudaSetDevice(h->device);
-    const int wpb = 8;
-    k_embed_bwd_tok<<<static_cast<unsigned>((vocab + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
+    k_embed_bwd_tok<<<static_cast<unsigned>(vocab), EMB_THREADS, 0, h->stream>>>(
         ids, dx, dtok, batch * t, static_cast<int>(d), static_cast<int>(vocab), accumulate);
     st_status s = st_after_launch(h, "k_embed_bwd_tok");
     if (s != ST_OK) return s;

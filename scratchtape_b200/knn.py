@@ -19,6 +19,7 @@ from . import _native as N
 from .device import handle, ptr
 
 MODES = {"dot": N.KNN_DOT, "l2": N.KNN_L2}
+DOC = 256  # value tag of keys added with add_doc (src/gpu_step/knn.rs:19)
 PRECS = {"exact": N.KNN_EXACT, "f16": N.KNN_F16REF}
 KMAX = N.KNN_KMAX
 
@@ -115,12 +116,14 @@ def decode(keys, queries, k=KMAX, mode="l2", prec="exact", out=None):
 class KnnStore:
     """KnnStore (src/gpu_step/knn.rs:114-331) for 2-bit keys.
 
-    ``add(keys, vals)`` appends keys (row-major [n, d]) and their values;
+    ``add(keys, vals)`` appends keys (row-major [n, d]) and their byte values;
+    ``add_doc`` marks them in-document (value ``DOC + byte``, knn.rs:157-160);
     ``finish()`` quantises pending keys on the device; ``search(queries, rows)``
     returns, per query, the 128 nearest keys as (distance, value) sorted
-    ascending, like the reference (L2 with |q|^2 added, clamped at 0).
-    ``search_ids`` returns key indices instead, and ``mode="dot"`` ranks by
-    the dot product.
+    ascending, like the reference (L2 with |q|^2 added, clamped at 0), the
+    value with its tag stripped; ``search_tagged`` keeps the tag;
+    ``search_tail`` scans only the keys from ``from_key`` on.  ``search_ids``
+    returns key indices instead, and ``mode="dot"`` ranks by the dot product.
     """
 
     def __init__(self, d: int, tile: int = 16384, device=None):
@@ -146,11 +149,20 @@ class KnnStore:
         return int(self.scales.shape[0]) + sum(int(p.shape[0]) for p in self._pending)
 
     def add(self, keys, vals=None):
+        self._add_tagged(keys, vals, 0)
+
+    def add_doc(self, keys, vals=None):
+        """``add``, but search_tagged returns DOC + byte for these keys (knn.rs:157-160)."""
+        self._add_tagged(keys, vals, DOC)
+
+    def _add_tagged(self, keys, vals, tag):
         keys = torch.as_tensor(keys, dtype=torch.float32).reshape(-1, self.d)
         self._pending.append(keys)
         v = torch.zeros(keys.shape[0], dtype=torch.int32) if vals is None else torch.as_tensor(
             np.asarray(vals), dtype=torch.int32).reshape(-1)
-        self._pending_vals.append(v)
+        if v.shape[0] != keys.shape[0]:
+            raise ValueError("one value per key")
+        self._pending_vals.append(v + tag)
 
     def add_codes(self, codes: torch.Tensor, scales: torch.Tensor, vals=None):
         """Appends already-quantised keys (codes [n, d/4], scales [n])."""
@@ -176,28 +188,50 @@ class KnnStore:
 
     def search_ids(self, queries, rows: Optional[int] = None, k: int = KMAX, mode: str = "l2", prec: str = "exact"):
         self.finish()
+        return search(self.codes, self.scales, self._queries(queries, rows), k=k, mode=mode, prec=prec)
+
+    def _values(self, ids):
+        """Stored values of key indices; -1 where a list ran out of keys."""
+        return torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
+
+    def _queries(self, queries, rows):
         q = torch.as_tensor(queries, dtype=torch.float32).reshape(-1, self.d).to(self.device)
-        if rows is not None:
-            q = q[:rows]
-        return search(self.codes, self.scales, q, k=k, mode=mode, prec=prec)
+        return q if rows is None else q[:rows]
+
+    def search_tagged(self, queries, rows: Optional[int] = None, mask=None, mode: str = "l2", prec: str = "exact"):
+        """(distance or score, value) with DOC + byte for add_doc keys
+        (knn.rs:291-294); mask = (ranges [rows, 2], always) or None."""
+        self.finish()
+        q = self._queries(queries, rows)
+        if mask is None:
+            scores, ids = search(self.codes, self.scales, q, k=KMAX, mode=mode, prec=prec)
+        else:
+            ranges, always = mask
+            scores, ids = search_masked(self.codes, self.scales, q, torch.as_tensor(np.asarray(ranges)), always,
+                                        mode=mode, prec=prec)
+        return scores, self._values(ids)
 
     def search_masked(self, queries, rows: Optional[int] = None, mask=None, mode: str = "l2", prec: str = "exact"):
-        """search() with mask = (ranges [rows, 2], always) as in knn.rs:287-291;
-        mask None searches every key."""
-        if mask is None:
-            return self.search(queries, rows, mode, prec)
-        self.finish()
-        q = torch.as_tensor(queries, dtype=torch.float32).reshape(-1, self.d).to(self.device)
-        if rows is not None:
-            q = q[:rows]
-        ranges, always = mask
-        scores, ids = search_masked(self.codes, self.scales, q, torch.as_tensor(np.asarray(ranges)), always,
-                                    mode=mode, prec=prec)
-        vals = torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
-        return scores, vals
+        """search() with mask = (ranges [rows, 2], always) as in knn.rs:287-289:
+        query r sees key j iff j < always or ranges[r, 0] <= j < ranges[r, 1];
+        mask None searches every key.  Values come back without their tag."""
+        scores, vals = self.search_tagged(queries, rows, mask, mode, prec)
+        return scores, torch.where(vals >= 0, vals % DOC, vals)
 
     def search(self, queries, rows: Optional[int] = None, mode: str = "l2", prec: str = "exact"):
         """(distance or score, value) pairs, [rows, 128] each, best first."""
-        scores, ids = self.search_ids(queries, rows, KMAX, mode, prec)
-        vals = torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
-        return scores, vals
+        return self.search_masked(queries, rows, None, mode, prec)
+
+    def search_tail(self, queries, rows: Optional[int], ranges, from_key: int, mode: str = "l2",
+                    prec: str = "exact"):
+        """The 128 best among keys j with ranges[r, 0] <= j < ranges[r, 1], every
+        ranges[r, 0] >= from_key (knn.rs:296-301): only keys from_key.. are
+        scanned, with their global indices.  Values keep their tag."""
+        self.finish()
+        ranges = np.asarray(ranges, dtype=np.int64).reshape(-1, 2)
+        if (ranges[:, 0] < from_key).any() or not 0 <= from_key < len(self):
+            raise ValueError("search_tail: every range must start at or after from_key")
+        q = self._queries(queries, rows)
+        scores, ids = search_masked(self.codes[from_key:], self.scales[from_key:], q, torch.from_numpy(ranges), 0,
+                                    mode=mode, prec=prec, index_base=from_key)
+        return scores, self._values(ids)

@@ -126,10 +126,31 @@ class TinyLM:
         self.loss = f(1)
         self.dx, self.dxm, self.dtmp = f(rows, c.d), f(rows, c.d), f(rows, c.d)
         self.dqkv, self.dhid = f(rows, 3 * c.d), f(rows, c.dff)
+        # the weight-gradient GEMMs (off the backward's critical path) run on a
+        # side stream with a handle (and scratch) of their own
+        from .device import handle_for_stream
+        self.side = torch.cuda.Stream(dev)
+        self.side_h = handle_for_stream(self.side)
 
     # -- pieces -------------------------------------------------------------
-    def _gemm(self, a, b, out, m, k, n, ta=False, tb=False, epi=None):
-        matmul_with(MatRef(a, trans=ta), MatRef(b, trans=tb), MatRef(out), 1, m, k, n, epi, TF32)
+    def _gemm(self, a, b, out, m, k, n, ta=False, tb=False, epi=None, h=None):
+        matmul_with(MatRef(a, trans=ta), MatRef(b, trans=tb), MatRef(out), 1, m, k, n, epi, TF32, h)
+
+    def _mark(self):
+        """An event on the current stream, now."""
+        ev = torch.cuda.Event()
+        ev.record()
+        return ev
+
+    def _side_gemm(self, after, *args, **kw):
+        """A weight-gradient GEMM on the side stream once `after` has happened;
+        returns the event of its completion."""
+        self.side.wait_event(after)
+        with torch.cuda.stream(self.side):
+            self._gemm(*args, h=self.side_h, **kw)
+        ev = torch.cuda.Event()
+        ev.record(self.side)
+        return ev
 
     def _ln(self, x, gname, bname, y, stats):
         handle(self.device).call("st_layernorm_fwd", ptr(x), ptr(self.p[gname]), ptr(self.p[bname]), ptr(y),
@@ -169,40 +190,60 @@ class TinyLM:
         return self.loss
 
     def backward(self, ids: torch.Tensor):
-        """Gradients of the last forward() into self.grads (overwritten)."""
-        c, h = self.c, handle(self.device)
+        """Gradients of the last forward() into self.grads (overwritten).
+
+        The chain dlogits -> dx -> ... -> embedding runs on the current stream;
+        each weight gradient (a TN GEMM over all rows, with its bias gradient
+        as a column-sum epilogue) runs on the side stream as soon as its
+        inputs exist.  Before the chain overwrites a buffer that a pending
+        side GEMM reads (dx, dxm, dhid, dqkv), it waits for that GEMM; at the
+        end it waits for the side stream, so Adam sees every gradient."""
+        c = self.c
         rows = c.batch * c.t
         scale = 1.0 / (c.d // c.heads) ** 0.5
+        main = torch.cuda.current_stream(self.device)
         self.grads.zero_()
-        # head: dxf = dlogits . tok ; dtok = dlogits^T . xf
+        # head: dxf = dlogits . tok (chain); dtok = dlogits^T . xf (side)
+        last = self._side_gemm(self._mark(), self.dlogits, self.xf, self.g["tok"], c.vocab, rows, c.d, ta=True)
+        tok_done = last
         self._gemm(self.dlogits, self.p["tok"], self.dtmp, rows, c.vocab, c.d)
-        self._gemm(self.dlogits, self.xf, self.g["tok"], c.vocab, rows, c.d, ta=True)
         self._ln_bwd(self.dtmp, self.x[c.layers], "lnf_g", "lnf_b", self.lnf_stats, self.dx, False)
+        reads = {}  # buffer -> completion event of the last side GEMM reading it
         for i in reversed(range(c.layers)):
             p = "l%d." % i
             # MLP: x[i+1] = xm + relu(bn W1 + b1) W2 + b2
+            w2_done = self._side_gemm(self._mark(), self.hid[i], self.dx, self.g[p + "w2"], c.dff, rows, c.d,
+                                      ta=True, epi=Epilogue(col_sum=(self.g[p + "b2"], 0, 0)))
+            if "dhid" in reads:
+                main.wait_event(reads["dhid"])
             self._gemm(self.dx, self.p[p + "w2"], self.dhid, rows, c.d, c.dff, tb=True,
                        epi=Epilogue(mask=(self.hid[i], 0)))
-            self._gemm(self.hid[i], self.dx, self.g[p + "w2"], c.dff, rows, c.d, ta=True,
-                       epi=Epilogue(col_sum=(self.g[p + "b2"], 0, 0)))
+            reads["dhid"] = self._side_gemm(self._mark(), self.bn[i], self.dhid, self.g[p + "w1"], c.d, rows, c.dff,
+                                            ta=True, epi=Epilogue(col_sum=(self.g[p + "b1"], 0, 0)))
             self._gemm(self.dhid, self.p[p + "w1"], self.dtmp, rows, c.dff, c.d, tb=True)
-            self._gemm(self.bn[i], self.dhid, self.g[p + "w1"], c.d, rows, c.dff, ta=True,
-                       epi=Epilogue(col_sum=(self.g[p + "b1"], 0, 0)))
+            if "dxm" in reads:
+                main.wait_event(reads["dxm"])
             self.dxm.copy_(self.dx)
             self._ln_bwd(self.dtmp, self.xm[i], p + "ln2_g", p + "ln2_b", self.ln_stats[i][1], self.dxm, True)
             # attention: xm = x + attn(qkv(LN1 x)) Wo + bo
+            reads["dxm"] = self._side_gemm(self._mark(), self.o[i], self.dxm, self.g[p + "wo"], c.d, rows, c.d,
+                                           ta=True, epi=Epilogue(col_sum=(self.g[p + "bo"], 0, 0)))
             self._gemm(self.dxm, self.p[p + "wo"], self.dtmp, rows, c.d, c.d, tb=True)
-            self._gemm(self.o[i], self.dxm, self.g[p + "wo"], c.d, rows, c.d, ta=True,
-                       epi=Epilogue(col_sum=(self.g[p + "bo"], 0, 0)))
+            if "dqkv" in reads:
+                main.wait_event(reads["dqkv"])
             attention_bwd_packed(self.qkv[i], self.o[i], self.dtmp, self.lse[i], c.batch, c.heads, c.t, scale, True,
                                  out=self.dqkv)
+            last = reads["dqkv"] = self._side_gemm(self._mark(), self.a[i], self.dqkv, self.g[p + "wqkv"], c.d, rows,
+                                                   3 * c.d, ta=True,
+                                                   epi=Epilogue(col_sum=(self.g[p + "bqkv"], 0, 0)))
             self._gemm(self.dqkv, self.p[p + "wqkv"], self.dtmp, rows, 3 * c.d, c.d, tb=True)
-            self._gemm(self.a[i], self.dqkv, self.g[p + "wqkv"], c.d, rows, 3 * c.d, ta=True,
-                       epi=Epilogue(col_sum=(self.g[p + "bqkv"], 0, 0)))
+            main.wait_event(w2_done)
             self.dx.copy_(self.dxm)
             self._ln_bwd(self.dtmp, self.x[i], p + "ln1_g", p + "ln1_b", self.ln_stats[i][0], self.dx, True)
-        h.call("st_embed_bwd", ptr(ids), ptr(self.dx), ptr(self.g["tok"]), ptr(self.g["pos"]), c.batch, c.t, c.d,
-               c.vocab, 1)
+        main.wait_event(tok_done)
+        handle(self.device).call("st_embed_bwd", ptr(ids), ptr(self.dx), ptr(self.g["tok"]), ptr(self.g["pos"]),
+                                 c.batch, c.t, c.d, c.vocab, 1)
+        main.wait_event(last)
 
     def adam_step(self):
         c = self.c

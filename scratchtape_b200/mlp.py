@@ -12,6 +12,7 @@ import numpy as np
 import torch
 
 from .matmul import MatRef, Epilogue, matmul_with, TF32
+from .pipeline import HostPipeline
 
 
 @dataclass
@@ -121,3 +122,15 @@ def forward_backward_host(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, dy: np.
         dst.copy_(src, non_blocking=True)
     torch.cuda.current_stream().synchronize()
     return outs
+
+
+class HostStream(HostPipeline):
+    """MLP layer steps from host arrays, pipelined (``HostPipeline``):
+    ``submit((x, w1, w2, dy), (y, dx, dw1, dw2))`` with pinned host tensors."""
+
+    def __init__(self, m, d, dff, device=None, depth=3, precision=TF32):
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.bufs = [MlpBuffers.allocate(m, d, dff, dev) for _ in range(depth)]
+        self.sides = StepStreams(dev)
+        sets = [([b.x, b.w1, b.w2, b.dy], [b.y, b.dx, b.dw1, b.dw2]) for b in self.bufs]
+        super().__init__(sets, lambda j: forward_backward(self.bufs[j], precision, self.sides), dev)

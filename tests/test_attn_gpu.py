@@ -84,3 +84,23 @@ def test_unsupported_shapes_return_status(dev):
     with pytest.raises(N.StError) as e:
         attention_fwd(q, q, q, 0.1)
     assert e.value.status == N.ST_UNSUPPORTED_SHAPE
+
+
+def test_host_stream_pipelined_steps(dev):
+    """attention.HostStream: four different steps in flight through two buffer
+    sets; each step's downloaded (o, dq, dk, dv) equal the direct calls'."""
+    from scratchtape_b200.attention import HostStream, attention_bwd, attention_fwd
+    bh, t = 8, 128
+    pipe = HostStream(bh, t, 0.125)
+    steps = [tuple(x.cpu().pin_memory() for x in _inputs(bh, t, 64, seed=40 + i)) for i in range(4)]
+    outs = [tuple(torch.empty((bh, t, 64), dtype=torch.float16).pin_memory() for _ in range(4)) for _ in steps]
+    tickets = [pipe.submit(inp, o) for inp, o in zip(steps, outs)]
+    for tk in tickets:
+        pipe.wait(tk)
+    for (q, k, v, dout), got in zip(steps, outs):
+        q, k, v, dout = (x.cuda() for x in (q, k, v, dout))
+        o, lse = attention_fwd(q, k, v, 0.125)
+        want = (o,) + attention_bwd(q, k, v, o, dout, lse, 0.125)
+        for g, w in zip(got, want):
+            assert torch.equal(g, w.cpu())
+    pipe.close()

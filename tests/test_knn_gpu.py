@@ -211,3 +211,49 @@ def test_masked_search_matches_oracle(dev, mode):
         assert np.array_equal(got[r][~valid], wi[r][~valid])
         t = tau[r] if mode == "dot" else 2 * tau[r] + 1e-3
         assert np.all(np.abs(ws_g[r][valid] - ws[r][valid]) <= 2 * t + 1e-6 * np.abs(ws[r][valid]))
+
+
+def test_tagged_keys_come_back_tagged_and_plain_search_strips_the_tag(dev):
+    """knn.rs:911-930 at a 2-bit d: keys 400.. added with add_doc come back as
+    DOC + byte from search_tagged; search returns the same list untagged."""
+    import scratchtape_b200.knn as K
+    d, n, rows = 64, 600, 8
+    rng = np.random.default_rng(5)
+    keys = _keys(rng, n, d)
+    vals = np.arange(n) % 251
+    q = rng.standard_normal((rows, d)).astype(np.float32)
+    store = K.KnnStore(d)
+    store.set_key_bits(2)
+    store.add(keys[:400], vals[:400])
+    store.add_doc(keys[400:], vals[400:])
+    store.finish()
+    ts, tv = store.search_tagged(q, rows)
+    ps, pv = store.search(q, rows)
+    assert torch.equal(ts, ps)
+    assert torch.equal(tv % K.DOC, pv)
+    doc = int((tv >= K.DOC).sum())
+    assert 0 < doc < tv.numel()
+
+
+def test_tail_search_equals_the_masked_search_over_the_same_ranges(dev):
+    """knn.rs:932-950: search_tail from key 1500 equals search_tagged with the
+    same ranges; some queries see fewer than 128 keys."""
+    import scratchtape_b200.knn as K
+    d, n, rows, start = 64, 2000, 30, 1500
+    rng = np.random.default_rng(13)
+    keys = _keys(rng, n, d)
+    q = rng.standard_normal((rows, d)).astype(np.float32)
+    store = K.KnnStore(d)
+    store.set_key_bits(2)
+    store.add(keys, np.arange(n) % 251)
+    ranges = np.array([(start + (r * 7) % 100, 1700 + (r * 31) % 300) for r in range(rows)], np.int64)
+    ts, tv = store.search_tail(q, rows, ranges, start)
+    ms, mv = store.search_tagged(q, rows, (ranges, 0))
+    assert torch.equal(ts, ms) and torch.equal(tv, mv)
+    narrow = ranges.copy()
+    narrow[:, 1] = narrow[:, 0] + 50
+    ts, tv = store.search_tail(q, rows, narrow, start)
+    assert bool((tv[:, 50:] == -1).all()) and bool((tv[:, :50] >= 0).all())
+    assert bool(torch.isinf(ts[:, 50:]).all())
+    with pytest.raises(ValueError):
+        store.search_tail(q, rows, ranges, start + 200)

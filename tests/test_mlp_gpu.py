@@ -76,3 +76,24 @@ def test_mlp_step_graph_replay(dev):
     torch.cuda.synchronize()
     want = _oracle_step(x, w1, w2, dy, b.h.cpu().numpy())
     _check((b.y, b.dx, b.dw1, b.dw2), want)
+
+
+def test_host_stream_pipelined_steps(dev):
+    """HostStream: five different steps in flight through two buffer sets; each
+    step's downloaded results equal the blocking call's on the same inputs."""
+    from scratchtape_b200 import mlp
+    dev_ = torch.device("cuda:0")
+    m = 1024
+    pipe = mlp.HostStream(m, 128, 512, dev_)
+    steps = [tuple(torch.from_numpy(a).pin_memory() for a in _inputs(m=m, seed=10 + i)) for i in range(5)]
+    outs = [tuple(torch.empty(s, dtype=torch.float32).pin_memory() for s in ((m, 128), (m, 128), (128, 512),
+                                                                              (512, 128))) for _ in steps]
+    tickets = [pipe.submit(inp, o) for inp, o in zip(steps, outs)]
+    for t in tickets:
+        pipe.wait(t)
+    bufs = mlp.MlpBuffers.allocate(m, 128, 512, dev_)
+    for inp, got in zip(steps, outs):
+        want = mlp.forward_backward_host(*inp, bufs=bufs)
+        for g, w in zip(got, want):
+            assert torch.equal(g, w)
+    pipe.close()
