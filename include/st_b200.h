@@ -125,6 +125,25 @@ ST_API int64_t st_scratch_bytes(const st_handle *h);
 ST_API st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch, int64_t m,
                   int64_t k, int64_t n, const st_epilogue *epi, st_precision prec);
 
+/* One GEMM of a group: out (+)= epilogue(a . b), batch 1, TF32.  after: bit j
+ * set when this GEMM reads the output of the group's GEMM j (j < its index). */
+typedef struct {
+    st_mat a, b, out;
+    int64_t m, k, n;
+    const st_epilogue *epi; /* NULL, or an epilogue without col_sum */
+    uint32_t after;
+    int32_t reserved;
+} st_group_gemm;
+
+/* Up to 8 dependent TF32 GEMMs in one persistent launch: the sequence of
+ * matmul calls that Tape::backward's MatMul arm and the layer forward issue
+ * one by one (src/tape.rs:505-510, src/gpu_step/matmul.rs:106-192), with the
+ * same results as calling st_gemm on each in order.  A tile of GEMM i starts
+ * as soon as every GEMM named in its `after` mask has finished.  Needs
+ * 16-byte aligned rows and n % 4 == 0 for every output; returns
+ * ST_UNSUPPORTED_SHAPE otherwise (call st_gemm per GEMM then). */
+ST_API st_status st_gemm_group(st_handle *h, const st_group_gemm *gemms, int32_t count);
+
 /* st_gemm with ST_PREC_TF32 for callers that cannot let this library call
  * cudaMalloc: a host program that has already divided the GPU's memory among
  * its own pools and lends none to plug-ins, or a latency-critical loop where

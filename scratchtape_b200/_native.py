@@ -40,6 +40,12 @@ class StEpilogue(ctypes.Structure):
                 ("col_sum_stride", ctypes.c_int64), ("relu", ctypes.c_int32), ("accumulate", ctypes.c_int32)]
 
 
+class StGroupGemm(ctypes.Structure):
+    _fields_ = [("a", StMat), ("b", StMat), ("out", StMat), ("m", ctypes.c_int64), ("k", ctypes.c_int64),
+                ("n", ctypes.c_int64), ("epi", ctypes.POINTER(StEpilogue)), ("after", ctypes.c_uint32),
+                ("reserved", ctypes.c_int32)]
+
+
 _h = ctypes.c_void_p
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -59,6 +65,7 @@ SIGNATURES = {
     "st_last_kernel": (ctypes.c_char_p, [_h]),
     "st_gemm": (_st, [_h, ctypes.POINTER(StMat), ctypes.POINTER(StMat), ctypes.POINTER(StMat), _i64, _i64, _i64, _i64,
                       ctypes.POINTER(StEpilogue), ctypes.c_int]),
+    "st_gemm_group": (_st, [_h, ctypes.POINTER(StGroupGemm), _i32]),
     "st_gemm_tf32_fixed_scratch": (_st, [_h, ctypes.POINTER(StMat), ctypes.POINTER(StMat), ctypes.POINTER(StMat), _i64,
                                          _i64, _i64, _i64, ctypes.POINTER(StEpilogue)]),
     "st_matmul_host": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_int]),

@@ -193,9 +193,9 @@ __device__ __forceinline__ void epilogue_vec(const GemmArgs &g, uint8_t *smem, u
 // 32x32 box in this warp's staging area (two boxes, alternating), and lane 0
 // hands the box to a TMA store.  The store engine clips rows and columns that
 // fall outside out.
-template <int BN>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMap *tmC, uint8_t *stage, uint32_t tmem,
-                                             int q, int lane, int m0, int n0, int z, bool have) {
+                                             int q, int lane, int m0, int n0, int z, bool have, int BN,
+                                             uint64_t *acc_release = nullptr) {
     const int row = m0 + q * 32 + lane;
     const bool rin = row < g.M;
     const int64_t zbase = g.c_off + static_cast<int64_t>(z / g.c_grp) * g.c_stride +
@@ -210,6 +210,11 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMa
         uint32_t r[32];
         st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
         st::tmem_ld_wait();
+        if (acc_release && (c0 + 32 >= BN || n0 + c0 + 32 >= g.N)) {  // last TMEM read of this warp
+            st::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) st::mbar_arrive(acc_release);
+        }
         float x[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) x[j] = have ? __uint_as_float(r[j]) : 0.0f;
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(192, 2)
         st::tc_fence_after();
         st::grid_dep_launch();  // the MMAs are done: let the next kernel start its prologue
         if (g.tma_store) {
-            epilogue_tma<BN>(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0);
+            epilogue_tma(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN);
         } else if (g.vec) {
             epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         } else {
@@ -477,6 +482,8 @@ __global__ void k_splitk_reduce(const GemmArgs g) {
         }
     }
 }
+
+#include "st_gemm_group.cuh"
 
 __device__ __forceinline__ float load_op(const Operand &o, int z, int r, int c) {
     const int64_t base = o.off + static_cast<int64_t>(z / o.grp) * o.stride + static_cast<int64_t>(z % o.grp) * o.inner;
@@ -1105,4 +1112,135 @@ extern "C" st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, c
         if (cudaGetLastError() != cudaSuccess) return ST_CUDA_ERROR;
     }
     return ST_OK;
+}
+
+// ---- grouped GEMM ----------------------------------------------------------
+
+extern "C" st_status st_gemm_group(st_handle *h, const st_group_gemm *gemms, int32_t count) {
+    if (!h) return ST_INVALID_ARG;
+    if (!gemms || count < 1 || count > GRP_MAX) return h->fail(ST_INVALID_ARG, "st_gemm_group: 1..%d GEMMs", GRP_MAX);
+    cudaSetDevice(h->device);
+    static GroupPlan plan;  // host staging of the kernel parameter (large: built in place)
+    static std::mutex plan_mu;
+    std::lock_guard<std::mutex> lock(plan_mu);
+    std::memset(&plan, 0, sizeof plan);
+    plan.count = count;
+    plan.status = h->d_status;
+    int tasks = 0, split_tiles = 0;
+    int64_t part_floats = 0;
+    for (int i = 0; i < count; i++) {
+        const st_group_gemm &q = gemms[i];
+        GroupGemm &G = plan.gemm[i];
+        GroupMaps &MP = plan.maps[i];
+        const int64_t m = q.m, k = q.k, n = q.n;
+        if (!q.a.ptr || !q.b.ptr || !q.out.ptr || m < 1 || k < 1 || n < 1 || !fits_i32(m) || !fits_i32(n) ||
+            !fits_i32(k) || q.out.trans || q.a.off < 0 || q.b.off < 0 || q.out.off < 0 || q.a.ld < 0 || q.b.ld < 0 ||
+            q.out.ld < 0 || (q.after >> i) != 0)
+            return h->fail(ST_INVALID_ARG, "st_gemm_group: bad GEMM %d", i);
+        if (q.a.dtype != ST_F32 || q.b.dtype != ST_F32 || q.out.dtype != ST_F32 || (q.epi && q.epi->col_sum))
+            return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm_group: GEMM %d: f32 operands, no col_sum", i);
+        st_epilogue e{};
+        if (q.epi) e = *q.epi;
+        GemmArgs &g = G.g;
+        g.M = static_cast<int>(m);
+        g.N = static_cast<int>(n);
+        g.K = static_cast<int>(k);
+        g.batch = 1;
+        g.splits = 1;
+        g.c = static_cast<float *>(q.out.ptr);
+        g.c_off = q.out.off;
+        g.c_ld = q.out.ld ? q.out.ld : n;
+        g.c_grp = 1;
+        g.bias = e.bias;
+        g.bias_off = e.bias_off;
+        g.mask = e.mask;
+        g.mask_off = e.mask_off;
+        g.residual = e.residual;
+        g.residual_off = e.residual_off;
+        g.relu = e.relu;
+        g.accumulate = e.accumulate;
+        g.status = h->d_status;
+        auto al16 = [](const void *p, int64_t off) {
+            return (reinterpret_cast<uintptr_t>(p) + static_cast<uintptr_t>(off) * 4) % 16 == 0;
+        };
+        g.vec = (n % 4 == 0) && (g.c_ld % 4 == 0) && al16(g.c, g.c_off) && (!g.mask || al16(g.mask, g.mask_off)) &&
+                (!g.residual || al16(g.residual, g.residual_off));
+        if (!g.vec) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm_group: GEMM %d: output rows not 16-byte aligned", i);
+        g.tma_store = 1;
+        const Operand A = to_operand(&q.a, q.a.trans ? m : k);
+        const Operand B = to_operand(&q.b, q.b.trans ? k : n);
+        G.a_mn = q.a.trans != 0;
+        G.b_mn = q.b.trans == 0;
+        const int64_t m_tiles = (m + BM - 1) / BM;
+        const int64_t tiles128 = m_tiles * ((n + 127) / 128);
+        G.bn = (n > 64 && (tiles128 >= h->num_sms || tiles128 * 8 <= h->num_sms)) ? 128 : 64;
+        const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        const bool ok = (G.a_mn ? operand_map(&MP.tmA, A, 1, k, m, 32, 32, mnmaj, nullptr)
+                                : operand_map(&MP.tmA, A, 1, m, k, 32, BM, kmaj, nullptr)) &&
+                        (G.b_mn ? operand_map(&MP.tmB, B, 1, k, n, 32, 32, mnmaj, nullptr)
+                                : operand_map(&MP.tmB, B, 1, n, k, 32, static_cast<uint32_t>(G.bn), kmaj, nullptr)) &&
+                        operand_map(&MP.tmC, to_operand(&q.out, n), 1, m, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    nullptr);
+        if (!ok) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm_group: GEMM %d is not TMA-describable", i);
+        G.m_tiles = static_cast<int>(m_tiles);
+        G.n_tiles = static_cast<int>((n + G.bn - 1) / G.bn);
+        const int tiles = G.m_tiles * G.n_tiles;
+        const int kb_total = static_cast<int>((k + BK - 1) / BK);
+        // split k while the GEMM's tiles fill less than half the GPU, >= 4 k blocks per split
+        int splits = 1;
+        if (tiles * 2 <= h->num_sms && kb_total >= 8)
+            splits = std::max(1, std::min(std::min(h->num_sms / tiles, kb_total / 4), 16));
+        G.kb_per_split = (kb_total + splits - 1) / splits;
+        G.splits = (kb_total + G.kb_per_split - 1) / G.kb_per_split;
+        // a split GEMM's tiles are summed by red_parts reduction tasks each (row bands of 16 rows)
+        G.red_parts = G.splits > 1 ? BM / 16 : 0;
+        G.need = G.splits > 1 ? tiles * G.red_parts : tiles;
+        G.task_begin = tasks;
+        tasks += tiles * G.splits + tiles * G.red_parts;
+        G.tile_begin = split_tiles;
+        if (G.splits > 1) {
+            split_tiles += tiles;
+            g.partial = reinterpret_cast<float *>(part_floats);  // offset for now; based below
+            part_floats += static_cast<int64_t>(G.splits) * m * n;
+        }
+        G.after = q.after;
+    }
+    plan.tasks = tasks;
+    float *part = nullptr;
+    if (part_floats > 0) {
+        part = static_cast<float *>(st_scratch(h, SLOT_SPLITK, sizeof(float) * part_floats));
+        if (!part) return ST_NO_MEMORY;
+    }
+    for (int i = 0; i < count; i++) {
+        GroupGemm &G = plan.gemm[i];
+        if (G.splits == 1) continue;
+        GroupMaps &MP = plan.maps[i];
+        G.g.partial = part + reinterpret_cast<intptr_t>(G.g.partial);
+        Operand P{};
+        P.ptr = G.g.partial;
+        P.ld = G.g.N;
+        P.grp = G.splits;
+        P.inner = static_cast<int64_t>(G.g.M) * G.g.N;
+        if (!operand_map(&MP.tmP, P, G.splits, G.g.M, G.g.N, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, nullptr))
+            return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm_group: partials of GEMM %d not TMA-describable", i);
+    }
+    // the counters are left at zero by every launch (the last CTA resets them);
+    // they are zeroed here only when their memory is new
+    plan.ctl_words = CTL_TILES + split_tiles;
+    const size_t ctl_bytes = sizeof(unsigned int) * plan.ctl_words;
+    plan.ctl = static_cast<unsigned int *>(st_scratch(h, SLOT_GROUP, ctl_bytes));
+    if (!plan.ctl) return ST_NO_MEMORY;
+    if (plan.ctl != h->group_ctl || ctl_bytes > h->group_ctl_bytes) {
+        ST_CHECK_CUDA(h, cudaMemsetAsync(plan.ctl, 0, ctl_bytes, h->stream));
+        h->group_ctl = plan.ctl;
+        h->group_ctl_bytes = ctl_bytes;
+    }
+    static bool attr_set[64] = {};
+    if (h->device >= 0 && h->device < 64 && !attr_set[h->device]) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_gemm_group, cudaFuncAttributeMaxDynamicSharedMemorySize, GRP_SMEM));
+        attr_set[h->device] = true;
+    }
+    const int grid = std::min(2 * h->num_sms, tasks);  // two CTAs per SM
+    k_gemm_group<<<grid, GRP_THREADS, GRP_SMEM, h->stream>>>(plan);
+    return st_after_launch(h, "k_gemm_group");
 }

@@ -24,6 +24,7 @@ enum StScratchSlot {
     SLOT_STEP,        // LayerNorm parameter-gradient partials
     SLOT_STEP_ROWS,   // per-row cross-entropy losses
     SLOT_COLSUM,      // column-sum partials of the GEMM epilogue
+    SLOT_GROUP,       // grouped GEMM: ticket / finished-tile / split counters
     SLOT_COUNT
 };
 
@@ -37,6 +38,8 @@ struct st_handle {
     int64_t launches = 0;
     const char *last_kernel = "";
     int num_sms = 148;
+    void *group_ctl = nullptr;   // grouped GEMM counters: where they were last zeroed, and how many bytes
+    size_t group_ctl_bytes = 0;
 
     st_status fail(st_status s, const char *fmt, ...) {
         char buf[512];

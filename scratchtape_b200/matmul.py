@@ -149,3 +149,35 @@ def gpu_matmul(a: np.ndarray, b: np.ndarray, precision=TF32, ta=False, tb=False,
     h.call("st_matmul_host", a.ctypes.data_as(ctypes.c_void_p), b.ctypes.data_as(ctypes.c_void_p),
            out.ctypes.data_as(ctypes.c_void_p), m, k, n, int(ta), int(tb), precision)
     return out
+
+
+def matmul_group(gemms, h=None):
+    """Several dependent TF32 GEMMs in one persistent launch (st_gemm_group).
+
+    ``gemms``: up to 8 tuples (a, b, out, m, k, n, epi, after) of MatRefs,
+    shape, Epilogue (or None, no col_sum) and the indices of earlier GEMMs
+    whose outputs this one reads.  Results equal matmul_with on each in order;
+    raises StError(ST_UNSUPPORTED_SHAPE) for layouts the grouped kernel does
+    not take (unaligned rows, n % 4 != 0)."""
+    if not gemms:
+        return
+    dev = gemms[0][2].h.device
+    if h is None:
+        h = handle(dev)
+    arr = (N.StGroupGemm * len(gemms))()
+    keep = []
+    for i, (a, b, out, m, k, n, epi, after) in enumerate(gemms):
+        g = arr[i]
+        g.a, g.b, g.out = a._c(), b._c(), out._c()
+        g.m, g.k, g.n = m, k, n
+        if epi is not None:
+            ce = epi._c(out.h)
+            keep.append(ce)
+            g.epi = ctypes.pointer(ce)
+        mask = 0
+        for j in after:
+            if not 0 <= j < i:
+                raise ValueError("GEMM %d may only follow earlier GEMMs" % i)
+            mask |= 1 << j
+        g.after = mask
+    h.call("st_gemm_group", arr, len(gemms))

@@ -11,7 +11,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .matmul import MatRef, Epilogue, matmul_with, TF32
+from .matmul import MatRef, Epilogue, matmul_group, matmul_with, TF32
 from .pipeline import HostPipeline
 
 
@@ -48,6 +48,19 @@ def gemm_list(b: MlpBuffers):
         (MatRef(b.dh), MatRef(b.w1, trans=True), MatRef(b.dx), m, dff, d, None),                 # dX = dH W1^T
         (MatRef(b.x, trans=True), MatRef(b.dh), MatRef(b.dw1), d, m, dff, None),                 # dW1 = X^T dH
     ]
+
+
+# which GEMMs of gemm_list each one reads the output of
+GEMM_AFTER = [(), (0,), (0,), (0,), (2,), (2,)]
+
+
+def forward_backward_grouped(b: MlpBuffers):
+    """The six GEMMs as one persistent grouped launch (matmul_group), on torch's
+    current stream: H first, then Y, dH and dW2 as soon as H is complete,
+    then dX and dW1 once dH is."""
+    g = gemm_list(b)
+    matmul_group([(a_, b_, o_, m, k, n, epi, after) for (a_, b_, o_, m, k, n, epi), after in zip(g, GEMM_AFTER)])
+    return b
 
 
 def gemm_bytes(m, d, dff):
