@@ -47,6 +47,7 @@ struct GemmArgs {
     int relu, accumulate;
     int vec;  // out/mask/residual rows 16-byte aligned with N % 4 == 0: float4 epilogue
     int tma_store;   // no split-k and a TMA-describable out: epilogue through TMA stores
+    int tma_aux;     // with tma_store: mask / residual tiles loaded by TMA (maps tmM / tmR)
     int c_outer;     // out has a batch stride (TMA batch coordinate z / c_grp)
     float *partial;  // split-k partials, [batch*splits][M][N]
     int *status;
@@ -193,20 +194,39 @@ __device__ __forceinline__ void epilogue_vec(const GemmArgs &g, uint8_t *smem, u
 // 32x32 box in this warp's staging area (two boxes, alternating), and lane 0
 // hands the box to a TMA store.  The store engine clips rows and columns that
 // fall outside out.
+// Mask / residual tiles by TMA: per warp two 8 KB buffers (mask box, then
+// residual box, 32 rows x 32 columns each, 128-byte swizzled) and two
+// mbarriers; the box of chunk i+1 is in flight while chunk i is processed.
+struct EpiAux {
+    const CUtensorMap *mask, *residual;  // null: that operand is not loaded by TMA
+    uint8_t *buf;                        // this warp's 16 KB
+    uint64_t *bar;                       // this warp's 2 mbarriers
+};
+
 __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMap *tmC, uint8_t *stage, uint32_t tmem,
                                              int q, int lane, int m0, int n0, int z, bool have, int BN,
-                                             uint64_t *acc_release = nullptr) {
+                                             uint64_t *acc_release = nullptr, const EpiAux *aux = nullptr) {
     const int row = m0 + q * 32 + lane;
     const bool rin = row < g.M;
     const int64_t zbase = g.c_off + static_cast<int64_t>(z / g.c_grp) * g.c_stride +
                           static_cast<int64_t>(z % g.c_grp) * g.c_inner;
     const float *bias_z = g.bias ? g.bias + g.bias_off + static_cast<int64_t>(z) * g.bias_stride : nullptr;
     const int cz2 = g.c_grp > 1 ? z % g.c_grp : 0, cz3 = g.c_outer ? z / g.c_grp : 0;
-    const bool row_loads = rin && (g.mask || g.residual || g.accumulate);
+    const bool tma_aux = aux != nullptr;
+    const bool row_loads = rin && ((!tma_aux && (g.mask || g.residual)) || g.accumulate);
+    const uint32_t aux_bytes = tma_aux ? 4096u * ((aux->mask ? 1u : 0u) + (aux->residual ? 1u : 0u)) : 0u;
+    auto aux_issue = [&](int i, int c) {  // lane 0: the boxes of chunk i (columns n0 + c ..)
+        uint8_t *b = aux->buf + (i & 1) * 8192;
+        st::mbar_arrive_expect_tx(&aux->bar[i & 1], aux_bytes);
+        if (aux->mask) st::tma_load_4d(b, aux->mask, &aux->bar[i & 1], n0 + c, m0 + q * 32, cz2, cz3);
+        if (aux->residual) st::tma_load_4d(b + 4096, aux->residual, &aux->bar[i & 1], n0 + c, m0 + q * 32, cz2, cz3);
+    };
+    if (tma_aux && lane == 0) aux_issue(0, 0);
     int it = 0;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32, ++it) {
         if (n0 + c0 >= g.N) break;
+        if (tma_aux && lane == 0 && c0 + 32 < BN && n0 + c0 + 32 < g.N) aux_issue(it + 1, c0 + 32);
         uint32_t r[32];
         st::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
         st::tmem_ld_wait();
@@ -234,6 +254,29 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMa
 #pragma unroll
             for (int j = 0; j < 32; j++) x[j] = fmaxf(x[j], 0.0f);
         }
+        if (tma_aux) {
+            const bool ok = st::mbar_wait(&aux->bar[it & 1], (it >> 1) & 1, g.status, st::DEV_TIMEOUT_FULL);
+            const uint8_t *b = aux->buf + (it & 1) * 8192;
+            if (ok) {
+#pragma unroll
+                for (int j4 = 0; j4 < 8; j4++) {
+                    if (aux->mask) {
+                        const float4 m = *reinterpret_cast<const float4 *>(b + st::sw128_offset(lane, j4));
+                        if (!(m.x > 0.0f)) x[4 * j4] = 0.0f;
+                        if (!(m.y > 0.0f)) x[4 * j4 + 1] = 0.0f;
+                        if (!(m.z > 0.0f)) x[4 * j4 + 2] = 0.0f;
+                        if (!(m.w > 0.0f)) x[4 * j4 + 3] = 0.0f;
+                    }
+                    if (aux->residual) {
+                        const float4 rr = *reinterpret_cast<const float4 *>(b + 4096 + st::sw128_offset(lane, j4));
+                        x[4 * j4] = x[4 * j4] + rr.x;
+                        x[4 * j4 + 1] = x[4 * j4 + 1] + rr.y;
+                        x[4 * j4 + 2] = x[4 * j4 + 2] + rr.z;
+                        x[4 * j4 + 3] = x[4 * j4 + 3] + rr.w;
+                    }
+                }
+            }
+        }
         if (row_loads) {
             const int64_t rel0 = static_cast<int64_t>(row) * g.c_ld + (zbase - g.c_off);
 #pragma unroll
@@ -242,14 +285,14 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMa
                 if (col >= g.N) break;
                 const int64_t rel = rel0 + col;
                 float v[4] = {x[4 * j4], x[4 * j4 + 1], x[4 * j4 + 2], x[4 * j4 + 3]};
-                if (g.mask) {
+                if (g.mask && !tma_aux) {
                     const float4 m = __ldg(reinterpret_cast<const float4 *>(g.mask + g.mask_off + rel));
                     if (!(m.x > 0.0f)) v[0] = 0.0f;
                     if (!(m.y > 0.0f)) v[1] = 0.0f;
                     if (!(m.z > 0.0f)) v[2] = 0.0f;
                     if (!(m.w > 0.0f)) v[3] = 0.0f;
                 }
-                if (g.residual) {
+                if (g.residual && !tma_aux) {
                     const float4 rr = __ldg(reinterpret_cast<const float4 *>(g.residual + g.residual_off + rel));
                     v[0] = v[0] + rr.x;
                     v[1] = v[1] + rr.y;
@@ -325,7 +368,8 @@ __device__ __forceinline__ void epilogue_scalar(const GemmArgs &g, uint8_t *smem
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(192, 2)
     k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, const GemmArgs g) {
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmM,
+                const __grid_constant__ CUtensorMap tmR, const GemmArgs g) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -333,6 +377,7 @@ __global__ void __launch_bounds__(192, 2)
     uint64_t *empty = full + STAGES;
     uint64_t *acc_full = empty + STAGES;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    uint64_t *aux_bar = acc_full + 2;  // [4 epilogue warps][2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
@@ -347,6 +392,7 @@ __global__ void __launch_bounds__(192, 2)
             st::mbar_init(&empty[s], 1);
         }
         st::mbar_init(acc_full, 1);
+        for (int b = 0; b < 8; b++) st::mbar_init(&aux_bar[b], 1);
         st::fence_mbar_init();
     }
     if (warp == 1) {
@@ -421,7 +467,11 @@ __global__ void __launch_bounds__(192, 2)
         st::tc_fence_after();
         st::grid_dep_launch();  // the MMAs are done: let the next kernel start its prologue
         if (g.tma_store) {
-            epilogue_tma(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN);
+            // the operand ring is free once acc_full has fired: store boxes in
+            // its first 32 KB, mask / residual boxes in the next 64 KB
+            EpiAux aux{g.mask ? &tmM : nullptr, g.residual ? &tmR : nullptr, smem + 32768 + q * 16384, aux_bar + 2 * q};
+            epilogue_tma(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN, nullptr,
+                         g.tma_aux ? &aux : nullptr);
         } else if (g.vec) {
             epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         } else {
@@ -692,7 +742,7 @@ st_status launch_pdl(st_handle *h, K kern, dim3 grid, dim3 block, Args... args) 
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
-                      const GemmArgs &g, dim3 grid) {
+                      const CUtensorMap &mm, const CUtensorMap &mr, const GemmArgs &g, dim3 grid) {
     using C = Cfg<BN, STAGES>;
     auto kern = k_gemm_tf32<BN, STAGES, A_MN, B_MN>;
     static bool attr_done = false;  // per instantiation
@@ -710,17 +760,18 @@ st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, g));
+    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mm, mr, g));
     return st_after_launch(h, "k_gemm_tf32");
 }
 
 template <int BN, int STAGES>
 st_status dispatch_tf32(st_handle *h, bool a_mn, bool b_mn, const CUtensorMap &ma, const CUtensorMap &mb,
-                        const CUtensorMap &mc, const GemmArgs &g, dim3 grid) {
-    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, mc, g, grid);
-    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, mc, g, grid);
-    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, mc, g, grid);
-    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, mc, g, grid);
+                        const CUtensorMap &mc, const CUtensorMap &mm, const CUtensorMap &mr, const GemmArgs &g,
+                        dim3 grid) {
+    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, mc, mm, mr, g, grid);
+    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, mc, mm, mr, g, grid);
+    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, mc, mm, mr, g, grid);
+    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, mc, mm, mr, g, grid);
 }
 
 Operand to_operand(const st_mat *m, int64_t packed_ld) {
@@ -911,10 +962,24 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             const Operand Cm = to_operand(out, n);
             g.tma_store = operand_map(&mc, Cm, batch, m, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, nullptr) ? 1 : 0;
         }
+        // mask / residual (out's layout at their own offsets) by TMA as well
+        CUtensorMap mm, mr;
+        std::memset(&mm, 0, sizeof mm);
+        std::memset(&mr, 0, sizeof mr);
+        if (g.tma_store && (g.mask || g.residual)) {
+            auto aux_map = [&](CUtensorMap *map, const float *ptr, int64_t off) {
+                Operand o = to_operand(out, n);
+                o.ptr = ptr;
+                o.off = off;
+                return operand_map(map, o, batch, m, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B, nullptr);
+            };
+            g.tma_aux = (!g.mask || aux_map(&mm, g.mask, g.mask_off)) &&
+                        (!g.residual || aux_map(&mr, g.residual, g.residual_off)) ? 1 : 0;
+        }
         dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
                   static_cast<unsigned>(batch * splits));
-        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, g, grid)
-                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, g, grid);
+        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
         if (s != ST_OK) return s;
         if (splits > 1) {
             const int groups = static_cast<int>((n + 3) / 4);
@@ -1098,10 +1163,12 @@ extern "C" st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, c
     }
     dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
               static_cast<unsigned>(batch * splits));
-    CUtensorMap mc;
-    std::memset(&mc, 0, sizeof mc);  // the fixed-scratch path keeps the register-staged epilogue (tma_store = 0)
-    const st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, g, grid)
-                                 : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, g, grid);
+    CUtensorMap mc, mm, mr;  // the fixed-scratch path keeps the register-staged epilogue (tma_store = 0)
+    std::memset(&mc, 0, sizeof mc);
+    std::memset(&mm, 0, sizeof mm);
+    std::memset(&mr, 0, sizeof mr);
+    const st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                                 : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
     if (s != ST_OK) return s;
     if (splits > 1) {
         const int groups = static_cast<int>((n + 3) / 4);
