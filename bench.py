@@ -44,7 +44,11 @@ C2 = dict(m=32 * 128, d=128, dff=512)
 C5 = dict(keys=1 << 27, d=256, nq=4096, k=128)
 # dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the C2
 # step, averaged over its launches, from profiles/gemm_tf32_c2.md (ncu, 1 pass).
-C2_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per k_gemm_tf32 launch of the C2 step from one ncu capture (profiles/
+# gemm_tf32_c2.md): H = relu(X W1) 2.43 MB, Y = H W2 8.72 MB, dW2 = H^T dY 10.56 MB (writes stay in L2); the mean
+C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
+# DRAM bytes of one k_attn_fwd + one k_attn_bwd launch at C3 from one ncu capture (profiles/attn_c3.md)
+C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
 
 
 def parse_args():
@@ -383,6 +387,9 @@ def run_ours(args):
                        "graph": "step replayed from one CUDA graph"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": C2_TRAFFIC_PER_LAUNCH, "peak_source": peak_src,
+                         "traffic_note": "mean DRAM read+write per k_gemm_tf32 launch over the three launches of "
+                                         "one ncu capture (H, Y, dW2); algorithmic bytes per launch are "
+                                         "per_gemm_bytes",
                          "kernel": "k_gemm_tf32 (+k_splitk_reduce)",
                          "per_gemm_us": [round(t * 1e3, 2) for t in gemm_ms],
                          "per_gemm_bytes": per_bytes,
@@ -808,7 +815,10 @@ def run_ours_c3(args):
                        "parallelism": "heads sharded x%d (no collective)" % world if world > 1 else "single GPU",
                        "l2": "flushed (256 MiB write) before every timed step, outside its events"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": None, "peak_source": peak_src, "kernel": "k_attn_fwd + k_attn_bwd",
+                         "traffic": C3_TRAFFIC_PER_STEP * frac_b, "peak_source": peak_src,
+                         "traffic_note": "DRAM read+write of one k_attn_fwd + one k_attn_bwd launch from one ncu "
+                                         "capture (cold caches), per step like achieved",
+                         "kernel": "k_attn_fwd + k_attn_bwd",
                          "fwd_us": fwd_ms * 1e3, "bwd_us": bwd_ms * 1e3,
                          "bytes": {k2: int(v2 * frac_b) for k2, v2 in by.items()},
                          "tensor_frac_of_bf16_peak": c3_flops() * frac_b / ((fwd_ms + bwd_ms) / 1e3) / 1e12 /
