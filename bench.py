@@ -59,6 +59,9 @@ def parse_args():
     p.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
     p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
+    p.add_argument("--key-source", default="uniform", choices=["uniform", "rotated"],
+                   help="C5 keys: uniform codes with |N(0,1)| scales (BASELINE), or Gaussian vectors rotated on the "
+                        "device and run through the 2-bit quantiser (the realistic variant)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     a = p.parse_args()
@@ -489,7 +492,10 @@ def run_ours_c5(args):
     n_total = args.keys
     first, last = shard_range(n_total, world, rank)
     n_local = last - first
-    codes, scales = K.synth_keys(n_local, d, seed=1, first_key=first, device=device)
+    if args.key_source == "uniform":
+        codes, scales = K.synth_keys(n_local, d, seed=1, first_key=first, device=device)
+    else:
+        codes, scales = c5_rotated_keys(n_local, d, first, device)
     qh = c5_queries(nq, d)
     q = torch.from_numpy(qh).to(device)
     keys_local = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
@@ -590,6 +596,8 @@ def run_ours_c5(args):
                                    "query; keys sharded evenly over GPUs, local top-128 all-gathered over NCCL and "
                                    "merged",
                        "keys": n_total, "queries": nq, "dim": d, "k": k, "prec": args.prec,
+                       "key_source": "uniform codes, |N(0,1)| scales" if args.key_source == "uniform" else
+                                     "N(0,1) vectors rotated on the device (TF32 GEMM) and 2-bit quantised",
                        "parallelism": "key-sharded x%d" % world if world > 1 else "single GPU",
                        "l2": "inputs (%.1f GB of codes + scales) far larger than L2; no flush needed"
                              % (n_total * (d / 4 + 4) / 1e9)},
@@ -641,6 +649,30 @@ def c3_bytes():
     bh, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
     tile = bh * t * d * 2
     return {"fwd": 4 * tile + bh * t * 4, "bwd": 8 * tile + bh * t * 4}
+
+
+def c5_rotated_keys(n, d, first, device, chunk=1 << 22):
+    """The realistic C5 keys: N(0,1) vectors, rotated by a random orthogonal
+    matrix (keys.random_rotation, tier_eval.rs:1282-1297) with the TF32 GEMM,
+    then the 2-bit quantiser -- chunk by chunk on the device."""
+    import torch
+    import scratchtape_b200.knn as K
+    from scratchtape_b200.keys import Whitener, build_keys, random_rotation, rotate_whitener
+    from scratchtape_b200.matmul import TF32
+    wh = Whitener(np.zeros(d, np.float32), rotate_whitener(np.eye(d, dtype=np.float32), random_rotation(d, 17)),
+                  device=device)
+    codes = torch.empty((n, d // 4), dtype=torch.uint8, device=device)
+    scales = torch.empty(n, dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    for a in range(0, n, chunk):
+        b = min(n, a + chunk)
+        g.manual_seed(1000003 + first + a)
+        x = torch.randn((b - a, d), generator=g, device=device)
+        c, s, _ = build_keys(x, wh, TF32)
+        codes[a:b].copy_(c)
+        scales[a:b].copy_(s)
+    torch.cuda.synchronize(device)
+    return codes, scales
 
 
 def c3_host_inputs(bh, seed=0):

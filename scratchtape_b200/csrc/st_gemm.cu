@@ -203,6 +203,9 @@ struct EpiAux {
     uint64_t *bar;                       // this warp's 2 mbarriers
 };
 
+// AUX: mask / residual come from `aux` (compiled out when false, so the plain
+// epilogue carries none of that code).
+template <bool AUX = false>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMap *tmC, uint8_t *stage, uint32_t tmem,
                                              int q, int lane, int m0, int n0, int z, bool have, int BN,
                                              uint64_t *acc_release = nullptr, const EpiAux *aux = nullptr) {
@@ -212,7 +215,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs &g, const CUtensorMa
                           static_cast<int64_t>(z % g.c_grp) * g.c_inner;
     const float *bias_z = g.bias ? g.bias + g.bias_off + static_cast<int64_t>(z) * g.bias_stride : nullptr;
     const int cz2 = g.c_grp > 1 ? z % g.c_grp : 0, cz3 = g.c_outer ? z / g.c_grp : 0;
-    const bool tma_aux = aux != nullptr;
+    constexpr bool tma_aux = AUX;
     const bool row_loads = rin && ((!tma_aux && (g.mask || g.residual)) || g.accumulate);
     const uint32_t aux_bytes = tma_aux ? 4096u * ((aux->mask ? 1u : 0u) + (aux->residual ? 1u : 0u)) : 0u;
     auto aux_issue = [&](int i, int c) {  // lane 0: the boxes of chunk i (columns n0 + c ..)
@@ -469,9 +472,14 @@ __global__ void __launch_bounds__(192, 2)
         if (g.tma_store) {
             // the operand ring is free once acc_full has fired: store boxes in
             // its first 32 KB, mask / residual boxes in the next 64 KB
-            EpiAux aux{g.mask ? &tmM : nullptr, g.residual ? &tmR : nullptr, smem + 32768 + q * 16384, aux_bar + 2 * q};
-            epilogue_tma(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN, nullptr,
-                         g.tma_aux ? &aux : nullptr);
+            if (g.tma_aux) {
+                const EpiAux aux{g.mask ? &tmM : nullptr, g.residual ? &tmR : nullptr, smem + 32768 + q * 16384,
+                                 aux_bar + 2 * q};
+                epilogue_tma<true>(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN, nullptr,
+                                   &aux);
+            } else {
+                epilogue_tma<false>(g, &tmC, smem + q * 8192, tmem, q, lane, m0, n0, z, ok && nkb > 0, BN);
+            }
         } else if (g.vec) {
             epilogue_vec<BN>(g, smem, tmem, q, lane, m0, n0, z, ok && nkb > 0);
         } else {

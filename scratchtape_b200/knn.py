@@ -175,6 +175,28 @@ class KnnStore:
         v = torch.zeros(n, dtype=torch.int32) if vals is None else torch.as_tensor(np.asarray(vals), dtype=torch.int32)
         self.vals = torch.cat([self.vals, v.to(self.device)])
 
+    def add_states(self, x: torch.Tensor, vals=None, whitener=None, precision=None):
+        """Appends keys built on the device from hidden states x (device f32
+        [n, d]): the whitening / rotation GEMM of ``whitener`` (a
+        keys.Whitener; None: x already is the key), then the quantiser -- the
+        reference's whiten_device + KnnStore::add (tier_eval.rs:1202-1222,
+        knn.rs:153-221) without the host round trip."""
+        from .keys import build_keys
+        from .matmul import F32_EXACT
+        self.finish()
+        if whitener is not None:
+            codes, scales, norms = build_keys(x, whitener, F32_EXACT if precision is None else precision)
+        else:
+            codes, scales, norms = quantize(x)
+        if codes.shape[1] * 4 != self.d:
+            raise ValueError("keys are %d wide, the store holds %d" % (codes.shape[1] * 4, self.d))
+        n = codes.shape[0]
+        self.codes = torch.cat([self.codes, codes])
+        self.scales = torch.cat([self.scales, scales])
+        self.norms = torch.cat([self.norms, norms])
+        v = torch.zeros(n, dtype=torch.int32) if vals is None else torch.as_tensor(np.asarray(vals), dtype=torch.int32)
+        self.vals = torch.cat([self.vals, v.to(self.device)])
+
     def finish(self):
         if not self._pending:
             return
