@@ -136,6 +136,7 @@ class KnnStore:
         self.scales = torch.empty(0, dtype=torch.float32, device=self.device)
         self.norms = torch.empty(0, dtype=torch.float32, device=self.device)
         self.vals = torch.empty(0, dtype=torch.int32, device=self.device)
+        self.first = 0  # global index of the first key (a loaded shard)
         self._pending = []
         self._pending_vals = []
 
@@ -197,6 +198,53 @@ class KnnStore:
         v = torch.zeros(n, dtype=torch.int32) if vals is None else torch.as_tensor(np.asarray(vals), dtype=torch.int32)
         self.vals = torch.cat([self.vals, v.to(self.device)])
 
+    def save(self, path, key: str, extra: int = 0):
+        """KnnStore::save (src/gpu_step/knn/cache.rs:33-79): the store's keys
+        in tiles of ``tile`` keys, tagged with ``key``; see memfile."""
+        from .memfile import write_mem
+        self.finish()
+        write_mem(path, key, extra, self.d, self.tile, self.codes.cpu().numpy(), self.scales.cpu().numpy(),
+                  self.norms.cpu().numpy(), self.vals.cpu().numpy().astype(np.float32))
+
+    @staticmethod
+    def load(path, key: str, device=None, rows=None):
+        """KnnStore::load (cache.rs:81-135): (store, extra), or None when there
+        is no file or it was saved under another key.  ``rows = (lo, hi)``
+        loads only keys lo..hi -- one rank's shard; the store then reports
+        global key indices (its scans run with index_base = lo).  Tiles stream
+        from a reader thread into pinned buffers and up on a side stream."""
+        from .memfile import read_mem
+        dev = _dev(device)
+        parts = []
+        stream = torch.cuda.Stream(dev)
+        inflight = []
+
+        def on_tile(first, codes, scales, norms, vals):
+            host = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in (codes, scales, norms, vals)]
+            with torch.cuda.stream(stream):
+                devs = [t.to(dev, non_blocking=True) for t in host]
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            inflight.append((ev, host))
+            while len(inflight) > 4:  # bound the pinned memory held by copies in flight
+                inflight.pop(0)[0].synchronize()
+            parts.append((first, devs))
+
+        meta = read_mem(path, key, rows=rows, on_tile=on_tile)
+        if meta is None:
+            return None
+        stream.synchronize()
+        store = KnnStore(meta["d"], tile=meta["tile"], device=dev)
+        store.kbits = 2
+        if parts:
+            store.codes = torch.cat([p[1][0] for p in parts])
+            store.scales = torch.cat([p[1][1] for p in parts])
+            store.norms = torch.cat([p[1][2] for p in parts])
+            store.vals = torch.cat([p[1][3] for p in parts]).to(torch.int32)
+        store.first = meta["first"]
+        store.ivf_raw = meta["ivf"]  # kept for a later IVF search; flat scans ignore it
+        return store, meta["extra"]
+
     def finish(self):
         if not self._pending:
             return
@@ -210,11 +258,13 @@ class KnnStore:
 
     def search_ids(self, queries, rows: Optional[int] = None, k: int = KMAX, mode: str = "l2", prec: str = "exact"):
         self.finish()
-        return search(self.codes, self.scales, self._queries(queries, rows), k=k, mode=mode, prec=prec)
+        return search(self.codes, self.scales, self._queries(queries, rows), k=k, mode=mode, prec=prec,
+                      index_base=self.first)
 
     def _values(self, ids):
         """Stored values of key indices; -1 where a list ran out of keys."""
-        return torch.where(ids >= 0, self.vals[ids.clamp(min=0)], torch.full_like(ids, -1, dtype=torch.int32))
+        return torch.where(ids >= 0, self.vals[(ids - self.first).clamp(min=0)],
+                           torch.full_like(ids, -1, dtype=torch.int32))
 
     def _queries(self, queries, rows):
         q = torch.as_tensor(queries, dtype=torch.float32).reshape(-1, self.d).to(self.device)
@@ -226,11 +276,11 @@ class KnnStore:
         self.finish()
         q = self._queries(queries, rows)
         if mask is None:
-            scores, ids = search(self.codes, self.scales, q, k=KMAX, mode=mode, prec=prec)
+            scores, ids = search(self.codes, self.scales, q, k=KMAX, mode=mode, prec=prec, index_base=self.first)
         else:
             ranges, always = mask
             scores, ids = search_masked(self.codes, self.scales, q, torch.as_tensor(np.asarray(ranges)), always,
-                                        mode=mode, prec=prec)
+                                        mode=mode, prec=prec, index_base=self.first)
         return scores, self._values(ids)
 
     def search_masked(self, queries, rows: Optional[int] = None, mask=None, mode: str = "l2", prec: str = "exact"):
@@ -251,9 +301,10 @@ class KnnStore:
         scanned, with their global indices.  Values keep their tag."""
         self.finish()
         ranges = np.asarray(ranges, dtype=np.int64).reshape(-1, 2)
-        if (ranges[:, 0] < from_key).any() or not 0 <= from_key < len(self):
+        loc = from_key - self.first  # row of key from_key in this store
+        if (ranges[:, 0] < from_key).any() or not 0 <= loc < len(self):
             raise ValueError("search_tail: every range must start at or after from_key")
         q = self._queries(queries, rows)
-        scores, ids = search_masked(self.codes[from_key:], self.scales[from_key:], q, torch.from_numpy(ranges), 0,
+        scores, ids = search_masked(self.codes[loc:], self.scales[loc:], q, torch.from_numpy(ranges), 0,
                                     mode=mode, prec=prec, index_base=from_key)
         return scores, self._values(ids)

@@ -257,3 +257,31 @@ def test_tail_search_equals_the_masked_search_over_the_same_ranges(dev):
     assert bool(torch.isinf(ts[:, 50:]).all())
     with pytest.raises(ValueError):
         store.search_tail(q, rows, ranges, start + 200)
+
+
+def test_mem_file_round_trip_and_sharded_load(dev, tmp_path):
+    """KnnStore.save / load (src/gpu_step/knn/cache.rs): a reloaded store answers
+    exactly like the saved one; two half shards, each searched with its global
+    index base and merged, answer like the whole store."""
+    import scratchtape_b200.knn as K
+    rng = np.random.default_rng(31)
+    d, n = 128, 3000
+    store = K.KnnStore(d, tile=700)
+    store.set_key_bits(2)
+    store.add(_keys(rng, n, d), np.arange(n) % 251)
+    path = tmp_path / "store.mem"
+    store.save(path, "model-x", extra=42)
+    assert K.KnnStore.load(path, "model-y") is None
+    back, extra = K.KnnStore.load(path, "model-x")
+    assert extra == 42 and len(back) == n
+    q = rng.standard_normal((5, d)).astype(np.float32)
+    a, b = store.search(q), back.search(q)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    halves = [K.KnnStore.load(path, "model-x", rows=r)[0] for r in ((0, 1400), (1400, n))]
+    qd = torch.from_numpy(q).cuda()
+    lists = torch.stack([K.topk_keys(h.codes, h.scales, qd, mode="l2", index_base=h.first) for h in halves])
+    merged = K.merge_keys(lists, 5)
+    whole = K.topk_keys(store.codes, store.scales, qd, mode="l2")
+    assert torch.equal(merged, whole)
+    _, ids = halves[1].search_ids(q)
+    assert int(ids[ids >= 0].min()) >= 1400
