@@ -581,6 +581,32 @@ def run_ours_c5(args):
         e_total = float(t.item())
     e2e_value = n_total / (e_total / e2e_steps / 1e3)
 
+    # the small pass: 32 queries over the same keys, where the scan would be
+    # HBM-bound if it ran at the tensor pipe's full rate (the ridge is ~33
+    # queries per pass at 68 B/key); reported against the HBM roofline
+    q32 = q[:32].contiguous()
+    keys32 = torch.empty((32, K.KMAX), dtype=torch.int64, device=device)
+    K.topk_keys(codes, scales, q32, mode="dot", prec=args.prec, index_base=first, out=keys32)
+    ev32 = []
+    for _ in range(3):
+        a32, b32 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a32.record()
+        K.topk_keys(codes, scales, q32, mode="dot", prec=args.prec, index_base=first, out=keys32)
+        b32.record()
+        ev32.append((a32, b32))
+    torch.cuda.synchronize()
+    ms32 = float(np.median([a.elapsed_time(b) for a, b in ev32]))
+    if world > 1:
+        t = torch.tensor([ms32], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms32 = float(t.item())
+    bytes32 = n_local * (d / 4 + 4) + 32 * d * 4
+    small_pass = {"queries": 32, "scan_ms": ms32, "keys_per_s": n_total / (ms32 / 1e3),
+                  "hbm_gbs": bytes32 / (ms32 / 1e3) / 1e9, "hbm_frac": bytes32 / (ms32 / 1e3) / 1e9 /
+                  float(peaks["hbm_gbs"]),
+                  "note": "one k_knn_scan launch; the MMA tile is 128 queries, so 32 queries run at the 128-query "
+                          "cost: tensor-bound, not HBM-bound"}
+
     flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
     achieved = flops_alg / (scan_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
@@ -606,6 +632,7 @@ def run_ours_c5(args):
                          "traffic_note": "algorithmic bytes per scan launch (codes + scales + queries); ncu DRAM "
                                          "figures in profiles/knn_scan_c5.md",
                          "peak_source": peak_src + " (bf16 dense, sustained)", "kernel": "k_knn_scan (+k_knn_merge)",
+                         "small_pass": small_pass,
                          "scan_ms": scan_ms, "tensor_passes": passes,
                          "executed_tflops": achieved * passes,
                          "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9},

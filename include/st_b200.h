@@ -314,6 +314,37 @@ ST_API st_status st_knn_quantize(st_handle *h, const float *keys, int64_t n, int
  * |N(0,1)|, from a counter-based hash of (seed, first_key + row), so each
  * shard makes its own rows independently.  No reference counterpart (the
  * reference builds keys from trained hidden states). */
+/* The fused scan over a table of work units -- the IVF search of
+ * src/gpu_step/knn/ivf.rs:466-690 (search_ivf / scan_group): unit u scans
+ * store rows unit_keys[2u] .. unit_keys[2u + 1] (a cell) for the queries
+ * unit_q[u * 128 + r] (-1: an empty row), and row r's best 128 become list
+ * unit_list[u * 128 + r] (< n_lists) of that query; out_keys [nq, 128]
+ * (device u64, as st_knn_topk_keys) is each query's best 128 over its lists.
+ * The three tables are HOST arrays, checked before anything is launched. */
+ST_API st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                   int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
+                                   int64_t index_base, int64_t n_units, const int32_t *unit_q,
+                                   const int32_t *unit_list, const int64_t *unit_keys, int32_t n_lists,
+                                   uint64_t *out_keys);
+/* out [n, dim] f32 = (u - 1.5) * scale of 2-bit rows (k_dequant, knn.rs:630-643, kept in f32). */
+ST_API st_status st_knn_dequant(st_handle *h, const uint8_t *codes, const float *scales, int64_t n, int32_t dim,
+                                float *out);
+/* out[r] = the nearest centroid of row r from dots = rows . centroids^T [n, nlist]
+ * and cnorm = |centroid|^2 (argmin of cnorm - 2 dot, lowest index on ties;
+ * k_argmin, ivf.rs:75-113). */
+ST_API st_status st_knn_nearest(st_handle *h, const float *dots, const float *cnorm, int64_t n, int32_t nlist,
+                                int32_t *out);
+/* out [nq, nprobe] = each query's nprobe nearest centroids, nearest first
+ * (k_probe, ivf.rs:126-165); nprobe <= min(nlist, 64). */
+ST_API st_status st_knn_probe(st_handle *h, const float *dots, const float *cnorm, int64_t nq, int32_t nlist,
+                              int32_t nprobe, int32_t *out);
+/* dst row i = src row perm[i] (device i64) for i < n, rows of row_bytes (a
+ * multiple of 4): the cell-order reordering of build_ivf (ivf.rs:395-425) on
+ * the device.  An entry outside [0, n_src) gives a zero row and ST_INVALID_ARG
+ * at the next st_sync. */
+ST_API st_status st_gather_rows(st_handle *h, const void *src, int64_t n_src, void *dst, const int64_t *perm,
+                                int64_t n, int64_t row_bytes);
+
 ST_API st_status st_knn_synth_keys(st_handle *h, uint8_t *codes, float *scales, int64_t n, int32_t dim, uint64_t seed,
                                    int64_t first_key);
 

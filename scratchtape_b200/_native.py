@@ -88,6 +88,12 @@ SIGNATURES = {
     "st_knn_merge_keys": (_st, [_h, _vp, _i64, _i64, _i64, _vp]),
     "st_knn_decode": (_st, [_h, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp]),
     "st_knn_quantize": (_st, [_h, _vp, _i64, _i32, _vp, _vp, _vp]),
+    "st_knn_scan_units": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i64, _i64, _vp, _vp, _vp, _i32,
+                                _vp]),
+    "st_knn_dequant": (_st, [_h, _vp, _vp, _i64, _i32, _vp]),
+    "st_knn_nearest": (_st, [_h, _vp, _vp, _i64, _i32, _vp]),
+    "st_knn_probe": (_st, [_h, _vp, _vp, _i64, _i32, _i32, _vp]),
+    "st_gather_rows": (_st, [_h, _vp, _i64, _vp, _vp, _i64, _i64]),
     "st_knn_synth_keys": (_st, [_h, _vp, _vp, _i64, _i32, ctypes.c_uint64, _i64]),
 }
 

@@ -3,6 +3,7 @@
 #include <mutex>
 
 #include "st_internal.h"
+#include "st_ptx.cuh"
 
 extern "C" st_status st_create(int device, void *stream, st_handle **out) {
     if (!out) return ST_INVALID_ARG;
@@ -67,6 +68,7 @@ extern "C" st_status st_sync(st_handle *h) {
     ST_CHECK_CUDA(h, cudaMemcpy(&status, h->d_status, sizeof(int), cudaMemcpyDeviceToHost));
     if (status != 0) {
         ST_CHECK_CUDA(h, cudaMemset(h->d_status, 0, sizeof(int)));
+        if (status == st::DEV_BAD_ARG) return h->fail(ST_INVALID_ARG, "a kernel met an out-of-range index");
         return h->fail(ST_TIMEOUT, "device-side bounded wait ran out (code %d)", status);
     }
     return ST_OK;

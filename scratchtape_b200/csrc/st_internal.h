@@ -25,6 +25,7 @@ enum StScratchSlot {
     SLOT_STEP_ROWS,   // per-row cross-entropy losses
     SLOT_COLSUM,      // column-sum partials of the GEMM epilogue
     SLOT_GROUP,       // grouped GEMM: ticket / finished-tile / split counters
+    SLOT_KNN_UNITS,   // kNN unit-table scans: the device copy of the unit tables
     SLOT_COUNT
 };
 

@@ -95,6 +95,13 @@ struct ScanArgs {
     uint64_t *unit_out;  // [splits * 2][nq_pad][KTOP]: one list per (split, column half)
     const int64_t *ranges;  // masked scans: [nq][2] global key range [lo, hi) per query, or null
     int64_t always;         // masked scans: keys below this global index are visible to every query
+    // unit-table scans (IVF): unit u scans store rows unit_keys[2u] .. unit_keys[2u + 1] for the queries
+    // unit_q[u * KQ + r] (-1: an empty row), writing row r's list to output list unit_list[u * KQ + r];
+    // null: the units are (query block, key split)
+    const int *unit_q;
+    const int *unit_list;
+    const int64_t *unit_keys;
+    int n_units;
     int *status;
 };
 
@@ -227,6 +234,21 @@ __device__ __forceinline__ void key_tile_range(const ScanArgs &g, int split, int
     k0 = static_cast<int64_t>(split) * g.tiles_per_split * KT;
     k1 = min(g.n_keys, k0 + g.tiles_per_split * KT);
 }
+// A unit's key rows, the query of each of its rows and the list that row writes.
+__device__ __forceinline__ void unit_key_range(const ScanArgs &g, int unit, int64_t &k0, int64_t &k1) {
+    if (g.unit_q) {
+        k0 = g.unit_keys[2 * static_cast<int64_t>(unit)];
+        k1 = g.unit_keys[2 * static_cast<int64_t>(unit) + 1];
+    } else {
+        key_tile_range(g, unit / g.nqb, k0, k1);
+    }
+}
+__device__ __forceinline__ int unit_query(const ScanArgs &g, int unit, int r) {
+    return g.unit_q ? g.unit_q[static_cast<int64_t>(unit) * KQ + r] : (unit % g.nqb) * KQ + r;
+}
+__device__ __forceinline__ int unit_out_list(const ScanArgs &g, int unit, int r) {
+    return g.unit_q ? g.unit_list[static_cast<int64_t>(unit) * KQ + r] : unit / g.nqb;
+}
 
 // Codes (d/4 bytes, zero-padded to 64) and scale of key `key` when it lies
 // below k1; zeros otherwise.
@@ -262,7 +284,7 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nchunks = g.d / 64;
-    const int units = g.nqb * g.splits;
+    const int units = g.unit_q ? g.n_units : g.nqb * g.splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < KSTAGES; s++) {
@@ -307,13 +329,12 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
         uint32_t lc = 0, gt = 0, ui = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ui) {
-            const int qb = unit % g.nqb, split = unit / g.nqb;
             // queries of this unit: row r, lane = 8 dims
             if (ui > 0 && !kwait(qfree, (ui - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
             for (int r = pw; r < KQ; r += NPROD / 32) {
-                const int qi = qb * KQ + r;
+                const int qi = unit_query(g, unit, r);
                 float x[8];
-                const bool live = qi < g.nq && lane * 8 < g.d;
+                const bool live = qi >= 0 && qi < g.nq && lane * 8 < g.d;
                 if (live) {
                     const float4 *src = reinterpret_cast<const float4 *>(g.q + static_cast<int64_t>(qi) * g.d + lane * 8);
                     const float4 a = __ldg(src), b = __ldg(src + 1);
@@ -350,7 +371,7 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             st::mbar_arrive(qfull);
 
             int64_t k0, k1;
-            key_tile_range(g, split, k0, k1);
+            unit_key_range(g, unit, k0, k1);
             uint4 nx_cw[4];
             float nx_sk;
             load_key_codes(g, k0 + pt, k1, nchunks, nx_cw, nx_sk);
@@ -441,11 +462,10 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             uint32_t lc = 0, gt = 0, ui = 0;
             bool ok = true;
             for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++ui) {
-                const int split = unit / g.nqb;
                 if (!kwait(qfull, ui & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
                 st::tc_fence_after();
                 int64_t k0, k1;
-                key_tile_range(g, split, k0, k1);
+                unit_key_range(g, unit, k0, k1);
                 for (int64_t tb = k0; tb < k1 && ok; tb += KT, ++gt) {
                     const uint32_t b = gt & 1u, use = gt >> 1;
                     if (use > 0 && !kwait(&acce[b], (use - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
@@ -495,9 +515,8 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
         uint32_t gt = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
-            const int qb = unit % g.nqb, split = unit / g.nqb;
-            const int qi = qb * KQ + row;
-            const bool qlive = qi < g.nq;
+            const int qi = unit_query(g, unit, row);
+            const bool qlive = qi >= 0 && qi < g.nq;
             // search_masked (src/gpu_step/knn.rs:280-291): key j visible iff
             // j < always or lo <= j < hi
             int64_t mlo = 0, mhi = 0;
@@ -518,7 +537,7 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
             int cnt = 0;
             float thr = -INFINITY;
             int64_t k0, k1;
-            key_tile_range(g, split, k0, k1);
+            unit_key_range(g, unit, k0, k1);
             for (int64_t tb = k0; tb < k1; tb += KT, ++gt) {
                 const uint32_t b = gt & 1u, use = gt >> 1;
                 if (!kwait(&accf[b], use & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
@@ -582,7 +601,8 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                 if (need) warp_compact(need, my_buf, cnt, thr, nullptr, false);
             }
             if (!ok) break;
-            uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(split) * 2 + half) * g.nq_pad + qi) * KTOP;
+            const int list = qlive ? unit_out_list(g, unit, row) : 0;
+            uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(list) * 2 + half) * g.nq_pad + (qlive ? qi : 0)) * KTOP;
             const unsigned need = __ballot_sync(0xffffffffu, qlive);
             if (need) warp_compact(need, my_buf, cnt, thr, my_out, true);
         }
@@ -804,6 +824,106 @@ st_status check_common(st_handle *h, const uint8_t *codes, const float *scales, 
     return ST_OK;
 }
 
+// ---- IVF building blocks (src/gpu_step/knn/ivf.rs) -------------------------
+
+// out[r, j] = (u_j - 1.5) * scale_r: the 2-bit rows as f32 (k_dequant, knn.rs:630-643, without the f16 rounding).
+__global__ void k_knn_dequant(const uint8_t *codes, const float *scales, int64_t n, int d, float *out) {
+    const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;  // one code byte
+    const int64_t nb = n * (d / 4);
+    if (e >= nb) return;
+    const int64_t r = e / (d / 4);
+    const uint32_t byte = codes[e];
+    const float sc = scales[r];
+    float4 v;
+    v.x = (static_cast<float>(byte & 3u) - 1.5f) * sc;
+    v.y = (static_cast<float>((byte >> 2) & 3u) - 1.5f) * sc;
+    v.z = (static_cast<float>((byte >> 4) & 3u) - 1.5f) * sc;
+    v.w = (static_cast<float>((byte >> 6) & 3u) - 1.5f) * sc;
+    reinterpret_cast<float4 *>(out)[e] = v;
+}
+
+// Nearest cell of each row from dots = rows . centroids^T: argmin over c of
+// cnorm[c] - 2 dots[r, c], the lowest c among equals (k_argmin, ivf.rs:75-113).
+// One warp per row.
+__global__ void k_knn_nearest(const float *dots, const float *cnorm, int64_t n, int nl, int32_t *out) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    const float *row = dots + r * nl;
+    float best = INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < nl; c += 32) {
+        const float v = fmaf(-2.0f, row[c], cnorm[c]);
+        if (v < best) {  // lanes visit their columns in increasing order: the first minimum is kept
+            best = v;
+            bi = c;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov < best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) out[r] = bi;
+}
+
+// Each query's nprobe nearest cells, nearest first, ties to the lower cell
+// (k_probe, ivf.rs:126-165): nprobe rounds of a warp minimum over the entries
+// after the last one taken in (distance, cell) order.
+__global__ void k_knn_probe(const float *dots, const float *cnorm, int64_t nq, int nl, int nprobe, int32_t *out) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= nq) return;
+    const float *row = dots + r * nl;
+    float last = -INFINITY;
+    int lasti = -1;
+    for (int p = 0; p < nprobe; p++) {
+        float best = INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = lane; c < nl; c += 32) {
+            const float v = fmaf(-2.0f, row[c], cnorm[c]);
+            const bool after = v > last || (v == last && c > lasti);
+            if (after && (v < best || (v == best && c < bi))) {
+                best = v;
+                bi = c;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov < best || (ov == best && oi < bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) out[r * nprobe + p] = bi < nl ? bi : -1;
+        last = best;
+        lasti = bi;
+    }
+}
+
+// dst row i = src row perm[i]; rows of `words` 32-bit words.  A perm entry
+// outside [0, n_src) yields a zero row and a DEV_BAD_ARG status.
+__global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst, const int64_t *perm, int64_t n,
+                              int words, int *status) {
+    const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (e >= n * words) return;
+    const int64_t i = e / words;
+    const int w = static_cast<int>(e % words);
+    const int64_t j = perm[i];
+    if (j < 0 || j >= n_src) {
+        dst[e] = 0u;
+        if (w == 0) st::set_status(status, st::DEV_BAD_ARG);
+        return;
+    }
+    dst[e] = src[j * words + w];
+}
+
 }  // namespace
 
 static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
@@ -859,6 +979,76 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     }
     if (s != ST_OK) return s;
     k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, 2 * splits, nq_pad * KTOP, out_keys);
+    return st_after_launch(h, "k_knn_merge");
+}
+
+extern "C" st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,
+                                       int32_t dim, const float *queries, int64_t nq, int32_t mode, int32_t prec,
+                                       int64_t index_base, int64_t n_units, const int32_t *unit_q,
+                                       const int32_t *unit_list, const int64_t *unit_keys, int32_t n_lists,
+                                       uint64_t *out_keys) {
+    const char *who = "st_knn_scan_units";
+    if (!h) return ST_INVALID_ARG;
+    st_status s = check_common(h, codes, scales, n_keys, dim, queries, nq, mode, prec, index_base, who);
+    if (s != ST_OK) return s;
+    if (!out_keys || !unit_q || !unit_list || !unit_keys || n_units < 1 || n_units > (1LL << 30) || n_lists < 1 ||
+        n_lists > 4096)
+        return h->fail(ST_INVALID_ARG, "%s: bad unit tables", who);
+    // the tables are host arrays: every row and range is checked here, before any device read depends on them
+    for (int64_t u = 0; u < n_units; u++) {
+        const int64_t k0 = unit_keys[2 * u], k1 = unit_keys[2 * u + 1];
+        if (k0 < 0 || k1 < k0 || k1 > n_keys) return h->fail(ST_INVALID_ARG, "%s: unit %lld key range", who, (long long)u);
+        for (int r = 0; r < KQ; r++) {
+            const int32_t q = unit_q[u * KQ + r], l = unit_list[u * KQ + r];
+            if (q < -1 || q >= nq || (q >= 0 && (l < 0 || l >= n_lists)))
+                return h->fail(ST_INVALID_ARG, "%s: unit %lld row %d", who, (long long)u, r);
+        }
+    }
+    cudaSetDevice(h->device);
+    const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
+    const int64_t nq_pad = static_cast<int64_t>(nqb) * KQ;
+    const int grid = static_cast<int>(std::min<int64_t>(n_units, h->num_sms));
+    const size_t tab_bytes = sizeof(int32_t) * 2 * n_units * KQ + sizeof(int64_t) * 2 * n_units;
+    uint8_t *tab = static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_UNITS, tab_bytes));
+    uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * NEPI * KCAP));
+    const size_t out_bytes = sizeof(uint64_t) * 2 * static_cast<size_t>(n_lists) * nq_pad * KTOP;
+    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes));
+    if (!tab || !cbuf || !unit_out) return ST_NO_MEMORY;
+    int64_t *d_keys = reinterpret_cast<int64_t *>(tab);
+    int32_t *d_q = reinterpret_cast<int32_t *>(tab + sizeof(int64_t) * 2 * n_units);
+    int32_t *d_list = d_q + n_units * KQ;
+    ST_CHECK_CUDA(h, cudaMemcpyAsync(d_keys, unit_keys, sizeof(int64_t) * 2 * n_units, cudaMemcpyHostToDevice, h->stream));
+    ST_CHECK_CUDA(h, cudaMemcpyAsync(d_q, unit_q, sizeof(int32_t) * n_units * KQ, cudaMemcpyHostToDevice, h->stream));
+    ST_CHECK_CUDA(h, cudaMemcpyAsync(d_list, unit_list, sizeof(int32_t) * n_units * KQ, cudaMemcpyHostToDevice,
+                                     h->stream));
+    // lists no unit writes (a query with fewer probes than lists) read as empty
+    ST_CHECK_CUDA(h, cudaMemsetAsync(unit_out, 0, out_bytes, h->stream));
+
+    ScanArgs g{};
+    g.codes = codes;
+    g.scales = scales;
+    g.q = queries;
+    g.n_keys = n_keys;
+    g.d = dim;
+    g.nq = static_cast<int>(nq);
+    g.nq_pad = static_cast<int>(nq_pad);
+    g.nqb = nqb;
+    g.splits = 1;
+    g.tiles_per_split = 1;
+    g.index_base = static_cast<uint32_t>(index_base);
+    g.cbuf = cbuf;
+    g.unit_out = unit_out;
+    g.unit_q = d_q;
+    g.unit_list = d_list;
+    g.unit_keys = d_keys;
+    g.n_units = static_cast<int>(n_units);
+    g.status = h->d_status;
+    if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT, false>(h, g, grid);
+    else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF, false>(h, g, grid);
+    else if (prec == 0) s = launch_scan<MODE_L2, PREC_EXACT, false>(h, g, grid);
+    else s = launch_scan<MODE_L2, PREC_F16REF, false>(h, g, grid);
+    if (s != ST_OK) return s;
+    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, 2 * n_lists, nq_pad * KTOP, out_keys);
     return st_after_launch(h, "k_knn_merge");
 }
 
@@ -941,4 +1131,49 @@ extern "C" st_status st_knn_search_masked(st_handle *h, const uint8_t *codes, co
                             "st_knn_search_masked");
     if (s != ST_OK) return s;
     return st_knn_decode(h, keys, queries, nq, dim, k, mode, prec, out_scores, out_ids);
+}
+
+// ---- IVF building blocks ---------------------------------------------------
+
+extern "C" st_status st_knn_dequant(st_handle *h, const uint8_t *codes, const float *scales, int64_t n, int32_t dim,
+                                    float *out) {
+    if (!h) return ST_INVALID_ARG;
+    if (!codes || !scales || !out || n < 1 || dim < 4 || dim % 4 != 0)
+        return h->fail(ST_INVALID_ARG, "st_knn_dequant: bad arguments");
+    cudaSetDevice(h->device);
+    const int64_t nb = n * (dim / 4);
+    k_knn_dequant<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, h->stream>>>(codes, scales, n, dim, out);
+    return st_after_launch(h, "k_knn_dequant");
+}
+
+extern "C" st_status st_knn_nearest(st_handle *h, const float *dots, const float *cnorm, int64_t n, int32_t nlist,
+                                    int32_t *out) {
+    if (!h) return ST_INVALID_ARG;
+    if (!dots || !cnorm || !out || n < 1 || nlist < 1) return h->fail(ST_INVALID_ARG, "st_knn_nearest: bad arguments");
+    cudaSetDevice(h->device);
+    k_knn_nearest<<<static_cast<unsigned>((n + 7) / 8), 256, 0, h->stream>>>(dots, cnorm, n, nlist, out);
+    return st_after_launch(h, "k_knn_nearest");
+}
+
+extern "C" st_status st_knn_probe(st_handle *h, const float *dots, const float *cnorm, int64_t nq, int32_t nlist,
+                                  int32_t nprobe, int32_t *out) {
+    if (!h) return ST_INVALID_ARG;
+    if (!dots || !cnorm || !out || nq < 1 || nlist < 1 || nprobe < 1 || nprobe > nlist || nprobe > 64)
+        return h->fail(ST_INVALID_ARG, "st_knn_probe: bad arguments (1 <= nprobe <= min(nlist, 64))");
+    cudaSetDevice(h->device);
+    k_knn_probe<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, h->stream>>>(dots, cnorm, nq, nlist, nprobe, out);
+    return st_after_launch(h, "k_knn_probe");
+}
+
+extern "C" st_status st_gather_rows(st_handle *h, const void *src, int64_t n_src, void *dst, const int64_t *perm,
+                                    int64_t n, int64_t row_bytes) {
+    if (!h) return ST_INVALID_ARG;
+    if (!src || !dst || !perm || n < 1 || n_src < 1 || row_bytes < 4 || row_bytes % 4 != 0 || row_bytes > (1 << 20))
+        return h->fail(ST_INVALID_ARG, "st_gather_rows: bad arguments");
+    cudaSetDevice(h->device);
+    const int words = static_cast<int>(row_bytes / 4);
+    const int64_t total = n * words;
+    k_gather_rows<<<static_cast<unsigned>((total + 255) / 256), 256, 0, h->stream>>>(
+        static_cast<const uint32_t *>(src), n_src, static_cast<uint32_t *>(dst), perm, n, words, h->d_status);
+    return st_after_launch(h, "k_gather_rows");
 }

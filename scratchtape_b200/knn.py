@@ -10,6 +10,7 @@ first as (score, key index) -- and, when values were stored, the values.
 
 There is no CPU path: every method calls libst_b200.so.
 """
+import ctypes
 from typing import Optional
 
 import numpy as np
@@ -111,6 +112,105 @@ def decode(keys, queries, k=KMAX, mode="l2", prec="exact", out=None):
     handle(queries.device).call("st_knn_decode", ptr(keys), ptr(queries), nq, d, k, MODES[mode], PRECS[prec],
                                 ptr(out[0]), ptr(out[1]))
     return out
+
+
+def dequant(codes: torch.Tensor, scales: torch.Tensor):
+    """2-bit rows -> f32 [n, d]: (u - 1.5) * scale."""
+    n = codes.shape[0]
+    out = torch.empty((n, codes.shape[1] * 4), dtype=torch.float32, device=codes.device)
+    handle(codes.device).call("st_knn_dequant", ptr(codes), ptr(scales), n, codes.shape[1] * 4, ptr(out))
+    return out
+
+
+def gather_rows(src: torch.Tensor, perm: torch.Tensor):
+    """src[perm] on the device (st_gather_rows); rows of 4-byte multiples."""
+    src = src.contiguous()
+    perm = perm.to(device=src.device, dtype=torch.int64).contiguous()
+    out = torch.empty((perm.shape[0],) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row_bytes = src[0].numel() * src.element_size()
+    handle(src.device).call("st_gather_rows", ptr(src), src.shape[0], ptr(out), ptr(perm), perm.shape[0], row_bytes)
+    return out
+
+
+def _centroid_dots(x: torch.Tensor, cent: torch.Tensor, out=None):
+    """x . cent^T [n, nlist] on the TF32 tensor cores."""
+    from .matmul import TF32, MatRef, matmul_with
+    n, nl = x.shape[0], cent.shape[0]
+    if out is None:
+        out = torch.empty((n, nl), dtype=torch.float32, device=x.device)
+    matmul_with(MatRef(x), MatRef(cent, trans=True), MatRef(out), 1, n, x.shape[1], nl, None, TF32)
+    return out
+
+
+def nearest_cells(x: torch.Tensor, cent: torch.Tensor, cnorm: torch.Tensor, chunk_bytes: int = 1 << 30):
+    """Each row's nearest centroid (argmin |c|^2 - 2 x.c), int32 [n], in chunks
+    whose distance block stays under chunk_bytes."""
+    n, nl = x.shape[0], cent.shape[0]
+    out = torch.empty(n, dtype=torch.int32, device=x.device)
+    rows = max(1024, chunk_bytes // (4 * nl))
+    buf = torch.empty((min(rows, n), nl), dtype=torch.float32, device=x.device)
+    h = handle(x.device)
+    for a in range(0, n, rows):
+        b = min(n, a + rows)
+        dots = _centroid_dots(x[a:b], cent, out=buf[:b - a])
+        h.call("st_knn_nearest", ptr(dots), ptr(cnorm), b - a, nl, ptr(out[a:]))
+    return out
+
+
+def probe_cells(q: torch.Tensor, cent: torch.Tensor, cnorm: torch.Tensor, nprobe: int):
+    """Each query's nprobe nearest centroids, nearest first: int32 [nq, nprobe]."""
+    dots = _centroid_dots(q, cent)
+    out = torch.empty((q.shape[0], nprobe), dtype=torch.int32, device=q.device)
+    handle(q.device).call("st_knn_probe", ptr(dots), ptr(cnorm), q.shape[0], cent.shape[0], nprobe, ptr(out))
+    return out
+
+
+def ivf_units(probes: np.ndarray, starts: np.ndarray):
+    """The scan's unit tables for queries probing cells: one unit per (cell,
+    up to 128 of the queries probing it); row r of a unit is (query, its probe
+    slot).  Returns (unit_q int32 [u, 128], unit_list int32 [u, 128],
+    unit_keys int64 [u, 2])."""
+    nq, nprobe = probes.shape
+    cells = probes.reshape(-1).astype(np.int64)
+    qs = np.repeat(np.arange(nq, dtype=np.int32), nprobe)
+    slots = np.tile(np.arange(nprobe, dtype=np.int32), nq)
+    order = np.argsort(cells, kind="stable")
+    cells, qs, slots = cells[order], qs[order], slots[order]
+    new_run = np.r_[True, cells[1:] != cells[:-1]]
+    run_id = np.cumsum(new_run) - 1
+    run_first = np.flatnonzero(new_run)
+    rank = np.arange(len(cells)) - run_first[run_id]
+    run_len = np.diff(np.r_[run_first, len(cells)])
+    run_units = (run_len + KQ_ROWS - 1) // KQ_ROWS
+    unit_base = np.r_[0, np.cumsum(run_units)[:-1]]
+    unit = unit_base[run_id] + rank // KQ_ROWS
+    row = rank % KQ_ROWS
+    n_units = int(run_units.sum())
+    unit_q = np.full((n_units, KQ_ROWS), -1, np.int32)
+    unit_list = np.zeros((n_units, KQ_ROWS), np.int32)
+    unit_q[unit, row] = qs
+    unit_list[unit, row] = slots
+    unit_cell = cells[run_first][np.repeat(np.arange(len(run_first)), run_units)]
+    unit_keys = np.stack([starts[unit_cell], starts[unit_cell + 1]], axis=1).astype(np.int64)
+    return unit_q, unit_list, np.ascontiguousarray(unit_keys)
+
+
+def scan_units(codes, scales, queries, unit_q, unit_list, unit_keys, n_lists, mode="l2", prec="exact",
+               index_base=0, out=None):
+    """The fused scan over unit tables (host numpy arrays): sortable keys [nq, 128]."""
+    queries = queries.contiguous().float()
+    nq, d = queries.shape
+    if out is None:
+        out = torch.empty((nq, KMAX), dtype=torch.int64, device=queries.device)
+    uq, ul, uk = (np.ascontiguousarray(a) for a in (unit_q, unit_list, unit_keys))
+    handle(queries.device).call("st_knn_scan_units", ptr(codes), ptr(scales), codes.shape[0], d, ptr(queries), nq,
+                                MODES[mode], PRECS[prec], index_base, uq.shape[0], uq.ctypes.data_as(ctypes.c_void_p),
+                                ul.ctypes.data_as(ctypes.c_void_p), uk.ctypes.data_as(ctypes.c_void_p), n_lists,
+                                ptr(out))
+    return out
+
+
+KQ_ROWS = 128  # queries per scan unit (the MMA tile's M)
 
 
 class KnnStore:
@@ -220,7 +320,8 @@ class KnnStore:
         inflight = []
 
         def on_tile(first, codes, scales, norms, vals):
-            host = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in (codes, scales, norms, vals)]
+            host = [torch.from_numpy(np.require(a, requirements=["C", "W"])).pin_memory()
+                    for a in (codes, scales, norms, vals)]
             with torch.cuda.stream(stream):
                 devs = [t.to(dev, non_blocking=True) for t in host]
             ev = torch.cuda.Event()
@@ -244,6 +345,75 @@ class KnnStore:
         store.first = meta["first"]
         store.ivf_raw = meta["ivf"]  # kept for a later IVF search; flat scans ignore it
         return store, meta["extra"]
+
+    def build_ivf(self, nlist: int, iters: int = 10, sample: Optional[int] = None):
+        """KnnStore::build_ivf (src/gpu_step/knn/ivf.rs:337-449): Lloyd's
+        k-means on an evenly spaced sample of the keys (starting from evenly
+        spaced sample keys; an empty cell restarts at another sample key, as
+        the reference does), then every key's nearest cell, then the keys,
+        scales, norms and values reordered cell by cell on the device.  The
+        distance GEMMs run on the TF32 tensor cores and the assignments in
+        st_knn_nearest; the centroid sums are taken on the host in f64 over
+        the sample (the reference sums on the host too).  ``self.ivf_order``
+        maps the new key positions to the old ones."""
+        self.finish()
+        n, d = len(self), self.d
+        if not 1 <= nlist <= n:
+            raise ValueError("build_ivf: 1 <= nlist <= keys")
+        ns = min(n, sample if sample is not None else max(8 * nlist, min(n, 32 * nlist)))
+        idx = (torch.arange(ns, dtype=torch.int64, device=self.device) * n) // ns
+        xs = dequant(gather_rows(self.codes, idx), gather_rows(self.scales.view(-1, 1), idx).view(-1))
+        xs_h = xs.cpu().numpy().astype(np.float64)
+        cent = xs_h[(np.arange(nlist) * ns) // nlist].copy()
+        for it in range(iters):
+            c_dev = torch.from_numpy(cent.astype(np.float32)).to(self.device)
+            cnorm = torch.from_numpy(np.square(cent).sum(1).astype(np.float32)).to(self.device)
+            a = nearest_cells(xs, c_dev, cnorm).cpu().numpy().astype(np.int64)
+            order = np.argsort(a, kind="stable")
+            counts = np.bincount(a, minlength=nlist)
+            sums = np.zeros((nlist, d))
+            nz = np.flatnonzero(counts)
+            sums[nz] = np.add.reduceat(xs_h[order], np.r_[0, np.cumsum(counts)[:-1]][nz], axis=0)
+            for c in range(nlist):
+                if counts[c] > 0:
+                    cent[c] = sums[c] / counts[c]
+                else:
+                    cent[c] = xs_h[(c * 7919 + it * 104729) % ns]
+        c_dev = torch.from_numpy(cent.astype(np.float32)).to(self.device)
+        cnorm = torch.from_numpy(np.square(cent).sum(1).astype(np.float32)).to(self.device)
+        cell = torch.empty(n, dtype=torch.int32, device=self.device)
+        chunk = 1 << 16
+        for a0 in range(0, n, chunk):
+            b0 = min(n, a0 + chunk)
+            cell[a0:b0] = nearest_cells(dequant(self.codes[a0:b0], self.scales[a0:b0]), c_dev, cnorm)
+        cell_h = cell.cpu().numpy().astype(np.int64)
+        order = np.argsort(cell_h, kind="stable")
+        starts = np.r_[0, np.cumsum(np.bincount(cell_h, minlength=nlist))].astype(np.int64)
+        perm = torch.from_numpy(order).to(self.device)
+        self.codes = gather_rows(self.codes, perm)
+        self.scales = gather_rows(self.scales.view(-1, 1), perm).view(-1)
+        self.norms = gather_rows(self.norms.view(-1, 1), perm).view(-1)
+        self.vals = gather_rows(self.vals.view(-1, 1), perm).view(-1)
+        self.ivf_order = order
+        self.ivf = {"cent": c_dev, "cnorm": cnorm, "starts": starts, "nlist": nlist}
+
+    def search_ivf(self, queries, rows: Optional[int] = None, nprobe: int = 8, mode: str = "l2",
+                   prec: str = "exact", with_ids: bool = False):
+        """KnnStore::search_ivf (ivf.rs:466-526): for each query, the 128 best
+        among the keys of its nprobe nearest cells.  One scan launch over a
+        table of (cell, up to 128 queries probing it) units, then one merge of
+        each query's nprobe lists.  Returns (scores, values), or (scores, key
+        indices) with ``with_ids``."""
+        if getattr(self, "ivf", None) is None:
+            raise RuntimeError("search_ivf needs build_ivf")
+        q = self._queries(queries, rows)
+        iv = self.ivf
+        probes = probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
+        uq, ul, uk = ivf_units(probes, iv["starts"])
+        keys = scan_units(self.codes, self.scales, q, uq, ul, uk, nprobe, mode=mode, prec=prec,
+                          index_base=self.first)
+        scores, ids = decode(keys, q, KMAX, mode=mode, prec=prec)
+        return (scores, ids) if with_ids else (scores, self._values(ids))
 
     def finish(self):
         if not self._pending:
