@@ -604,8 +604,8 @@ def run_ours_c5(args):
     small_pass = {"queries": 32, "scan_ms": ms32, "keys_per_s": n_total / (ms32 / 1e3),
                   "hbm_gbs": bytes32 / (ms32 / 1e3) / 1e9, "hbm_frac": bytes32 / (ms32 / 1e3) / 1e9 /
                   float(peaks["hbm_gbs"]),
-                  "note": "one k_knn_scan launch; the MMA tile is 128 queries, so 32 queries run at the 128-query "
-                          "cost: tensor-bound, not HBM-bound"}
+                  "note": "the narrow scan (k_knn_narrow: 128 keys per MMA in TMEM, queries as 4 int8 limbs, "
+                          "exact integer products) seeded by a 1-in-64 tile sample pass, + k_knn_merge"}
 
     flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
     achieved = flops_alg / (scan_ms / 1e3) / 1e12

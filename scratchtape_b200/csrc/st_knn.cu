@@ -924,6 +924,616 @@ __global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst,
     dst[e] = src[j * words + w];
 }
 
+
+// ---- the narrow scan: at most 32 queries per pass --------------------------
+//
+// With a handful of queries the scan above runs at its 128-query cost.  On the
+// tensor core an M = 128 MMA costs at least ~50 cycles whatever N is (the A
+// operand, 4 KB, is read for every instruction), so few queries only pay if
+// each instruction does more work per key: k_knn_narrow puts 128 keys on the
+// M side, in tensor memory, as one byte per dimension (u = 0..3), and runs
+// kind::i8 (K = 32 per instruction, 8 instructions per 128-key tile) against
+// the queries as NL signed-byte limbs of a fixed-point integer X_i =
+// round(q_i 2^(e + 8 NL - 17)) (max |X| < 2^(8 NL - 2)), limb l of query q in
+// B row l * NQP + q.  The products and sums are exact integers:
+//   A_l = sum_i u_i limb_l,i     and     S = sum_l 2^8l (A_l - C_l) = sum_i (u_i - 1.5) X_i,
+// with C_l = 1.5 sum_i limb_l,i, so the only rounding is the query's to 8 NL - 2
+// bits (EXACT: NL = 4; F16REF: NL = 3, still finer than the reference's f16).
+// Roles (448 threads, one CTA per SM, one key split per CTA):
+//   warp 13 (one thread): bulk-copies each 128-key tile's codes (8 KB) and the
+//     16-byte blocks holding its scales into a 12-stage shared-memory ring.
+//   warps 4-11 (producers; warp w writes TMEM lanes 32 (w % 4) + 16 (w / 8)..):
+//     spread the codes into bytes -- (word >> 2s) & 0x03030303 puts codes s,
+//     s + 4, s + 8, s + 12 of a 16-code word into one 32-bit word -- and store
+//     them with tcgen05.st (16x256b: a warp's 512 contiguous code bytes map onto
+//     16 TMEM lanes without shuffles); the queries' K order follows that
+//     permutation of the dimensions.
+//   warp 12 (one thread): tcgen05.mma kind::i8, A = keys (u8, TMEM), B = limbs
+//     (s8, shared memory), D = s32, N = NL * NQP columns; two accumulators.
+//   warps 0-3 (epilogue; warp w reads TMEM lanes 32 w..): thread = key.  A
+//     limb column plus 0x4B400000, viewed as a float, is 1.5 2^23 + A_l
+//     exactly (|A_l| < 2^17); the two top limbs
+//     bound S within +-R (R from the per-query sums of |limb|), and one FMA,
+//     one FMA and a compare per (key, query) test the key against the query's
+//     running 128th-best score with every term lowered -- never rejecting a
+//     key whose exact score passes.  Keys that pass take the exact S from all
+//     limbs and go into the candidate buffer of (warp, query), owned by lane q
+//     of the warp.  The 128th-best scores are shared: each warp publishes its
+//     own through a global atomicMax per query and filters against the best
+//     any warp of any CTA has published (a key below another list's 128th
+//     best cannot be in the final top 128), so after the first tiles keys
+//     rarely reach the exact path.
+// Scores come out in the wide scan's units, so k_knn_merge and k_knn_decode
+// are shared.
+constexpr int NQ = 32;                                  // queries per pass
+constexpr int NK = 128;                                 // keys per tile (MMA M, TMEM lanes)
+constexpr int N_STAGES = 12;                            // code / scale ring
+constexpr int N_CODE_BYTES = NK * 64;                   // dim 256: 64 code bytes per key
+constexpr int N_STAGE_BYTES = N_CODE_BYTES + NK * 4 + 16;  // scales from the 16-byte block of the first
+constexpr int N_A = 4;                                  // TMEM A buffers, 64 columns each
+constexpr int N_ACC = 2;                                // TMEM accumulators, 128 columns each
+constexpr int N_ACC_COLS = 128;
+constexpr int N_KF = 8;                                 // per-key factor slots (lifetime: see the producer)
+constexpr int N_EPI = 4, N_PROD = 8;
+constexpr int N_MMA_WARP = N_EPI + N_PROD;              // 12
+constexpr int N_TMA_WARP = N_MMA_WARP + 1;              // 13
+constexpr int N_THREADS = 32 * (N_TMA_WARP + 1);        // 448
+constexpr int NO_Q = 0;                                 // B: [2 K chunks][128 rows x 128 B], SW128
+constexpr int NQ_CHUNK = 128 * 128;
+constexpr int NO_RING = NO_Q + 2 * NQ_CHUNK;
+constexpr int NO_KF = NO_RING + N_STAGES * N_STAGE_BYTES;  // [N_KF][128] scale
+constexpr int NO_KN = NO_KF + N_KF * NK * 4;               // [N_KF][128] |k|^2 (L2)
+constexpr int NO_QC = NO_KN + N_KF * NK * 4;               // [8][32] per-query constants
+constexpr int NO_THR = NO_QC + 8 * NQ * 4;                 // [2][4 warps][32] thresholds
+constexpr int NO_SLOT = NO_THR + 2 * N_EPI * NQ * 4;       // [32 queries][128 threads] exact scores
+constexpr int NO_BAR = NO_SLOT + N_EPI * 32 * NQ * 4;
+constexpr int N_NBARS = 2 * N_STAGES + 2 * N_A + 2 * N_ACC + N_KF + 2;
+constexpr int NO_MISC = NO_BAR + N_NBARS * 8;              // tmem slot, abort flag
+constexpr int NARROW_SMEM = NO_MISC + 16 + 1024;
+constexpr uint32_t N_TMEM_COLS = 512;
+constexpr uint32_t N_ACC_COL = N_A * 64;                   // accumulators after the A buffers
+constexpr int MAGIC_I = 0x4B400000;                        // float 1.5 * 2^23
+constexpr float MAGIC_F = 12582912.0f;
+
+static_assert(NARROW_SMEM <= 232448, "narrow kNN scan shared memory exceeds the sm_100 limit");
+static_assert(N_ACC_COL + N_ACC * N_ACC_COLS <= N_TMEM_COLS, "narrow kNN scan TMEM budget");
+
+struct NarrowArgs {
+    const uint8_t *codes;  // [n_keys, 64], 16-byte aligned
+    const float *scales;   // [n_keys], 4-byte aligned
+    const float *q;        // [nq, 256]
+    int64_t n_keys;
+    int nq, nqp, splits;   // nqp: queries per limb block of B (a multiple of 8, NL * nqp % 16 == 0)
+    // unit u scans 128-key tiles u * unit_step + i * tile_step, i < tiles_per_unit, below n_tiles
+    int64_t n_tiles, unit_step, tile_step, tiles_per_unit;
+    uint32_t index_base;
+    uint64_t *cbuf;        // [gridDim.x][4 warps][32 queries][KCAP]
+    uint64_t *unit_out;    // [splits * 4][32][KTOP]
+    uint32_t *gthr;        // [32] order-preserving bits of the best published 128th score (0: none)
+    int *status;
+};
+
+// Dimension (0..255) held by byte k of the narrow scan's A rows.
+__device__ __forceinline__ int narrow_dim(int k) {
+    const int col = k >> 2, p = k & 3;
+    const int r = col >> 3, c = (col >> 1) & 3, b = col & 1;
+    const int m = r >> 1, s = 2 * (r & 1) + b;
+    return 16 * (4 * c + m) + 4 * p + s;
+}
+
+// x lowered by 2^-12 of its magnitude (-inf and +inf unchanged).
+__device__ __forceinline__ float lowered(float x) { return x - fabsf(x) * 0.000244140625f; }
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Stores 16 TMEM lanes x 64 columns (16x256b, 8 repetitions): repetition j,
+// thread t: r[4j], r[4j+1] -> lane t/4, columns 8j + 2(t%4) + {0,1};
+// r[4j+2], r[4j+3] -> lane 8 + t/4, the same columns.
+__device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
+
+// kwait for the narrow scan's hand-offs, which come every few hundred
+// nanoseconds: polls without a suspend hint (a woken sleeper would add its
+// wake-up latency to every tile), still bounded by the time limit and the
+// CTA's abort flag.
+__device__ __forceinline__ bool nwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                      int code) {
+    if (st::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = st::globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (st::mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (st::globaltimer() - t0 > st::WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                st::set_status(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Tile i of unit `unit`: its first key tb and key count nk; false past the unit's end.
+__device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64_t i, int64_t &tb, int &nk) {
+    if (i >= g.tiles_per_unit) return false;
+    const int64_t t = static_cast<int64_t>(unit) * g.unit_step + i * g.tile_step;
+    if (t >= g.n_tiles) return false;
+    tb = t * NK;
+    nk = static_cast<int>(g.n_keys - tb < NK ? g.n_keys - tb : NK);
+    return true;
+}
+
+template <int MODE, int PREC>
+__global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g) {
+    constexpr int NL = PREC == PREC_EXACT ? 4 : 3;   // query limbs
+    constexpr int EB = 8 * NL - 17;                  // X = round(2^(e + EB) q)
+    constexpr float SH = NL == 4 ? 1.52587890625e-05f : 0.00390625f;  // 2^-8 (NL - 2)
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *kf = reinterpret_cast<float *>(smem + NO_KF);
+    float *kn = reinterpret_cast<float *>(smem + NO_KN);
+    float *qc = reinterpret_cast<float *>(smem + NO_QC);
+    float *qc_c = qc;            // filter constant (v units), lowered
+    float *qc_ql = qc + NQ;      // qf / P * SH, lowered (L2)
+    float *qc_P = qc + 2 * NQ;   // s = S * scale * P - |k|^2 qf
+    float *qc_qf = qc + 3 * NQ;
+    float *qc_C = qc + 4 * NQ;   // [4][32]: C_l
+    float *thr_s = reinterpret_cast<float *>(smem + NO_THR);  // [4][32] effective 128th-best score
+    float *thr_l = thr_s + N_EPI * NQ;                        // [4][32] the same / P * SH, lowered
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NO_BAR);
+    uint64_t *rfull = bars, *rempty = bars + N_STAGES, *afull = bars + 2 * N_STAGES, *aempty = afull + N_A;
+    uint64_t *accf = aempty + N_A, *acce = accf + N_ACC, *kfr = acce + N_ACC, *qready = kfr + N_KF, *fin = qready + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + NO_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + NO_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nqp = g.nqp;
+    if (threadIdx.x == 0) {
+        // one arrival per warp: a warp's lanes meet at __syncwarp and lane 0 arrives
+        for (int s = 0; s < N_STAGES; s++) {
+            st::mbar_init(&rfull[s], 1);
+            st::mbar_init(&rempty[s], N_PROD);
+        }
+        for (int b = 0; b < N_A; b++) {
+            st::mbar_init(&afull[b], N_PROD);
+            st::mbar_init(&aempty[b], 1);
+        }
+        for (int a = 0; a < N_ACC; a++) {
+            st::mbar_init(&accf[a], 1);
+            st::mbar_init(&acce[a], N_EPI);
+        }
+        for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
+        st::mbar_init(qready, N_PROD);
+        st::mbar_init(fin, 1);
+        *abort_flag = 0;
+        st::fence_mbar_init();
+    }
+    if (warp == N_MMA_WARP) {
+        st::tmem_alloc(tmem_slot, N_TMEM_COLS);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == N_TMA_WARP) {
+        // ------------------------------------------------------------ code / scale loader
+        if (lane == 0) {
+            uint32_t gt = 0;
+            bool ok = true;
+            for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+                int64_t tb;
+                int nk;
+                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                    const uint32_t s = gt % N_STAGES;
+                    if (gt >= N_STAGES &&
+                        !nwait(&rempty[s], ((gt / N_STAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    // the scales go as the 16-byte blocks that hold them: a bulk copy
+                    // starts and ends on 16-byte boundaries, and those blocks lie
+                    // inside the scales' allocation
+                    const uintptr_t s0 = reinterpret_cast<uintptr_t>(g.scales + tb) & ~uintptr_t(15);
+                    const uintptr_t s1 = (reinterpret_cast<uintptr_t>(g.scales + tb + nk) + 15) & ~uintptr_t(15);
+                    const uint32_t cb = static_cast<uint32_t>(nk) * 64u, sb = static_cast<uint32_t>(s1 - s0);
+                    uint8_t *dst = smem + NO_RING + s * N_STAGE_BYTES;
+                    st::mbar_arrive_expect_tx(&rfull[s], cb + sb);
+                    st::bulk_load(dst, g.codes + tb * 64, cb, &rfull[s]);
+                    st::bulk_load(dst + N_CODE_BYTES, reinterpret_cast<const void *>(s0), sb, &rfull[s]);
+                }
+            }
+            // copies still in flight land before the CTA's shared memory goes away
+            const uint32_t first = gt > N_STAGES ? gt - N_STAGES : 0;
+            for (uint32_t i = first; i < gt; i++)
+                st::mbar_wait(&rfull[i % N_STAGES], (i / N_STAGES) & 1u, g.status, st::DEV_TIMEOUT_FULL);
+        }
+    } else if (warp >= N_EPI && warp < N_MMA_WARP) {
+        // ------------------------------------------------------------ producers
+        const int pw = warp - N_EPI;  // 0..7
+        const int quad = warp & 3, half = pw >> 2;
+        // queries: warp pw prepares queries pw, pw + 8, ..; lane l writes bytes
+        // 8l .. 8l + 7 of every limb row (K chunk l / 16) of the first nqp
+        for (int r = pw; r < NQ; r += N_PROD) {
+            const bool live = r < g.nq;
+            const float *qrow = g.q + static_cast<int64_t>(live ? r : 0) * 256;
+            float m = 0.0f;
+            for (int i = lane; i < 256; i += 32) m = fmaxf(m, live ? fabsf(__ldg(qrow + i)) : 0.0f);
+            m = warp_max(m);
+            const int e = query_exp(m);
+            const float sc = pow2f(e + EB);  // |X| < 2^(8 NL - 2)
+            uint32_t lw[NL][2];
+            int lsum[NL], labs[NL];
+#pragma unroll
+            for (int l = 0; l < NL; l++) {
+                lw[l][0] = lw[l][1] = 0u;
+                lsum[l] = labs[l] = 0;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int dim = narrow_dim(8 * lane + i);
+                int x = __float2int_rn((live ? __ldg(qrow + dim) : 0.0f) * sc);
+#pragma unroll
+                for (int l = 0; l < NL; l++) {
+                    int limb;
+                    if (l < NL - 1) {
+                        limb = ((x + 128) & 255) - 128;  // balanced digit in [-128, 127]
+                        x = (x - limb) >> 8;
+                    } else {
+                        limb = x;  // |top limb| <= 64
+                    }
+                    lw[l][i >> 2] |= (static_cast<uint32_t>(limb) & 255u) << (8 * (i & 3));
+                    lsum[l] += limb;
+                    labs[l] += abs(limb);
+                }
+            }
+#pragma unroll
+            for (int l = 0; l < NL; l++) {
+                lsum[l] = warp_sum(lsum[l]);
+                labs[l] = warp_sum(labs[l]);
+                if (r < nqp) {
+                    const int row = l * nqp + r;
+                    const uint32_t off =
+                        (lane >> 4) * NQ_CHUNK + st::sw128_offset(row, (lane & 15) >> 1) + 8 * (lane & 1);
+                    *reinterpret_cast<uint2 *>(smem + NO_Q + off) = make_uint2(lw[l][0], lw[l][1]);
+                }
+            }
+            if (lane == 0) {
+                // S = sum_l 2^8l (A_l - C_l);  v = 2^8 (1.5 2^23 + A_top) + 1.5 2^23 + A_next
+                // (rounded by at most 128) and S <= 2^(8 (NL - 2)) (v - K) + R
+                float K = 257.0f * MAGIC_F, R = 0.0f;
+                for (int l = 0; l < NL; l++) {
+                    const float C = 1.5f * static_cast<float>(lsum[l]);
+                    qc_C[l * NQ + r] = C;
+                    if (l == NL - 1) K += 256.0f * C;
+                    else if (l == NL - 2) K += C;
+                    else R += 1.5f * static_cast<float>(labs[l]) * pow2f(8 * l);
+                }
+                float P, qf;
+                if (MODE == MODE_DOT) {
+                    P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(-e - EB);
+                    qf = 0.0f;
+                } else {
+                    P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(1 - e - EB);
+                    qf = PREC == PREC_EXACT ? pow2f(e - 1) : 1.0f;
+                }
+                // v and the filter's right-hand side round by at most 128 each, and
+                // K (about 3.2e9) by at most 256
+                qc_c[r] = live ? K - R * SH - 768.0f : INFINITY;
+                qc_ql[r] = lowered(qf / P * SH);
+                qc_P[r] = P;
+                qc_qf[r] = qf;
+            }
+        }
+        st::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) st::mbar_arrive(qready);
+
+        uint32_t gt = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+            int64_t tb;
+            int nk;
+            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                const uint32_t s = gt % N_STAGES, b = gt % N_A, f = gt % N_KF;
+                if (!nwait(&rfull[s], (gt / N_STAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *stage = smem + NO_RING + s * N_STAGE_BYTES;
+                const int sofs = static_cast<int>((reinterpret_cast<uintptr_t>(g.scales + tb) & 15u) >> 2);
+                uint4 cw[2];
+                int key[2];
+                float scl[2], nrm[2];
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const int j = 2 * half + jj;
+                    key[jj] = 32 * quad + 8 * j + (lane >> 2);
+                    const bool in = key[jj] < nk;
+                    cw[jj] = in ? *reinterpret_cast<const uint4 *>(stage + 2048 * quad + 512 * j + 16 * lane)
+                                : make_uint4(0u, 0u, 0u, 0u);
+                    scl[jj] = in ? reinterpret_cast<const float *>(stage + N_CODE_BYTES)[sofs + key[jj]] : 0.0f;
+                    int c3 = 0;  // codes u in {0, 3}: the two bits are equal
+                    if (MODE == MODE_L2) {
+                        const uint32_t w[4] = {cw[jj].x, cw[jj].y, cw[jj].z, cw[jj].w};
+#pragma unroll
+                        for (int t = 0; t < 4; t++) c3 += __popc(~(w[t] ^ (w[t] >> 1)) & 0x55555555u);
+                        c3 += __shfl_xor_sync(0xffffffffu, c3, 1);
+                        c3 += __shfl_xor_sync(0xffffffffu, c3, 2);
+                    }
+                    if (PREC == PREC_EXACT) {
+                        nrm[jj] = scl[jj] * scl[jj] * static_cast<float>(64 + 2 * c3);
+                    } else {
+                        const float h1 = __half2float(__float2half_rn(0.5f * scl[jj]));
+                        const float h3 = __half2float(__float2half_rn(1.5f * scl[jj]));
+                        nrm[jj] = static_cast<float>(256 - c3) * (h1 * h1) + static_cast<float>(c3) * (h3 * h3);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&rempty[s]);  // the stage's bytes are in registers
+                // A buffer b is free once the MMAs of tile gt - 4 are done.  Slot
+                // f = gt % 8 is then free too: those MMAs started only after the
+                // epilogue released the accumulator of tile gt - 6, so it is done
+                // with every tile up to gt - 6, and slot f last held tile gt - 8.
+                if (gt >= N_A &&
+                    !nwait(&aempty[b], ((gt / N_A) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                if ((lane & 3) == 0) {
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        kf[f * NK + key[jj]] = scl[jj];
+                        kn[f * NK + key[jj]] = nrm[jj];
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&kfr[f]);
+                // codes -> bytes: register 4r + {0,1} belongs to key j = 2 half
+                // (lane base + lane / 4), 4r + {2,3} to key j + 1 (lane base + 8 + lane / 4)
+                uint32_t v[32];
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const uint32_t w[4] = {cw[jj].x, cw[jj].y, cw[jj].z, cw[jj].w};
+#pragma unroll
+                    for (int m = 0; m < 4; m++)
+#pragma unroll
+                        for (int s2 = 0; s2 < 4; s2++)
+                            v[4 * (2 * m + (s2 >> 1)) + 2 * jj + (s2 & 1)] = (w[m] >> (2 * s2)) & 0x03030303u;
+                }
+                const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quad + 16 * half) << 16) + b * 64u;
+                tmem_st_16x256b_x8(taddr, v);
+                st::tmem_st_wait();
+                st::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&afull[b]);
+            }
+        }
+    } else if (warp == N_MMA_WARP) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            // kind::i8: D s32, A unsigned 8-bit, B signed 8-bit, M = 128
+            const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NL * nqp >> 3) << 17) |
+                                   (static_cast<uint32_t>(NK >> 4) << 24);
+            bool ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
+            st::tc_fence_after();
+            const uint32_t qb = st::smem_u32(smem + NO_Q);
+            uint32_t gt = 0;
+            for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+                int64_t tb;
+                int nk;
+                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                    const uint32_t b = gt % N_A, a = gt % N_ACC;
+                    if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL) ||
+                        (gt >= N_ACC &&
+                         !nwait(&acce[a], ((gt / N_ACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY))) {
+                        ok = false;
+                        break;
+                    }
+                    st::tc_fence_after();
+                    const uint32_t acc = tmem + N_ACC_COL + a * N_ACC_COLS, abuf = tmem + b * 64u;
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t boff = (kk >> 2) * NQ_CHUNK + (kk & 3) * 32;
+                        umma_i8_ts(acc, abuf + 8 * kk, st::sdesc_sw128(qb + boff, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                    }
+                    st::umma_commit(&aempty[b]);
+                    st::umma_commit(&accf[a]);
+                }
+            }
+            // every MMA issued above completes before the TMEM is released
+            st::umma_commit(fin);
+            nwait(fin, 0, abort_flag, g.status, st::DEV_TIMEOUT_ACC);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp;  // TMEM lanes 32 quad ..: keys 32 quad + lane of every tile
+        const unsigned lt = (1u << lane) - 1u;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
+        uint64_t *bufs = g.cbuf + (static_cast<int64_t>(blockIdx.x) * N_EPI + warp) * NQ * KCAP;
+        uint64_t *my_buf = bufs + static_cast<int64_t>(lane) * KCAP;  // lane = query of this buffer
+        float *slot = reinterpret_cast<float *>(smem + NO_SLOT) + threadIdx.x;  // slot[q * 128]
+        float *wthr = thr_s + warp * NQ, *wthrl = thr_l + warp * NQ;
+        const bool qlive = lane < g.nq;
+        bool ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
+        uint32_t gt = 0;
+        const int top = (NL - 1) * nqp, next = (NL - 2) * nqp;
+        for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+            int cnt = 0;
+            float thr = qlive ? -INFINITY : INFINITY;  // this list's 128th best
+            float eff = thr;                           // the best 128th any list has published
+            wthr[lane] = eff;
+            wthrl[lane] = eff;
+            __syncwarp();
+            int64_t tb;
+            int nk;
+            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                const uint32_t a = gt % N_ACC, f = gt % N_KF;
+                // the published thresholds, read now and merged after this tile
+                uint32_t pub = 0u;
+                if (qlive && (gt & 3u) == 0u) pub = *reinterpret_cast<volatile uint32_t *>(g.gthr + lane);
+                if (!nwait(&accf[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
+                    !nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+                    ok = false;
+                    break;
+                }
+                st::tc_fence_after();
+                const uint32_t acc = tmem + lane_addr + N_ACC_COL + a * N_ACC_COLS;
+                uint32_t rt[32], rn[32];
+                st::tmem_ld32(acc + top, rt);
+                st::tmem_ld32(acc + next, rn);
+                const int kk = 32 * quad + lane;
+                const float scale = kf[f * NK + kk];
+                const float nrm = kn[f * NK + kk];
+                st::tmem_ld_wait();
+                const bool klive = kk < nk;
+                const float inv_s = rcp_approx(scale);
+                bool any = false;
+#pragma unroll
+                for (int q4 = 0; q4 < NQ; q4 += 4) {
+                    const float4 cc = *reinterpret_cast<const float4 *>(qc_c + q4);
+                    const float4 th = *reinterpret_cast<const float4 *>(wthrl + q4);
+                    const float ca[4] = {cc.x, cc.y, cc.z, cc.w}, tha[4] = {th.x, th.y, th.z, th.w};
+                    float qla[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (MODE == MODE_L2) {
+                        const float4 ql = *reinterpret_cast<const float4 *>(qc_ql + q4);
+                        qla[0] = ql.x; qla[1] = ql.y; qla[2] = ql.z; qla[3] = ql.w;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float v = fmaf(__uint_as_float(rt[q4 + i] + MAGIC_I), 256.0f,
+                                             __uint_as_float(rn[q4 + i] + MAGIC_I));
+                        const float t = MODE == MODE_L2 ? fmaf(nrm, qla[i], tha[i]) : tha[i];
+                        any |= v >= fmaf(t, inv_s, ca[i]);
+                    }
+                }
+                any = any && klive;
+                if (__any_sync(0xffffffffu, any)) {
+                    // the exact path: S = sum_l 2^8l (A_l - C_l) from every limb, top
+                    // down, the partial sums kept in this thread's score slots
+                    float *sl = slot;
+                    if (any) {
+#pragma unroll
+                        for (int q = 0; q < NQ; q++)
+                            sl[q * (N_EPI * 32)] =
+                                fmaf(__uint_as_float(rt[q] + MAGIC_I) - MAGIC_F - qc_C[(NL - 1) * NQ + q], 256.0f,
+                                     __uint_as_float(rn[q] + MAGIC_I) - MAGIC_F - qc_C[(NL - 2) * NQ + q]);
+                    }
+#pragma unroll 1
+                    for (int l = NL - 3; l >= 0; l--) {
+                        st::tmem_ld32(acc + l * nqp, rt);
+                        st::tmem_ld_wait();
+                        if (any) {
+#pragma unroll
+                            for (int q = 0; q < NQ; q++)
+                                sl[q * (N_EPI * 32)] =
+                                    fmaf(sl[q * (N_EPI * 32)], 256.0f,
+                                         __uint_as_float(rt[q] + MAGIC_I) - MAGIC_F - qc_C[l * NQ + q]);
+                        }
+                    }
+                    uint32_t pass = 0;
+                    if (any) {
+#pragma unroll
+                        for (int q = 0; q < NQ; q++) {
+                            float sc = sl[q * (N_EPI * 32)] * scale * qc_P[q];
+                            if (MODE == MODE_L2) sc = fmaf(-nrm, qc_qf[q], sc);
+                            sl[q * (N_EPI * 32)] = sc;
+                            pass |= (sc >= wthr[q] ? 1u : 0u) << q;
+                        }
+                    }
+                    unsigned qm = __reduce_or_sync(0xffffffffu, pass);
+                    const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
+                    while (qm) {
+                        const int q = __ffs(qm) - 1;
+                        qm &= qm - 1;
+                        const bool p = (pass >> q) & 1u;
+                        const unsigned m = __ballot_sync(0xffffffffu, p);
+                        const int base = __shfl_sync(0xffffffffu, cnt, q);
+                        if (p)
+                            bufs[static_cast<int64_t>(q) * KCAP + base + __popc(m & lt)] =
+                                make_key(slot[q * (N_EPI * 32)], idx);
+                        if (lane == q) cnt += __popc(m);
+                    }
+                }
+                st::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&acce[a]);
+                const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - NK / 4);
+                if (need) {
+                    const float before = thr;
+                    warp_compact(need, my_buf, cnt, thr, nullptr, false);
+                    if (thr > before) atomicMax(g.gthr + lane, ord_f32(thr));
+                }
+                const float ne = fmaxf(fmaxf(thr, thr_of(pub)), eff);
+                if (__any_sync(0xffffffffu, ne > eff)) {
+                    if (qlive) {
+                        eff = ne;
+                        wthr[lane] = eff;
+                        wthrl[lane] = lowered(eff / qc_P[lane] * SH);
+                    }
+                    __syncwarp();
+                }
+            }
+            if (!ok) break;
+            uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(unit) * N_EPI + warp) * NQ + lane) * KTOP;
+            const unsigned need = __ballot_sync(0xffffffffu, qlive);
+            warp_compact(need, my_buf, cnt, thr, my_out, true);
+        }
+    }
+
+    st::tc_fence_before();
+    __syncthreads();
+    if (warp == N_MMA_WARP) {
+        st::tc_fence_after();
+        st::tmem_dealloc(tmem, N_TMEM_COLS);
+    }
+}
+
+// gthr[q] = the score bits of the 128th best key of keys[q] (0 when the list
+// holds fewer): a lower bound for query q's final 128th best, since the keys
+// behind it are a subset of the keys scanned.
+__global__ void k_knn_seed(const uint64_t *keys, int nq, uint32_t *gthr) {
+    const int q = threadIdx.x;
+    if (q < nq) gthr[q] = static_cast<uint32_t>(keys[static_cast<int64_t>(q) * KTOP + KTOP - 1] >> 32);
+}
+
+template <int MODE, int PREC>
+st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
+    auto kern = k_knn_narrow<MODE, PREC>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, NARROW_SMEM));
+        attr_done = true;
+    }
+    kern<<<grid, N_THREADS, NARROW_SMEM, h->stream>>>(g);
+    return st_after_launch(h, "k_knn_narrow");
+}
+
 }  // namespace
 
 static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
@@ -934,6 +1544,75 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (s != ST_OK) return s;
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
+    if (!ranges && dim == 256 && nq <= NQ && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
+        // a few queries: the narrow scan (keys on the MMA's M side), one pass
+        const int64_t tiles = (n_keys + NK - 1) / NK;
+        int64_t splits = std::min<int64_t>(tiles, h->num_sms);
+        const int64_t tps = (tiles + splits - 1) / splits;
+        splits = (tiles + tps - 1) / tps;
+        const int grid = static_cast<int>(splits);
+        uint64_t *cbuf = static_cast<uint64_t *>(
+            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_EPI * NQ * KCAP));
+        const size_t out_bytes = sizeof(uint64_t) * splits * N_EPI * NQ * KTOP;
+        const size_t seed_bytes = sizeof(uint64_t) * NQ * KTOP;
+        uint8_t *part = static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + 256));
+        if (!cbuf || !part) return ST_NO_MEMORY;
+        uint64_t *unit_out = reinterpret_cast<uint64_t *>(part);
+        uint64_t *seed_keys = reinterpret_cast<uint64_t *>(part + out_bytes);
+        uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes);
+        ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, NQ * sizeof(uint32_t), h->stream));
+        // queries per limb block: a multiple of 8 with (limbs x it) a multiple of 16
+        const int nqp = prec == 0 ? static_cast<int>((nq + 3) / 4 * 4) : static_cast<int>((nq + 15) / 16 * 16);
+        NarrowArgs g{};
+        g.codes = codes;
+        g.scales = scales;
+        g.q = queries;
+        g.n_keys = n_keys;
+        g.nq = static_cast<int>(nq);
+        g.nqp = std::max(nqp, 8);
+        g.n_tiles = tiles;
+        g.index_base = static_cast<uint32_t>(index_base);
+        g.cbuf = cbuf;
+        g.unit_out = unit_out;
+        g.gthr = gthr;
+        g.status = h->d_status;
+        auto run = [&](const NarrowArgs &a, int gr) {
+            if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT>(h, a, gr);
+            if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF>(h, a, gr);
+            if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT>(h, a, gr);
+            return launch_narrow<MODE_L2, PREC_F16REF>(h, a, gr);
+        };
+        // Large scans first take every 64th tile: the best 128 of that sample
+        // bound each query's final 128th best from below, and every list of the
+        // full scan starts from it instead of from its own first keys.
+        constexpr int64_t SEED_STRIDE = 64;
+        const int64_t sample = (tiles + SEED_STRIDE - 1) / SEED_STRIDE;
+        if (sample >= 2 * h->num_sms) {
+            NarrowArgs gs = g;
+            const int gsplits = h->num_sms;
+            gs.splits = gsplits;
+            gs.unit_step = SEED_STRIDE;
+            gs.tile_step = SEED_STRIDE * gsplits;
+            gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
+            s = run(gs, gsplits);
+            if (s != ST_OK) return s;
+            k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, gsplits * N_EPI, NQ * KTOP,
+                                                                        seed_keys);
+            s = st_after_launch(h, "k_knn_merge");
+            if (s != ST_OK) return s;
+            k_knn_seed<<<1, 32, 0, h->stream>>>(seed_keys, static_cast<int>(nq), gthr);
+            s = st_after_launch(h, "k_knn_seed");
+            if (s != ST_OK) return s;
+        }
+        g.splits = static_cast<int>(splits);
+        g.unit_step = tps;
+        g.tile_step = 1;
+        g.tiles_per_unit = tps;
+        s = run(g, grid);
+        if (s != ST_OK) return s;
+        k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, splits * N_EPI, NQ * KTOP, out_keys);
+        return st_after_launch(h, "k_knn_merge");
+    }
     const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
     const int64_t tiles = (n_keys + KT - 1) / KT;
     // about eight units per SM, every split non-empty

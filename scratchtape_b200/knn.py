@@ -304,7 +304,51 @@ class KnnStore:
         from .memfile import write_mem
         self.finish()
         write_mem(path, key, extra, self.d, self.tile, self.codes.cpu().numpy(), self.scales.cpu().numpy(),
-                  self.norms.cpu().numpy(), self.vals.cpu().numpy().astype(np.float32))
+                  self.norms.cpu().numpy(), self.vals.cpu().numpy().astype(np.float32), ivf=self._ivf_section())
+
+    def _ivf_section(self):
+        """The IVF part of a .mem file (cache.rs:54-70): centroids as f16
+        rows padded to a multiple of 16, their squared norms, and each cell
+        as pieces (tile, a, b, g0) -- rows a..b of tile ``tile``, which are
+        store rows g0.. (ivf.rs:37-43, 451-460).  None without an IVF."""
+        iv = getattr(self, "ivf", None)
+        if iv is None or self.first != 0:
+            return None
+        nl = iv["nlist"]
+        cent = iv["cent"].cpu().numpy().astype(np.float16)
+        pad = np.zeros(((nl + 15) // 16 * 16, self.d), np.float16)
+        pad[:nl] = cent
+        cells = []
+        for c in range(nl):
+            a, b = int(iv["starts"][c]), int(iv["starts"][c + 1])
+            pieces = []
+            for t in range(a // self.tile, (b + self.tile - 1) // self.tile):
+                lo, hi = max(a, t * self.tile), min(b, (t + 1) * self.tile)
+                if lo < hi:
+                    pieces.append((t, lo - t * self.tile, hi - t * self.tile, lo))
+            cells.append(pieces)
+        return {"nlist": nl, "n": int(iv["starts"][-1]), "keys": pad.tobytes(), "norm": iv["cnorm"].cpu().numpy(),
+                "cells": cells}
+
+    def _restore_ivf(self, raw):
+        """Rebuilds the device IVF from a file's IVF section when its cells are
+        consecutive store ranges in cell order (what build_ivf writes, and the
+        reference's build_ivf too, ivf.rs:385-447); otherwise leaves it out."""
+        nl, d = int(raw["nlist"]), self.d
+        starts = np.zeros(nl + 1, np.int64)
+        pos = 0
+        for c, cell in enumerate(raw["cells"]):
+            for (t, a, b, g0) in cell:
+                if g0 != pos or t * self.tile + a != g0 or b < a:
+                    return
+                pos += b - a
+            starts[c + 1] = pos
+        if pos != raw["n"] or pos > len(self) or len(raw["keys"]) < nl * d * 2 or len(raw["norm"]) < nl:
+            return
+        cent = np.frombuffer(raw["keys"], np.float16)[:nl * d].reshape(nl, d).astype(np.float32)
+        self.ivf = {"cent": torch.from_numpy(cent).to(self.device),
+                    "cnorm": torch.from_numpy(np.asarray(raw["norm"][:nl], np.float32).copy()).to(self.device),
+                    "starts": starts, "nlist": nl}
 
     @staticmethod
     def load(path, key: str, device=None, rows=None):
@@ -343,7 +387,9 @@ class KnnStore:
             store.norms = torch.cat([p[1][2] for p in parts])
             store.vals = torch.cat([p[1][3] for p in parts]).to(torch.int32)
         store.first = meta["first"]
-        store.ivf_raw = meta["ivf"]  # kept for a later IVF search; flat scans ignore it
+        store.ivf_raw = meta["ivf"]
+        if meta["ivf"] is not None and rows is None:
+            store._restore_ivf(meta["ivf"])  # a shard keeps only the raw section
         return store, meta["extra"]
 
     def build_ivf(self, nlist: int, iters: int = 10, sample: Optional[int] = None):
@@ -379,6 +425,9 @@ class KnnStore:
                     cent[c] = sums[c] / counts[c]
                 else:
                     cent[c] = xs_h[(c * 7919 + it * 104729) % ns]
+        # the final centroids are rounded to f16, as the reference keeps them
+        # (ivf.rs:433-434), so a store saved and loaded probes the same cells
+        cent = cent.astype(np.float16).astype(np.float64)
         c_dev = torch.from_numpy(cent.astype(np.float32)).to(self.device)
         cnorm = torch.from_numpy(np.square(cent).sum(1).astype(np.float32)).to(self.device)
         cell = torch.empty(n, dtype=torch.int32, device=self.device)

@@ -100,3 +100,36 @@ def test_ivf_section_round_trips(tmp_path):
     meta, _ = _collect(p, "k")
     assert meta["ivf"]["nlist"] == 2 and meta["ivf"]["keys"] == ivf["keys"]
     assert meta["ivf"]["cells"] == ivf["cells"]
+
+
+def test_store_ivf_section_restores_cells(tmp_path):
+    """KnnStore's IVF section: cells written as per-tile pieces of consecutive
+    store ranges (ivf.rs:451-460) come back as the same cell starts, f16
+    centroids and norms; a section whose cells are not consecutive is left
+    out rather than misread."""
+    import torch
+    from scratchtape_b200.knn import KnnStore
+    from scratchtape_b200.memfile import read_mem, write_mem
+    d, tile, n, nl = 64, 32, 100, 5
+    codes, scales, norms, vals = _data(n, d, 4)
+    st = KnnStore(d, tile=tile, device="cpu")
+    st.codes, st.scales = torch.from_numpy(codes), torch.from_numpy(scales)
+    starts = np.array([0, 7, 40, 40, 71, 100], np.int64)
+    cent = np.random.default_rng(1).standard_normal((nl, d)).astype(np.float16).astype(np.float32)
+    st.ivf = {"cent": torch.from_numpy(cent), "cnorm": torch.from_numpy((cent * cent).sum(1)), "starts": starts,
+              "nlist": nl}
+    sec = st._ivf_section()
+    assert sec["cells"][1] == [(0, 7, 32, 7), (1, 0, 8, 32)] and sec["cells"][2] == []
+    p = tmp_path / "m.mem"
+    write_mem(p, "k", 0, d, tile, codes, scales, norms, vals, ivf=sec)
+    raw = read_mem(p, "k")["ivf"]
+    st2 = KnnStore(d, tile=tile, device="cpu")
+    st2.codes, st2.scales = st.codes, st.scales
+    st2._restore_ivf(raw)
+    assert np.array_equal(st2.ivf["starts"], starts)
+    assert torch.equal(st2.ivf["cent"], st.ivf["cent"]) and torch.equal(st2.ivf["cnorm"], st.ivf["cnorm"])
+    raw["cells"][1] = [(1, 0, 8, 32), (0, 7, 32, 7)]  # out of order: not a consecutive range
+    st3 = KnnStore(d, tile=tile, device="cpu")
+    st3.codes, st3.scales = st.codes, st.scales
+    st3._restore_ivf(raw)
+    assert getattr(st3, "ivf", None) is None
