@@ -620,12 +620,22 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
 // lists[l * list_stride + q * KTOP + r], sorted best first (0 = empty).
 // One 256-thread CTA per query: an exact 8-bit-digit radix select of the
 // KTOP-th largest key, a gather of the keys at or above it, a rank sort.
+// With gridDim.y = G > 1, block (q, y) merges only lists y * ceil(n/G) .. and
+// writes its best KTOP to out[(y * gridDim.x + q) * KTOP]: the first stage of a
+// two-stage merge whose second stage merges those G lists.
 __global__ void __launch_bounds__(256) k_knn_merge(const uint64_t *lists, int64_t n_lists, int64_t list_stride,
                                                    uint64_t *out) {
     __shared__ int hist[256];
     __shared__ uint64_t sel[KTOP];
     __shared__ int s_digit, s_need, s_count;
     const int64_t q = blockIdx.x;
+    if (gridDim.y > 1) {
+        const int64_t per = (n_lists + gridDim.y - 1) / gridDim.y;
+        const int64_t l0 = blockIdx.y * per;
+        n_lists = l0 < n_lists ? (n_lists - l0 < per ? n_lists - l0 : per) : 0;
+        lists += l0 * list_stride;
+        out += static_cast<int64_t>(blockIdx.y) * gridDim.x * KTOP;
+    }
     const int64_t total = n_lists * KTOP;
     auto at = [&](int64_t i) { return __ldg(lists + (i / KTOP) * list_stride + q * KTOP + (i % KTOP)); };
     uint64_t prefix = 0, mask = 0;
@@ -939,20 +949,21 @@ __global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst,
 //   A_l = sum_i u_i limb_l,i     and     S = sum_l 2^8l (A_l - C_l) = sum_i (u_i - 1.5) X_i,
 // with C_l = 1.5 sum_i limb_l,i, so the only rounding is the query's to 8 NL - 2
 // bits (EXACT: NL = 4; F16REF: NL = 3, still finer than the reference's f16).
-// Roles (448 threads, one CTA per SM, one key split per CTA):
-//   warp 13 (one thread): bulk-copies each 128-key tile's codes (8 KB) and the
+// Roles (576 threads, one CTA per SM, one key split per CTA):
+//   warp 17 (one thread): bulk-copies each 128-key tile's codes (8 KB) and the
 //     16-byte blocks holding its scales into a 12-stage shared-memory ring.
-//   warps 4-11 (producers; warp w writes TMEM lanes 32 (w % 4) + 16 (w / 8)..):
+//   warps 8-15 (producers; warp w writes TMEM lanes 32 (w % 4) + 16 (w / 12)..):
 //     spread the codes into bytes -- (word >> 2s) & 0x03030303 puts codes s,
 //     s + 4, s + 8, s + 12 of a 16-code word into one 32-bit word -- and store
 //     them with tcgen05.st (16x256b: a warp's 512 contiguous code bytes map onto
 //     16 TMEM lanes without shuffles); the queries' K order follows that
 //     permutation of the dimensions.
-//   warp 12 (one thread): tcgen05.mma kind::i8, A = keys (u8, TMEM), B = limbs
+//   warp 16 (one thread): tcgen05.mma kind::i8, A = keys (u8, TMEM), B = limbs
 //     (s8, shared memory), D = s32, N = NL * NQP columns; two accumulators.
-//   warps 0-3 (epilogue; warp w reads TMEM lanes 32 w..): thread = key.  A
-//     limb column plus 0x4B400000, viewed as a float, is 1.5 2^23 + A_l
-//     exactly (|A_l| < 2^17); the two top limbs
+//   warps 0-7 (epilogue; warp w reads TMEM lanes 32 (w % 4).. and the columns
+//     of queries 16 (w / 4)..): thread = key.  The accumulators start at
+//     0x4B400000 (written back after each use), so the float view of a limb
+//     column is 1.5 2^23 + A_l exactly (|A_l| < 2^17); the two top limbs
 //     bound S within +-R (R from the per-query sums of |limb|), and one FMA,
 //     one FMA and a compare per (key, query) test the key against the query's
 //     running 128th-best score with every term lowered -- never rejecting a
@@ -970,23 +981,25 @@ constexpr int NK = 128;                                 // keys per tile (MMA M,
 constexpr int N_STAGES = 12;                            // code / scale ring
 constexpr int N_CODE_BYTES = NK * 64;                   // dim 256: 64 code bytes per key
 constexpr int N_STAGE_BYTES = N_CODE_BYTES + NK * 4 + 16;  // scales from the 16-byte block of the first
-constexpr int N_A = 4;                                  // TMEM A buffers, 64 columns each
-constexpr int N_ACC = 2;                                // TMEM accumulators, 128 columns each
+constexpr int N_A = 2;                                  // TMEM A buffers, 64 columns each
+constexpr int N_ACC = 3;                                // TMEM accumulators, 128 columns each
 constexpr int N_ACC_COLS = 128;
 constexpr int N_KF = 8;                                 // per-key factor slots (lifetime: see the producer)
-constexpr int N_EPI = 4, N_PROD = 8;
-constexpr int N_MMA_WARP = N_EPI + N_PROD;              // 12
-constexpr int N_TMA_WARP = N_MMA_WARP + 1;              // 13
-constexpr int N_THREADS = 32 * (N_TMA_WARP + 1);        // 448
+constexpr int N_QUAD = 4;                               // TMEM lane quadrants: one candidate list per query each
+constexpr int N_EPI = 8, N_PROD = 8;                    // epilogue warp w: quadrant w % 4, queries 16 (w / 4) ..
+constexpr int EQ = NQ / 2;                              // queries per epilogue warp
+constexpr int N_MMA_WARP = N_EPI + N_PROD;              // 16
+constexpr int N_TMA_WARP = N_MMA_WARP + 1;              // 17
+constexpr int N_THREADS = 32 * (N_TMA_WARP + 1);        // 576
 constexpr int NO_Q = 0;                                 // B: [2 K chunks][128 rows x 128 B], SW128
 constexpr int NQ_CHUNK = 128 * 128;
 constexpr int NO_RING = NO_Q + 2 * NQ_CHUNK;
 constexpr int NO_KF = NO_RING + N_STAGES * N_STAGE_BYTES;  // [N_KF][128] scale
 constexpr int NO_KN = NO_KF + N_KF * NK * 4;               // [N_KF][128] |k|^2 (L2)
 constexpr int NO_QC = NO_KN + N_KF * NK * 4;               // [8][32] per-query constants
-constexpr int NO_THR = NO_QC + 8 * NQ * 4;                 // [2][4 warps][32] thresholds
-constexpr int NO_SLOT = NO_THR + 2 * N_EPI * NQ * 4;       // [32 queries][128 threads] exact scores
-constexpr int NO_BAR = NO_SLOT + N_EPI * 32 * NQ * 4;
+constexpr int NO_THR = NO_QC + 8 * NQ * 4;                 // [2][4 quadrants][32] thresholds
+constexpr int NO_SLOT = NO_THR + 2 * N_QUAD * NQ * 4;      // [16 queries][256 threads] exact scores
+constexpr int NO_BAR = NO_SLOT + EQ * N_EPI * 32 * 4;
 constexpr int N_NBARS = 2 * N_STAGES + 2 * N_A + 2 * N_ACC + N_KF + 2;
 constexpr int NO_MISC = NO_BAR + N_NBARS * 8;              // tmem slot, abort flag
 constexpr int NARROW_SMEM = NO_MISC + 16 + 1024;
@@ -1007,7 +1020,7 @@ struct NarrowArgs {
     // unit u scans 128-key tiles u * unit_step + i * tile_step, i < tiles_per_unit, below n_tiles
     int64_t n_tiles, unit_step, tile_step, tiles_per_unit;
     uint32_t index_base;
-    uint64_t *cbuf;        // [gridDim.x][4 warps][32 queries][KCAP]
+    uint64_t *cbuf;        // [gridDim.x][4 quadrants][32 queries][KCAP]
     uint64_t *unit_out;    // [splits * 4][32][KTOP]
     uint32_t *gthr;        // [32] order-preserving bits of the best published 128th score (0: none)
     int *status;
@@ -1044,6 +1057,15 @@ __device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_
         : "memory");
 }
 
+// Stores one 32-bit value into 16 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
+
 __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
     asm volatile(
@@ -1057,18 +1079,20 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
 __device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
 
 // kwait for the narrow scan's hand-offs, which come every few hundred
-// nanoseconds: polls without a suspend hint (a woken sleeper would add its
-// wake-up latency to every tile), still bounded by the time limit and the
-// CTA's abort flag.
+// nanoseconds: spins on the non-blocking test (a suspended or sleeping waiter
+// would add its wake-up latency to every tile), still bounded by the time
+// limit and the CTA's abort flag.
 __device__ __forceinline__ bool nwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
                                       int code) {
-    if (st::mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = st::globaltimer();
+    if (st::mbar_test_wait(bar, parity)) return true;
+    // the bound counts SM cycles (the SM's own counter, cheap to read):
+    // 8e9 cycles is at least the 2 s limit at any clock up to 4 GHz
+    const long long t0 = clock64();
     for (uint32_t i = 1;; ++i) {
-        if (st::mbar_try_wait(bar, parity)) return true;
+        if (st::mbar_test_wait(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (*abort_flag) return false;
-            if (st::globaltimer() - t0 > st::WAIT_LIMIT_NS) {
+            if (clock64() - t0 > 8000000000ll) {
                 *abort_flag = 1;
                 st::set_status(status, code);
                 return false;
@@ -1076,6 +1100,7 @@ __device__ __forceinline__ bool nwait(uint64_t *bar, uint32_t parity, volatile i
         }
     }
 }
+
 
 // Tile i of unit `unit`: its first key tb and key count nk; false past the unit's end.
 __device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64_t i, int64_t &tb, int &nk) {
@@ -1103,7 +1128,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
     float *qc_qf = qc + 3 * NQ;
     float *qc_C = qc + 4 * NQ;   // [4][32]: C_l
     float *thr_s = reinterpret_cast<float *>(smem + NO_THR);  // [4][32] effective 128th-best score
-    float *thr_l = thr_s + N_EPI * NQ;                        // [4][32] the same / P * SH, lowered
+    float *thr_l = thr_s + N_QUAD * NQ;                       // [4][32] the same / P * SH, lowered
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NO_BAR);
     uint64_t *rfull = bars, *rempty = bars + N_STAGES, *afull = bars + 2 * N_STAGES, *aempty = afull + N_A;
     uint64_t *accf = aempty + N_A, *acce = accf + N_ACC, *kfr = acce + N_ACC, *qready = kfr + N_KF, *fin = qready + 1;
@@ -1124,7 +1149,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
         }
         for (int a = 0; a < N_ACC; a++) {
             st::mbar_init(&accf[a], 1);
-            st::mbar_init(&acce[a], N_EPI);
+            st::mbar_init(&acce[a], nqp > EQ ? N_EPI : N_EPI / 2);  // the warps that have queries
         }
         for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
         st::mbar_init(qready, N_PROD);
@@ -1175,7 +1200,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
         }
     } else if (warp >= N_EPI && warp < N_MMA_WARP) {
         // ------------------------------------------------------------ producers
-        const int pw = warp - N_EPI;  // 0..7
+        const int pw = warp - N_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
         const int quad = warp & 3, half = pw >> 2;
         // queries: warp pw prepares queries pw, pw + 8, ..; lane l writes bytes
         // 8l .. 8l + 7 of every limb row (K chunk l / 16) of the first nqp
@@ -1296,10 +1321,10 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 }
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&rempty[s]);  // the stage's bytes are in registers
-                // A buffer b is free once the MMAs of tile gt - 4 are done.  Slot
+                // A buffer b is free once the MMAs of tile gt - 2 are done.  Slot
                 // f = gt % 8 is then free too: those MMAs started only after the
-                // epilogue released the accumulator of tile gt - 6, so it is done
-                // with every tile up to gt - 6, and slot f last held tile gt - 8.
+                // epilogue released the accumulator of tile gt - 5, so it is done
+                // with every tile up to gt - 5, and slot f last held tile gt - 8.
                 if (gt >= N_A &&
                     !nwait(&aempty[b], ((gt / N_A) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
                     ok = false;
@@ -1349,9 +1374,9 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 int nk;
                 for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
                     const uint32_t b = gt % N_A, a = gt % N_ACC;
+                    // acce's first phase is the epilogue's initial fill of the accumulators
                     if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL) ||
-                        (gt >= N_ACC &&
-                         !nwait(&acce[a], ((gt / N_ACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY))) {
+                        !nwait(&acce[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
@@ -1360,7 +1385,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
                         const uint32_t boff = (kk >> 2) * NQ_CHUNK + (kk & 3) * 32;
-                        umma_i8_ts(acc, abuf + 8 * kk, st::sdesc_sw128(qb + boff, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                        umma_i8_ts(acc, abuf + 8 * kk, st::sdesc_sw128(qb + boff, 16, 1024), idesc, 1u);
                     }
                     st::umma_commit(&aempty[b]);
                     st::umma_commit(&accf[a]);
@@ -1372,41 +1397,66 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int quad = warp;  // TMEM lanes 32 quad ..: keys 32 quad + lane of every tile
+        // Warp w reads TMEM lanes 32 (w % 4) .. (keys 32 (w % 4) + lane of every
+        // tile) and the columns of queries q0 = 16 (w / 4) .. q0 + 15; lane l < 16
+        // owns the candidate buffer, count and thresholds of query q0 + l for its
+        // quadrant.
+        const int quad = warp & 3, q0 = EQ * (warp >> 2);
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
-        uint64_t *bufs = g.cbuf + (static_cast<int64_t>(blockIdx.x) * N_EPI + warp) * NQ * KCAP;
-        uint64_t *my_buf = bufs + static_cast<int64_t>(lane) * KCAP;  // lane = query of this buffer
-        float *slot = reinterpret_cast<float *>(smem + NO_SLOT) + threadIdx.x;  // slot[q * 128]
-        float *wthr = thr_s + warp * NQ, *wthrl = thr_l + warp * NQ;
-        const bool qlive = lane < g.nq;
-        bool ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
+        uint64_t *bufs = g.cbuf + (static_cast<int64_t>(blockIdx.x) * N_QUAD + quad) * NQ * KCAP;
+        uint64_t *my_buf = bufs + static_cast<int64_t>(q0 + (lane & (EQ - 1))) * KCAP;
+        float *slot = reinterpret_cast<float *>(smem + NO_SLOT) + threadIdx.x;  // slot[i * 256]: query q0 + i
+        float *wthr = thr_s + quad * NQ, *wthrl = thr_l + quad * NQ;
+        const bool qlive = lane < EQ && q0 + lane < g.nq;
+        const uint32_t acc0 = tmem + lane_addr + N_ACC_COL;
+        // the columns this warp reads -- limb l, queries q0.. -- start at the magic
+        // value, and are put back to it after each tile, so the MMA accumulates onto it
+        auto refill = [&](uint32_t acc) {
+#pragma unroll
+            for (int l = 0; l < NL; l++) tmem_fill16(acc + l * nqp + q0, static_cast<uint32_t>(MAGIC_I));
+            st::tmem_st_wait();
+        };
+        bool ok = q0 < nqp;  // with 16 queries per limb block the second warp of each quadrant has none
+        if (ok) {
+            for (int a = 0; a < N_ACC; a++) refill(acc0 + a * N_ACC_COLS);
+            st::tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                for (int a = 0; a < N_ACC; a++) st::mbar_arrive(&acce[a]);
+            ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
+        }
         uint32_t gt = 0;
-        const int top = (NL - 1) * nqp, next = (NL - 2) * nqp;
+        const int top = (NL - 1) * nqp + q0, next = (NL - 2) * nqp + q0;
         for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
             int cnt = 0;
             float thr = qlive ? -INFINITY : INFINITY;  // this list's 128th best
             float eff = thr;                           // the best 128th any list has published
-            wthr[lane] = eff;
-            wthrl[lane] = eff;
+            uint32_t pub = 0u, pub_next = 0u;          // published thresholds, read one tile ahead of use
+            if (lane < EQ) {
+                wthr[q0 + lane] = eff;
+                wthrl[q0 + lane] = eff;
+            }
             __syncwarp();
             int64_t tb;
             int nk;
             for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
                 const uint32_t a = gt % N_ACC, f = gt % N_KF;
-                // the published thresholds, read now and merged after this tile
-                uint32_t pub = 0u;
-                if (qlive && (gt & 3u) == 0u) pub = *reinterpret_cast<volatile uint32_t *>(g.gthr + lane);
+                // the published thresholds: read now, merged after the next tile (the
+                // read's latency stays off this tile's path)
+                pub = pub_next;
+                pub_next = 0u;
+                if (qlive && (gt & 3u) == 0u) pub_next = *reinterpret_cast<volatile uint32_t *>(g.gthr + q0 + lane);
                 if (!nwait(&accf[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
                     !nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                     ok = false;
                     break;
                 }
                 st::tc_fence_after();
-                const uint32_t acc = tmem + lane_addr + N_ACC_COL + a * N_ACC_COLS;
-                uint32_t rt[32], rn[32];
-                st::tmem_ld32(acc + top, rt);
-                st::tmem_ld32(acc + next, rn);
+                const uint32_t acc = acc0 + a * N_ACC_COLS;
+                uint32_t rt[EQ], rn[EQ];
+                st::tmem_ld16(acc + top, rt);
+                st::tmem_ld16(acc + next, rn);
                 const int kk = 32 * quad + lane;
                 const float scale = kf[f * NK + kk];
                 const float nrm = kn[f * NK + kk];
@@ -1415,19 +1465,18 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 const float inv_s = rcp_approx(scale);
                 bool any = false;
 #pragma unroll
-                for (int q4 = 0; q4 < NQ; q4 += 4) {
-                    const float4 cc = *reinterpret_cast<const float4 *>(qc_c + q4);
-                    const float4 th = *reinterpret_cast<const float4 *>(wthrl + q4);
+                for (int q4 = 0; q4 < EQ; q4 += 4) {
+                    const float4 cc = *reinterpret_cast<const float4 *>(qc_c + q0 + q4);
+                    const float4 th = *reinterpret_cast<const float4 *>(wthrl + q0 + q4);
                     const float ca[4] = {cc.x, cc.y, cc.z, cc.w}, tha[4] = {th.x, th.y, th.z, th.w};
                     float qla[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                     if (MODE == MODE_L2) {
-                        const float4 ql = *reinterpret_cast<const float4 *>(qc_ql + q4);
+                        const float4 ql = *reinterpret_cast<const float4 *>(qc_ql + q0 + q4);
                         qla[0] = ql.x; qla[1] = ql.y; qla[2] = ql.z; qla[3] = ql.w;
                     }
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        const float v = fmaf(__uint_as_float(rt[q4 + i] + MAGIC_I), 256.0f,
-                                             __uint_as_float(rn[q4 + i] + MAGIC_I));
+                        const float v = fmaf(__uint_as_float(rt[q4 + i]), 256.0f, __uint_as_float(rn[q4 + i]));
                         const float t = MODE == MODE_L2 ? fmaf(nrm, qla[i], tha[i]) : tha[i];
                         any |= v >= fmaf(t, inv_s, ca[i]);
                     }
@@ -1439,47 +1488,48 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                     float *sl = slot;
                     if (any) {
 #pragma unroll
-                        for (int q = 0; q < NQ; q++)
-                            sl[q * (N_EPI * 32)] =
-                                fmaf(__uint_as_float(rt[q] + MAGIC_I) - MAGIC_F - qc_C[(NL - 1) * NQ + q], 256.0f,
-                                     __uint_as_float(rn[q] + MAGIC_I) - MAGIC_F - qc_C[(NL - 2) * NQ + q]);
+                        for (int i = 0; i < EQ; i++)
+                            sl[i * (N_EPI * 32)] =
+                                fmaf(__uint_as_float(rt[i]) - MAGIC_F - qc_C[(NL - 1) * NQ + q0 + i], 256.0f,
+                                     __uint_as_float(rn[i]) - MAGIC_F - qc_C[(NL - 2) * NQ + q0 + i]);
                     }
 #pragma unroll 1
                     for (int l = NL - 3; l >= 0; l--) {
-                        st::tmem_ld32(acc + l * nqp, rt);
+                        st::tmem_ld16(acc + l * nqp + q0, rt);
                         st::tmem_ld_wait();
                         if (any) {
 #pragma unroll
-                            for (int q = 0; q < NQ; q++)
-                                sl[q * (N_EPI * 32)] =
-                                    fmaf(sl[q * (N_EPI * 32)], 256.0f,
-                                         __uint_as_float(rt[q] + MAGIC_I) - MAGIC_F - qc_C[l * NQ + q]);
+                            for (int i = 0; i < EQ; i++)
+                                sl[i * (N_EPI * 32)] =
+                                    fmaf(sl[i * (N_EPI * 32)], 256.0f,
+                                         __uint_as_float(rt[i]) - MAGIC_F - qc_C[l * NQ + q0 + i]);
                         }
                     }
                     uint32_t pass = 0;
                     if (any) {
 #pragma unroll
-                        for (int q = 0; q < NQ; q++) {
-                            float sc = sl[q * (N_EPI * 32)] * scale * qc_P[q];
-                            if (MODE == MODE_L2) sc = fmaf(-nrm, qc_qf[q], sc);
-                            sl[q * (N_EPI * 32)] = sc;
-                            pass |= (sc >= wthr[q] ? 1u : 0u) << q;
+                        for (int i = 0; i < EQ; i++) {
+                            float sc = sl[i * (N_EPI * 32)] * scale * qc_P[q0 + i];
+                            if (MODE == MODE_L2) sc = fmaf(-nrm, qc_qf[q0 + i], sc);
+                            sl[i * (N_EPI * 32)] = sc;
+                            pass |= (sc >= wthr[q0 + i] ? 1u : 0u) << i;
                         }
                     }
                     unsigned qm = __reduce_or_sync(0xffffffffu, pass);
                     const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
                     while (qm) {
-                        const int q = __ffs(qm) - 1;
+                        const int i = __ffs(qm) - 1;
                         qm &= qm - 1;
-                        const bool p = (pass >> q) & 1u;
+                        const bool p = (pass >> i) & 1u;
                         const unsigned m = __ballot_sync(0xffffffffu, p);
-                        const int base = __shfl_sync(0xffffffffu, cnt, q);
+                        const int base = __shfl_sync(0xffffffffu, cnt, i);
                         if (p)
-                            bufs[static_cast<int64_t>(q) * KCAP + base + __popc(m & lt)] =
-                                make_key(slot[q * (N_EPI * 32)], idx);
-                        if (lane == q) cnt += __popc(m);
+                            bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(m & lt)] =
+                                make_key(slot[i * (N_EPI * 32)], idx);
+                        if (lane == i) cnt += __popc(m);
                     }
                 }
+                refill(acc);
                 st::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&acce[a]);
@@ -1487,20 +1537,21 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 if (need) {
                     const float before = thr;
                     warp_compact(need, my_buf, cnt, thr, nullptr, false);
-                    if (thr > before) atomicMax(g.gthr + lane, ord_f32(thr));
+                    if (thr > before) atomicMax(g.gthr + q0 + lane, ord_f32(thr));
                 }
                 const float ne = fmaxf(fmaxf(thr, thr_of(pub)), eff);
                 if (__any_sync(0xffffffffu, ne > eff)) {
                     if (qlive) {
                         eff = ne;
-                        wthr[lane] = eff;
-                        wthrl[lane] = lowered(eff / qc_P[lane] * SH);
+                        wthr[q0 + lane] = eff;
+                        wthrl[q0 + lane] = lowered(eff / qc_P[q0 + lane] * SH);
                     }
                     __syncwarp();
                 }
             }
             if (!ok) break;
-            uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(unit) * N_EPI + warp) * NQ + lane) * KTOP;
+            uint64_t *my_out =
+                g.unit_out + ((static_cast<int64_t>(unit) * N_QUAD + quad) * NQ + q0 + (lane & (EQ - 1))) * KTOP;
             const unsigned need = __ballot_sync(0xffffffffu, qlive);
             warp_compact(need, my_buf, cnt, thr, my_out, true);
         }
@@ -1520,6 +1571,24 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
 __global__ void k_knn_seed(const uint64_t *keys, int nq, uint32_t *gthr) {
     const int q = threadIdx.x;
     if (q < nq) gthr[q] = static_cast<uint32_t>(keys[static_cast<int64_t>(q) * KTOP + KTOP - 1] >> 32);
+}
+
+// Best KTOP per query over n_lists lists (stride list_stride) into out, in two
+// stages when the lists are many: G groups in parallel into tmp [G][nq][KTOP],
+// then one merge of the G partial lists.
+st_status merge_lists(st_handle *h, const uint64_t *lists, int64_t n_lists, int64_t list_stride, int64_t nq,
+                      uint64_t *tmp, int groups, uint64_t *out) {
+    if (n_lists > 2 * groups && tmp) {
+        k_knn_merge<<<dim3(static_cast<unsigned>(nq), static_cast<unsigned>(groups)), 256, 0, h->stream>>>(
+            lists, n_lists, list_stride, tmp);
+        st_status s = st_after_launch(h, "k_knn_merge");
+        if (s != ST_OK) return s;
+        lists = tmp;
+        n_lists = groups;
+        list_stride = nq * KTOP;
+    }
+    k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(lists, n_lists, list_stride, out);
+    return st_after_launch(h, "k_knn_merge");
 }
 
 template <int MODE, int PREC>
@@ -1552,24 +1621,29 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         splits = (tiles + tps - 1) / tps;
         const int grid = static_cast<int>(splits);
         uint64_t *cbuf = static_cast<uint64_t *>(
-            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_EPI * NQ * KCAP));
-        const size_t out_bytes = sizeof(uint64_t) * splits * N_EPI * NQ * KTOP;
+            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_QUAD * NQ * KCAP));
+        const size_t out_bytes = sizeof(uint64_t) * splits * N_QUAD * NQ * KTOP;
         const size_t seed_bytes = sizeof(uint64_t) * NQ * KTOP;
-        uint8_t *part = static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + 256));
+        constexpr int MERGE_GROUPS = 16;
+        const size_t tmp_bytes = sizeof(uint64_t) * MERGE_GROUPS * NQ * KTOP;
+        uint8_t *part =
+            static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + tmp_bytes + 256));
         if (!cbuf || !part) return ST_NO_MEMORY;
         uint64_t *unit_out = reinterpret_cast<uint64_t *>(part);
         uint64_t *seed_keys = reinterpret_cast<uint64_t *>(part + out_bytes);
-        uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes);
+        uint64_t *merge_tmp = reinterpret_cast<uint64_t *>(part + out_bytes + seed_bytes);
+        uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes + tmp_bytes);
         ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, NQ * sizeof(uint32_t), h->stream));
         // queries per limb block: a multiple of 8 with (limbs x it) a multiple of 16
-        const int nqp = prec == 0 ? static_cast<int>((nq + 3) / 4 * 4) : static_cast<int>((nq + 15) / 16 * 16);
+        // queries per limb block: 16 or 32 (an epilogue warp takes 16; NL x 16 is a multiple of 16)
+        const int nqp = nq <= EQ ? EQ : NQ;
         NarrowArgs g{};
         g.codes = codes;
         g.scales = scales;
         g.q = queries;
         g.n_keys = n_keys;
         g.nq = static_cast<int>(nq);
-        g.nqp = std::max(nqp, 8);
+        g.nqp = nqp;
         g.n_tiles = tiles;
         g.index_base = static_cast<uint32_t>(index_base);
         g.cbuf = cbuf;
@@ -1582,23 +1656,23 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
             if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT>(h, a, gr);
             return launch_narrow<MODE_L2, PREC_F16REF>(h, a, gr);
         };
-        // Large scans first take every 64th tile: the best 128 of that sample
+        // Large scans first take a sample of the tiles: the best 128 of a sample
         // bound each query's final 128th best from below, and every list of the
-        // full scan starts from it instead of from its own first keys.
-        constexpr int64_t SEED_STRIDE = 64;
-        const int64_t sample = (tiles + SEED_STRIDE - 1) / SEED_STRIDE;
-        if (sample >= 2 * h->num_sms) {
+        // next pass starts from it instead of from its own first keys.  Two
+        // levels: every 1024th tile seeds a pass over every 16th, which seeds the
+        // full scan.
+        for (int64_t stride : {int64_t(1024), int64_t(16)}) {
+            const int64_t sample = (tiles + stride - 1) / stride;
+            if (sample < 2 * h->num_sms) continue;
             NarrowArgs gs = g;
             const int gsplits = h->num_sms;
             gs.splits = gsplits;
-            gs.unit_step = SEED_STRIDE;
-            gs.tile_step = SEED_STRIDE * gsplits;
+            gs.unit_step = stride;
+            gs.tile_step = stride * gsplits;
             gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
             s = run(gs, gsplits);
             if (s != ST_OK) return s;
-            k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, gsplits * N_EPI, NQ * KTOP,
-                                                                        seed_keys);
-            s = st_after_launch(h, "k_knn_merge");
+            s = merge_lists(h, unit_out, gsplits * N_QUAD, NQ * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
             if (s != ST_OK) return s;
             k_knn_seed<<<1, 32, 0, h->stream>>>(seed_keys, static_cast<int>(nq), gthr);
             s = st_after_launch(h, "k_knn_seed");
@@ -1610,8 +1684,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.tiles_per_unit = tps;
         s = run(g, grid);
         if (s != ST_OK) return s;
-        k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, splits * N_EPI, NQ * KTOP, out_keys);
-        return st_after_launch(h, "k_knn_merge");
+        return merge_lists(h, unit_out, splits * N_QUAD, NQ * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
     }
     const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
     const int64_t tiles = (n_keys + KT - 1) / KT;
