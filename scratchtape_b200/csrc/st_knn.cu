@@ -1079,17 +1079,18 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
 __device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
 
 // kwait for the narrow scan's hand-offs, which come every few hundred
-// nanoseconds: spins on the non-blocking test (a suspended or sleeping waiter
-// would add its wake-up latency to every tile), still bounded by the time
-// limit and the CTA's abort flag.
+// nanoseconds: try_wait without a sleep hint (the hardware parks the thread
+// until the phase completes, so waiting warps take no issue slots from the
+// working ones, and wakes it at once), still bounded by the time limit and
+// the CTA's abort flag.
 __device__ __forceinline__ bool nwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
                                       int code) {
-    if (st::mbar_test_wait(bar, parity)) return true;
+    if (st::mbar_try_wait(bar, parity)) return true;
     // the bound counts SM cycles (the SM's own counter, cheap to read):
     // 8e9 cycles is at least the 2 s limit at any clock up to 4 GHz
     const long long t0 = clock64();
     for (uint32_t i = 1;; ++i) {
-        if (st::mbar_test_wait(bar, parity)) return true;
+        if (st::mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0) {
             if (*abort_flag) return false;
             if (clock64() - t0 > 8000000000ll) {
