@@ -605,7 +605,8 @@ def run_ours_c5(args):
                   "hbm_gbs": bytes32 / (ms32 / 1e3) / 1e9, "hbm_frac": bytes32 / (ms32 / 1e3) / 1e9 /
                   float(peaks["hbm_gbs"]),
                   "note": "the narrow scan (k_knn_narrow: 128 keys per MMA in TMEM, queries as 4 int8 limbs, "
-                          "exact integer products) seeded by a 1-in-64 tile sample pass, + k_knn_merge"}
+                          "exact integer products), seeded by 1-in-1024 and 1-in-16 tile sample passes, + a "
+                          "two-stage k_knn_merge; bytes = codes + scales + queries of one full pass"}
 
     flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
     achieved = flops_alg / (scan_ms / 1e3) / 1e12
