@@ -961,9 +961,9 @@ __global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst,
 //   warp 16 (one thread): tcgen05.mma kind::i8, A = keys (u8, TMEM), B = limbs
 //     (s8, shared memory), D = s32, N = NL * NQP columns; two accumulators.
 //   warps 0-7 (epilogue; warp w reads TMEM lanes 32 (w % 4).. and the columns
-//     of queries 16 (w / 4)..): thread = key.  The accumulators start at
-//     0x4B400000 (written back after each use), so the float view of a limb
-//     column is 1.5 2^23 + A_l exactly (|A_l| < 2^17); the two top limbs
+//     of queries 16 (w / 4)..): thread = key.  A limb column plus 0x4B400000,
+//     viewed as a float, is 1.5 2^23 + A_l exactly (|A_l| < 2^17); the accumulator
+//     goes back to the MMA as soon as its last column is read; the two top limbs
 //     bound S within +-R (R from the per-query sums of |limb|), and one FMA,
 //     one FMA and a compare per (key, query) test the key against the query's
 //     running 128th-best score with every term lowered -- never rejecting a
@@ -1054,15 +1054,6 @@ __device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-        : "memory");
-}
-
-// Stores one 32-bit value into 16 consecutive TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1};" ::"r"(taddr),
-        "r"(v)
         : "memory");
 }
 
@@ -1369,25 +1360,25 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
             bool ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
             st::tc_fence_after();
             const uint32_t qb = st::smem_u32(smem + NO_Q);
+            uint64_t bdesc[8];  // the queries' descriptors do not change from tile to tile
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) bdesc[kk] = st::sdesc_sw128(qb + (kk >> 2) * NQ_CHUNK + (kk & 3) * 32, 16, 1024);
             uint32_t gt = 0;
             for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
                 int64_t tb;
                 int nk;
                 for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
                     const uint32_t b = gt % N_A, a = gt % N_ACC;
-                    // acce's first phase is the epilogue's initial fill of the accumulators
                     if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL) ||
-                        !nwait(&acce[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                        (gt >= N_ACC &&
+                         !nwait(&acce[a], ((gt / N_ACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY))) {
                         ok = false;
                         break;
                     }
                     st::tc_fence_after();
                     const uint32_t acc = tmem + N_ACC_COL + a * N_ACC_COLS, abuf = tmem + b * 64u;
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t boff = (kk >> 2) * NQ_CHUNK + (kk & 3) * 32;
-                        umma_i8_ts(acc, abuf + 8 * kk, st::sdesc_sw128(qb + boff, 16, 1024), idesc, 1u);
-                    }
+                    for (int kk = 0; kk < 8; kk++) umma_i8_ts(acc, abuf + 8 * kk, bdesc[kk], idesc, kk > 0 ? 1u : 0u);
                     st::umma_commit(&aempty[b]);
                     st::umma_commit(&accf[a]);
                 }
@@ -1411,22 +1402,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
         float *wthr = thr_s + quad * NQ, *wthrl = thr_l + quad * NQ;
         const bool qlive = lane < EQ && q0 + lane < g.nq;
         const uint32_t acc0 = tmem + lane_addr + N_ACC_COL;
-        // the columns this warp reads -- limb l, queries q0.. -- start at the magic
-        // value, and are put back to it after each tile, so the MMA accumulates onto it
-        auto refill = [&](uint32_t acc) {
-#pragma unroll
-            for (int l = 0; l < NL; l++) tmem_fill16(acc + l * nqp + q0, static_cast<uint32_t>(MAGIC_I));
-            st::tmem_st_wait();
-        };
         bool ok = q0 < nqp;  // with 16 queries per limb block the second warp of each quadrant has none
-        if (ok) {
-            for (int a = 0; a < N_ACC; a++) refill(acc0 + a * N_ACC_COLS);
-            st::tc_fence_before();
-            __syncwarp();
-            if (lane == 0)
-                for (int a = 0; a < N_ACC; a++) st::mbar_arrive(&acce[a]);
-            ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
-        }
+        if (ok) ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
         uint32_t gt = 0;
         const int top = (NL - 1) * nqp + q0, next = (NL - 2) * nqp + q0;
         for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
@@ -1447,7 +1424,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 // read's latency stays off this tile's path)
                 pub = pub_next;
                 pub_next = 0u;
-                if (qlive && (gt & 3u) == 0u) pub_next = *reinterpret_cast<volatile uint32_t *>(g.gthr + q0 + lane);
+                if (qlive && (gt & 15u) == 0u) pub_next = __ldcg(g.gthr + q0 + lane);
                 if (!nwait(&accf[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
                     !nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                     ok = false;
@@ -1477,13 +1454,20 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                     }
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        const float v = fmaf(__uint_as_float(rt[q4 + i]), 256.0f, __uint_as_float(rn[q4 + i]));
+                        const float v = fmaf(__uint_as_float(rt[q4 + i] + MAGIC_I), 256.0f,
+                                             __uint_as_float(rn[q4 + i] + MAGIC_I));
                         const float t = MODE == MODE_L2 ? fmaf(nrm, qla[i], tha[i]) : tha[i];
                         any |= v >= fmaf(t, inv_s, ca[i]);
                     }
                 }
                 any = any && klive;
-                if (__any_sync(0xffffffffu, any)) {
+                const bool slow = __any_sync(0xffffffffu, any);
+                if (!slow) {  // nothing more to read: the accumulator goes back to the MMA now
+                    st::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) st::mbar_arrive(&acce[a]);
+                }
+                if (slow) {
                     // the exact path: S = sum_l 2^8l (A_l - C_l) from every limb, top
                     // down, the partial sums kept in this thread's score slots
                     float *sl = slot;
@@ -1491,8 +1475,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
 #pragma unroll
                         for (int i = 0; i < EQ; i++)
                             sl[i * (N_EPI * 32)] =
-                                fmaf(__uint_as_float(rt[i]) - MAGIC_F - qc_C[(NL - 1) * NQ + q0 + i], 256.0f,
-                                     __uint_as_float(rn[i]) - MAGIC_F - qc_C[(NL - 2) * NQ + q0 + i]);
+                                fmaf(__uint_as_float(rt[i] + MAGIC_I) - MAGIC_F - qc_C[(NL - 1) * NQ + q0 + i], 256.0f,
+                                     __uint_as_float(rn[i] + MAGIC_I) - MAGIC_F - qc_C[(NL - 2) * NQ + q0 + i]);
                     }
 #pragma unroll 1
                     for (int l = NL - 3; l >= 0; l--) {
@@ -1503,9 +1487,12 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                             for (int i = 0; i < EQ; i++)
                                 sl[i * (N_EPI * 32)] =
                                     fmaf(sl[i * (N_EPI * 32)], 256.0f,
-                                         __uint_as_float(rt[i]) - MAGIC_F - qc_C[l * NQ + q0 + i]);
+                                         __uint_as_float(rt[i] + MAGIC_I) - MAGIC_F - qc_C[l * NQ + q0 + i]);
                         }
                     }
+                    st::tc_fence_before();  // every limb is read: release the accumulator
+                    __syncwarp();
+                    if (lane == 0) st::mbar_arrive(&acce[a]);
                     uint32_t pass = 0;
                     if (any) {
 #pragma unroll
@@ -1530,10 +1517,6 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                         if (lane == i) cnt += __popc(m);
                     }
                 }
-                refill(acc);
-                st::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) st::mbar_arrive(&acce[a]);
                 const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - NK / 4);
                 if (need) {
                     const float before = thr;
