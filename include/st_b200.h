@@ -49,8 +49,13 @@ typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2 } st_dtype;
 /* Arithmetic of st_gemm.
  * F32_EXACT: SIMT, each output a k-ascending sequence of f32 multiply then
  *            add from 0 -- bit-identical to NdArray::matmul (src/tensor.rs:248-276).
- * TF32:      tcgen05 kind::tf32 tensor cores, f32 accumulate in TMEM. */
-typedef enum { ST_PREC_F32_EXACT = 0, ST_PREC_TF32 = 1 } st_precision;
+ * TF32:      tcgen05 kind::tf32 tensor cores, f32 accumulate in TMEM.
+ * F16:       a and b in f16 (ST_F16) or bf16 (ST_BF16), both the same; tcgen05
+ *            kind::f16, f32 accumulate and an f32 out -- the reference's f16 x
+ *            f16 -> f32 matrix-core path (k_matmul_cmma, src/gpu_step/matmul.rs:632-880).
+ *            No col_sum; operands must be TMA-describable (16-byte aligned
+ *            starts and row strides). */
+typedef enum { ST_PREC_F32_EXACT = 0, ST_PREC_TF32 = 1, ST_PREC_F16 = 2 } st_precision;
 
 typedef struct st_handle st_handle;
 

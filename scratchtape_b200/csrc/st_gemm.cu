@@ -26,9 +26,11 @@ constexpr int BM = 128;
 constexpr int BK = 32;  // f32 elements per k block = one 128-byte swizzle row
 
 struct Operand {  // element (z, r, c) of a logical [rows, cols] matrix
-    const float *ptr;
+    const float *ptr;  // element type: f32, or f16 / bf16 (esize 2; only TMA reads those)
     int64_t off, stride, inner, ld;
     int grp, trans;
+    int esize = 4;
+    CUtensorMapDataType tdt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
 };
 
 struct GemmArgs {
@@ -368,12 +370,19 @@ __device__ __forceinline__ void epilogue_scalar(const GemmArgs &g, uint8_t *smem
     }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 2)
-    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmM,
-                const __grid_constant__ CUtensorMap tmR, const GemmArgs g) {
+// One CTA of the tensor-core GEMM.  AB: operand type -- 0 f32 (kind::tf32,
+// 32 elements per 128-byte k row), 1 f16 / 2 bf16 (kind::f16, 64 elements per
+// k row).  A k block is one 128-byte swizzled row per tile row either way, so
+// the stage layout, the four MMAs per k block and the K-major descriptors are
+// shared; MN-major 16-bit tiles are 64-element (128-byte) rows along MN, k in
+// rows, 64-wide MN atoms one 64-row TMA box (8 KB) apart.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int AB>
+__device__ __forceinline__ void gemm_cta(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmC,
+                                         const CUtensorMap &tmM, const CUtensorMap &tmR, const GemmArgs &g) {
     using C = Cfg<BN, STAGES>;
+    constexpr int BKE = AB ? 64 : BK;      // elements per k block
+    constexpr int MNW = AB ? 64 : 32;      // MN-major box width (elements)
+    constexpr int MNBOX = MNW * BKE * (AB ? 2 : 4);  // bytes of one MN-major box
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
@@ -385,7 +394,7 @@ __global__ void __launch_bounds__(192, 2)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int z = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
-    const int kb_total = (g.K + BK - 1) / BK;
+    const int kb_total = (g.K + BKE - 1) / BKE;
     const int kb_begin = split * g.kb_per_split;
     const int nkb = max(0, min(kb_total, kb_begin + g.kb_per_split) - kb_begin);
 
@@ -421,26 +430,28 @@ __global__ void __launch_bounds__(192, 2)
                 if (i >= STAGES && !st::mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, g.status, st::DEV_TIMEOUT_EMPTY))
                     break;
                 st::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-                const int kc = (kb_begin + i) * BK;
+                const int kc = (kb_begin + i) * BKE;
                 uint8_t *sa = smem + s * C::STAGE_BYTES;
                 uint8_t *sb = sa + C::A_BYTES;
                 if (!A_MN) {
                     st::tma_load_4d(sa, &tmA, &full[s], kc, m0, ca2, ca3);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < BM / 32; j++) st::tma_load_4d(sa + j * 4096, &tmA, &full[s], m0 + 32 * j, kc, ca2, ca3);
+                    for (int j = 0; j < BM / MNW; j++)
+                        st::tma_load_4d(sa + j * MNBOX, &tmA, &full[s], m0 + MNW * j, kc, ca2, ca3);
                 }
                 if (!B_MN) {
                     st::tma_load_4d(sb, &tmB, &full[s], kc, n0, cb2, cb3);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < BN / 32; j++) st::tma_load_4d(sb + j * 4096, &tmB, &full[s], n0 + 32 * j, kc, cb2, cb3);
+                    for (int j = 0; j < BN / MNW; j++)
+                        st::tma_load_4d(sb + j * MNBOX, &tmB, &full[s], n0 + MNW * j, kc, cb2, cb3);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t idesc = st::idesc_make(1, 2, A_MN, B_MN, BM, BN);
+            constexpr uint32_t idesc = st::idesc_make(1, AB ? AB - 1 : 2, A_MN, B_MN, BM, BN);
             for (int i = 0; i < nkb; i++) {
                 const int s = i % STAGES;
                 if (!st::mbar_wait(&full[s], (i / STAGES) & 1, g.status, st::DEV_TIMEOUT_FULL)) break;
@@ -448,17 +459,28 @@ __global__ void __launch_bounds__(192, 2)
                 const uint32_t sa = st::smem_u32(smem + s * C::STAGE_BYTES);
                 const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 8; kk++) {
-                    // K-major (128B swizzle): advance 32 bytes (8 tf32) along the
-                    // swizzled row; 8-row groups 1024 bytes apart.
-                    // MN-major (128B swizzle on a 32B base): advance 8 k rows
+                for (int kk = 0; kk < 4; kk++) {
+                    // K-major (128B swizzle): advance 32 bytes (8 tf32 or 16
+                    // f16) along the swizzled row; 8-row groups 1024 bytes apart.
+                    // MN-major tf32 (128B swizzle on a 32B base): advance 8 k rows
                     // (1024 bytes); 4-row atoms 512 bytes apart; 32-wide MN
                     // chunks (one TMA box each) 4096 bytes apart.
-                    const uint64_t ad = A_MN ? st::sdesc_make(sa + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
-                                             : st::sdesc_sw128(sa + kk * 32, 16, 1024);
-                    const uint64_t bd = B_MN ? st::sdesc_make(sb + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
-                                             : st::sdesc_sw128(sb + kk * 32, 16, 1024);
-                    st::umma_tf32(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    // MN-major 16-bit (128B swizzle): advance 16 k rows (2048
+                    // bytes); 8-row atoms 1024 bytes apart; 64-wide MN chunks 8 KB apart.
+                    uint64_t ad, bd;
+                    if (AB) {
+                        ad = A_MN ? st::sdesc_make(sa + kk * 2048, MNBOX, 1024, st::LAYOUT_SW128)
+                                  : st::sdesc_sw128(sa + kk * 32, 16, 1024);
+                        bd = B_MN ? st::sdesc_make(sb + kk * 2048, MNBOX, 1024, st::LAYOUT_SW128)
+                                  : st::sdesc_sw128(sb + kk * 32, 16, 1024);
+                        st::umma_f16(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        ad = A_MN ? st::sdesc_make(sa + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
+                                  : st::sdesc_sw128(sa + kk * 32, 16, 1024);
+                        bd = B_MN ? st::sdesc_make(sb + kk * 1024, 4096, 512, st::LAYOUT_SW128_BASE32B)
+                                  : st::sdesc_sw128(sb + kk * 32, 16, 1024);
+                        st::umma_tf32(tmem, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 st::umma_commit(&empty[s]);
             }
@@ -492,6 +514,23 @@ __global__ void __launch_bounds__(192, 2)
         st::tc_fence_after();
         st::tmem_dealloc(tmem, C::TMEM_COLS);
     }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 2)
+    k_gemm_tf32(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmM,
+                const __grid_constant__ CUtensorMap tmR, const GemmArgs g) {
+    gemm_cta<BN, STAGES, A_MN, B_MN, 0>(tmA, tmB, tmC, tmM, tmR, g);
+}
+
+// The same CTA on f16 (AB 1) or bf16 (AB 2) operands: kind::f16, f32 accumulate.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int AB>
+__global__ void __launch_bounds__(192, 2)
+    k_gemm_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmM,
+               const __grid_constant__ CUtensorMap tmR, const GemmArgs g) {
+    gemm_cta<BN, STAGES, A_MN, B_MN, AB>(tmA, tmB, tmC, tmM, tmR, g);
 }
 
 // Sums split-k partials in split order, then applies the epilogue.  Thread
@@ -748,11 +787,11 @@ st_status launch_pdl(st_handle *h, K kern, dim3 grid, dim3 block, Args... args) 
     return ST_OK;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int AB>
 st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc,
                       const CUtensorMap &mm, const CUtensorMap &mr, const GemmArgs &g, dim3 grid) {
     using C = Cfg<BN, STAGES>;
-    auto kern = k_gemm_tf32<BN, STAGES, A_MN, B_MN>;
+    auto kern = AB ? k_gemm_f16<BN, STAGES, A_MN, B_MN, AB> : k_gemm_tf32<BN, STAGES, A_MN, B_MN>;
     static bool attr_done = false;  // per instantiation
     if (!attr_done) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
@@ -769,17 +808,17 @@ st_status launch_tf32(st_handle *h, const CUtensorMap &ma, const CUtensorMap &mb
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mm, mr, g));
-    return st_after_launch(h, "k_gemm_tf32");
+    return st_after_launch(h, AB ? "k_gemm_f16" : "k_gemm_tf32");
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int AB = 0>
 st_status dispatch_tf32(st_handle *h, bool a_mn, bool b_mn, const CUtensorMap &ma, const CUtensorMap &mb,
                         const CUtensorMap &mc, const CUtensorMap &mm, const CUtensorMap &mr, const GemmArgs &g,
                         dim3 grid) {
-    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false>(h, ma, mb, mc, mm, mr, g, grid);
-    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true>(h, ma, mb, mc, mm, mr, g, grid);
-    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false>(h, ma, mb, mc, mm, mr, g, grid);
-    return launch_tf32<BN, STAGES, true, true>(h, ma, mb, mc, mm, mr, g, grid);
+    if (!a_mn && !b_mn) return launch_tf32<BN, STAGES, false, false, AB>(h, ma, mb, mc, mm, mr, g, grid);
+    if (!a_mn && b_mn) return launch_tf32<BN, STAGES, false, true, AB>(h, ma, mb, mc, mm, mr, g, grid);
+    if (a_mn && !b_mn) return launch_tf32<BN, STAGES, true, false, AB>(h, ma, mb, mc, mm, mr, g, grid);
+    return launch_tf32<BN, STAGES, true, true, AB>(h, ma, mb, mc, mm, mr, g, grid);
 }
 
 Operand to_operand(const st_mat *m, int64_t packed_ld) {
@@ -791,20 +830,24 @@ Operand to_operand(const st_mat *m, int64_t packed_ld) {
     o.ld = m->ld ? m->ld : packed_ld;
     o.grp = m->group > 0 ? m->group : 1;
     o.trans = m->trans;
+    o.esize = m->dtype == ST_F32 ? 4 : 2;
+    o.tdt = m->dtype == ST_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+            : m->dtype == ST_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     return o;
 }
 
 // Tensor map for an operand stored as [srows, scols] (scols contiguous).
 bool operand_map(CUtensorMap *map, const Operand &o, int64_t batch, int64_t srows, int64_t scols, uint32_t box_cols,
                  uint32_t box_rows, CUtensorMapSwizzle swz, std::string *why) {
-    const float *base = o.ptr + o.off;
+    const void *base = reinterpret_cast<const char *>(o.ptr) + o.off * o.esize;
     const int64_t outer = (o.stride != 0) ? (batch + o.grp - 1) / o.grp : 1;
     const int64_t grp = o.grp > 1 ? std::min<int64_t>(o.grp, batch) : 1;
     const uint64_t filler = static_cast<uint64_t>(o.ld) * srows;  // any valid stride for extent-1 dims
     const uint64_t inner = grp > 1 ? static_cast<uint64_t>(o.inner) : filler;
     const uint64_t stride = o.stride != 0 ? static_cast<uint64_t>(o.stride) : filler;
-    return st_make_map_4d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, scols, srows, grp, outer, o.ld, inner, stride,
-                          box_cols, box_rows, swz, why);
+    return st_make_map_4d(map, o.tdt, o.esize, base, scols, srows, grp, outer, o.ld, inner, stride, box_cols, box_rows,
+                          swz, why);
 }
 
 }  // namespace
@@ -819,11 +862,18 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         return h->fail(ST_INVALID_ARG, "st_gemm: bad shape batch=%lld m=%lld k=%lld n=%lld", (long long)batch,
                        (long long)m, (long long)k, (long long)n);
     if (out->trans) return h->fail(ST_INVALID_ARG, "st_gemm: out must be stored row-major (trans = 0)");
-    if (a->dtype != ST_F32 || b->dtype != ST_F32 || out->dtype != ST_F32)
-        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: operands must be f32");
+    auto ab_of = [](int dt) { return dt == ST_F16 ? 1 : dt == ST_BF16 ? 2 : dt == ST_F32 ? 0 : -1; };
+    const int ab = ab_of(a->dtype);
+    if (out->dtype != ST_F32 || ab < 0 || ab_of(b->dtype) != ab)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: a and b must both be f32, f16 or bf16, out f32");
     if (a->off < 0 || b->off < 0 || out->off < 0 || a->ld < 0 || b->ld < 0 || out->ld < 0)
         return h->fail(ST_INVALID_ARG, "st_gemm: negative offset or ld");
-    if (prec != ST_PREC_F32_EXACT && prec != ST_PREC_TF32) return h->fail(ST_INVALID_ARG, "st_gemm: unknown precision");
+    if (prec != ST_PREC_F32_EXACT && prec != ST_PREC_TF32 && prec != ST_PREC_F16)
+        return h->fail(ST_INVALID_ARG, "st_gemm: unknown precision");
+    if ((ab != 0) != (prec == ST_PREC_F16))
+        return h->fail(ST_INVALID_ARG, "st_gemm: ST_PREC_F16 goes with f16 / bf16 operands, the others with f32");
+    if (ab && epi && epi->col_sum)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum needs f32 operands");
     cudaSetDevice(h->device);
 
     const Operand A = to_operand(a, a->trans ? m : k);
@@ -910,7 +960,9 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         }
     }
 
-    bool use_tc = (prec == ST_PREC_TF32) && k >= 1;
+    bool use_tc = (prec == ST_PREC_TF32 || prec == ST_PREC_F16) && k >= 1;
+    const int bke = ab ? 64 : BK;  // elements per 128-byte k row
+    const uint32_t mnw = ab ? 64 : 32;
     CUtensorMap ma, mb;
     std::string why;
     const bool a_mn = a->trans != 0, b_mn = b->trans == 0;
@@ -925,14 +977,20 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         // K-major tiles: 128-byte swizzle.  MN-major tf32 tiles: 128-byte
         // swizzle of 32-byte chunks (the layout the tensor core reads for
         // 32-bit MN-major operands).
-        const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B, mnmaj = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-        bool okA = a_mn ? operand_map(&ma, A, batch, k, m, 32, 32, mnmaj, &why)
-                        : operand_map(&ma, A, batch, m, k, 32, BM, kmaj, &why);
-        bool okB = okA && (b_mn ? operand_map(&mb, B, batch, k, n, 32, 32, mnmaj, &why)
-                                : operand_map(&mb, B, batch, n, k, 32, static_cast<uint32_t>(BN), kmaj, &why));
+        // 16-bit MN-major tiles: 128-byte swizzle of 64-element rows.
+        const CUtensorMapSwizzle kmaj = CU_TENSOR_MAP_SWIZZLE_128B,
+                                 mnmaj = ab ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+        const uint32_t kb = static_cast<uint32_t>(bke);
+        bool okA = a_mn ? operand_map(&ma, A, batch, k, m, mnw, kb, mnmaj, &why)
+                        : operand_map(&ma, A, batch, m, k, kb, BM, kmaj, &why);
+        bool okB = okA && (b_mn ? operand_map(&mb, B, batch, k, n, mnw, kb, mnmaj, &why)
+                                : operand_map(&mb, B, batch, n, k, kb, static_cast<uint32_t>(BN), kmaj, &why));
         use_tc = okA && okB;
     }
     if (use_tc && m_tiles > 65535) use_tc = false;
+    if (ab && !use_tc)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: f16 / bf16 operands need a TMA-describable layout (%s)",
+                       why.empty() ? "m too large" : why.c_str());
     if (use_tc) {
         g.a_grp = A.grp > 1 ? static_cast<int>(std::min<int64_t>(A.grp, batch)) : 1;
         g.a_outer = A.stride != 0;
@@ -940,7 +998,7 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         g.b_outer = B.stride != 0;
         if (A.grp > 1) g.a_grp = A.grp;
         if (B.grp > 1) g.b_grp = B.grp;
-        const int kb_total = static_cast<int>((k + BK - 1) / BK);
+        const int kb_total = static_cast<int>((k + bke - 1) / bke);
         const int64_t tiles = m_tiles * ((n + BN - 1) / BN) * batch;
         // Split k only when the tiles fill less than half the GPU, keeping
         // at least 4 k blocks (128) per split.
@@ -986,8 +1044,16 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         }
         dim3 grid(static_cast<unsigned>((n + BN - 1) / BN), static_cast<unsigned>(m_tiles),
                   static_cast<unsigned>(batch * splits));
-        st_status s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
-                               : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
+        st_status s;
+        if (ab == 1)
+            s = BN == 64 ? dispatch_tf32<64, 4, 1>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                         : dispatch_tf32<128, 3, 1>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
+        else if (ab == 2)
+            s = BN == 64 ? dispatch_tf32<64, 4, 2>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                         : dispatch_tf32<128, 3, 2>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
+        else
+            s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                         : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
         if (s != ST_OK) return s;
         if (splits > 1) {
             const int groups = static_cast<int>((n + 3) / 4);

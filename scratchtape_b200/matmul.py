@@ -9,7 +9,10 @@ Tape::batched_matmul's forward (src/tape.rs:73-85).
 
 Precision: ``matmul`` runs on the tcgen05 TF32 tensor cores (the role the
 reference's default f16 matrix-core path plays); ``matmul_f32`` runs the
-SIMT kernel whose every output is bit-identical to NdArray::matmul.
+SIMT kernel whose every output is bit-identical to NdArray::matmul; with
+float16 or bfloat16 operand buffers and ``precision=F16`` the product runs on
+the kind::f16 tensor cores into an f32 out (the reference's f16 x f16 -> f32
+k_matmul_cmma, src/gpu_step/matmul.rs:632-880).
 """
 import ctypes
 from dataclasses import dataclass
@@ -23,6 +26,8 @@ from .device import handle
 
 TF32 = N.PREC_TF32
 F32_EXACT = N.PREC_F32_EXACT
+F16 = N.PREC_F16
+_DTYPES = {torch.float32: N.ST_F32, torch.float16: N.ST_F16, torch.bfloat16: N.ST_BF16}
 
 
 @dataclass
@@ -45,10 +50,10 @@ class MatRef:
         return MatRef(h, off=col0, stride=t * cols, ld=cols, group=heads, inner=width)
 
     def _c(self):
-        if self.h.dtype != torch.float32 or not self.h.is_cuda:
-            raise TypeError("MatRef buffers are CUDA float32 tensors")
+        if self.h.dtype not in _DTYPES or not self.h.is_cuda:
+            raise TypeError("MatRef buffers are CUDA float32, float16 or bfloat16 tensors")
         return N.StMat(self.h.data_ptr(), self.off, self.stride, self.inner, self.ld, max(self.group, 1),
-                       int(self.trans), N.ST_F32, 0)
+                       int(self.trans), _DTYPES[self.h.dtype], 0)
 
 
 @dataclass
@@ -111,8 +116,12 @@ def matmul_f32(a, b, out, batch, m, k, n, epi=None):
     return matmul_with(a, b, out, batch, m, k, n, epi, F32_EXACT)
 
 
-def mm(a: torch.Tensor, b: torch.Tensor, ta=False, tb=False, precision=TF32, out=None):
-    """op(a) @ op(b) for 2-D CUDA float32 tensors (ta: a holds A^T; tb: b holds B^T)."""
+def mm(a: torch.Tensor, b: torch.Tensor, ta=False, tb=False, precision=None, out=None):
+    """op(a) @ op(b) for 2-D CUDA tensors (ta: a holds A^T; tb: b holds B^T):
+    float32 operands on TF32 (default) or F32_EXACT, float16 / bfloat16 on F16;
+    the out is float32."""
+    if precision is None:
+        precision = TF32 if a.dtype == torch.float32 else F16
     m, k = (a.shape[1], a.shape[0]) if ta else a.shape
     n = b.shape[0] if tb else b.shape[1]
     if out is None:
