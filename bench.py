@@ -975,6 +975,36 @@ def _lm_config():
     return Cfg()
 
 
+def large_gemm_probe(torch, device, peaks):
+    """Throughput of the tensor-core GEMM at large M, per layout: bf16 operands
+    (ST_PREC_F16, kind::f16, f32 out) at 16384 x 4096 x 4096 and TF32 at
+    8192^3 -- the "large-M GEMM" share of the north star's GEMM target, beside
+    the C4 step whose own GEMMs are d_model 256 wide.  CUDA events over 10
+    back-to-back launches after 3 warm-up launches; operands 160-512 MB (> L2)."""
+    import scratchtape_b200 as st
+    peak = float(peaks["bf16_tflops"])
+    res = {}
+    for name, dt, (m, k, n) in (("bf16", torch.bfloat16, (16384, 4096, 4096)), ("tf32", torch.float32, (8192, 8192, 8192))):
+        for ta, tb in ((False, False), (False, True), (True, False)):
+            a = torch.randn((k, m) if ta else (m, k), device=device).to(dt)
+            b = torch.randn((n, k) if tb else (k, n), device=device).to(dt)
+            out = torch.empty((m, n), device=device)
+            for _ in range(3):
+                st.mm(a, b, ta=ta, tb=tb, out=out)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                st.mm(a, b, ta=ta, tb=tb, out=out)
+            e1.record()
+            e1.synchronize()
+            tf = 2.0 * m * n * k / (e0.elapsed_time(e1) / 10 / 1e3) / 1e12
+            res["%s_%s" % (name, "NN" if not (ta or tb) else ("NT" if tb else "TN"))] = {
+                "shape": [m, k, n], "tflops": tf, "frac_of_bf16_peak": tf / peak}
+            del a, b, out
+    res["peak_source"] = "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS bf16 8192^3)"
+    return res
+
+
 def run_ours_c4(args):
     import torch
     import torch.distributed as dist
@@ -1101,6 +1131,7 @@ def run_ours_c4(args):
                     "api": "scratchtape_b200.lm.TinyLM.capture_step graph replay (pinned host bytes in, loss out)"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
+            "large_gemm": large_gemm_probe(torch, device, peaks),
         }
         if world == 1 and not args.no_cpu_baseline:
             el = cpu_baseline_c4(cfg)
