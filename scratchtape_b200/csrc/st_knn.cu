@@ -102,6 +102,9 @@ struct ScanArgs {
     const int *unit_list;
     const int64_t *unit_keys;
     int n_units;
+    // [nq] order-preserving bits of the best 128th score any list of the
+    // query has reached (0: none yet), shared by every unit of the query
+    uint32_t *gthr;
     int *status;
 };
 
@@ -112,6 +115,8 @@ __device__ __forceinline__ uint32_t ord_f32(float f) {
 __device__ __forceinline__ float unord_f32(uint32_t o) {
     return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
+// A published threshold's bits back to a score (0: none published).
+__device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
 __device__ __forceinline__ uint64_t make_key(float s, uint32_t idx) {
     return (static_cast<uint64_t>(ord_f32(s)) << 32) | static_cast<uint64_t>(0xffffffffu - idx);
 }
@@ -535,11 +540,18 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                 qf = pow2f(query_exp(m) - 1);
             }
             int cnt = 0;
-            float thr = -INFINITY;
+            float thr = -INFINITY;  // this list's 128th best
+            // The 128th best of any list of the query bounds its final 128th
+            // best from below, so keys under the best one published cannot
+            // place: read one tile ahead of use, published at each compaction.
+            float pubd = -INFINITY;
+            uint32_t pub = qlive ? __ldcg(g.gthr + qi) : 0u;
             int64_t k0, k1;
             unit_key_range(g, unit, k0, k1);
             for (int64_t tb = k0; tb < k1; tb += KT, ++gt) {
                 const uint32_t b = gt & 1u, use = gt >> 1;
+                const float teff = fmaxf(thr, thr_of(pub));
+                if (qlive) pub = __ldcg(g.gthr + qi);
                 if (!kwait(&accf[b], use & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
                     !kwait(&kfr[b], use & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                     ok = false;
@@ -571,7 +583,7 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                         } else {
                             sc[jj] = PREC == PREC_EXACT ? fmaf(-nk[jj], qf, dot * f[jj]) : fmaf(2.0f, dot, -nk[jj]);
                         }
-                        pass |= (sc[jj] >= thr ? 1u : 0u) << jj;
+                        pass |= (sc[jj] >= teff ? 1u : 0u) << jj;
                     }
                     const int lim = ncols - c0;
                     if (lim < 16) pass &= (1u << lim) - 1u;
@@ -598,13 +610,20 @@ __global__ void __launch_bounds__(KNN_THREADS, 1) k_knn_scan(const ScanArgs g) {
                 st::tc_fence_before();
                 st::mbar_arrive(&acce[b]);
                 const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - KT / 2);
-                if (need) warp_compact(need, my_buf, cnt, thr, nullptr, false);
+                if (need) {
+                    warp_compact(need, my_buf, cnt, thr, nullptr, false);
+                    if (qlive && thr > pubd) {
+                        atomicMax(g.gthr + qi, ord_f32(thr));
+                        pubd = thr;
+                    }
+                }
             }
             if (!ok) break;
             const int list = qlive ? unit_out_list(g, unit, row) : 0;
             uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(list) * 2 + half) * g.nq_pad + (qlive ? qi : 0)) * KTOP;
             const unsigned need = __ballot_sync(0xffffffffu, qlive);
             if (need) warp_compact(need, my_buf, cnt, thr, my_out, true);
+            if (qlive && thr > pubd) atomicMax(g.gthr + qi, ord_f32(thr));
         }
     }
 
@@ -1067,7 +1086,6 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
-__device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
 
 // kwait for the narrow scan's hand-offs, which come every few hundred
 // nanoseconds: try_wait without a sleep hint (the hardware parks the thread
@@ -1682,8 +1700,11 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     const int64_t nq_pad = static_cast<int64_t>(nqb) * KQ;
 
     uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * NEPI * KCAP));
-    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, sizeof(uint64_t) * 2 * splits * nq_pad * KTOP));
+    const size_t part_bytes = sizeof(uint64_t) * 2 * splits * nq_pad * KTOP;
+    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, part_bytes + sizeof(uint32_t) * nq_pad));
     if (!cbuf || !unit_out) return ST_NO_MEMORY;
+    uint32_t *gthr = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(unit_out) + part_bytes);
+    ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, sizeof(uint32_t) * nq_pad, h->stream));
 
     ScanArgs g{};
     g.codes = codes;
@@ -1701,6 +1722,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     g.unit_out = unit_out;
     g.ranges = ranges;
     g.always = always;
+    g.gthr = gthr;
     g.status = h->d_status;
     if (ranges) {
         if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT, true>(h, g, grid);
@@ -1748,7 +1770,7 @@ extern "C" st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const
     uint8_t *tab = static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_UNITS, tab_bytes));
     uint64_t *cbuf = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * NEPI * KCAP));
     const size_t out_bytes = sizeof(uint64_t) * 2 * static_cast<size_t>(n_lists) * nq_pad * KTOP;
-    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes));
+    uint64_t *unit_out = static_cast<uint64_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes + sizeof(uint32_t) * nq_pad));
     if (!tab || !cbuf || !unit_out) return ST_NO_MEMORY;
     int64_t *d_keys = reinterpret_cast<int64_t *>(tab);
     int32_t *d_q = reinterpret_cast<int32_t *>(tab + sizeof(int64_t) * 2 * n_units);
@@ -1757,8 +1779,9 @@ extern "C" st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const
     ST_CHECK_CUDA(h, cudaMemcpyAsync(d_q, unit_q, sizeof(int32_t) * n_units * KQ, cudaMemcpyHostToDevice, h->stream));
     ST_CHECK_CUDA(h, cudaMemcpyAsync(d_list, unit_list, sizeof(int32_t) * n_units * KQ, cudaMemcpyHostToDevice,
                                      h->stream));
-    // lists no unit writes (a query with fewer probes than lists) read as empty
-    ST_CHECK_CUDA(h, cudaMemsetAsync(unit_out, 0, out_bytes, h->stream));
+    // lists no unit writes (a query with fewer probes than lists) read as
+    // empty; the published thresholds behind them start at none
+    ST_CHECK_CUDA(h, cudaMemsetAsync(unit_out, 0, out_bytes + sizeof(uint32_t) * nq_pad, h->stream));
 
     ScanArgs g{};
     g.codes = codes;
@@ -1778,6 +1801,7 @@ extern "C" st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const
     g.unit_list = d_list;
     g.unit_keys = d_keys;
     g.n_units = static_cast<int>(n_units);
+    g.gthr = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(unit_out) + out_bytes);
     g.status = h->d_status;
     if (mode == 0 && prec == 0) s = launch_scan<MODE_DOT, PREC_EXACT, false>(h, g, grid);
     else if (mode == 0) s = launch_scan<MODE_DOT, PREC_F16REF, false>(h, g, grid);

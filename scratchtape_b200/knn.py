@@ -165,22 +165,39 @@ def probe_cells(q: torch.Tensor, cent: torch.Tensor, cnorm: torch.Tensor, nprobe
     return out
 
 
-def ivf_units(probes: np.ndarray, starts: np.ndarray):
-    """The scan's unit tables for queries probing cells: one unit per (cell,
-    up to 128 of the queries probing it); row r of a unit is (query, its probe
-    slot).  Returns (unit_q int32 [u, 128], unit_list int32 [u, 128],
-    unit_keys int64 [u, 2])."""
+def ivf_units(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int] = None):
+    """The scan's unit tables for queries probing cells: one unit per (cell
+    chunk, up to 128 of the queries probing the cell).  A cell longer than
+    ``chunk`` keys is scanned as several chunks, each its own unit and its own
+    list of the query, so that one crowded cell does not leave a single CTA
+    scanning it while the others idle (None: whole cells).  Row r of a unit is
+    (query, list).  Returns (unit_q int32 [u, 128], unit_list int32 [u, 128],
+    unit_keys int64 [u, 2], n_lists)."""
     nq, nprobe = probes.shape
-    cells = probes.reshape(-1).astype(np.int64)
-    qs = np.repeat(np.arange(nq, dtype=np.int32), nprobe)
-    slots = np.tile(np.arange(nprobe, dtype=np.int32), nq)
-    order = np.argsort(cells, kind="stable")
-    cells, qs, slots = cells[order], qs[order], slots[order]
-    new_run = np.r_[True, cells[1:] != cells[:-1]]
+    starts = np.asarray(starts, np.int64)
+    cells = probes.astype(np.int64)
+    size = starts[cells + 1] - starts[cells]
+    if chunk is None:
+        nch = np.ones_like(size)
+        chunk = int(max(1, size.max()))
+    else:
+        nch = np.maximum(1, (size + chunk - 1) // chunk)
+    base = np.cumsum(nch, axis=1) - nch            # first list of each (query, probe)
+    n_lists = int((base[:, -1] + nch[:, -1]).max())
+    # one entry per (query, probe, chunk)
+    qs = np.repeat(np.repeat(np.arange(nq, dtype=np.int64), nprobe), nch.reshape(-1))
+    cl = np.repeat(cells.reshape(-1), nch.reshape(-1))
+    first = np.repeat(base.reshape(-1), nch.reshape(-1))
+    j = np.arange(len(qs)) - np.repeat(np.cumsum(nch.reshape(-1)) - nch.reshape(-1), nch.reshape(-1))
+    lists = first + j
+    key = cl * (int(nch.max()) + 1) + j              # (cell, chunk)
+    order = np.argsort(key, kind="stable")
+    key, qs, lists, cl, j = key[order], qs[order], lists[order], cl[order], j[order]
+    new_run = np.r_[True, key[1:] != key[:-1]]
     run_id = np.cumsum(new_run) - 1
     run_first = np.flatnonzero(new_run)
-    rank = np.arange(len(cells)) - run_first[run_id]
-    run_len = np.diff(np.r_[run_first, len(cells)])
+    rank = np.arange(len(key)) - run_first[run_id]
+    run_len = np.diff(np.r_[run_first, len(key)])
     run_units = (run_len + KQ_ROWS - 1) // KQ_ROWS
     unit_base = np.r_[0, np.cumsum(run_units)[:-1]]
     unit = unit_base[run_id] + rank // KQ_ROWS
@@ -189,10 +206,34 @@ def ivf_units(probes: np.ndarray, starts: np.ndarray):
     unit_q = np.full((n_units, KQ_ROWS), -1, np.int32)
     unit_list = np.zeros((n_units, KQ_ROWS), np.int32)
     unit_q[unit, row] = qs
-    unit_list[unit, row] = slots
-    unit_cell = cells[run_first][np.repeat(np.arange(len(run_first)), run_units)]
-    unit_keys = np.stack([starts[unit_cell], starts[unit_cell + 1]], axis=1).astype(np.int64)
-    return unit_q, unit_list, np.ascontiguousarray(unit_keys)
+    unit_list[unit, row] = lists
+    run_cell = np.repeat(cl[run_first], run_units)
+    run_chunk = np.repeat(j[run_first], run_units)
+    k0 = starts[run_cell] + run_chunk * chunk
+    k1 = np.minimum(starts[run_cell + 1], k0 + chunk)
+    unit_keys = np.stack([k0, k1], axis=1).astype(np.int64)
+    # longest units first: CTAs take units u, u + grid, ..., so this spreads
+    # the long ones over the SMs before the short ones fill the gaps
+    order = np.argsort(-(k1 - k0), kind="stable")
+    return unit_q[order], unit_list[order], np.ascontiguousarray(unit_keys[order]), n_lists
+
+
+def ivf_chunk(probes: np.ndarray, starts: np.ndarray, n_sms: int = 148, max_lists: int = 64) -> int:
+    """A chunk length that spreads the probed keys over about two units per SM
+    (at least 16384 keys, a multiple of the 256-key tile), coarsened until no
+    query has more than ``max_lists`` lists."""
+    starts = np.asarray(starts, np.int64)
+    size = starts[probes.astype(np.int64) + 1] - starts[probes.astype(np.int64)]
+    # a cell's keys are scanned once per 128 queries probing it
+    cells, counts = np.unique(probes, return_counts=True)
+    work = int(((starts[cells + 1] - starts[cells]) * ((counts + KQ_ROWS - 1) // KQ_ROWS)).sum())
+    chunk = max(16384, -(-work // (2 * n_sms)))
+    chunk = -(-chunk // 256) * 256
+    while True:
+        per_q = np.maximum(1, (size + chunk - 1) // chunk).sum(axis=1).max()
+        if per_q <= max_lists:
+            return chunk
+        chunk *= 2
 
 
 def scan_units(codes, scales, queries, unit_q, unit_list, unit_keys, n_lists, mode="l2", prec="exact",
@@ -450,16 +491,17 @@ class KnnStore:
                    prec: str = "exact", with_ids: bool = False):
         """KnnStore::search_ivf (ivf.rs:466-526): for each query, the 128 best
         among the keys of its nprobe nearest cells.  One scan launch over a
-        table of (cell, up to 128 queries probing it) units, then one merge of
-        each query's nprobe lists.  Returns (scores, values), or (scores, key
-        indices) with ``with_ids``."""
+        table of (cell chunk, up to 128 queries probing it) units -- crowded
+        cells split so the SMs share them -- then one merge of each query's
+        lists.  Returns (scores, values), or (scores, key indices) with
+        ``with_ids``."""
         if getattr(self, "ivf", None) is None:
             raise RuntimeError("search_ivf needs build_ivf")
         q = self._queries(queries, rows)
         iv = self.ivf
         probes = probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
-        uq, ul, uk = ivf_units(probes, iv["starts"])
-        keys = scan_units(self.codes, self.scales, q, uq, ul, uk, nprobe, mode=mode, prec=prec,
+        uq, ul, uk, n_lists = ivf_units(probes, iv["starts"], ivf_chunk(probes, iv["starts"]))
+        keys = scan_units(self.codes, self.scales, q, uq, ul, uk, n_lists, mode=mode, prec=prec,
                           index_base=self.first)
         scores, ids = decode(keys, q, KMAX, mode=mode, prec=prec)
         return (scores, ids) if with_ids else (scores, self._values(ids))

@@ -9,7 +9,8 @@ def test_unit_tables_cover_every_probe_once():
     probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
     probes[:200, 0] = 7  # one crowded cell: 200 queries -> two units
     starts = np.r_[0, np.cumsum(rng.integers(0, 50, nlist))].astype(np.int64)
-    uq, ul, uk = ivf_units(probes, starts)
+    uq, ul, uk, n_lists = ivf_units(probes, starts)
+    assert n_lists == nprobe
     assert uq.shape[1] == 128 and ul.shape == uq.shape and uk.shape == (uq.shape[0], 2)
     seen = set()
     for u in range(uq.shape[0]):
@@ -23,3 +24,38 @@ def test_unit_tables_cover_every_probe_once():
             seen.add((q, slot))
     assert len(seen) == nq * nprobe
     assert (uq == -1).sum() == uq.size - nq * nprobe
+
+
+def test_chunked_units_cover_every_key_of_every_probe_once():
+    """Cells longer than the chunk become several units, each a list of its
+    own: every (query, probed key) pair is scanned exactly once, and each
+    query's lists are distinct and below n_lists."""
+    from scratchtape_b200.knn import ivf_chunk, ivf_units
+    rng = np.random.default_rng(1)
+    nq, nprobe, nlist = 200, 4, 30
+    # 150 queries probe the crowded cell 3 first, the rest of each row distinct
+    probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
+    for r in range(150):
+        probes[r] = np.r_[3, rng.choice(np.r_[0:3, 4:nlist], nprobe - 1, replace=False)]
+    sizes = rng.integers(0, 60, nlist)
+    sizes[3] = 1000
+    starts = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    chunk = 64
+    uq, ul, uk, n_lists = ivf_units(probes, starts, chunk)
+    assert (uk[:, 1] - uk[:, 0] <= chunk).all()
+    pairs = {}
+    lists_of = {}
+    for u in range(uq.shape[0]):
+        for q, lst in zip(uq[u][uq[u] >= 0], ul[u][uq[u] >= 0]):
+            assert 0 <= lst < n_lists
+            assert (q, lst) not in lists_of, "two units write one list"
+            lists_of[(q, lst)] = u
+            for key in range(uk[u, 0], uk[u, 1]):
+                assert (q, key) not in pairs, "a key scanned twice for one query"
+                pairs[(q, key)] = u
+    for q in range(nq):
+        want = set()
+        for c in probes[q]:
+            want.update(range(starts[c], starts[c + 1]))
+        assert {k for (qq, k) in pairs if qq == q} == want
+    assert ivf_chunk(probes, starts, n_sms=4, max_lists=64) % 256 == 0

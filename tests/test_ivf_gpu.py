@@ -50,6 +50,25 @@ def test_probing_all_cells_is_the_flat_search(dev, mode):
     assert torch.equal(s1, s2) and torch.equal(i1, i2)
 
 
+@pytest.mark.parametrize("mode", ["l2", "dot"])
+def test_chunked_units_match_whole_cells(dev, mode):
+    """Cells scanned as 256- and 1024-key chunks, each its own list, give the
+    same top-128 as whole cells, bit for bit."""
+    import scratchtape_b200.knn as K
+    st, rng = _store(12000, 128, 8)
+    st.build_ivf(12, iters=4)
+    q = torch.from_numpy(rng.standard_normal((300, 128)).astype(np.float32)).cuda()
+    probes = K.probe_cells(q, st.ivf["cent"], st.ivf["cnorm"], 3).cpu().numpy()
+    want = None
+    for chunk in (None, 1024, 256):
+        uq, ul, uk, nl = K.ivf_units(probes, st.ivf["starts"], chunk)
+        got = K.scan_units(st.codes, st.scales, q, uq, ul, uk, nl, mode=mode).cpu()
+        if want is None:
+            want = got
+        else:
+            assert nl > 3 and torch.equal(got, want)
+
+
 def test_fewer_cells_are_exact_over_the_probed_cells(dev):
     import scratchtape_b200.knn as K
     st, rng = _store(20000, 64, 4)
