@@ -42,6 +42,9 @@ METRIC = "GEMM TFLOP/s & % of B200 peak per layout; kNN keys/s vs HBM; vs CPU te
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 C2 = dict(m=32 * 128, d=128, dff=512)
 C5 = dict(keys=1 << 27, d=256, nq=4096, k=128)
+# The reference's IVF search as it quotes it (16384 queries x 8 probes over a
+# 37M-key store, docs/tiers_design.md:1468; 12288 cells, README.md:76-85)
+C5_IVF = dict(keys=37_000_000, nlist=12288, nprobe=8, nq=16384, clusters=12288, noise=0.5)
 # dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the C2
 # step, averaged over its launches, from profiles/gemm_tf32_c2.md (ncu, 1 pass).
 # DRAM bytes (read + write) per k_gemm_tf32 launch of the C2 step from one ncu capture (profiles/
@@ -49,6 +52,9 @@ C5 = dict(keys=1 << 27, d=256, nq=4096, k=128)
 C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
 # DRAM bytes of one k_attn_fwd + one k_attn_bwd launch at C3 from one ncu capture (profiles/attn_c3.md)
 C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
+# DRAM bytes (read + write) of one k_mlp_step + k_mlp_reduce pair at C2 from one ncu capture
+# (profiles/mlp_fused_c2.md); None until captured
+C2_FUSED_TRAFFIC = None
 
 
 def parse_args():
@@ -64,6 +70,9 @@ def parse_args():
                         "device and run through the 2-bit quantiser (the realistic variant)")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-ivf", action="store_true", help="C5: skip the IVF search measurement")
+    p.add_argument("--c2-path", default="gemms", choices=["fused", "gemms"],
+                   help="C2: the fused one-kernel step, or six separate GEMM launches")
     a = p.parse_args()
     if a.steps is None:
         a.steps = {"c5": 5, "c4": 24}.get(a.config, 200)
@@ -253,21 +262,29 @@ def run_ours(args):
     bufs.dy.copy_(dy)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
+    fused = mlp.fused_fits(m, d, dff) and args.c2_path == "fused"
+    stream = torch.cuda.Stream(device)
+    sides = mlp.StepStreams(device)
+    step = (lambda: mlp.forward_backward_fused(bufs)) if fused else \
+        (lambda: mlp.forward_backward(bufs, streams=sides))
+
     # eager warm-up: grows scratch, sets kernel attributes, counts launches
     n0 = h.launches
-    mlp.forward_backward(bufs)
+    mlp.forward_backward_fused(bufs) if fused else mlp.forward_backward(bufs)
     torch.cuda.synchronize()
     launches_per_step = h.launches - n0
 
-    stream = torch.cuda.Stream(device)
-    sides = mlp.StepStreams(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        mlp.forward_backward(bufs, streams=sides)  # warm on the capture streams
-    torch.cuda.synchronize()
-    with torch.cuda.graph(graph, stream=stream):
-        mlp.forward_backward(bufs, streams=sides)
-    torch.cuda.synchronize()
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            fn()  # warm on the capture streams
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            fn()
+        torch.cuda.synchronize()
+        return gr
+
+    graph = capture(step)
 
     def barrier():
         if world > 1:
@@ -297,29 +314,37 @@ def run_ours(args):
         total_ms = float(t.item())
     value = c2_flops() * args.steps * world / (total_ms / 1e3) / 1e12
 
-    # per-launch roofline of the TF32 GEMM kernel: each of the six GEMMs timed
-    # alone with cold L2, algorithmic bytes / duration
-    per_bytes = mlp.gemm_bytes(m, d, dff)
-    gl = mlp.gemm_list(bufs)
-    reps = 20
-    gemm_ms = []
-    for (a_, b_, o_, mm_, kk_, nn_, epi), nb in zip(gl, per_bytes):
-        gg = torch.cuda.CUDAGraph()  # one GEMM (and its split-k reduce) per graph: no host gaps
-        with torch.cuda.graph(gg, stream=stream):
-            st.matmul_with(a_, b_, o_, 1, mm_, kk_, nn_, epi, st.TF32)
+    def replay_ms(gr, reps=20):
         ts = []
         for _ in range(reps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            gg.replay()
+            gr.replay()
             e1.record()
             ts.append((e0, e1))
         torch.cuda.synchronize()
-        gemm_ms.append(float(np.mean([a.elapsed_time(b) for a, b in ts])))
-        del gg
+        return float(np.mean([a.elapsed_time(b) for a, b in ts]))
+
+    # per-launch roofline, cold L2, algorithmic bytes (the six GEMMs' f32
+    # operands and results) / duration: of the fused kernel and its reduction
+    # together, or of each of the six GEMMs alone
+    per_bytes = mlp.gemm_bytes(m, d, dff)
     bytes_total = float(sum(per_bytes))
-    achieved = bytes_total / (sum(gemm_ms) / 1e3) / 1e9
+    gemm_ms = []
+    if fused:
+        fused_ms = replay_ms(graph)
+        achieved = bytes_total / (fused_ms / 1e3) / 1e9
+        six = capture(lambda: mlp.forward_backward(bufs, streams=sides))
+        six_ms = replay_ms(six)
+        del six
+    else:
+        for (a_, b_, o_, mm_, kk_, nn_, epi), nb in zip(mlp.gemm_list(bufs), per_bytes):
+            # one GEMM (and its split-k reduce) per graph: no host gaps
+            gg = capture(lambda: st.matmul_with(a_, b_, o_, 1, mm_, kk_, nn_, epi, st.TF32))
+            gemm_ms.append(replay_ms(gg))
+            del gg
+        achieved = bytes_total / (sum(gemm_ms) / 1e3) / 1e9
     hbm = float(peaks["hbm_gbs"])
 
     # e2e through the host-array APIs, pinned host buffers in and out every step:
@@ -331,20 +356,20 @@ def run_ours(args):
     outs = tuple(torch.empty(t.shape, dtype=torch.float32, pin_memory=True) for t in (bufs.y, bufs.dx, bufs.dw1,
                                                                                       bufs.dw2))
     for _ in range(max(3, args.warmup // 4)):
-        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides)
+        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides, fused=fused)
     e2e_steps = max(10, min(args.steps, 200))
     e_ms = []
     for _ in range(e2e_steps):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides)
+        mlp.forward_backward_host(hx, hw1, hw2, hdy, bufs, outs, streams=sides, fused=fused)
         e1.record()
         e1.synchronize()
         e_ms.append(e0.elapsed_time(e1))
     call_total = float(sum(e_ms))
 
-    pipe = mlp.HostStream(m, d, dff, device)
+    pipe = mlp.HostStream(m, d, dff, device, fused=fused)
     pouts = [tuple(torch.empty_like(t).pin_memory() for t in outs) for _ in range(len(pipe.bufs))]
 
     def pipe_run(steps):
@@ -387,17 +412,31 @@ def run_ours(args):
                        "global_batch": 32 * world, "seq_len": 128,
                        "parallelism": "replicas only" if world > 1 else "single GPU",
                        "l2": "flushed (256 MiB write) before every timed step, outside its events",
-                       "graph": "step replayed from one CUDA graph"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "traffic": C2_TRAFFIC_PER_LAUNCH, "peak_source": peak_src,
-                         "traffic_note": "mean DRAM read+write per k_gemm_tf32 launch over the three launches of "
-                                         "one ncu capture (H, Y, dW2); algorithmic bytes per launch are "
-                                         "per_gemm_bytes",
-                         "kernel": "k_gemm_tf32 (+k_splitk_reduce)",
-                         "per_gemm_us": [round(t * 1e3, 2) for t in gemm_ms],
-                         "per_gemm_bytes": per_bytes,
-                         "tensor_frac_of_bf16_peak": c2_flops() / (sum(gemm_ms) / 1e3) / 1e12 /
-                         float(peaks["bf16_tflops"])},
+                       "graph": "step replayed from one CUDA graph",
+                       "step": "fused: the six GEMMs in one tcgen05 kernel (k_mlp_step) + a fixed-order "
+                               "reduction of per-block partials (k_mlp_reduce); H and dH written out too"
+                               if fused else "six GEMM launches on three streams"},
+            "roofline": ({"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                          "frac": achieved / hbm, "traffic": C2_FUSED_TRAFFIC, "peak_source": peak_src,
+                          "traffic_note": "DRAM read+write of one k_mlp_step + k_mlp_reduce pair from one ncu "
+                                          "capture (profiles/mlp_fused_c2.md); algorithmic bytes are the six "
+                                          "GEMMs' f32 operands and results (sum of per_gemm_bytes)",
+                          "kernel": "k_mlp_step (+k_mlp_reduce), timed together",
+                          "step_us": round(fused_ms * 1e3, 2), "algorithmic_bytes": bytes_total,
+                          "per_gemm_bytes": per_bytes,
+                          "six_gemm_step_us": round(six_ms * 1e3, 2),
+                          "tensor_frac_of_bf16_peak": c2_flops() / (fused_ms / 1e3) / 1e12 /
+                          float(peaks["bf16_tflops"])} if fused else
+                         {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                          "traffic": C2_TRAFFIC_PER_LAUNCH, "peak_source": peak_src,
+                          "traffic_note": "mean DRAM read+write per k_gemm_tf32 launch over the three launches of "
+                                          "one ncu capture (H, Y, dW2); algorithmic bytes per launch are "
+                                          "per_gemm_bytes",
+                          "kernel": "k_gemm_tf32 (+k_splitk_reduce)",
+                          "per_gemm_us": [round(t * 1e3, 2) for t in gemm_ms],
+                          "per_gemm_bytes": per_bytes,
+                          "tensor_frac_of_bf16_peak": c2_flops() / (sum(gemm_ms) / 1e3) / 1e12 /
+                          float(peaks["bf16_tflops"])}),
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e_total / e2e_steps, "steps": e2e_steps,
                     "api": "scratchtape_b200.mlp.HostStream.submit (pinned host arrays; consecutive steps "
@@ -608,6 +647,10 @@ def run_ours_c5(args):
                           "exact integer products), seeded by 1-in-1024 and 1-in-16 tile sample passes, + a "
                           "two-stage k_knn_merge; bytes = codes + scales + queries of one full pass"}
 
+    ivf_pass = None
+    if world == 1 and not args.no_ivf:
+        ivf_pass = c5_ivf_pass(device, d)
+
     flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
     achieved = flops_alg / (scan_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
@@ -634,6 +677,7 @@ def run_ours_c5(args):
                                          "figures in profiles/knn_scan_c5.md",
                          "peak_source": peak_src + " (bf16 dense, sustained)", "kernel": "k_knn_scan (+k_knn_merge)",
                          "small_pass": small_pass,
+                         "ivf_pass": ivf_pass,
                          "scan_ms": scan_ms, "tensor_passes": passes,
                          "executed_tflops": achieved * passes,
                          "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9},
@@ -677,6 +721,82 @@ def c3_bytes():
     bh, t, d = C3["b"] * C3["h"], C3["t"], C3["d"]
     tile = bh * t * d * 2
     return {"fwd": 4 * tile + bh * t * 4, "bwd": 8 * tile + bh * t * 4}
+
+
+def c5_ivf_pass(device, d, reps=3):
+    """KnnStore::search_ivf at the reference's quoted shape: 16384 queries x 8
+    probes over 37M 2-bit keys in 12288 k-means cells (the reference's figure
+    is for 4-bit keys).  Keys and queries are seeded clustered synthetics --
+    a mixture of 12288 N(0,1) centres plus N(0, 0.5^2) noise, quantised on
+    the device -- so the cells are populated as trained hidden states would
+    populate them.  ``wall_ms`` is the public call with host queries in and
+    host (distance, value) lists out, probe + host unit tables + scan +
+    merge + decode; ``scan_ms`` the scan + merge launch alone (CUDA events)."""
+    import torch
+    import scratchtape_b200.knn as K
+    cfg = C5_IVF
+    n, nlist, nprobe, nq = cfg["keys"], cfg["nlist"], cfg["nprobe"], cfg["nq"]
+    g = torch.Generator(device=device)
+    g.manual_seed(4242)
+    centers = torch.randn((cfg["clusters"], d), generator=g, device=device)
+    st = K.KnnStore(d, device=device)
+    codes = torch.empty((n, d // 4), dtype=torch.uint8, device=device)
+    scales = torch.empty(n, dtype=torch.float32, device=device)
+    norms = torch.empty(n, dtype=torch.float32, device=device)
+    for a in range(0, n, 1 << 22):
+        b = min(n, a + (1 << 22))
+        idx = torch.randint(0, cfg["clusters"], (b - a,), generator=g, device=device)
+        x = centers[idx] + cfg["noise"] * torch.randn((b - a, d), generator=g, device=device)
+        c, s_, nm = K.quantize(x)
+        codes[a:b].copy_(c)
+        scales[a:b].copy_(s_)
+        norms[a:b].copy_(nm)
+        del x, c, s_, nm
+    st.codes, st.scales, st.norms = codes, scales, norms
+    st.vals = (torch.arange(n, device=device) & 0xffff).to(torch.int32)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    st.build_ivf(nlist, iters=6)
+    torch.cuda.synchronize(device)
+    build_s = time.perf_counter() - t0
+    qidx = torch.randint(0, cfg["clusters"], (nq,), generator=g, device=device)
+    qh = (centers[qidx] + cfg["noise"] * torch.randn((nq, d), generator=g, device=device)).cpu().numpy()
+    st.search_ivf(qh, nprobe=nprobe, mode="l2")
+    torch.cuda.synchronize(device)
+    walls = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        sc, vals = st.search_ivf(qh, nprobe=nprobe, mode="l2")
+        sc.cpu(), vals.cpu()
+        walls.append((time.perf_counter() - t0) * 1e3)
+    q = torch.from_numpy(qh).to(device)
+    iv = st.ivf
+    probes = K.probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
+    uq, ul, uk, n_lists = K.ivf_units(probes, iv["starts"], K.ivf_chunk(probes, iv["starts"]))
+    out = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
+    K.scan_units(st.codes, st.scales, q, uq, ul, uk, n_lists, mode="l2", out=out)
+    evs = []
+    for _ in range(reps):
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        K.scan_units(st.codes, st.scales, q, uq, ul, uk, n_lists, mode="l2", out=out)
+        b_.record()
+        evs.append((a_, b_))
+    torch.cuda.synchronize(device)
+    scan_ms = float(np.median([a_.elapsed_time(b_) for a_, b_ in evs]))
+    sizes = np.diff(iv["starts"])
+    pairs = int(sizes[probes.astype(np.int64)].sum())  # (query, key) scores one call needs
+    wall_ms = float(np.median(walls))
+    return {"queries": nq, "nprobe": nprobe, "keys": n, "cells": nlist, "mode": "l2", "prec": "exact",
+            "wall_ms": wall_ms, "queries_per_s": nq / (wall_ms / 1e3), "scan_ms": scan_ms,
+            "scored_pairs": pairs, "pairs_per_s_scan": pairs / (scan_ms / 1e3), "units": int(uq.shape[0]),
+            "lists_per_query": int(n_lists),
+            "cell_keys_min_mean_max": [int(sizes.min()), float(sizes.mean()), int(sizes.max())],
+            "build_ivf_s": build_s,
+            "reference": "2.05 s per call for 16384 queries x 8 probes over 37M 4-bit keys (RX 9060 XT, Vulkan; "
+                         "docs/tiers_design.md:1468); not run here",
+            "data": "seeded clustered synthetic keys: %d N(0,1) centres + N(0, %.1f^2) noise, 2-bit quantised on "
+                    "the device; queries drawn the same way" % (cfg["clusters"], cfg["noise"])}
 
 
 def c5_rotated_keys(n, d, first, device, chunk=1 << 22):

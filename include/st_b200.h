@@ -170,6 +170,21 @@ ST_API st_status st_gemm_group(st_handle *h, const st_group_gemm *gemms, int32_t
 ST_API st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out,
                                             int64_t batch, int64_t m, int64_t k, int64_t n, const st_epilogue *epi);
 
+/* One Linear -> ReLU -> Linear layer without bias, forward and backward --
+ * the six GEMMs Tape::backward's MatMul and Relu arms issue for it
+ * (src/tape.rs:505-510, :530-534): h = relu(x w1), y = h w2,
+ * dh = (dy w2^T) * (h > 0), dw2 = h^T dy, dx = dh w1^T, dw1 = x^T dh, on the
+ * TF32 tensor cores in one fused kernel (h and dh never make a round trip
+ * through global memory; each token block makes its own) and one
+ * fixed-order reduction of the per-block partial products, so results are
+ * deterministic.  Row-major device f32: x, dy, y, dx [m, d]; w1, dw1 [d, f];
+ * w2, dw2 [f, d]; h, dh [m, f] (outputs; either may be null to skip writing
+ * it).  Needs d == 128, m and f multiples of 128, 16-byte aligned buffers;
+ * returns ST_UNSUPPORTED_SHAPE otherwise (use st_gemm per product then). */
+ST_API st_status st_mlp_step_tf32(st_handle *h, const float *x, const float *w1, const float *w2, const float *dy,
+                                  float *hout, float *y, float *dhout, float *dx, float *dw1, float *dw2, int64_t m,
+                                  int64_t d, int64_t f);
+
 /* NdArray::matmul with host buffers (src/tensor.rs:241 and the drop-in
  * gpu_matmul, src/gpu.rs:98-169): out[m, n] = op(a) . op(b), row-major host
  * f32, ta: a stored [k, m], tb: b stored [n, k].  Copies in, computes,

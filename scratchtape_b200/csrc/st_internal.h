@@ -26,6 +26,7 @@ enum StScratchSlot {
     SLOT_COLSUM,      // column-sum partials of the GEMM epilogue
     SLOT_GROUP,       // grouped GEMM: ticket / finished-tile / split counters
     SLOT_KNN_UNITS,   // kNN unit-table scans: the device copy of the unit tables
+    SLOT_MLP_PART,    // fused MLP step: per-block partial products
     SLOT_COUNT
 };
 

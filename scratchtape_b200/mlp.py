@@ -63,6 +63,30 @@ def forward_backward_grouped(b: MlpBuffers):
     return b
 
 
+def fused_fits(m, d, dff) -> bool:
+    """Shapes the fused step (forward_backward_fused) takes."""
+    return d == 128 and m % 128 == 0 and dff % 128 == 0
+
+
+def forward_backward_fused(b: MlpBuffers, write_h: bool = True):
+    """The six GEMMs in one fused tcgen05 kernel (st_mlp_step_tf32) plus a
+    fixed-order reduction, on torch's current stream: each 128-token block
+    makes its own slice of H and dH and uses it at once from TMEM and shared
+    memory.  Needs d == 128 and m, dff multiples of 128.  ``write_h`` False
+    leaves b.h and b.dh unwritten."""
+    from .device import handle, ptr
+    m, d = b.x.shape
+    dff = b.w1.shape[1]
+    for t in (b.x, b.w1, b.w2, b.dy, b.h, b.y, b.dh, b.dx, b.dw1, b.dw2):
+        if not (t.is_contiguous() and t.dtype == torch.float32):
+            raise ValueError("forward_backward_fused needs contiguous f32 buffers")
+    hh = ptr(b.h) if write_h else None
+    dh = ptr(b.dh) if write_h else None
+    handle(b.x.device).call("st_mlp_step_tf32", ptr(b.x), ptr(b.w1), ptr(b.w2), ptr(b.dy), hh, ptr(b.y), dh,
+                            ptr(b.dx), ptr(b.dw1), ptr(b.dw2), m, d, dff)
+    return b
+
+
 def gemm_bytes(m, d, dff):
     """Algorithmic f32 bytes each GEMM must move (read A, B, mask; write C)."""
     x, w, hh = m * d * 4, d * dff * 4, m * dff * 4
@@ -116,10 +140,11 @@ def forward_backward(b: MlpBuffers, precision=TF32, streams: StepStreams = None)
 
 
 def forward_backward_host(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, dy: np.ndarray, bufs: MlpBuffers = None,
-                          outs=None, precision=TF32, streams: StepStreams = None):
+                          outs=None, precision=TF32, streams: StepStreams = None, fused: bool = False):
     """Host arrays in, host gradients out: copies x, w1, w2, dy to the device,
     runs the layer forward and backward, and reads back (y, dx, dw1, dw2).
-    ``outs`` may hold preallocated (pinned) host tensors for the results."""
+    ``outs`` may hold preallocated (pinned) host tensors for the results.
+    ``fused``: the one-kernel step where the shape allows it (TF32 only)."""
     m, d = x.shape
     dff = w1.shape[1]
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -127,7 +152,10 @@ def forward_backward_host(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, dy: np.
         bufs = MlpBuffers.allocate(m, d, dff, dev)
     for dst, src in ((bufs.x, x), (bufs.w1, w1), (bufs.w2, w2), (bufs.dy, dy)):
         dst.copy_(torch.as_tensor(src), non_blocking=True)
-    forward_backward(bufs, precision, streams)
+    if fused and precision == TF32 and fused_fits(m, d, dff):
+        forward_backward_fused(bufs)
+    else:
+        forward_backward(bufs, precision, streams)
     if outs is None:
         outs = tuple(torch.empty(t.shape, dtype=torch.float32, pin_memory=True) for t in (bufs.y, bufs.dx, bufs.dw1,
                                                                                           bufs.dw2))
@@ -141,9 +169,13 @@ class HostStream(HostPipeline):
     """MLP layer steps from host arrays, pipelined (``HostPipeline``):
     ``submit((x, w1, w2, dy), (y, dx, dw1, dw2))`` with pinned host tensors."""
 
-    def __init__(self, m, d, dff, device=None, depth=3, precision=TF32):
+    def __init__(self, m, d, dff, device=None, depth=3, precision=TF32, fused: bool = False):
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.bufs = [MlpBuffers.allocate(m, d, dff, dev) for _ in range(depth)]
         self.sides = StepStreams(dev)
         sets = [([b.x, b.w1, b.w2, b.dy], [b.y, b.dx, b.dw1, b.dw2]) for b in self.bufs]
-        super().__init__(sets, lambda j: forward_backward(self.bufs[j], precision, self.sides), dev)
+        if fused and precision == TF32 and fused_fits(m, d, dff):
+            step = lambda j: forward_backward_fused(self.bufs[j])
+        else:
+            step = lambda j: forward_backward(self.bufs[j], precision, self.sides)
+        super().__init__(sets, step, dev)
