@@ -52,7 +52,7 @@ C5_IVF = dict(keys=37_000_000, nlist=12288, nprobe=8, nq=16384, clusters=12288, 
 C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
 # DRAM bytes of one k_attn_fwd + one k_attn_bwd launch at C3 from one ncu capture (profiles/attn_c3.md)
 C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
-# DRAM bytes (read + write) of one k_mlp_step + k_mlp_reduce pair at C2 from one ncu capture
+# DRAM bytes (read + write) of one k_mlp_step launch at C2 from one ncu capture
 # (profiles/mlp_fused_c2.md); None until captured
 C2_FUSED_TRAFFIC = None
 
@@ -71,7 +71,7 @@ def parse_args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ivf", action="store_true", help="C5: skip the IVF search measurement")
-    p.add_argument("--c2-path", default="gemms", choices=["fused", "gemms"],
+    p.add_argument("--c2-path", default="fused", choices=["fused", "gemms"],
                    help="C2: the fused one-kernel step, or six separate GEMM launches")
     a = p.parse_args()
     if a.steps is None:
@@ -413,15 +413,15 @@ def run_ours(args):
                        "parallelism": "replicas only" if world > 1 else "single GPU",
                        "l2": "flushed (256 MiB write) before every timed step, outside its events",
                        "graph": "step replayed from one CUDA graph",
-                       "step": "fused: the six GEMMs in one tcgen05 kernel (k_mlp_step) + a fixed-order "
-                               "reduction of per-block partials (k_mlp_reduce); H and dH written out too"
+                       "step": "fused: the six GEMMs in one tcgen05 kernel (k_mlp_step) with fixed-order "
+                               "in-kernel reductions of the per-block partials; H and dH written out too"
                                if fused else "six GEMM launches on three streams"},
             "roofline": ({"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                           "frac": achieved / hbm, "traffic": C2_FUSED_TRAFFIC, "peak_source": peak_src,
-                          "traffic_note": "DRAM read+write of one k_mlp_step + k_mlp_reduce pair from one ncu "
-                                          "capture (profiles/mlp_fused_c2.md); algorithmic bytes are the six "
-                                          "GEMMs' f32 operands and results (sum of per_gemm_bytes)",
-                          "kernel": "k_mlp_step (+k_mlp_reduce), timed together",
+                          "traffic_note": "DRAM read+write of one k_mlp_step launch from one ncu capture "
+                                          "(profiles/mlp_fused_c2.md); algorithmic bytes are the six GEMMs' f32 "
+                                          "operands and results (sum of per_gemm_bytes)",
+                          "kernel": "k_mlp_step (one cooperative launch, reductions inside)",
                           "step_us": round(fused_ms * 1e3, 2), "algorithmic_bytes": bytes_total,
                           "per_gemm_bytes": per_bytes,
                           "six_gemm_step_us": round(six_ms * 1e3, 2),

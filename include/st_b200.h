@@ -174,13 +174,15 @@ ST_API st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, const
  * the six GEMMs Tape::backward's MatMul and Relu arms issue for it
  * (src/tape.rs:505-510, :530-534): h = relu(x w1), y = h w2,
  * dh = (dy w2^T) * (h > 0), dw2 = h^T dy, dx = dh w1^T, dw1 = x^T dh, on the
- * TF32 tensor cores in one fused kernel (h and dh never make a round trip
- * through global memory; each token block makes its own) and one
- * fixed-order reduction of the per-block partial products, so results are
- * deterministic.  Row-major device f32: x, dy, y, dx [m, d]; w1, dw1 [d, f];
- * w2, dw2 [f, d]; h, dh [m, f] (outputs; either may be null to skip writing
- * it).  Needs d == 128, m and f multiples of 128, 16-byte aligned buffers;
- * returns ST_UNSUPPORTED_SHAPE otherwise (use st_gemm per product then). */
+ * TF32 tensor cores in one fused cooperative kernel (h and dh never make a
+ * round trip through global memory; each 128 x 128 block makes its own) that
+ * also adds up the per-block partial products in a fixed order, so results
+ * are deterministic.  Row-major device f32: x, dy, y, dx [m, d]; w1, dw1
+ * [d, f]; w2, dw2 [f, d]; h, dh [m, f] (outputs; either may be null to skip
+ * writing it).  Needs d == 128, m and f multiples of 128, (m/128)*(f/128) no
+ * more than the GPU's SMs, 16-byte aligned buffers; returns
+ * ST_UNSUPPORTED_SHAPE otherwise (use st_gemm per product then).  Calls on
+ * one handle must not overlap on the GPU (they share its scratch). */
 ST_API st_status st_mlp_step_tf32(st_handle *h, const float *x, const float *w1, const float *w2, const float *dy,
                                   float *hout, float *y, float *dhout, float *dx, float *dw1, float *dw2, int64_t m,
                                   int64_t d, int64_t f);

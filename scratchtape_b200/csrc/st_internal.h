@@ -27,6 +27,7 @@ enum StScratchSlot {
     SLOT_GROUP,       // grouped GEMM: ticket / finished-tile / split counters
     SLOT_KNN_UNITS,   // kNN unit-table scans: the device copy of the unit tables
     SLOT_MLP_PART,    // fused MLP step: per-block partial products
+    SLOT_MLP_CTL,     // fused MLP step: per-block arrival / departure counters
     SLOT_COUNT
 };
 
@@ -42,6 +43,8 @@ struct st_handle {
     int num_sms = 148;
     void *group_ctl = nullptr;   // grouped GEMM counters: where they were last zeroed, and how many bytes
     size_t group_ctl_bytes = 0;
+    void *mlp_ctl = nullptr;     // fused MLP step counters: where they were last zeroed, and how many bytes
+    size_t mlp_ctl_bytes = 0;
 
     st_status fail(st_status s, const char *fmt, ...) {
         char buf[512];

@@ -14,10 +14,16 @@
 //       P2), transposed into shared memory (an operand of P3), and to H / dH
 //   P2  Y_p = H W2[cc, :],  dX_p = dH W1[:, cc]^T           (A from TMEM)
 //   P3  dW2_p = H^T dY_rb,  dW1_p = X_rb^T dH               (K = 128 tokens)
-//   E2  the four partial products to a scratch buffer
-// Y and dX are sums over the F / 128 column blocks, dW1 and dW2 over the
-// M / 128 token blocks: k_mlp_reduce adds the partials in block order, so the
-// results are deterministic.
+//   E3  H and dH to global memory from their transposed shared-memory tiles
+//       (while P2 runs)
+//   E2  the four partial products to a scratch buffer (Y_p, dX_p while P3 runs)
+//   R1  Y and dX: the ncc = F/128 CTAs of a token block each sum 128/ncc rows
+//       over the block's ncc partials
+//   R2  dW2 and dW1: the nrb = M/128 CTAs of a column block each sum 256/nrb
+//       of its columns over the block's nrb partials
+// R1 and R2 wait (bounded) on per-block arrival counters, so the launch is
+// cooperative (every CTA resident); every output is summed in one fixed
+// block order, so the results are deterministic.
 //
 // Roles (320 threads): warp 0 issues TMA loads (16 loads of 32 KB: 8 for P1,
 // 4 for P2, 4 for P3), warp 1 issues the MMAs, warps 2..9 are the epilogue
@@ -48,11 +54,15 @@ constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers, then slack for 1024-byt
 constexpr int NEPI = 256;
 constexpr int THREADS = 64 + NEPI;
 constexpr int N_LOADS = 16;
+constexpr int R1_ITEMS = 8, R1_K = 4;  // Y / dX reduction: items per thread per pass, partials per load round
+constexpr int R2_K = 32;               // dW reduction: partials per load round
 static_assert(SMEM <= 232448, "MLP step kernel exceeds the sm_100 shared-memory limit");
 
 struct MlpArgs {
     float *h, *dh;  // [M, F] outputs, or null
-    float *part;    // Y_p [F/128][M][D], dX_p [F/128][M][D], dW2_p [M/128][F][D], dW1_p [M/128][D][F]
+    float *y, *dx, *dw1, *dw2;
+    unsigned *ctl;  // [M/128] arrivals, [M/128] departures per token block; the same per column block; abort
+    float *part;    // Y_p, dX_p [F/128][M/128] tiles; dW2_p, dW1_p [M/128][F/128] tiles (128 x 128, column-major)
     int m, f;
     int *status;
 };
@@ -80,13 +90,59 @@ __device__ __forceinline__ uint8_t *slot_ptr(uint8_t *smem, int slot) {
 __device__ __forceinline__ uint64_t kdesc(uint32_t a) { return st::sdesc_sw128(a, 16, 1024); }
 __device__ __forceinline__ uint64_t ndesc(uint32_t a) { return st::sdesc_make(a, 4096, 512, st::LAYOUT_SW128_BASE32B); }
 
-__device__ __forceinline__ void st_v4(float *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    *reinterpret_cast<float4 *>(p) = make_float4(__uint_as_float(a), __uint_as_float(b), __uint_as_float(c),
-                                                 __uint_as_float(d));
+// Barrier of the 256 epilogue threads only (warps 2..9).
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(NEPI) : "memory"); }
+
+// epi_bar that also returns whether `v` holds in every epilogue thread, so
+// that branches holding further barriers are taken by all of them or none.
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "n"(NEPI)
+        : "memory");
+    return r != 0;
 }
-__device__ __forceinline__ void st_row32(float *p, const uint32_t (&r)[32]) {
-#pragma unroll
-    for (int i = 0; i < 8; i++) st_v4(p + 4 * i, r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// With `ok` (the same in every epilogue thread), thread `et` == 0 spins
+// (bounded) until *ctr >= need -- the CTAs it waits for are resident with it
+// (cooperative launch) -- and shares the outcome with the other epilogue
+// threads.  On expiry: the status word and the abort flag.
+__device__ bool wait_count(const MlpArgs &g, const unsigned *ctr, unsigned need, int et, bool ok_in) {
+    __shared__ int s_ok;
+    if (et == 0) {
+        int ok = ok_in ? 1 : 0;
+        const unsigned *abort_flag = g.ctl + 2 * (g.m / MT) + 2 * (g.f / CT);
+        const uint64_t t0 = st::globaltimer();
+#pragma unroll 1
+        for (uint32_t i = 0; ok; ++i) {
+            if (ld_acquire(ctr) >= need) break;
+            if (ld_acquire(abort_flag)) {
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+            if ((i & 15u) == 0 && st::globaltimer() - t0 > st::WAIT_LIMIT_NS) {
+                st::set_status(g.status, st::DEV_TIMEOUT_FULL);
+                atomicExch(const_cast<unsigned *>(abort_flag), 1u);
+                ok = 0;
+                break;
+            }
+        }
+        s_ok = ok;
+    }
+    epi_bar();
+    return s_ok != 0;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) k_mlp_step(const __grid_constant__ MlpMaps mp, const MlpArgs g) {
@@ -216,9 +272,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_mlp_step(const __grid_constant__
             }
         }
     } else {  // -------------------------------------------------------- epilogue
-        const int q = warp & 3, half = (warp - 2) >> 2;
+        const int q = warp & 3, half = (warp - 2) >> 2, ew = warp - 2;
         const int row = q * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0..255
         const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        const int ncc = g.f / CT, nrb = g.m / MT;
         // E1: H and dH.  acc1 also means every P1 load has been consumed, so
         // the H^T / dH^T region (P1's extra load slots) is free to write.
         bool ok = st::mbar_wait(acc1, 0, g.status, st::DEV_TIMEOUT_ACC);
@@ -250,27 +308,46 @@ __global__ void __launch_bounds__(THREADS, 1) k_mlp_step(const __grid_constant__
                     *reinterpret_cast<uint32_t *>(ht + off) = hr[i];
                     *reinterpret_cast<uint32_t *>(dht + off) = gr[i];
                 }
-                const int64_t gi = static_cast<int64_t>(t0 + row) * g.f + c0 + col;
-                if (g.h) st_row32(g.h + gi, hr);
-                if (g.dh) st_row32(g.dh + gi, gr);
             }
         }
         st::tmem_st_wait();
         st::fence_proxy_async_smem();
         st::tc_fence_before();
         st::mbar_arrive(hs_ready);
+        ok = epi_all(ok);  // the H^T / dH^T tiles are complete
 
-        // E2: the partial products
-        const int ncc = g.f / CT;
+        // E3: H and dH out of their transposed shared-memory tiles while P2
+        // runs (the tiles are final; P3 only reads them): lane = column, so
+        // each store is one 128-byte line
+        if (ok && (g.h || g.dh)) {
+#pragma unroll 1
+            for (int tt = 0; tt < MT / 8; tt++) {
+                const int t = ew * (MT / 8) + tt;
+                const uint32_t tin = static_cast<uint32_t>(t & 31);
+                const uint8_t *ht = smem + OFF_HT + (t >> 5) * (TILE / 4);
+                const int64_t gi = static_cast<int64_t>(t0 + t) * g.f + c0 + lane;
+#pragma unroll
+                for (int ch = 0; ch < CT / 32; ch++) {
+                    const uint32_t off =
+                        st::sw128_offset(static_cast<uint32_t>(ch * 32 + lane), tin >> 2) + (tin & 3u) * 4u;
+                    if (g.h) g.h[gi + ch * 32] = *reinterpret_cast<const float *>(ht + off);
+                    if (g.dh) g.dh[gi + ch * 32] = *reinterpret_cast<const float *>(ht + TILE + off);
+                }
+            }
+        }
+
+        // E2: the partial products, each 128 x 128 tile column-major (element
+        // (lane, column) at column * 128 + lane), so a warp's store of one
+        // column is one full 128-byte line
         float *yp = g.part;
-        float *xp = yp + static_cast<int64_t>(ncc) * g.m * DM;
-        float *w2p = xp + static_cast<int64_t>(ncc) * g.m * DM;
-        float *w1p = w2p + static_cast<int64_t>(g.m / MT) * g.f * DM;
+        float *xp = yp + static_cast<int64_t>(ncc) * nrb * (MT * CT);
+        float *w2p = xp + static_cast<int64_t>(ncc) * nrb * (MT * CT);
+        float *w1p = w2p + static_cast<int64_t>(ncc) * nrb * (MT * CT);
         ok = ok && st::mbar_wait(acc2, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
         if (ok) {
-            float *y_row = yp + (static_cast<int64_t>(cc) * g.m + t0 + row) * DM;
-            float *x_row = xp + (static_cast<int64_t>(cc) * g.m + t0 + row) * DM;
+            float *yt = yp + static_cast<int64_t>(cc * nrb + rb) * (MT * CT) + row;
+            float *xt = xp + static_cast<int64_t>(cc * nrb + rb) * (MT * CT) + row;
 #pragma unroll 1
             for (int j = 0; j < 2; j++) {
                 const int col = half * 64 + j * 32;
@@ -278,15 +355,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_mlp_step(const __grid_constant__
                 st::tmem_ld32(tmem + lanes + 256 + col, r);
                 st::tmem_ld32(tmem + lanes + 384 + col, u);
                 st::tmem_ld_wait();
-                st_row32(y_row + col, r);
-                st_row32(x_row + col, u);
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    yt[(col + i) * MT] = __uint_as_float(r[i]);
+                    xt[(col + i) * MT] = __uint_as_float(u[i]);
+                }
             }
         }
+        __threadfence();
+        ok = epi_all(ok);
+        if (et == 0 && ok) atomicAdd(g.ctl + rb, 1u);
         ok = ok && st::mbar_wait(acc3, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
         if (ok) {
-            float *w2_row = w2p + (static_cast<int64_t>(rb) * g.f + c0 + row) * DM;  // lane = c, columns = d
-            float *w1_row = w1p + (static_cast<int64_t>(rb) * DM + row) * g.f + c0;  // lane = d, columns = c
+            float *w2t = w2p + static_cast<int64_t>(rb * ncc + cc) * (MT * CT) + row;  // lane = c, columns = d
+            float *w1t = w1p + static_cast<int64_t>(rb * ncc + cc) * (MT * CT) + row;  // lane = d, columns = c
 #pragma unroll 1
             for (int j = 0; j < 2; j++) {
                 const int col = half * 64 + j * 32;
@@ -294,59 +377,119 @@ __global__ void __launch_bounds__(THREADS, 1) k_mlp_step(const __grid_constant__
                 st::tmem_ld32(tmem + lanes + col, r);
                 st::tmem_ld32(tmem + lanes + 128 + col, u);
                 st::tmem_ld_wait();
-                st_row32(w2_row + col, r);
-                st_row32(w1_row + col, u);
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    w2t[(col + i) * MT] = __uint_as_float(r[i]);
+                    w1t[(col + i) * MT] = __uint_as_float(u[i]);
+                }
             }
         }
-        st::grid_dep_launch();
+        __threadfence();
+        ok = epi_all(ok);
+        if (et == 0 && ok) atomicAdd(g.ctl + 2 * nrb + cc, 1u);
+
+        // R1: rows [r0, r0 + R) of this token block's Y and dX, each the sum
+        // of its ncc partials in column-block order; staged row-major in the
+        // (now free) shared memory and written out a row at a time
+        float *stage = reinterpret_cast<float *>(smem);
+        ok = wait_count(g, g.ctl + rb, static_cast<unsigned>(ncc), et, ok);
+        if (ok) {
+            const int q0 = cc * (MT / 4) / ncc, q1 = (cc + 1) * (MT / 4) / ncc, nq4 = q1 - q0;
+            const int items = 2 * CT * nq4;
+            const int64_t step4 = static_cast<int64_t>(nrb) * (MT * CT) / 4;
+            // R1_ITEMS items per thread per pass, R1_K partials per load round,
+            // every load of a round in flight before the first addition
+            for (int i0 = 0; i0 < items; i0 += R1_ITEMS * NEPI) {
+                const float4 *p[R1_ITEMS];
+                float4 a[R1_ITEMS];
+#pragma unroll
+                for (int j = 0; j < R1_ITEMS; j++) {
+                    const int i = min(i0 + j * NEPI + et, items - 1);
+                    const int o = i / (CT * nq4), rem = i % (CT * nq4), c = rem / nq4, qq = rem % nq4;
+                    p[j] = reinterpret_cast<const float4 *>((o ? xp : yp) + static_cast<int64_t>(rb) * (MT * CT) +
+                                                            c * MT + 4 * (q0 + qq));
+                    a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                for (int k0 = 0; k0 < ncc; k0 += R1_K) {
+                    float4 v[R1_ITEMS][R1_K];
+#pragma unroll
+                    for (int j = 0; j < R1_ITEMS; j++)
+#pragma unroll
+                        for (int k = 0; k < R1_K; k++)
+                            v[j][k] = k0 + k < ncc ? __ldcg(p[j] + (k0 + k) * step4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int j = 0; j < R1_ITEMS; j++)
+#pragma unroll
+                        for (int k = 0; k < R1_K; k++)
+                            if (k0 + k < ncc) a[j].x += v[j][k].x, a[j].y += v[j][k].y, a[j].z += v[j][k].z, a[j].w += v[j][k].w;
+                }
+#pragma unroll
+                for (int j = 0; j < R1_ITEMS; j++) {
+                    const int i = i0 + j * NEPI + et;
+                    if (i >= items) continue;
+                    const int o = i / (CT * nq4), rem = i % (CT * nq4), c = rem / nq4, qq = rem % nq4;
+                    float *sr = stage + (o * MT + 4 * qq) * (CT + 4) + c;
+                    sr[0] = a[j].x, sr[CT + 4] = a[j].y, sr[2 * (CT + 4)] = a[j].z, sr[3 * (CT + 4)] = a[j].w;
+                }
+            }
+            epi_bar();
+            const int rows = 4 * nq4;
+            for (int i = et; i < 2 * rows * (DM / 4); i += NEPI) {
+                const int o = i / (rows * (DM / 4)), rem = i % (rows * (DM / 4)), r = rem / (DM / 4), c4 = rem % (DM / 4);
+                const float *sr = stage + (o * MT + r) * (CT + 4) + 4 * c4;
+                float *dst = (o ? g.dx : g.y) + static_cast<int64_t>(t0 + 4 * q0 + r) * DM + 4 * c4;
+                *reinterpret_cast<float4 *>(dst) = make_float4(sr[0], sr[1], sr[2], sr[3]);
+            }
+            epi_bar();
+            if (et == 0 && atomicAdd(g.ctl + nrb + rb, 1u) == static_cast<unsigned>(ncc - 1)) {
+                atomicExch(g.ctl + rb, 0u);  // every CTA of this token block is past its wait
+                atomicExch(g.ctl + nrb + rb, 0u);
+            }
+        }
+
+        // R2: columns [u0, u1) of this column block's dW2 (units 0..127 = its
+        // d columns) and dW1 (units 128..255 = its c columns), each the sum of
+        // its nrb partials in token-block order
+        ok = wait_count(g, g.ctl + 2 * nrb + cc, static_cast<unsigned>(nrb), et, ok);
+        if (ok) {
+            const int u0 = rb * 256 / nrb, u1 = (rb + 1) * 256 / nrb, nu = u1 - u0;
+            const int64_t step = static_cast<int64_t>(ncc) * (MT * CT);
+            for (int i = et; i < nu * (MT / 4); i += NEPI) {
+                const int ul = i / (MT / 4), r4 = (i % (MT / 4)) * 4, u = u0 + ul;
+                const float *base = (u < DM ? w2p : w1p) + static_cast<int64_t>(cc) * (MT * CT) + (u & 127) * MT + r4;
+                const float4 *p = reinterpret_cast<const float4 *>(base);
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int k0 = 0; k0 < nrb; k0 += R2_K) {  // R2_K loads in flight, then their sums in order
+                    float4 v[R2_K];
+#pragma unroll
+                    for (int t = 0; t < R2_K; t++)
+                        v[t] = k0 + t < nrb ? __ldcg(p + (k0 + t) * (step / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int t = 0; t < R2_K; t++)
+                        if (k0 + t < nrb) a.x += v[t].x, a.y += v[t].y, a.z += v[t].z, a.w += v[t].w;
+                }
+                float *sr = stage + r4 * (nu + 1) + ul;
+                sr[0] = a.x, sr[nu + 1] = a.y, sr[2 * (nu + 1)] = a.z, sr[3 * (nu + 1)] = a.w;
+            }
+            epi_bar();
+            for (int i = et; i < MT * nu; i += NEPI) {
+                const int r = i / nu, ul = i % nu, u = u0 + ul;
+                const float v = stage[r * (nu + 1) + ul];
+                if (u < DM) g.dw2[static_cast<int64_t>(c0 + r) * DM + u] = v;   // row c, column d
+                else g.dw1[static_cast<int64_t>(r) * g.f + c0 + (u - DM)] = v;   // row d, column c
+            }
+            epi_bar();
+            if (et == 0 && atomicAdd(g.ctl + 2 * nrb + ncc + cc, 1u) == static_cast<unsigned>(nrb - 1)) {
+                atomicExch(g.ctl + 2 * nrb + cc, 0u);
+                atomicExch(g.ctl + 2 * nrb + ncc + cc, 0u);
+            }
+        }
     }
     st::tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         st::tc_fence_after();
         st::tmem_dealloc(tmem, 512);
-    }
-}
-
-// Y = sum of the F/128 partials, dX likewise; dW2 and dW1 = sums of the
-// M/128 partials; each output float4 adds its partials in block order.
-__global__ void __launch_bounds__(256) k_mlp_reduce(const float *part, float *y, float *dx, float *dw1, float *dw2,
-                                                    int m, int f) {
-    st::grid_dep_wait();
-    const int ncc = f / CT, nrb = m / MT;
-    const int64_t ny = static_cast<int64_t>(m) * DM / 4, nw = static_cast<int64_t>(f) * DM / 4;
-    const float4 *yp = reinterpret_cast<const float4 *>(part), *xp = yp + ncc * ny, *w2p = xp + ncc * ny,
-                 *w1p = w2p + nrb * nw;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < 2 * ny + 2 * nw;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float4 *src;
-        float4 *dst;
-        int n;
-        int64_t stride;
-        if (i < ny) {
-            src = yp + i, dst = reinterpret_cast<float4 *>(y) + i, n = ncc, stride = ny;
-        } else if (i < 2 * ny) {
-            src = xp + (i - ny), dst = reinterpret_cast<float4 *>(dx) + (i - ny), n = ncc, stride = ny;
-        } else if (i < 2 * ny + nw) {
-            src = w2p + (i - 2 * ny), dst = reinterpret_cast<float4 *>(dw2) + (i - 2 * ny), n = nrb, stride = nw;
-        } else {
-            src = w1p + (i - 2 * ny - nw), dst = reinterpret_cast<float4 *>(dw1) + (i - 2 * ny - nw), n = nrb,
-            stride = nw;
-        }
-        float4 s = __ldcg(src);
-        int k = 1;
-        for (; k + 8 <= n; k += 8) {
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = __ldcg(src + (k + u) * stride);
-#pragma unroll
-            for (int u = 0; u < 8; u++) s.x += v[u].x, s.y += v[u].y, s.z += v[u].z, s.w += v[u].w;
-        }
-        for (; k < n; k++) {
-            const float4 v = __ldcg(src + k * stride);
-            s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
-        }
-        *dst = s;
     }
 }
 
@@ -382,15 +525,31 @@ extern "C" st_status st_mlp_step_tf32(st_handle *h, const float *x, const float 
         !map2d(&mp.w1n, w1, f, DM, 32, true, &why) || !map2d(&mp.w1k, w1, f, DM, 128, false, &why) ||
         !map2d(&mp.w2k, w2, DM, f, 128, false, &why) || !map2d(&mp.w2n, w2, DM, f, 32, true, &why))
         return h->fail(ST_UNSUPPORTED_SHAPE, "%s: %s", who, why.c_str());
-    const int64_t part_floats = 2 * (f / CT) * m * DM + 2 * (m / MT) * f * DM;
+    // every CTA of the grid must be resident at once: CTAs wait for the
+    // partial products of the other CTAs of their token and column blocks
+    const int64_t ctas = (m / MT) * (f / CT);
+    if (ctas > h->num_sms)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "%s: (m/128)*(f/128) = %lld CTAs exceeds the %d SMs", who,
+                       (long long)ctas, h->num_sms);
+    const int64_t part_floats = 4 * ctas * MT * CT;
     float *part = static_cast<float *>(st_scratch(h, SLOT_MLP_PART, sizeof(float) * part_floats));
     if (!part) return ST_NO_MEMORY;
-    MlpArgs g{hout, dhout, part, static_cast<int>(m), static_cast<int>(f), h->d_status};
+    // the counters are left at zero by every launch (the last CTA out of each
+    // group resets its pair); they are zeroed here only when their memory is new
+    const size_t ctl_bytes = sizeof(unsigned) * (2 * (m / MT) + 2 * (f / CT) + 1);
+    unsigned *ctl = static_cast<unsigned *>(st_scratch(h, SLOT_MLP_CTL, ctl_bytes));
+    if (!ctl) return ST_NO_MEMORY;
+    if (ctl != h->mlp_ctl || ctl_bytes > h->mlp_ctl_bytes) {
+        ST_CHECK_CUDA(h, cudaMemsetAsync(ctl, 0, h->slot_bytes[SLOT_MLP_CTL], h->stream));
+        h->mlp_ctl = ctl;
+        h->mlp_ctl_bytes = h->slot_bytes[SLOT_MLP_CTL];
+    }
+    MlpArgs g{hout, dhout, y, dx, dw1, dw2, ctl, part, static_cast<int>(m), static_cast<int>(f), h->d_status};
 
-    static bool attr_done = false;
-    if (!attr_done) {
+    static bool attr_set[64] = {};
+    if (h->device >= 0 && h->device < 64 && !attr_set[h->device]) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_mlp_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        attr_done = true;
+        attr_set[h->device] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(f / CT), static_cast<unsigned>(m / MT));
@@ -398,18 +557,10 @@ extern "C" st_status st_mlp_step_tf32(st_handle *h, const float *x, const float 
     cfg.dynamicSmemBytes = SMEM;
     cfg.stream = h->stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, k_mlp_step, mp, g));
-    st_status s = st_after_launch(h, "k_mlp_step");
-    if (s != ST_OK) return s;
-    const int64_t items = 2 * (m * DM / 4) + 2 * (f * DM / 4);
-    cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((items + 255) / 256, 8LL * h->num_sms)));
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    ST_CHECK_CUDA(h, cudaLaunchKernelEx(&cfg, k_mlp_reduce, static_cast<const float *>(part), y, dx, dw1, dw2,
-                                        static_cast<int>(m), static_cast<int>(f)));
-    return st_after_launch(h, "k_mlp_reduce");
+    return st_after_launch(h, "k_mlp_step");
 }

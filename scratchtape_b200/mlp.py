@@ -63,17 +63,22 @@ def forward_backward_grouped(b: MlpBuffers):
     return b
 
 
-def fused_fits(m, d, dff) -> bool:
-    """Shapes the fused step (forward_backward_fused) takes."""
-    return d == 128 and m % 128 == 0 and dff % 128 == 0
+def fused_fits(m, d, dff, device=None) -> bool:
+    """Shapes the fused step (forward_backward_fused) takes: d == 128, m and
+    dff multiples of 128, and no more 128 x 128 blocks than the GPU has SMs
+    (they all run at once)."""
+    if not (d == 128 and m % 128 == 0 and dff % 128 == 0):
+        return False
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    return (m // 128) * (dff // 128) <= torch.cuda.get_device_properties(dev).multi_processor_count
 
 
 def forward_backward_fused(b: MlpBuffers, write_h: bool = True):
     """The six GEMMs in one fused tcgen05 kernel (st_mlp_step_tf32) plus a
     fixed-order reduction, on torch's current stream: each 128-token block
     makes its own slice of H and dH and uses it at once from TMEM and shared
-    memory.  Needs d == 128 and m, dff multiples of 128.  ``write_h`` False
-    leaves b.h and b.dh unwritten."""
+    memory.  Shapes: ``fused_fits``.  ``write_h`` False leaves b.h and b.dh
+    unwritten."""
     from .device import handle, ptr
     m, d = b.x.shape
     dff = b.w1.shape[1]

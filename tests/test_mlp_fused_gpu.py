@@ -1,5 +1,5 @@
 """The fused MLP layer step (st_mlp_step_tf32: six TF32 GEMMs in one kernel
-plus a fixed-order reduction) against the CPU oracle's tape restatement
+with in-kernel fixed-order reductions) against the CPU oracle's tape restatement
 (src/tape.rs:505-510, :530-534), at the C2 shape and smaller ones; H and dH
 outputs, determinism, graph replay, and the shapes it turns away."""
 import numpy as np
@@ -124,7 +124,7 @@ def test_fused_step_host_api_and_pipeline(dev):
 def test_fused_step_rejects_other_shapes(dev):
     import scratchtape_b200._native as N
     from scratchtape_b200 import mlp
-    for m, d, dff in ((100, 128, 512), (512, 64, 512), (512, 128, 200)):
+    for m, d, dff in ((100, 128, 512), (512, 64, 512), (512, 128, 200), (8192, 128, 4096)):
         b = mlp.MlpBuffers.allocate(m, d, dff, torch.device("cuda:0"))
         with pytest.raises(N.StError) as e:
             mlp.forward_backward_fused(b)
