@@ -52,9 +52,8 @@ C5_IVF = dict(keys=37_000_000, nlist=12288, nprobe=8, nq=16384, clusters=12288, 
 C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
 # DRAM bytes of one k_attn_fwd + one k_attn_bwd launch at C3 from one ncu capture (profiles/attn_c3.md)
 C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
-# DRAM bytes (read + write) of one k_mlp_step launch at C2 from one ncu capture
-# (profiles/mlp_fused_c2.md); None until captured
-C2_FUSED_TRAFFIC = None
+# DRAM bytes (read + write) of one k_mlp_step launch at C2 from one ncu capture (profiles/mlp_fused_c2.md)
+C2_FUSED_TRAFFIC = 4.800256e6 + 5.820416e6
 
 
 def parse_args():
