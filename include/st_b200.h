@@ -348,6 +348,21 @@ ST_API st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const flo
                                    int64_t index_base, int64_t n_units, const int32_t *unit_q,
                                    const int32_t *unit_list, const int64_t *unit_keys, int32_t n_lists,
                                    uint64_t *out_keys);
+/* Host-side planning of that scan for an IVF search (the cell loop of
+ * search_ivf, src/gpu_step/knn/ivf.rs:466-526): probes [nq, nprobe] (host
+ * int32, each query's probed cells), starts [nlist + 1] (host, cell c holds
+ * store rows starts[c] .. starts[c + 1]).  A cell longer than `chunk` keys is
+ * scanned as several chunks, each its own unit and its own list of the
+ * query; chunk <= 0 picks one that gives about two units of work per SM
+ * (n_sms) and at most max_lists lists per query.  Units are (cell chunk, up
+ * to 128 of the queries probing it), longest first.  Call it first with
+ * NULL tables to learn *n_units (and *n_lists, *chunk_used), then with
+ * tables of that many units (unit_q, unit_list [n_units, 128],
+ * unit_keys [n_units, 2]) for st_knn_scan_units.  Needs no handle and no GPU. */
+ST_API st_status st_knn_ivf_units(const int32_t *probes, int64_t nq, int32_t nprobe, const int64_t *starts,
+                                  int32_t nlist, int32_t n_sms, int64_t chunk, int32_t max_lists, int32_t *unit_q,
+                                  int32_t *unit_list, int64_t *unit_keys, int64_t *n_units, int32_t *n_lists,
+                                  int64_t *chunk_used);
 /* out [n, dim] f32 = (u - 1.5) * scale of 2-bit rows (k_dequant, knn.rs:630-643, kept in f32). */
 ST_API st_status st_knn_dequant(st_handle *h, const uint8_t *codes, const float *scales, int64_t n, int32_t dim,
                                 float *out);

@@ -69,6 +69,7 @@ SIGNATURES = {
     "st_gemm_tf32_fixed_scratch": (_st, [_h, ctypes.POINTER(StMat), ctypes.POINTER(StMat), ctypes.POINTER(StMat), _i64,
                                          _i64, _i64, _i64, ctypes.POINTER(StEpilogue)]),
     "st_matmul_host": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_int]),
+    "st_knn_ivf_units": (_st, [_vp, _i64, _i32, _vp, _i32, _i32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "st_mlp_step_tf32": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64]),
     "st_softmax_rows": (_st, [_h, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),

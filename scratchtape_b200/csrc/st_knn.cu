@@ -48,6 +48,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "st_internal.h"
 #include "st_ptx.cuh"
@@ -1810,6 +1811,89 @@ extern "C" st_status st_knn_scan_units(st_handle *h, const uint8_t *codes, const
     if (s != ST_OK) return s;
     k_knn_merge<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(unit_out, 2 * n_lists, nq_pad * KTOP, out_keys);
     return st_after_launch(h, "k_knn_merge");
+}
+
+extern "C" st_status st_knn_ivf_units(const int32_t *probes, int64_t nq, int32_t nprobe, const int64_t *starts,
+                                      int32_t nlist, int32_t n_sms, int64_t chunk, int32_t max_lists, int32_t *unit_q,
+                                      int32_t *unit_list, int64_t *unit_keys, int64_t *n_units, int32_t *n_lists,
+                                      int64_t *chunk_used) {
+    if (!probes || !starts || nq < 1 || nprobe < 1 || nlist < 1 || !n_units || !n_lists || !chunk_used ||
+        nq * nprobe > (1LL << 31))
+        return ST_INVALID_ARG;
+    for (int64_t i = 0; i < nq * nprobe; i++)
+        if (probes[i] < 0 || probes[i] >= nlist) return ST_INVALID_ARG;
+    for (int32_t c = 0; c < nlist; c++)
+        if (starts[c + 1] < starts[c] || starts[c] < 0) return ST_INVALID_ARG;
+    auto size_of = [&](int32_t c) { return starts[c + 1] - starts[c]; };
+    auto nch_of = [&](int32_t c, int64_t ch) { return std::max<int64_t>(1, (size_of(c) + ch - 1) / ch); };
+    auto lists_needed = [&](int64_t ch) {
+        int64_t worst = 0;
+        for (int64_t q = 0; q < nq; q++) {
+            int64_t t = 0;
+            for (int32_t p = 0; p < nprobe; p++) t += nch_of(probes[q * nprobe + p], ch);
+            worst = std::max(worst, t);
+        }
+        return worst;
+    };
+    std::vector<int64_t> count(nlist, 0);  // queries probing each cell
+    for (int64_t i = 0; i < nq * nprobe; i++) count[probes[i]]++;
+    if (chunk <= 0) {
+        // about two units of work per SM: a cell's keys are scanned once per 128 queries probing it
+        int64_t work = 0;
+        for (int32_t c = 0; c < nlist; c++)
+            if (count[c]) work += size_of(c) * ((count[c] + KQ - 1) / KQ);
+        chunk = std::max<int64_t>(16384, (work + 2LL * std::max(1, n_sms) - 1) / (2LL * std::max(1, n_sms)));
+        chunk = (chunk + 255) / 256 * 256;
+        while (lists_needed(chunk) > std::max(1, max_lists)) chunk *= 2;
+    }
+    const int64_t nl = lists_needed(chunk);
+    if (nl > 4096) return ST_UNSUPPORTED_SHAPE;
+    // (cell, chunk) runs in cell order; each (query, probe, chunk) entry joins its run in query order
+    std::vector<int64_t> run0(nlist + 1, 0);
+    for (int32_t c = 0; c < nlist; c++) run0[c + 1] = run0[c] + (count[c] ? nch_of(c, chunk) : 0);
+    const int64_t runs = run0[nlist];
+    std::vector<int64_t> unit0(runs + 1, 0);  // first unit of each run
+    for (int32_t c = 0; c < nlist; c++)
+        for (int64_t j = 0; j < run0[c + 1] - run0[c]; j++)
+            unit0[run0[c] + j + 1] = unit0[run0[c] + j] + (count[c] + KQ - 1) / KQ;
+    const int64_t nu = unit0[runs];
+    *n_units = nu;
+    *n_lists = static_cast<int32_t>(nl);
+    *chunk_used = chunk;
+    if (!unit_q && !unit_list && !unit_keys) return ST_OK;
+    if (!unit_q || !unit_list || !unit_keys) return ST_INVALID_ARG;
+    // unit -> (cell, chunk) and its key range; then the longest-first order
+    std::vector<int64_t> k0(nu), k1(nu);
+    for (int32_t c = 0; c < nlist; c++)
+        for (int64_t j = 0; j < run0[c + 1] - run0[c]; j++) {
+            const int64_t a = starts[c] + j * chunk, b = std::min(starts[c + 1], a + chunk);
+            for (int64_t u = unit0[run0[c] + j]; u < unit0[run0[c] + j + 1]; u++) k0[u] = a, k1[u] = b;
+        }
+    std::vector<int64_t> order(nu), pos(nu);
+    for (int64_t u = 0; u < nu; u++) order[u] = u;
+    std::stable_sort(order.begin(), order.end(), [&](int64_t x, int64_t y) { return k1[x] - k0[x] > k1[y] - k0[y]; });
+    for (int64_t i = 0; i < nu; i++) {
+        pos[order[i]] = i;
+        unit_keys[2 * i] = k0[order[i]];
+        unit_keys[2 * i + 1] = k1[order[i]];
+    }
+    std::fill(unit_q, unit_q + nu * KQ, -1);
+    std::fill(unit_list, unit_list + nu * KQ, 0);
+    std::vector<int64_t> fill(runs, 0);
+    for (int64_t q = 0; q < nq; q++) {
+        int64_t list = 0;
+        for (int32_t p = 0; p < nprobe; p++) {
+            const int32_t c = probes[q * nprobe + p];
+            const int64_t nch = nch_of(c, chunk);
+            for (int64_t j = 0; j < nch; j++, list++) {
+                const int64_t r = run0[c] + j, k = fill[r]++;
+                const int64_t u = pos[unit0[r] + k / KQ];
+                unit_q[u * KQ + k % KQ] = static_cast<int32_t>(q);
+                unit_list[u * KQ + k % KQ] = static_cast<int32_t>(list);
+            }
+        }
+    }
+    return ST_OK;
 }
 
 extern "C" st_status st_knn_topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys,

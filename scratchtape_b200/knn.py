@@ -236,6 +236,29 @@ def ivf_chunk(probes: np.ndarray, starts: np.ndarray, n_sms: int = 148, max_list
         chunk *= 2
 
 
+def ivf_units_native(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int] = None, n_sms: int = 148,
+                     max_lists: int = 64):
+    """ivf_units (with ivf_chunk's choice when chunk is None) in the
+    library's native planner, st_knn_ivf_units: the same tables in the same
+    order, built with counting sorts over the cells.  Returns (unit_q,
+    unit_list, unit_keys, n_lists)."""
+    probes = np.ascontiguousarray(probes, np.int32)
+    starts = np.ascontiguousarray(starts, np.int64)
+    nq, nprobe = probes.shape
+    nu, nl, ch = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int64()
+    args = (probes.ctypes.data_as(ctypes.c_void_p), nq, nprobe, starts.ctypes.data_as(ctypes.c_void_p),
+            len(starts) - 1, n_sms, 0 if chunk is None else int(chunk), max_lists)
+    N.check(None, N.lib.st_knn_ivf_units(*args, None, None, None, ctypes.byref(nu), ctypes.byref(nl),
+                                         ctypes.byref(ch)))
+    uq = np.empty((nu.value, KQ_ROWS), np.int32)
+    ul = np.empty((nu.value, KQ_ROWS), np.int32)
+    uk = np.empty((nu.value, 2), np.int64)
+    N.check(None, N.lib.st_knn_ivf_units(*args, uq.ctypes.data_as(ctypes.c_void_p), ul.ctypes.data_as(ctypes.c_void_p),
+                                         uk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(nu), ctypes.byref(nl),
+                                         ctypes.byref(ch)))
+    return uq, ul, uk, int(nl.value)
+
+
 def scan_units(codes, scales, queries, unit_q, unit_list, unit_keys, n_lists, mode="l2", prec="exact",
                index_base=0, out=None):
     """The fused scan over unit tables (host numpy arrays): sortable keys [nq, 128]."""
@@ -252,6 +275,10 @@ def scan_units(codes, scales, queries, unit_q, unit_list, unit_keys, n_lists, mo
 
 
 KQ_ROWS = 128  # queries per scan unit (the MMA tile's M)
+
+
+def _num_sms(device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
 
 
 class KnnStore:
@@ -500,7 +527,7 @@ class KnnStore:
         q = self._queries(queries, rows)
         iv = self.ivf
         probes = probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
-        uq, ul, uk, n_lists = ivf_units(probes, iv["starts"], ivf_chunk(probes, iv["starts"]))
+        uq, ul, uk, n_lists = ivf_units_native(probes, iv["starts"], n_sms=_num_sms(q.device))
         keys = scan_units(self.codes, self.scales, q, uq, ul, uk, n_lists, mode=mode, prec=prec,
                           index_base=self.first)
         scores, ids = decode(keys, q, KMAX, mode=mode, prec=prec)

@@ -59,3 +59,22 @@ def test_chunked_units_cover_every_key_of_every_probe_once():
             want.update(range(starts[c], starts[c + 1]))
         assert {k for (qq, k) in pairs if qq == q} == want
     assert ivf_chunk(probes, starts, n_sms=4, max_lists=64) % 256 == 0
+
+
+def test_native_planner_matches_the_numpy_tables():
+    """st_knn_ivf_units (the library's host planner) builds the same unit
+    tables, in the same order, as ivf_units, and picks ivf_chunk's chunk."""
+    from scratchtape_b200.knn import ivf_chunk, ivf_units, ivf_units_native
+    rng = np.random.default_rng(3)
+    for nq, nprobe, nlist, big in ((300, 5, 40, 0), (700, 4, 50, 3000), (64, 8, 12, 100000)):
+        probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
+        sizes = rng.integers(0, 60, nlist)
+        sizes[0] = 0
+        sizes[2] = big
+        starts = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+        for chunk in (None, 64, 1000):
+            want = ivf_units(probes, starts, chunk if chunk is not None else ivf_chunk(probes, starts, n_sms=4))
+            got = ivf_units_native(probes, starts, chunk, n_sms=4)
+            assert got[3] == want[3]
+            for a, b in zip(got[:3], want[:3]):
+                assert np.array_equal(a, b)
