@@ -937,6 +937,54 @@ __global__ void k_knn_probe(const float *dots, const float *cnorm, int64_t nq, i
     }
 }
 
+// (v, c) before (w, d) in (distance, cell) order.
+__device__ __forceinline__ bool probe_less(float v, int c, float w, int d) { return v < w || (v == w && c < d); }
+
+// k_knn_probe for nprobe <= PMAX in one pass over the row: each lane keeps
+// its PMAX best (distance, cell) pairs sorted in registers, then nprobe
+// rounds of a warp minimum over the lanes' heads take them in order.  Same
+// results as k_knn_probe (the order is total: distance, then cell).
+template <int PMAX>
+__global__ void k_knn_probe_small(const float *dots, const float *cnorm, int64_t nq, int nl, int nprobe, int32_t *out) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (r >= nq) return;
+    const float *row = dots + r * nl;
+    float lv[PMAX];
+    int li[PMAX];
+#pragma unroll
+    for (int k = 0; k < PMAX; k++) lv[k] = INFINITY, li[k] = 0x7fffffff;
+    for (int c = lane; c < nl; c += 32) {
+        const float v = fmaf(-2.0f, row[c], cnorm[c]);
+        if (probe_less(v, c, lv[PMAX - 1], li[PMAX - 1])) {
+            lv[PMAX - 1] = v, li[PMAX - 1] = c;
+#pragma unroll
+            for (int k = PMAX - 1; k > 0; k--)
+                if (probe_less(lv[k], li[k], lv[k - 1], li[k - 1])) {
+                    const float tv = lv[k];
+                    const int ti = li[k];
+                    lv[k] = lv[k - 1], li[k] = li[k - 1], lv[k - 1] = tv, li[k - 1] = ti;
+                }
+        }
+    }
+    for (int p = 0; p < nprobe; p++) {
+        float best = lv[0];
+        int bi = li[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (probe_less(ov, oi, best, bi)) best = ov, bi = oi;
+        }
+        if (lane == 0) out[r * nprobe + p] = bi < nl ? bi : -1;
+        if (li[0] == bi) {  // the lane holding the winner moves to its next
+#pragma unroll
+            for (int k = 0; k < PMAX - 1; k++) lv[k] = lv[k + 1], li[k] = li[k + 1];
+            lv[PMAX - 1] = INFINITY, li[PMAX - 1] = 0x7fffffff;
+        }
+    }
+}
+
 // dst row i = src row perm[i]; rows of `words` 32-bit words.  A perm entry
 // outside [0, n_src) yields a zero row and a DEV_BAD_ARG status.
 __global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst, const int64_t *perm, int64_t n,
@@ -2005,6 +2053,11 @@ extern "C" st_status st_knn_probe(st_handle *h, const float *dots, const float *
     if (!dots || !cnorm || !out || nq < 1 || nlist < 1 || nprobe < 1 || nprobe > nlist || nprobe > 64)
         return h->fail(ST_INVALID_ARG, "st_knn_probe: bad arguments (1 <= nprobe <= min(nlist, 64))");
     cudaSetDevice(h->device);
+    if (nprobe <= 8) {
+        k_knn_probe_small<8><<<static_cast<unsigned>((nq + 7) / 8), 256, 0, h->stream>>>(dots, cnorm, nq, nlist, nprobe,
+                                                                                         out);
+        return st_after_launch(h, "k_knn_probe_small");
+    }
     k_knn_probe<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, h->stream>>>(dots, cnorm, nq, nlist, nprobe, out);
     return st_after_launch(h, "k_knn_probe");
 }

@@ -39,6 +39,24 @@ def test_nearest_and_probe_match_numpy(dev):
     assert np.array_equal(pr, want)
 
 
+@pytest.mark.parametrize("nprobe", [1, 8, 9, 20])
+def test_probe_ties_and_both_kernels(dev, nprobe):
+    """Duplicated centroids make exact distance ties: every probe count (the
+    one-pass kernel up to 8, the multi-pass one beyond) returns numpy's
+    stable order -- distance, then the lower cell."""
+    import scratchtape_b200.knn as K
+    rng = np.random.default_rng(5)
+    base = rng.standard_normal((150, 64)).astype(np.float32)
+    cent_h = np.concatenate([base, base[::3], base[:40]])  # exact duplicates
+    x = torch.from_numpy(rng.standard_normal((1000, 64)).astype(np.float32)).cuda()
+    cent = torch.from_numpy(cent_h).cuda()
+    cnorm = (cent * cent).sum(1)
+    dots = K._centroid_dots(x, cent).cpu().numpy()
+    dist = cnorm.cpu().numpy()[None, :] - 2 * dots
+    got = K.probe_cells(x, cent, cnorm, nprobe).cpu().numpy()
+    assert np.array_equal(got, np.argsort(dist, axis=1, kind="stable")[:, :nprobe])
+
+
 @pytest.mark.parametrize("mode", ["l2", "dot"])
 def test_probing_all_cells_is_the_flat_search(dev, mode):
     st, rng = _store(6000, 128, 1)
