@@ -182,7 +182,10 @@ ST_API st_status st_gemm_tf32_fixed_scratch(st_handle *h, const st_mat *a, const
  * writing it).  Needs d == 128, m and f multiples of 128, (m/128)*(f/128) no
  * more than the GPU's SMs, 16-byte aligned buffers; returns
  * ST_UNSUPPORTED_SHAPE otherwise (use st_gemm per product then).  Calls on
- * one handle must not overlap on the GPU (they share its scratch). */
+ * one handle must not overlap on the GPU (they share its scratch and its
+ * block counters).  The CTAs wait for each other with bounded waits; a wait
+ * that runs out sets ST_TIMEOUT on the handle and leaves its counters
+ * unusable: destroy that handle and create a new one. */
 ST_API st_status st_mlp_step_tf32(st_handle *h, const float *x, const float *w1, const float *w2, const float *dy,
                                   float *hout, float *y, float *dhout, float *dx, float *dw1, float *dw2, int64_t m,
                                   int64_t d, int64_t f);
