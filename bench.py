@@ -733,7 +733,8 @@ def c5_ivf_pass(device, d, reps=3):
     the device -- so the cells are populated as trained hidden states would
     populate them.  ``wall_ms`` is the public call with host queries in and
     host (distance, value) lists out, probe + host unit tables + scan +
-    merge + decode; ``scan_ms`` the scan + merge launch alone (CUDA events)."""
+    merge + decode, the queries in pinned host memory; ``scan_ms`` the scan +
+    merge launch alone (CUDA events)."""
     import torch
     import scratchtape_b200.knn as K
     cfg = C5_IVF
@@ -762,7 +763,7 @@ def c5_ivf_pass(device, d, reps=3):
     torch.cuda.synchronize(device)
     build_s = time.perf_counter() - t0
     qidx = torch.randint(0, cfg["clusters"], (nq,), generator=g, device=device)
-    qh = (centers[qidx] + cfg["noise"] * torch.randn((nq, d), generator=g, device=device)).cpu().numpy()
+    qh = (centers[qidx] + cfg["noise"] * torch.randn((nq, d), generator=g, device=device)).cpu().pin_memory()
     st.search_ivf(qh, nprobe=nprobe, mode="l2")
     torch.cuda.synchronize(device)
     walls = []
@@ -771,7 +772,7 @@ def c5_ivf_pass(device, d, reps=3):
         sc, vals = st.search_ivf(qh, nprobe=nprobe, mode="l2")
         sc.cpu(), vals.cpu()
         walls.append((time.perf_counter() - t0) * 1e3)
-    q = torch.from_numpy(qh).to(device)
+    q = qh.to(device)
     iv = st.ivf
     probes = K.probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
     uq, ul, uk, n_lists = K.ivf_units(probes, iv["starts"], K.ivf_chunk(probes, iv["starts"]))

@@ -237,11 +237,12 @@ def ivf_chunk(probes: np.ndarray, starts: np.ndarray, n_sms: int = 148, max_list
 
 
 def ivf_units_native(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int] = None, n_sms: int = 148,
-                     max_lists: int = 64):
+                     max_lists: int = 64, reuse: Optional[dict] = None):
     """ivf_units (with ivf_chunk's choice when chunk is None) in the
     library's native planner, st_knn_ivf_units: the same tables in the same
     order, built with counting sorts over the cells.  Returns (unit_q,
-    unit_list, unit_keys, n_lists)."""
+    unit_list, unit_keys, n_lists).  ``reuse``: a dict whose arrays are kept
+    and refilled by later calls (the returned tables are views of them)."""
     probes = np.ascontiguousarray(probes, np.int32)
     starts = np.ascontiguousarray(starts, np.int64)
     nq, nprobe = probes.shape
@@ -250,9 +251,15 @@ def ivf_units_native(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int
             len(starts) - 1, n_sms, 0 if chunk is None else int(chunk), max_lists)
     N.check(None, N.lib.st_knn_ivf_units(*args, None, None, None, ctypes.byref(nu), ctypes.byref(nl),
                                          ctypes.byref(ch)))
-    uq = np.empty((nu.value, KQ_ROWS), np.int32)
-    ul = np.empty((nu.value, KQ_ROWS), np.int32)
-    uk = np.empty((nu.value, 2), np.int64)
+    n = nu.value
+    if reuse is None:
+        reuse = {}
+    if reuse.get("cap", -1) < n:
+        reuse["cap"] = max(n, int(reuse.get("cap", 0) * 1.25))
+        reuse["q"] = np.empty((reuse["cap"], KQ_ROWS), np.int32)
+        reuse["l"] = np.empty((reuse["cap"], KQ_ROWS), np.int32)
+        reuse["k"] = np.empty((reuse["cap"], 2), np.int64)
+    uq, ul, uk = reuse["q"][:n], reuse["l"][:n], reuse["k"][:n]
     N.check(None, N.lib.st_knn_ivf_units(*args, uq.ctypes.data_as(ctypes.c_void_p), ul.ctypes.data_as(ctypes.c_void_p),
                                          uk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(nu), ctypes.byref(nl),
                                          ctypes.byref(ch)))
@@ -527,7 +534,8 @@ class KnnStore:
         q = self._queries(queries, rows)
         iv = self.ivf
         probes = probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
-        uq, ul, uk, n_lists = ivf_units_native(probes, iv["starts"], n_sms=_num_sms(q.device))
+        uq, ul, uk, n_lists = ivf_units_native(probes, iv["starts"], n_sms=_num_sms(q.device),
+                                               reuse=iv.setdefault("plan", {}))
         keys = scan_units(self.codes, self.scales, q, uq, ul, uk, n_lists, mode=mode, prec=prec,
                           index_base=self.first)
         scores, ids = decode(keys, q, KMAX, mode=mode, prec=prec)
