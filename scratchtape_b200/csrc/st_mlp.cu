@@ -1,5 +1,6 @@
 // st_mlp.cu -- one Linear -> ReLU -> Linear layer (no bias), forward and
-// backward, as one tcgen05 kernel plus one fixed-order reduction.
+// backward, as one tcgen05 kernel whose CTAs also add up each other's partial
+// products in a fixed order.
 //
 // The six TF32 GEMMs of the layer (src/tape.rs:505-510 for the MatMul arm,
 // :530-534 for ReLU's mask; the C2 configuration of the MLP step):
@@ -11,7 +12,7 @@
 // through TMEM and shared memory instead of through global memory:
 //   P1  acc_H = X_rb W1[:, cc],  acc_G = dY_rb W2[cc, :]^T   (K = D, streamed)
 //   E1  H = relu(acc_H), dH = acc_G * (H > 0): back into TMEM (the A operand of
-//       P2), transposed into shared memory (an operand of P3), and to H / dH
+//       P2) and, transposed, into shared memory (an operand of P3)
 //   P2  Y_p = H W2[cc, :],  dX_p = dH W1[:, cc]^T           (A from TMEM)
 //   P3  dW2_p = H^T dY_rb,  dW1_p = X_rb^T dH               (K = 128 tokens)
 //   E3  H and dH to global memory from their transposed shared-memory tiles
