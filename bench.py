@@ -169,6 +169,20 @@ def c2_flops():
     return 6 * 2 * C2["m"] * C2["d"] * C2["dff"]
 
 
+def c2_bytes():
+    """The C2 step's algorithmic bytes, the per-step figure of the north star's
+    measurement table: six GEMMs, each reading its two f32 operands and
+    writing its f32 result (M.d + d.F + M.F elements)."""
+    return 6 * 4 * (C2["m"] * C2["d"] + C2["d"] * C2["dff"] + C2["m"] * C2["dff"])
+
+
+def c2_unique_bytes():
+    """What the fused step must move at least: X, dY, W1, W2 in; H, dH, Y, dX,
+    dW1, dW2 out (f32)."""
+    m, d, f = C2["m"], C2["d"], C2["dff"]
+    return 4 * (2 * m * d + 2 * d * f + 2 * m * f + 2 * m * d + 2 * d * f)
+
+
 def cpu_step_c2(x, w1, w2, dy, threads):
     """One C2 step on the CPU oracle: the tape's six matmuls (NT/TN through
     explicit transposes, src/tape.rs:505-510), ReLU and its mask."""
@@ -331,7 +345,7 @@ def run_ours(args):
     # operands and results) / duration: of the fused kernel and its reduction
     # together, or of each of the six GEMMs alone
     per_bytes = mlp.gemm_bytes(m, d, dff)
-    bytes_total = float(sum(per_bytes))
+    bytes_total = float(c2_bytes())
     gemm_ms = []
     if fused:
         fused_ms = replay_ms(graph)
@@ -421,8 +435,10 @@ def run_ours(args):
             "roofline": ({"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                           "frac": achieved / hbm, "traffic": C2_FUSED_TRAFFIC, "peak_source": peak_src,
                           "traffic_note": "DRAM read+write of one k_mlp_step launch from one ncu capture "
-                                          "(profiles/mlp_fused_c2.md); algorithmic bytes are the six GEMMs' f32 "
-                                          "operands and results (sum of per_gemm_bytes)",
+                                          "(profiles/mlp_fused_c2.md); algorithmic bytes: the six GEMMs' f32 "
+                                          "operands and results, 6 x 10.75 MB",
+                          "unique_io_bytes": c2_unique_bytes(),
+                          "unique_io_frac": c2_unique_bytes() / (fused_ms / 1e3) / 1e9 / hbm,
                           "kernel": "k_mlp_step (one cooperative launch, reductions inside)",
                           "step_us": round(fused_ms * 1e3, 2), "algorithmic_bytes": bytes_total,
                           "per_gemm_bytes": per_bytes,
@@ -432,8 +448,8 @@ def run_ours(args):
                          {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                           "traffic": C2_TRAFFIC_PER_LAUNCH, "peak_source": peak_src,
                           "traffic_note": "mean DRAM read+write per k_gemm_tf32 launch over the three launches of "
-                                          "one ncu capture (H, Y, dW2); algorithmic bytes per launch are "
-                                          "per_gemm_bytes",
+                                          "one ncu capture (H, Y, dW2); algorithmic bytes: the six GEMMs' f32 "
+                                          "operands and results, 6 x 10.75 MB (per_gemm_bytes adds the mask read)",
                           "kernel": "k_gemm_tf32 (+k_splitk_reduce)",
                           "per_gemm_us": [round(t * 1e3, 2) for t in gemm_ms],
                           "per_gemm_bytes": per_bytes,
