@@ -249,8 +249,12 @@ def ivf_units_native(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int
     nu, nl, ch = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int64()
     args = (probes.ctypes.data_as(ctypes.c_void_p), nq, nprobe, starts.ctypes.data_as(ctypes.c_void_p),
             len(starts) - 1, n_sms, 0 if chunk is None else int(chunk), max_lists)
-    N.check(None, N.lib.st_knn_ivf_units(*args, None, None, None, ctypes.byref(nu), ctypes.byref(nl),
-                                         ctypes.byref(ch)))
+    def planned(status):
+        if status != N.ST_OK:
+            raise N.StError(status, "st_knn_ivf_units: probes must name cells < len(starts) - 1, starts must not "
+                                    "decrease, and a query may need at most 4096 lists")
+
+    planned(N.lib.st_knn_ivf_units(*args, None, None, None, ctypes.byref(nu), ctypes.byref(nl), ctypes.byref(ch)))
     n = nu.value
     if reuse is None:
         reuse = {}
@@ -260,9 +264,9 @@ def ivf_units_native(probes: np.ndarray, starts: np.ndarray, chunk: Optional[int
         reuse["l"] = np.empty((reuse["cap"], KQ_ROWS), np.int32)
         reuse["k"] = np.empty((reuse["cap"], 2), np.int64)
     uq, ul, uk = reuse["q"][:n], reuse["l"][:n], reuse["k"][:n]
-    N.check(None, N.lib.st_knn_ivf_units(*args, uq.ctypes.data_as(ctypes.c_void_p), ul.ctypes.data_as(ctypes.c_void_p),
-                                         uk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(nu), ctypes.byref(nl),
-                                         ctypes.byref(ch)))
+    planned(N.lib.st_knn_ivf_units(*args, uq.ctypes.data_as(ctypes.c_void_p), ul.ctypes.data_as(ctypes.c_void_p),
+                                   uk.ctypes.data_as(ctypes.c_void_p), ctypes.byref(nu), ctypes.byref(nl),
+                                   ctypes.byref(ch)))
     return uq, ul, uk, int(nl.value)
 
 

@@ -78,3 +78,20 @@ def test_native_planner_matches_the_numpy_tables():
             assert got[3] == want[3]
             for a, b in zip(got[:3], want[:3]):
                 assert np.array_equal(a, b)
+
+
+def test_native_planner_rejects_bad_tables():
+    """A probe naming a cell that does not exist, or cell starts that go
+    backwards, come back as ST_INVALID_ARG before anything is planned."""
+    import pytest
+    import scratchtape_b200._native as N
+    from scratchtape_b200.knn import ivf_units_native
+    starts = np.array([0, 10, 25, 40], np.int64)
+    good = np.array([[0, 2], [1, 0]], np.int32)
+    assert ivf_units_native(good, starts)[3] == 2
+    for probes, st in ((np.array([[0, 3]], np.int32), starts),
+                       (np.array([[0, -1]], np.int32), starts),
+                       (good, np.array([0, 10, 5, 40], np.int64))):
+        with pytest.raises(N.StError) as e:
+            ivf_units_native(probes, st)
+        assert e.value.status == N.ST_INVALID_ARG
