@@ -335,10 +335,6 @@ ST_API st_status st_knn_decode(st_handle *h, const uint64_t *keys, const float *
  * norms [n] (sum of f16-rounded squares; may be NULL). */
 ST_API st_status st_knn_quantize(st_handle *h, const float *keys, int64_t n, int32_t dim, uint8_t *codes,
                                  float *scales, float *norms);
-/* Synthetic keys (benchmark and tests): codes uniform on 0..3 and scale =
- * |N(0,1)|, from a counter-based hash of (seed, first_key + row), so each
- * shard makes its own rows independently.  No reference counterpart (the
- * reference builds keys from trained hidden states). */
 /* The fused scan over a table of work units -- the IVF search of
  * src/gpu_step/knn/ivf.rs:466-690 (search_ivf / scan_group): unit u scans
  * store rows unit_keys[2u] .. unit_keys[2u + 1] (a cell) for the queries
@@ -385,6 +381,10 @@ ST_API st_status st_knn_probe(st_handle *h, const float *dots, const float *cnor
 ST_API st_status st_gather_rows(st_handle *h, const void *src, int64_t n_src, void *dst, const int64_t *perm,
                                 int64_t n, int64_t row_bytes);
 
+/* Synthetic keys (benchmark and tests): codes uniform on 0..3 and scale =
+ * |N(0,1)|, from a counter-based hash of (seed, first_key + row), so each
+ * shard makes its own rows independently.  No reference counterpart (the
+ * reference builds keys from trained hidden states). */
 ST_API st_status st_knn_synth_keys(st_handle *h, uint8_t *codes, float *scales, int64_t n, int32_t dim, uint64_t seed,
                                    int64_t first_key);
 
