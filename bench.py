@@ -791,7 +791,8 @@ def c5_ivf_pass(device, d, reps=3):
     q = qh.to(device)
     iv = st.ivf
     probes = K.probe_cells(q, iv["cent"], iv["cnorm"], nprobe).cpu().numpy()
-    uq, ul, uk, n_lists = K.ivf_units(probes, iv["starts"], K.ivf_chunk(probes, iv["starts"]))
+    uq, ul, uk, n_lists = K.ivf_units_native(probes, iv["starts"],
+                                             n_sms=torch.cuda.get_device_properties(device).multi_processor_count)
     out = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
     K.scan_units(st.codes, st.scales, q, uq, ul, uk, n_lists, mode="l2", out=out)
     evs = []

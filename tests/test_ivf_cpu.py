@@ -1,9 +1,10 @@
-"""Host side of the IVF search: the unit tables handed to the scan."""
+"""Host side of the IVF search: the unit tables handed to the scan -- the
+numpy restatement's properties, and the native planner against it."""
 import numpy as np
 
 
 def test_unit_tables_cover_every_probe_once():
-    from scratchtape_b200.knn import ivf_units
+    from ivf_plan_numpy import ivf_units
     rng = np.random.default_rng(0)
     nq, nprobe, nlist = 300, 5, 40
     probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
@@ -30,7 +31,7 @@ def test_chunked_units_cover_every_key_of_every_probe_once():
     """Cells longer than the chunk become several units, each a list of its
     own: every (query, probed key) pair is scanned exactly once, and each
     query's lists are distinct and below n_lists."""
-    from scratchtape_b200.knn import ivf_chunk, ivf_units
+    from ivf_plan_numpy import ivf_chunk, ivf_units
     rng = np.random.default_rng(1)
     nq, nprobe, nlist = 200, 4, 30
     # 150 queries probe the crowded cell 3 first, the rest of each row distinct
@@ -64,7 +65,8 @@ def test_chunked_units_cover_every_key_of_every_probe_once():
 def test_native_planner_matches_the_numpy_tables():
     """st_knn_ivf_units (the library's host planner) builds the same unit
     tables, in the same order, as ivf_units, and picks ivf_chunk's chunk."""
-    from scratchtape_b200.knn import ivf_chunk, ivf_units, ivf_units_native
+    from ivf_plan_numpy import ivf_chunk, ivf_units
+    from scratchtape_b200.knn import ivf_units_native
     rng = np.random.default_rng(3)
     for nq, nprobe, nlist, big in ((300, 5, 40, 0), (700, 4, 50, 3000), (64, 8, 12, 100000)):
         probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
@@ -72,8 +74,9 @@ def test_native_planner_matches_the_numpy_tables():
         sizes[0] = 0
         sizes[2] = big
         starts = np.r_[0, np.cumsum(sizes)].astype(np.int64)
-        for chunk in (None, 64, 1000):
-            want = ivf_units(probes, starts, chunk if chunk is not None else ivf_chunk(probes, starts, n_sms=4))
+        for chunk in (None, 64, 1000, 1 << 40):
+            # native None: the automatic chunk; 1 << 40: longer than any cell, the numpy planner's whole cells
+            want = ivf_units(probes, starts, {None: ivf_chunk(probes, starts, n_sms=4), 1 << 40: None}.get(chunk, chunk))
             got = ivf_units_native(probes, starts, chunk, n_sms=4)
             assert got[3] == want[3]
             for a, b in zip(got[:3], want[:3]):

@@ -78,8 +78,8 @@ def test_chunked_units_match_whole_cells(dev, mode):
     q = torch.from_numpy(rng.standard_normal((300, 128)).astype(np.float32)).cuda()
     probes = K.probe_cells(q, st.ivf["cent"], st.ivf["cnorm"], 3).cpu().numpy()
     want = None
-    for chunk in (None, 1024, 256):
-        uq, ul, uk, nl = K.ivf_units(probes, st.ivf["starts"], chunk)
+    for chunk in (1 << 40, 1024, 256):  # the first: longer than any cell, so whole cells
+        uq, ul, uk, nl = K.ivf_units_native(probes, st.ivf["starts"], chunk)
         got = K.scan_units(st.codes, st.scales, q, uq, ul, uk, nl, mode=mode).cpu()
         if want is None:
             want = got
