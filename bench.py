@@ -46,14 +46,12 @@ C5 = dict(keys=1 << 27, d=256, nq=4096, k=128)
 # The reference's IVF search as it quotes it (16384 queries x 8 probes over a
 # 37M-key store, docs/tiers_design.md:1468; 12288 cells, README.md:76-85)
 C5_IVF = dict(keys=37_000_000, nlist=12288, nprobe=8, nq=16384, clusters=12288, noise=0.5)
-# dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the C2
-# step, averaged over its launches, from profiles/gemm_tf32_c2.md (ncu, 1 pass).
-# DRAM bytes (read + write) per k_gemm_tf32 launch of the C2 step from one ncu capture (profiles/
-# gemm_tf32_c2.md): H = relu(X W1) 2.43 MB, Y = H W2 8.72 MB, dW2 = H^T dY 10.56 MB (writes stay in L2); the mean
+# dram__bytes_read.sum + dram__bytes_write.sum per k_gemm_tf32 launch of the six-launch C2 step, from one ncu
+# capture: H = relu(X W1) 2.43 MB, Y = H W2 8.72 MB, dW2 = H^T dY 10.56 MB (writes stay in L2); the mean
 C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
-# DRAM bytes of one k_attn_fwd + one k_attn_bwd launch at C3 from one ncu capture (profiles/attn_c3.md)
+# DRAM bytes (read + write) of one k_attn_fwd + one k_attn_bwd launch at C3, from one ncu capture
 C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
-# DRAM bytes (read + write) of one k_mlp_step launch at C2 from one ncu capture (profiles/mlp_fused_c2.md)
+# DRAM bytes (read + write) of one k_mlp_step launch at C2, from one ncu capture
 C2_FUSED_TRAFFIC = 4.800256e6 + 5.820416e6
 
 
