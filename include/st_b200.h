@@ -160,8 +160,10 @@ ST_API st_status st_gemm_group(st_handle *h, const st_group_gemm *gemms, int32_t
  * Limits: batch * m * n <= 1,048,576 output elements, k >= 1, f32 operands
  * that TMA can describe (16-byte aligned starts and rows); beyond them the
  * call returns ST_UNSUPPORTED_SHAPE (bad arguments: ST_INVALID_ARG) and
- * launches nothing.  Errors are reported by the return value only
- * (st_last_error is not updated).  The first call on each device looks up the
+ * launches nothing.  Argument and shape refusals come back as the return
+ * value only (st_last_error keeps its old text); a launch that fails returns
+ * ST_CUDA_ERROR and also sets st_last_error; a device-side wait that runs out
+ * is reported later, by st_sync (ST_TIMEOUT).  The first call on each device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before
  * any stream capture.  All calls share the one array and it keeps the last
  * call's contents: calls that overlap on the GPU (other streams, other host

@@ -1886,13 +1886,22 @@ extern "C" st_status st_knn_ivf_units(const int32_t *probes, int64_t nq, int32_t
     std::vector<int64_t> count(nlist, 0);  // queries probing each cell
     for (int64_t i = 0; i < nq * nprobe; i++) count[probes[i]]++;
     if (chunk <= 0) {
+        // every probe is at least one list of its query, so fewer than nprobe
+        // lists per query cannot be met by any chunk size
+        if (max_lists < nprobe) return ST_INVALID_ARG;
         // about two units of work per SM: a cell's keys are scanned once per 128 queries probing it
-        int64_t work = 0;
+        int64_t work = 0, largest = 1;
         for (int32_t c = 0; c < nlist; c++)
-            if (count[c]) work += size_of(c) * ((count[c] + KQ - 1) / KQ);
+            if (count[c]) {
+                work += size_of(c) * ((count[c] + KQ - 1) / KQ);
+                largest = std::max(largest, size_of(c));
+            }
         chunk = std::max<int64_t>(16384, (work + 2LL * std::max(1, n_sms) - 1) / (2LL * std::max(1, n_sms)));
         chunk = (chunk + 255) / 256 * 256;
-        while (lists_needed(chunk) > std::max(1, max_lists)) chunk *= 2;
+        // once a chunk holds the largest probed cell each probe is one list
+        // (nprobe <= max_lists), so the doubling stops there at the latest
+        while (lists_needed(chunk) > max_lists && chunk < largest) chunk *= 2;
+        if (lists_needed(chunk) > max_lists) return ST_UNSUPPORTED_SHAPE;
     }
     const int64_t nl = lists_needed(chunk);
     if (nl > 4096) return ST_UNSUPPORTED_SHAPE;

@@ -251,6 +251,7 @@ class KnnStore:
         self.norms = torch.empty(0, dtype=torch.float32, device=self.device)
         self.vals = torch.empty(0, dtype=torch.int32, device=self.device)
         self.first = 0  # global index of the first key (a loaded shard)
+        self.f16 = 1    # the .mem header's f16 flag: kept from a loaded file, written back by save
         self._pending = []
         self._pending_vals = []
 
@@ -318,7 +319,8 @@ class KnnStore:
         from .memfile import write_mem
         self.finish()
         write_mem(path, key, extra, self.d, self.tile, self.codes.cpu().numpy(), self.scales.cpu().numpy(),
-                  self.norms.cpu().numpy(), self.vals.cpu().numpy().astype(np.float32), ivf=self._ivf_section())
+                  self.norms.cpu().numpy(), self.vals.cpu().numpy().astype(np.float32), ivf=self._ivf_section(),
+                  f16=self.f16)
 
     def _ivf_section(self):
         """The IVF part of a .mem file (cache.rs:54-70): centroids as f16
@@ -401,6 +403,7 @@ class KnnStore:
             store.norms = torch.cat([p[1][2] for p in parts])
             store.vals = torch.cat([p[1][3] for p in parts]).to(torch.int32)
         store.first = meta["first"]
+        store.f16 = int(meta["f16"])
         store.ivf_raw = meta["ivf"]
         if meta["ivf"] is not None and rows is None:
             store._restore_ivf(meta["ivf"])  # a shard keeps only the raw section

@@ -53,10 +53,14 @@ def _get_bytes(f):
 
 
 def write_mem(path, key: str, extra: int, d: int, tile: int, codes: np.ndarray, scales: np.ndarray,
-              norms: np.ndarray, vals: np.ndarray, kbits: int = 2, ivf=None):
+              norms: np.ndarray, vals: np.ndarray, kbits: int = 2, ivf=None, f16: int = 1):
     """Writes a 2-bit store (host arrays: codes u8 [n, d*kbits/8], scales /
     norms / vals [n]) in tiles of `tile` keys, through a temporary file so a
-    crash never leaves a half-written cache (cache.rs:35-78)."""
+    crash never leaves a half-written cache (cache.rs:35-78).  ``f16`` is the
+    header's f16 flag, written as given (a store read from a file passes the
+    flag it was read with, so a re-save keeps it).  The temporary file is the
+    path with its extension replaced by ``.part``, as the reference's
+    ``path.with_extension("part")`` names it."""
     n = int(codes.shape[0])
     kb = d * kbits // 8
     codes = np.ascontiguousarray(codes, dtype=np.uint8).reshape(n, kb)
@@ -64,11 +68,11 @@ def write_mem(path, key: str, extra: int, d: int, tile: int, codes: np.ndarray, 
     norms = np.asarray(norms, dtype=np.float32).reshape(n)
     vals = np.asarray(vals, dtype=np.float32).reshape(n)
     ntiles = (n + tile - 1) // tile
-    tmp = os.fspath(path) + ".part"
+    tmp = os.path.splitext(os.fspath(path))[0] + ".part"
     with open(tmp, "wb") as f:
         _put(f, MAGIC)
         _put_bytes(f, key.encode())
-        for x in (extra, d, tile, 1, kbits, ntiles):
+        for x in (extra, d, tile, int(f16), kbits, ntiles):
             _put(f, x)
         for t in range(ntiles):
             a, b = t * tile, min(n, (t + 1) * tile)
@@ -171,7 +175,7 @@ def read_mem(path, key: str, rows=None, on_tile=None):
                    "norm": np.frombuffer(_get_bytes(f), np.float32).copy(), "cells": []}
             for _ in range(nlist):
                 ivf["cells"].append([tuple(_get(f) for _ in range(4)) for _ in range(_get(f))])
-        return {"extra": extra, "d": d, "tile": tile, "kbits": kbits, "n": total,
+        return {"extra": extra, "d": d, "tile": tile, "f16": f16, "kbits": kbits, "n": total,
                 "first": min(lo, total), "ivf": ivf}
     finally:
         f.close()

@@ -98,3 +98,23 @@ def test_native_planner_rejects_bad_tables():
         with pytest.raises(N.StError) as e:
             ivf_units_native(probes, st)
         assert e.value.status == N.ST_INVALID_ARG
+
+
+def test_native_planner_rejects_more_probes_than_lists():
+    """Every probe is at least one list of its query: asking the automatic
+    chunk for fewer lists per query than probes is refused with
+    ST_INVALID_ARG (it used to double the chunk without end)."""
+    import pytest
+    import scratchtape_b200._native as N
+    from scratchtape_b200.knn import ivf_units_native
+    rng = np.random.default_rng(9)
+    nq, nprobe, nlist = 50, 8, 20
+    probes = np.stack([rng.choice(nlist, nprobe, replace=False) for _ in range(nq)]).astype(np.int32)
+    starts = np.r_[0, np.cumsum(rng.integers(1, 40, nlist))].astype(np.int64)
+    for max_lists in (0, 1, nprobe - 1):
+        with pytest.raises(N.StError) as e:
+            ivf_units_native(probes, starts, None, n_sms=4, max_lists=max_lists)
+        assert e.value.status == N.ST_INVALID_ARG
+    # exactly nprobe lists: every probed cell fits one chunk
+    uq, ul, uk, n_lists = ivf_units_native(probes, starts, None, n_sms=4, max_lists=nprobe)
+    assert n_lists == nprobe

@@ -133,3 +133,21 @@ def test_store_ivf_section_restores_cells(tmp_path):
     st3.codes, st3.scales = st.codes, st.scales
     st3._restore_ivf(raw)
     assert getattr(st3, "ivf", None) is None
+
+
+def test_f16_flag_round_trips_and_temp_name(tmp_path):
+    """The header's f16 flag is written as given and read back (a store that
+    was loaded re-saves with the flag it came with), and the temporary file is
+    named as path.with_extension("part") names it (cache.rs:36-41): the
+    extension replaced, and gone once the write is complete."""
+    from scratchtape_b200.memfile import read_header, read_mem, write_mem
+    n, d, tile = 100, 64, 64
+    codes, scales, norms, vals = _data(n, d, seed=4)
+    for flag in (0, 1):
+        p = tmp_path / ("f%d.mem" % flag)
+        write_mem(p, "k", 3, d, tile, codes, scales, norms, vals, f16=flag)
+        with open(p, "rb") as f:
+            assert read_header(f, "k")[3] == flag
+        assert read_mem(p, "k")["f16"] == flag
+        assert not (tmp_path / ("f%d.part" % flag)).exists()
+        assert not (tmp_path / ("f%d.mem.part" % flag)).exists()

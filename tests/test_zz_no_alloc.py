@@ -72,6 +72,72 @@ def test_fixed_scratch_matches_st_gemm_twice(dev, shape):
         N.lib.st_destroy(h)
 
 
+def _call_both(h, a, b, want, got, batch, m, k, n, ta, tb, strides, epi):
+    """st_gemm into `want`, then the fixed-scratch entry point into `got`,
+    same operands and epilogue; checks the pool did not grow."""
+    import scratchtape_b200._native as N
+    sa, sb, sc = strides
+    mk = lambda t, tr, st: N.StMat(t.data_ptr(), 0, st, 0, 0, 1, int(tr), N.ST_F32, 0)
+    assert N.lib.st_gemm(h, ctypes.byref(mk(a, ta, sa)), ctypes.byref(mk(b, tb, sb)), ctypes.byref(mk(want, 0, sc)),
+                         batch, m, k, n, ctypes.byref(epi) if epi else None, N.PREC_TF32) == N.ST_OK
+    assert N.lib.st_sync(h) == N.ST_OK
+    pool_before = N.lib.st_scratch_bytes(h)
+    assert N.lib.st_gemm_tf32_fixed_scratch(h, ctypes.byref(mk(a, ta, sa)), ctypes.byref(mk(b, tb, sb)),
+                                            ctypes.byref(mk(got, 0, sc)), batch, m, k, n,
+                                            ctypes.byref(epi) if epi else None) == N.ST_OK
+    assert N.lib.st_sync(h) == N.ST_OK
+    assert N.lib.st_scratch_bytes(h) == pool_before
+
+
+def test_fixed_scratch_batched_split_matches_st_gemm_twice(dev):
+    """batch 4 of 128 x 4096 x 128: few tiles, so the k dimension splits and
+    each batch's partials sit at their own offset of the fixed array."""
+    batch, m, k, n = 4, 128, 4096, 128
+    h = _fresh_handle()
+    try:
+        for call in range(2):
+            g = torch.Generator(device="cuda").manual_seed(7 + call)
+            a = torch.randn((batch, m, k), device="cuda", generator=g)
+            b = torch.randn((batch, k, n), device="cuda", generator=g)
+            want = torch.empty((batch, m, n), device="cuda")
+            got = torch.full((batch, m, n), float("nan"), device="cuda")
+            _call_both(h, a, b, want, got, batch, m, k, n, False, False, (m * k, k * n, m * n), None)
+            assert torch.isfinite(got).all()
+            scale = want.abs().max().item()
+            assert (got - want).abs().max().item() <= TF32_TOL * scale
+            ref = a.double() @ b.double()
+            assert (got.double() - ref).abs().max().item() <= TF32_TOL * ref.abs().max().item()
+    finally:
+        import scratchtape_b200._native as N
+        N.lib.st_destroy(h)
+
+
+def test_fixed_scratch_split_with_bias_and_accumulate(dev):
+    """A split-k call whose reduction applies the epilogue: + bias[col], then
+    + the value already in out (accumulate)."""
+    import scratchtape_b200._native as N
+    m, k, n = 512, 4096, 128  # dW-like: TN, 16 splits
+    h = _fresh_handle()
+    try:
+        for call in range(2):
+            g = torch.Generator(device="cuda").manual_seed(31 + call)
+            a = torch.randn((k, m), device="cuda", generator=g)
+            b = torch.randn((k, n), device="cuda", generator=g)
+            bias = torch.randn(n, device="cuda", generator=g)
+            prior = torch.randn((m, n), device="cuda", generator=g)
+            want, got = prior.clone(), prior.clone()
+            epi = N.StEpilogue()
+            epi.bias = bias.data_ptr()
+            epi.accumulate = 1
+            _call_both(h, a, b, want, got, 1, m, k, n, True, False, (0, 0, 0), epi)
+            scale = want.abs().max().item()
+            assert (got - want).abs().max().item() <= TF32_TOL * scale
+            ref = a.double().T @ b.double() + bias.double() + prior.double()
+            assert (got.double() - ref).abs().max().item() <= TF32_TOL * ref.abs().max().item()
+    finally:
+        N.lib.st_destroy(h)
+
+
 def test_fixed_scratch_rejects_outputs_beyond_its_array(dev):
     import scratchtape_b200._native as N
     h = _fresh_handle()
