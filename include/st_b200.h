@@ -281,6 +281,67 @@ ST_API st_status st_adam(st_handle *h, float *p, const float *g, float *m, float
 ST_API st_status st_adam_dev(st_handle *h, float *p, const float *g, float *m, float *v, int64_t n, int32_t *step,
                              float lr, float beta1, float beta2, float eps);
 
+/* ---- device optimiser, model average, dropout ---------------------------- */
+
+/* p -= lr * g over n parameters (device f32).  Replaces DeviceParams::sgd
+ * (src/gpu_step/mod.rs:153-157, k_sgd :232-238); same f32 operations. */
+ST_API st_status st_sgd(st_handle *h, float *p, const float *g, int64_t n, float lr);
+/* Heavy-ball momentum: with mask (may be NULL) first p *= 1 - shrink * mask,
+ * then v = mu * v + g; p -= lr * v (v: device f32 [n], zero at the start).
+ * Replaces DeviceParams::momentum (mod.rs:159-166, k_momentum :240-251). */
+ST_API st_status st_momentum(st_handle *h, float *p, const float *g, float *v, const float *mask, int64_t n, float lr,
+                             float mu, float shrink);
+/* p *= 1 - shrink * mask (mask 0 or 1 per parameter).  Replaces
+ * DeviceParams::decay (mod.rs:168-174, k_decay :253-259). */
+ST_API st_status st_decay(st_handle *h, float *p, const float *mask, int64_t n, float shrink);
+/* models consecutive parameter vectors of stride floats on one device, split
+ * into consecutive groups of `group`: every model becomes its group's mean
+ * (summed in model order, divided by group).  Replaces
+ * DeviceParams::average_models / average_groups (mod.rs:182-195,
+ * k_average_models :261-275). */
+ST_API st_status st_average_models(st_handle *h, float *p, int64_t stride, int32_t models, int32_t group);
+/* y = x / (1 - rate) where lowbias32(i + seed * 0x9e3779b9) >= rate * 2^32,
+ * else 0 (n < 2^32, 0 <= rate < 1).  The same call on dy with the same seed is
+ * dropout's backward.  Replaces gpu_step::tape::dropout
+ * (src/gpu_step/tape.rs:526-534, k_dropout :557-568); bit-identical mask. */
+ST_API st_status st_dropout(st_handle *h, const float *x, float *y, int64_t n, float rate, uint32_t seed);
+/* dx = dropout(dy) where relu_y > 0, else 0: dropout's backward fused with
+ * ReLU's (tape.rs:536-543, k_dropout_relu_bwd :570-582). */
+ST_API st_status st_dropout_relu_bwd(st_handle *h, const float *dy, const float *relu_y, float *dx, int64_t n,
+                                     float rate, uint32_t seed);
+
+/* ---- across GPUs: NCCL over NVLink ------------------------------------------ */
+/* NCCL is loaded at run time (libnccl.so.2, the process's own copy when one
+ * is loaded); without it these return ST_NCCL_ERROR.  `comm` is an
+ * ncclComm_t -- the host's own, or one from st_nccl_comm_init. */
+
+/* 128 bytes of an ncclUniqueId, made on one rank and sent to the others by
+ * the host's own channel. */
+ST_API st_status st_nccl_unique_id(uint8_t *out);
+/* ncclCommInitRank on `device` (made current): every rank calls it with the
+ * same id; it returns once all nranks have joined. */
+ST_API st_status st_nccl_comm_init(int32_t nranks, int32_t rank, const uint8_t *unique_id, int32_t device,
+                                   void **comm_out);
+ST_API st_status st_nccl_comm_destroy(void *comm);
+/* Local-SGD model average across ranks: p (device f32 [n], the flat
+ * parameters) becomes the mean over the communicator's ranks -- an in-place
+ * sum all-reduce on the handle's stream, then p / world.  Replaces
+ * DeviceParams::average_models (src/gpu_step/mod.rs:182-195) across GPUs, as
+ * the training driver calls it every sync_every steps
+ * (examples/tiny_lm/fused_models_check.rs:394). */
+ST_API st_status st_avg_params(st_handle *h, float *p, int64_t n, void *comm);
+/* st_knn_search over a key set split by rows across the communicator's
+ * ranks: this rank holds rows index_base .. index_base + n_local - 1 (codes,
+ * scales as st_knn_search; n_local may be 0) and every rank passes the same
+ * queries.  Each rank scans its shard, the per-query best-128 lists are
+ * all-gathered over NCCL and merged, and every rank gets the global best k
+ * (out_scores / out_ids as st_knn_search, ids global).  Replaces
+ * k_sort_lists + k_merge_parts (src/gpu_step/knn.rs:661-715) across GPUs. */
+ST_API st_status st_knn_search_sharded(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_local,
+                                       int32_t dim, const float *queries, int64_t nq, int32_t k, int32_t mode,
+                                       int32_t prec, int64_t index_base, void *comm, float *out_scores,
+                                       int64_t *out_ids);
+
 /* ---- kNN memory: 2-bit key scan fused with top-k ------------------------- */
 
 /* Ranking modes (src/gpu_step/knn.rs:5, :522-532, :855).

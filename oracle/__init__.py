@@ -67,6 +67,12 @@ def lib():
             "orc_powi": (_f32, [_f32, _int]),
             "orc_adam": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _int, _f32, _f32, _f32, _f32]),
             "orc_average_models": (None, [_f32p, _i64, _i64]),
+            "orc_sgd": (None, [_f32p, _f32p, _i64, _f32]),
+            "orc_momentum": (None, [_f32p, _f32p, _f32p, _f32p, _i64, _f32, _f32, _f32]),
+            "orc_decay": (None, [_f32p, _f32p, _i64, _f32]),
+            "orc_average_groups": (None, [_f32p, _i64, _i64, _i64]),
+            "orc_dropout_bits": (ctypes.c_uint32, [ctypes.c_uint32, ctypes.c_uint32]),
+            "orc_dropout": (None, [_f32p, _f32p, _f32p, _i64, _f32, ctypes.c_uint32]),
             "orc_round_f16": (_f32, [_f32]),
             "orc_quantize_rows": (None, [_f32p, _i64, _i64, _int, _u8p, _f32p, _f32p]),
             "orc_dequant_rows": (None, [_u8p, _f32p, _i64, _i64, _int, _int, _f32p]),
@@ -234,6 +240,36 @@ def average_models(p, models):
     lib().orc_average_models(_p(p, _f32p), p.size // models, models)
 
 
+def sgd(p, g, lr):
+    """In place (src/gpu_step/mod.rs:232-238)."""
+    lib().orc_sgd(_p(p, _f32p), _p(_c(g, np.float32), _f32p), p.size, lr)
+
+
+def momentum(p, g, v, lr, mu, mask=None, shrink=0.0):
+    """In place on p and v (src/gpu_step/mod.rs:240-251)."""
+    lib().orc_momentum(_p(p, _f32p), _p(_c(g, np.float32), _f32p), _p(v, _f32p),
+                       None if mask is None else _p(_c(mask, np.float32), _f32p), p.size, lr, mu, shrink)
+
+
+def decay(p, mask, shrink):
+    """In place (src/gpu_step/mod.rs:253-259)."""
+    lib().orc_decay(_p(p, _f32p), _p(_c(mask, np.float32), _f32p), p.size, shrink)
+
+
+def average_groups(p, models, group):
+    """In place: p holds `models` vectors (src/gpu_step/mod.rs:261-275)."""
+    lib().orc_average_groups(_p(p, _f32p), p.size // models, models, group)
+
+
+def dropout(x, rate, seed, relu_y=None):
+    """(src/gpu_step/tape.rs:526-582)"""
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_dropout(_p(x, _f32p), None if relu_y is None else _p(_c(relu_y, np.float32), _f32p), _p(y, _f32p),
+                      x.size, rate, seed)
+    return y
+
+
 def round_f16(x):
     return lib().orc_round_f16(x)
 
@@ -282,3 +318,22 @@ def knn_pair_dots(codes, scales, queries, qi, kj):
     lib().orc_knn_pair_dots(_p(codes, _u8p), _p(scales, _f32p), queries.shape[1], _p(queries, _f32p), _p(qi, _i64p),
                             _p(kj, _i64p), qi.shape[0], _p(out, _f64p))
     return out
+
+
+def pack_keys(scores, ids):
+    """A best-k list in the scan's exchange format: order-preserving f32
+    score bits << 32 | 0xFFFFFFFF - index (the higher key ranks first), 0
+    for an empty entry (id < 0).  DOT scores (the higher the better)."""
+    u = np.asarray(scores, np.float32).view(np.uint32).astype(np.uint64)
+    o = np.where(u & 0x80000000, ~u & 0xFFFFFFFF, u | 0x80000000)
+    keys = (o << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(ids, np.int64).astype(np.uint64))
+    return np.where(np.asarray(ids) >= 0, keys, 0).astype(np.uint64)
+
+
+def merge_keys(lists, k=128):
+    """k_merge_parts (src/gpu_step/knn.rs:661-702) on exchange-format lists
+    [n_lists, nq, width] (u64): each query's best k over all lists, best
+    first (keys are unique per key index, so the order is total)."""
+    lists = np.asarray(lists, np.uint64)
+    allk = np.concatenate(list(lists), axis=1)
+    return np.sort(allk, axis=1)[:, ::-1][:, :k].copy()

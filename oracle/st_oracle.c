@@ -647,3 +647,66 @@ EXPORT void orc_average_models(float *p, int64_t n, int64_t models) {
         for (int64_t mm = 0; mm < models; mm++) p[mm * n + i] = mean;
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Device optimiser steps, in-device model average and dropout              */
+/* (src/gpu_step/mod.rs:232-275, src/gpu_step/tape.rs:526-582)              */
+/* ------------------------------------------------------------------------ */
+
+/* k_sgd (mod.rs:232-238): p -= lr * g */
+EXPORT void orc_sgd(float *p, const float *g, int64_t n, float lr) {
+    for (int64_t i = 0; i < n; i++) p[i] -= lr * g[i];
+}
+
+/* k_momentum (mod.rs:240-251): [p *= 1 - shrink * mask]; v = mu * v + g; p -= lr * v */
+EXPORT void orc_momentum(float *p, const float *g, float *v, const float *mask, int64_t n, float lr, float mu,
+                         float shrink) {
+    for (int64_t i = 0; i < n; i++) {
+        if (mask) p[i] *= 1.0f - shrink * mask[i];
+        v[i] = mu * v[i] + g[i];
+        p[i] -= lr * v[i];
+    }
+}
+
+/* k_decay (mod.rs:253-259): p *= 1 - shrink * mask */
+EXPORT void orc_decay(float *p, const float *mask, int64_t n, float shrink) {
+    for (int64_t i = 0; i < n; i++) p[i] *= 1.0f - shrink * mask[i];
+}
+
+/* k_average_models (mod.rs:261-275): models k of `stride` floats, each group
+ * of `group` consecutive models gets its mean (sequential sum / group). */
+EXPORT void orc_average_groups(float *p, int64_t stride, int64_t k, int64_t group) {
+    for (int64_t i = 0; i < stride; i++)
+        for (int64_t g = 0; g < k / group; g++) {
+            float s = 0.0f;
+            for (int64_t m = 0; m < group; m++) s += p[(g * group + m) * stride + i];
+            float mean = s / (float)group;
+            for (int64_t m = 0; m < group; m++) p[(g * group + m) * stride + i] = mean;
+        }
+}
+
+/* dropout_bits (tape.rs:545-555): lowbias32 of i + seed * 0x9e3779b9, wrapping u32. */
+EXPORT uint32_t orc_dropout_bits(uint32_t i, uint32_t seed) {
+    uint32_t h = i + seed * 0x9e3779b9u;
+    h ^= h >> 16;
+    h *= 0x7feb352du;
+    h ^= h >> 15;
+    h *= 0x846ca68bu;
+    return h ^ (h >> 16);
+}
+
+/* dropout / dropout_relu_backward (tape.rs:526-543, k_dropout :557-568,
+ * k_dropout_relu_bwd :570-582): threshold = (rate as f64 * 2^32) as u32
+ * (saturating), scale = 1 / (1 - rate); relu_y may be NULL. */
+EXPORT void orc_dropout(const float *x, const float *relu_y, float *y, int64_t n, float rate, uint32_t seed) {
+    double t = (double)rate * 4294967296.0;
+    uint32_t thr = !(t > 0.0) ? 0u : (t >= 4294967295.0 ? 0xffffffffu : (uint32_t)t);
+    float scale = 1.0f / (1.0f - rate);
+    for (int64_t i = 0; i < n; i++) {
+        float v = 0.0f;
+        int keep = orc_dropout_bits((uint32_t)i, seed) >= thr;
+        if (relu_y) keep = keep && relu_y[i] > 0.0f;
+        if (keep) v = x[i] * scale;
+        y[i] = v;
+    }
+}

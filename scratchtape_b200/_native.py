@@ -97,6 +97,17 @@ SIGNATURES = {
     "st_knn_probe": (_st, [_h, _vp, _vp, _i64, _i32, _i32, _vp]),
     "st_gather_rows": (_st, [_h, _vp, _i64, _vp, _vp, _i64, _i64]),
     "st_knn_synth_keys": (_st, [_h, _vp, _vp, _i64, _i32, ctypes.c_uint64, _i64]),
+    "st_sgd": (_st, [_h, _vp, _vp, _i64, _f32]),
+    "st_momentum": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32]),
+    "st_decay": (_st, [_h, _vp, _vp, _i64, _f32]),
+    "st_average_models": (_st, [_h, _vp, _i64, _i32, _i32]),
+    "st_dropout": (_st, [_h, _vp, _vp, _i64, _f32, ctypes.c_uint32]),
+    "st_dropout_relu_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _f32, ctypes.c_uint32]),
+    "st_nccl_unique_id": (_st, [_vp]),
+    "st_nccl_comm_init": (_st, [_i32, _i32, _vp, _i32, ctypes.POINTER(_vp)]),
+    "st_nccl_comm_destroy": (_st, [_vp]),
+    "st_avg_params": (_st, [_h, _vp, _i64, _vp]),
+    "st_knn_search_sharded": (_st, [_h, _vp, _vp, _i64, _i32, _vp, _i64, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/st_b200.h"
@@ -28,6 +29,7 @@ enum StScratchSlot {
     SLOT_KNN_UNITS,   // kNN unit-table scans: the device copy of the unit tables
     SLOT_MLP_PART,    // fused MLP step: per-block partial products
     SLOT_MLP_CTL,     // fused MLP step: per-block arrival / departure counters
+    SLOT_COMM,        // sharded kNN search: local, gathered and merged best-128 lists
     SLOT_COUNT
 };
 

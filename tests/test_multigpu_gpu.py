@@ -6,6 +6,9 @@
 * attention heads split over ranks: each rank's heads identical to the
   single-GPU result for the same heads.
 * local-SGD average over NCCL.
+* the same search and average through the C ABI (st_knn_search_sharded,
+  st_avg_params on a communicator made by st_nccl_comm_init): identical to
+  the torch.distributed route.
 """
 import os
 import socket
@@ -43,8 +46,18 @@ def _worker(rank, world, port, result_path):
     g = torch.Generator(device="cuda").manual_seed(1)
     q = torch.randn((nq, d), device="cuda", generator=g)
     s, i = shard.knn_search_sharded(codes, scales, q, lo, k=128, mode="dot")
+    comm = shard.NcclComm()
+    s_abi, i_abi = shard.knn_search_sharded(codes, scales, q, lo, k=128, mode="dot", comm=comm)
     flat = torch.full((1000,), float(rank + 1), device="cuda")
     shard.average_params(flat)
+    gp = torch.Generator(device="cuda").manual_seed(50 + rank)
+    p_torch = torch.randn(100_003, device="cuda", generator=gp)
+    p_abi = p_torch.clone()
+    shard.average_params(p_torch)
+    shard.average_params(p_abi, comm=comm)
+    torch.cuda.synchronize()
+    comm.close()
+    ok_abi = torch.equal(s_abi, s) and torch.equal(i_abi, i) and torch.equal(p_abi, p_torch)
     # heads: this rank's slice of 16 heads
     gh = torch.Generator(device="cuda").manual_seed(2)
     qh, kh, vh = (torch.randn((16, 128, 64), device="cuda", generator=gh).half() / 8 for _ in range(3))
@@ -52,15 +65,15 @@ def _worker(rank, world, port, result_path):
     o_part, _ = attention_fwd(qh[h0:h1], kh[h0:h1], vh[h0:h1], 0.125)
     o_all, _ = attention_fwd(qh, kh, vh, 0.125)
     ok_heads = torch.equal(o_part, o_all[h0:h1])
-    oks = torch.tensor([int(ok_heads), int(torch.allclose(flat, torch.full_like(flat, (world + 1) / 2)))],
-                       device="cuda")
+    oks = torch.tensor([int(ok_heads), int(torch.allclose(flat, torch.full_like(flat, (world + 1) / 2))),
+                        int(ok_abi)], device="cuda")
     dist.all_reduce(oks, op=dist.ReduceOp.MIN)
     if rank == 0:
         ac, asc = K.synth_keys(n, d, seed=11)
         ws, wi = K.search(ac, asc, q, k=128, mode="dot")
         ok_knn = torch.equal(wi, i) and torch.equal(ws, s)
         with open(result_path, "w") as f:
-            f.write("%d %d %d" % (int(ok_knn), int(oks[0].item()), int(oks[1].item())))
+            f.write("%d %d %d %d" % (int(ok_knn), int(oks[0].item()), int(oks[1].item()), int(oks[2].item())))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -70,7 +83,8 @@ def test_two_gpu_sharded_paths(tmp_path):
         pytest.skip("needs 2 GPUs")
     path = str(tmp_path / "res.txt")
     mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, start_method="spawn", join=True)
-    ok_knn, ok_heads, ok_avg = open(path).read().split()
+    ok_knn, ok_heads, ok_avg, ok_abi = open(path).read().split()
     assert ok_knn == "1", "sharded kNN differs from the single-GPU scan"
     assert ok_heads == "1", "head-sharded attention differs"
     assert ok_avg == "1", "NCCL parameter average wrong"
+    assert ok_abi == "1", "the C-ABI route (st_knn_search_sharded / st_avg_params) differs from the torch route"
