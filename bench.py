@@ -60,7 +60,8 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None, help="timed steps (c2: 200, c5: 5)")
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (c2: 20, c5: 3)")
-    p.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    p.add_argument("--config", default="all", choices=["all", "c1", "c2", "c3", "c4", "c5"],
+                   help="all (default): the C5 line with c1-c4 sub-objects; cN: that config alone")
     p.add_argument("--prec", default="exact", choices=["exact", "f16"], help="C5 arithmetic")
     p.add_argument("--keys", type=int, default=C5["keys"], help="C5 total key count (all GPUs)")
     p.add_argument("--key-source", default="uniform", choices=["uniform", "rotated"],
@@ -69,13 +70,14 @@ def parse_args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ivf", action="store_true", help="C5: skip the IVF search measurement")
+    p.add_argument("--no-parity", action="store_true", help="C5: skip the full-size parity check against the oracle")
     p.add_argument("--c2-path", default="fused", choices=["fused", "gemms"],
                    help="C2: the fused one-kernel step, or six separate GEMM launches")
     a = p.parse_args()
     if a.steps is None:
-        a.steps = {"c5": 5, "c4": 24}.get(a.config, 200)
+        a.steps = {"c5": 5, "all": 5, "c4": 24}.get(a.config, 200)
     if a.warmup is None:
-        a.warmup = {"c5": 3, "c4": 4}.get(a.config, 20)
+        a.warmup = {"c5": 3, "all": 3, "c4": 4}.get(a.config, 20)
     return a
 
 
@@ -148,6 +150,36 @@ def dist_setup():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return world, rank, local
+
+
+_PG = {"up": False}
+
+
+def dist_init():
+    """(world, rank, local): the NCCL process group is set up once per process
+    (one rank per GPU) and shared by every measurement of the run; with one
+    rank there is none."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_setup()
+    if world > 1:
+        torch.cuda.set_device(local)
+        if not _PG["up"]:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            _PG["up"] = True
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def dist_close():
+    if _PG["up"]:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+        _PG["up"] = False
 
 
 def mlp_inputs(torch, device, seed=0):
@@ -251,14 +283,7 @@ def run_reference(args):
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    world, rank, local = dist_setup()
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
+    world, rank, local = dist_init()
     device = torch.device("cuda", torch.cuda.current_device())
     import scratchtape_b200 as st
     from scratchtape_b200 import mlp
@@ -465,11 +490,10 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        return line
     if world > 1:
         del graph
-        dist.barrier()
-        dist.destroy_process_group()
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -477,6 +501,9 @@ def run_ours(args):
 # top-128 per query.
 # ---------------------------------------------------------------------------
 C5_METRIC_UNIT = "keys/s"
+C5_DTYPE = {"exact": "f16x2-split query (exact) x 2-bit codes, f32 accumulate (tcgen05 kind::f16)",
+            "f16": "f16 query x f16 dequantised keys, f32 accumulate (tcgen05 kind::f16)"}
+C5_KERNEL = {"exact": "k_knn_scan (+k_knn_merge)", "f16": "k_knn_scan (+k_knn_merge)"}
 
 
 def c5_queries(n, d, seed=0):
@@ -525,27 +552,66 @@ def run_reference_c5(args):
     print(json.dumps(line), flush=True)
 
 
+def c5_parity_check(d, n_total, out_s, out_i, q_host, device, nq_check=4):
+    """The full-size parity spot check: the first `nq_check` queries' top-128
+    from the timed scan against the oracle's exact f64 brute force over ALL
+    n_total synthetic keys (codes regenerated on the host from the same
+    counter-based generator, scales regenerated on the device by the same
+    kernel in 2^24-key chunks and copied back).  Bar, as the kNN parity
+    tests: indices identical outside tie bands, every returned key's exact
+    score within 2 tau of the oracle's score at that rank, every returned
+    score within tau of its key's exact score; tau = 2^-20 * sum|q| * 1.5 *
+    max scale.  Rank 0 only."""
+    import torch
+    import oracle
+    import scratchtape_b200.knn as K
+    t0 = time.perf_counter()
+    scales = np.empty(n_total, np.float32)
+    chunk = 1 << 24
+    for a in range(0, n_total, chunk):
+        b = min(n_total, a + chunk)
+        _, sc = K.synth_keys(b - a, d, seed=1, first_key=a, device=device)
+        scales[a:b] = sc.cpu().numpy()
+        del sc
+    torch.cuda.empty_cache()
+    q = np.ascontiguousarray(q_host[:nq_check])
+    threads = os.cpu_count() or 1
+    ws, wi = oracle.knn_topk_synth(1, 0, n_total, d, scales, q, C5["k"], threads=threads)
+    gs = out_s[:nq_check].cpu().numpy().astype(np.float64)
+    gi = out_i[:nq_check].cpu().numpy()
+    tau = 2.0 ** -20 * np.abs(q).astype(np.float64).sum(1) * 1.5 * float(scales.max())
+    ok, worst, outside = True, 0.0, 0
+    for r in range(nq_check):
+        exact = oracle.knn_pair_dots_synth(1, 0, d, scales, q, np.full(gi.shape[1], r), gi[r])
+        ok &= bool(np.all(np.abs(exact - ws[r]) <= 2 * tau[r] + 1e-30))
+        ok &= bool(np.all(np.abs(gs[r] - exact) <= tau[r] + 1e-6 * np.abs(exact)))
+        gap_prev = np.r_[np.inf, ws[r][:-1] - ws[r][1:]]
+        gap_next = np.r_[ws[r][:-1] - ws[r][1:], np.inf]
+        tied = (gap_prev <= 2 * tau[r]) | (gap_next <= 2 * tau[r])
+        outside += int(np.sum(gi[r][~tied] != wi[r][~tied]))
+        worst = max(worst, float(np.max(np.abs(gs[r] - exact) / tau[r])))
+    ok &= outside == 0
+    return {"ok": bool(ok), "queries": nq_check, "keys": n_total,
+            "ids_differing_outside_tie_bands": outside, "max_score_err_over_tau": worst,
+            "oracle_s": time.perf_counter() - t0,
+            "how": "oracle brute force (exact f64) over all %d keys for the first %d queries, codes regenerated on "
+                   "the host, scales by the device generator; %d threads" % (n_total, nq_check, threads)}
+
+
 def run_ours_c5(args):
     import torch
     import torch.distributed as dist
-    world, rank, local = dist_setup()
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
+    world, rank, local = dist_init()
     device = torch.device("cuda", torch.cuda.current_device())
     import scratchtape_b200 as st
     import scratchtape_b200.knn as K
+    from scratchtape_b200 import shard
 
     peaks, peak_src = load_peaks()
     h = st.handle()
     d, nq, k = C5["d"], C5["nq"], C5["k"]
-    from scratchtape_b200.shard import shard_range
     n_total = args.keys
-    first, last = shard_range(n_total, world, rank)
+    first, last = shard.shard_range(n_total, world, rank)
     n_local = last - first
     if args.key_source == "uniform":
         codes, scales = K.synth_keys(n_local, d, seed=1, first_key=first, device=device)
@@ -553,25 +619,30 @@ def run_ours_c5(args):
         codes, scales = c5_rotated_keys(n_local, d, first, device)
     qh = c5_queries(nq, d)
     q = torch.from_numpy(qh).to(device)
-    keys_local = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
-    gathered = torch.empty((world, nq, K.KMAX), dtype=torch.int64, device=device)
-    merged = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
     out_s = torch.empty((nq, k), dtype=torch.float32, device=device)
     out_i = torch.empty((nq, k), dtype=torch.int64, device=device)
+    comm = shard.NcclComm() if world > 1 else None
 
     def step(q_dev):
-        # local scan of this rank's shard -> exchange of the local top-128s -> merge -> decode
-        K.topk_keys(codes, scales, q_dev, mode="dot", prec=args.prec, index_base=first, out=keys_local)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, keys_local)
-            K.merge_keys(gathered, nq, out=merged)
-            K.decode(merged, q_dev, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+        # one public call: local scan of this rank's shard; with several ranks
+        # the NCCL all-gather of the local best-128 lists, merge and decode
+        # inside st_knn_search_sharded
+        if comm is not None:
+            shard.knn_search_sharded(codes, scales, q_dev, first, k=k, mode="dot", prec=args.prec, comm=comm,
+                                     out=(out_s, out_i))
         else:
-            K.decode(keys_local, q_dev, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+            K.search(codes, scales, q_dev, k=k, mode="dot", prec=args.prec, out=(out_s, out_i))
 
     def barrier():
         if world > 1:
             dist.barrier()
+
+    def max_over_ranks(*vals):
+        if world == 1:
+            return vals
+        t = torch.tensor(vals, device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return tuple(float(x) for x in t.tolist())
 
     n0 = h.launches
     step(q)
@@ -581,35 +652,52 @@ def run_ours_c5(args):
         step(q)
     torch.cuda.synchronize()
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    scan_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     sampler = ClockSampler(local if world > 1 else torch.cuda.current_device(), period=0.05)
     barrier()
     torch.cuda.synchronize()
     with sampler:
         for i in range(args.steps):
-            starts[i].record()
-            scan_ev[i][0].record()
-            K.topk_keys(codes, scales, q, mode="dot", prec=args.prec, index_base=first, out=keys_local)
-            scan_ev[i][1].record()
-            if world > 1:
-                dist.all_gather_into_tensor(gathered, keys_local)
-                K.merge_keys(gathered, nq, out=merged)
-                K.decode(merged, q, k, mode="dot", prec=args.prec, out=(out_s, out_i))
-            else:
-                K.decode(keys_local, q, k, mode="dot", prec=args.prec, out=(out_s, out_i))
-            ends[i].record()
+            ev[i][0].record()
+            step(q)
+            ev[i][1].record()
         torch.cuda.synchronize()
     barrier()
-    total_ms = float(sum(a.elapsed_time(b) for a, b in zip(starts, ends)))
-    scan_ms = float(np.mean([a.elapsed_time(b) for a, b in scan_ev]))
-    if world > 1:
-        t = torch.tensor([total_ms, scan_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, scan_ms = float(t[0].item()), float(t[1].item())
+    total_ms, = max_over_ranks(float(sum(a.elapsed_time(b) for a, b in ev)))
     ms_per_step = total_ms / args.steps
     value = n_total / (ms_per_step / 1e3)
+
+    # where a step's time goes: the same work as separate library calls with
+    # events between them -- the local scan, the all-gather (NCCL), the merge
+    # of the world's lists and the decode
+    lists = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
+    gathered = torch.empty((world, nq, K.KMAX), dtype=torch.int64, device=device)
+    merged = torch.empty((nq, K.KMAX), dtype=torch.int64, device=device)
+    split_steps = 3
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(split_steps)]
+    barrier()
+    for i in range(split_steps):
+        e = evs[i]
+        e[0].record()
+        K.topk_keys(codes, scales, q, mode="dot", prec=args.prec, index_base=first, out=lists)
+        e[1].record()
+        if world > 1:
+            shard.gather_lists(lists, out=gathered)
+        e[2].record()
+        if world > 1:
+            K.merge_keys(gathered, nq, out=merged)
+        e[3].record()
+        K.decode(merged if world > 1 else lists, q, k, mode="dot", prec=args.prec, out=(out_s, out_i))
+        e[4].record()
+    torch.cuda.synchronize()
+    parts = [float(np.mean([e[j].elapsed_time(e[j + 1]) for e in evs])) for j in range(4)]
+    scan_ms, gather_ms, merge_ms, decode_ms = max_over_ranks(*parts)
+    split = {"scan_ms": scan_ms, "allgather_ms": gather_ms, "merge_ms": merge_ms, "decode_ms": decode_ms,
+             "allgather_bytes_per_rank": nq * K.KMAX * 8,
+             "limiter": "the local scan (k_knn_narrow / k_knn_scan): %.1f %% of a step" %
+                        (100.0 * scan_ms / max(1e-9, scan_ms + gather_ms + merge_ms + decode_ms)),
+             "how": "the same step as separate calls (topk_keys, torch all_gather_into_tensor, merge_keys, decode) "
+                    "with CUDA events between them, mean of %d, max over ranks" % split_steps}
 
     # e2e through the public API: host queries in, host results out, every step
     hq = torch.from_numpy(qh).pin_memory()
@@ -629,11 +717,7 @@ def run_ours_c5(args):
         e1.record()
         e1.synchronize()
         e_ms.append(e0.elapsed_time(e1))
-    e_total = float(sum(e_ms))
-    if world > 1:
-        t = torch.tensor([e_total], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_total = float(t.item())
+    e_total, = max_over_ranks(float(sum(e_ms)))
     e2e_value = n_total / (e_total / e2e_steps / 1e3)
 
     # the small pass: 32 queries over the same keys, where the scan would be
@@ -650,11 +734,7 @@ def run_ours_c5(args):
         b32.record()
         ev32.append((a32, b32))
     torch.cuda.synchronize()
-    ms32 = float(np.median([a.elapsed_time(b) for a, b in ev32]))
-    if world > 1:
-        t = torch.tensor([ms32], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms32 = float(t.item())
+    ms32, = max_over_ranks(float(np.median([a.elapsed_time(b) for a, b in ev32])))
     bytes32 = n_local * (d / 4 + 4) + 32 * d * 4
     small_pass = {"queries": 32, "scan_ms": ms32, "keys_per_s": n_total / (ms32 / 1e3),
                   "hbm_gbs": bytes32 / (ms32 / 1e3) / 1e9, "hbm_frac": bytes32 / (ms32 / 1e3) / 1e9 /
@@ -667,41 +747,58 @@ def run_ours_c5(args):
     if world == 1 and not args.no_ivf:
         ivf_pass = c5_ivf_pass(device, d)
 
+    parity = None
+    if args.key_source == "uniform" and not args.no_parity:
+        # out_s / out_i hold the last step's results (every rank has the merged list)
+        barrier()
+        if rank == 0:
+            del codes
+            torch.cuda.empty_cache()
+            parity = c5_parity_check(d, n_total, out_s, out_i, qh, device)
+        barrier()
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
+
     flops_alg = 2.0 * d * nq * n_local  # per scan launch on this rank
     achieved = flops_alg / (scan_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-    passes = 2 if args.prec == "exact" else 1
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": C5_METRIC_UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16x2-split (exact) / f32 accumulate" if passes == 2 else "f16",
-            "data": "synthetic",
+            "vs_baseline": None, "dtype": C5_DTYPE[args.prec], "data": "synthetic",
             "config": {"workload": "C5 kNN scoring (BASELINE configs[4]): 4096 f32 queries x 2^27 keys, dim 256, "
                                    "2-bit codes {-3,-1,1,3} x per-key scale, exact dot-product scores, top-128 per "
-                                   "query; keys sharded evenly over GPUs, local top-128 all-gathered over NCCL and "
-                                   "merged",
-                       "keys": n_total, "queries": nq, "dim": d, "k": k, "prec": args.prec,
+                                   "query; keys sharded evenly over GPUs (strong scaling), local top-128 "
+                                   "all-gathered over NCCL and merged",
+                       "keys": n_total, "keys_per_rank": n_local, "queries": nq, "dim": d, "k": k, "prec": args.prec,
                        "key_source": "uniform codes, |N(0,1)| scales" if args.key_source == "uniform" else
                                      "N(0,1) vectors rotated on the device (TF32 GEMM) and 2-bit quantised",
-                       "parallelism": "key-sharded x%d" % world if world > 1 else "single GPU",
+                       "parallelism": "key-sharded x%d (st_knn_search_sharded: scan, ncclAllGather, merge)" % world
+                                      if world > 1 else "single GPU (st_knn_search)",
                        "l2": "inputs (%.1f GB of codes + scales) far larger than L2; no flush needed"
                              % (n_total * (d / 4 + 4) / 1e9)},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": n_local * (d / 4 + 4) + nq * d * 4,
-                         "traffic_note": "algorithmic bytes per scan launch (codes + scales + queries); ncu DRAM "
-                                         "figures in profiles/knn_scan_c5.md",
-                         "peak_source": peak_src + " (bf16 dense, sustained)", "kernel": "k_knn_scan (+k_knn_merge)",
-                         "small_pass": small_pass,
-                         "ivf_pass": ivf_pass,
-                         "scan_ms": scan_ms, "tensor_passes": passes,
-                         "executed_tflops": achieved * passes,
-                         "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9},
+                         "traffic_note": "algorithmic bytes per scan launch (codes + scales + queries); the ncu "
+                                         "capture's DRAM bytes are dominated by candidate-buffer inserts that grow "
+                                         "with the number of work units, not with the keys, so they do not scale "
+                                         "to a full launch",
+                         "peak_source": peak_src + " (bf16 dense, sustained; the scan runs kind::i8, whose dense "
+                                                   "rate is twice bf16's)",
+                         "kernel": C5_KERNEL[args.prec],
+                         "scan_ms": scan_ms, "algorithmic_tflop_per_scan": flops_alg / 1e12,
+                         "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9,
+                         "small_pass": small_pass, "ivf_pass": ivf_pass},
+            "time_split": split,
+            "parity": parity,
             "e2e": {"value": e2e_value, "unit": C5_METRIC_UNIT, "h2d_bytes_per_step": int(hq.numel() * 4),
                     "d2h_bytes_per_step": int(hs.numel() * 4 + hi.numel() * 8), "ms_per_step": e_total / e2e_steps,
                     "steps": e2e_steps,
-                    "api": "scratchtape_b200.knn.topk_keys/decode (st_knn_topk_keys/st_knn_decode) with the index "
-                           "resident in HBM; pinned host queries in, host scores/ids out"},
+                    "api": ("st_knn_search_sharded (shard.knn_search_sharded with an NcclComm)" if world > 1 else
+                            "st_knn_search (knn.search)") + " with the keys resident in HBM; pinned host queries "
+                           "in, host scores/ids out, every step"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
         }
@@ -712,10 +809,8 @@ def run_ours_c5(args):
                                     "sample": "64 queries x 2^20 synthetic keys, exact f64 brute force top-128 "
                                               "(oracle, %d threads), %.1f s; keys/s scaled to a 4096-query batch"
                                               % (threads, el)}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        return line
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -893,14 +988,7 @@ def run_reference_c3(args):
 def run_ours_c3(args):
     import torch
     import torch.distributed as dist
-    world, rank, local = dist_setup()
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
+    world, rank, local = dist_init()
     device = torch.device("cuda", torch.cuda.current_device())
     import scratchtape_b200 as st
     from scratchtape_b200.attention import attention_bwd, attention_fwd
@@ -1048,10 +1136,8 @@ def run_ours_c3(args):
             line["cpu_baseline"] = {"value": c3_flops() / el / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
                                     "sample": "16 heads of fwd+bwd on the oracle's restated tape attention (f32, 1 "
                                               "thread, as the reference), scaled to 128 heads"}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        return line
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -1066,26 +1152,92 @@ def c4_batch(cfg, seed, step):
     return ids[:-1].copy(), ids[1:].copy()
 
 
-def cpu_baseline_c4(cfg):
-    """The restated tensor.rs matmul on one thread over one step's GEMM shapes
-    at batch 1 (128 tokens), extrapolated x64 to the configured batch.  The
-    non-GEMM work (LN, softmax, CE, Adam) is not counted, so the figure flatters
-    the CPU."""
+def cpu_tape_step_c4(cfg):
+    """One whole training step of the C4 model on the CPU oracle at batch 1
+    (t = 128 tokens), one thread as the reference runs: the embedding; per
+    layer the oracle's bitwise block forward (LayerNorm, QKV projection, causal
+    softmax attention, output projection + residual, LayerNorm, ReLU FFN +
+    residual: src/nn.rs:627-712 on the restated tensor.rs matmul); the final
+    LayerNorm, the tied head and the cross-entropy; the backward -- every
+    linear's dX and dW GEMM with the tape's explicit transposes
+    (src/tape.rs:505-510), the attention backward (restated softmax backward),
+    the LayerNorm backwards, the embedding scatter -- and Adam over all
+    parameters (src/optim.rs:42-57).  The backward runs on stand-in values of
+    the forward's shapes (the arithmetic per element is the same).  Returns
+    (seconds of the batch-proportional part, seconds of Adam)."""
     import oracle
-    rows = cfg.t
+    rows, d, f, hh, t = cfg.t, cfg.d, cfg.dff, cfg.heads, cfg.t
+    dk = d // hh
     rng = np.random.default_rng(0)
-    shapes = []
-    for _ in range(cfg.layers):
-        for (k, n) in ((cfg.d, 3 * cfg.d), (cfg.d, cfg.d), (cfg.d, cfg.dff), (cfg.dff, cfg.d)):
-            shapes += [(rows, k, n), (rows, n, k), (k, rows, n)]  # fwd, dX, dW
-    shapes += [(rows, cfg.d, cfg.vocab), (rows, cfg.vocab, cfg.d), (cfg.vocab, rows, cfg.d)]
-    mats = [(rng.standard_normal((m, k)).astype(np.float32), rng.standard_normal((k, n)).astype(np.float32))
-            for m, k, n in shapes]
+    r = lambda *sh: rng.standard_normal(sh).astype(np.float32) * 0.05
+    blocks = [oracle.block_init(oracle.Rng(11 + i), d, hh, f) for i in range(cfg.layers)]
+    tok, pos = r(cfg.vocab, d), r(t, d)
+    ids = rng.integers(0, cfg.vocab, rows)
+    tg = rng.integers(0, cfg.vocab, rows)
+    w = {"qkv": r(d, 3 * d), "o": r(d, d), "f1": r(d, f), "f2": r(f, d)}
+    acts = {"ln": r(rows, d), "qkv": r(rows, 3 * d), "hid": r(rows, f), "dx": r(rows, d), "att": r(hh, t, dk)}
+
+    def mm_nt(a, b):  # a . b^T through an explicit transpose, as the tape
+        return oracle.matmul_layout(a, oracle.transpose(b), threads=1)
+
+    def mm_tn(a, b):
+        return oracle.matmul_layout(oracle.transpose(a), b, threads=1)
+
+    def ln_bwd(x, dy):
+        mu = x.mean(1, keepdims=True, dtype=np.float32)
+        xc = x - mu
+        rstd = 1.0 / np.sqrt((xc * xc).mean(1, keepdims=True, dtype=np.float32) + np.float32(1e-5))
+        xh = xc * rstd
+        return (rstd * (dy - dy.mean(1, keepdims=True) - xh * (dy * xh).mean(1, keepdims=True))).astype(np.float32)
+
     t0 = time.perf_counter()
-    for a, b in mats:
-        oracle.matmul_layout(a, b, threads=1)
-    el = (time.perf_counter() - t0) * cfg.batch
-    return el
+    x = tok[ids] + pos
+    for p in blocks:
+        x = oracle.block_forward(p, x, 1, t, d, hh, f)
+    xf = oracle.layernorm_fwd(x, np.ones(d, np.float32), np.zeros(d, np.float32))
+    logits = oracle.matmul_layout(xf, oracle.transpose(tok), threads=1)
+    z = logits - logits.max(1, keepdims=True)
+    pr = np.exp(z)
+    pr /= pr.sum(1, keepdims=True)
+    dlog = pr.copy()
+    dlog[np.arange(rows), tg] -= 1.0
+    dlog = (dlog / rows).astype(np.float32)
+    mm_tn(dlog, xf)                                   # d tok (head)
+    dx = ln_bwd(x, oracle.matmul_layout(dlog, tok, threads=1))
+    for _ in range(cfg.layers):
+        mm_tn(acts["hid"], dx)                         # dW2
+        dh = mm_nt(dx, w["f2"]) * (acts["hid"] > 0)    # dH, ReLU mask
+        mm_tn(acts["ln"], dh)                          # dW1
+        d1 = ln_bwd(acts["ln"], mm_nt(dh, w["f1"])) + dx
+        mm_tn(acts["ln"], d1)                          # dWo
+        dm = mm_nt(d1, w["o"])
+        a = acts["att"]
+        oracle.attention_bwd(a, a, a, dm.reshape(t, hh, dk).transpose(1, 0, 2), 1.0 / dk ** 0.5)
+        mm_tn(acts["ln"], acts["qkv"])                 # dWqkv
+        dx = ln_bwd(acts["ln"], mm_nt(acts["qkv"], w["qkv"])) + d1
+    np.add.at(np.zeros_like(tok), ids, dx)            # embedding backward
+    t_rows = time.perf_counter() - t0
+    n = sum(b.size for b in blocks) + tok.size + pos.size + 2 * d
+    pp, gg, m1, v1 = (r(n) for _ in range(4))
+    t0 = time.perf_counter()
+    oracle.adam(pp, gg, m1, v1, 1, 1e-3)
+    return t_rows, time.perf_counter() - t0
+
+
+def cpu_baseline_c4(cfg):
+    """Seconds of one C4 step on the CPU: cpu_tape_step_c4 at batch 1 with its
+    batch-proportional part x batch (64) plus Adam once (median of 3)."""
+    ts = [cpu_tape_step_c4(cfg) for _ in range(3)]
+    rows = float(np.median([a for a, _ in ts]))
+    adam = float(np.median([b for _, b in ts]))
+    return rows * cfg.batch + adam
+
+
+C4_CPU_SAMPLE = ("one whole C4 training step on the CPU oracle at batch 1 (128 tokens), 1 thread as the reference "
+                 "runs: embedding, 4 blocks' bitwise forward (LN, QKV, causal softmax attention, projections, FFN), "
+                 "final LN, tied head, cross-entropy, the backward's GEMMs (tape transposes), attention and "
+                 "LayerNorm backwards, embedding scatter, then Adam over all parameters; the batch-proportional "
+                 "part x64 plus Adam once, median of 3")
 
 
 def run_reference_c4(args):
@@ -1101,10 +1253,9 @@ def run_reference_c4(args):
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C4 training step GEMMs (sampled at batch 1, x64)", "parallelism": "CPU, rank 0"},
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port",
-                             "sample": "one step's GEMM shapes at batch 1 on the restated tensor.rs matmul (1 thread), "
-                                       "extrapolated to batch 64; LN/softmax/CE/Adam not counted"},
+            "config": {"workload": "C4 training step (sampled at batch 1, x64; Adam once)",
+                       "parallelism": "CPU, rank 0"},
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port", "sample": C4_CPU_SAMPLE},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -1156,16 +1307,8 @@ def large_gemm_probe(torch, device, peaks):
 def run_ours_c4(args):
     import torch
     import torch.distributed as dist
-    world, rank, local = dist_setup()
-    group = None
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-        group = dist.group.WORLD
-    else:
-        torch.cuda.set_device(0)
+    world, rank, local = dist_init()
+    group = dist.group.WORLD if world > 1 else None
     device = torch.device("cuda", torch.cuda.current_device())
     import scratchtape_b200 as st
     from scratchtape_b200.lm import LmConfig, TinyLM
@@ -1189,14 +1332,24 @@ def run_ours_c4(args):
     tg_buf.copy_(tg_d[1])
     graph = model.capture_step(ids_buf, tg_buf)
 
-    def one_step(i):
+    from scratchtape_b200 import shard
+    comm = shard.NcclComm() if world > 1 else None
+    avg_ev = []
+
+    def one_step(i, timed=False):
         ids_buf.copy_(ids_d[i])
         tg_buf.copy_(tg_d[i])
         graph.replay()
         model.step_count += 1
-        if group is not None and model.step_count % cfg.sync_every == 0:
-            from scratchtape_b200.shard import average_params
-            average_params(model.params, group)
+        if comm is not None and model.step_count % cfg.sync_every == 0:
+            # local SGD: the model average over the ranks, st_avg_params (NCCL all-reduce + divide)
+            if timed:
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record()
+            shard.average_params(model.params, comm=comm)
+            if timed:
+                a1.record()
+                avg_ev.append((a0, a1))
         return model.loss
 
     for i in range(2, args.warmup):
@@ -1215,16 +1368,17 @@ def run_ours_c4(args):
     with sampler:
         for i in range(args.steps):
             ev[i][0].record()
-            loss = one_step(args.warmup + i)
+            loss = one_step(args.warmup + i, timed=True)
             ev[i][1].record()
             losses.append(loss.clone())
         torch.cuda.synchronize()
     barrier()
     total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    avg_ms = float(sum(a.elapsed_time(b) for a, b in avg_ev))
     if world > 1:
-        tt = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        tt = torch.tensor([total_ms, avg_ms], device=device, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms = float(tt.item())
+        total_ms, avg_ms = (float(x) for x in tt.tolist())
     ms = total_ms / args.steps
     value = cfg.flops_per_step() * world / (ms / 1e3) / 1e12
     tokens_s = cfg.batch * cfg.t * world / (ms / 1e3)
@@ -1242,9 +1396,8 @@ def run_ours_c4(args):
         tg_buf.copy_(htg[i], non_blocking=True)
         graph.replay()
         model.step_count += 1
-        if group is not None and model.step_count % cfg.sync_every == 0:
-            from scratchtape_b200.shard import average_params
-            average_params(model.params, group)
+        if comm is not None and model.step_count % cfg.sync_every == 0:
+            shard.average_params(model.params, comm=comm)
         hloss.copy_(model.loss, non_blocking=True)
     e1.record()
     e1.synchronize()
@@ -1254,6 +1407,9 @@ def run_ours_c4(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e_ms = float(tt.item())
     e2e_value = cfg.flops_per_step() * world * e2e_steps / (e_ms / 1e3) / 1e12
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -1266,6 +1422,11 @@ def run_ours_c4(args):
                        "parallelism": "dp%d local SGD (NCCL all-reduce every %d steps)" % (world, cfg.sync_every)
                        if world > 1 else "single GPU",
                        "tokens_per_s": tokens_s, "gemm_flops_per_step": cfg.flops_per_step(),
+                       "local_sgd": {"averages_in_timed_steps": len(avg_ev), "average_ms_total": avg_ms,
+                                     "share_of_step_time": avg_ms / total_ms if total_ms else 0.0,
+                                     "bytes_per_average": model.n_params * 4,
+                                     "api": "st_avg_params (ncclAllReduce sum + divide, on the step's stream)"}
+                       if world > 1 else None,
                        "loss_first_last": [float(losses[0].item()), float(losses[-1].item())],
                        "l2": "activations (~160 MB) exceed L2; no flush"},
             "roofline": {"bound": "tensor", "achieved": cfg.flops_per_step() / (ms / 1e3) / 1e12,
@@ -1284,13 +1445,9 @@ def run_ours_c4(args):
         if world == 1 and not args.no_cpu_baseline:
             el = cpu_baseline_c4(cfg)
             line["cpu_baseline"] = {"value": cfg.flops_per_step() / el / 1e12, "unit": "TFLOP/s", "cores": 1,
-                                    "kind": "port", "sample": "one step's GEMM shapes at batch 1 on the restated "
-                                    "tensor.rs matmul (1 thread), extrapolated to batch 64; LN/softmax/CE/Adam not "
-                                    "counted"}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+                                    "kind": "port", "sample": C4_CPU_SAMPLE, "ms_per_step": el * 1e3}
+        return line
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -1349,14 +1506,7 @@ def run_reference_c1(args):
 def run_ours_c1(args):
     import torch
     import torch.distributed as dist
-    world, rank, local = dist_setup()
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
+    world, rank, local = dist_init()
     device = torch.device("cuda", torch.cuda.current_device())
     import scratchtape_b200 as st
     peaks, peak_src = load_peaks()
@@ -1425,10 +1575,33 @@ def run_ours_c1(args):
         torch.cuda.synchronize()
     barrier()
     total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    # the same three GEMMs as ONE persistent grouped launch (st_gemm_group, the
+    # scheduler for tiny shapes): no dependencies, so every tile of all three
+    # starts at once
+    from scratchtape_b200.matmul import matmul_group
+    gsteps = max(20, min(args.steps, 200))
+    gr2 = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        matmul_group([(a_, b_, o_, C1_N, C1_N, C1_N, None, ()) for a_, b_, o_ in refs])
+    torch.cuda.synchronize()
+    with torch.cuda.graph(gr2, stream=s):
+        matmul_group([(a_, b_, o_, C1_N, C1_N, C1_N, None, ()) for a_, b_, o_ in refs])
+    gev = []
+    for i in range(gsteps + 3):
+        flush.zero_()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        gr2.replay()
+        g1.record()
+        if i >= 3:
+            gev.append((g0, g1))
+    torch.cuda.synchronize()
+    grouped_ms = float(np.mean([a.elapsed_time(b) for a, b in gev]))
+    del gr2
     if world > 1:
-        tt = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        tt = torch.tensor([total_ms, grouped_ms], device=device, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms = float(tt.item())
+        total_ms, grouped_ms = (float(x) for x in tt.tolist())
     ms = total_ms / args.steps
     value = c1_flops() * world / (ms / 1e3) / 1e12
     # e2e: the host-array drop-in (gpu_matmul -> st_matmul_host), copies in and out per GEMM
@@ -1462,7 +1635,11 @@ def run_ours_c1(args):
                                 "independent)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
                          "frac": achieved / float(peaks["hbm_gbs"]), "traffic": None, "peak_source": peak_src,
-                         "kernel": "k_gemm_tf32 (+k_splitk_reduce)", "us_per_gemm": ms * 1e3 / 3},
+                         "kernel": "k_gemm_tf32 (+k_splitk_reduce)", "us_per_gemm": ms * 1e3 / 3,
+                         "grouped_step_us": grouped_ms * 1e3,
+                         "grouped_tflops": c1_flops() / (grouped_ms / 1e3) / 1e12,
+                         "grouped_note": "the three GEMMs in one st_gemm_group launch (k_gemm_group), graph "
+                                         "replay, L2 flushed before each, mean of %d" % gsteps},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(3 * 2 * C1_N * C1_N * 4),
                     "d2h_bytes_per_step": int(3 * C1_N * C1_N * 4), "ms_per_step": e_s / e_steps * 1e3,
                     "steps": e_steps, "timing": "host wall clock (each call copies in, multiplies, copies out, syncs)",
@@ -1475,38 +1652,53 @@ def run_ours_c1(args):
             line["cpu_baseline"] = {"value": c1_flops() / el / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
                                     "sample": "the three layouts on the oracle's restated tensor.rs matmul (tape "
                                               "transposes included), 1 thread as the reference runs, median of 3"}
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        return line
+    return None
+
+
+# (sub-object, measurement, timed steps, warm-up steps): the configs that ride
+# along in the default line, each with its own roofline, cpu_baseline and e2e
+SUBS = (("c2", "run_ours", 200, 20), ("c1", "run_ours_c1", 200, 20), ("c3", "run_ours_c3", 200, 20),
+        ("c4", "run_ours_c4", 24, 4))
+
+
+def run_all(args):
+    """The default line: BASELINE configs[4] (C5, the 2-bit kNN scan over
+    2^27 keys, key-sharded across the ranks with an NCCL all-gather and merge)
+    as the headline, and configs[0]-[3] measured in the same run (every rank
+    takes part in each) as the sub-objects c1-c4."""
+    import copy
+    import torch
+    a5 = copy.copy(args)
+    a5.config = "c5"
+    line = run_ours_c5(a5)
+    torch.cuda.empty_cache()
+    for name, fn, steps, warm in SUBS:
+        a = copy.copy(args)
+        a.config, a.steps, a.warmup = name, steps, warm
+        sub = globals()[fn](a)
+        torch.cuda.empty_cache()
+        if line is not None and sub is not None:
+            sub.pop("metric", None)
+            line[name] = sub
+    return line
+
+
+REFERENCE = {"all": "run_reference_c5", "c5": "run_reference_c5", "c1": "run_reference_c1",
+             "c2": "run_reference", "c3": "run_reference_c3", "c4": "run_reference_c4"}
+OURS = {"all": "run_all", "c5": "run_ours_c5", "c1": "run_ours_c1", "c2": "run_ours", "c3": "run_ours_c3",
+        "c4": "run_ours_c4"}
 
 
 def main():
     args = parse_args()
-    if args.config == "c5":
-        if args.impl == "reference":
-            run_reference_c5(args)
-        else:
-            run_ours_c5(args)
-    elif args.config == "c1":
-        if args.impl == "reference":
-            run_reference_c1(args)
-        else:
-            run_ours_c1(args)
-    elif args.config == "c4":
-        if args.impl == "reference":
-            run_reference_c4(args)
-        else:
-            run_ours_c4(args)
-    elif args.config == "c3":
-        if args.impl == "reference":
-            run_reference_c3(args)
-        else:
-            run_ours_c3(args)
-    elif args.impl == "reference":
-        run_reference(args)
-    else:
-        run_ours(args)
+    if args.impl == "reference":
+        globals()[REFERENCE[args.config]](args)  # rank 0 prints its line; other ranks exit at once
+        return
+    line = globals()[OURS[args.config]](args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    dist_close()
 
 
 if __name__ == "__main__":

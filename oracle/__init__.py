@@ -79,6 +79,11 @@ def lib():
             "orc_knn_topk": (None, [_u8p, _f32p, _i64, _i64, _f32p, _i64, _i64, _int, _int, _i64p, _i64p, _i64,
                                     _f32p, _f64p, _i64p, _int]),
             "orc_knn_pair_dots": (None, [_u8p, _f32p, _i64, _f32p, _i64p, _i64p, _i64, _f64p]),
+            "orc_synth_codes": (None, [ctypes.c_uint64, _i64, _i64, _i64, _u8p]),
+            "orc_knn_topk_synth": (None, [ctypes.c_uint64, _i64, _i64, _i64, _f32p, _f32p, _i64, _i64, _f64p, _i64p,
+                                          _int]),
+            "orc_knn_pair_dots_synth": (None, [ctypes.c_uint64, _i64, _i64, _f32p, _f32p, _i64p, _i64p, _i64,
+                                               _f64p]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -337,3 +342,34 @@ def merge_keys(lists, k=128):
     lists = np.asarray(lists, np.uint64)
     allk = np.concatenate(list(lists), axis=1)
     return np.sort(allk, axis=1)[:, ::-1][:, :k].copy()
+
+
+def synth_codes(seed, first, n, d):
+    """The code bytes st_knn_synth_keys makes for keys first..first+n-1."""
+    out = np.empty((n, d // 4), np.uint8)
+    lib().orc_synth_codes(seed, first, n, d, _p(out, _u8p))
+    return out
+
+
+def knn_topk_synth(seed, first, n, d, scales, queries, k, threads=None):
+    """Exact f64 DOT top-k over the synthetic keys first..first+n-1 (codes
+    regenerated from the seed, scales as given, [n]): (scores f64, ids)."""
+    q = _c(queries, np.float32)
+    sc = _c(scales, np.float32)
+    nq = q.shape[0]
+    s = np.empty((nq, k), np.float64)
+    i = np.empty((nq, k), np.int64)
+    lib().orc_knn_topk_synth(seed, first, n, d, _p(sc, _f32p), _p(q, _f32p), nq, k, _p(s, _f64p), _p(i, _i64p),
+                             threads or (os.cpu_count() or 1))
+    return s, i
+
+
+def knn_pair_dots_synth(seed, first, d, scales, queries, qi, kj):
+    """Exact f64 q.k of (query qi[p], synthetic key kj[p]) pairs; scales [n] from key `first`."""
+    q = _c(queries, np.float32)
+    qi = _c(qi, np.int64)
+    kj = _c(kj, np.int64)
+    out = np.empty(qi.size, np.float64)
+    lib().orc_knn_pair_dots_synth(seed, first, d, _p(_c(scales, np.float32), _f32p), _p(q, _f32p), _p(qi, _i64p),
+                                  _p(kj, _i64p), qi.size, _p(out, _f64p))
+    return out

@@ -283,3 +283,142 @@ EXPORT void orc_knn_pair_dots(const uint8_t *codes, const float *scales, int64_t
         out[p] = dot * (double)scales[kj[p]];
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Brute force over the benchmark's synthetic keys, regenerated on the fly   */
+/* ------------------------------------------------------------------------ */
+
+/* The synthetic keys' code bytes (no reference counterpart: the library's
+ * st_knn_synth_keys, which makes the benchmark's 2^27 keys): the 64-bit
+ * words of key `key` are mix64(base + 1 + w), base = mix64(seed ^ mix64(key)),
+ * mix64 being SplitMix64's finaliser.  Integer arithmetic only, so the codes
+ * regenerate bit for bit; the scales (which use logf/cosf) are taken from the
+ * device instead. */
+static uint64_t mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+EXPORT void orc_synth_codes(uint64_t seed, int64_t first, int64_t n, int64_t d, uint8_t *codes) {
+    int64_t words = d / 32;
+    for (int64_t r = 0; r < n; r++) {
+        uint64_t base = mix64(seed ^ mix64((uint64_t)(first + r)));
+        for (int64_t w = 0; w < words; w++) {
+            uint64_t v = mix64(base + 1 + (uint64_t)w);
+            memcpy(codes + r * (d / 4) + 8 * w, &v, 8);
+        }
+    }
+}
+
+struct synth_job {
+    uint64_t seed;
+    int64_t first, a, b, d, nq, k;
+    const float *scales; /* [n], indexed by row */
+    const double *tab;   /* [nq][d/4][256] byte tables */
+    double *best_s;      /* [nq][k] this thread's best, descending */
+    int64_t *best_i;
+};
+
+/* insert (s, i) into a descending list of k (ties: lower index first) */
+static void put_best(double *bs, int64_t *bi, int64_t k, double s, int64_t i) {
+    if (!(s > bs[k - 1] || (s == bs[k - 1] && i < bi[k - 1]))) return;
+    int64_t p = k - 1;
+    while (p > 0 && (s > bs[p - 1] || (s == bs[p - 1] && i < bi[p - 1]))) {
+        bs[p] = bs[p - 1];
+        bi[p] = bi[p - 1];
+        p--;
+    }
+    bs[p] = s;
+    bi[p] = i;
+}
+
+static void *synth_worker(void *arg) {
+    struct synth_job *j = (struct synth_job *)arg;
+    int64_t kb = j->d / 4;
+    uint8_t codes[64];
+    for (int64_t q = 0; q < j->nq * j->k; q++) {
+        j->best_s[q] = -INFINITY;
+        j->best_i[q] = -1;
+    }
+    for (int64_t r = j->a; r < j->b; r++) {
+        orc_synth_codes(j->seed, j->first + r, 1, j->d, codes);
+        double sc = (double)j->scales[r];
+        for (int64_t q = 0; q < j->nq; q++) {
+            const double *t = j->tab + q * kb * 256;
+            double dot = 0;
+            for (int64_t c = 0; c < kb; c++) dot += t[c * 256 + codes[c]];
+            put_best(j->best_s + q * j->k, j->best_i + q * j->k, j->k, dot * sc, j->first + r);
+        }
+    }
+    return NULL;
+}
+
+/* DOT-mode top-k of nq queries over the n synthetic keys first..first+n-1
+ * (scales from the device), exact in f64: q.k = scale * sum_i (u_i - 1.5) q_i,
+ * the per-byte partial sums of four dimensions tabulated per query.  Scores
+ * descending, ties to the lower index; out_scores64 [nq, k], out_ids [nq, k]. */
+EXPORT void orc_knn_topk_synth(uint64_t seed, int64_t first, int64_t n, int64_t d, const float *scales,
+                               const float *queries, int64_t nq, int64_t k, double *out_scores64, int64_t *out_ids,
+                               int threads) {
+    int64_t kb = d / 4;
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    double *tab = (double *)malloc(sizeof(double) * nq * kb * 256);
+    static const double lut[4] = {-1.5, -0.5, 0.5, 1.5};
+    for (int64_t q = 0; q < nq; q++)
+        for (int64_t c = 0; c < kb; c++)
+            for (int v = 0; v < 256; v++) {
+                double s = 0;
+                for (int p = 0; p < 4; p++) s += lut[(v >> (2 * p)) & 3] * (double)queries[q * d + 4 * c + p];
+                tab[(q * kb + c) * 256 + v] = s;
+            }
+    pthread_t tid[256];
+    struct synth_job jobs[256];
+    int64_t per = (n + threads - 1) / threads;
+    int used = 0;
+    for (int t = 0; t < threads; t++) {
+        int64_t a = t * per, b = a + per < n ? a + per : n;
+        if (a >= b) break;
+        jobs[t] = (struct synth_job){seed, first, a, b, d, nq, k, scales, tab,
+                                     (double *)malloc(sizeof(double) * nq * k),
+                                     (int64_t *)malloc(sizeof(int64_t) * nq * k)};
+        pthread_create(&tid[t], NULL, synth_worker, &jobs[t]);
+        used++;
+    }
+    for (int t = 0; t < used; t++) pthread_join(tid[t], NULL);
+    for (int64_t q = 0; q < nq; q++) {
+        double *bs = out_scores64 + q * k;
+        int64_t *bi = out_ids + q * k;
+        for (int64_t i = 0; i < k; i++) {
+            bs[i] = -INFINITY;
+            bi[i] = -1;
+        }
+        for (int t = 0; t < used; t++)
+            for (int64_t i = 0; i < k; i++)
+                if (jobs[t].best_i[q * k + i] >= 0)
+                    put_best(bs, bi, k, jobs[t].best_s[q * k + i], jobs[t].best_i[q * k + i]);
+    }
+    for (int t = 0; t < used; t++) {
+        free(jobs[t].best_s);
+        free(jobs[t].best_i);
+    }
+    free(tab);
+}
+
+/* Exact f64 q.k for given (query, synthetic key) pairs (scales indexed by
+ * key - first). */
+EXPORT void orc_knn_pair_dots_synth(uint64_t seed, int64_t first, int64_t d, const float *scales,
+                                    const float *queries, const int64_t *qi, const int64_t *kj, int64_t pairs,
+                                    double *out) {
+    static const double lut[4] = {-1.5, -0.5, 0.5, 1.5};
+    uint8_t codes[64];
+    for (int64_t p = 0; p < pairs; p++) {
+        orc_synth_codes(seed, kj[p], 1, d, codes);
+        const float *q = queries + qi[p] * d;
+        double dot = 0;
+        for (int64_t i = 0; i < d; i++) dot += lut[(codes[i / 4] >> (2 * (i % 4))) & 3] * (double)q[i];
+        out[p] = dot * (double)scales[kj[p] - first];
+    }
+}

@@ -84,7 +84,8 @@ def gather_lists(local: torch.Tensor, group=None, out=None):
 
 
 def knn_search_sharded(codes: torch.Tensor, scales: torch.Tensor, queries: torch.Tensor, first: int, k: int = 128,
-                       mode: str = "dot", prec: str = "exact", group=None, work=None, comm: NcclComm = None):
+                       mode: str = "dot", prec: str = "exact", group=None, work=None, comm: NcclComm = None,
+                       out=None):
     """Best k of every query over all ranks' keys.  codes/scales: this rank's
     shard, whose first key has global index ``first``.  Returns (scores, ids)
     on every rank; ids are global key indices.  With ``comm`` the whole search
@@ -93,8 +94,8 @@ def knn_search_sharded(codes: torch.Tensor, scales: torch.Tensor, queries: torch
     nq = queries.shape[0]
     if comm is not None:
         dev = queries.device
-        scores = torch.empty((nq, k), dtype=torch.float32, device=dev)
-        ids = torch.empty((nq, k), dtype=torch.int64, device=dev)
+        scores, ids = out if out is not None else (torch.empty((nq, k), dtype=torch.float32, device=dev),
+                                                   torch.empty((nq, k), dtype=torch.int64, device=dev))
         q = queries.contiguous()
         handle(dev).call("st_knn_search_sharded", ptr(codes), ptr(scales), codes.shape[0], q.shape[1], ptr(q), nq,
                          k, knn.MODES[mode], knn.PRECS[prec], first, comm.ptr, ptr(scores), ptr(ids))
