@@ -1044,9 +1044,8 @@ __global__ void k_gather_rows(const uint32_t *src, int64_t n_src, uint32_t *dst,
 //     rarely reach the exact path.
 // Scores come out in the wide scan's units, so k_knn_merge and k_knn_decode
 // are shared.
-constexpr int NQ = 32;                                  // queries per pass
+constexpr int NQ = 32;                                  // queries per group (one accumulator's columns)
 constexpr int NK = 128;                                 // keys per tile (MMA M, TMEM lanes)
-constexpr int N_STAGES = 12;                            // code / scale ring
 constexpr int N_CODE_BYTES = NK * 64;                   // dim 256: 64 code bytes per key
 constexpr int N_STAGE_BYTES = N_CODE_BYTES + NK * 4 + 16;  // scales from the 16-byte block of the first
 constexpr int N_A = 2;                                  // TMEM A buffers, 64 columns each
@@ -1055,46 +1054,58 @@ constexpr int N_ACC_COLS = 128;
 constexpr int N_KF = 8;                                 // per-key factor slots (lifetime: see the producer)
 constexpr int N_QUAD = 4;                               // TMEM lane quadrants: one candidate list per query each
 constexpr int N_EPI = 8, N_PROD = 8;                    // epilogue warp w: quadrant w % 4, queries 16 (w / 4) ..
-constexpr int EQ = NQ / 2;                              // queries per epilogue warp
+constexpr int EQ = NQ / 2;                              // queries per epilogue warp and group
 constexpr int N_MMA_WARP = N_EPI + N_PROD;              // 16
 constexpr int N_TMA_WARP = N_MMA_WARP + 1;              // 17
 constexpr int N_THREADS = 32 * (N_TMA_WARP + 1);        // 576
-constexpr int NO_Q = 0;                                 // B: [2 K chunks][128 rows x 128 B], SW128
-constexpr int NQ_CHUNK = 128 * 128;
-constexpr int NO_RING = NO_Q + 2 * NQ_CHUNK;
-constexpr int NO_KF = NO_RING + N_STAGES * N_STAGE_BYTES;  // [N_KF][128] scale
-constexpr int NO_KN = NO_KF + N_KF * NK * 4;               // [N_KF][128] |k|^2 (L2)
-constexpr int NO_QC = NO_KN + N_KF * NK * 4;               // [8][32] per-query constants
-constexpr int NO_THR = NO_QC + 8 * NQ * 4;                 // [2][4 quadrants][32] thresholds
-constexpr int NO_SLOT = NO_THR + 2 * N_QUAD * NQ * 4;      // [16 queries][256 threads] exact scores
-constexpr int NO_BAR = NO_SLOT + EQ * N_EPI * 32 * 4;
-constexpr int N_NBARS = 2 * N_STAGES + 2 * N_A + 2 * N_ACC + N_KF + 2;
-constexpr int NO_MISC = NO_BAR + N_NBARS * 8;              // tmem slot, abort flag
-constexpr int NARROW_SMEM = NO_MISC + 16 + 1024;
+constexpr int NQ_CHUNK = 128 * 128;                     // one K chunk of a group's B: 128 rows x 128 B, SW128
 constexpr uint32_t N_TMEM_COLS = 512;
 constexpr uint32_t N_ACC_COL = N_A * 64;                   // accumulators after the A buffers
 constexpr int MAGIC_I = 0x4B400000;                        // float 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
+static_assert(N_ACC_COL + N_ACC * N_ACC_COLS <= N_TMEM_COLS, "keys-on-M kNN scan TMEM budget");
 
-static_assert(NARROW_SMEM <= 232448, "narrow kNN scan shared memory exceeds the sm_100 limit");
-static_assert(N_ACC_COL + N_ACC * N_ACC_COLS <= N_TMEM_COLS, "narrow kNN scan TMEM budget");
+// Shared-memory layout of the keys-on-M scan with NG groups of 32 queries
+// resident per unit (NG = 1: the narrow pass; NG = 4: 128 queries, the wide scan).
+template <int NG>
+struct NarrowSmem {
+    static constexpr int QB = NQ * NG;                       // queries per unit
+    static constexpr int STAGES = NG == 1 ? 12 : 6;          // code / scale ring
+    static constexpr int O_Q = 0;                            // NG x [2 K chunks][128 rows x 128 B]
+    static constexpr int O_RING = O_Q + NG * 2 * NQ_CHUNK;
+    static constexpr int O_KF = O_RING + STAGES * N_STAGE_BYTES;  // [N_KF][128] scale
+    static constexpr int O_KN = O_KF + N_KF * NK * 4;             // [N_KF][128] |k|^2 (L2)
+    static constexpr int O_QC = O_KN + N_KF * NK * 4;             // [2 units][8][QB] per-query constants
+    static constexpr int O_THR = O_QC + 2 * 8 * QB * 4;           // [2][4 quadrants][QB] thresholds
+    static constexpr int O_SLOT = O_THR + 2 * N_QUAD * QB * 4;    // [16 queries][256 threads] exact scores
+    static constexpr int O_BAR = O_SLOT + EQ * N_EPI * 32 * 4;
+    // rfull, rempty [STAGES]; afull, aempty [N_A]; accf, acce [N_ACC]; kfr [N_KF];
+    // qready [2]; edone [2]; qfree; fin
+    static constexpr int NBARS = 2 * STAGES + 2 * N_A + 2 * N_ACC + N_KF + 2 + 2 + 1 + 1;
+    static constexpr int O_MISC = O_BAR + NBARS * 8;              // tmem slot, abort flag
+    static constexpr int SMEM = O_MISC + 16 + 1024;
+    static_assert(SMEM <= 232448, "keys-on-M kNN scan shared memory exceeds the sm_100 limit");
+    static_assert(O_RING % 1024 == 0 && N_STAGE_BYTES % 16 == 0, "keys-on-M kNN scan alignment");
+};
 
 struct NarrowArgs {
     const uint8_t *codes;  // [n_keys, 64], 16-byte aligned
     const float *scales;   // [n_keys], 4-byte aligned
     const float *q;        // [nq, 256]
     int64_t n_keys;
-    int nq, nqp, splits;   // nqp: queries per limb block of B (a multiple of 8, NL * nqp % 16 == 0)
-    // unit u scans 128-key tiles u * unit_step + i * tile_step, i < tiles_per_unit, below n_tiles
+    int nq, nqp;           // nqp: queries per limb block of a group's B (16 or 32)
+    int nqb, units;        // query blocks of QB queries; units = nqb * splits, unit u = (split u / nqb, block u % nqb)
+    int nq_pad;            // nqb * QB: rows of unit_out's lists and of gthr
+    // split s scans 128-key tiles s * unit_step + i * tile_step, i < tiles_per_unit, below n_tiles
     int64_t n_tiles, unit_step, tile_step, tiles_per_unit;
     uint32_t index_base;
-    uint64_t *cbuf;        // [gridDim.x][4 quadrants][32 queries][KCAP]
-    uint64_t *unit_out;    // [splits * 4][32][KTOP]
-    uint32_t *gthr;        // [32] order-preserving bits of the best published 128th score (0: none)
+    uint64_t *cbuf;        // [gridDim.x][4 quadrants][QB queries][KCAP]
+    uint64_t *unit_out;    // [splits * 4][nq_pad][KTOP]: list (split, quadrant) of every query
+    uint32_t *gthr;        // [nq_pad] order-preserving bits of the best published 128th score (0: none)
     int *status;
 };
 
-// Dimension (0..255) held by byte k of the narrow scan's A rows.
+// Dimension (0..255) held by byte k of the keys-on-M scan's A rows.
 __device__ __forceinline__ int narrow_dim(int k) {
     const int col = k >> 2, p = k & 3;
     const int r = col >> 3, c = (col >> 1) & 3, b = col & 1;
@@ -1136,7 +1147,7 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
 }
 
 
-// kwait for the narrow scan's hand-offs, which come every few hundred
+// kwait for the keys-on-M scan's hand-offs, which come every few hundred
 // nanoseconds: try_wait without a sleep hint (the hardware parks the thread
 // until the phase completes, so waiting warps take no issue slots from the
 // working ones, and wakes it at once), still bounded by the time limit and
@@ -1164,41 +1175,48 @@ __device__ __forceinline__ bool nwait(uint64_t *bar, uint32_t parity, volatile i
 // Tile i of unit `unit`: its first key tb and key count nk; false past the unit's end.
 __device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64_t i, int64_t &tb, int &nk) {
     if (i >= g.tiles_per_unit) return false;
-    const int64_t t = static_cast<int64_t>(unit) * g.unit_step + i * g.tile_step;
+    const int64_t t = static_cast<int64_t>(unit / g.nqb) * g.unit_step + i * g.tile_step;
     if (t >= g.n_tiles) return false;
     tb = t * NK;
     nk = static_cast<int>(g.n_keys - tb < NK ? g.n_keys - tb : NK);
     return true;
 }
 
-template <int MODE, int PREC>
+// The keys-on-M 2-bit scan.  Unit u = (key split u / nqb, query block u % nqb)
+// scans its split's 128-key tiles against the block's QB = 32 NG queries,
+// which stay resident in shared memory as int8 limbs for the whole unit: each
+// key tile is loaded and expanded into TMEM once and meets NG groups of 32
+// queries, one accumulator each (8 MMAs of K = 32 per group).  NG = 1 is the
+// narrow pass (<= 32 queries); NG = 4 the wide scan, where a tile's 32 MMAs
+// (~2000 cycles) hide every per-tile hand-off.
+template <int MODE, int PREC, int NG>
 __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g) {
+    using L = NarrowSmem<NG>;
+    constexpr int QB = L::QB;
+    constexpr int STAGES = L::STAGES;
     constexpr int NL = PREC == PREC_EXACT ? 4 : 3;   // query limbs
     constexpr int EB = 8 * NL - 17;                  // X = round(2^(e + EB) q)
     constexpr float SH = NL == 4 ? 1.52587890625e-05f : 0.00390625f;  // 2^-8 (NL - 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *kf = reinterpret_cast<float *>(smem + NO_KF);
-    float *kn = reinterpret_cast<float *>(smem + NO_KN);
-    float *qc = reinterpret_cast<float *>(smem + NO_QC);
-    float *qc_c = qc;            // filter constant (v units), lowered
-    float *qc_ql = qc + NQ;      // qf / P * SH, lowered (L2)
-    float *qc_P = qc + 2 * NQ;   // s = S * scale * P - |k|^2 qf
-    float *qc_qf = qc + 3 * NQ;
-    float *qc_C = qc + 4 * NQ;   // [4][32]: C_l
-    float *thr_s = reinterpret_cast<float *>(smem + NO_THR);  // [4][32] effective 128th-best score
-    float *thr_l = thr_s + N_QUAD * NQ;                       // [4][32] the same / P * SH, lowered
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + NO_BAR);
-    uint64_t *rfull = bars, *rempty = bars + N_STAGES, *afull = bars + 2 * N_STAGES, *aempty = afull + N_A;
-    uint64_t *accf = aempty + N_A, *acce = accf + N_ACC, *kfr = acce + N_ACC, *qready = kfr + N_KF, *fin = qready + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + NO_MISC);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + NO_MISC + 4);
+    float *kf = reinterpret_cast<float *>(smem + L::O_KF);
+    float *kn = reinterpret_cast<float *>(smem + L::O_KN);
+    float *thr_s = reinterpret_cast<float *>(smem + L::O_THR);  // [4][QB] effective 128th-best score
+    float *thr_l = thr_s + N_QUAD * QB;                         // [4][QB] the same / P * SH, lowered
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::O_BAR);
+    uint64_t *rfull = bars, *rempty = bars + STAGES, *afull = bars + 2 * STAGES, *aempty = afull + N_A;
+    uint64_t *accf = aempty + N_A, *acce = accf + N_ACC, *kfr = acce + N_ACC, *qready = kfr + N_KF;
+    uint64_t *edone = qready + 2, *qfree = edone + 2, *fin = qfree + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::O_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::O_MISC + 4);
+    // the per-query constants of the CTA's unit j live in buffer j % 2: [8][QB] floats
+    float *qconst0 = reinterpret_cast<float *>(smem + L::O_QC);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqp = g.nqp;
     if (threadIdx.x == 0) {
         // one arrival per warp: a warp's lanes meet at __syncwarp and lane 0 arrives
-        for (int s = 0; s < N_STAGES; s++) {
+        for (int s = 0; s < STAGES; s++) {
             st::mbar_init(&rfull[s], 1);
             st::mbar_init(&rempty[s], N_PROD);
         }
@@ -1211,7 +1229,11 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
             st::mbar_init(&acce[a], nqp > EQ ? N_EPI : N_EPI / 2);  // the warps that have queries
         }
         for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
-        st::mbar_init(qready, N_PROD);
+        for (int j = 0; j < 2; j++) {
+            st::mbar_init(&qready[j], N_PROD);
+            st::mbar_init(&edone[j], N_EPI);
+        }
+        st::mbar_init(qfree, 1);
         st::mbar_init(fin, 1);
         *abort_flag = 0;
         st::fence_mbar_init();
@@ -1230,13 +1252,13 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
         if (lane == 0) {
             uint32_t gt = 0;
             bool ok = true;
-            for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x) {
                 int64_t tb;
                 int nk;
                 for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
-                    const uint32_t s = gt % N_STAGES;
-                    if (gt >= N_STAGES &&
-                        !nwait(&rempty[s], ((gt / N_STAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                    const uint32_t s = gt % STAGES;
+                    if (gt >= STAGES &&
+                        !nwait(&rempty[s], ((gt / STAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
@@ -1246,110 +1268,120 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                     const uintptr_t s0 = reinterpret_cast<uintptr_t>(g.scales + tb) & ~uintptr_t(15);
                     const uintptr_t s1 = (reinterpret_cast<uintptr_t>(g.scales + tb + nk) + 15) & ~uintptr_t(15);
                     const uint32_t cb = static_cast<uint32_t>(nk) * 64u, sb = static_cast<uint32_t>(s1 - s0);
-                    uint8_t *dst = smem + NO_RING + s * N_STAGE_BYTES;
+                    uint8_t *dst = smem + L::O_RING + s * N_STAGE_BYTES;
                     st::mbar_arrive_expect_tx(&rfull[s], cb + sb);
                     st::bulk_load(dst, g.codes + tb * 64, cb, &rfull[s]);
                     st::bulk_load(dst + N_CODE_BYTES, reinterpret_cast<const void *>(s0), sb, &rfull[s]);
                 }
             }
             // copies still in flight land before the CTA's shared memory goes away
-            const uint32_t first = gt > N_STAGES ? gt - N_STAGES : 0;
+            const uint32_t first = gt > STAGES ? gt - STAGES : 0;
             for (uint32_t i = first; i < gt; i++)
-                st::mbar_wait(&rfull[i % N_STAGES], (i / N_STAGES) & 1u, g.status, st::DEV_TIMEOUT_FULL);
+                st::mbar_wait(&rfull[i % STAGES], (i / STAGES) & 1u, g.status, st::DEV_TIMEOUT_FULL);
         }
     } else if (warp >= N_EPI && warp < N_MMA_WARP) {
         // ------------------------------------------------------------ producers
         const int pw = warp - N_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
         const int quad = warp & 3, half = pw >> 2;
-        // queries: warp pw prepares queries pw, pw + 8, ..; lane l writes bytes
-        // 8l .. 8l + 7 of every limb row (K chunk l / 16) of the first nqp
-        for (int r = pw; r < NQ; r += N_PROD) {
-            const bool live = r < g.nq;
-            const float *qrow = g.q + static_cast<int64_t>(live ? r : 0) * 256;
-            float m = 0.0f;
-            for (int i = lane; i < 256; i += 32) m = fmaxf(m, live ? fabsf(__ldg(qrow + i)) : 0.0f);
-            m = warp_max(m);
-            const int e = query_exp(m);
-            const float sc = pow2f(e + EB);  // |X| < 2^(8 NL - 2)
-            uint32_t lw[NL][2];
-            int lsum[NL], labs[NL];
-#pragma unroll
-            for (int l = 0; l < NL; l++) {
-                lw[l][0] = lw[l][1] = 0u;
-                lsum[l] = labs[l] = 0;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int dim = narrow_dim(8 * lane + i);
-                int x = __float2int_rn((live ? __ldg(qrow + dim) : 0.0f) * sc);
-#pragma unroll
-                for (int l = 0; l < NL; l++) {
-                    int limb;
-                    if (l < NL - 1) {
-                        limb = ((x + 128) & 255) - 128;  // balanced digit in [-128, 127]
-                        x = (x - limb) >> 8;
-                    } else {
-                        limb = x;  // |top limb| <= 64
-                    }
-                    lw[l][i >> 2] |= (static_cast<uint32_t>(limb) & 255u) << (8 * (i & 3));
-                    lsum[l] += limb;
-                    labs[l] += abs(limb);
-                }
-            }
-#pragma unroll
-            for (int l = 0; l < NL; l++) {
-                lsum[l] = warp_sum(lsum[l]);
-                labs[l] = warp_sum(labs[l]);
-                if (r < nqp) {
-                    const int row = l * nqp + r;
-                    const uint32_t off =
-                        (lane >> 4) * NQ_CHUNK + st::sw128_offset(row, (lane & 15) >> 1) + 8 * (lane & 1);
-                    *reinterpret_cast<uint2 *>(smem + NO_Q + off) = make_uint2(lw[l][0], lw[l][1]);
-                }
-            }
-            if (lane == 0) {
-                // S = sum_l 2^8l (A_l - C_l);  v = 2^8 (1.5 2^23 + A_top) + 1.5 2^23 + A_next
-                // (rounded by at most 128) and S <= 2^(8 (NL - 2)) (v - K) + R
-                float K = 257.0f * MAGIC_F, R = 0.0f;
-                for (int l = 0; l < NL; l++) {
-                    const float C = 1.5f * static_cast<float>(lsum[l]);
-                    qc_C[l * NQ + r] = C;
-                    if (l == NL - 1) K += 256.0f * C;
-                    else if (l == NL - 2) K += C;
-                    else R += 1.5f * static_cast<float>(labs[l]) * pow2f(8 * l);
-                }
-                float P, qf;
-                if (MODE == MODE_DOT) {
-                    P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(-e - EB);
-                    qf = 0.0f;
-                } else {
-                    P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(1 - e - EB);
-                    qf = PREC == PREC_EXACT ? pow2f(e - 1) : 1.0f;
-                }
-                // v and the filter's right-hand side round by at most 128 each, and
-                // K (about 3.2e9) by at most 256
-                qc_c[r] = live ? K - R * SH - 768.0f : INFINITY;
-                qc_ql[r] = lowered(qf / P * SH);
-                qc_P[r] = P;
-                qc_qf[r] = qf;
-            }
-        }
-        st::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) st::mbar_arrive(qready);
-
-        uint32_t gt = 0;
+        uint32_t gt = 0, uj = 0;
         bool ok = true;
-        for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            // the unit's queries: the limbs overwrite the previous unit's, so the
+            // MMAs of that unit must be done; the constants go to buffer uj % 2,
+            // which the epilogue of unit uj - 2 must be done with
+            if (uj >= 1 && !nwait(qfree, (uj - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) break;
+            if (uj >= 2 && !nwait(&edone[uj & 1u], ((uj - 2) >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC))
+                break;
+            float *qc = qconst0 + (uj & 1u) * 8 * QB;
+            float *qc_c = qc, *qc_ql = qc + QB, *qc_P = qc + 2 * QB, *qc_qf = qc + 3 * QB, *qc_C = qc + 4 * QB;
+            const int qbase = (unit % g.nqb) * QB;
+            // warp pw prepares queries pw, pw + 8, ..; lane l writes bytes
+            // 8l .. 8l + 7 of every limb row (K chunk l / 16) of its group
+            for (int r = pw; r < QB; r += N_PROD) {
+                const int qg = qbase + r, grp = r / NQ, rr = r % NQ;
+                const bool live = qg < g.nq;
+                const float *qrow = g.q + static_cast<int64_t>(live ? qg : 0) * 256;
+                float m = 0.0f;
+                for (int i = lane; i < 256; i += 32) m = fmaxf(m, live ? fabsf(__ldg(qrow + i)) : 0.0f);
+                m = warp_max(m);
+                const int e = query_exp(m);
+                const float sc = pow2f(e + EB);  // |X| < 2^(8 NL - 2)
+                uint32_t lw[NL][2];
+                int lsum[NL], labs[NL];
+#pragma unroll
+                for (int l = 0; l < NL; l++) {
+                    lw[l][0] = lw[l][1] = 0u;
+                    lsum[l] = labs[l] = 0;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int dim = narrow_dim(8 * lane + i);
+                    int x = __float2int_rn((live ? __ldg(qrow + dim) : 0.0f) * sc);
+#pragma unroll
+                    for (int l = 0; l < NL; l++) {
+                        int limb;
+                        if (l < NL - 1) {
+                            limb = ((x + 128) & 255) - 128;  // balanced digit in [-128, 127]
+                            x = (x - limb) >> 8;
+                        } else {
+                            limb = x;  // |top limb| <= 64
+                        }
+                        lw[l][i >> 2] |= (static_cast<uint32_t>(limb) & 255u) << (8 * (i & 3));
+                        lsum[l] += limb;
+                        labs[l] += abs(limb);
+                    }
+                }
+#pragma unroll
+                for (int l = 0; l < NL; l++) {
+                    lsum[l] = warp_sum(lsum[l]);
+                    labs[l] = warp_sum(labs[l]);
+                    if (rr < nqp) {
+                        const int row = l * nqp + rr;
+                        const uint32_t off = grp * 2 * NQ_CHUNK + (lane >> 4) * NQ_CHUNK +
+                                             st::sw128_offset(row, (lane & 15) >> 1) + 8 * (lane & 1);
+                        *reinterpret_cast<uint2 *>(smem + L::O_Q + off) = make_uint2(lw[l][0], lw[l][1]);
+                    }
+                }
+                if (lane == 0) {
+                    // S = sum_l 2^8l (A_l - C_l);  v = 2^8 (1.5 2^23 + A_top) + 1.5 2^23 + A_next
+                    // (rounded by at most 128) and S <= 2^(8 (NL - 2)) (v - K) + R
+                    float K = 257.0f * MAGIC_F, R = 0.0f;
+                    for (int l = 0; l < NL; l++) {
+                        const float C = 1.5f * static_cast<float>(lsum[l]);
+                        qc_C[l * QB + r] = C;
+                        if (l == NL - 1) K += 256.0f * C;
+                        else if (l == NL - 2) K += C;
+                        else R += 1.5f * static_cast<float>(labs[l]) * pow2f(8 * l);
+                    }
+                    float P, qf;
+                    if (MODE == MODE_DOT) {
+                        P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(-e - EB);
+                        qf = 0.0f;
+                    } else {
+                        P = PREC == PREC_EXACT ? pow2f(-EB) : pow2f(1 - e - EB);
+                        qf = PREC == PREC_EXACT ? pow2f(e - 1) : 1.0f;
+                    }
+                    // v and the filter's right-hand side round by at most 128 each, and
+                    // K (about 3.2e9) by at most 256
+                    qc_c[r] = live ? K - R * SH - 768.0f : INFINITY;
+                    qc_ql[r] = lowered(qf / P * SH);
+                    qc_P[r] = P;
+                    qc_qf[r] = qf;
+                }
+            }
+            st::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) st::mbar_arrive(&qready[uj & 1u]);
+
             int64_t tb;
             int nk;
             for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
-                const uint32_t s = gt % N_STAGES, b = gt % N_A, f = gt % N_KF;
-                if (!nwait(&rfull[s], (gt / N_STAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
+                const uint32_t s = gt % STAGES, b = gt % N_A, f = gt % N_KF;
+                if (!nwait(&rfull[s], (gt / STAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
                     ok = false;
                     break;
                 }
-                const uint8_t *stage = smem + NO_RING + s * N_STAGE_BYTES;
+                const uint8_t *stage = smem + L::O_RING + s * N_STAGE_BYTES;
                 const int sofs = static_cast<int>((reinterpret_cast<uintptr_t>(g.scales + tb) & 15u) >> 2);
                 uint4 cw[2];
                 int key[2];
@@ -1382,8 +1414,9 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 if (lane == 0) st::mbar_arrive(&rempty[s]);  // the stage's bytes are in registers
                 // A buffer b is free once the MMAs of tile gt - 2 are done.  Slot
                 // f = gt % 8 is then free too: those MMAs started only after the
-                // epilogue released the accumulator of tile gt - 5, so it is done
-                // with every tile up to gt - 5, and slot f last held tile gt - 8.
+                // epilogue released the accumulator of step (gt - 2) NG + NG - 4,
+                // so it is done with every tile up to gt - 5 (NG = 1) or gt - 3
+                // (NG = 4), and slot f last held tile gt - 8.
                 if (gt >= N_A &&
                     !nwait(&aempty[b], ((gt / N_A) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
                     ok = false;
@@ -1424,31 +1457,45 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
             // kind::i8: D s32, A unsigned 8-bit, B signed 8-bit, M = 128
             const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NL * nqp >> 3) << 17) |
                                    (static_cast<uint32_t>(NK >> 4) << 24);
-            bool ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
-            st::tc_fence_after();
-            const uint32_t qb = st::smem_u32(smem + NO_Q);
-            uint64_t bdesc[8];  // the queries' descriptors do not change from tile to tile
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) bdesc[kk] = st::sdesc_sw128(qb + (kk >> 2) * NQ_CHUNK + (kk & 3) * 32, 16, 1024);
-            uint32_t gt = 0;
-            for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
+            const uint32_t qbuf = st::smem_u32(smem + L::O_Q);
+            uint32_t gt = 0, gs = 0, uj = 0;  // tiles, (tile, group) steps, units so far
+            bool ok = true;
+            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+                if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+                st::tc_fence_after();
                 int64_t tb;
                 int nk;
                 for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
-                    const uint32_t b = gt % N_A, a = gt % N_ACC;
-                    if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL) ||
-                        (gt >= N_ACC &&
-                         !nwait(&acce[a], ((gt / N_ACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY))) {
+                    const uint32_t b = gt % N_A;
+                    if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
                         ok = false;
                         break;
                     }
                     st::tc_fence_after();
-                    const uint32_t acc = tmem + N_ACC_COL + a * N_ACC_COLS, abuf = tmem + b * 64u;
+                    const uint32_t abuf = tmem + b * 64u;
+#pragma unroll 1
+                    for (int grp = 0; grp < NG; grp++, gs++) {
+                        const uint32_t a = gs % N_ACC;
+                        if (gs >= N_ACC &&
+                            !nwait(&acce[a], ((gs / N_ACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        st::tc_fence_after();
+                        const uint32_t acc = tmem + N_ACC_COL + a * N_ACC_COLS;
+                        const uint32_t gq = qbuf + grp * 2 * NQ_CHUNK;
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) umma_i8_ts(acc, abuf + 8 * kk, bdesc[kk], idesc, kk > 0 ? 1u : 0u);
+                        for (int kk = 0; kk < 8; kk++)
+                            umma_i8_ts(acc, abuf + 8 * kk,
+                                       st::sdesc_sw128(gq + (kk >> 2) * NQ_CHUNK + (kk & 3) * 32, 16, 1024), idesc,
+                                       kk > 0 ? 1u : 0u);
+                        st::umma_commit(&accf[a]);
+                    }
+                    if (!ok) break;
                     st::umma_commit(&aempty[b]);
-                    st::umma_commit(&accf[a]);
                 }
+                // the unit's MMAs are done with its queries once this arrives
+                st::umma_commit(qfree);
             }
             // every MMA issued above completes before the TMEM is released
             st::umma_commit(fin);
@@ -1457,154 +1504,189 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
     } else {
         // ------------------------------------------------------------ epilogue
         // Warp w reads TMEM lanes 32 (w % 4) .. (keys 32 (w % 4) + lane of every
-        // tile) and the columns of queries q0 = 16 (w / 4) .. q0 + 15; lane l < 16
-        // owns the candidate buffer, count and thresholds of query q0 + l for its
-        // quadrant.
+        // tile) and, in every group, the columns of queries q0 = 16 (w / 4) ..
+        // q0 + 15; lane l < 16 owns the candidate buffer, count and thresholds
+        // of query 32 grp + q0 + l of its quadrant.
         const int quad = warp & 3, q0 = EQ * (warp >> 2);
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
-        uint64_t *bufs = g.cbuf + (static_cast<int64_t>(blockIdx.x) * N_QUAD + quad) * NQ * KCAP;
-        uint64_t *my_buf = bufs + static_cast<int64_t>(q0 + (lane & (EQ - 1))) * KCAP;
-        float *slot = reinterpret_cast<float *>(smem + NO_SLOT) + threadIdx.x;  // slot[i * 256]: query q0 + i
-        float *wthr = thr_s + quad * NQ, *wthrl = thr_l + quad * NQ;
-        const bool qlive = lane < EQ && q0 + lane < g.nq;
+        uint64_t *bufs = g.cbuf + (static_cast<int64_t>(blockIdx.x) * N_QUAD + quad) * QB * KCAP;
+        float *slot = reinterpret_cast<float *>(smem + L::O_SLOT) + threadIdx.x;  // slot[i * 256]: query q0 + i
+        float *wthr = thr_s + quad * QB, *wthrl = thr_l + quad * QB;
         const uint32_t acc0 = tmem + lane_addr + N_ACC_COL;
-        bool ok = q0 < nqp;  // with 16 queries per limb block the second warp of each quadrant has none
-        if (ok) ok = nwait(qready, 0, abort_flag, g.status, st::DEV_TIMEOUT_FULL);
-        uint32_t gt = 0;
+        const bool has_q = q0 < nqp;  // with 16 queries per limb block the second warp of each quadrant has none
         const int top = (NL - 1) * nqp + q0, next = (NL - 2) * nqp + q0;
-        for (int unit = blockIdx.x; unit < g.splits && ok; unit += gridDim.x) {
-            int cnt = 0;
-            float thr = qlive ? -INFINITY : INFINITY;  // this list's 128th best
-            float eff = thr;                           // the best 128th any list has published
-            uint32_t pub = 0u, pub_next = 0u;          // published thresholds, read one tile ahead of use
-            if (lane < EQ) {
-                wthr[q0 + lane] = eff;
-                wthrl[q0 + lane] = eff;
+        uint32_t gt = 0, gs = 0, uj = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            // every epilogue warp (even one without queries) waits for the unit's
+            // queries, so no warp's edone arrival runs two units ahead
+            if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+            const float *qc = qconst0 + (uj & 1u) * 8 * QB;
+            const float *qc_c = qc, *qc_ql = qc + QB, *qc_P = qc + 2 * QB, *qc_qf = qc + 3 * QB, *qc_C = qc + 4 * QB;
+            const int qbase = (unit % g.nqb) * QB;
+            int cnt[NG];
+            float thr[NG], eff[NG];          // this list's 128th best; the best 128th any list has published
+            uint32_t pub[NG], pub_next[NG];  // published thresholds, read one tile ahead of use
+            bool qlive[NG];
+#pragma unroll
+            for (int grp = 0; grp < NG; grp++) {
+                qlive[grp] = has_q && lane < EQ && qbase + NQ * grp + q0 + lane < g.nq;
+                cnt[grp] = 0;
+                thr[grp] = qlive[grp] ? -INFINITY : INFINITY;
+                eff[grp] = thr[grp];
+                pub[grp] = pub_next[grp] = 0u;
+                if (has_q && lane < EQ) {
+                    wthr[NQ * grp + q0 + lane] = eff[grp];
+                    wthrl[NQ * grp + q0 + lane] = eff[grp];
+                }
             }
             __syncwarp();
             int64_t tb;
             int nk;
-            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
-                const uint32_t a = gt % N_ACC, f = gt % N_KF;
-                // the published thresholds: read now, merged after the next tile (the
-                // read's latency stays off this tile's path)
-                pub = pub_next;
-                pub_next = 0u;
-                if (qlive && (gt & 15u) == 0u) pub_next = __ldcg(g.gthr + q0 + lane);
-                if (!nwait(&accf[a], (gt / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC) ||
-                    !nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+            for (int64_t i = 0; has_q && narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                const uint32_t f = gt % N_KF;
+                if (!nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                     ok = false;
                     break;
                 }
-                st::tc_fence_after();
-                const uint32_t acc = acc0 + a * N_ACC_COLS;
-                uint32_t rt[EQ], rn[EQ];
-                st::tmem_ld16(acc + top, rt);
-                st::tmem_ld16(acc + next, rn);
                 const int kk = 32 * quad + lane;
                 const float scale = kf[f * NK + kk];
                 const float nrm = kn[f * NK + kk];
-                st::tmem_ld_wait();
                 const bool klive = kk < nk;
                 const float inv_s = rcp_approx(scale);
-                bool any = false;
+                const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
 #pragma unroll
-                for (int q4 = 0; q4 < EQ; q4 += 4) {
-                    const float4 cc = *reinterpret_cast<const float4 *>(qc_c + q0 + q4);
-                    const float4 th = *reinterpret_cast<const float4 *>(wthrl + q0 + q4);
-                    const float ca[4] = {cc.x, cc.y, cc.z, cc.w}, tha[4] = {th.x, th.y, th.z, th.w};
-                    float qla[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    if (MODE == MODE_L2) {
-                        const float4 ql = *reinterpret_cast<const float4 *>(qc_ql + q0 + q4);
-                        qla[0] = ql.x; qla[1] = ql.y; qla[2] = ql.z; qla[3] = ql.w;
+                for (int grp = 0; grp < NG; grp++, gs++) {
+                    const uint32_t a = gs % N_ACC;
+                    const int qo = NQ * grp + q0;  // this warp's first query of the group, in the unit
+                    uint64_t *gbuf = bufs + static_cast<int64_t>(qo) * KCAP;
+                    uint64_t *my_buf = gbuf + static_cast<int64_t>(lane & (EQ - 1)) * KCAP;
+                    // the published thresholds: read now, merged after the next tile (the
+                    // read's latency stays off this tile's path)
+                    pub[grp] = pub_next[grp];
+                    pub_next[grp] = 0u;
+                    if (qlive[grp] && (gt & 15u) == 0u) pub_next[grp] = __ldcg(g.gthr + qbase + qo + lane);
+                    if (!nwait(&accf[a], (gs / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+                        ok = false;
+                        break;
                     }
+                    st::tc_fence_after();
+                    const uint32_t acc = acc0 + a * N_ACC_COLS;
+                    uint32_t rt[EQ], rn[EQ];
+                    st::tmem_ld16(acc + top, rt);
+                    st::tmem_ld16(acc + next, rn);
+                    st::tmem_ld_wait();
+                    bool any = false;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float v = fmaf(__uint_as_float(rt[q4 + i] + MAGIC_I), 256.0f,
-                                             __uint_as_float(rn[q4 + i] + MAGIC_I));
-                        const float t = MODE == MODE_L2 ? fmaf(nrm, qla[i], tha[i]) : tha[i];
-                        any |= v >= fmaf(t, inv_s, ca[i]);
-                    }
-                }
-                any = any && klive;
-                const bool slow = __any_sync(0xffffffffu, any);
-                if (!slow) {  // nothing more to read: the accumulator goes back to the MMA now
-                    st::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) st::mbar_arrive(&acce[a]);
-                }
-                if (slow) {
-                    // the exact path: S = sum_l 2^8l (A_l - C_l) from every limb, top
-                    // down, the partial sums kept in this thread's score slots
-                    float *sl = slot;
-                    if (any) {
+                    for (int q4 = 0; q4 < EQ; q4 += 4) {
+                        const float4 cc = *reinterpret_cast<const float4 *>(qc_c + qo + q4);
+                        const float4 th = *reinterpret_cast<const float4 *>(wthrl + qo + q4);
+                        const float ca[4] = {cc.x, cc.y, cc.z, cc.w}, tha[4] = {th.x, th.y, th.z, th.w};
+                        float qla[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        if (MODE == MODE_L2) {
+                            const float4 ql = *reinterpret_cast<const float4 *>(qc_ql + qo + q4);
+                            qla[0] = ql.x; qla[1] = ql.y; qla[2] = ql.z; qla[3] = ql.w;
+                        }
 #pragma unroll
-                        for (int i = 0; i < EQ; i++)
-                            sl[i * (N_EPI * 32)] =
-                                fmaf(__uint_as_float(rt[i] + MAGIC_I) - MAGIC_F - qc_C[(NL - 1) * NQ + q0 + i], 256.0f,
-                                     __uint_as_float(rn[i] + MAGIC_I) - MAGIC_F - qc_C[(NL - 2) * NQ + q0 + i]);
+                        for (int i2 = 0; i2 < 4; i2++) {
+                            const float v = fmaf(__uint_as_float(rt[q4 + i2] + MAGIC_I), 256.0f,
+                                                 __uint_as_float(rn[q4 + i2] + MAGIC_I));
+                            const float t = MODE == MODE_L2 ? fmaf(nrm, qla[i2], tha[i2]) : tha[i2];
+                            any |= v >= fmaf(t, inv_s, ca[i2]);
+                        }
                     }
-#pragma unroll 1
-                    for (int l = NL - 3; l >= 0; l--) {
-                        st::tmem_ld16(acc + l * nqp + q0, rt);
-                        st::tmem_ld_wait();
+                    any = any && klive;
+                    const bool slow = __any_sync(0xffffffffu, any);
+                    if (!slow) {  // nothing more to read: the accumulator goes back to the MMA now
+                        st::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) st::mbar_arrive(&acce[a]);
+                    }
+                    if (slow) {
+                        // the exact path: S = sum_l 2^8l (A_l - C_l) from every limb, top
+                        // down, the partial sums kept in this thread's score slots
+                        float *sl = slot;
                         if (any) {
 #pragma unroll
-                            for (int i = 0; i < EQ; i++)
-                                sl[i * (N_EPI * 32)] =
-                                    fmaf(sl[i * (N_EPI * 32)], 256.0f,
-                                         __uint_as_float(rt[i] + MAGIC_I) - MAGIC_F - qc_C[l * NQ + q0 + i]);
+                            for (int i2 = 0; i2 < EQ; i2++)
+                                sl[i2 * (N_EPI * 32)] =
+                                    fmaf(__uint_as_float(rt[i2] + MAGIC_I) - MAGIC_F - qc_C[(NL - 1) * QB + qo + i2],
+                                         256.0f,
+                                         __uint_as_float(rn[i2] + MAGIC_I) - MAGIC_F - qc_C[(NL - 2) * QB + qo + i2]);
                         }
-                    }
-                    st::tc_fence_before();  // every limb is read: release the accumulator
-                    __syncwarp();
-                    if (lane == 0) st::mbar_arrive(&acce[a]);
-                    uint32_t pass = 0;
-                    if (any) {
+#pragma unroll 1
+                        for (int l = NL - 3; l >= 0; l--) {
+                            st::tmem_ld16(acc + l * nqp + q0, rt);
+                            st::tmem_ld_wait();
+                            if (any) {
 #pragma unroll
-                        for (int i = 0; i < EQ; i++) {
-                            float sc = sl[i * (N_EPI * 32)] * scale * qc_P[q0 + i];
-                            if (MODE == MODE_L2) sc = fmaf(-nrm, qc_qf[q0 + i], sc);
-                            sl[i * (N_EPI * 32)] = sc;
-                            pass |= (sc >= wthr[q0 + i] ? 1u : 0u) << i;
+                                for (int i2 = 0; i2 < EQ; i2++)
+                                    sl[i2 * (N_EPI * 32)] =
+                                        fmaf(sl[i2 * (N_EPI * 32)], 256.0f,
+                                             __uint_as_float(rt[i2] + MAGIC_I) - MAGIC_F - qc_C[l * QB + qo + i2]);
+                            }
+                        }
+                        st::tc_fence_before();  // every limb is read: release the accumulator
+                        __syncwarp();
+                        if (lane == 0) st::mbar_arrive(&acce[a]);
+                        uint32_t pass = 0;
+                        if (any) {
+#pragma unroll
+                            for (int i2 = 0; i2 < EQ; i2++) {
+                                float sc = sl[i2 * (N_EPI * 32)] * scale * qc_P[qo + i2];
+                                if (MODE == MODE_L2) sc = fmaf(-nrm, qc_qf[qo + i2], sc);
+                                sl[i2 * (N_EPI * 32)] = sc;
+                                pass |= (sc >= wthr[qo + i2] ? 1u : 0u) << i2;
+                            }
+                        }
+                        unsigned qm = __reduce_or_sync(0xffffffffu, pass);
+                        while (qm) {
+                            const int i2 = __ffs(qm) - 1;
+                            qm &= qm - 1;
+                            const bool p = (pass >> i2) & 1u;
+                            const unsigned m = __ballot_sync(0xffffffffu, p);
+                            const int base = __shfl_sync(0xffffffffu, cnt[grp], i2);
+                            if (p)
+                                gbuf[static_cast<int64_t>(i2) * KCAP + base + __popc(m & lt)] =
+                                    make_key(slot[i2 * (N_EPI * 32)], idx);
+                            if (lane == i2) cnt[grp] += __popc(m);
                         }
                     }
-                    unsigned qm = __reduce_or_sync(0xffffffffu, pass);
-                    const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
-                    while (qm) {
-                        const int i = __ffs(qm) - 1;
-                        qm &= qm - 1;
-                        const bool p = (pass >> i) & 1u;
-                        const unsigned m = __ballot_sync(0xffffffffu, p);
-                        const int base = __shfl_sync(0xffffffffu, cnt, i);
-                        if (p)
-                            bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(m & lt)] =
-                                make_key(slot[i * (N_EPI * 32)], idx);
-                        if (lane == i) cnt += __popc(m);
+                    const unsigned need = __ballot_sync(0xffffffffu, cnt[grp] > KCAP - NK / 4);
+                    if (need) {
+                        const float before = thr[grp];
+                        warp_compact(need, my_buf, cnt[grp], thr[grp], nullptr, false);
+                        if (thr[grp] > before) atomicMax(g.gthr + qbase + qo + lane, ord_f32(thr[grp]));
+                    }
+                    const float ne = fmaxf(fmaxf(thr[grp], thr_of(pub[grp])), eff[grp]);
+                    if (__any_sync(0xffffffffu, ne > eff[grp])) {
+                        if (qlive[grp]) {
+                            eff[grp] = ne;
+                            wthr[qo + lane] = ne;
+                            wthrl[qo + lane] = lowered(ne / qc_P[qo + lane] * SH);
+                        }
+                        __syncwarp();
                     }
                 }
-                const unsigned need = __ballot_sync(0xffffffffu, cnt > KCAP - NK / 4);
-                if (need) {
-                    const float before = thr;
-                    warp_compact(need, my_buf, cnt, thr, nullptr, false);
-                    if (thr > before) atomicMax(g.gthr + q0 + lane, ord_f32(thr));
-                }
-                const float ne = fmaxf(fmaxf(thr, thr_of(pub)), eff);
-                if (__any_sync(0xffffffffu, ne > eff)) {
-                    if (qlive) {
-                        eff = ne;
-                        wthr[q0 + lane] = eff;
-                        wthrl[q0 + lane] = lowered(eff / qc_P[q0 + lane] * SH);
-                    }
-                    __syncwarp();
-                }
+                if (!ok) break;
             }
             if (!ok) break;
-            uint64_t *my_out =
-                g.unit_out + ((static_cast<int64_t>(unit) * N_QUAD + quad) * NQ + q0 + (lane & (EQ - 1))) * KTOP;
-            const unsigned need = __ballot_sync(0xffffffffu, qlive);
-            warp_compact(need, my_buf, cnt, thr, my_out, true);
+            if (has_q) {
+                const int split = unit / g.nqb;
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+                    const int qo = NQ * grp + q0;
+                    uint64_t *my_buf = bufs + static_cast<int64_t>(qo + (lane & (EQ - 1))) * KCAP;
+                    uint64_t *my_out = g.unit_out + ((static_cast<int64_t>(split) * N_QUAD + quad) * g.nq_pad +
+                                                     qbase + qo + (lane & (EQ - 1))) * KTOP;
+                    const unsigned need = __ballot_sync(0xffffffffu, qlive[grp]);
+                    warp_compact(need, my_buf, cnt[grp], thr[grp], my_out, true);
+                }
+            }
+            // this unit's constants may be overwritten now
+            __syncwarp();
+            if (lane == 0) st::mbar_arrive(&edone[uj & 1u]);
         }
     }
 
@@ -1620,7 +1702,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
 // holds fewer): a lower bound for query q's final 128th best, since the keys
 // behind it are a subset of the keys scanned.
 __global__ void k_knn_seed(const uint64_t *keys, int nq, uint32_t *gthr) {
-    const int q = threadIdx.x;
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q < nq) gthr[q] = static_cast<uint32_t>(keys[static_cast<int64_t>(q) * KTOP + KTOP - 1] >> 32);
 }
 
@@ -1642,16 +1724,17 @@ st_status merge_lists(st_handle *h, const uint64_t *lists, int64_t n_lists, int6
     return st_after_launch(h, "k_knn_merge");
 }
 
-template <int MODE, int PREC>
+template <int MODE, int PREC, int NG>
 st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
-    auto kern = k_knn_narrow<MODE, PREC>;
+    auto kern = k_knn_narrow<MODE, PREC, NG>;
     static bool attr_done = false;
     if (!attr_done) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, NARROW_SMEM));
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              NarrowSmem<NG>::SMEM));
         attr_done = true;
     }
-    kern<<<grid, N_THREADS, NARROW_SMEM, h->stream>>>(g);
-    return st_after_launch(h, "k_knn_narrow");
+    kern<<<grid, N_THREADS, NarrowSmem<NG>::SMEM, h->stream>>>(g);
+    return st_after_launch(h, NG == 1 ? "k_knn_narrow" : "k_knn_wide8");
 }
 
 }  // namespace
@@ -1664,30 +1747,47 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (s != ST_OK) return s;
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
-    if (!ranges && dim == 256 && nq <= NQ && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
-        // a few queries: the narrow scan (keys on the MMA's M side), one pass
+    if (!ranges && dim == 256 && (nq <= NQ || prec == 0) && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
+        // dim 256: the keys-on-M scan (keys as the kind::i8 A operand in TMEM).
+        // Up to 32 queries: one group per unit (the narrow pass).  More (EXACT):
+        // units of 128 queries (4 groups) resident in shared memory, every key
+        // tile meeting all four -- the wide scan.  F16REF with more queries
+        // stays on k_knn_scan, which rounds the dequantised keys to f16 as the
+        // reference does.
+        const bool wide = nq > NQ;
+        const int qb_size = wide ? 4 * NQ : NQ;
+        const int nqb = static_cast<int>((nq + qb_size - 1) / qb_size);
+        const int64_t nq_pad = static_cast<int64_t>(nqb) * qb_size;
         const int64_t tiles = (n_keys + NK - 1) / NK;
-        int64_t splits = std::min<int64_t>(tiles, h->num_sms);
+        // narrow: one key split per SM; wide: about eight units per SM
+        int64_t splits = wide ? std::max<int64_t>(1, (8LL * h->num_sms + nqb - 1) / nqb) : h->num_sms;
+        splits = std::min<int64_t>(splits, tiles);
         const int64_t tps = (tiles + splits - 1) / splits;
         splits = (tiles + tps - 1) / tps;
-        const int grid = static_cast<int>(splits);
+        const int64_t units = splits * nqb;
+        if (units > (1LL << 30)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
+        const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
+        const int64_t sample_splits = wide ? splits : h->num_sms;  // the sample passes' key splits
+        const int64_t max_splits = std::max(splits, sample_splits);
+        // candidate buffers for the widest grid any pass launches (the sample passes have up to
+        // sample_splits * nqb units)
+        const int64_t grid_max = std::min<int64_t>(std::max(units, sample_splits * nqb), h->num_sms);
         uint64_t *cbuf = static_cast<uint64_t *>(
-            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_QUAD * NQ * KCAP));
-        const size_t out_bytes = sizeof(uint64_t) * splits * N_QUAD * NQ * KTOP;
-        const size_t seed_bytes = sizeof(uint64_t) * NQ * KTOP;
+            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid_max * N_QUAD * qb_size * KCAP));
+        const size_t out_bytes = sizeof(uint64_t) * max_splits * N_QUAD * nq_pad * KTOP;
+        const size_t seed_bytes = sizeof(uint64_t) * nq_pad * KTOP;
         constexpr int MERGE_GROUPS = 16;
-        const size_t tmp_bytes = sizeof(uint64_t) * MERGE_GROUPS * NQ * KTOP;
-        uint8_t *part =
-            static_cast<uint8_t *>(st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + tmp_bytes + 256));
+        const size_t tmp_bytes = sizeof(uint64_t) * MERGE_GROUPS * nq_pad * KTOP;
+        uint8_t *part = static_cast<uint8_t *>(
+            st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + tmp_bytes + sizeof(uint32_t) * nq_pad + 256));
         if (!cbuf || !part) return ST_NO_MEMORY;
         uint64_t *unit_out = reinterpret_cast<uint64_t *>(part);
         uint64_t *seed_keys = reinterpret_cast<uint64_t *>(part + out_bytes);
         uint64_t *merge_tmp = reinterpret_cast<uint64_t *>(part + out_bytes + seed_bytes);
         uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes + tmp_bytes);
-        ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, NQ * sizeof(uint32_t), h->stream));
-        // queries per limb block: a multiple of 8 with (limbs x it) a multiple of 16
+        ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, nq_pad * sizeof(uint32_t), h->stream));
         // queries per limb block: 16 or 32 (an epilogue warp takes 16; NL x 16 is a multiple of 16)
-        const int nqp = nq <= EQ ? EQ : NQ;
+        const int nqp = (!wide && nq <= EQ) ? EQ : NQ;
         NarrowArgs g{};
         g.codes = codes;
         g.scales = scales;
@@ -1695,6 +1795,8 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.n_keys = n_keys;
         g.nq = static_cast<int>(nq);
         g.nqp = nqp;
+        g.nqb = nqb;
+        g.nq_pad = static_cast<int>(nq_pad);
         g.n_tiles = tiles;
         g.index_base = static_cast<uint32_t>(index_base);
         g.cbuf = cbuf;
@@ -1702,10 +1804,16 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.gthr = gthr;
         g.status = h->d_status;
         auto run = [&](const NarrowArgs &a, int gr) {
-            if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT>(h, a, gr);
-            if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF>(h, a, gr);
-            if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT>(h, a, gr);
-            return launch_narrow<MODE_L2, PREC_F16REF>(h, a, gr);
+            if (wide) {
+                if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT, 4>(h, a, gr);
+                if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF, 4>(h, a, gr);
+                if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT, 4>(h, a, gr);
+                return launch_narrow<MODE_L2, PREC_F16REF, 4>(h, a, gr);
+            }
+            if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT, 1>(h, a, gr);
+            if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF, 1>(h, a, gr);
+            if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT, 1>(h, a, gr);
+            return launch_narrow<MODE_L2, PREC_F16REF, 1>(h, a, gr);
         };
         // Large scans first take a sample of the tiles: the best 128 of a sample
         // bound each query's final 128th best from below, and every list of the
@@ -1716,26 +1824,27 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
             const int64_t sample = (tiles + stride - 1) / stride;
             if (sample < 2 * h->num_sms) continue;
             NarrowArgs gs = g;
-            const int gsplits = h->num_sms;
-            gs.splits = gsplits;
+            const int64_t gsplits = std::min<int64_t>(sample_splits, sample);
+            gs.units = static_cast<int>(gsplits * nqb);
             gs.unit_step = stride;
             gs.tile_step = stride * gsplits;
             gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
-            s = run(gs, gsplits);
+            s = run(gs, static_cast<int>(std::min<int64_t>(gs.units, h->num_sms)));
             if (s != ST_OK) return s;
-            s = merge_lists(h, unit_out, gsplits * N_QUAD, NQ * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
+            s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
             if (s != ST_OK) return s;
-            k_knn_seed<<<1, 32, 0, h->stream>>>(seed_keys, static_cast<int>(nq), gthr);
+            k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
+                                                                                       static_cast<int>(nq), gthr);
             s = st_after_launch(h, "k_knn_seed");
             if (s != ST_OK) return s;
         }
-        g.splits = static_cast<int>(splits);
+        g.units = static_cast<int>(units);
         g.unit_step = tps;
         g.tile_step = 1;
         g.tiles_per_unit = tps;
         s = run(g, grid);
         if (s != ST_OK) return s;
-        return merge_lists(h, unit_out, splits * N_QUAD, NQ * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
+        return merge_lists(h, unit_out, splits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
     }
     const int nqb = static_cast<int>((nq + KQ - 1) / KQ);
     const int64_t tiles = (n_keys + KT - 1) / KT;

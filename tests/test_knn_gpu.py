@@ -285,3 +285,36 @@ def test_mem_file_round_trip_and_sharded_load(dev, tmp_path):
     assert torch.equal(merged, whole)
     _, ids = halves[1].search_ids(q)
     assert int(ids[ids >= 0].min()) >= 1400
+
+
+@pytest.mark.parametrize("mode", ["dot", "l2"])
+@pytest.mark.parametrize("n,nq", [(129, 33), (70_001, 300), (700_001, 129), (2_600_000, 257)])
+def test_wide_keys_on_m_scan_matches_oracle(dev, mode, n, nq):
+    """More than 32 EXACT queries at dim 256 run the keys-on-M scan with 128
+    queries resident per unit (k_knn_wide8): ragged query blocks (33, 129,
+    257, 300 queries), ragged key tiles, scans big enough for the 1-in-1024
+    and 1-in-16 sample passes that seed the thresholds, every query block
+    meeting every key split.  Same bars as the other EXACT cases."""
+    import scratchtape_b200.knn as K
+    codes, scales = K.synth_keys(n, 256, seed=n % 97)
+    rng = np.random.default_rng(n + nq)
+    q = rng.standard_normal((nq, 256)).astype(np.float32)
+    q[1] *= 25.0
+    s, i = K.search(codes, scales, torch.from_numpy(q).cuda(), k=128, mode=mode, prec="exact")
+    _check_exact(q, codes.cpu().numpy(), scales.cpu().numpy(), s.cpu().numpy(), i.cpu().numpy(), 128, mode)
+
+
+def test_wide_scan_repeats_bit_for_bit_and_matches_shards(dev):
+    """The wide scan is deterministic, and two shards scanned with their own
+    index_base and merged give the one-scan result bit for bit."""
+    import scratchtape_b200.knn as K
+    n, nq = 1_000_003, 200
+    codes, scales = K.synth_keys(n, 256, seed=5)
+    q = torch.from_numpy(np.random.default_rng(6).standard_normal((nq, 256)).astype(np.float32)).cuda()
+    whole = K.topk_keys(codes, scales, q, mode="dot")
+    again = K.topk_keys(codes, scales, q, mode="dot")
+    assert torch.equal(whole, again)
+    cut = 400_001
+    parts = [K.topk_keys(codes[:cut], scales[:cut], q, mode="dot", index_base=0),
+             K.topk_keys(codes[cut:], scales[cut:], q, mode="dot", index_base=cut)]
+    assert torch.equal(K.merge_keys(torch.stack(parts), nq), whole)
