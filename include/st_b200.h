@@ -216,16 +216,20 @@ ST_API st_status st_softmax_rows_bwd(st_handle *h, const float *dy, const float 
 /* Fused attention over bh independent heads, f16 storage with f32
  * accumulation on tcgen05 (kind::f16): per head S = scale * Q K^T, causal
  * mask (column j visible to row i iff j <= i), P = softmax(S), O = P V.
+ * one: softmax1 instead -- a phantom zero logit in every row's denominator,
+ * shifted by max(row max, 0) (DeviceTape::causal_softmax(x, scale, one),
+ * src/gpu_step/tape.rs:225; Config.softmax1 :400).
  * q, k, v, o: device f16 [bh, t, d], head z at z*t*d (16-byte aligned);
  * lse: device f32 [bh, t], the natural-log sum of exp of each scaled, masked
- * row (for the backward).  t <= 128, d = 64.  Replaces the chain
+ * row, the phantom term included (for the backward).  t <= 256 (the
+ * reference's MAX_SEQ), d = 64.  Replaces the chain
  * batched_matmul(q, k, transpose_b) -> scale -> + mask -> softmax ->
  * batched_matmul(w, v) of TransformerBlock::forward_full (src/nn.rs:646-671)
  * and of DeviceTape::block_forward (src/gpu_step/tape.rs:481-484). */
 ST_API st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse, int64_t bh,
-                             int64_t t, int64_t d, float scale, int32_t causal);
+                             int64_t t, int64_t d, float scale, int32_t causal, int32_t one);
 /* Backward: dq, dk, dv (device f16 [bh, t, d]) from q, k, v, o, dout (f16)
- * and lse (f32) of st_attn_fwd.  Replaces batched_matmul_backward
+ * and lse (f32) of st_attn_fwd (softmax or softmax1: lse carries it).  Replaces batched_matmul_backward
  * (src/tape.rs:90-112) and the softmax backward (src/gpu_step/rows.rs:117-123,
  * src/gpu_step/tape.rs:363-375). */
 ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o, const void *dout,
@@ -239,7 +243,7 @@ ST_API st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const v
  * merged), lse [batch*heads, t].  Operands are rounded to f16 as they are
  * staged (f32 accumulation); no split/merge copies. */
 ST_API st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o, float *lse, int64_t batch, int64_t heads,
-                                    int64_t t, int64_t d, float scale, int32_t causal);
+                                    int64_t t, int64_t d, float scale, int32_t causal, int32_t one);
 /* Backward on the same layouts: dqkv [batch*t, 3*heads*d] from qkv, o, dout
  * [batch*t, heads*d] and lse. */
 ST_API st_status st_attn_bwd_packed(st_handle *h, const float *qkv, const float *o, const float *dout, const float *lse,

@@ -109,12 +109,12 @@ extern "C" {
     pub fn st_softmax_rows_bwd(h: *mut st_handle, dy: *const f32, y: *const f32, dx: *mut f32, rows: i64, n: i64,
                                scale: f32) -> st_status;
     pub fn st_attn_fwd(h: *mut st_handle, q: *const c_void, k: *const c_void, v: *const c_void, o: *mut c_void,
-                       lse: *mut f32, bh: i64, t: i64, d: i64, scale: f32, causal: i32) -> st_status;
+                       lse: *mut f32, bh: i64, t: i64, d: i64, scale: f32, causal: i32, one: i32) -> st_status;
     pub fn st_attn_bwd(h: *mut st_handle, q: *const c_void, k: *const c_void, v: *const c_void, o: *const c_void,
                        dout: *const c_void, lse: *const f32, dq: *mut c_void, dk: *mut c_void, dv: *mut c_void,
                        bh: i64, t: i64, d: i64, scale: f32, causal: i32) -> st_status;
     pub fn st_attn_fwd_packed(h: *mut st_handle, qkv: *const f32, o: *mut f32, lse: *mut f32, batch: i64, heads: i64,
-                              t: i64, d: i64, scale: f32, causal: i32) -> st_status;
+                              t: i64, d: i64, scale: f32, causal: i32, one: i32) -> st_status;
     pub fn st_attn_bwd_packed(h: *mut st_handle, qkv: *const f32, o: *const f32, dout: *const f32, lse: *const f32,
                               dqkv: *mut f32, batch: i64, heads: i64, t: i64, d: i64, scale: f32,
                               causal: i32) -> st_status;

@@ -73,9 +73,9 @@ SIGNATURES = {
     "st_mlp_step_tf32": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64]),
     "st_softmax_rows": (_st, [_h, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_softmax_rows_bwd": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _f32]),
-    "st_attn_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
+    "st_attn_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_attn_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i32]),
-    "st_attn_fwd_packed": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32]),
+    "st_attn_fwd_packed": (_st, [_h, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _i32]),
     "st_attn_bwd_packed": (_st, [_h, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32]),
     "st_embed_fwd": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i64, _i64]),
     "st_embed_bwd": (_st, [_h, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32]),

@@ -2,7 +2,9 @@
 
 Mirrors the attention of TransformerBlock::forward_full (src/nn.rs:646-671)
 and DeviceTape (src/gpu_step/tape.rs:481-484, :349-375): per head,
-O = softmax(scale * Q K^T + causal mask) V, and its backward.  One kernel
+O = softmax(scale * Q K^T + causal mask) V -- or softmax1 (a phantom zero
+logit, DeviceTape::causal_softmax(x, scale, one), tape.rs:225) -- and its
+backward, for sequences up to 256 (the reference's MAX_SEQ).  One kernel
 launch per direction for all heads (st_attn_fwd / st_attn_bwd); there is no
 CPU path.
 """
@@ -11,14 +13,16 @@ import torch
 from .device import handle, ptr
 
 
-def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = True, out=None):
-    """q, k, v: f16 [bh, t, d] (d = 64, t <= 128) -> (o f16 [bh, t, d], lse f32 [bh, t])."""
+def attention_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = True, out=None,
+                  one: bool = False):
+    """q, k, v: f16 [bh, t, d] (d = 64, t <= 256) -> (o f16 [bh, t, d], lse f32 [bh, t]).
+    ``one``: softmax1.  The backward needs no flag: lse carries it."""
     q, k, v = (x.contiguous() for x in (q, k, v))
     bh, t, d = q.shape
     if out is None:
         out = (torch.empty_like(q), torch.empty((bh, t), dtype=torch.float32, device=q.device))
     handle(q.device).call("st_attn_fwd", ptr(q), ptr(k), ptr(v), ptr(out[0]), ptr(out[1]), bh, t, d, float(scale),
-                          int(causal))
+                          int(causal), int(one))
     return out
 
 
@@ -34,7 +38,7 @@ def attention_bwd(q, k, v, o, dout, lse, scale: float, causal: bool = True, out=
 
 
 def attention_fwd_packed(qkv: torch.Tensor, batch: int, heads: int, t: int, scale: float, causal: bool = True,
-                         out=None):
+                         out=None, one: bool = False):
     """Fused attention on the packed f32 layout of the transformer step:
     qkv [batch*t, 3*heads*64] -> (o [batch*t, heads*64] f32, lse [batch*heads, t])."""
     d = 64
@@ -42,7 +46,7 @@ def attention_fwd_packed(qkv: torch.Tensor, batch: int, heads: int, t: int, scal
         out = (torch.empty((batch * t, heads * d), dtype=torch.float32, device=qkv.device),
                torch.empty((batch * heads, t), dtype=torch.float32, device=qkv.device))
     handle(qkv.device).call("st_attn_fwd_packed", ptr(qkv), ptr(out[0]), ptr(out[1]), batch, heads, t, d,
-                            float(scale), int(causal))
+                            float(scale), int(causal), int(one))
     return out
 
 

@@ -28,7 +28,8 @@
 
 namespace {
 
-constexpr int AT = 128;               // rows per head tile (max t)
+constexpr int AT = 128;               // rows per query / key tile
+constexpr int AMAXT = 256;            // longest sequence (the reference's MAX_SEQ)
 constexpr int AD = 64;                // head width
 constexpr int TILE = AT * AD * 2;     // one [128 x 64] f16 operand: 16 KB
 constexpr int PT = AT * AT * 2;       // one [128 x 128] f16 operand: 32 KB
@@ -55,6 +56,7 @@ struct AttnArgs {
     int bh, t, heads;
     float scale;
     int causal;
+    int one;  // softmax1 (forward): a phantom zero logit in every row's denominator
     int *status;
 };
 
@@ -71,32 +73,39 @@ __device__ __forceinline__ bool await(uint64_t *bar, uint32_t parity, int *statu
     }
 }
 
-// Half `half` (32 of the 64 columns) of row r (zeros when !live) into a
-// swizzled 16 KB f16 tile; F32 sources are rounded to f16 on the way.
-template <bool F32>
-__device__ __forceinline__ void stage_half_rows(uint8_t *dst, const void *base, int64_t off, int r, int half,
-                                                bool live) {
-    if (F32) {
-        const float4 *s = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off) + 8 * half;
+// Rows [row0, row0 + nrows) of head z of a tensor (row map m) into a
+// 128-byte-swizzled [nrows x 64] f16 tile, zero rows at and beyond t.  Every
+// thread first loads all of its 16-byte pieces (up to nrows / 32 of them),
+// then stores them, so a thread's loads are in flight together; F32 sources
+// are rounded to f16 on the way.
+template <bool F32, int NROWS>
+__device__ __forceinline__ void stage_rows(uint8_t *dst, const void *base, const RowMap &m, int z, int heads,
+                                           int row0, int t) {
+    constexpr int PER = NROWS * 8 / ATHREADS;  // 16-byte f16 pieces per thread
+    uint4 v[PER];
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (live) {
-                const float4 a = __ldg(s + 2 * c), b = __ldg(s + 2 * c + 1);
+    for (int i = 0; i < PER; i++) {
+        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
+        const int gr = row0 + r;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (gr < t) {
+            const int64_t off = m.at(z, heads, gr) + 8 * c;
+            if (F32) {
+                const float4 *s = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off);
+                const float4 a = __ldg(s), b = __ldg(s + 1);
                 const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
                 const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
-                v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
-                               *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+                v[i] = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                                  *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            } else {
+                v[i] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __half *>(base) + off));
             }
-            *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, 4 * half + c)) = v;
         }
-    } else {
-        const uint4 *s = reinterpret_cast<const uint4 *>(static_cast<const __half *>(base) + off) + 4 * half;
+    }
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const uint4 v = live ? __ldg(s + c) : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, 4 * half + c)) = v;
-        }
+    for (int i = 0; i < PER; i++) {
+        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
+        *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, c)) = v[i];
     }
 }
 
@@ -163,18 +172,18 @@ __device__ __forceinline__ void pack16(const float (&x)[16], uint32_t (&o)[8]) {
     }
 }
 
-// Columns [c0, c0+16) of row r of a [128 x 128] f16 operand tile (two 64-column
-// 128-byte-swizzled halves of 16 KB).
+// Columns [c0, c0+16) of row r of a [128 x 64n] f16 operand tile (n 64-column
+// 128-byte-swizzled blocks of 16 KB).
 __device__ __forceinline__ void put16(uint8_t *tile, int r, int c0, const uint32_t (&o)[8]) {
-    uint8_t *half = tile + (c0 >> 6) * (PT / 2);
+    uint8_t *blk = tile + (c0 >> 6) * (PT / 2);
     const int piece = (c0 & 63) >> 3;
-    *reinterpret_cast<uint4 *>(half + st::sw128_offset(r, piece)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4 *>(half + st::sw128_offset(r, piece + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    *reinterpret_cast<uint4 *>(blk + st::sw128_offset(r, piece)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4 *>(blk + st::sw128_offset(r, piece + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 // K-major operand descriptor: [rows x 64] chunk at `base`, k step kk (16 elements).
 __device__ __forceinline__ uint64_t kmaj(uint32_t base, int kk) { return st::sdesc_sw128(base + kk * 32, 16, 1024); }
-// K-major descriptor into a [128 x 128] tile: k step kk of 8 (64 columns per half).
+// K-major descriptor into a [128 x 64n] tile of 64-column blocks: k step kk (16 columns).
 __device__ __forceinline__ uint64_t kmaj128(uint32_t base, int kk) {
     return st::sdesc_sw128(base + (kk >> 2) * (PT / 2) + (kk & 3) * 32, 16, 1024);
 }
@@ -188,21 +197,38 @@ __device__ __forceinline__ uint64_t mnmaj(uint32_t base, int kk, uint32_t mn_str
 // to f16 right after, so its ~2 ulp f32 error is far below what is kept.
 __device__ __forceinline__ float fast_exp(float x) { return exp2f(x * 1.4426950408889634f); }
 
-// Threads r and r + 128 share row r % 128: thread r < 128 owns columns
-// [0, 64) of the row, thread r + 128 columns [64, 128) (warps w and w + 4 read
-// the same TMEM lanes).  Row reductions combine the two halves through `red`.
-template <bool F32>
+// Shared-memory layout of the forward for TK staged key rows (128 or 256).
+template <int TK>
+struct FwdSmem {
+    static constexpr int Q = 0, K = TILE, V = K + TK * 128, P = V + TK * 128;
+    static constexpr int RED = P + AT * TK * 2;  // [2][128] f32
+    static constexpr int BAR = RED + 2 * AT * 4;
+    static constexpr int SIZE = BAR + 64 + 1024;
+    static constexpr uint32_t TMEM = TK == 128 ? 256 : 512;  // S (TK columns) + O (64)
+};
+
+// Forward.  CTA = (head z = blockIdx.x, query tile blockIdx.y of 128 rows): S = Q K^T over every
+// key the tile sees (at most TK = 256 columns, so a row's scores fit one TMEM
+// row and need no online rescaling), the masked softmax (or softmax1) of
+// scale * S in registers, P as f16 into shared memory, O = P V.  Threads r
+// and r + 128 share row r: each takes half of the row's key columns (warps w
+// and w + 4 read the same TMEM lanes); row reductions go through `red`.
+template <bool F32, int TK>
 __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
+    using L = FwdSmem<TK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem, *sK = smem + TILE, *sV = smem + 2 * TILE, *sP = smem + 3 * TILE;
-    float *red = reinterpret_cast<float *>(sP + PT);  // [2][128]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 2 * AT);
+    uint8_t *sQ = smem + L::Q, *sK = smem + L::K, *sV = smem + L::V, *sP = smem + L::P;
+    float *red = reinterpret_cast<float *>(smem + L::RED);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
     const int tid = threadIdx.x, warp = tid >> 5;
     const int r = tid & (AT - 1), half = tid >> 7;
-    const int64_t rq = g.mq.at(blockIdx.x, g.heads, r), ro = g.mo.at(blockIdx.x, g.heads, r);
-    const bool live = r < g.t;
+    const int z = blockIdx.x, q0 = blockIdx.y * AT, gr = q0 + r;
+    const int kc = g.causal ? min(g.t, q0 + AT) : g.t;  // keys this tile sees
+    const int kc16 = (kc + 15) & ~15;                      // the MMAs' N / K extent over keys
+    const int64_t ro = g.mo.at(z, g.heads, gr < g.t ? gr : 0);
+    const bool live = gr < g.t;
 
     if (tid == 0) {
         st::mbar_init(&bar[0], 1);
@@ -210,21 +236,21 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
         st::fence_mbar_init();
     }
     if (warp == 0) {
-        st::tmem_alloc(tslot, 256);
+        st::tmem_alloc(tslot, L::TMEM);
         st::tmem_relinquish();
     }
-    stage_half_rows<F32>(sQ, g.q, rq, r, half, live);
-    stage_half_rows<F32>(sK, g.k, rq, r, half, live);
-    stage_half_rows<F32>(sV, g.v, rq, r, half, live);
+    stage_rows<F32, AT>(sQ, g.q, g.mq, z, g.heads, q0, g.t);
+    stage_rows<F32, TK>(sK, g.k, g.mq, z, g.heads, 0, kc);
+    stage_rows<F32, TK>(sV, g.v, g.mq, z, g.heads, 0, kc);
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
-    const uint32_t tmem = *tslot, tS = tmem, tO = tmem + 128;
+    const uint32_t tmem = *tslot, tS = tmem, tO = tmem + TK;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
-    if (tid == 0) {  // S = Q K^T
-        constexpr uint32_t id = st::idesc_make(1, 0, false, false, AT, AT);
+    if (tid == 0) {  // S = Q K^T over kc16 keys
+        const uint32_t id = st::idesc_make(1, 0, false, false, AT, kc16);
         const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK);
 #pragma unroll
         for (int kk = 0; kk < AD / 16; kk++) st::umma_f16(tS, kmaj(q, kk), kmaj(k, kk), id, kk > 0 ? 1u : 0u);
@@ -233,34 +259,39 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     bool ok = await(&bar[0], 0, g.status);
     st::tc_fence_after();
 
-    // softmax of row r over this thread's 64 columns: masked max, exchange,
-    // p = exp(s - max) as f16 into sP, partial sums, exchange
-    const int lim = r < g.t ? (g.causal ? r + 1 : g.t) : 0;  // columns < lim are visible
-    const int cbase = half * 64;
-    uint32_t x[64];
-    st::tmem_ld32(tS + lane_base + cbase, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-    st::tmem_ld32(tS + lane_base + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
-    st::tmem_ld_wait();
+    // this thread's columns [c_lo, c_hi): the row's kc16 columns split in two 16-aligned halves
+    const int cw = ((kc16 >> 1) + 15) & ~15;
+    const int c_lo = half ? cw : 0, c_hi = half ? kc16 : cw;
+    const int lim = live ? (g.causal ? gr + 1 : g.t) : 0;  // columns < lim are visible
     float m = -INFINITY;
+#pragma unroll 1
+    for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        uint32_t x[16];
+        st::tmem_ld16(tS + lane_base + c0, x);
+        st::tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 64; j++)
-        if (cbase + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
+        for (int j = 0; j < 16; j++)
+            if (c0 + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
+    }
     red[half * AT + r] = m;
     __syncthreads();
     m = fmaxf(m, red[(half ^ 1) * AT + r]);
+    if (g.one) m = fmaxf(m, 0.0f);  // softmax1 shifts by max(row max, 0)
     float l = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
+#pragma unroll 1
+    for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        uint32_t x[16];
+        st::tmem_ld16(tS + lane_base + c0, x);
+        st::tmem_ld_wait();
         float p[16];
 #pragma unroll
         for (int j = 0; j < 16; j++) {
-            const int col = cbase + 16 * c + j;
-            p[j] = col < lim ? fast_exp(__uint_as_float(x[16 * c + j]) * g.scale - m) : 0.0f;
+            p[j] = c0 + j < lim ? fast_exp(__uint_as_float(x[j]) * g.scale - m) : 0.0f;
             l += p[j];
         }
         uint32_t o[8];
         pack16(p, o);
-        put16(sP, r, cbase + 16 * c, o);
+        put16(sP, r, c0, o);
     }
     __syncthreads();  // every thread has read red (max) before it is reused for sums
     red[half * AT + r] = l;
@@ -269,13 +300,14 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     __syncthreads();
     st::tc_fence_after();
     l += red[(half ^ 1) * AT + r];
-    if (half == 0 && r < g.t) g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] = lim > 0 ? m + logf(l) : -INFINITY;
+    if (g.one && lim > 0) l += fast_exp(-m);  // softmax1's phantom zero logit
+    if (half == 0 && live) g.lse[static_cast<int64_t>(z) * g.t + gr] = lim > 0 ? m + logf(l) : -INFINITY;
 
-    if (tid == 0) {  // O = P V   (V: B operand, N = d contiguous -> MN-major)
+    if (tid == 0) {  // O = P V   (V: B operand, N = d contiguous -> MN-major), K = kc16 keys
         constexpr uint32_t id = st::idesc_make(1, 0, false, true, AT, AD);
         const uint32_t p = st::smem_u32(sP), v = st::smem_u32(sV);
-#pragma unroll
-        for (int kk = 0; kk < AT / 16; kk++) st::umma_f16(tO, kmaj128(p, kk), mnmaj(v, kk, TILE), id, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kc16 / 16; kk++)
+            st::umma_f16(tO, kmaj128(p, kk), mnmaj(v, kk, TILE), id, kk > 0 ? 1u : 0u);
         st::umma_commit(&bar[1]);
     }
     ok = await(&bar[1], 0, g.status) && ok;
@@ -295,54 +327,44 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     __syncthreads();
     if (warp == 0) {
         st::tc_fence_after();
-        st::tmem_dealloc(tmem, 256);
+        st::tmem_dealloc(tmem, L::TMEM);
     }
 }
 
+// Backward shared memory: two [128 x 64] operand pairs and two [128 x 128] f16 tiles.
+constexpr int B_Q = 0, B_DO = TILE, B_K = 2 * TILE, B_V = 3 * TILE, B_P = 4 * TILE, B_S = B_P + PT;
+constexpr int B_RED = B_S + PT, B_BAR = B_RED + 2 * AT * 4;
+constexpr int BWD_SMEM = B_BAR + 64 + 1024;
+
+// For query tile qt: D_r = sum_d dO[r,d] O[r,d] (both halves, the same order
+// on both threads of the row) and the row's log-sum-exp; Q and dO staged.
 template <bool F32>
-__global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem, *sK = smem + TILE, *sV = smem + 2 * TILE, *sO = smem + 3 * TILE;  // sO holds dO
-    uint8_t *sP = smem + 4 * TILE, *sS = sP + PT;                                          // P, dS
-    float *red = reinterpret_cast<float *>(sS + PT);                                       // [2][128]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 2 * AT);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int r = tid & (AT - 1), half = tid >> 7;
-    const int64_t rq = g.mq.at(blockIdx.x, g.heads, r), ro = g.mo.at(blockIdx.x, g.heads, r);
-    const bool live = r < g.t;
-
-    if (tid == 0) {
-        st::mbar_init(&bar[0], 1);
-        st::mbar_init(&bar[1], 1);
-        st::fence_mbar_init();
-    }
-    if (warp == 0) {
-        st::tmem_alloc(tslot, 512);
-        st::tmem_relinquish();
-    }
-    stage_half_rows<F32>(sQ, g.q, rq, r, half, live);
-    stage_half_rows<F32>(sK, g.k, rq, r, half, live);
-    stage_half_rows<F32>(sV, g.v, rq, r, half, live);
-    stage_half_rows<F32>(sO, g.dout, ro, r, half, live);
-    // D_r = sum_d dO[r,d] * O[r,d], this thread's 32 of the 64 d, then exchanged
-    const float dsum_half = live ? dot_half<F32>(g.o, g.dout, ro, half) : 0.0f;
-    float dsum = dsum_half;
-    red[half * AT + r] = dsum;
-    const float lse = r < g.t ? g.lse[static_cast<int64_t>(blockIdx.x) * g.t + r] : 0.0f;
-    st::fence_proxy_async_smem();
-    st::tc_fence_before();
+__device__ __forceinline__ void bwd_stage_queries(const AttnArgs &g, uint8_t *smem, float *red, int z, int qt,
+                                                  float &dsum, float &lse) {
+    const int r = threadIdx.x & (AT - 1), half = threadIdx.x >> 7, gr = qt * AT + r;
+    stage_rows<F32, AT>(smem + B_Q, g.q, g.mq, z, g.heads, qt * AT, g.t);
+    stage_rows<F32, AT>(smem + B_DO, g.dout, g.mo, z, g.heads, qt * AT, g.t);
+    const float part = gr < g.t ? dot_half<F32>(g.o, g.dout, g.mo.at(z, g.heads, gr), half) : 0.0f;
+    red[half * AT + r] = part;
+    lse = gr < g.t ? g.lse[static_cast<int64_t>(z) * g.t + gr] : 0.0f;
     __syncthreads();
-    st::tc_fence_after();
-    dsum = red[0 * AT + r] + red[1 * AT + r];  // same order in both halves
-    const uint32_t tmem = *tslot;
-    const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    dsum = red[r] + red[AT + r];
+    __syncthreads();
+}
 
-    if (tid == 0) {  // S = Q K^T, dP = dO V^T
+// S = Q K^T and dP = dO V^T of one (query tile, key tile) pair, then P =
+// exp(scale S - lse) and dS = scale P (dP - D) (masked entries 0) as f16
+// tiles in shared memory (P only when want_p).  Rows are queries.
+template <bool F32>
+__device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uint32_t tmem, uint64_t *bar,
+                                           uint32_t &phase, int qt, int kt, float dsum, float lse, bool want_p) {
+    const int tid = threadIdx.x, warp = tid >> 5, r = tid & (AT - 1), half = tid >> 7;
+    const uint32_t tS = tmem, tdP = tmem + 128;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    if (tid == 0) {
         constexpr uint32_t id = st::idesc_make(1, 0, false, false, AT, AT);
-        const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK), v = st::smem_u32(sV), d = st::smem_u32(sO);
+        const uint32_t q = st::smem_u32(smem + B_Q), k = st::smem_u32(smem + B_K), v = st::smem_u32(smem + B_V),
+                       d = st::smem_u32(smem + B_DO);
 #pragma unroll
         for (int kk = 0; kk < AD / 16; kk++) {
             st::umma_f16(tS, kmaj(q, kk), kmaj(k, kk), id, kk > 0 ? 1u : 0u);
@@ -350,11 +372,12 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
         }
         st::umma_commit(&bar[0]);
     }
-    bool ok = await(&bar[0], 0, g.status);
+    const bool ok = await(&bar[0], phase, g.status);
+    phase ^= 1u;
     st::tc_fence_after();
-
-    // P = exp(scale*S - lse) (masked: 0) and dS = scale * P * (dP - D), both f16
-    const int lim = r < g.t ? (g.causal ? r + 1 : g.t) : 0;
+    const int gr = qt * AT + r;
+    // key column c of this tile is key kt*128 + c; visible iff < t and (causal) <= gr
+    const int lim = gr < g.t ? min(g.t, g.causal ? gr + 1 : g.t) - kt * AT : 0;
 #pragma unroll 1
     for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
         uint32_t xs[16], xd[16];
@@ -369,48 +392,143 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
             ds[j] = p[j] * (__uint_as_float(xd[j]) - dsum) * g.scale;
         }
         uint32_t o[8];
-        pack16(p, o);
-        put16(sP, r, c0, o);
+        if (want_p) {
+            pack16(p, o);
+            put16(smem + B_P, r, c0, o);
+        }
         pack16(ds, o);
-        put16(sS, r, c0, o);
+        put16(smem + B_S, r, c0, o);
     }
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
+    return ok;
+}
+
+// Backward.  Two kinds of CTA per head (blockIdx.x = head; blockIdx.y <
+// ntile: key tile kt = blockIdx.y, else query tile qt = blockIdx.y - ntile):
+//  * key tile kt: dV = sum over query tiles of P^T dO, dK = sum of dS^T Q
+//    (accumulated in TMEM across the query tiles that see the keys);
+//  * query tile qt: dQ = sum over the key tiles it sees of dS K.
+// Both recompute S and dP from Q, K, V, dO and the forward's log-sum-exp
+// (D = rowsum(dO O) gives the softmax backward for softmax and softmax1
+// alike).  Every transposed operand is a shared-memory descriptor.
+template <bool F32>
+__global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *red = reinterpret_cast<float *>(smem + B_RED);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + B_BAR);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, r = tid & (AT - 1), half = tid >> 7;
+    const int z = blockIdx.x, ntile = (g.t + AT - 1) / AT;
+    const bool key_role = static_cast<int>(blockIdx.y) < ntile;
+    const int tile = key_role ? blockIdx.y : blockIdx.y - ntile;
 
     if (tid == 0) {
-        // dV = P^T dO and dK = dS^T Q: A = P^T / dS^T (stored [i][j]: MN-major, M = j),
-        // B = dO / Q (stored [i][d]: MN-major, N = d), K = i
-        constexpr uint32_t id_tt = st::idesc_make(1, 0, true, true, AT, AD);
-        // dQ = dS K: A = dS (K-major, K = j), B = K (stored [j][d]: MN-major, N = d)
-        constexpr uint32_t id_nt = st::idesc_make(1, 0, false, true, AT, AD);
-        const uint32_t p = st::smem_u32(sP), s = st::smem_u32(sS), q = st::smem_u32(sQ), k = st::smem_u32(sK),
-                       d = st::smem_u32(sO);
-#pragma unroll
-        for (int kk = 0; kk < AT / 16; kk++) {
-            st::umma_f16(tdV, mnmaj(p, kk, PT / 2), mnmaj(d, kk, TILE), id_tt, kk > 0 ? 1u : 0u);
-            st::umma_f16(tdK, mnmaj(s, kk, PT / 2), mnmaj(q, kk, TILE), id_tt, kk > 0 ? 1u : 0u);
-            st::umma_f16(tdQ, kmaj128(s, kk), mnmaj(k, kk, TILE), id_nt, kk > 0 ? 1u : 0u);
-        }
-        st::umma_commit(&bar[1]);
+        st::mbar_init(&bar[0], 1);
+        st::mbar_init(&bar[1], 1);
+        st::fence_mbar_init();
     }
-    ok = await(&bar[1], 0, g.status) && ok;
+    if (warp == 0) {
+        st::tmem_alloc(tslot, 512);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
     st::tc_fence_after();
-    // row r of dV, dK (rows = keys) and dQ (rows = queries), this thread's 32 columns
+    const uint32_t tmem = *tslot, tA = tmem + 256, tB = tmem + 320;  // dV / dQ, dK
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint32_t ph0 = 0, ph1 = 0;
+    bool ok = true;
+    if (key_role) {
+        const int kt = tile;
+        stage_rows<F32, AT>(smem + B_K, g.k, g.mq, z, g.heads, kt * AT, g.t);
+        stage_rows<F32, AT>(smem + B_V, g.v, g.mq, z, g.heads, kt * AT, g.t);
+        bool first = true;
+        for (int qt = g.causal ? kt : 0; qt < ntile && ok; qt++) {
+            float dsum, lse;
+            bwd_stage_queries<F32>(g, smem, red, z, qt, dsum, lse);
+            st::fence_proxy_async_smem();
+            st::tc_fence_before();
+            __syncthreads();
+            st::tc_fence_after();
+            ok = bwd_scores<F32>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, true) && ok;
+            if (tid == 0) {
+                // dV += P^T dO, dK += dS^T Q: A = P^T / dS^T (stored [query][key]: MN-major, M = key),
+                // B = dO / Q (stored [query][d]: MN-major, N = d), K = the tile's 128 queries
+                constexpr uint32_t id_tt = st::idesc_make(1, 0, true, true, AT, AD);
+                const uint32_t p = st::smem_u32(smem + B_P), s = st::smem_u32(smem + B_S),
+                               q = st::smem_u32(smem + B_Q), d = st::smem_u32(smem + B_DO);
 #pragma unroll
-    for (int w = 0; w < 3; w++) {
-        void *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
-        const uint32_t src = w == 0 ? tdV : w == 1 ? tdK : tdQ;
+                for (int kk = 0; kk < AT / 16; kk++) {
+                    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+                    st::umma_f16(tA, mnmaj(p, kk, PT / 2), mnmaj(d, kk, TILE), id_tt, acc);
+                    st::umma_f16(tB, mnmaj(s, kk, PT / 2), mnmaj(q, kk, TILE), id_tt, acc);
+                }
+                st::umma_commit(&bar[1]);
+            }
+            // the next query tile restages Q, dO, P and dS: these MMAs must be done
+            ok = await(&bar[1], ph1, g.status) && ok;
+            ph1 ^= 1u;
+            st::tc_fence_after();
+            first = false;
+        }
+        const int gk = kt * AT + r;
+        const int64_t rk = g.mq.at(z, g.heads, gk < g.t ? gk : 0);
+#pragma unroll
+        for (int w = 0; w < 2; w++) {
+            void *dst_t = w == 0 ? g.dv : g.dk;
+            const uint32_t src = w == 0 ? tA : tB;
+#pragma unroll
+            for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+                uint32_t x[16];
+                st::tmem_ld16(src + lane_base + c0, x);
+                st::tmem_ld_wait();
+                float y[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) y[j] = __uint_as_float(x[j]);
+                if (gk < g.t && ok) store16<F32>(dst_t, rk + c0, y);
+            }
+        }
+    } else {
+        const int qt = tile;
+        float dsum, lse;
+        bwd_stage_queries<F32>(g, smem, red, z, qt, dsum, lse);
+        const int last = g.causal ? qt : ntile - 1;
+        for (int kt = 0; kt <= last && ok; kt++) {
+            stage_rows<F32, AT>(smem + B_K, g.k, g.mq, z, g.heads, kt * AT, g.t);
+            stage_rows<F32, AT>(smem + B_V, g.v, g.mq, z, g.heads, kt * AT, g.t);
+            st::fence_proxy_async_smem();
+            st::tc_fence_before();
+            __syncthreads();
+            st::tc_fence_after();
+            ok = bwd_scores<F32>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, false) && ok;
+            if (tid == 0) {
+                // dQ += dS K: A = dS (K-major, K = key), B = K (stored [key][d]: MN-major, N = d)
+                constexpr uint32_t id_nt = st::idesc_make(1, 0, false, true, AT, AD);
+                const uint32_t s = st::smem_u32(smem + B_S), k = st::smem_u32(smem + B_K);
+#pragma unroll
+                for (int kk = 0; kk < AT / 16; kk++)
+                    st::umma_f16(tA, kmaj128(s, kk), mnmaj(k, kk, TILE), id_nt, (kt == 0 && kk == 0) ? 0u : 1u);
+                st::umma_commit(&bar[1]);
+            }
+            ok = await(&bar[1], ph1, g.status) && ok;  // K and dS are restaged by the next key tile
+            ph1 ^= 1u;
+            st::tc_fence_after();
+        }
+        const int gq = qt * AT + r;
+        const int64_t rq = g.mq.at(z, g.heads, gq < g.t ? gq : 0);
 #pragma unroll
         for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
             uint32_t x[16];
-            st::tmem_ld16(src + lane_base + c0, x);
+            st::tmem_ld16(tA + lane_base + c0, x);
             st::tmem_ld_wait();
             float y[16];
 #pragma unroll
             for (int j = 0; j < 16; j++) y[j] = __uint_as_float(x[j]);
-            if (live && ok) store16<F32>(dst_t, rq + c0, y);
+            if (gq < g.t && ok) store16<F32>(g.dq, rq + c0, y);
         }
     }
     st::tc_fence_before();
@@ -421,30 +539,34 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     }
 }
 
-constexpr int FWD_SMEM = 3 * TILE + PT + 2 * AT * 4 + 64 + 1024;
-constexpr int BWD_SMEM = 4 * TILE + 2 * PT + 2 * AT * 4 + 64 + 1024;
-
 st_status check(st_handle *h, const void *q, const void *k, const void *v, int64_t bh, int64_t t, int64_t d,
                 const char *who) {
     if (!q || !k || !v) return h->fail(ST_INVALID_ARG, "%s: null buffer", who);
     if (bh < 1 || bh > (1 << 30) || t < 1) return h->fail(ST_INVALID_ARG, "%s: bad bh / t", who);
-    if (t > AT || d != AD)
-        return h->fail(ST_UNSUPPORTED_SHAPE, "%s: the fused kernel takes t <= %d and d = %d (got t=%lld d=%lld)", who, AT,
-                       AD, (long long)t, (long long)d);
+    if (t > AMAXT || d != AD)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "%s: the fused kernel takes t <= %d and d = %d (got t=%lld d=%lld)", who,
+                       AMAXT, AD, (long long)t, (long long)d);
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)
         return h->fail(ST_INVALID_ARG, "%s: q, k, v must be 16-byte aligned", who);
     return ST_OK;
 }
 
-template <bool F32>
-st_status launch_fwd(st_handle *h, const AttnArgs &g) {
+template <bool F32, int TK>
+st_status launch_fwd_tk(st_handle *h, const AttnArgs &g) {
     static bool attr = false;
     if (!attr) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<F32, TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              FwdSmem<TK>::SIZE));
         attr = true;
     }
-    k_attn_fwd<F32><<<static_cast<unsigned>(g.bh), ATHREADS, FWD_SMEM, h->stream>>>(g);
+    const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>((g.t + AT - 1) / AT));
+    k_attn_fwd<F32, TK><<<grid, ATHREADS, FwdSmem<TK>::SIZE, h->stream>>>(g);
     return st_after_launch(h, "k_attn_fwd");
+}
+
+template <bool F32>
+st_status launch_fwd(st_handle *h, const AttnArgs &g) {
+    return g.t <= AT ? launch_fwd_tk<F32, AT>(h, g) : launch_fwd_tk<F32, AMAXT>(h, g);
 }
 
 template <bool F32>
@@ -454,7 +576,8 @@ st_status launch_bwd(st_handle *h, const AttnArgs &g) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
         attr = true;
     }
-    k_attn_bwd<F32><<<static_cast<unsigned>(g.bh), ATHREADS, BWD_SMEM, h->stream>>>(g);
+    const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(2 * ((g.t + AT - 1) / AT)));
+    k_attn_bwd<F32><<<grid, ATHREADS, BWD_SMEM, h->stream>>>(g);
     return st_after_launch(h, "k_attn_bwd");
 }
 
@@ -463,7 +586,7 @@ bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
 extern "C" st_status st_attn_fwd(st_handle *h, const void *q, const void *k, const void *v, void *o, float *lse,
-                                 int64_t bh, int64_t t, int64_t d, float scale, int32_t causal) {
+                                 int64_t bh, int64_t t, int64_t d, float scale, int32_t causal, int32_t one) {
     if (!h) return ST_INVALID_ARG;
     st_status s = check(h, q, k, v, bh, t, d, "st_attn_fwd");
     if (s != ST_OK) return s;
@@ -482,6 +605,7 @@ extern "C" st_status st_attn_fwd(st_handle *h, const void *q, const void *k, con
     g.heads = 1;
     g.scale = scale;
     g.causal = causal;
+    g.one = one;
     g.status = h->d_status;
     return launch_fwd<false>(h, g);
 }
@@ -517,7 +641,8 @@ extern "C" st_status st_attn_bwd(st_handle *h, const void *q, const void *k, con
 }
 
 extern "C" st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o, float *lse, int64_t batch,
-                                        int64_t heads, int64_t t, int64_t d, float scale, int32_t causal) {
+                                        int64_t heads, int64_t t, int64_t d, float scale, int32_t causal,
+                                        int32_t one) {
     if (!h) return ST_INVALID_ARG;
     if (batch < 1 || heads < 1 || batch * heads > (1 << 30)) return h->fail(ST_INVALID_ARG, "st_attn_fwd_packed: bad shape");
     st_status s = check(h, qkv, qkv, qkv, batch * heads, t, d, "st_attn_fwd_packed");
@@ -538,6 +663,7 @@ extern "C" st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o
     g.heads = static_cast<int>(heads);
     g.scale = scale;
     g.causal = causal;
+    g.one = one;
     g.status = h->d_status;
     return launch_fwd<true>(h, g);
 }

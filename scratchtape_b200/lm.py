@@ -40,6 +40,7 @@ class LmConfig:
     beta2: float = 0.999
     adam_eps: float = 1e-8
     sync_every: int = 8
+    softmax1: bool = False  # the device tape's Config.softmax1 (src/gpu_step/tape.rs:400)
 
     def flops_per_step(self):
         """GEMM flops of one forward + backward (attention over causal pairs)."""
@@ -174,7 +175,8 @@ class TinyLM:
             self._ln(self.x[i], p + "ln1_g", p + "ln1_b", self.a[i], self.ln_stats[i][0])
             self._gemm(self.a[i], self.p[p + "wqkv"], self.qkv[i], rows, c.d, 3 * c.d,
                        epi=Epilogue(bias=(self.p[p + "bqkv"], 0)))
-            attention_fwd_packed(self.qkv[i], c.batch, c.heads, c.t, scale, True, out=(self.o[i], self.lse[i]))
+            attention_fwd_packed(self.qkv[i], c.batch, c.heads, c.t, scale, True, out=(self.o[i], self.lse[i]),
+                                 one=c.softmax1)
             self._gemm(self.o[i], self.p[p + "wo"], self.xm[i], rows, c.d, c.d,
                        epi=Epilogue(bias=(self.p[p + "bo"], 0), residual=(self.x[i], 0)))
             self._ln(self.xm[i], p + "ln2_g", p + "ln2_b", self.bn[i], self.ln_stats[i][1])

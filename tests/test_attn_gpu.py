@@ -8,7 +8,11 @@ the oracle runs in f32 on the same f16 values.  Bar: the north star's
 tensor-core tolerance, 5e-3 of the output's scale, for O, dQ, dK and dV; the
 log-sum-exp the kernel saves is checked against an f64 evaluation.
 Shapes follow the reference's head-view cases (src/gpu_step/matmul.rs:1113-1195)
-plus config 3 itself (32 x 4 heads, t 128, d 64) and ragged t.
+plus config 3 itself (32 x 4 heads, t 128, d 64), ragged t, sequences past one
+128-row tile up to the reference's MAX_SEQ 256
+(examples/tiny_lm/fused_models_check.rs:59-60), and softmax1 on and off (the
+device tape's Config.softmax1, src/gpu_step/tape.rs:400, tested with
+softmax1: true at :710).
 """
 import numpy as np
 import pytest
@@ -39,27 +43,66 @@ def _close(got, want, what):
     assert err <= TOL * scale, "%s: max err %.3g vs scale %.3g" % (what, err, scale)
 
 
-@pytest.mark.parametrize("bh,t,causal", [(128, 128, True), (3, 77, True), (2, 1, True), (5, 100, False),
-                                         (4, 128, False), (6, 33, True)])
-def test_forward_and_backward_match_oracle(dev, bh, t, causal):
-    from scratchtape_b200.attention import attention_bwd, attention_fwd
-    d, scale = 64, 1.0 / 8.0
-    q, k, v, dout = _inputs(bh, t, d, seed=bh * 1000 + t)
-    o, lse = attention_fwd(q, k, v, scale, causal)
-    want_o = oracle.attention_fwd(_f32(q), _f32(k), _f32(v), scale, causal=causal)
-    _close(o, want_o, "O")
-    # lse in f64
+def _want_lse(q, k, scale, causal, one):
+    """The log-sum-exp of each scaled, masked row in f64 (softmax1: with the
+    phantom zero logit)."""
+    t = q.shape[1]
     s = np.einsum("bid,bjd->bij", _f32(q).astype(np.float64), _f32(k).astype(np.float64)) * scale
     if causal:
         s = np.where(np.tril(np.ones((t, t), bool))[None], s, -np.inf)
+    if one:
+        s = np.concatenate([s, np.zeros(s.shape[:2] + (1,))], -1)
     m = s.max(-1, keepdims=True)
-    want_lse = (m + np.log(np.exp(s - m).sum(-1, keepdims=True)))[..., 0]
-    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-3
+    return (m + np.log(np.exp(s - m).sum(-1, keepdims=True)))[..., 0]
+
+
+@pytest.mark.parametrize("one", [False, True])
+@pytest.mark.parametrize("bh,t,causal", [(128, 128, True), (3, 77, True), (2, 1, True), (5, 100, False),
+                                         (4, 128, False), (6, 33, True), (4, 256, True), (3, 200, True),
+                                         (2, 129, True), (3, 256, False), (2, 181, False)])
+def test_forward_and_backward_match_oracle(dev, bh, t, causal, one):
+    from scratchtape_b200.attention import attention_bwd, attention_fwd
+    d, scale = 64, 1.0 / 8.0
+    q, k, v, dout = _inputs(bh, t, d, seed=bh * 1000 + t)
+    if one:
+        q = q * 4  # larger logits, so the phantom zero logit is not the largest everywhere
+    o, lse = attention_fwd(q, k, v, scale, causal, one=one)
+    want_o = oracle.attention_fwd(_f32(q), _f32(k), _f32(v), scale, causal=causal, one=one)
+    _close(o, want_o, "O")
+    assert np.abs(lse.cpu().numpy() - _want_lse(q, k, scale, causal, one)).max() <= 1e-3
     dq, dk, dv = attention_bwd(q, k, v, o, dout, lse, scale, causal)
-    wq, wk, wv = oracle.attention_bwd(_f32(q), _f32(k), _f32(v), _f32(dout), scale, causal=causal)
+    wq, wk, wv = oracle.attention_bwd(_f32(q), _f32(k), _f32(v), _f32(dout), scale, causal=causal, one=one)
     _close(dq, wq, "dQ")
     _close(dk, wk, "dK")
     _close(dv, wv, "dV")
+
+
+@pytest.mark.parametrize("one", [False, True])
+def test_packed_layout_matches_per_head_layout(dev, one):
+    """st_attn_fwd/bwd_packed read Q, K, V as head views of the fused QKV
+    projection [B*T, 3*H*64] (f32, rounded to f16 as staged) and write O
+    merged [B*T, H*64]: the same numbers as the per-head f16 entry points on
+    the same f16-rounded values, at t = 256 across two tiles."""
+    from scratchtape_b200.attention import (attention_bwd, attention_bwd_packed, attention_fwd,
+                                            attention_fwd_packed)
+    b, h, t, d = 2, 3, 256, 64
+    g = torch.Generator(device="cuda").manual_seed(77)
+    qkv = (torch.randn((b * t, 3 * h * d), generator=g, device="cuda") / 4).half().float()
+    dout = torch.randn((b * t, h * d), generator=g, device="cuda").half().float()
+    o, lse = attention_fwd_packed(qkv, b, h, t, 0.125, True, one=one)
+    dqkv = attention_bwd_packed(qkv, o, dout, lse, b, h, t, 0.125, True)
+
+    def heads(x, j):  # [b*t, (3)*h*d] column block j -> [b*h, t, d]
+        return x[:, j * h * d:(j + 1) * h * d].reshape(b, t, h, d).transpose(1, 2).reshape(b * h, t, d)
+
+    q, k, v = (heads(qkv, j).half().contiguous() for j in range(3))
+    o2, lse2 = attention_fwd(q, k, v, 0.125, True, one=one)
+    assert torch.allclose(heads(o, 0), o2.float(), atol=2e-3, rtol=2e-3)
+    assert torch.allclose(lse, lse2, atol=1e-5)
+    g2 = attention_bwd(q, k, v, o2, heads(dout, 0).half().contiguous(), lse2, 0.125, True)
+    for j in range(3):
+        got, want = heads(dqkv, j), g2[j].float()
+        assert (got - want).abs().max().item() <= 5e-3 * want.abs().max().item()
 
 
 def test_deterministic(dev):
@@ -80,7 +123,7 @@ def test_unsupported_shapes_return_status(dev):
     with pytest.raises(N.StError) as e:
         attention_fwd(q, q, q, 0.1)
     assert e.value.status == N.ST_UNSUPPORTED_SHAPE
-    q = torch.zeros((1, 129, 64), dtype=torch.half, device="cuda")
+    q = torch.zeros((1, 257, 64), dtype=torch.half, device="cuda")
     with pytest.raises(N.StError) as e:
         attention_fwd(q, q, q, 0.1)
     assert e.value.status == N.ST_UNSUPPORTED_SHAPE
