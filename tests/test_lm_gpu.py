@@ -3,8 +3,12 @@
 The loss and every parameter gradient of scratchtape_b200.lm.TinyLM are
 compared with a plain PyTorch fp32 reference of the same model (TF32 off),
 fed the same parameters and bytes: this is a floating-point path, so the
-check is against an fp32 statement of the same arithmetic, with the
-tensor-core tolerance widened for the f16 attention operands.  The ReLU
+check is against an fp32 statement of the same arithmetic.  Bars per
+gradient tensor: the north star's 5e-3 relative (as the relative Frobenius
+norm of the error), and every element within 2e-2 of the tensor's largest
+(TF32 products and f16 attention operands).  Cases go up to BASELINE
+configs[3]'s model at full width and depth (batch reduced), t = 256, and
+softmax1.  The ReLU
 masks are taken from the device's own hidden activations: TF32 and fp32
 pre-activations disagree in sign on ~0.1 % of units near zero, which moves
 every upstream gradient by ~3 % without any arithmetic being wrong -- the
@@ -41,7 +45,12 @@ def _reference_loss(model, ids, targets):
         q, k, v = (qkv[:, j * c.d:(j + 1) * c.d].reshape(c.batch, c.t, c.heads, dh).transpose(1, 2) for j in range(3))
         s = (q @ k.transpose(-1, -2)) / dh ** 0.5
         s = s.masked_fill(~mask, float("-inf"))
-        o = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(rows, c.d)
+        if c.softmax1:  # a phantom zero logit in the denominator (Tape::softmax1, src/tape.rs:418-431)
+            s = torch.cat([s, torch.zeros(s.shape[:-1] + (1,), device=s.device)], -1)
+            w = torch.softmax(s, -1)[..., :-1]
+        else:
+            w = torch.softmax(s, -1)
+        o = (w @ v).transpose(1, 2).reshape(rows, c.d)
         x = x + o @ P[p + "wo"] + P[p + "bo"]
         b = ln(x, P[p + "ln2_g"], P[p + "ln2_b"])
         keep = (model.hid[i] > 0).float()  # the device's ReLU mask (see the module docstring)
@@ -54,7 +63,11 @@ def _reference_loss(model, ids, targets):
 
 
 @pytest.mark.parametrize("cfg", [dict(d=128, heads=2, layers=2, dff=256, t=64, batch=4),
-                                 dict(d=256, heads=4, layers=1, dff=1024, t=128, batch=2)])
+                                 dict(d=256, heads=4, layers=1, dff=1024, t=128, batch=2),
+                                 # BASELINE configs[3]'s model at full width and depth, batch reduced to 2
+                                 dict(d=256, heads=4, layers=4, dff=1024, t=128, batch=2),
+                                 dict(d=256, heads=4, layers=2, dff=1024, t=256, batch=1),
+                                 dict(d=128, heads=2, layers=2, dff=256, t=64, batch=4, softmax1=True)])
 def test_loss_and_gradients_match_fp32_reference(dev, cfg):
     from scratchtape_b200.lm import LmConfig, TinyLM
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -69,6 +82,13 @@ def test_loss_and_gradients_match_fp32_reference(dev, cfg):
     assert abs(loss.item() - want_loss.item()) <= 2e-3 * abs(want_loss.item())
     for name, wg in want_g.items():
         got = model.g[name]
+        # the north star's 5e-3 relative bar, per gradient tensor, as a relative
+        # Frobenius norm of the error; and no single element off by more than
+        # 2e-2 of the tensor's largest (TF32 products and f16 attention operands
+        # against an fp32 reference: a few elements of the deepest gradients
+        # carry the most accumulated rounding)
+        rel = ((got - wg).norm() / wg.norm().clamp_min(1e-30)).item()
+        assert rel <= 5e-3, "%s: relative error %.3g" % (name, rel)
         scale = wg.abs().max().item()
         err = (got - wg).abs().max().item()
         assert err <= 2e-2 * scale + 1e-7, "%s: err %.3g vs scale %.3g" % (name, err, scale)
