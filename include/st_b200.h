@@ -54,8 +54,13 @@ typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2 } st_dtype;
  *            kind::f16, f32 accumulate and an f32 out -- the reference's f16 x
  *            f16 -> f32 matrix-core path (k_matmul_cmma, src/gpu_step/matmul.rs:632-880).
  *            No col_sum; operands must be TMA-describable (16-byte aligned
- *            starts and row strides). */
-typedef enum { ST_PREC_F32_EXACT = 0, ST_PREC_TF32 = 1, ST_PREC_F16 = 2 } st_precision;
+ *            starts and row strides).
+ * TF32X3:    f32 operands, each split into a TF32 high part and a TF32 rest;
+ *            three TF32 tensor-core products (hi.hi + hi.lo + lo.hi) over
+ *            operands concatenated along k (scratch: 3x each operand), error
+ *            about 2^-21 of |a| |b| per product -- f32 accuracy at tensor-core
+ *            speed, for what matmul_f32 (src/gpu_step/matmul.rs:93) keeps in f32. */
+typedef enum { ST_PREC_F32_EXACT = 0, ST_PREC_TF32 = 1, ST_PREC_F16 = 2, ST_PREC_TF32X3 = 3 } st_precision;
 
 typedef struct st_handle st_handle;
 

@@ -32,6 +32,7 @@ pub const ST_BF16: i32 = 2;
 pub const ST_PREC_F32_EXACT: c_int = 0;
 pub const ST_PREC_TF32: c_int = 1;
 pub const ST_PREC_F16: c_int = 2;
+pub const ST_PREC_TF32X3: c_int = 3;
 pub const ST_KNN_DOT: i32 = 0;
 pub const ST_KNN_L2: i32 = 1;
 pub const ST_KNN_EXACT: i32 = 0;

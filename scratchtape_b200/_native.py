@@ -21,7 +21,7 @@ ST_OK, ST_INVALID_ARG, ST_UNSUPPORTED_SHAPE, ST_CUDA_ERROR, ST_NCCL_ERROR, ST_TI
 STATUS_NAMES = ["OK", "INVALID_ARG", "UNSUPPORTED_SHAPE", "CUDA_ERROR", "NCCL_ERROR", "TIMEOUT", "NO_MEMORY",
                 "NOT_FOUND"]
 ST_F32, ST_F16, ST_BF16 = 0, 1, 2
-PREC_F32_EXACT, PREC_TF32, PREC_F16 = 0, 1, 2
+PREC_F32_EXACT, PREC_TF32, PREC_F16, PREC_TF32X3 = 0, 1, 2, 3
 KNN_DOT, KNN_L2 = 0, 1
 KNN_EXACT, KNN_F16REF = 0, 1
 KNN_KMAX = 128

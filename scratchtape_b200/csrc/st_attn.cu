@@ -109,6 +109,50 @@ __device__ __forceinline__ void stage_rows(uint8_t *dst, const void *base, const
     }
 }
 
+// The forward's Q (128 rows from q0), K and V (TK rows from 0, zero from kc
+// on) with every thread's loads of all three issued before any store.
+template <bool F32, int TK>
+__device__ __forceinline__ void stage_qkv(uint8_t *sq, uint8_t *sk, uint8_t *sv, const AttnArgs &g, int z, int q0,
+                                          int kc) {
+    constexpr int PQ = AT * 8 / ATHREADS, PK = TK * 8 / ATHREADS;
+    uint4 v[PQ + 2 * PK];
+    auto load = [&](const void *base, int row, int c) {
+        if (F32) {
+            const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(base) +
+                                                                 g.mq.at(z, g.heads, row) + 8 * c);
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            return make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                              *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+        }
+        return __ldg(reinterpret_cast<const uint4 *>(static_cast<const __half *>(base) + g.mq.at(z, g.heads, row)) +
+                     c);
+    };
+#pragma unroll
+    for (int i = 0; i < PQ; i++) {
+        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
+        v[i] = q0 + r < g.t ? load(g.q, q0 + r, c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < PK; i++) {
+        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
+        v[PQ + i] = r < kc ? load(g.k, r, c) : make_uint4(0u, 0u, 0u, 0u);
+        v[PQ + PK + i] = r < kc ? load(g.v, r, c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < PQ; i++) {
+        const int p = threadIdx.x + i * ATHREADS;
+        *reinterpret_cast<uint4 *>(sq + st::sw128_offset(p >> 3, p & 7)) = v[i];
+    }
+#pragma unroll
+    for (int i = 0; i < PK; i++) {
+        const int p = threadIdx.x + i * ATHREADS;
+        *reinterpret_cast<uint4 *>(sk + st::sw128_offset(p >> 3, p & 7)) = v[PQ + i];
+        *reinterpret_cast<uint4 *>(sv + st::sw128_offset(p >> 3, p & 7)) = v[PQ + PK + i];
+    }
+}
+
 // 16 consecutive output values at element `off` of `base` (f16 or f32).
 template <bool F32>
 __device__ __forceinline__ void store16(void *base, int64_t off, const float (&y)[16]) {
@@ -239,9 +283,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
         st::tmem_alloc(tslot, L::TMEM);
         st::tmem_relinquish();
     }
-    stage_rows<F32, AT>(sQ, g.q, g.mq, z, g.heads, q0, g.t);
-    stage_rows<F32, TK>(sK, g.k, g.mq, z, g.heads, 0, kc);
-    stage_rows<F32, TK>(sV, g.v, g.mq, z, g.heads, 0, kc);
+    stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
@@ -259,39 +301,69 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
     bool ok = await(&bar[0], 0, g.status);
     st::tc_fence_after();
 
-    // this thread's columns [c_lo, c_hi): the row's kc16 columns split in two 16-aligned halves
-    const int cw = ((kc16 >> 1) + 15) & ~15;
-    const int c_lo = half ? cw : 0, c_hi = half ? kc16 : cw;
     const int lim = live ? (g.causal ? gr + 1 : g.t) : 0;  // columns < lim are visible
-    float m = -INFINITY;
-#pragma unroll 1
-    for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        uint32_t x[16];
-        st::tmem_ld16(tS + lane_base + c0, x);
+    float m = -INFINITY, l = 0.0f;
+    if (TK == AT) {
+        // up to 128 key columns: thread half h takes columns 64h .. 64h + 63 in
+        // registers (one TMEM read); columns at and past kc16 are masked
+        const int cbase = half * 64;
+        uint32_t x[64];
+        st::tmem_ld32(tS + lane_base + cbase, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+        st::tmem_ld32(tS + lane_base + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
         st::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; j++)
-            if (c0 + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
-    }
-    red[half * AT + r] = m;
-    __syncthreads();
-    m = fmaxf(m, red[(half ^ 1) * AT + r]);
-    if (g.one) m = fmaxf(m, 0.0f);  // softmax1 shifts by max(row max, 0)
-    float l = 0.0f;
-#pragma unroll 1
-    for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        uint32_t x[16];
-        st::tmem_ld16(tS + lane_base + c0, x);
-        st::tmem_ld_wait();
-        float p[16];
+        for (int j = 0; j < 64; j++)
+            if (cbase + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
+        red[half * AT + r] = m;
+        __syncthreads();
+        m = fmaxf(m, red[(half ^ 1) * AT + r]);
+        if (g.one) m = fmaxf(m, 0.0f);  // softmax1 shifts by max(row max, 0)
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            p[j] = c0 + j < lim ? fast_exp(__uint_as_float(x[j]) * g.scale - m) : 0.0f;
-            l += p[j];
+        for (int c = 0; c < 4; c++) {
+            float p[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int col = cbase + 16 * c + j;
+                p[j] = col < lim ? fast_exp(__uint_as_float(x[16 * c + j]) * g.scale - m) : 0.0f;
+                l += p[j];
+            }
+            uint32_t o[8];
+            pack16(p, o);
+            put16(sP, r, cbase + 16 * c, o);
         }
-        uint32_t o[8];
-        pack16(p, o);
-        put16(sP, r, c0, o);
+    } else {
+        // up to 256 columns: the row's kc16 columns split in two 16-aligned
+        // halves, read from TMEM twice (max, then exponentials)
+        const int cw = ((kc16 >> 1) + 15) & ~15;
+        const int c_lo = half ? cw : 0, c_hi = half ? kc16 : cw;
+#pragma unroll 1
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+            uint32_t x[16];
+            st::tmem_ld16(tS + lane_base + c0, x);
+            st::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                if (c0 + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
+        }
+        red[half * AT + r] = m;
+        __syncthreads();
+        m = fmaxf(m, red[(half ^ 1) * AT + r]);
+        if (g.one) m = fmaxf(m, 0.0f);  // softmax1 shifts by max(row max, 0)
+#pragma unroll 1
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+            uint32_t x[16];
+            st::tmem_ld16(tS + lane_base + c0, x);
+            st::tmem_ld_wait();
+            float p[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                p[j] = c0 + j < lim ? fast_exp(__uint_as_float(x[j]) * g.scale - m) : 0.0f;
+                l += p[j];
+            }
+            uint32_t o[8];
+            pack16(p, o);
+            put16(sP, r, c0, o);
+        }
     }
     __syncthreads();  // every thread has read red (max) before it is reused for sums
     red[half * AT + r] = l;
@@ -407,7 +479,8 @@ __device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uin
 }
 
 // Backward.  Two kinds of CTA per head (blockIdx.x = head; blockIdx.y <
-// ntile: key tile kt = blockIdx.y, else query tile qt = blockIdx.y - ntile):
+// ntile: key tile kt = blockIdx.y, else query tile qt = blockIdx.y - ntile;
+// a sequence of one tile has one CTA per head, which does both):
 //  * key tile kt: dV = sum over query tiles of P^T dO, dK = sum of dS^T Q
 //    (accumulated in TMEM across the query tiles that see the keys);
 //  * query tile qt: dQ = sum over the key tiles it sees of dS K.
@@ -439,6 +512,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     __syncthreads();
     st::tc_fence_after();
     const uint32_t tmem = *tslot, tA = tmem + 256, tB = tmem + 320;  // dV / dQ, dK
+    const uint32_t tQ = tmem + 384;                                   // dQ of a one-tile sequence
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t ph0 = 0, ph1 = 0;
     bool ok = true;
@@ -467,6 +541,14 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
                     st::umma_f16(tA, mnmaj(p, kk, PT / 2), mnmaj(d, kk, TILE), id_tt, acc);
                     st::umma_f16(tB, mnmaj(s, kk, PT / 2), mnmaj(q, kk, TILE), id_tt, acc);
                 }
+                if (ntile == 1) {
+                    // one tile of keys and queries: this CTA also has everything dQ = dS K needs
+                    constexpr uint32_t id_nt = st::idesc_make(1, 0, false, true, AT, AD);
+                    const uint32_t k = st::smem_u32(smem + B_K);
+#pragma unroll
+                    for (int kk = 0; kk < AT / 16; kk++)
+                        st::umma_f16(tQ, kmaj128(s, kk), mnmaj(k, kk, TILE), id_nt, kk > 0 ? 1u : 0u);
+                }
                 st::umma_commit(&bar[1]);
             }
             // the next query tile restages Q, dO, P and dS: these MMAs must be done
@@ -477,10 +559,9 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
         }
         const int gk = kt * AT + r;
         const int64_t rk = g.mq.at(z, g.heads, gk < g.t ? gk : 0);
-#pragma unroll
-        for (int w = 0; w < 2; w++) {
-            void *dst_t = w == 0 ? g.dv : g.dk;
-            const uint32_t src = w == 0 ? tA : tB;
+        for (int w = 0; w < (ntile == 1 ? 3 : 2); w++) {
+            void *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
+            const uint32_t src = w == 0 ? tA : w == 1 ? tB : tQ;
 #pragma unroll
             for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
                 uint32_t x[16];
@@ -576,7 +657,8 @@ st_status launch_bwd(st_handle *h, const AttnArgs &g) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
         attr = true;
     }
-    const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(2 * ((g.t + AT - 1) / AT)));
+    const int ntile = (g.t + AT - 1) / AT;
+    const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(ntile == 1 ? 1 : 2 * ntile));
     k_attn_bwd<F32><<<grid, ATHREADS, BWD_SMEM, h->stream>>>(g);
     return st_after_launch(h, "k_attn_bwd");
 }

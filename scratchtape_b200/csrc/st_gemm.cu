@@ -852,7 +852,142 @@ bool operand_map(CUtensorMap *map, const Operand &o, int64_t batch, int64_t srow
 
 }  // namespace
 
+// Epilogue::col_sum: col_sum[z][col] += the sum over k of b[z][:, col], in a
+// fixed order (per-chunk partials, then the chunks in order).
+st_status launch_col_sum(st_handle *h, const Operand &B, int64_t batch, int64_t k, int64_t n, const st_epilogue &e) {
+    GemmArgs g{};
+    g.K = static_cast<int>(k);
+    g.N = static_cast<int>(n);
+    g.batch = static_cast<int>(batch);
+    const bool quad = !B.trans && n % 4 == 0 && B.ld % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(B.ptr + B.off) % 16) == 0 &&
+                      (batch == 1 || (B.stride % 4 == 0 && (B.grp == 1 || B.inner % 4 == 0)));
+    if (quad) {
+        // B's rows 16-byte aligned: chunks of 32 rows (one round of loads
+        // per thread), 64 column quads per block
+        int64_t rpc = 32;
+        if ((k + rpc - 1) / rpc > 65535) rpc = (k + 65534) / 65535;
+        const int64_t chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
+        float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
+        if (!part) return ST_NO_MEMORY;
+        dim3 grid(static_cast<unsigned>((n / 4 + COL_QUADS - 1) / COL_QUADS), static_cast<unsigned>(chunks),
+                  static_cast<unsigned>(batch));
+        k_col_sum_part4<<<grid, dim3(COL_QUADS, COL_GROUPS), 0, h->stream>>>(B, g.K, g.N, rpc, part);
+        st_status s = st_after_launch(h, "k_col_sum_part4");
+        if (s != ST_OK) return s;
+        k_col_sum_fin32<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(batch)),
+                          COLF_WARPS * 32, 0, h->stream>>>(part, static_cast<int>(chunks), g.N, e.col_sum,
+                                                           e.col_sum_off, e.col_sum_stride);
+        s = st_after_launch(h, "k_col_sum_fin32");
+        if (s != ST_OK) return s;
+    } else {
+        // one column per thread, chunks of >= 64 rows, so that batch * column
+        // blocks * chunks fills the GPU
+        const int64_t col_blocks = (n + 127) / 128;
+        int64_t chunks = std::max<int64_t>(
+            1, std::min<int64_t>((k + 63) / 64, (4LL * h->num_sms) / (col_blocks * batch) + 1));
+        chunks = std::min<int64_t>(chunks, 65535);
+        const int64_t rpc = std::max<int64_t>(1, (k + chunks - 1) / chunks);
+        chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
+        float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
+        if (!part) return ST_NO_MEMORY;
+        dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(chunks), static_cast<unsigned>(batch));
+        k_col_sum_part<<<grid, 128, 0, h->stream>>>(B, g.K, g.N, rpc, part);
+        st_status s = st_after_launch(h, "k_col_sum_part");
+        if (s != ST_OK) return s;
+        const int64_t fin_blocks = (batch * n + 7) / 8;
+        if (fin_blocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum too wide");
+        k_col_sum_fin<<<static_cast<unsigned>(fin_blocks), 256, 0, h->stream>>>(
+            part, static_cast<int>(chunks), g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
+        s = st_after_launch(h, "k_col_sum_fin");
+        if (s != ST_OK) return s;
+    }
+    return ST_OK;
+}
+
 static bool fits_i32(int64_t v) { return v >= 0 && v < (1ll << 31); }
+
+// ---- TF32X3: three TF32 products that together carry an f32 product -----
+//
+// x = hi + lo with hi = x rounded to TF32 (cvt.rna.tf32.f32) and lo = the
+// remainder, rounded to TF32 the same way (x - hi is exact in f32), so both
+// reach the tensor core with their low 13 bits already zero.  Then
+//   a b = a_hi b_hi + a_hi b_lo + a_lo b_hi + a_lo b_lo,
+// and the last term is below 2^-22 of |a| |b|: a GEMM with K' = 3K over the
+// operands concatenated along k -- A' = [a_hi  a_hi  a_lo], B' = [b_hi; b_lo;
+// b_hi] -- is the f32 product to about 2^-21, on the TF32 tensor cores, with
+// the TF32 kernel, its split-k and its epilogue unchanged.
+
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// The stored [srows, scols] matrix of every batch item of `src`, copied into
+// dst with its k axis (the columns if kcols, else the rows) three times as
+// long: copy j of each element is hi, or lo where j == lo_copy.
+__global__ void k_split3(const Operand src, int64_t srows, int64_t scols, int batch, int kcols, int lo_copy,
+                         float *dst, int64_t dld, int64_t dstride) {
+    const int64_t per = srows * scols, total = per * batch;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += step) {
+        const int z = static_cast<int>(i / per);
+        const int64_t e = i % per, r = e / scols, c = e % scols;
+        const float x = src.ptr[src.off + static_cast<int64_t>(z / src.grp) * src.stride +
+                                static_cast<int64_t>(z % src.grp) * src.inner + r * src.ld + c];
+        const float hi = tf32_rna(x), lo = tf32_rna(x - hi);
+        float *d = dst + z * dstride;
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            const float v = j == lo_copy ? lo : hi;
+            if (kcols) d[r * dld + c + j * scols] = v;
+            else d[(r + j * srows) * dld + c] = v;
+        }
+    }
+}
+
+st_status gemm_tf32x3(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch, int64_t m,
+                      int64_t k, int64_t n, const st_epilogue *epi) {
+    if (a->dtype != ST_F32 || b->dtype != ST_F32 || out->dtype != ST_F32)
+        return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: ST_PREC_TF32X3 takes f32 operands");
+    if (3 * k >= (1ll << 31)) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: k too large for TF32X3");
+    cudaSetDevice(h->device);
+    const Operand A = to_operand(a, a->trans ? m : k);
+    const Operand B = to_operand(b, b->trans ? k : n);
+    auto r4 = [](int64_t v) { return (v + 3) / 4 * 4; };
+    // A' logical [m, 3k]: stored [m, 3k] or (trans) [3k, m]; B' logical [3k, n]: stored [3k, n] or (trans) [n, 3k]
+    const int64_t a_ld = a->trans ? r4(m) : r4(3 * k), a_rows = a->trans ? 3 * k : m;
+    const int64_t b_ld = b->trans ? r4(3 * k) : r4(n), b_rows = b->trans ? n : 3 * k;
+    const int64_t a_str = a_rows * a_ld, b_str = b_rows * b_ld;
+    float *buf = static_cast<float *>(st_scratch(h, SLOT_X3, sizeof(float) * batch * (a_str + b_str)));
+    if (!buf) return ST_NO_MEMORY;
+    float *a3 = buf, *b3 = buf + batch * a_str;
+    auto split = [&](const Operand &src, int64_t srows, int64_t scols, bool kcols, int lo_copy, float *dst,
+                     int64_t dld, int64_t dstr) {
+        const int64_t total = srows * scols * batch;
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 16LL * h->num_sms));
+        k_split3<<<blocks, 256, 0, h->stream>>>(src, srows, scols, static_cast<int>(batch), kcols ? 1 : 0, lo_copy,
+                                                dst, dld, dstr);
+        return st_after_launch(h, "k_split3");
+    };
+    // A' = [hi hi lo] along k: k is A's stored columns unless A is stored transposed
+    st_status s = a->trans ? split(A, k, m, false, 2, a3, a_ld, a_str) : split(A, m, k, true, 2, a3, a_ld, a_str);
+    if (s != ST_OK) return s;
+    // B' = [hi; lo; hi] along k: k is B's stored rows unless B is stored transposed
+    s = b->trans ? split(B, n, k, true, 1, b3, b_ld, b_str) : split(B, k, n, false, 1, b3, b_ld, b_str);
+    if (s != ST_OK) return s;
+    st_epilogue e{};
+    if (epi) e = *epi;
+    if (e.col_sum) {  // the column sums of the original b
+        s = launch_col_sum(h, B, batch, k, n, e);
+        if (s != ST_OK) return s;
+        e.col_sum = nullptr;
+    }
+    const st_mat a2{a3, 0, a_str, 0, a_ld, 1, a->trans, ST_F32, 0};
+    const st_mat b2{b3, 0, b_str, 0, b_ld, 1, b->trans, ST_F32, 0};
+    return st_gemm(h, &a2, &b2, out, batch, m, 3 * k, n, &e, ST_PREC_TF32);
+}
 
 extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, const st_mat *out, int64_t batch,
                              int64_t m, int64_t k, int64_t n, const st_epilogue *epi, st_precision prec) {
@@ -868,8 +1003,12 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: a and b must both be f32, f16 or bf16, out f32");
     if (a->off < 0 || b->off < 0 || out->off < 0 || a->ld < 0 || b->ld < 0 || out->ld < 0)
         return h->fail(ST_INVALID_ARG, "st_gemm: negative offset or ld");
-    if (prec != ST_PREC_F32_EXACT && prec != ST_PREC_TF32 && prec != ST_PREC_F16)
+    if (prec != ST_PREC_F32_EXACT && prec != ST_PREC_TF32 && prec != ST_PREC_F16 && prec != ST_PREC_TF32X3)
         return h->fail(ST_INVALID_ARG, "st_gemm: unknown precision");
+    if (prec == ST_PREC_TF32X3) {
+        if (k == 0) prec = ST_PREC_TF32;  // nothing to split: the epilogue alone
+        else return gemm_tf32x3(h, a, b, out, batch, m, k, n, epi);
+    }
     if ((ab != 0) != (prec == ST_PREC_F16))
         return h->fail(ST_INVALID_ARG, "st_gemm: ST_PREC_F16 goes with f16 / bf16 operands, the others with f32");
     if (ab && epi && epi->col_sum)
@@ -915,49 +1054,8 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     }
 
     if (e.col_sum) {
-        const bool quad = !B.trans && n % 4 == 0 && B.ld % 4 == 0 &&
-                          (reinterpret_cast<uintptr_t>(B.ptr + B.off) % 16) == 0 &&
-                          (batch == 1 || (B.stride % 4 == 0 && (B.grp == 1 || B.inner % 4 == 0)));
-        if (quad) {
-            // B's rows 16-byte aligned: chunks of 32 rows (one round of loads
-            // per thread), 64 column quads per block
-            int64_t rpc = 32;
-            if ((k + rpc - 1) / rpc > 65535) rpc = (k + 65534) / 65535;
-            const int64_t chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
-            float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
-            if (!part) return ST_NO_MEMORY;
-            dim3 grid(static_cast<unsigned>((n / 4 + COL_QUADS - 1) / COL_QUADS), static_cast<unsigned>(chunks),
-                      static_cast<unsigned>(batch));
-            k_col_sum_part4<<<grid, dim3(COL_QUADS, COL_GROUPS), 0, h->stream>>>(B, g.K, g.N, rpc, part);
-            st_status s = st_after_launch(h, "k_col_sum_part4");
-            if (s != ST_OK) return s;
-            k_col_sum_fin32<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(batch)),
-                              COLF_WARPS * 32, 0, h->stream>>>(part, static_cast<int>(chunks), g.N, e.col_sum,
-                                                               e.col_sum_off, e.col_sum_stride);
-            s = st_after_launch(h, "k_col_sum_fin32");
-            if (s != ST_OK) return s;
-        } else {
-            // one column per thread, chunks of >= 64 rows, so that batch * column
-            // blocks * chunks fills the GPU
-            const int64_t col_blocks = (n + 127) / 128;
-            int64_t chunks = std::max<int64_t>(
-                1, std::min<int64_t>((k + 63) / 64, (4LL * h->num_sms) / (col_blocks * batch) + 1));
-            chunks = std::min<int64_t>(chunks, 65535);
-            const int64_t rpc = std::max<int64_t>(1, (k + chunks - 1) / chunks);
-            chunks = std::max<int64_t>(1, (k + rpc - 1) / rpc);
-            float *part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * batch * chunks * n));
-            if (!part) return ST_NO_MEMORY;
-            dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(chunks), static_cast<unsigned>(batch));
-            k_col_sum_part<<<grid, 128, 0, h->stream>>>(B, g.K, g.N, rpc, part);
-            st_status s = st_after_launch(h, "k_col_sum_part");
-            if (s != ST_OK) return s;
-            const int64_t fin_blocks = (batch * n + 7) / 8;
-            if (fin_blocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_gemm: col_sum too wide");
-            k_col_sum_fin<<<static_cast<unsigned>(fin_blocks), 256, 0, h->stream>>>(
-                part, static_cast<int>(chunks), g.N, g.batch, e.col_sum, e.col_sum_off, e.col_sum_stride);
-            s = st_after_launch(h, "k_col_sum_fin");
-            if (s != ST_OK) return s;
-        }
+        const st_status s = launch_col_sum(h, B, batch, k, n, e);
+        if (s != ST_OK) return s;
     }
 
     bool use_tc = (prec == ST_PREC_TF32 || prec == ST_PREC_F16) && k >= 1;

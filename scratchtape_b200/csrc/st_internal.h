@@ -30,6 +30,7 @@ enum StScratchSlot {
     SLOT_MLP_PART,    // fused MLP step: per-block partial products
     SLOT_MLP_CTL,     // fused MLP step: per-block arrival / departure counters
     SLOT_COMM,        // sharded kNN search: local, gathered and merged best-128 lists
+    SLOT_X3,          // TF32X3: the operands split into TF32 parts, concatenated along k
     SLOT_COUNT
 };
 

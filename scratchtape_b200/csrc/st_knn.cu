@@ -1531,14 +1531,17 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
             bool qlive[NG];
 #pragma unroll
             for (int grp = 0; grp < NG; grp++) {
-                qlive[grp] = has_q && lane < EQ && qbase + NQ * grp + q0 + lane < g.nq;
+                const int qu = NQ * grp + q0 + lane;  // this lane's query in the unit
+                qlive[grp] = has_q && lane < EQ && qbase + qu < g.nq;
                 cnt[grp] = 0;
                 thr[grp] = qlive[grp] ? -INFINITY : INFINITY;
-                eff[grp] = thr[grp];
+                // a unit starts from the best 128th score any list of the query has
+                // published (the sample passes' seeds, and earlier units'), not from -inf
+                eff[grp] = qlive[grp] ? thr_of(__ldcg(g.gthr + qbase + qu)) : INFINITY;
                 pub[grp] = pub_next[grp] = 0u;
                 if (has_q && lane < EQ) {
-                    wthr[NQ * grp + q0 + lane] = eff[grp];
-                    wthrl[NQ * grp + q0 + lane] = eff[grp];
+                    wthr[qu] = eff[grp];
+                    wthrl[qu] = qlive[grp] ? lowered(eff[grp] / qc_P[qu] * SH) : eff[grp];
                 }
             }
             __syncwarp();
@@ -1566,7 +1569,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                     // read's latency stays off this tile's path)
                     pub[grp] = pub_next[grp];
                     pub_next[grp] = 0u;
-                    if (qlive[grp] && (gt & 15u) == 0u) pub_next[grp] = __ldcg(g.gthr + qbase + qo + lane);
+                    if (qlive[grp] && (i & 15) == 15) pub_next[grp] = __ldcg(g.gthr + qbase + qo + lane);
                     if (!nwait(&accf[a], (gs / N_ACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                         ok = false;
                         break;

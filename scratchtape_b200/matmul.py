@@ -27,6 +27,7 @@ from .device import handle
 TF32 = N.PREC_TF32
 F32_EXACT = N.PREC_F32_EXACT
 F16 = N.PREC_F16
+TF32X3 = N.PREC_TF32X3  # three TF32 products per f32 product: f32 accuracy on the tensor cores
 _DTYPES = {torch.float32: N.ST_F32, torch.float16: N.ST_F16, torch.bfloat16: N.ST_BF16}
 
 

@@ -4,7 +4,9 @@ Case lists follow the reference's own device test (src/gpu_step/matmul.rs:962-10
 ragged shapes, batch strides, odd buffer offsets, every epilogue, the step's
 real shapes, and column sums.  F32_EXACT must be bit-identical to the oracle
 (same k-ascending multiply-then-add chain).  TF32 (tcgen05) is held to 5e-3
-of the output scale, the north-star tensor-core tolerance.
+of the output scale, the north-star tensor-core tolerance; TF32X3 (three
+TF32 products per f32 product) to the north star's f32 bar,
+1e-5 sqrt(K) max|a| max|b|.
 """
 import numpy as np
 import pytest
@@ -160,6 +162,40 @@ def test_tf32_tensor_cores(dev, ci):
     scale = np.abs(want[:cs_off]).max()
     err = np.abs(got[:cs_off] - want[:cs_off]).max()
     assert err <= TF32_TOL * scale, (err, scale)
+    cs_scale = np.abs(want[cs_off:]).max()
+    assert np.abs(got[cs_off:] - want[cs_off:]).max() <= 1e-4 * cs_scale
+
+
+def _f32_bar(case, seed, aligned):
+    """The north star's f32 bar, max |err| <= 1e-5 sqrt(K) max|a| max|b|, for
+    the operands _run_case draws (Gaussian, regenerated from the same seed)."""
+    batch, m, k, n = case[:4]
+    rng = np.random.default_rng(seed)
+    r4 = (lambda x: (x + 3) // 4 * 4) if aligned else (lambda x: x)
+    a_off, b_off = (4, 8) if aligned else (3, 5)
+    sa, sb = r4(m * k + 1), (r4(k * n + 2) if batch > 1 else 0)
+    a = _gauss(rng, a_off + batch * sa)
+    b = _gauss(rng, b_off + max(batch, 1) * max(sb, k * n))
+    return 1e-5 * np.sqrt(k) * np.abs(a).max() * np.abs(b).max()
+
+
+@pytest.mark.parametrize("aligned,ci", [(True, i) for i in range(len(CASES_TC))] +
+                                       [(False, i) for i in range(len(CASES_F32))])
+def test_tf32x3_reaches_the_f32_bar(dev, aligned, ci):
+    """TF32X3: each operand split into a TF32 high part and a TF32 rest, three
+    tensor-core products (hi.hi + hi.lo + lo.hi) over the split operands
+    concatenated along k.  Held to the north star's f32 SIMT bar against the
+    oracle's tensor.rs matmul -- the accuracy plain TF32 (5e-3) does not have
+    -- on every layout, batch stride, epilogue and column sum, aligned or not
+    (the split copies feed the tensor cores either way)."""
+    import scratchtape_b200 as st
+    case = (CASES_TC if aligned else CASES_F32)[ci]
+    seed = 500 + ci + (0 if aligned else 1000)
+    got, want, cs_off, kernel = _run_case(st, case, st.TF32X3, aligned, seed)
+    assert kernel in ("k_gemm_tf32", "k_splitk_reduce"), kernel
+    tol = _f32_bar(case, seed, aligned)
+    err = np.abs(got[:cs_off] - want[:cs_off]).max()
+    assert err <= tol, (err, tol)
     cs_scale = np.abs(want[cs_off:]).max()
     assert np.abs(got[cs_off:] - want[cs_off:]).max() <= 1e-4 * cs_scale
 
