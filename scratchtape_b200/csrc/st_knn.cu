@@ -1066,7 +1066,7 @@ constexpr float MAGIC_F = 12582912.0f;
 static_assert(N_ACC_COL + N_ACC * N_ACC_COLS <= N_TMEM_COLS, "keys-on-M kNN scan TMEM budget");
 
 // Shared-memory layout of the keys-on-M scan with NG groups of 32 queries
-// resident per unit (NG = 1: the narrow pass; NG = 4: 128 queries, the wide scan).
+// resident per unit (the library launches NG = 1, the narrow pass).
 template <int NG>
 struct NarrowSmem {
     static constexpr int QB = NQ * NG;                       // queries per unit
@@ -1186,9 +1186,9 @@ __device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64
 // scans its split's 128-key tiles against the block's QB = 32 NG queries,
 // which stay resident in shared memory as int8 limbs for the whole unit: each
 // key tile is loaded and expanded into TMEM once and meets NG groups of 32
-// queries, one accumulator each (8 MMAs of K = 32 per group).  NG = 1 is the
-// narrow pass (<= 32 queries); NG = 4 the wide scan, where a tile's 32 MMAs
-// (~2000 cycles) hide every per-tile hand-off.
+// queries, one accumulator each (8 MMAs of K = 32 per group).  The library
+// launches NG = 1 (the narrow pass, <= 32 queries); a unit's thresholds start
+// from the best 128th score any list of the query has published.
 template <int MODE, int PREC, int NG>
 __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g) {
     using L = NarrowSmem<NG>;
@@ -1737,7 +1737,7 @@ st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
         attr_done = true;
     }
     kern<<<grid, N_THREADS, NarrowSmem<NG>::SMEM, h->stream>>>(g);
-    return st_after_launch(h, NG == 1 ? "k_knn_narrow" : "k_knn_wide8");
+    return st_after_launch(h, "k_knn_narrow");
 }
 
 }  // namespace
@@ -1750,27 +1750,27 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (s != ST_OK) return s;
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
-    if (!ranges && dim == 256 && (nq <= NQ || prec == 0) && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
-        // dim 256: the keys-on-M scan (keys as the kind::i8 A operand in TMEM).
-        // Up to 32 queries: one group per unit (the narrow pass).  More (EXACT):
-        // units of 128 queries (4 groups) resident in shared memory, every key
-        // tile meeting all four -- the wide scan.  F16REF with more queries
-        // stays on k_knn_scan, which rounds the dequantised keys to f16 as the
-        // reference does.
-        const bool wide = nq > NQ;
-        const int qb_size = wide ? 4 * NQ : NQ;
-        const int nqb = static_cast<int>((nq + qb_size - 1) / qb_size);
-        const int64_t nq_pad = static_cast<int64_t>(nqb) * qb_size;
+    if (!ranges && dim == 256 && nq <= NQ && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
+        // dim 256, up to 32 queries: the keys-on-M scan (keys as the kind::i8 A
+        // operand in TMEM), one group of 32 queries per unit.  More queries run
+        // k_knn_scan below: with 128 resident queries per unit (four groups per
+        // key tile) the keys-on-M scan measured 0.96-1.0 s at 4096 x 2^27 against
+        // k_knn_scan's 0.5 s -- its epilogue reads two limb columns per (key,
+        // query) pair and every accumulator step passes through all eight
+        // epilogue warps in turn (ncu: tensor pipe 10.6 %, issue 18.9 %) -- and
+        // four int8 limbs cost the tensor core what k_knn_scan's f16 hi + lo
+        // pair costs, so it could not win by much even with a faster epilogue.
+        constexpr int qb_size = NQ;  // one query block: NG = 1
+        const int nqb = 1;
+        const int64_t nq_pad = qb_size;
         const int64_t tiles = (n_keys + NK - 1) / NK;
-        // narrow: one key split per SM; wide: about eight units per SM
-        int64_t splits = wide ? std::max<int64_t>(1, (8LL * h->num_sms + nqb - 1) / nqb) : h->num_sms;
-        splits = std::min<int64_t>(splits, tiles);
+        int64_t splits = std::min<int64_t>(h->num_sms, tiles);  // one key split per SM
         const int64_t tps = (tiles + splits - 1) / splits;
         splits = (tiles + tps - 1) / tps;
         const int64_t units = splits * nqb;
         if (units > (1LL << 30)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
         const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
-        const int64_t sample_splits = wide ? splits : h->num_sms;  // the sample passes' key splits
+        const int64_t sample_splits = h->num_sms;  // the sample passes' key splits
         const int64_t max_splits = std::max(splits, sample_splits);
         // candidate buffers for the widest grid any pass launches (the sample passes have up to
         // sample_splits * nqb units)
@@ -1790,7 +1790,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes + tmp_bytes);
         ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, nq_pad * sizeof(uint32_t), h->stream));
         // queries per limb block: 16 or 32 (an epilogue warp takes 16; NL x 16 is a multiple of 16)
-        const int nqp = (!wide && nq <= EQ) ? EQ : NQ;
+        const int nqp = nq <= EQ ? EQ : NQ;
         NarrowArgs g{};
         g.codes = codes;
         g.scales = scales;
@@ -1807,12 +1807,6 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.gthr = gthr;
         g.status = h->d_status;
         auto run = [&](const NarrowArgs &a, int gr) {
-            if (wide) {
-                if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT, 4>(h, a, gr);
-                if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF, 4>(h, a, gr);
-                if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT, 4>(h, a, gr);
-                return launch_narrow<MODE_L2, PREC_F16REF, 4>(h, a, gr);
-            }
             if (mode == 0 && prec == 0) return launch_narrow<MODE_DOT, PREC_EXACT, 1>(h, a, gr);
             if (mode == 0) return launch_narrow<MODE_DOT, PREC_F16REF, 1>(h, a, gr);
             if (prec == 0) return launch_narrow<MODE_L2, PREC_EXACT, 1>(h, a, gr);

@@ -41,6 +41,7 @@ class LmConfig:
     adam_eps: float = 1e-8
     sync_every: int = 8
     softmax1: bool = False  # the device tape's Config.softmax1 (src/gpu_step/tape.rs:400)
+    gemm_prec: int = TF32   # the linear layers' arithmetic: TF32, or TF32X3 (three TF32 products, f32 accuracy)
 
     def flops_per_step(self):
         """GEMM flops of one forward + backward (attention over causal pairs)."""
@@ -135,7 +136,7 @@ class TinyLM:
 
     # -- pieces -------------------------------------------------------------
     def _gemm(self, a, b, out, m, k, n, ta=False, tb=False, epi=None, h=None):
-        matmul_with(MatRef(a, trans=ta), MatRef(b, trans=tb), MatRef(out), 1, m, k, n, epi, TF32, h)
+        matmul_with(MatRef(a, trans=ta), MatRef(b, trans=tb), MatRef(out), 1, m, k, n, epi, self.c.gemm_prec, h)
 
     def _mark(self):
         """An event on the current stream, now."""

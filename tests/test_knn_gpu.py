@@ -289,12 +289,11 @@ def test_mem_file_round_trip_and_sharded_load(dev, tmp_path):
 
 @pytest.mark.parametrize("mode", ["dot", "l2"])
 @pytest.mark.parametrize("n,nq", [(129, 33), (70_001, 300), (700_001, 129), (2_600_000, 257)])
-def test_wide_keys_on_m_scan_matches_oracle(dev, mode, n, nq):
-    """More than 32 EXACT queries at dim 256 run the keys-on-M scan with 128
-    queries resident per unit (k_knn_wide8): ragged query blocks (33, 129,
-    257, 300 queries), ragged key tiles, scans big enough for the 1-in-1024
-    and 1-in-16 sample passes that seed the thresholds, every query block
-    meeting every key split.  Same bars as the other EXACT cases."""
+def test_wide_scan_matches_oracle_at_scale(dev, mode, n, nq):
+    """More than 32 EXACT queries at dim 256 (the wide scan, k_knn_scan):
+    ragged query blocks (33, 129, 257, 300 queries), ragged key tiles, up to
+    2.6 M keys, so that every query block meets many key splits and the
+    shared published thresholds.  Same bars as the other EXACT cases."""
     import scratchtape_b200.knn as K
     codes, scales = K.synth_keys(n, 256, seed=n % 97)
     rng = np.random.default_rng(n + nq)
