@@ -1334,6 +1334,11 @@ def run_ours_c4(args):
 
     from scratchtape_b200 import shard
     comm = shard.NcclComm() if world > 1 else None
+    if comm is not None:
+        # NCCL sets up a new communicator's connections on its first collective:
+        # do that with a same-size all-reduce now, outside the timed steps
+        shard.average_params(torch.zeros_like(model.params), comm=comm)
+        torch.cuda.synchronize()
     avg_ev = []
 
     def one_step(i, timed=False):
