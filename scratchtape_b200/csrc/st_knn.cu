@@ -1740,6 +1740,563 @@ st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
     return st_after_launch(h, "k_knn_narrow");
 }
 
+
+// ---- the wide scan with keys in tensor memory (k_knn_tmem) -----------------
+//
+// For more than 32 EXACT queries at dim 256.  A unit is (key split, block of
+// TQ = 256 queries).  The block's queries stay in shared memory for the whole
+// unit as f16, each prescaled by its power of two 2^e (max |q| 2^e in [2^14,
+// 2^15), so hi = f16(q 2^e) neither overflows nor flushes).  Each 128-key tile
+// is expanded once -- code u to the f16 value u - 1.5, exact -- straight into
+// TMEM, where it is the A operand (M = 128 keys) of one tcgen05 kind::f16 pass
+// per 128-query step (N = 128, K = 256 in 16 MMAs): every expanded key meets
+// all 256 queries, and shared memory carries only the queries' B tiles (no
+// expanded keys, no second pass).
+//
+// The product hi . (u - 1.5) is exact; it differs from the exact q 2^e .
+// (u - 1.5) by at most E_q = 1.5 sum |q_i 2^e - hi_i| plus the tensor core's
+// f32 accumulation error, bounded generously by 2^-12 1.5 sum |hi_i|.  The
+// epilogue (lane = key, columns = queries) keeps a (key, query) pair only if
+// acc >= (T_q + kn_k) / s_k - E_q, where T_q is the query's running 128th-best
+// score in dot units (lowered by 2^-18 to cover the reciprocal's rounding) and
+// kn_k = |k|^2 / 2 in L2 mode: no key whose exact score reaches the threshold
+// is dropped.  A kept pair's exact score -- s_k sum (u_i - 1.5) q_i 2^e in f64
+// from the key's codes and the f32 query, rounded once -- decides its entry in
+// the candidate buffer of (query, TMEM lane quadrant), as in k_knn_narrow;
+// lists, thresholds published through gthr, sample-pass seeding and the merge
+// are the narrow scan's.  Scores come out in the wide scan's units (DOT:
+// q.k 2^e; L2: (2 q.k - |k|^2) 2^(e-1)), so k_knn_merge and k_knn_decode are
+// shared.
+//
+// Roles (576 threads, one CTA per SM): warp 17 bulk-copies each tile's codes
+// and scales into an 8-stage ring; warps 8-15 expand codes into TMEM (a warp
+// per 16 lanes, 16x256b stores; u - 1.5 as f16 through a byte permute of a
+// four-entry table) and publish per-key scale and |k|^2 / 2; warp 16 issues
+// the MMAs (two A buffers, two 128-column accumulators); warps 0-7 filter
+// (warp w: lane quadrant w % 4, queries 64 (w / 4) .. of each step).
+constexpr int TQ = 256;                       // queries per unit: two 128-query steps
+constexpr int T_STAGES = 8;
+constexpr int T_NACC = 2;
+constexpr int TO_Q = 0;                       // [2 steps][4 K chunks][128 rows x 128 B] f16, SW128
+constexpr int TO_RING = TO_Q + 2 * 4 * 16384;
+constexpr int TO_KF = TO_RING + T_STAGES * N_STAGE_BYTES;   // [N_KF][128] scale
+constexpr int TO_KN = TO_KF + N_KF * NK * 4;                // [N_KF][128] |k|^2 / 2 (L2)
+constexpr int TO_QC = TO_KN + N_KF * NK * 4;                // [2 units][4][TQ]: E_q, 2^-e, 2^e, live
+constexpr int TO_THR = TO_QC + 2 * 4 * TQ * 4;              // [4 quadrants][TQ] thresholds: stored units
+constexpr int TO_THF = TO_THR + N_QUAD * TQ * 4;            // [4 quadrants][TQ] the same in dot units, lowered
+constexpr int TO_BAR = TO_THF + N_QUAD * TQ * 4;
+constexpr int T_NBARS = 2 * T_STAGES + 2 * N_A + 2 * T_NACC + N_KF + 2 + 2 + 1 + 1;
+constexpr int TO_MISC = TO_BAR + T_NBARS * 8;
+constexpr int TMEM_SMEM = TO_MISC + 16 + 1024;
+static_assert(TMEM_SMEM <= 232448, "keys-in-TMEM kNN scan shared memory exceeds the sm_100 limit");
+static_assert(N_A * 128 + T_NACC * 128 <= 512, "keys-in-TMEM kNN scan TMEM budget");
+
+// f16 bit patterns of u - 1.5 for u = 0..3, as the byte table of a permute:
+// bytes 2u, 2u + 1 of {T1:T0} hold the value for code u.
+constexpr uint32_t TM_T0 = 0xB800BE00u;  // -0.5 (u = 1) | -1.5 (u = 0)
+constexpr uint32_t TM_T1 = 0x3E003800u;  //  1.5 (u = 3) |  0.5 (u = 2)
+
+// Two f16 (u - 1.5) for the two codes in bits 0-3 of x (code a = bits 0-1,
+// the lower half of the result; b = bits 2-3, the upper half).
+__device__ __forceinline__ uint32_t tm_pair(uint32_t x) {
+    // selector nibbles (2a, 2a+1, 2b, 2b+1) = (a + 256 b) * 34 + 0x1010
+    const uint32_t ab = (x & 3u) | ((x << 6) & 0x300u);
+    const uint32_t sel = ab * 34u + 0x1010u;
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(TM_T0), "r"(TM_T1), "r"(sel));
+    return r;
+}
+
+// The exact stored score of (key with codes `codes` and scale s, query row
+// qrow with p2e = 2^e): DOT s sum (u - 1.5) q 2^e; L2 (2 q.k - |k|^2) 2^(e-1)
+// with |k|^2 = s^2 (64 + 2 c3) (c3: codes 0 or 3), in f64, rounded once.
+template <int MODE>
+__device__ __noinline__ float tm_exact(const uint8_t *codes, float s, const float *qrow, float p2e, int c3) {
+    double acc = 0.0;
+    const uint4 *kc = reinterpret_cast<const uint4 *>(codes);
+#pragma unroll 1
+    for (int w = 0; w < 4; w++) {
+        const uint4 c = __ldg(kc + w);
+        const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float4 *q4 = reinterpret_cast<const float4 *>(qrow + 64 * w + 16 * i);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float4 q = __ldg(q4 + j);
+                const uint32_t byte = (cw[i] >> (8 * j)) & 0xffu;
+                acc += (static_cast<double>(byte & 3u) - 1.5) * q.x;
+                acc += (static_cast<double>((byte >> 2) & 3u) - 1.5) * q.y;
+                acc += (static_cast<double>((byte >> 4) & 3u) - 1.5) * q.z;
+                acc += (static_cast<double>(byte >> 6) - 1.5) * q.w;
+            }
+        }
+    }
+    const double dot = acc * static_cast<double>(s) * static_cast<double>(p2e);  // q.k 2^e
+    if (MODE == MODE_DOT) return static_cast<float>(dot);
+    const double kn = static_cast<double>(s) * s * (64.0 + 2.0 * c3);         // |k|^2
+    return static_cast<float>(dot - kn * 0.5 * static_cast<double>(p2e));      // (2 q.k - |k|^2) 2^(e-1)
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *kf = reinterpret_cast<float *>(smem + TO_KF);
+    float *kn = reinterpret_cast<float *>(smem + TO_KN);
+    float *thr_s = reinterpret_cast<float *>(smem + TO_THR);  // [4][TQ] effective 128th best (stored units)
+    float *thr_f = reinterpret_cast<float *>(smem + TO_THF);  // [4][TQ] the same, lowered (the filter's)
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TO_BAR);
+    uint64_t *rfull = bars, *rempty = bars + T_STAGES, *afull = bars + 2 * T_STAGES, *aempty = afull + N_A;
+    uint64_t *accf = aempty + N_A, *acce = accf + T_NACC, *kfr = acce + T_NACC, *qready = kfr + N_KF;
+    uint64_t *edone = qready + 2, *qfree = edone + 2, *fin = qfree + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + TO_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + TO_MISC + 4);
+    // per-query constants of the CTA's unit j, buffer j % 2: E_q, 2^e, live (1 / 0)
+    float *qconst0 = reinterpret_cast<float *>(smem + TO_QC);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < T_STAGES; s++) {
+            st::mbar_init(&rfull[s], 1);
+            st::mbar_init(&rempty[s], N_PROD);
+        }
+        for (int b = 0; b < N_A; b++) {
+            st::mbar_init(&afull[b], N_PROD);
+            st::mbar_init(&aempty[b], 1);
+        }
+        for (int a = 0; a < T_NACC; a++) {
+            st::mbar_init(&accf[a], 1);
+            st::mbar_init(&acce[a], N_EPI);
+        }
+        for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
+        for (int j = 0; j < 2; j++) {
+            st::mbar_init(&qready[j], N_PROD);
+            st::mbar_init(&edone[j], N_EPI);
+        }
+        st::mbar_init(qfree, 1);
+        st::mbar_init(fin, 1);
+        *abort_flag = 0;
+        st::fence_mbar_init();
+    }
+    if (warp == N_MMA_WARP) {
+        st::tmem_alloc(tmem_slot, N_TMEM_COLS);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t ACC_COL = N_A * 128;  // accumulators after the two 128-column A buffers
+
+    if (warp == N_TMA_WARP) {
+        // ------------------------------------------------------------ code / scale loader
+        if (lane == 0) {
+            uint32_t gt = 0;
+            bool ok = true;
+            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x) {
+                int64_t tb;
+                int nk;
+                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                    const uint32_t s = gt % T_STAGES;
+                    if (gt >= T_STAGES &&
+                        !nwait(&rempty[s], ((gt / T_STAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    const uintptr_t s0 = reinterpret_cast<uintptr_t>(g.scales + tb) & ~uintptr_t(15);
+                    const uintptr_t s1 = (reinterpret_cast<uintptr_t>(g.scales + tb + nk) + 15) & ~uintptr_t(15);
+                    const uint32_t cb = static_cast<uint32_t>(nk) * 64u, sb = static_cast<uint32_t>(s1 - s0);
+                    uint8_t *dst = smem + TO_RING + s * N_STAGE_BYTES;
+                    st::mbar_arrive_expect_tx(&rfull[s], cb + sb);
+                    st::bulk_load(dst, g.codes + tb * 64, cb, &rfull[s]);
+                    st::bulk_load(dst + N_CODE_BYTES, reinterpret_cast<const void *>(s0), sb, &rfull[s]);
+                }
+            }
+            const uint32_t first = gt > T_STAGES ? gt - T_STAGES : 0;
+            for (uint32_t i = first; i < gt; i++)
+                st::mbar_wait(&rfull[i % T_STAGES], (i / T_STAGES) & 1u, g.status, st::DEV_TIMEOUT_FULL);
+        }
+    } else if (warp >= N_EPI && warp < N_MMA_WARP) {
+        // ------------------------------------------------------------ producers
+        const int pw = warp - N_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
+        const int quad = warp & 3, half = pw >> 2;
+        const int m = lane & 3;       // the byte of each code word this thread expands
+        uint32_t gt = 0, uj = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            if (uj >= 1 && !nwait(qfree, (uj - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) break;
+            if (uj >= 2 && !nwait(&edone[uj & 1u], ((uj - 2) >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC))
+                break;
+            float *qc = qconst0 + (uj & 1u) * 4 * TQ;
+            const int qbase = (unit % g.nqb) * TQ;
+            // warp pw prepares queries pw, pw + 8, ..; lane l writes dims 8l .. 8l + 7 (one
+            // 16-byte piece of the row's K chunk l / 8) as f16 of q 2^e
+            for (int r = pw; r < TQ; r += N_PROD) {
+                const int qg = qbase + r;
+                const bool live = qg < g.nq;
+                const float *qrow = g.q + static_cast<int64_t>(live ? qg : 0) * 256;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+                if (live) {
+                    a = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane);
+                    b = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane + 1);
+                }
+                const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                float mx = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) mx = fmaxf(mx, fabsf(v[i]));
+                mx = warp_max(mx);
+                const int e = query_exp(mx);
+                const float p2e = pow2f(e);
+                float err = 0.0f, mag = 0.0f;
+                uint32_t hw[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float x0 = v[2 * i] * p2e, x1 = v[2 * i + 1] * p2e;
+                    const __half2 hh = __floats2half2_rn(x0, x1);
+                    const float2 hf = __half22float2(hh);
+                    err += fabsf(x0 - hf.x) + fabsf(x1 - hf.y);
+                    mag += fabsf(hf.x) + fabsf(hf.y);
+                    hw[i] = *reinterpret_cast<const uint32_t *>(&hh);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    err += __shfl_xor_sync(0xffffffffu, err, o);
+                    mag += __shfl_xor_sync(0xffffffffu, mag, o);
+                }
+                const int step = r >> 7, row = r & 127;
+                *reinterpret_cast<uint4 *>(smem + TO_Q + step * 65536 + (lane >> 3) * 16384 +
+                                           st::sw128_offset(row, lane & 7)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                if (lane == 0) {
+                    // the sums round up by far less than the 2^-12 slack on the accumulation
+                    qc[r] = live ? 1.5f * err + 1.5f * 0.000244140625f * mag + 1e-30f : 0.0f;
+                    qc[TQ + r] = p2e;
+                    qc[2 * TQ + r] = live ? 1.0f : 0.0f;
+                }
+            }
+            st::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) st::mbar_arrive(&qready[uj & 1u]);
+
+            int64_t tb;
+            int nk;
+            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                const uint32_t s = gt % T_STAGES, b = gt % N_A, f = gt % N_KF;
+                if (!nwait(&rfull[s], (gt / T_STAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *stage = smem + TO_RING + s * N_STAGE_BYTES;
+                const int sofs = static_cast<int>((reinterpret_cast<uintptr_t>(g.scales + tb) & 15u) >> 2);
+                // this thread's two keys: lanes base + lane / 4 and base + 8 + lane / 4 of the warp's 16
+                const int kb = 32 * quad + 16 * half + (lane >> 2);
+                uint4 cw[2][4];
+                float scl[2], nrm[2];
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const int key = kb + 8 * jj;
+                    const bool in = key < nk;
+                    const uint4 *src = reinterpret_cast<const uint4 *>(stage + 64 * key);
+#pragma unroll
+                    for (int w = 0; w < 4; w++) cw[jj][w] = in ? src[w] : make_uint4(0u, 0u, 0u, 0u);
+                    scl[jj] = in ? reinterpret_cast<const float *>(stage + N_CODE_BYTES)[sofs + key] : 0.0f;
+                    nrm[jj] = 0.0f;
+                    if (MODE == MODE_L2) {  // |k|^2 / 2 = s^2 (64 + 2 c3) / 2, c3 = codes 0 or 3
+                        int c3 = 0;
+#pragma unroll
+                        for (int w = 0; w < 4; w++) {
+                            const uint32_t ws[4] = {cw[jj][w].x, cw[jj][w].y, cw[jj][w].z, cw[jj][w].w};
+#pragma unroll
+                            for (int t = 0; t < 4; t++) c3 += __popc(~(ws[t] ^ (ws[t] >> 1)) & 0x55555555u);
+                        }
+                        nrm[jj] = scl[jj] * scl[jj] * static_cast<float>(32 + c3);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&rempty[s]);
+                // A buffer b is free once the MMAs of tile gt - 2 are done; they waited for
+                // the epilogue to release step 2 (gt - 2) - 1, so it is done with tile gt - 3,
+                // and slot f last held tile gt - 8
+                if (gt >= N_A &&
+                    !nwait(&aempty[b], ((gt / N_A) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                    ok = false;
+                    break;
+                }
+                if (m == 0) {
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        kf[f * NK + kb + 8 * jj] = scl[jj];
+                        kn[f * NK + kb + 8 * jj] = nrm[jj];
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&kfr[f]);
+                // column c of a key's A row holds dims 2c, 2c + 1; in half h of the row,
+                // repetition j of the 16x256b store gives this thread columns 64h + 8j + 2m +
+                // {0, 1} = byte 32h + 4j + m of the key's codes, its low and high nibble
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint32_t v[32];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+#pragma unroll
+                        for (int jj = 0; jj < 2; jj++) {
+                            const uint4 q4 = cw[jj][2 * h + (j >> 2)];
+                            const uint32_t wsel = (j & 3) == 0 ? q4.x : (j & 3) == 1 ? q4.y : (j & 3) == 2 ? q4.z : q4.w;
+                            const uint32_t x = wsel >> (8 * m);
+                            v[4 * j + 2 * jj] = tm_pair(x);
+                            v[4 * j + 2 * jj + 1] = tm_pair(x >> 4);
+                        }
+                    }
+                    const uint32_t taddr =
+                        tmem + (static_cast<uint32_t>(32 * quad + 16 * half) << 16) + b * 128u + 64u * h;
+                    tmem_st_16x256b_x8(taddr, v);
+                }
+                st::tmem_st_wait();
+                st::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&afull[b]);
+            }
+        }
+    } else if (warp == N_MMA_WARP) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, 128, 128);  // f32 <- f16 x f16
+            const uint32_t qbuf = st::smem_u32(smem + TO_Q);
+            uint32_t gt = 0, gs = 0, uj = 0;
+            bool ok = true;
+            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+                if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+                st::tc_fence_after();
+                int64_t tb;
+                int nk;
+                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                    const uint32_t b = gt % N_A;
+                    if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    st::tc_fence_after();
+                    const uint32_t abuf = tmem + b * 128u;
+#pragma unroll 1
+                    for (int step = 0; step < 2; step++, gs++) {
+                        const uint32_t a = gs % T_NACC;
+                        if (gs >= T_NACC &&
+                            !nwait(&acce[a], ((gs / T_NACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        st::tc_fence_after();
+                        const uint32_t acc = tmem + ACC_COL + a * 128u;
+                        const uint32_t qs = qbuf + step * 65536;
+#pragma unroll
+                        for (int kk = 0; kk < 16; kk++)
+                            st::umma_f16_ts(acc, abuf + 8 * kk,
+                                            st::sdesc_sw128(qs + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), idesc,
+                                            kk > 0 ? 1u : 0u);
+                        st::umma_commit(&accf[a]);
+                    }
+                    if (!ok) break;
+                    st::umma_commit(&aempty[b]);
+                }
+                st::umma_commit(qfree);
+            }
+            st::umma_commit(fin);
+            nwait(fin, 0, abort_flag, g.status, st::DEV_TIMEOUT_ACC);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // Warp w: TMEM lanes 32 (w % 4) .. (keys), accumulator columns 64 (w / 4) .. + 63
+        // (queries 128 step + 64 (w / 4) + c of the unit).  Lane l owns the candidate
+        // buffer, count and thresholds of the unit's queries 128 (s / 2) + 64 (w / 4) +
+        // 32 (s % 2) + l for its four slots s.
+        const int quad = warp & 3, hq = warp >> 2;
+        const unsigned lt = (1u << lane) - 1u;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
+        uint64_t *bufs = g.cbuf + static_cast<int64_t>(blockIdx.x * N_QUAD + quad) * TQ * KCAP;
+        float *wthr = thr_s + quad * TQ, *wthf = thr_f + quad * TQ;
+        const uint32_t acc0 = tmem + lane_addr + ACC_COL;
+        uint32_t gt = 0, gs = 0, uj = 0;
+        bool ok = true;
+        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
+            const float *qc = qconst0 + (uj & 1u) * 4 * TQ;
+            const float *qc_e = qc, *qc_p = qc + TQ, *qc_live = qc + 2 * TQ;
+            const int qbase = (unit % g.nqb) * TQ;
+            int cnt[4];
+            float thr[4], eff[4];
+#pragma unroll
+            for (int sl = 0; sl < 4; sl++) {
+                const int qu = 128 * (sl >> 1) + 64 * hq + 32 * (sl & 1) + lane;
+                const bool live = qc_live[qu] > 0.0f;
+                cnt[sl] = 0;
+                thr[sl] = live ? -INFINITY : INFINITY;
+                eff[sl] = live ? thr_of(__ldcg(g.gthr + qbase + qu)) : INFINITY;
+                wthr[qu] = eff[sl];
+                wthf[qu] = live ? lowered(eff[sl]) : INFINITY;  // lowered(+inf) would be NaN
+            }
+            __syncwarp();
+            int64_t tb;
+            int nk;
+            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                const uint32_t f = gt % N_KF;
+                if (!nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+                    ok = false;
+                    break;
+                }
+                const int kk = 32 * quad + lane;
+                const float scale = kf[f * NK + kk];
+                const float knh = kn[f * NK + kk];
+                const bool klive = kk < nk;
+                const float inv_s = rcp_approx(scale);
+                const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
+#pragma unroll
+                for (int step = 0; step < 2; step++, gs++) {
+                    const uint32_t a = gs % T_NACC;
+                    if (!nwait(&accf[a], (gs / T_NACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
+                        ok = false;
+                        break;
+                    }
+                    st::tc_fence_after();
+                    const uint32_t acc = acc0 + a * 128u + 64u * hq;
+                    uint32_t pass[4];  // per 16-query chunk, bit i: the pair passed the bound
+                    bool any = false;
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t r[16];
+                        st::tmem_ld16(acc + 16 * c, r);
+                        st::tmem_ld_wait();
+                        const int q0 = 128 * step + 64 * hq + 16 * c;
+                        uint32_t pm = 0;
+#pragma unroll
+                        for (int i4 = 0; i4 < 16; i4 += 4) {
+                            const float4 tf = *reinterpret_cast<const float4 *>(wthf + q0 + i4);
+                            const float4 ev = *reinterpret_cast<const float4 *>(qc_e + q0 + i4);
+                            const float ta[4] = {tf.x, tf.y, tf.z, tf.w}, ea[4] = {ev.x, ev.y, ev.z, ev.w};
+                            float pa[4] = {0.f, 0.f, 0.f, 0.f};
+                            if (MODE == MODE_L2) {
+                                const float4 p4 = *reinterpret_cast<const float4 *>(qc_p + q0 + i4);
+                                pa[0] = p4.x; pa[1] = p4.y; pa[2] = p4.z; pa[3] = p4.w;
+                            }
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const float t = MODE == MODE_L2 ? fmaf(knh, pa[i], ta[i]) : ta[i];
+                                pm |= (__uint_as_float(r[i4 + i]) >= fmaf(t, inv_s, -ea[i]) ? 1u : 0u) << (i4 + i);
+                            }
+                        }
+                        pass[c] = klive ? pm : 0u;
+                        any |= pass[c] != 0u;
+                    }
+                    // every column is read: the accumulator goes back to the MMA
+                    st::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) st::mbar_arrive(&acce[a]);
+                    if (__any_sync(0xffffffffu, any)) {
+                        // exact scores of the kept pairs, then the inserts, chunk by chunk
+                        const uint8_t *kcodes = g.codes + (tb + kk) * 64;
+                        int c3 = 0;
+                        if (MODE == MODE_L2 && any) {
+                            const uint4 *kc4 = reinterpret_cast<const uint4 *>(kcodes);
+#pragma unroll 1
+                            for (int w = 0; w < 4; w++) {
+                                const uint4 cq = __ldg(kc4 + w);
+                                const uint32_t ws[4] = {cq.x, cq.y, cq.z, cq.w};
+                                for (int t = 0; t < 4; t++) c3 += __popc(~(ws[t] ^ (ws[t] >> 1)) & 0x55555555u);
+                            }
+                        }
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const int q0 = 128 * step + 64 * hq + 16 * c;
+                            float sc[16];
+                            uint32_t ins = 0;
+                            uint32_t pm = pass[c];
+                            while (pm) {
+                                const int i = __ffs(pm) - 1;
+                                pm &= pm - 1;
+                                const int qu = q0 + i;
+                                const float e = tm_exact<MODE>(kcodes, scale, g.q + static_cast<int64_t>(qbase + qu) * 256,
+                                                               qc_p[qu], c3);
+                                sc[i] = e;
+                                ins |= (e >= wthr[qu] ? 1u : 0u) << i;
+                            }
+                            unsigned qm = __reduce_or_sync(0xffffffffu, ins);
+                            const int sl = 2 * step + (c >> 1);  // the owners' slot
+                            while (qm) {
+                                const int i = __ffs(qm) - 1;
+                                qm &= qm - 1;
+                                const bool p = (ins >> i) & 1u;
+                                const unsigned mb = __ballot_sync(0xffffffffu, p);
+                                const int owner = 16 * (c & 1) + i;
+                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
+                                if (p)
+                                    bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(mb & lt)] =
+                                        make_key(sc[i], idx);
+                                if (lane == owner) cnt[sl] += __popc(mb);
+                            }
+                        }
+                    }
+                    // compaction when a list fills up; thresholds: own 128th best, published
+#pragma unroll
+                    for (int sh = 0; sh < 2; sh++) {
+                        const int sl = 2 * step + sh;
+                        const int qu = 128 * step + 64 * hq + 32 * sh + lane;
+                        uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
+                        const unsigned need = __ballot_sync(0xffffffffu, cnt[sl] > KCAP - NK);
+                        if (need) {
+                            const float before = thr[sl];
+                            warp_compact(need, my_buf, cnt[sl], thr[sl], nullptr, false);
+                            if (thr[sl] > before) atomicMax(g.gthr + qbase + qu, ord_f32(thr[sl]));
+                        }
+                        float ne = fmaxf(thr[sl], eff[sl]);
+                        if ((i & 15) == 15 && qc_live[qu] > 0.0f) ne = fmaxf(ne, thr_of(__ldcg(g.gthr + qbase + qu)));
+                        if (__any_sync(0xffffffffu, ne > eff[sl])) {
+                            if (ne > eff[sl]) {
+                                eff[sl] = ne;
+                                wthr[qu] = ne;
+                                wthf[qu] = lowered(ne);
+                            }
+                            __syncwarp();
+                        }
+                    }
+                }
+                if (!ok) break;
+            }
+            if (!ok) break;
+            const int split = unit / g.nqb;
+#pragma unroll
+            for (int sl = 0; sl < 4; sl++) {
+                const int qu = 128 * (sl >> 1) + 64 * hq + 32 * (sl & 1) + lane;
+                uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
+                uint64_t *my_out =
+                    g.unit_out + ((static_cast<int64_t>(split) * N_QUAD + quad) * g.nq_pad + qbase + qu) * KTOP;
+                const unsigned need = __ballot_sync(0xffffffffu, qc_live[qu] > 0.0f);
+                warp_compact(need, my_buf, cnt[sl], thr[sl], my_out, true);
+            }
+            __syncwarp();
+            if (lane == 0) st::mbar_arrive(&edone[uj & 1u]);
+        }
+    }
+
+    st::tc_fence_before();
+    __syncthreads();
+    if (warp == N_MMA_WARP) {
+        st::tc_fence_after();
+        st::tmem_dealloc(tmem, N_TMEM_COLS);
+    }
+}
+
+template <int MODE>
+st_status launch_tmem(st_handle *h, const NarrowArgs &g, int grid) {
+    auto kern = k_knn_tmem<MODE>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TMEM_SMEM));
+        attr_done = true;
+    }
+    kern<<<grid, N_THREADS, TMEM_SMEM, h->stream>>>(g);
+    return st_after_launch(h, "k_knn_tmem");
+}
+
 }  // namespace
 
 static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
@@ -1750,6 +2307,78 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (s != ST_OK) return s;
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
+    if (!ranges && dim == 256 && nq > NQ && prec == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
+        // more than 32 EXACT queries at dim 256: keys in TMEM (k_knn_tmem), units of
+        // (key split, 256 queries), about eight units per SM
+        const int nqb = static_cast<int>((nq + TQ - 1) / TQ);
+        const int64_t nq_pad = static_cast<int64_t>(nqb) * TQ;
+        const int64_t tiles = (n_keys + NK - 1) / NK;
+        int64_t splits = std::max<int64_t>(1, (8LL * h->num_sms + nqb - 1) / nqb);
+        splits = std::min<int64_t>(splits, tiles);
+        const int64_t tps = (tiles + splits - 1) / splits;
+        splits = (tiles + tps - 1) / tps;
+        const int64_t units = splits * nqb;
+        if (units > (1LL << 30)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
+        const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
+        uint64_t *cbuf = static_cast<uint64_t *>(
+            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_QUAD * TQ * KCAP));
+        const size_t out_bytes = sizeof(uint64_t) * splits * N_QUAD * nq_pad * KTOP;
+        const size_t seed_bytes = sizeof(uint64_t) * nq_pad * KTOP;
+        constexpr int MERGE_GROUPS = 16;
+        const size_t tmp_bytes = sizeof(uint64_t) * MERGE_GROUPS * nq_pad * KTOP;
+        uint8_t *part = static_cast<uint8_t *>(
+            st_scratch(h, SLOT_KNN_PART, out_bytes + seed_bytes + tmp_bytes + sizeof(uint32_t) * nq_pad + 256));
+        if (!cbuf || !part) return ST_NO_MEMORY;
+        uint64_t *unit_out = reinterpret_cast<uint64_t *>(part);
+        uint64_t *seed_keys = reinterpret_cast<uint64_t *>(part + out_bytes);
+        uint64_t *merge_tmp = reinterpret_cast<uint64_t *>(part + out_bytes + seed_bytes);
+        uint32_t *gthr = reinterpret_cast<uint32_t *>(part + out_bytes + seed_bytes + tmp_bytes);
+        ST_CHECK_CUDA(h, cudaMemsetAsync(gthr, 0, nq_pad * sizeof(uint32_t), h->stream));
+        NarrowArgs g{};
+        g.codes = codes;
+        g.scales = scales;
+        g.q = queries;
+        g.n_keys = n_keys;
+        g.nq = static_cast<int>(nq);
+        g.nqb = nqb;
+        g.nq_pad = static_cast<int>(nq_pad);
+        g.n_tiles = tiles;
+        g.index_base = static_cast<uint32_t>(index_base);
+        g.cbuf = cbuf;
+        g.unit_out = unit_out;
+        g.gthr = gthr;
+        g.status = h->d_status;
+        auto run = [&](const NarrowArgs &a, int gr) {
+            return mode == 0 ? launch_tmem<MODE_DOT>(h, a, gr) : launch_tmem<MODE_L2>(h, a, gr);
+        };
+        // the narrow scan's two sample passes seed the thresholds (every 1024th, then
+        // every 16th tile), with the full pass's key splits
+        for (int64_t stride : {int64_t(1024), int64_t(16)}) {
+            const int64_t sample = (tiles + stride - 1) / stride;
+            if (sample < 2 * h->num_sms) continue;
+            NarrowArgs gs = g;
+            const int64_t gsplits = std::min<int64_t>(splits, sample);
+            gs.units = static_cast<int>(gsplits * nqb);
+            gs.unit_step = stride;
+            gs.tile_step = stride * gsplits;
+            gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
+            s = run(gs, static_cast<int>(std::min<int64_t>(gs.units, h->num_sms)));
+            if (s != ST_OK) return s;
+            s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
+            if (s != ST_OK) return s;
+            k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
+                                                                                       static_cast<int>(nq), gthr);
+            s = st_after_launch(h, "k_knn_seed");
+            if (s != ST_OK) return s;
+        }
+        g.units = static_cast<int>(units);
+        g.unit_step = tps;
+        g.tile_step = 1;
+        g.tiles_per_unit = tps;
+        s = run(g, grid);
+        if (s != ST_OK) return s;
+        return merge_lists(h, unit_out, splits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
+    }
     if (!ranges && dim == 256 && nq <= NQ && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
         // dim 256, up to 32 queries: the keys-on-M scan (keys as the kind::i8 A
         // operand in TMEM), one group of 32 queries per unit.  More queries run
