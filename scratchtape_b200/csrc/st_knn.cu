@@ -1102,6 +1102,7 @@ struct NarrowArgs {
     uint64_t *cbuf;        // [gridDim.x][4 quadrants][QB queries][KCAP]
     uint64_t *unit_out;    // [splits * 4][nq_pad][KTOP]: list (split, quadrant) of every query
     uint32_t *gthr;        // [nq_pad] order-preserving bits of the best published 128th score (0: none)
+    int exact;             // k_knn_tmem: 1 = exact scores (the full pass), 0 = lower bounds (a sample pass)
     int *status;
 };
 
@@ -1807,35 +1808,30 @@ __device__ __forceinline__ uint32_t tm_pair(uint32_t x) {
     return r;
 }
 
-// The exact stored score of (key with codes `codes` and scale s, query row
-// qrow with p2e = 2^e): DOT s sum (u - 1.5) q 2^e; L2 (2 q.k - |k|^2) 2^(e-1)
-// with |k|^2 = s^2 (64 + 2 c3) (c3: codes 0 or 3), in f64, rounded once.
+// The exact stored score of one (key, query) pair, computed by the whole warp
+// (every lane calls it with the same arguments): key codes `codes` (64 bytes)
+// and scale s, query row qrow (f32) with p2e = 2^e.  Lane l takes dims 8l ..
+// 8l + 7 (its two code bytes, two float4 of the query), products and sums in
+// f64, rounded once: DOT s sum (u - 1.5) q 2^e; L2 (2 q.k - |k|^2) 2^(e-1)
+// with |k|^2 = s^2 (64 + 2 c3) (c3: codes 0 or 3).
 template <int MODE>
-__device__ __noinline__ float tm_exact(const uint8_t *codes, float s, const float *qrow, float p2e, int c3) {
+__device__ __forceinline__ float tm_exact_warp(const uint8_t *codes, float s, const float *qrow, float p2e) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t cb = __ldg(reinterpret_cast<const uint16_t *>(codes) + lane);
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane);
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane + 1);
+    const float q[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     double acc = 0.0;
-    const uint4 *kc = reinterpret_cast<const uint4 *>(codes);
-#pragma unroll 1
-    for (int w = 0; w < 4; w++) {
-        const uint4 c = __ldg(kc + w);
-        const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 *q4 = reinterpret_cast<const float4 *>(qrow + 64 * w + 16 * i);
+    for (int i = 0; i < 8; i++) acc += (static_cast<double>((cb >> (2 * i)) & 3u) - 1.5) * static_cast<double>(q[i]);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float4 q = __ldg(q4 + j);
-                const uint32_t byte = (cw[i] >> (8 * j)) & 0xffu;
-                acc += (static_cast<double>(byte & 3u) - 1.5) * q.x;
-                acc += (static_cast<double>((byte >> 2) & 3u) - 1.5) * q.y;
-                acc += (static_cast<double>((byte >> 4) & 3u) - 1.5) * q.z;
-                acc += (static_cast<double>(byte >> 6) - 1.5) * q.w;
-            }
-        }
-    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     const double dot = acc * static_cast<double>(s) * static_cast<double>(p2e);  // q.k 2^e
     if (MODE == MODE_DOT) return static_cast<float>(dot);
-    const double kn = static_cast<double>(s) * s * (64.0 + 2.0 * c3);         // |k|^2
-    return static_cast<float>(dot - kn * 0.5 * static_cast<double>(p2e));      // (2 q.k - |k|^2) 2^(e-1)
+    int c3 = __popc(~(cb ^ (cb >> 1)) & 0x5555u);
+    c3 = warp_sum(c3);
+    const double kn = static_cast<double>(s) * s * (64.0 + 2.0 * c3);  // |k|^2
+    return static_cast<float>(dot - kn * 0.5 * static_cast<double>(p2e));  // (2 q.k - |k|^2) 2^(e-1)
 }
 
 template <int MODE>
@@ -2160,7 +2156,10 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     st::tc_fence_after();
                     const uint32_t acc = acc0 + a * 128u + 64u * hq;
                     uint32_t pass[4];  // per 16-query chunk, bit i: the pair passed the bound
-                    bool any = false;
+                    // full pass: keep a pair if its exact score can reach the threshold,
+                    // acc >= t / s - E_q; sample pass: keep it if its lower bound
+                    // (acc - E_q) s does, acc >= t / s + E_q, and insert that bound
+                    const float esign = g.exact ? -1.0f : 1.0f;
 #pragma unroll
                     for (int c = 0; c < 4; c++) {
                         uint32_t r[16];
@@ -2181,57 +2180,70 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 #pragma unroll
                             for (int i = 0; i < 4; i++) {
                                 const float t = MODE == MODE_L2 ? fmaf(knh, pa[i], ta[i]) : ta[i];
-                                pm |= (__uint_as_float(r[i4 + i]) >= fmaf(t, inv_s, -ea[i]) ? 1u : 0u) << (i4 + i);
+                                pm |= (__uint_as_float(r[i4 + i]) >= fmaf(t, inv_s, esign * ea[i]) ? 1u : 0u)
+                                      << (i4 + i);
                             }
                         }
-                        pass[c] = klive ? pm : 0u;
-                        any |= pass[c] != 0u;
+                        pm = klive ? pm : 0u;
+                        pass[c] = pm;
+                        if (!g.exact) {
+                            // sample pass: insert the lower bound (acc - E_q) s [- |k|^2 2^(e-1)],
+                            // lowered by 2^-12 for its own rounding: every entry is at most its
+                            // key's exact score, so a list's 128th best bounds the final one
+                            unsigned qm = __reduce_or_sync(0xffffffffu, pm);
+                            const int sl = 2 * step + (c >> 1);
+                            while (qm) {
+                                const int i = __ffs(qm) - 1;
+                                qm &= qm - 1;
+                                const bool p = (pm >> i) & 1u;
+                                const unsigned mb = __ballot_sync(0xffffffffu, p);
+                                const int owner = 16 * (c & 1) + i;
+                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
+                                if (p) {
+                                    float lb = (__uint_as_float(r[i]) - qc_e[q0 + i]) * scale;
+                                    if (MODE == MODE_L2) lb = fmaf(-knh, qc_p[q0 + i], lb);
+                                    bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(mb & lt)] =
+                                        make_key(lowered(lb), idx);
+                                }
+                                if (lane == owner) cnt[sl] += __popc(mb);
+                            }
+                        }
                     }
                     // every column is read: the accumulator goes back to the MMA
                     st::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) st::mbar_arrive(&acce[a]);
-                    if (__any_sync(0xffffffffu, any)) {
-                        // exact scores of the kept pairs, then the inserts, chunk by chunk
-                        const uint8_t *kcodes = g.codes + (tb + kk) * 64;
-                        int c3 = 0;
-                        if (MODE == MODE_L2 && any) {
-                            const uint4 *kc4 = reinterpret_cast<const uint4 *>(kcodes);
-#pragma unroll 1
-                            for (int w = 0; w < 4; w++) {
-                                const uint4 cq = __ldg(kc4 + w);
-                                const uint32_t ws[4] = {cq.x, cq.y, cq.z, cq.w};
-                                for (int t = 0; t < 4; t++) c3 += __popc(~(ws[t] ^ (ws[t] >> 1)) & 0x55555555u);
-                            }
-                        }
+                    if (g.exact) {
+                        // full pass: each kept pair's exact score, by the whole warp; insert if
+                        // it reaches the list's threshold
 #pragma unroll
                         for (int c = 0; c < 4; c++) {
                             const int q0 = 128 * step + 64 * hq + 16 * c;
-                            float sc[16];
-                            uint32_t ins = 0;
-                            uint32_t pm = pass[c];
-                            while (pm) {
-                                const int i = __ffs(pm) - 1;
-                                pm &= pm - 1;
-                                const int qu = q0 + i;
-                                const float e = tm_exact<MODE>(kcodes, scale, g.q + static_cast<int64_t>(qbase + qu) * 256,
-                                                               qc_p[qu], c3);
-                                sc[i] = e;
-                                ins |= (e >= wthr[qu] ? 1u : 0u) << i;
-                            }
-                            unsigned qm = __reduce_or_sync(0xffffffffu, ins);
-                            const int sl = 2 * step + (c >> 1);  // the owners' slot
-                            while (qm) {
-                                const int i = __ffs(qm) - 1;
-                                qm &= qm - 1;
-                                const bool p = (ins >> i) & 1u;
-                                const unsigned mb = __ballot_sync(0xffffffffu, p);
-                                const int owner = 16 * (c & 1) + i;
-                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
-                                if (p)
-                                    bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(mb & lt)] =
-                                        make_key(sc[i], idx);
-                                if (lane == owner) cnt[sl] += __popc(mb);
+                            const int sl = 2 * step + (c >> 1);
+                            unsigned lanes = __ballot_sync(0xffffffffu, pass[c] != 0u);
+                            while (lanes) {
+                                const int L = __ffs(lanes) - 1;
+                                lanes &= lanes - 1;
+                                uint32_t bits = __shfl_sync(0xffffffffu, pass[c], L);
+                                const float sL = __shfl_sync(0xffffffffu, scale, L);
+                                const int keyL = 32 * quad + L;
+                                const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
+                                const uint32_t idxL = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
+                                while (bits) {
+                                    const int i = __ffs(bits) - 1;
+                                    bits &= bits - 1;
+                                    const int qu = q0 + i;
+                                    const float e = tm_exact_warp<MODE>(kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256,
+                                                                        qc_p[qu]);
+                                    if (e >= wthr[qu]) {
+                                        const int owner = 16 * (c & 1) + i;
+                                        const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
+                                        if (lane == owner) {
+                                            bufs[static_cast<int64_t>(qu) * KCAP + base] = make_key(e, idxL);
+                                            cnt[sl] = base + 1;
+                                        }
+                                    }
+                                }
                             }
                         }
                     }
@@ -2357,6 +2369,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
             const int64_t sample = (tiles + stride - 1) / stride;
             if (sample < 2 * h->num_sms) continue;
             NarrowArgs gs = g;
+            gs.exact = 0;
             const int64_t gsplits = std::min<int64_t>(splits, sample);
             gs.units = static_cast<int>(gsplits * nqb);
             gs.unit_step = stride;
@@ -2375,6 +2388,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.unit_step = tps;
         g.tile_step = 1;
         g.tiles_per_unit = tps;
+        g.exact = 1;
         s = run(g, grid);
         if (s != ST_OK) return s;
         return merge_lists(h, unit_out, splits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
