@@ -118,8 +118,11 @@ __device__ __forceinline__ float unord_f32(uint32_t o) {
 }
 // A published threshold's bits back to a score (0: none published).
 __device__ __forceinline__ float thr_of(uint32_t v) { return v == 0u ? -INFINITY : unord_f32(v); }
+// A candidate key: score bits above (0xffffffff - index), so that equal scores
+// rank the lower index first; -0 is stored as +0 (s + 0 = +0 for s = -0), the
+// two being one score.
 __device__ __forceinline__ uint64_t make_key(float s, uint32_t idx) {
-    return (static_cast<uint64_t>(ord_f32(s)) << 32) | static_cast<uint64_t>(0xffffffffu - idx);
+    return (static_cast<uint64_t>(ord_f32(s + 0.0f)) << 32) | static_cast<uint64_t>(0xffffffffu - idx);
 }
 
 // Power-of-two exponent e with max|q| * 2^e in [2^14, 2^15) (0 for an all-zero
@@ -1744,77 +1747,101 @@ st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
 
 // ---- the wide scan with keys in tensor memory (k_knn_tmem) -----------------
 //
-// For more than 32 EXACT queries at dim 256.  A unit is (key split, block of
-// TQ = 256 queries).  The block's queries stay in shared memory for the whole
-// unit as f16, each prescaled by its power of two 2^e (max |q| 2^e in [2^14,
-// 2^15), so hi = f16(q 2^e) neither overflows nor flushes).  Each 128-key tile
-// is expanded once -- code u to the f16 value u - 1.5, exact -- straight into
-// TMEM, where it is the A operand (M = 128 keys) of one tcgen05 kind::f16 pass
-// per 128-query step (N = 128, K = 256 in 16 MMAs): every expanded key meets
-// all 256 queries, and shared memory carries only the queries' B tiles (no
-// expanded keys, no second pass).
+// For more than 32 EXACT dot-product queries at dim 256.  A unit is (key
+// split, block of TQ = 256 queries).  The block's queries stay in shared
+// memory for the whole unit as hi = f16(q 2^e), 2^e chosen per query (max |q|
+// 2^e in [2^14, 2^15), so hi neither overflows nor flushes).  Each 128-key
+// tile is expanded once into TMEM -- code u of a key with scale s to the f16
+// value v = f16((u - 1.5) s) -- where it is the A operand (M = 128 keys) of
+// one tcgen05 kind::f16 pass per 128-query step (N = 128, K = 256 in 16
+// MMAs): every expanded key meets all 256 queries, and shared memory carries
+// only the queries' B tiles.
 //
-// The product hi . (u - 1.5) is exact; it differs from the exact q 2^e .
-// (u - 1.5) by at most E_q = 1.5 sum |q_i 2^e - hi_i| plus the tensor core's
-// f32 accumulation error, bounded generously by 2^-12 1.5 sum |hi_i|.  The
-// epilogue (lane = key, columns = queries) keeps a (key, query) pair only if
-// acc >= (T_q + kn_k) / s_k - E_q, where T_q is the query's running 128th-best
-// score in dot units (lowered by 2^-18 to cover the reciprocal's rounding) and
-// kn_k = |k|^2 / 2 in L2 mode: no key whose exact score reaches the threshold
-// is dropped.  A kept pair's exact score -- s_k sum (u_i - 1.5) q_i 2^e in f64
-// from the key's codes and the f32 query, rounded once -- decides its entry in
-// the candidate buffer of (query, TMEM lane quadrant), as in k_knn_narrow;
-// lists, thresholds published through gthr, sample-pass seeding and the merge
-// are the narrow scan's.  Scores come out in the wide scan's units (DOT:
-// q.k 2^e; L2: (2 q.k - |k|^2) 2^(e-1)), so k_knn_merge and k_knn_decode are
-// shared.
+// A 17th MMA per step (both operands in shared memory, K = 16) adds each
+// pair's filter terms: the key's filter row holds (1024, s16), the query's
+// (w, +-E16), so the accumulator ends at acc' = sum hi v + 1024 w +- s16 E16.
+//   s16 = |s| rounded up to f16.
+//   E16 = E rounded up, E = (1.5 sum |q 2^e - hi| + 2^-9 sum |hi|) (1 + 2^-10)
+//         + 2^-24: the query's rounding, the rounding of v (2^-11 relative) and
+//         an f32 accumulation error of up to 2^-12 of the terms' magnitudes.
+//   w   = -T' / 1024 rounded up to f16, T' = T - 2^-10 |T| - 2^-22 sum |hi|
+//         - 2^-30 for the query's running 128th-best score T.
+// A pair whose exact score s sum (u - 1.5) q 2^e reaches T then has acc' >=
+// 0, so the full pass keeps only pairs whose accumulator is not negative -- a
+// test of sign bits, by AND over 16 columns at a time.  Thresholds rise
+// during the scan: the epilogue rewrites w in shared memory, and an MMA that
+// still reads an older (smaller) threshold only keeps more pairs.  A key with
+// |s| < 2^-13 is expanded as zeros with s16 = |s| 1024 rounded up (v would
+// leave the normal f16 range; the bound then covers the whole dropped
+// product); a key with |s| >= 2^14 or a non-finite scale as zeros with s16 =
+// +inf, so that all its pairs are kept.
 //
-// Roles (576 threads, one CTA per SM): warp 17 bulk-copies each tile's codes
-// and scales into an 8-stage ring; warps 8-15 expand codes into TMEM (a warp
-// per 16 lanes, 16x256b stores; u - 1.5 as f16 through a byte permute of a
-// four-entry table) and publish per-key scale and |k|^2 / 2; warp 16 issues
-// the MMAs (two A buffers, two 128-column accumulators); warps 0-7 filter
-// (warp w: lane quadrant w % 4, queries 64 (w / 4) .. of each step).
+// A kept pair's exact score -- s sum (u_i - 1.5) q_i 2^e in f64 from the
+// key's codes and the f32 query, rounded once, computed by the whole warp --
+// decides its entry in the candidate buffer of (query, TMEM lane quadrant),
+// as in k_knn_narrow.  The sample passes (every 1024th, then every 16th tile)
+// stage w = 0 and -E16 instead: acc' is then a lower bound of the pair's
+// exact score, and a pair whose acc' reaches its list's threshold enters the
+// list as that bound lowered by 2^-12, so a list's 128th best bounds the
+// final one from below and seeds the full pass.  Scores come out in the wide
+// scan's units (q.k 2^e), so k_knn_merge and k_knn_decode are shared.
+//
+// Roles (448 threads, one CTA per SM, up to 128 registers a thread): warp 13
+// bulk-copies each tile's codes and scales into a 7-stage ring; warps 4-11
+// expand codes into TMEM (a warp per 16 lanes, 16x256b stores, v through a
+// byte permute of the key's four-entry table) and write the keys' filter
+// rows; warp 12 issues the MMAs (two A buffers, two 128-column accumulators);
+// warps 0-3 filter (warp w: lane quadrant w, all 128 columns of each step).
 constexpr int TQ = 256;                       // queries per unit: two 128-query steps
-constexpr int T_STAGES = 8;
+constexpr int T_EPI = 4;                      // filter warps: one per TMEM lane quadrant
+constexpr int T_MMA_WARP = T_EPI + N_PROD;    // 12
+constexpr int T_TMA_WARP = T_MMA_WARP + 1;    // 13
+constexpr int T_THREADS = 32 * (T_TMA_WARP + 1);
+constexpr int T_STAGES = 7;
 constexpr int T_NACC = 2;
 constexpr int TO_Q = 0;                       // [2 steps][4 K chunks][128 rows x 128 B] f16, SW128
-constexpr int TO_RING = TO_Q + 2 * 4 * 16384;
+constexpr int TO_X = TO_Q + 2 * 4 * 16384;    // filter rows [128 x 128 B] SW128, K slice j (dims 16 j ..):
+                                              //   j = 0, 1 keys of A buffer j; j = 2, 3 queries of step j - 2
+constexpr int TO_RING = TO_X + 16384;
 constexpr int TO_KF = TO_RING + T_STAGES * N_STAGE_BYTES;   // [N_KF][128] scale
-constexpr int TO_KN = TO_KF + N_KF * NK * 4;                // [N_KF][128] |k|^2 / 2 (L2)
-constexpr int TO_QC = TO_KN + N_KF * NK * 4;                // [2 units][4][TQ]: E_q, 2^-e, 2^e, live
-constexpr int TO_THR = TO_QC + 2 * 4 * TQ * 4;              // [4 quadrants][TQ] thresholds: stored units
-constexpr int TO_THF = TO_THR + N_QUAD * TQ * 4;            // [4 quadrants][TQ] the same in dot units, lowered
-constexpr int TO_BAR = TO_THF + N_QUAD * TQ * 4;
+constexpr int TO_QC = TO_KF + N_KF * NK * 4;                // [2 units][4][TQ]: E, 2^e, live, sum |hi|
+constexpr int TO_THR = TO_QC + 2 * 4 * TQ * 4;              // [4 quadrants][TQ] thresholds (stored units)
+constexpr int TO_BAR = TO_THR + N_QUAD * TQ * 4;
 constexpr int T_NBARS = 2 * T_STAGES + 2 * N_A + 2 * T_NACC + N_KF + 2 + 2 + 1 + 1;
 constexpr int TO_MISC = TO_BAR + T_NBARS * 8;
 constexpr int TMEM_SMEM = TO_MISC + 16 + 1024;
 static_assert(TMEM_SMEM <= 232448, "keys-in-TMEM kNN scan shared memory exceeds the sm_100 limit");
 static_assert(N_A * 128 + T_NACC * 128 <= 512, "keys-in-TMEM kNN scan TMEM budget");
+static_assert(TO_X % 1024 == 0 && TO_RING % 16 == 0 && N_STAGE_BYTES % 16 == 0, "keys-in-TMEM kNN scan alignment");
+constexpr float TM_SMALL = 1.220703125e-4f;   // 2^-13: smaller |s| expand as zeros (bound widened)
+constexpr float TM_BIG = 16384.0f;            // 2^14: larger |s| expand as zeros (every pair kept)
+constexpr uint32_t TM_H1024 = 0x6400u;        // f16 bit patterns: 1024, -inf, +inf
+constexpr uint32_t TM_HNINF = 0xFC00u, TM_HPINF = 0x7C00u;
 
-// f16 bit patterns of u - 1.5 for u = 0..3, as the byte table of a permute:
-// bytes 2u, 2u + 1 of {T1:T0} hold the value for code u.
-constexpr uint32_t TM_T0 = 0xB800BE00u;  // -0.5 (u = 1) | -1.5 (u = 0)
-constexpr uint32_t TM_T1 = 0x3E003800u;  //  1.5 (u = 3) |  0.5 (u = 2)
-
-// Two f16 (u - 1.5) for the two codes in bits 0-3 of x (code a = bits 0-1,
-// the lower half of the result; b = bits 2-3, the upper half).
-__device__ __forceinline__ uint32_t tm_pair(uint32_t x) {
+// Two f16 values of the key's table {t1:t0} (bytes 2u, 2u + 1: the value for
+// code u) for the two codes in bits 0-3 of x (code a = bits 0-1 to the lower
+// half of the result, b = bits 2-3 to the upper half).
+__device__ __forceinline__ uint32_t tm_pair(uint32_t x, uint32_t t0, uint32_t t1) {
     // selector nibbles (2a, 2a+1, 2b, 2b+1) = (a + 256 b) * 34 + 0x1010
     const uint32_t ab = (x & 3u) | ((x << 6) & 0x300u);
     const uint32_t sel = ab * 34u + 0x1010u;
     uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(TM_T0), "r"(TM_T1), "r"(sel));
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(t0), "r"(t1), "r"(sel));
     return r;
+}
+
+// The filter threshold w of a query (f16 bits): -T' / 1024 rounded up, T' =
+// t - 2^-10 |t| - 2^-22 mag - 2^-30 (t = -inf: +inf, every pair kept).
+__device__ __forceinline__ uint32_t tm_w_bits(float t, float mag) {
+    const float tl = t - fabsf(t) * 0.0009765625f - mag * 2.384185791015625e-7f - 9.313225746154785e-10f;
+    return __half_as_ushort(__float2half_ru(-tl * 0.0009765625f));
 }
 
 // The exact stored score of one (key, query) pair, computed by the whole warp
 // (every lane calls it with the same arguments): key codes `codes` (64 bytes)
 // and scale s, query row qrow (f32) with p2e = 2^e.  Lane l takes dims 8l ..
-// 8l + 7 (its two code bytes, two float4 of the query), products and sums in
-// f64, rounded once: DOT s sum (u - 1.5) q 2^e; L2 (2 q.k - |k|^2) 2^(e-1)
-// with |k|^2 = s^2 (64 + 2 c3) (c3: codes 0 or 3).
-template <int MODE>
+// 8l + 7 (its two code bytes, two float4 of the query); products and sums in
+// f64, rounded once: s sum (u - 1.5) q 2^e.
 __device__ __forceinline__ float tm_exact_warp(const uint8_t *codes, float s, const float *qrow, float p2e) {
     const int lane = threadIdx.x & 31;
     const uint32_t cb = __ldg(reinterpret_cast<const uint16_t *>(codes) + lane);
@@ -1826,32 +1853,37 @@ __device__ __forceinline__ float tm_exact_warp(const uint8_t *codes, float s, co
     for (int i = 0; i < 8; i++) acc += (static_cast<double>((cb >> (2 * i)) & 3u) - 1.5) * static_cast<double>(q[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    const double dot = acc * static_cast<double>(s) * static_cast<double>(p2e);  // q.k 2^e
-    if (MODE == MODE_DOT) return static_cast<float>(dot);
-    int c3 = __popc(~(cb ^ (cb >> 1)) & 0x5555u);
-    c3 = warp_sum(c3);
-    const double kn = static_cast<double>(s) * s * (64.0 + 2.0 * c3);  // |k|^2
-    return static_cast<float>(dot - kn * 0.5 * static_cast<double>(p2e));  // (2 q.k - |k|^2) 2^(e-1)
+    return static_cast<float>(acc * static_cast<double>(s) * static_cast<double>(p2e));
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
+// r[i] for a warp-uniform runtime i (a select chain: indexing the register
+// array at run time would move it to local memory).
+__device__ __forceinline__ uint32_t tm_pick16(const uint32_t (&r)[16], int i) {
+    uint32_t v = r[0];
+#pragma unroll
+    for (int k = 1; k < 16; k++) v = i == k ? r[k] : v;
+    return v;
+}
+
+__global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *kf = reinterpret_cast<float *>(smem + TO_KF);
-    float *kn = reinterpret_cast<float *>(smem + TO_KN);
     float *thr_s = reinterpret_cast<float *>(smem + TO_THR);  // [4][TQ] effective 128th best (stored units)
-    float *thr_f = reinterpret_cast<float *>(smem + TO_THF);  // [4][TQ] the same, lowered (the filter's)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TO_BAR);
     uint64_t *rfull = bars, *rempty = bars + T_STAGES, *afull = bars + 2 * T_STAGES, *aempty = afull + N_A;
     uint64_t *accf = aempty + N_A, *acce = accf + T_NACC, *kfr = acce + T_NACC, *qready = kfr + N_KF;
     uint64_t *edone = qready + 2, *qfree = edone + 2, *fin = qfree + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + TO_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + TO_MISC + 4);
-    // per-query constants of the CTA's unit j, buffer j % 2: E_q, 2^e, live (1 / 0)
+    // per-query constants of the CTA's unit j, buffer j % 2: E, 2^e, live (1 / 0), sum |hi|
     float *qconst0 = reinterpret_cast<float *>(smem + TO_QC);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the filter rows' unused dims stay zero
+    for (int i = threadIdx.x; i < 16384 / 16; i += T_THREADS)
+        reinterpret_cast<uint4 *>(smem + TO_X)[i] = make_uint4(0u, 0u, 0u, 0u);
+    st::fence_proxy_async_smem();
     if (threadIdx.x == 0) {
         for (int s = 0; s < T_STAGES; s++) {
             st::mbar_init(&rfull[s], 1);
@@ -1863,19 +1895,19 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         }
         for (int a = 0; a < T_NACC; a++) {
             st::mbar_init(&accf[a], 1);
-            st::mbar_init(&acce[a], N_EPI);
+            st::mbar_init(&acce[a], T_EPI);
         }
         for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
         for (int j = 0; j < 2; j++) {
             st::mbar_init(&qready[j], N_PROD);
-            st::mbar_init(&edone[j], N_EPI);
+            st::mbar_init(&edone[j], T_EPI);
         }
         st::mbar_init(qfree, 1);
         st::mbar_init(fin, 1);
         *abort_flag = 0;
         st::fence_mbar_init();
     }
-    if (warp == N_MMA_WARP) {
+    if (warp == T_MMA_WARP) {
         st::tmem_alloc(tmem_slot, N_TMEM_COLS);
         st::tmem_relinquish();
     }
@@ -1885,7 +1917,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     const uint32_t tmem = *tmem_slot;
     constexpr uint32_t ACC_COL = N_A * 128;  // accumulators after the two 128-column A buffers
 
-    if (warp == N_TMA_WARP) {
+    if (warp == T_TMA_WARP) {
         // ------------------------------------------------------------ code / scale loader
         if (lane == 0) {
             uint32_t gt = 0;
@@ -1913,16 +1945,20 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             for (uint32_t i = first; i < gt; i++)
                 st::mbar_wait(&rfull[i % T_STAGES], (i / T_STAGES) & 1u, g.status, st::DEV_TIMEOUT_FULL);
         }
-    } else if (warp >= N_EPI && warp < N_MMA_WARP) {
+    } else if (warp >= T_EPI && warp < T_MMA_WARP) {
         // ------------------------------------------------------------ producers
-        const int pw = warp - N_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
+        const int pw = warp - T_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
         const int quad = warp & 3, half = pw >> 2;
         const int m = lane & 3;       // the byte of each code word this thread expands
         uint32_t gt = 0, uj = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            // the query tiles and filter rows are rewritten once the MMAs and the
+            // epilogue (which writes thresholds into the filter rows) are done with
+            // the previous unit
             if (uj >= 1 && !nwait(qfree, (uj - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) break;
-            if (uj >= 2 && !nwait(&edone[uj & 1u], ((uj - 2) >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC))
+            if (uj >= 1 &&
+                !nwait(&edone[(uj - 1) & 1u], ((uj - 1) >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC))
                 break;
             float *qc = qconst0 + (uj & 1u) * 4 * TQ;
             const int qbase = (unit % g.nqb) * TQ;
@@ -1964,10 +2000,26 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 *reinterpret_cast<uint4 *>(smem + TO_Q + step * 65536 + (lane >> 3) * 16384 +
                                            st::sw128_offset(row, lane & 7)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                 if (lane == 0) {
-                    // the sums round up by far less than the 2^-12 slack on the accumulation
-                    qc[r] = live ? 1.5f * err + 1.5f * 0.000244140625f * mag + 1e-30f : 0.0f;
+                    // the sums round up by far less than the 2^-10 slack
+                    const float eb = live ? (1.5f * err + 0.001953125f * mag) * 1.0009765625f + 5.9604644775390625e-8f
+                                          : 0.0f;
+                    qc[r] = eb;
                     qc[TQ + r] = p2e;
                     qc[2 * TQ + r] = live ? 1.0f : 0.0f;
+                    qc[3 * TQ + r] = mag;
+                    // the query's filter row: (w, E16) in the full pass, (0, -E16) in a sample pass
+                    uint32_t wb = TM_HNINF, ebits = 0u;
+                    if (live) {
+                        ebits = __half_as_ushort(__float2half_ru(eb));
+                        if (g.exact) {
+                            wb = tm_w_bits(thr_of(__ldcg(g.gthr + qg)), mag);
+                        } else {
+                            wb = 0u;
+                            ebits ^= 0x8000u;
+                        }
+                    }
+                    *reinterpret_cast<uint4 *>(smem + TO_X + st::sw128_offset(row, 2 * (2 + step))) =
+                        make_uint4(wb | (ebits << 16), 0u, 0u, 0u);
                 }
             }
             st::fence_proxy_async_smem();
@@ -1987,7 +2039,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 // this thread's two keys: lanes base + lane / 4 and base + 8 + lane / 4 of the warp's 16
                 const int kb = 32 * quad + 16 * half + (lane >> 2);
                 uint4 cw[2][4];
-                float scl[2], nrm[2];
+                uint32_t t0[2], t1[2], xrow[2];
+                float scl[2];
 #pragma unroll
                 for (int jj = 0; jj < 2; jj++) {
                     const int key = kb + 8 * jj;
@@ -1996,23 +2049,24 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 #pragma unroll
                     for (int w = 0; w < 4; w++) cw[jj][w] = in ? src[w] : make_uint4(0u, 0u, 0u, 0u);
                     scl[jj] = in ? reinterpret_cast<const float *>(stage + N_CODE_BYTES)[sofs + key] : 0.0f;
-                    nrm[jj] = 0.0f;
-                    if (MODE == MODE_L2) {  // |k|^2 / 2 = s^2 (64 + 2 c3) / 2, c3 = codes 0 or 3
-                        int c3 = 0;
-#pragma unroll
-                        for (int w = 0; w < 4; w++) {
-                            const uint32_t ws[4] = {cw[jj][w].x, cw[jj][w].y, cw[jj][w].z, cw[jj][w].w};
-#pragma unroll
-                            for (int t = 0; t < 4; t++) c3 += __popc(~(ws[t] ^ (ws[t] >> 1)) & 0x55555555u);
-                        }
-                        nrm[jj] = scl[jj] * scl[jj] * static_cast<float>(32 + c3);
-                    }
+                    // the key's table (u - 1.5) s and filter row (1024, s16)
+                    const float ab = fabsf(scl[jj]);
+                    const bool small = ab < TM_SMALL, normal = !small && ab < TM_BIG;  // NaN: neither
+                    const float sv = normal ? scl[jj] : 0.0f;
+                    const __half2 lo = __floats2half2_rn(-1.5f * sv, -0.5f * sv);
+                    const __half2 hi = __floats2half2_rn(0.5f * sv, 1.5f * sv);
+                    t0[jj] = *reinterpret_cast<const uint32_t *>(&lo);
+                    t1[jj] = *reinterpret_cast<const uint32_t *>(&hi);
+                    const uint32_t s16 = small    ? __half_as_ushort(__float2half_ru(ab * 1024.0f))
+                                         : normal ? __half_as_ushort(__float2half_ru(ab))
+                                                  : TM_HPINF;
+                    xrow[jj] = TM_H1024 | (s16 << 16);
                 }
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&rempty[s]);
-                // A buffer b is free once the MMAs of tile gt - 2 are done; they waited for
-                // the epilogue to release step 2 (gt - 2) - 1, so it is done with tile gt - 3,
-                // and slot f last held tile gt - 8
+                // A buffer b (and its filter rows) is free once the MMAs of tile gt - 2 are
+                // done; they waited for the epilogue to release step 2 (gt - 2) - 1, so it
+                // is done with tile gt - 3, and slot f last held tile gt - 8
                 if (gt >= N_A &&
                     !nwait(&aempty[b], ((gt / N_A) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
                     ok = false;
@@ -2022,7 +2076,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 #pragma unroll
                     for (int jj = 0; jj < 2; jj++) {
                         kf[f * NK + kb + 8 * jj] = scl[jj];
-                        kn[f * NK + kb + 8 * jj] = nrm[jj];
+                        *reinterpret_cast<uint4 *>(smem + TO_X + st::sw128_offset(kb + 8 * jj, 2 * b)) =
+                            make_uint4(xrow[jj], 0u, 0u, 0u);
                     }
                 }
                 __syncwarp();
@@ -2040,8 +2095,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                             const uint4 q4 = cw[jj][2 * h + (j >> 2)];
                             const uint32_t wsel = (j & 3) == 0 ? q4.x : (j & 3) == 1 ? q4.y : (j & 3) == 2 ? q4.z : q4.w;
                             const uint32_t x = wsel >> (8 * m);
-                            v[4 * j + 2 * jj] = tm_pair(x);
-                            v[4 * j + 2 * jj + 1] = tm_pair(x >> 4);
+                            v[4 * j + 2 * jj] = tm_pair(x, t0[jj], t1[jj]);
+                            v[4 * j + 2 * jj + 1] = tm_pair(x >> 4, t0[jj], t1[jj]);
                         }
                     }
                     const uint32_t taddr =
@@ -2049,16 +2104,17 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     tmem_st_16x256b_x8(taddr, v);
                 }
                 st::tmem_st_wait();
+                st::fence_proxy_async_smem();  // the filter rows, for the MMA's shared-memory reads
                 st::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&afull[b]);
             }
         }
-    } else if (warp == N_MMA_WARP) {
+    } else if (warp == T_MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, 128, 128);  // f32 <- f16 x f16
-            const uint32_t qbuf = st::smem_u32(smem + TO_Q);
+            const uint32_t qbuf = st::smem_u32(smem + TO_Q), xbuf = st::smem_u32(smem + TO_X);
             uint32_t gt = 0, gs = 0, uj = 0;
             bool ok = true;
             for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
@@ -2090,6 +2146,9 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                             st::umma_f16_ts(acc, abuf + 8 * kk,
                                             st::sdesc_sw128(qs + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), idesc,
                                             kk > 0 ? 1u : 0u);
+                        // the filter terms: K slice b of the keys' rows x slice 2 + step of the queries'
+                        st::umma_f16(acc, st::sdesc_sw128(xbuf + b * 32, 16, 1024),
+                                     st::sdesc_sw128(xbuf + (2 + step) * 32, 16, 1024), idesc, 1u);
                         st::umma_commit(&accf[a]);
                     }
                     if (!ok) break;
@@ -2102,35 +2161,38 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        // Warp w: TMEM lanes 32 (w % 4) .. (keys), accumulator columns 64 (w / 4) .. + 63
-        // (queries 128 step + 64 (w / 4) + c of the unit).  Lane l owns the candidate
-        // buffer, count and thresholds of the unit's queries 128 (s / 2) + 64 (w / 4) +
-        // 32 (s % 2) + l for its four slots s.
-        const int quad = warp & 3, hq = warp >> 2;
+        // Warp w: TMEM lanes 32 w .. (keys), all 128 accumulator columns of each step
+        // (queries 128 step + c of the unit).  Lane l owns the candidate buffer, count
+        // and thresholds of the unit's queries 32 s + l for its eight slots s.
+        const int quad = warp;
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
         uint64_t *bufs = g.cbuf + static_cast<int64_t>(blockIdx.x * N_QUAD + quad) * TQ * KCAP;
-        float *wthr = thr_s + quad * TQ, *wthf = thr_f + quad * TQ;
+        float *wthr = thr_s + quad * TQ;
         const uint32_t acc0 = tmem + lane_addr + ACC_COL;
         uint32_t gt = 0, gs = 0, uj = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
             if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
             const float *qc = qconst0 + (uj & 1u) * 4 * TQ;
-            const float *qc_e = qc, *qc_p = qc + TQ, *qc_live = qc + 2 * TQ;
+            const float *qc_p = qc + TQ, *qc_live = qc + 2 * TQ, *qc_mag = qc + 3 * TQ;
             const int qbase = (unit % g.nqb) * TQ;
-            int cnt[4];
-            float thr[4], eff[4];
+            const int nlive = g.nq - qbase;  // the unit's queries from nlive on are padding
+            int cnt[8];
+            float thr[8], eff[8];
 #pragma unroll
-            for (int sl = 0; sl < 4; sl++) {
-                const int qu = 128 * (sl >> 1) + 64 * hq + 32 * (sl & 1) + lane;
+            for (int sl = 0; sl < 8; sl++) {
+                const int qu = 32 * sl + lane;
                 const bool live = qc_live[qu] > 0.0f;
                 cnt[sl] = 0;
                 thr[sl] = live ? -INFINITY : INFINITY;
                 eff[sl] = live ? thr_of(__ldcg(g.gthr + qbase + qu)) : INFINITY;
                 wthr[qu] = eff[sl];
-                wthf[qu] = live ? lowered(eff[sl]) : INFINITY;  // lowered(+inf) would be NaN
+                if (g.exact && live)
+                    *reinterpret_cast<uint16_t *>(smem + TO_X + st::sw128_offset(qu & 127, 2 * (2 + (qu >> 7)))) =
+                        static_cast<uint16_t>(tm_w_bits(eff[sl], qc_mag[qu]));
             }
+            st::fence_proxy_async_smem();
             __syncwarp();
             int64_t tb;
             int nk;
@@ -2142,9 +2204,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 }
                 const int kk = 32 * quad + lane;
                 const float scale = kf[f * NK + kk];
-                const float knh = kn[f * NK + kk];
                 const bool klive = kk < nk;
-                const float inv_s = rcp_approx(scale);
                 const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
 #pragma unroll
                 for (int step = 0; step < 2; step++, gs++) {
@@ -2154,72 +2214,40 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         break;
                     }
                     st::tc_fence_after();
-                    const uint32_t acc = acc0 + a * 128u + 64u * hq;
-                    uint32_t pass[4];  // per 16-query chunk, bit i: the pair passed the bound
-                    // full pass: keep a pair if its exact score can reach the threshold,
-                    // acc >= t / s - E_q; sample pass: keep it if its lower bound
-                    // (acc - E_q) s does, acc >= t / s + E_q, and insert that bound
-                    const float esign = g.exact ? -1.0f : 1.0f;
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        uint32_t r[16];
-                        st::tmem_ld16(acc + 16 * c, r);
-                        st::tmem_ld_wait();
-                        const int q0 = 128 * step + 64 * hq + 16 * c;
-                        uint32_t pm = 0;
-#pragma unroll
-                        for (int i4 = 0; i4 < 16; i4 += 4) {
-                            const float4 tf = *reinterpret_cast<const float4 *>(wthf + q0 + i4);
-                            const float4 ev = *reinterpret_cast<const float4 *>(qc_e + q0 + i4);
-                            const float ta[4] = {tf.x, tf.y, tf.z, tf.w}, ea[4] = {ev.x, ev.y, ev.z, ev.w};
-                            float pa[4] = {0.f, 0.f, 0.f, 0.f};
-                            if (MODE == MODE_L2) {
-                                const float4 p4 = *reinterpret_cast<const float4 *>(qc_p + q0 + i4);
-                                pa[0] = p4.x; pa[1] = p4.y; pa[2] = p4.z; pa[3] = p4.w;
-                            }
-#pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const float t = MODE == MODE_L2 ? fmaf(knh, pa[i], ta[i]) : ta[i];
-                                pm |= (__uint_as_float(r[i4 + i]) >= fmaf(t, inv_s, esign * ea[i]) ? 1u : 0u)
-                                      << (i4 + i);
-                            }
-                        }
-                        pm = klive ? pm : 0u;
-                        pass[c] = pm;
-                        if (!g.exact) {
-                            // sample pass: insert the lower bound (acc - E_q) s [- |k|^2 2^(e-1)],
-                            // lowered by 2^-12 for its own rounding: every entry is at most its
-                            // key's exact score, so a list's 128th best bounds the final one
-                            unsigned qm = __reduce_or_sync(0xffffffffu, pm);
-                            const int sl = 2 * step + (c >> 1);
-                            while (qm) {
-                                const int i = __ffs(qm) - 1;
-                                qm &= qm - 1;
-                                const bool p = (pm >> i) & 1u;
-                                const unsigned mb = __ballot_sync(0xffffffffu, p);
-                                const int owner = 16 * (c & 1) + i;
-                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
-                                if (p) {
-                                    float lb = (__uint_as_float(r[i]) - qc_e[q0 + i]) * scale;
-                                    if (MODE == MODE_L2) lb = fmaf(-knh, qc_p[q0 + i], lb);
-                                    bufs[static_cast<int64_t>(q0 + i) * KCAP + base + __popc(mb & lt)] =
-                                        make_key(lowered(lb), idx);
-                                }
-                                if (lane == owner) cnt[sl] += __popc(mb);
-                            }
-                        }
-                    }
-                    // every column is read: the accumulator goes back to the MMA
-                    st::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) st::mbar_arrive(&acce[a]);
+                    const uint32_t acc = acc0 + a * 128u;
                     if (g.exact) {
-                        // full pass: each kept pair's exact score, by the whole warp; insert if
-                        // it reaches the list's threshold
+                        // full pass: a pair is kept if its filtered accumulator is not negative
+                        uint32_t pass[8];  // per 16-query chunk, bit i: the pair was kept
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const int q0 = 128 * step + 64 * hq + 16 * c;
-                            const int sl = 2 * step + (c >> 1);
+                        for (int c2 = 0; c2 < 4; c2++) {
+                            uint32_t r[32];
+                            st::tmem_ld32(acc + 32 * c2, r);
+                            st::tmem_ld_wait();
+#pragma unroll
+                            for (int hh = 0; hh < 2; hh++) {
+                                uint32_t all = r[16 * hh];
+#pragma unroll
+                                for (int j = 1; j < 16; j++) all &= r[16 * hh + j];
+                                uint32_t pm = 0u;
+                                if (!(all >> 31)) {
+#pragma unroll
+                                    for (int j = 0; j < 16; j++) pm |= ((~r[16 * hh + j]) >> 31) << j;
+                                }
+                                const int lim = nlive - (128 * step + 32 * c2 + 16 * hh);
+                                const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
+                                pass[2 * c2 + hh] = klive ? pm & qmask : 0u;
+                            }
+                        }
+                        // every column is read: the accumulator goes back to the MMA
+                        st::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) st::mbar_arrive(&acce[a]);
+                        // each kept pair's exact score, by the whole warp; inserted if it
+                        // reaches the list's threshold
+#pragma unroll
+                        for (int c = 0; c < 8; c++) {
+                            const int q0 = 128 * step + 16 * c;
+                            const int sl = 4 * step + (c >> 1);
                             unsigned lanes = __ballot_sync(0xffffffffu, pass[c] != 0u);
                             while (lanes) {
                                 const int L = __ffs(lanes) - 1;
@@ -2228,15 +2256,16 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                                 const float sL = __shfl_sync(0xffffffffu, scale, L);
                                 const int keyL = 32 * quad + L;
                                 const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
-                                const uint32_t idxL = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
+                                const uint32_t idxL =
+                                    g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
                                 while (bits) {
-                                    const int i = __ffs(bits) - 1;
+                                    const int ib = __ffs(bits) - 1;
                                     bits &= bits - 1;
-                                    const int qu = q0 + i;
-                                    const float e = tm_exact_warp<MODE>(kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256,
-                                                                        qc_p[qu]);
+                                    const int qu = q0 + ib;
+                                    const float e = tm_exact_warp(kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256,
+                                                                  qc_p[qu]);
                                     if (e >= wthr[qu]) {
-                                        const int owner = 16 * (c & 1) + i;
+                                        const int owner = 16 * (c & 1) + ib;
                                         const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
                                         if (lane == owner) {
                                             bufs[static_cast<int64_t>(qu) * KCAP + base] = make_key(e, idxL);
@@ -2246,12 +2275,51 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                                 }
                             }
                         }
+                    } else {
+                        // sample pass: acc' is a lower bound of the pair's score; a pair enters
+                        // its list, lowered by 2^-12, if the bound reaches the threshold
+#pragma unroll
+                        for (int c = 0; c < 8; c++) {
+                            uint32_t r[16];
+                            st::tmem_ld16(acc + 16 * c, r);
+                            st::tmem_ld_wait();
+                            const int q0 = 128 * step + 16 * c;
+                            uint32_t pm = 0u;
+#pragma unroll
+                            for (int i4 = 0; i4 < 16; i4 += 4) {
+                                const float4 tf = *reinterpret_cast<const float4 *>(wthr + q0 + i4);
+                                pm |= (__uint_as_float(r[i4]) >= tf.x ? 1u : 0u) << i4;
+                                pm |= (__uint_as_float(r[i4 + 1]) >= tf.y ? 1u : 0u) << (i4 + 1);
+                                pm |= (__uint_as_float(r[i4 + 2]) >= tf.z ? 1u : 0u) << (i4 + 2);
+                                pm |= (__uint_as_float(r[i4 + 3]) >= tf.w ? 1u : 0u) << (i4 + 3);
+                            }
+                            const int lim = nlive - q0;
+                            const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
+                            pm = klive ? pm & qmask : 0u;
+                            unsigned qm = __reduce_or_sync(0xffffffffu, pm);
+                            const int sl = 4 * step + (c >> 1);
+                            while (qm) {
+                                const int ib = __ffs(qm) - 1;
+                                qm &= qm - 1;
+                                const bool p = (pm >> ib) & 1u;
+                                const unsigned mb = __ballot_sync(0xffffffffu, p);
+                                const int owner = 16 * (c & 1) + ib;
+                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
+                                if (p)
+                                    bufs[static_cast<int64_t>(q0 + ib) * KCAP + base + __popc(mb & lt)] =
+                                        make_key(lowered(__uint_as_float(tm_pick16(r, ib))), idx);
+                                if (lane == owner) cnt[sl] += __popc(mb);
+                            }
+                        }
+                        st::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) st::mbar_arrive(&acce[a]);
                     }
                     // compaction when a list fills up; thresholds: own 128th best, published
 #pragma unroll
-                    for (int sh = 0; sh < 2; sh++) {
-                        const int sl = 2 * step + sh;
-                        const int qu = 128 * step + 64 * hq + 32 * sh + lane;
+                    for (int sh = 0; sh < 4; sh++) {
+                        const int sl = 4 * step + sh;
+                        const int qu = 32 * sl + lane;
                         uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
                         const unsigned need = __ballot_sync(0xffffffffu, cnt[sl] > KCAP - NK);
                         if (need) {
@@ -2265,8 +2333,12 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                             if (ne > eff[sl]) {
                                 eff[sl] = ne;
                                 wthr[qu] = ne;
-                                wthf[qu] = lowered(ne);
+                                if (g.exact)
+                                    *reinterpret_cast<uint16_t *>(smem + TO_X +
+                                                                  st::sw128_offset(qu & 127, 2 * (2 + (qu >> 7)))) =
+                                        static_cast<uint16_t>(tm_w_bits(ne, qc_mag[qu]));
                             }
+                            st::fence_proxy_async_smem();
                             __syncwarp();
                         }
                     }
@@ -2276,8 +2348,8 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             if (!ok) break;
             const int split = unit / g.nqb;
 #pragma unroll
-            for (int sl = 0; sl < 4; sl++) {
-                const int qu = 128 * (sl >> 1) + 64 * hq + 32 * (sl & 1) + lane;
+            for (int sl = 0; sl < 8; sl++) {
+                const int qu = 32 * sl + lane;
                 uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
                 uint64_t *my_out =
                     g.unit_out + ((static_cast<int64_t>(split) * N_QUAD + quad) * g.nq_pad + qbase + qu) * KTOP;
@@ -2291,21 +2363,19 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 
     st::tc_fence_before();
     __syncthreads();
-    if (warp == N_MMA_WARP) {
+    if (warp == T_MMA_WARP) {
         st::tc_fence_after();
         st::tmem_dealloc(tmem, N_TMEM_COLS);
     }
 }
 
-template <int MODE>
 st_status launch_tmem(st_handle *h, const NarrowArgs &g, int grid) {
-    auto kern = k_knn_tmem<MODE>;
     static bool attr_done = false;
     if (!attr_done) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TMEM_SMEM));
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_knn_tmem, cudaFuncAttributeMaxDynamicSharedMemorySize, TMEM_SMEM));
         attr_done = true;
     }
-    kern<<<grid, N_THREADS, TMEM_SMEM, h->stream>>>(g);
+    k_knn_tmem<<<grid, T_THREADS, TMEM_SMEM, h->stream>>>(g);
     return st_after_launch(h, "k_knn_tmem");
 }
 
@@ -2319,9 +2389,9 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (s != ST_OK) return s;
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
-    if (!ranges && dim == 256 && nq > NQ && prec == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
-        // more than 32 EXACT queries at dim 256: keys in TMEM (k_knn_tmem), units of
-        // (key split, 256 queries), about eight units per SM
+    if (!ranges && dim == 256 && nq > NQ && prec == 0 && mode == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
+        // more than 32 EXACT dot-product queries at dim 256: keys in TMEM (k_knn_tmem),
+        // units of (key split, 256 queries), about eight units per SM
         const int nqb = static_cast<int>((nq + TQ - 1) / TQ);
         const int64_t nq_pad = static_cast<int64_t>(nqb) * TQ;
         const int64_t tiles = (n_keys + NK - 1) / NK;
@@ -2360,9 +2430,7 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.unit_out = unit_out;
         g.gthr = gthr;
         g.status = h->d_status;
-        auto run = [&](const NarrowArgs &a, int gr) {
-            return mode == 0 ? launch_tmem<MODE_DOT>(h, a, gr) : launch_tmem<MODE_L2>(h, a, gr);
-        };
+        auto run = [&](const NarrowArgs &a, int gr) { return launch_tmem(h, a, gr); };
         // the narrow scan's two sample passes seed the thresholds (every 1024th, then
         // every 16th tile), with the full pass's key splits
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {

@@ -303,6 +303,42 @@ def test_wide_scan_matches_oracle_at_scale(dev, mode, n, nq):
     _check_exact(q, codes.cpu().numpy(), scales.cpu().numpy(), s.cpu().numpy(), i.cpu().numpy(), 128, mode)
 
 
+def test_wide_scan_edge_scales_and_queries(dev):
+    """The wide dot-product scan with keys outside the f16 expansion's range
+    (scales below 2^-13, zero, negative, at or above 2^14) and queries that
+    are all zero, tiny or huge, over two ragged query blocks.  Bars: every
+    returned score within 2^-22 of the largest returned score of its row of
+    the exact f64 score of its key, and indices identical to the oracle's
+    except inside such bands."""
+    import scratchtape_b200.knn as K
+    n, nq = 30_011, 300
+    codes, scales = K.synth_keys(n, 256, seed=11)
+    sc = scales.cpu().numpy().copy()
+    sc[:40] *= 1e-5          # |s| < 2^-13: expanded as zeros, bound widened
+    sc[40:50] = 0.0
+    sc[50:400] *= -1.0       # negative scales
+    sc[400:403] = [20000.0, -17000.0, 16384.0]  # |s| >= 2^14: every pair kept and rescored
+    rng = np.random.default_rng(12)
+    q = rng.standard_normal((nq, 256)).astype(np.float32)
+    q[0] = 0.0
+    q[1] *= 1e-6
+    q[2] *= 1e6
+    q[299] = 0.0
+    got_s, got_i = K.search(codes, torch.from_numpy(sc).cuda(), torch.from_numpy(q).cuda(), k=128, mode="dot",
+                            prec="exact")
+    got_s, got_i = got_s.cpu().numpy(), got_i.cpu().numpy()
+    codes_h = codes.cpu().numpy()
+    want_s, want_i = oracle.knn_topk(codes_h, sc, q, 128, mode="dot", prec="exact")
+    for r in range(nq):
+        band = 2.0 ** -22 * np.abs(want_s[r]).max() + 1e-30
+        exact = oracle.knn_pair_dots(codes_h, sc, q, np.full(128, r), got_i[r])
+        assert np.all(np.abs(got_s[r] - exact) <= band), "row %d: scores off" % r
+        assert np.all(np.abs(exact - want_s[r]) <= 2 * band), "row %d: not the best keys" % r
+        ws = want_s[r]
+        tied = np.r_[False, np.abs(np.diff(ws)) <= 2 * band] | np.r_[np.abs(np.diff(ws)) <= 2 * band, False]
+        assert np.array_equal(got_i[r][~tied], want_i[r][~tied]), "row %d: indices differ outside ties" % r
+
+
 def test_wide_scan_repeats_bit_for_bit_and_matches_shards(dev):
     """The wide scan is deterministic, and two shards scanned with their own
     index_base and merged give the one-scan result bit for bit."""
