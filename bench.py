@@ -457,9 +457,10 @@ def run_ours(args):
                                if fused else "six GEMM launches on three streams"},
             "roofline": ({"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                           "frac": achieved / hbm, "traffic": C2_FUSED_TRAFFIC, "peak_source": peak_src,
-                          "traffic_note": "DRAM read+write of one k_mlp_step launch from one ncu capture "
-                                          "(profiles/mlp_fused_c2.md); algorithmic bytes: the six GEMMs' f32 "
-                                          "operands and results, 6 x 10.75 MB",
+                          "traffic_note": "DRAM read+write (dram__bytes_read.sum + dram__bytes_write.sum) of one "
+                                          "k_mlp_step launch at the C2 shape, from one ncu --set full capture "
+                                          "(one launch, --clock-control none); algorithmic bytes: the six GEMMs' "
+                                          "f32 operands and results, 6 x 10.75 MB",
                           "unique_io_bytes": c2_unique_bytes(),
                           "unique_io_frac": c2_unique_bytes() / (fused_ms / 1e3) / 1e9 / hbm,
                           "kernel": "k_mlp_step (one cooperative launch, reductions inside)",

@@ -1787,7 +1787,7 @@ st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
 // scan's units (q.k 2^e), so k_knn_merge and k_knn_decode are shared.
 //
 // Roles (448 threads, one CTA per SM, up to 128 registers a thread): warp 13
-// bulk-copies each tile's codes and scales into a 7-stage ring; warps 4-11
+// bulk-copies each tile's codes and scales into a 6-stage ring; warps 4-11
 // expand codes into TMEM (a warp per 16 lanes, 16x256b stores, v through a
 // byte permute of the key's four-entry table) and write the keys' filter
 // rows; warp 12 issues the MMAs (two A buffers, two 128-column accumulators);
@@ -1797,7 +1797,7 @@ constexpr int T_EPI = 4;                      // filter warps: one per TMEM lane
 constexpr int T_MMA_WARP = T_EPI + N_PROD;    // 12
 constexpr int T_TMA_WARP = T_MMA_WARP + 1;    // 13
 constexpr int T_THREADS = 32 * (T_TMA_WARP + 1);
-constexpr int T_STAGES = 7;
+constexpr int T_STAGES = 6;
 constexpr int T_NACC = 2;
 constexpr int TO_Q = 0;                       // [2 steps][4 K chunks][128 rows x 128 B] f16, SW128
 constexpr int TO_X = TO_Q + 2 * 4 * 16384;    // filter rows [128 x 128 B] SW128, K slice j (dims 16 j ..):
@@ -1805,8 +1805,10 @@ constexpr int TO_X = TO_Q + 2 * 4 * 16384;    // filter rows [128 x 128 B] SW128
 constexpr int TO_RING = TO_X + 16384;
 constexpr int TO_KF = TO_RING + T_STAGES * N_STAGE_BYTES;   // [N_KF][128] scale
 constexpr int TO_QC = TO_KF + N_KF * NK * 4;                // [2 units][4][TQ]: E, 2^e, live, sum |hi|
-constexpr int TO_THR = TO_QC + 2 * 4 * TQ * 4;              // [4 quadrants][TQ] thresholds (stored units)
-constexpr int TO_BAR = TO_THR + N_QUAD * TQ * 4;
+constexpr int TO_THR = TO_QC + 2 * 4 * TQ * 4;              // [4 quadrants][TQ] effective thresholds (stored units)
+constexpr int TO_OTHR = TO_THR + N_QUAD * TQ * 4;           // [4 quadrants][TQ] lists' own 128th best
+constexpr int TO_OCNT = TO_OTHR + N_QUAD * TQ * 4;          // [4 quadrants][TQ] lists' entry counts
+constexpr int TO_BAR = TO_OCNT + N_QUAD * TQ * 4;
 constexpr int T_NBARS = 2 * T_STAGES + 2 * N_A + 2 * T_NACC + N_KF + 2 + 2 + 1 + 1;
 constexpr int TO_MISC = TO_BAR + T_NBARS * 8;
 constexpr int TMEM_SMEM = TO_MISC + 16 + 1024;
@@ -1865,11 +1867,14 @@ __device__ __forceinline__ uint32_t tm_pick16(const uint32_t (&r)[16], int i) {
     return v;
 }
 
+template <bool EXACT>
 __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *kf = reinterpret_cast<float *>(smem + TO_KF);
     float *thr_s = reinterpret_cast<float *>(smem + TO_THR);  // [4][TQ] effective 128th best (stored units)
+    float *thr_o = reinterpret_cast<float *>(smem + TO_OTHR);
+    int *cnt_o = reinterpret_cast<int *>(smem + TO_OCNT);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TO_BAR);
     uint64_t *rfull = bars, *rempty = bars + T_STAGES, *afull = bars + 2 * T_STAGES, *aempty = afull + N_A;
     uint64_t *accf = aempty + N_A, *acce = accf + T_NACC, *kfr = acce + T_NACC, *qready = kfr + N_KF;
@@ -2011,7 +2016,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     uint32_t wb = TM_HNINF, ebits = 0u;
                     if (live) {
                         ebits = __half_as_ushort(__float2half_ru(eb));
-                        if (g.exact) {
+                        if (EXACT) {
                             wb = tm_w_bits(thr_of(__ldcg(g.gthr + qg)), mag);
                         } else {
                             wb = 0u;
@@ -2162,13 +2167,18 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     } else {
         // ------------------------------------------------------------ epilogue
         // Warp w: TMEM lanes 32 w .. (keys), all 128 accumulator columns of each step
-        // (queries 128 step + c of the unit).  Lane l owns the candidate buffer, count
-        // and thresholds of the unit's queries 32 s + l for its eight slots s.
+        // (queries 128 step + c of the unit).  Lane l owns the candidate buffer of the
+        // unit's queries 32 s + l (slots s = 0..7); the lists' counts, own 128th-best
+        // scores and effective thresholds live in shared memory, so that the loops over
+        // chunks and slots stay rolled (small code: the four roles share the SM's
+        // instruction cache).
         const int quad = warp;
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
         uint64_t *bufs = g.cbuf + static_cast<int64_t>(blockIdx.x * N_QUAD + quad) * TQ * KCAP;
-        float *wthr = thr_s + quad * TQ;
+        float *wthr = thr_s + quad * TQ;   // effective threshold (stored units)
+        float *othr = thr_o + quad * TQ;   // the list's own 128th best
+        int *ocnt = cnt_o + quad * TQ;     // the list's entries
         const uint32_t acc0 = tmem + lane_addr + ACC_COL;
         uint32_t gt = 0, gs = 0, uj = 0;
         bool ok = true;
@@ -2178,19 +2188,17 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             const float *qc_p = qc + TQ, *qc_live = qc + 2 * TQ, *qc_mag = qc + 3 * TQ;
             const int qbase = (unit % g.nqb) * TQ;
             const int nlive = g.nq - qbase;  // the unit's queries from nlive on are padding
-            int cnt[8];
-            float thr[8], eff[8];
-#pragma unroll
+#pragma unroll 1
             for (int sl = 0; sl < 8; sl++) {
                 const int qu = 32 * sl + lane;
-                const bool live = qc_live[qu] > 0.0f;
-                cnt[sl] = 0;
-                thr[sl] = live ? -INFINITY : INFINITY;
-                eff[sl] = live ? thr_of(__ldcg(g.gthr + qbase + qu)) : INFINITY;
-                wthr[qu] = eff[sl];
-                if (g.exact && live)
+                const bool live = qu < nlive;
+                ocnt[qu] = 0;
+                othr[qu] = live ? -INFINITY : INFINITY;
+                const float e0 = live ? thr_of(__ldcg(g.gthr + qbase + qu)) : INFINITY;
+                wthr[qu] = e0;
+                if (EXACT && live)
                     *reinterpret_cast<uint16_t *>(smem + TO_X + st::sw128_offset(qu & 127, 2 * (2 + (qu >> 7)))) =
-                        static_cast<uint16_t>(tm_w_bits(eff[sl], qc_mag[qu]));
+                        static_cast<uint16_t>(tm_w_bits(e0, qc_mag[qu]));
             }
             st::fence_proxy_async_smem();
             __syncwarp();
@@ -2206,7 +2214,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 const float scale = kf[f * NK + kk];
                 const bool klive = kk < nk;
                 const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
-#pragma unroll
+#pragma unroll 1
                 for (int step = 0; step < 2; step++, gs++) {
                     const uint32_t a = gs % T_NACC;
                     if (!nwait(&accf[a], (gs / T_NACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
@@ -2215,7 +2223,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     }
                     st::tc_fence_after();
                     const uint32_t acc = acc0 + a * 128u;
-                    if (g.exact) {
+                    const int lim0 = nlive - 128 * step;
+                    if (EXACT) {
                         // full pass: a pair is kept if its filtered accumulator is not negative
                         uint32_t pass[8];  // per 16-query chunk, bit i: the pair was kept
 #pragma unroll
@@ -2233,7 +2242,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 #pragma unroll
                                     for (int j = 0; j < 16; j++) pm |= ((~r[16 * hh + j]) >> 31) << j;
                                 }
-                                const int lim = nlive - (128 * step + 32 * c2 + 16 * hh);
+                                const int lim = lim0 - (32 * c2 + 16 * hh);
                                 const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
                                 pass[2 * c2 + hh] = klive ? pm & qmask : 0u;
                             }
@@ -2242,34 +2251,37 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         st::tc_fence_before();
                         __syncwarp();
                         if (lane == 0) st::mbar_arrive(&acce[a]);
-                        // each kept pair's exact score, by the whole warp; inserted if it
-                        // reaches the list's threshold
+                        // each kept pair's exact score, by the whole warp; inserted by the
+                        // list's owner lane if it reaches the threshold
+                        const unsigned any = __ballot_sync(0xffffffffu, (pass[0] | pass[1] | pass[2] | pass[3] |
+                                                                         pass[4] | pass[5] | pass[6] | pass[7]) != 0u);
+                        if (any) {
+#pragma unroll 1
+                            for (int c = 0; c < 8; c++) {
+                                uint32_t pc = pass[0];
 #pragma unroll
-                        for (int c = 0; c < 8; c++) {
-                            const int q0 = 128 * step + 16 * c;
-                            const int sl = 4 * step + (c >> 1);
-                            unsigned lanes = __ballot_sync(0xffffffffu, pass[c] != 0u);
-                            while (lanes) {
-                                const int L = __ffs(lanes) - 1;
-                                lanes &= lanes - 1;
-                                uint32_t bits = __shfl_sync(0xffffffffu, pass[c], L);
-                                const float sL = __shfl_sync(0xffffffffu, scale, L);
-                                const int keyL = 32 * quad + L;
-                                const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
-                                const uint32_t idxL =
-                                    g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
-                                while (bits) {
-                                    const int ib = __ffs(bits) - 1;
-                                    bits &= bits - 1;
-                                    const int qu = q0 + ib;
-                                    const float e = tm_exact_warp(kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256,
-                                                                  qc_p[qu]);
-                                    if (e >= wthr[qu]) {
-                                        const int owner = 16 * (c & 1) + ib;
-                                        const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
-                                        if (lane == owner) {
+                                for (int j = 1; j < 8; j++) pc = c == j ? pass[j] : pc;
+                                unsigned lanes = __ballot_sync(0xffffffffu, pc != 0u);
+                                const int q0 = 128 * step + 16 * c;
+                                while (lanes) {
+                                    const int L = __ffs(lanes) - 1;
+                                    lanes &= lanes - 1;
+                                    uint32_t bits = __shfl_sync(0xffffffffu, pc, L);
+                                    const float sL = __shfl_sync(0xffffffffu, scale, L);
+                                    const int keyL = 32 * quad + L;
+                                    const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
+                                    const uint32_t idxL =
+                                        g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
+                                    while (bits) {
+                                        const int ib = __ffs(bits) - 1;
+                                        bits &= bits - 1;
+                                        const int qu = q0 + ib;
+                                        const float e = tm_exact_warp(
+                                            kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256, qc_p[qu]);
+                                        if (lane == 16 * (c & 1) + ib && e >= wthr[qu]) {
+                                            const int base = ocnt[qu];
                                             bufs[static_cast<int64_t>(qu) * KCAP + base] = make_key(e, idxL);
-                                            cnt[sl] = base + 1;
+                                            ocnt[qu] = base + 1;
                                         }
                                     }
                                 }
@@ -2278,7 +2290,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     } else {
                         // sample pass: acc' is a lower bound of the pair's score; a pair enters
                         // its list, lowered by 2^-12, if the bound reaches the threshold
-#pragma unroll
+#pragma unroll 1
                         for (int c = 0; c < 8; c++) {
                             uint32_t r[16];
                             st::tmem_ld16(acc + 16 * c, r);
@@ -2293,22 +2305,23 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                                 pm |= (__uint_as_float(r[i4 + 2]) >= tf.z ? 1u : 0u) << (i4 + 2);
                                 pm |= (__uint_as_float(r[i4 + 3]) >= tf.w ? 1u : 0u) << (i4 + 3);
                             }
-                            const int lim = nlive - q0;
+                            const int lim = lim0 - 16 * c;
                             const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
                             pm = klive ? pm & qmask : 0u;
                             unsigned qm = __reduce_or_sync(0xffffffffu, pm);
-                            const int sl = 4 * step + (c >> 1);
                             while (qm) {
                                 const int ib = __ffs(qm) - 1;
                                 qm &= qm - 1;
                                 const bool p = (pm >> ib) & 1u;
                                 const unsigned mb = __ballot_sync(0xffffffffu, p);
-                                const int owner = 16 * (c & 1) + ib;
-                                const int base = __shfl_sync(0xffffffffu, cnt[sl], owner);
+                                const int qu = q0 + ib;
+                                const int base = ocnt[qu];
                                 if (p)
-                                    bufs[static_cast<int64_t>(q0 + ib) * KCAP + base + __popc(mb & lt)] =
+                                    bufs[static_cast<int64_t>(qu) * KCAP + base + __popc(mb & lt)] =
                                         make_key(lowered(__uint_as_float(tm_pick16(r, ib))), idx);
-                                if (lane == owner) cnt[sl] += __popc(mb);
+                                __syncwarp();  // every lane has read the count
+                                if (lane == 16 * (c & 1) + ib) ocnt[qu] = base + __popc(mb);
+                                __syncwarp();
                             }
                         }
                         st::tc_fence_before();
@@ -2316,29 +2329,31 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         if (lane == 0) st::mbar_arrive(&acce[a]);
                     }
                     // compaction when a list fills up; thresholds: own 128th best, published
-#pragma unroll
+#pragma unroll 1
                     for (int sh = 0; sh < 4; sh++) {
-                        const int sl = 4 * step + sh;
-                        const int qu = 32 * sl + lane;
-                        uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
-                        const unsigned need = __ballot_sync(0xffffffffu, cnt[sl] > KCAP - NK);
+                        const int qu = 128 * step + 32 * sh + lane;
+                        int cn = ocnt[qu];
+                        float th = othr[qu];
+                        const unsigned need = __ballot_sync(0xffffffffu, cn > KCAP - NK);
                         if (need) {
-                            const float before = thr[sl];
-                            warp_compact(need, my_buf, cnt[sl], thr[sl], nullptr, false);
-                            if (thr[sl] > before) atomicMax(g.gthr + qbase + qu, ord_f32(thr[sl]));
+                            const float before = th;
+                            warp_compact(need, bufs + static_cast<int64_t>(qu) * KCAP, cn, th, nullptr, false);
+                            ocnt[qu] = cn;
+                            othr[qu] = th;
+                            if (th > before) atomicMax(g.gthr + qbase + qu, ord_f32(th));
                         }
-                        float ne = fmaxf(thr[sl], eff[sl]);
-                        if ((i & 15) == 15 && qc_live[qu] > 0.0f) ne = fmaxf(ne, thr_of(__ldcg(g.gthr + qbase + qu)));
-                        if (__any_sync(0xffffffffu, ne > eff[sl])) {
-                            if (ne > eff[sl]) {
-                                eff[sl] = ne;
+                        const float ef = wthr[qu];
+                        float ne = fmaxf(th, ef);
+                        if ((i & 15) == 15 && qu < nlive) ne = fmaxf(ne, thr_of(__ldcg(g.gthr + qbase + qu)));
+                        if (__any_sync(0xffffffffu, ne > ef)) {
+                            if (ne > ef) {
                                 wthr[qu] = ne;
-                                if (g.exact)
+                                if (EXACT)
                                     *reinterpret_cast<uint16_t *>(smem + TO_X +
                                                                   st::sw128_offset(qu & 127, 2 * (2 + (qu >> 7)))) =
                                         static_cast<uint16_t>(tm_w_bits(ne, qc_mag[qu]));
                             }
-                            st::fence_proxy_async_smem();
+                            if (EXACT) st::fence_proxy_async_smem();
                             __syncwarp();
                         }
                     }
@@ -2347,14 +2362,15 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             }
             if (!ok) break;
             const int split = unit / g.nqb;
-#pragma unroll
+#pragma unroll 1
             for (int sl = 0; sl < 8; sl++) {
                 const int qu = 32 * sl + lane;
-                uint64_t *my_buf = bufs + static_cast<int64_t>(qu) * KCAP;
+                int cn = ocnt[qu];
+                float th = othr[qu];
                 uint64_t *my_out =
                     g.unit_out + ((static_cast<int64_t>(split) * N_QUAD + quad) * g.nq_pad + qbase + qu) * KTOP;
-                const unsigned need = __ballot_sync(0xffffffffu, qc_live[qu] > 0.0f);
-                warp_compact(need, my_buf, cnt[sl], thr[sl], my_out, true);
+                const unsigned need = __ballot_sync(0xffffffffu, qu < nlive);
+                warp_compact(need, bufs + static_cast<int64_t>(qu) * KCAP, cn, th, my_out, true);
             }
             __syncwarp();
             if (lane == 0) st::mbar_arrive(&edone[uj & 1u]);
@@ -2369,14 +2385,21 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     }
 }
 
-st_status launch_tmem(st_handle *h, const NarrowArgs &g, int grid) {
+template <bool EXACT>
+st_status launch_tmem_t(st_handle *h, const NarrowArgs &g, int grid) {
     static bool attr_done = false;
     if (!attr_done) {
-        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_knn_tmem, cudaFuncAttributeMaxDynamicSharedMemorySize, TMEM_SMEM));
+        ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_knn_tmem<EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              TMEM_SMEM));
         attr_done = true;
     }
-    k_knn_tmem<<<grid, T_THREADS, TMEM_SMEM, h->stream>>>(g);
+    k_knn_tmem<EXACT><<<grid, T_THREADS, TMEM_SMEM, h->stream>>>(g);
     return st_after_launch(h, "k_knn_tmem");
+}
+
+// The full pass (exact scores) or a sample pass (lower bounds), as g.exact says.
+st_status launch_tmem(st_handle *h, const NarrowArgs &g, int grid) {
+    return g.exact ? launch_tmem_t<true>(h, g, grid) : launch_tmem_t<false>(h, g, grid);
 }
 
 }  // namespace
