@@ -1819,6 +1819,9 @@ constexpr float TM_SMALL = 1.220703125e-4f;   // 2^-13: smaller |s| expand as ze
 constexpr float TM_BIG = 16384.0f;            // 2^14: larger |s| expand as zeros (every pair kept)
 constexpr uint32_t TM_H1024 = 0x6400u;        // f16 bit patterns: 1024, -inf, +inf
 constexpr uint32_t TM_HNINF = 0xFC00u, TM_HPINF = 0x7C00u;
+constexpr int TM_MAINT = 16;                  // tiles between the lists' compaction / threshold rounds
+static_assert(KCAP - 32 * TM_MAINT >= KTOP && 32 * TM_MAINT <= KCAP - 32 * TM_MAINT,
+              "a list must not overflow between two rounds");
 
 // Two f16 values of the key's table {t1:t0} (bytes 2u, 2u + 1: the value for
 // code u) for the two codes in bits 0-3 of x (code a = bits 0-1 to the lower
@@ -2228,23 +2231,26 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         // full pass: a pair is kept if its filtered accumulator is not negative
                         uint32_t pass[8];  // per 16-query chunk, bit i: the pair was kept
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; c2++) {
-                            uint32_t r[32];
-                            st::tmem_ld32(acc + 32 * c2, r);
+                        for (int c4 = 0; c4 < 2; c4++) {
+                            uint32_t r[2][32];  // 64 columns per wait
+                            st::tmem_ld32(acc + 64 * c4, r[0]);
+                            st::tmem_ld32(acc + 64 * c4 + 32, r[1]);
                             st::tmem_ld_wait();
 #pragma unroll
-                            for (int hh = 0; hh < 2; hh++) {
-                                uint32_t all = r[16 * hh];
-#pragma unroll
-                                for (int j = 1; j < 16; j++) all &= r[16 * hh + j];
+                            for (int hh = 0; hh < 4; hh++) {
+                                const uint32_t *rc = r[hh >> 1] + 16 * (hh & 1);
+                                // all 16 negative <=> the AND of their sign bits is set
+                                const uint32_t a0 = rc[0] & rc[1] & rc[2] & rc[3], a1 = rc[4] & rc[5] & rc[6] & rc[7];
+                                const uint32_t a2 = rc[8] & rc[9] & rc[10] & rc[11];
+                                const uint32_t a3 = rc[12] & rc[13] & rc[14] & rc[15];
                                 uint32_t pm = 0u;
-                                if (!(all >> 31)) {
+                                if (!((a0 & a1 & a2 & a3) >> 31)) {
 #pragma unroll
-                                    for (int j = 0; j < 16; j++) pm |= ((~r[16 * hh + j]) >> 31) << j;
+                                    for (int j = 0; j < 16; j++) pm |= ((~rc[j]) >> 31) << j;
                                 }
-                                const int lim = lim0 - (32 * c2 + 16 * hh);
+                                const int lim = lim0 - (64 * c4 + 16 * hh);
                                 const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
-                                pass[2 * c2 + hh] = klive ? pm & qmask : 0u;
+                                pass[4 * c4 + hh] = klive ? pm & qmask : 0u;
                             }
                         }
                         // every column is read: the accumulator goes back to the MMA
@@ -2328,13 +2334,16 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         __syncwarp();
                         if (lane == 0) st::mbar_arrive(&acce[a]);
                     }
-                    // compaction when a list fills up; thresholds: own 128th best, published
+                    // every TM_MAINT tiles: compaction of lists that could overflow before the
+                    // next round (a list gains at most 32 entries a tile); thresholds: own
+                    // 128th best, published, and the best any list of the query has published
+                    if (i % TM_MAINT != TM_MAINT - 1) continue;
 #pragma unroll 1
                     for (int sh = 0; sh < 4; sh++) {
                         const int qu = 128 * step + 32 * sh + lane;
                         int cn = ocnt[qu];
                         float th = othr[qu];
-                        const unsigned need = __ballot_sync(0xffffffffu, cn > KCAP - NK);
+                        const unsigned need = __ballot_sync(0xffffffffu, cn > KCAP - 32 * TM_MAINT);
                         if (need) {
                             const float before = th;
                             warp_compact(need, bufs + static_cast<int64_t>(qu) * KCAP, cn, th, nullptr, false);
@@ -2344,7 +2353,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         }
                         const float ef = wthr[qu];
                         float ne = fmaxf(th, ef);
-                        if ((i & 15) == 15 && qu < nlive) ne = fmaxf(ne, thr_of(__ldcg(g.gthr + qbase + qu)));
+                        if (qu < nlive) ne = fmaxf(ne, thr_of(__ldcg(g.gthr + qbase + qu)));
                         if (__any_sync(0xffffffffu, ne > ef)) {
                             if (ne > ef) {
                                 wthr[qu] = ne;
