@@ -1787,14 +1787,16 @@ st_status launch_narrow(st_handle *h, const NarrowArgs &g, int grid) {
 // scan's units (q.k 2^e), so k_knn_merge and k_knn_decode are shared.
 //
 // Roles (448 threads, one CTA per SM, up to 128 registers a thread): warp 13
-// bulk-copies each tile's codes and scales into a 6-stage ring; warps 4-11
-// expand codes into TMEM (a warp per 16 lanes, 16x256b stores, v through a
-// byte permute of the key's four-entry table) and write the keys' filter
-// rows; warp 12 issues the MMAs (two A buffers, two 128-column accumulators);
-// warps 0-3 filter (warp w: lane quadrant w, all 128 columns of each step).
+// bulk-copies each tile's codes and scales into a 6-stage ring; warps 8-11
+// expand codes into TMEM (thread = key = TMEM lane, 32x32b stores; v through
+// a byte permute of the key's four-entry table, eight values per code word
+// from four shared selector computations) and write the keys' filter rows;
+// warp 12 issues the MMAs (two A buffers, two 128-column accumulators); warps
+// 0-7 filter (warp w: lane quadrant w % 4, columns 64 (w / 4) .. of each step).
 constexpr int TQ = 256;                       // queries per unit: two 128-query steps
-constexpr int T_EPI = 4;                      // filter warps: one per TMEM lane quadrant
-constexpr int T_MMA_WARP = T_EPI + N_PROD;    // 12
+constexpr int T_EPI = 8;                      // filter warps: two per TMEM lane quadrant
+constexpr int T_PROD = 4;                     // expanding warps: one per TMEM lane quadrant
+constexpr int T_MMA_WARP = T_EPI + T_PROD;    // 12
 constexpr int T_TMA_WARP = T_MMA_WARP + 1;    // 13
 constexpr int T_THREADS = 32 * (T_TMA_WARP + 1);
 constexpr int T_STAGES = 6;
@@ -1823,16 +1825,27 @@ constexpr int TM_MAINT = 16;                  // tiles between the lists' compac
 static_assert(KCAP - 32 * TM_MAINT >= KTOP && 32 * TM_MAINT <= KCAP - 32 * TM_MAINT,
               "a list must not overflow between two rounds");
 
-// Two f16 values of the key's table {t1:t0} (bytes 2u, 2u + 1: the value for
-// code u) for the two codes in bits 0-3 of x (code a = bits 0-1 to the lower
-// half of the result, b = bits 2-3 to the upper half).
-__device__ __forceinline__ uint32_t tm_pair(uint32_t x, uint32_t t0, uint32_t t1) {
-    // selector nibbles (2a, 2a+1, 2b, 2b+1) = (a + 256 b) * 34 + 0x1010
-    const uint32_t ab = (x & 3u) | ((x << 6) & 0x300u);
-    const uint32_t sel = ab * 34u + 0x1010u;
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(t0), "r"(t1), "r"(sel));
-    return r;
+// The 16 codes of word w (code i in bits 2i, 2i + 1) as eight pairs of f16
+// values from the key's table {t1:t0} (bytes 2u, 2u + 1: the value for code
+// u): out[p] holds codes 2p (lower half) and 2p + 1 (upper half).  The codes
+// are spread one per byte (s_j: codes 4 i + j), bytes paired into (a + 256 b)
+// per 16-bit half, and one multiply-add makes two permute selectors with
+// nibbles (2a, 2a+1, 2b, 2b+1) = (a + 256 b) 34 + 0x1010.
+__device__ __forceinline__ void tm_expand_word(uint32_t w, uint32_t t0, uint32_t t1, uint32_t *out) {
+    const uint32_t s0 = w & 0x03030303u, s1 = (w >> 2) & 0x03030303u;
+    const uint32_t s2 = (w >> 4) & 0x03030303u, s3 = (w >> 6) & 0x03030303u;
+    const uint32_t q0 = __byte_perm(s0, s1, 0x5140) * 34u + 0x10101010u;  // pairs 0 | 2
+    const uint32_t q1 = __byte_perm(s2, s3, 0x5140) * 34u + 0x10101010u;  // pairs 1 | 3
+    const uint32_t q2 = __byte_perm(s0, s1, 0x7362) * 34u + 0x10101010u;  // pairs 4 | 6
+    const uint32_t q3 = __byte_perm(s2, s3, 0x7362) * 34u + 0x10101010u;  // pairs 5 | 7
+    out[0] = __byte_perm(t0, t1, q0 & 0xffffu);
+    out[2] = __byte_perm(t0, t1, q0 >> 16);
+    out[1] = __byte_perm(t0, t1, q1 & 0xffffu);
+    out[3] = __byte_perm(t0, t1, q1 >> 16);
+    out[4] = __byte_perm(t0, t1, q2 & 0xffffu);
+    out[6] = __byte_perm(t0, t1, q2 >> 16);
+    out[5] = __byte_perm(t0, t1, q3 & 0xffffu);
+    out[7] = __byte_perm(t0, t1, q3 >> 16);
 }
 
 // The filter threshold w of a query (f16 bits): -T' / 1024 rounded up, T' =
@@ -1895,19 +1908,19 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < T_STAGES; s++) {
             st::mbar_init(&rfull[s], 1);
-            st::mbar_init(&rempty[s], N_PROD);
+            st::mbar_init(&rempty[s], T_PROD);
         }
         for (int b = 0; b < N_A; b++) {
-            st::mbar_init(&afull[b], N_PROD);
+            st::mbar_init(&afull[b], T_PROD);
             st::mbar_init(&aempty[b], 1);
         }
         for (int a = 0; a < T_NACC; a++) {
             st::mbar_init(&accf[a], 1);
             st::mbar_init(&acce[a], T_EPI);
         }
-        for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], N_PROD);
+        for (int k = 0; k < N_KF; k++) st::mbar_init(&kfr[k], T_PROD);
         for (int j = 0; j < 2; j++) {
-            st::mbar_init(&qready[j], N_PROD);
+            st::mbar_init(&qready[j], T_PROD);
             st::mbar_init(&edone[j], T_EPI);
         }
         st::mbar_init(qfree, 1);
@@ -1955,9 +1968,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         }
     } else if (warp >= T_EPI && warp < T_MMA_WARP) {
         // ------------------------------------------------------------ producers
-        const int pw = warp - T_EPI;  // 0..7: TMEM lanes 32 (warp % 4) + 16 (pw / 4) ..
-        const int quad = warp & 3, half = pw >> 2;
-        const int m = lane & 3;       // the byte of each code word this thread expands
+        const int pw = warp - T_EPI;  // 0..3: TMEM lanes 32 pw .. (warp % 4 = pw)
+        const int quad = warp & 3;
         uint32_t gt = 0, uj = 0;
         bool ok = true;
         for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
@@ -1970,9 +1982,9 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 break;
             float *qc = qconst0 + (uj & 1u) * 4 * TQ;
             const int qbase = (unit % g.nqb) * TQ;
-            // warp pw prepares queries pw, pw + 8, ..; lane l writes dims 8l .. 8l + 7 (one
+            // warp pw prepares queries pw, pw + 4, ..; lane l writes dims 8l .. 8l + 7 (one
             // 16-byte piece of the row's K chunk l / 8) as f16 of q 2^e
-            for (int r = pw; r < TQ; r += N_PROD) {
+            for (int r = pw; r < TQ; r += T_PROD) {
                 const int qg = qbase + r;
                 const bool live = qg < g.nq;
                 const float *qrow = g.q + static_cast<int64_t>(live ? qg : 0) * 256;
@@ -2044,32 +2056,24 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 }
                 const uint8_t *stage = smem + TO_RING + s * N_STAGE_BYTES;
                 const int sofs = static_cast<int>((reinterpret_cast<uintptr_t>(g.scales + tb) & 15u) >> 2);
-                // this thread's two keys: lanes base + lane / 4 and base + 8 + lane / 4 of the warp's 16
-                const int kb = 32 * quad + 16 * half + (lane >> 2);
-                uint4 cw[2][4];
-                uint32_t t0[2], t1[2], xrow[2];
-                float scl[2];
+                const int key = 32 * quad + lane;  // this thread's key: TMEM lane 32 quad + lane
+                const bool in = key < nk;
+                const uint4 *src = reinterpret_cast<const uint4 *>(stage + 64 * key);
+                uint4 cw[4];
 #pragma unroll
-                for (int jj = 0; jj < 2; jj++) {
-                    const int key = kb + 8 * jj;
-                    const bool in = key < nk;
-                    const uint4 *src = reinterpret_cast<const uint4 *>(stage + 64 * key);
-#pragma unroll
-                    for (int w = 0; w < 4; w++) cw[jj][w] = in ? src[w] : make_uint4(0u, 0u, 0u, 0u);
-                    scl[jj] = in ? reinterpret_cast<const float *>(stage + N_CODE_BYTES)[sofs + key] : 0.0f;
-                    // the key's table (u - 1.5) s and filter row (1024, s16)
-                    const float ab = fabsf(scl[jj]);
-                    const bool small = ab < TM_SMALL, normal = !small && ab < TM_BIG;  // NaN: neither
-                    const float sv = normal ? scl[jj] : 0.0f;
-                    const __half2 lo = __floats2half2_rn(-1.5f * sv, -0.5f * sv);
-                    const __half2 hi = __floats2half2_rn(0.5f * sv, 1.5f * sv);
-                    t0[jj] = *reinterpret_cast<const uint32_t *>(&lo);
-                    t1[jj] = *reinterpret_cast<const uint32_t *>(&hi);
-                    const uint32_t s16 = small    ? __half_as_ushort(__float2half_ru(ab * 1024.0f))
-                                         : normal ? __half_as_ushort(__float2half_ru(ab))
-                                                  : TM_HPINF;
-                    xrow[jj] = TM_H1024 | (s16 << 16);
-                }
+                for (int w = 0; w < 4; w++) cw[w] = in ? src[w] : make_uint4(0u, 0u, 0u, 0u);
+                const float scl = in ? reinterpret_cast<const float *>(stage + N_CODE_BYTES)[sofs + key] : 0.0f;
+                // the key's table (u - 1.5) s and filter row (1024, s16)
+                const float ab = fabsf(scl);
+                const bool small = ab < TM_SMALL, normal = !small && ab < TM_BIG;  // NaN: neither
+                const float sv = normal ? scl : 0.0f;
+                const __half2 lo = __floats2half2_rn(-1.5f * sv, -0.5f * sv);
+                const __half2 hi = __floats2half2_rn(0.5f * sv, 1.5f * sv);
+                const uint32_t t0 = *reinterpret_cast<const uint32_t *>(&lo);
+                const uint32_t t1 = *reinterpret_cast<const uint32_t *>(&hi);
+                const uint32_t s16 = small    ? __half_as_ushort(__float2half_ru(ab * 1024.0f))
+                                     : normal ? __half_as_ushort(__float2half_ru(ab))
+                                              : TM_HPINF;
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&rempty[s]);
                 // A buffer b (and its filter rows) is free once the MMAs of tile gt - 2 are
@@ -2080,36 +2084,22 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     ok = false;
                     break;
                 }
-                if (m == 0) {
-#pragma unroll
-                    for (int jj = 0; jj < 2; jj++) {
-                        kf[f * NK + kb + 8 * jj] = scl[jj];
-                        *reinterpret_cast<uint4 *>(smem + TO_X + st::sw128_offset(kb + 8 * jj, 2 * b)) =
-                            make_uint4(xrow[jj], 0u, 0u, 0u);
-                    }
-                }
+                kf[f * NK + key] = scl;
+                *reinterpret_cast<uint4 *>(smem + TO_X + st::sw128_offset(key, 2 * b)) =
+                    make_uint4(TM_H1024 | (s16 << 16), 0u, 0u, 0u);
                 __syncwarp();
                 if (lane == 0) st::mbar_arrive(&kfr[f]);
-                // column c of a key's A row holds dims 2c, 2c + 1; in half h of the row,
-                // repetition j of the 16x256b store gives this thread columns 64h + 8j + 2m +
-                // {0, 1} = byte 32h + 4j + m of the key's codes, its low and high nibble
+                // column c of the key's A row holds dims 2c, 2c + 1: code word j (dims 16 j ..)
+                // fills columns 8 j .. 8 j + 7, 32 columns (four words) per store
+                const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quad) << 16) + b * 128u;
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
+                for (int h = 0; h < 4; h++) {
                     uint32_t v[32];
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-#pragma unroll
-                        for (int jj = 0; jj < 2; jj++) {
-                            const uint4 q4 = cw[jj][2 * h + (j >> 2)];
-                            const uint32_t wsel = (j & 3) == 0 ? q4.x : (j & 3) == 1 ? q4.y : (j & 3) == 2 ? q4.z : q4.w;
-                            const uint32_t x = wsel >> (8 * m);
-                            v[4 * j + 2 * jj] = tm_pair(x, t0[jj], t1[jj]);
-                            v[4 * j + 2 * jj + 1] = tm_pair(x >> 4, t0[jj], t1[jj]);
-                        }
-                    }
-                    const uint32_t taddr =
-                        tmem + (static_cast<uint32_t>(32 * quad + 16 * half) << 16) + b * 128u + 64u * h;
-                    tmem_st_16x256b_x8(taddr, v);
+                    tm_expand_word(cw[h].x, t0, t1, v);
+                    tm_expand_word(cw[h].y, t0, t1, v + 8);
+                    tm_expand_word(cw[h].z, t0, t1, v + 16);
+                    tm_expand_word(cw[h].w, t0, t1, v + 24);
+                    st::tmem_st32(trow + 32u * h, v);
                 }
                 st::tmem_st_wait();
                 st::fence_proxy_async_smem();  // the filter rows, for the MMA's shared-memory reads
@@ -2169,13 +2159,13 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        // Warp w: TMEM lanes 32 w .. (keys), all 128 accumulator columns of each step
-        // (queries 128 step + c of the unit).  Lane l owns the candidate buffer of the
-        // unit's queries 32 s + l (slots s = 0..7); the lists' counts, own 128th-best
-        // scores and effective thresholds live in shared memory, so that the loops over
-        // chunks and slots stay rolled (small code: the four roles share the SM's
-        // instruction cache).
-        const int quad = warp;
+        // Warp w: TMEM lanes 32 (w % 4) .. (keys), accumulator columns 64 (w / 4) .. + 63
+        // of each step (queries 128 step + 64 (w / 4) + c of the unit).  Lane l owns the
+        // candidate buffers of the unit's queries 128 (s / 2) + 64 (w / 4) + 32 (s % 2) + l
+        // (slots s = 0..3); the lists' counts, own 128th-best scores and effective
+        // thresholds live in shared memory, so that the loops over chunks and slots stay
+        // rolled (small code: the four roles share the SM's instruction cache).
+        const int quad = warp & 3, hw = warp >> 2;
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
         uint64_t *bufs = g.cbuf + static_cast<int64_t>(blockIdx.x * N_QUAD + quad) * TQ * KCAP;
@@ -2192,8 +2182,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             const int qbase = (unit % g.nqb) * TQ;
             const int nlive = g.nq - qbase;  // the unit's queries from nlive on are padding
 #pragma unroll 1
-            for (int sl = 0; sl < 8; sl++) {
-                const int qu = 32 * sl + lane;
+            for (int sl = 0; sl < 4; sl++) {
+                const int qu = 128 * (sl >> 1) + 64 * hw + 32 * (sl & 1) + lane;
                 const bool live = qu < nlive;
                 ocnt[qu] = 0;
                 othr[qu] = live ? -INFINITY : INFINITY;
@@ -2225,16 +2215,15 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         break;
                     }
                     st::tc_fence_after();
-                    const uint32_t acc = acc0 + a * 128u;
-                    const int lim0 = nlive - 128 * step;
+                    const uint32_t acc = acc0 + a * 128u + 64u * hw;
+                    const int lim0 = nlive - (128 * step + 64 * hw);
                     if (EXACT) {
                         // full pass: a pair is kept if its filtered accumulator is not negative
-                        uint32_t pass[8];  // per 16-query chunk, bit i: the pair was kept
-#pragma unroll
-                        for (int c4 = 0; c4 < 2; c4++) {
-                            uint32_t r[2][32];  // 64 columns per wait
-                            st::tmem_ld32(acc + 64 * c4, r[0]);
-                            st::tmem_ld32(acc + 64 * c4 + 32, r[1]);
+                        uint32_t pass[4];  // per 16-query chunk, bit i: the pair was kept
+                        {
+                            uint32_t r[2][32];  // the warp's 64 columns, one wait
+                            st::tmem_ld32(acc, r[0]);
+                            st::tmem_ld32(acc + 32, r[1]);
                             st::tmem_ld_wait();
 #pragma unroll
                             for (int hh = 0; hh < 4; hh++) {
@@ -2248,9 +2237,9 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 #pragma unroll
                                     for (int j = 0; j < 16; j++) pm |= ((~rc[j]) >> 31) << j;
                                 }
-                                const int lim = lim0 - (64 * c4 + 16 * hh);
+                                const int lim = lim0 - 16 * hh;
                                 const uint32_t qmask = lim >= 16 ? 0xffffu : lim <= 0 ? 0u : (1u << lim) - 1u;
-                                pass[4 * c4 + hh] = klive ? pm & qmask : 0u;
+                                pass[hh] = klive ? pm & qmask : 0u;
                             }
                         }
                         // every column is read: the accumulator goes back to the MMA
@@ -2259,16 +2248,13 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         if (lane == 0) st::mbar_arrive(&acce[a]);
                         // each kept pair's exact score, by the whole warp; inserted by the
                         // list's owner lane if it reaches the threshold
-                        const unsigned any = __ballot_sync(0xffffffffu, (pass[0] | pass[1] | pass[2] | pass[3] |
-                                                                         pass[4] | pass[5] | pass[6] | pass[7]) != 0u);
+                        const unsigned any = __ballot_sync(0xffffffffu, (pass[0] | pass[1] | pass[2] | pass[3]) != 0u);
                         if (any) {
 #pragma unroll 1
-                            for (int c = 0; c < 8; c++) {
-                                uint32_t pc = pass[0];
-#pragma unroll
-                                for (int j = 1; j < 8; j++) pc = c == j ? pass[j] : pc;
+                            for (int c = 0; c < 4; c++) {
+                                const uint32_t pc = c == 0 ? pass[0] : c == 1 ? pass[1] : c == 2 ? pass[2] : pass[3];
                                 unsigned lanes = __ballot_sync(0xffffffffu, pc != 0u);
-                                const int q0 = 128 * step + 16 * c;
+                                const int q0 = 128 * step + 64 * hw + 16 * c;
                                 while (lanes) {
                                     const int L = __ffs(lanes) - 1;
                                     lanes &= lanes - 1;
@@ -2297,11 +2283,11 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         // sample pass: acc' is a lower bound of the pair's score; a pair enters
                         // its list, lowered by 2^-12, if the bound reaches the threshold
 #pragma unroll 1
-                        for (int c = 0; c < 8; c++) {
+                        for (int c = 0; c < 4; c++) {
                             uint32_t r[16];
                             st::tmem_ld16(acc + 16 * c, r);
                             st::tmem_ld_wait();
-                            const int q0 = 128 * step + 16 * c;
+                            const int q0 = 128 * step + 64 * hw + 16 * c;
                             uint32_t pm = 0u;
 #pragma unroll
                             for (int i4 = 0; i4 < 16; i4 += 4) {
@@ -2339,8 +2325,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     // 128th best, published, and the best any list of the query has published
                     if (i % TM_MAINT != TM_MAINT - 1) continue;
 #pragma unroll 1
-                    for (int sh = 0; sh < 4; sh++) {
-                        const int qu = 128 * step + 32 * sh + lane;
+                    for (int sh = 0; sh < 2; sh++) {
+                        const int qu = 128 * step + 64 * hw + 32 * sh + lane;
                         int cn = ocnt[qu];
                         float th = othr[qu];
                         const unsigned need = __ballot_sync(0xffffffffu, cn > KCAP - 32 * TM_MAINT);
@@ -2372,8 +2358,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             if (!ok) break;
             const int split = unit / g.nqb;
 #pragma unroll 1
-            for (int sl = 0; sl < 8; sl++) {
-                const int qu = 32 * sl + lane;
+            for (int sl = 0; sl < 4; sl++) {
+                const int qu = 128 * (sl >> 1) + 64 * hw + 32 * (sl & 1) + lane;
                 int cn = ocnt[qu];
                 float th = othr[qu];
                 uint64_t *my_out =
