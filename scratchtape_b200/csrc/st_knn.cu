@@ -180,17 +180,33 @@ __device__ __forceinline__ void lds_f32x16(uint32_t addr, float (&v)[16]) {
 // stopped as soon as the count is exactly k (keys are distinct, so the full
 // 64-bit search ends at the k-th largest key, where the count is k).
 __device__ __forceinline__ uint64_t warp_select_threshold(const uint64_t (&v)[32], int k) {
-    uint64_t prefix = 0;
-#pragma unroll 1
-    for (int bit = 63; bit >= 0; --bit) {
-        const uint64_t cand = prefix | (1ull << bit);
-        int c = 0;
+    // the leading bits that every non-zero entry shares are the prefix's: the search
+    // starts below them (entries are distinct, so with more than k of them some bit differs)
+    uint64_t a = ~0ull, o = 0ull;
 #pragma unroll
-        for (int i = 0; i < 32; i++) c += v[i] >= cand ? 1 : 0;
-        c = warp_sum(c);
-        if (c >= k) {
+    for (int i = 0; i < 32; i++)
+        if (v[i] != 0ull) {
+            a &= v[i];
+            o |= v[i];
+        }
+    const uint64_t all = (static_cast<uint64_t>(__reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a >> 32))) << 32) |
+                         __reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a));
+    const uint64_t any = (static_cast<uint64_t>(__reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o >> 32))) << 32) |
+                         __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o));
+    const uint64_t diff = all ^ any;
+    if (diff == 0ull) return all;
+    const int top = 63 - __clzll(static_cast<long long>(diff));
+    uint64_t prefix = all & ~((2ull << top) - 1ull);
+#pragma unroll 1
+    for (int bit = top; bit >= 0; --bit) {
+        const uint64_t cand = prefix | (1ull << bit);
+        unsigned c = 0;
+#pragma unroll
+        for (int i = 0; i < 32; i++) c += v[i] >= cand ? 1u : 0u;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (c >= static_cast<unsigned>(k)) {
             prefix = cand;
-            if (c == k) break;
+            if (c == static_cast<unsigned>(k)) break;
         }
     }
     return prefix;
@@ -1106,6 +1122,11 @@ struct NarrowArgs {
     uint64_t *unit_out;    // [splits * 4][nq_pad][KTOP]: list (split, quadrant) of every query
     uint32_t *gthr;        // [nq_pad] order-preserving bits of the best published 128th score (0: none)
     int exact;             // k_knn_tmem: 1 = exact scores (the full pass), 0 = lower bounds (a sample pass)
+    // k_knn_tmem: the pass's (query block, sample) sequence, block-major, seg_len samples per block
+    // (sample j = tile j * unit_step), flat_len = nqb * seg_len, cut into gridDim.x equal ranges;
+    // nslot lists per (query, quadrant) in unit_out
+    int64_t flat_len, seg_len;
+    int nslot;
     int *status;
 };
 
@@ -1182,6 +1203,47 @@ __device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64
     const int64_t t = static_cast<int64_t>(unit / g.nqb) * g.unit_step + i * g.tile_step;
     if (t >= g.n_tiles) return false;
     tb = t * NK;
+    nk = static_cast<int>(g.n_keys - tb < NK ? g.n_keys - tb : NK);
+    return true;
+}
+
+// k_knn_tmem's work split: CTA c takes the flat range [c L / G, (c + 1) L / G) of
+// the pass's (query block, sample) sequence (L = g.flat_len, G = gridDim.x,
+// block-major, g.seg_len samples per block), so every CTA has the same number
+// of tiles and crosses at most a few block boundaries.  A piece is the part of
+// the range inside one query block; the CTAs that cover block b write their
+// lists to slots 0, 1, .. in range order (slot = c - the CTA holding b's first
+// sample).
+struct TPiece {
+    int64_t pos, end;  // the CTA's remaining flat range
+    int64_t j0, j1;    // the piece's samples of block qb
+    int qb, slot;
+};
+__device__ __forceinline__ int64_t tm_seg_start(const NarrowArgs &g, int64_t c) {
+    return c * g.flat_len / gridDim.x;
+}
+__device__ __forceinline__ void tm_begin(const NarrowArgs &g, TPiece &p) {
+    p.pos = tm_seg_start(g, blockIdx.x);
+    p.end = tm_seg_start(g, blockIdx.x + 1);
+}
+__device__ __forceinline__ bool tm_next(const NarrowArgs &g, TPiece &p) {
+    if (p.pos >= p.end) return false;
+    const int64_t qb = p.pos / g.seg_len;
+    p.qb = static_cast<int>(qb);
+    p.j0 = p.pos - qb * g.seg_len;
+    p.j1 = min(g.seg_len, p.j0 + (p.end - p.pos));
+    p.pos += p.j1 - p.j0;
+    // the last CTA c0 with c0 L / G <= x (x = the block's first flat index): c0 = ceil((x + 1) G / L) - 1
+    const int64_t x = qb * g.seg_len;
+    const int64_t c0 = ((x + 1) * gridDim.x + g.flat_len - 1) / g.flat_len - 1;
+    p.slot = static_cast<int>(blockIdx.x - c0);
+    return true;
+}
+// Tile i of piece p: sample j0 + i is tile (j0 + i) * unit_step.
+__device__ __forceinline__ bool tm_tile(const NarrowArgs &g, const TPiece &p, int64_t i, int64_t &tb, int &nk) {
+    const int64_t j = p.j0 + i;
+    if (j >= p.j1) return false;
+    tb = j * g.unit_step * NK;
     nk = static_cast<int>(g.n_keys - tb < NK ? g.n_keys - tb : NK);
     return true;
 }
@@ -1943,10 +2005,12 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         if (lane == 0) {
             uint32_t gt = 0;
             bool ok = true;
-            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x) {
+            TPiece pc;
+            tm_begin(g, pc);
+            while (ok && tm_next(g, pc)) {
                 int64_t tb;
                 int nk;
-                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                for (int64_t i = 0; tm_tile(g, pc, i, tb, nk); ++i, ++gt) {
                     const uint32_t s = gt % T_STAGES;
                     if (gt >= T_STAGES &&
                         !nwait(&rempty[s], ((gt / T_STAGES) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
@@ -1972,16 +2036,18 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         const int quad = warp & 3;
         uint32_t gt = 0, uj = 0;
         bool ok = true;
-        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+        TPiece pc;
+        tm_begin(g, pc);
+        for (; ok && tm_next(g, pc); ++uj) {
             // the query tiles and filter rows are rewritten once the MMAs and the
             // epilogue (which writes thresholds into the filter rows) are done with
-            // the previous unit
+            // the previous piece
             if (uj >= 1 && !nwait(qfree, (uj - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) break;
             if (uj >= 1 &&
                 !nwait(&edone[(uj - 1) & 1u], ((uj - 1) >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC))
                 break;
             float *qc = qconst0 + (uj & 1u) * 4 * TQ;
-            const int qbase = (unit % g.nqb) * TQ;
+            const int qbase = pc.qb * TQ;
             // warp pw prepares queries pw, pw + 4, ..; lane l writes dims 8l .. 8l + 7 (one
             // 16-byte piece of the row's K chunk l / 8) as f16 of q 2^e
             for (int r = pw; r < TQ; r += T_PROD) {
@@ -2048,7 +2114,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
 
             int64_t tb;
             int nk;
-            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+            for (int64_t i = 0; tm_tile(g, pc, i, tb, nk); ++i, ++gt) {
                 const uint32_t s = gt % T_STAGES, b = gt % N_A, f = gt % N_KF;
                 if (!nwait(&rfull[s], (gt / T_STAGES) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
                     ok = false;
@@ -2115,12 +2181,14 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             const uint32_t qbuf = st::smem_u32(smem + TO_Q), xbuf = st::smem_u32(smem + TO_X);
             uint32_t gt = 0, gs = 0, uj = 0;
             bool ok = true;
-            for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+            TPiece pc;
+            tm_begin(g, pc);
+            for (; ok && tm_next(g, pc); ++uj) {
                 if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
                 st::tc_fence_after();
                 int64_t tb;
                 int nk;
-                for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+                for (int64_t i = 0; tm_tile(g, pc, i, tb, nk); ++i, ++gt) {
                     const uint32_t b = gt % N_A;
                     if (!nwait(&afull[b], (gt / N_A) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) {
                         ok = false;
@@ -2175,11 +2243,13 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         const uint32_t acc0 = tmem + lane_addr + ACC_COL;
         uint32_t gt = 0, gs = 0, uj = 0;
         bool ok = true;
-        for (int unit = blockIdx.x; unit < g.units && ok; unit += gridDim.x, ++uj) {
+        TPiece pc;
+        tm_begin(g, pc);
+        for (; ok && tm_next(g, pc); ++uj) {
             if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
             const float *qc = qconst0 + (uj & 1u) * 4 * TQ;
             const float *qc_p = qc + TQ, *qc_live = qc + 2 * TQ, *qc_mag = qc + 3 * TQ;
-            const int qbase = (unit % g.nqb) * TQ;
+            const int qbase = pc.qb * TQ;
             const int nlive = g.nq - qbase;  // the unit's queries from nlive on are padding
 #pragma unroll 1
             for (int sl = 0; sl < 4; sl++) {
@@ -2197,7 +2267,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             __syncwarp();
             int64_t tb;
             int nk;
-            for (int64_t i = 0; narrow_tile(g, unit, i, tb, nk); ++i, ++gt) {
+            for (int64_t i = 0; tm_tile(g, pc, i, tb, nk); ++i, ++gt) {
                 const uint32_t f = gt % N_KF;
                 if (!nwait(&kfr[f], (gt / N_KF) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                     ok = false;
@@ -2356,14 +2426,18 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 if (!ok) break;
             }
             if (!ok) break;
-            const int split = unit / g.nqb;
+            if (pc.slot < 0 || pc.slot >= g.nslot) {  // the host sized nslot for every piece: not reached
+                st::set_status(g.status, st::DEV_BAD_ARG);
+                *abort_flag = 1;
+                break;
+            }
 #pragma unroll 1
             for (int sl = 0; sl < 4; sl++) {
                 const int qu = 128 * (sl >> 1) + 64 * hw + 32 * (sl & 1) + lane;
                 int cn = ocnt[qu];
                 float th = othr[qu];
                 uint64_t *my_out =
-                    g.unit_out + ((static_cast<int64_t>(split) * N_QUAD + quad) * g.nq_pad + qbase + qu) * KTOP;
+                    g.unit_out + ((static_cast<int64_t>(pc.slot) * N_QUAD + quad) * g.nq_pad + qbase + qu) * KTOP;
                 const unsigned need = __ballot_sync(0xffffffffu, qu < nlive);
                 warp_compact(need, bufs + static_cast<int64_t>(qu) * KCAP, cn, th, my_out, true);
             }
@@ -2408,21 +2482,35 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
     if (!out_keys) return h->fail(ST_INVALID_ARG, "%s: null output", who);
     cudaSetDevice(h->device);
     if (!ranges && dim == 256 && nq > NQ && prec == 0 && mode == 0 && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
-        // more than 32 EXACT dot-product queries at dim 256: keys in TMEM (k_knn_tmem),
-        // units of (key split, 256 queries), about eight units per SM
+        // more than 32 EXACT dot-product queries at dim 256: keys in TMEM (k_knn_tmem).
+        // Every pass cuts its (query block of 256, 128-key tile) sequence into one
+        // equal range per CTA; the CTAs covering a block each leave one list per
+        // (query, lane quadrant), in slots 0 .. nslot - 1 (unused slots stay zero).
         const int nqb = static_cast<int>((nq + TQ - 1) / TQ);
         const int64_t nq_pad = static_cast<int64_t>(nqb) * TQ;
         const int64_t tiles = (n_keys + NK - 1) / NK;
-        int64_t splits = std::max<int64_t>(1, (8LL * h->num_sms + nqb - 1) / nqb);
-        splits = std::min<int64_t>(splits, tiles);
-        const int64_t tps = (tiles + splits - 1) / splits;
-        splits = (tiles + tps - 1) / tps;
-        const int64_t units = splits * nqb;
-        if (units > (1LL << 30)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
-        const int grid = static_cast<int>(std::min<int64_t>(units, h->num_sms));
+        if (static_cast<int64_t>(nqb) * tiles > (1LL << 50)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
+        // a pass over `samples` tiles per block: its grid and the slots its pieces need
+        auto plan = [&](int64_t samples, int &grid, int &nslot) {
+            const int64_t flat = static_cast<int64_t>(nqb) * samples;
+            grid = static_cast<int>(std::min<int64_t>(flat, h->num_sms));
+            const int64_t shortest = flat / grid;  // every CTA's range holds at least this many samples
+            nslot = static_cast<int>((samples + shortest - 1) / shortest + 1);
+        };
+        int grid_full, nslot_full;
+        plan(tiles, grid_full, nslot_full);
+        int nslot_max = nslot_full;
+        for (int64_t stride : {int64_t(1024), int64_t(16)}) {
+            const int64_t sample = (tiles + stride - 1) / stride;
+            if (sample * nqb < 4 * h->num_sms || sample >= tiles) continue;
+            int gr, ns;
+            plan(sample, gr, ns);
+            nslot_max = std::max(nslot_max, ns);
+        }
+        const int grid_cap = h->num_sms;
         uint64_t *cbuf = static_cast<uint64_t *>(
-            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid * N_QUAD * TQ * KCAP));
-        const size_t out_bytes = sizeof(uint64_t) * splits * N_QUAD * nq_pad * KTOP;
+            st_scratch(h, SLOT_KNN_CAND, sizeof(uint64_t) * grid_cap * N_QUAD * TQ * KCAP));
+        const size_t out_bytes = sizeof(uint64_t) * nslot_max * N_QUAD * nq_pad * KTOP;
         const size_t seed_bytes = sizeof(uint64_t) * nq_pad * KTOP;
         constexpr int MERGE_GROUPS = 16;
         const size_t tmp_bytes = sizeof(uint64_t) * MERGE_GROUPS * nq_pad * KTOP;
@@ -2448,36 +2536,37 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         g.unit_out = unit_out;
         g.gthr = gthr;
         g.status = h->d_status;
-        auto run = [&](const NarrowArgs &a, int gr) { return launch_tmem(h, a, gr); };
-        // the narrow scan's two sample passes seed the thresholds (every 1024th, then
-        // every 16th tile), with the full pass's key splits
+        // one pass over every stride-th tile: lists zeroed, scan, merge into `dst`
+        auto pass = [&](int64_t stride, int exact, uint64_t *dst) -> st_status {
+            const int64_t samples = (tiles + stride - 1) / stride;
+            int grid, nslot;
+            plan(samples, grid, nslot);
+            NarrowArgs a = g;
+            a.exact = exact;
+            a.unit_step = stride;
+            a.seg_len = samples;
+            a.flat_len = static_cast<int64_t>(nqb) * samples;
+            a.nslot = nslot;
+            ST_CHECK_CUDA(h, cudaMemsetAsync(unit_out, 0, sizeof(uint64_t) * nslot * N_QUAD * nq_pad * KTOP,
+                                             h->stream));
+            st_status r = launch_tmem(h, a, grid);
+            if (r != ST_OK) return r;
+            return merge_lists(h, unit_out, static_cast<int64_t>(nslot) * N_QUAD, nq_pad * KTOP, nq, merge_tmp,
+                               MERGE_GROUPS, dst);
+        };
+        // two sample passes seed the thresholds (every 1024th, then every 16th tile):
+        // a list's 128th best over a subset bounds the final 128th best from below
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
-            if (sample < 2 * h->num_sms) continue;
-            NarrowArgs gs = g;
-            gs.exact = 0;
-            const int64_t gsplits = std::min<int64_t>(splits, sample);
-            gs.units = static_cast<int>(gsplits * nqb);
-            gs.unit_step = stride;
-            gs.tile_step = stride * gsplits;
-            gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
-            s = run(gs, static_cast<int>(std::min<int64_t>(gs.units, h->num_sms)));
-            if (s != ST_OK) return s;
-            s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
+            if (sample * nqb < 4 * h->num_sms || sample >= tiles) continue;
+            s = pass(stride, 0, seed_keys);
             if (s != ST_OK) return s;
             k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
                                                                                        static_cast<int>(nq), gthr);
             s = st_after_launch(h, "k_knn_seed");
             if (s != ST_OK) return s;
         }
-        g.units = static_cast<int>(units);
-        g.unit_step = tps;
-        g.tile_step = 1;
-        g.tiles_per_unit = tps;
-        g.exact = 1;
-        s = run(g, grid);
-        if (s != ST_OK) return s;
-        return merge_lists(h, unit_out, splits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, out_keys);
+        return pass(1, 1, out_keys);
     }
     if (!ranges && dim == 256 && nq <= NQ && (reinterpret_cast<uintptr_t>(scales) & 3u) == 0) {
         // dim 256, up to 32 queries: the keys-on-M scan (keys as the kind::i8 A
