@@ -737,6 +737,144 @@ __global__ void __launch_bounds__(256) k_knn_merge(const uint64_t *lists, int64_
     }
 }
 
+// The same merge with every candidate of the block's query in registers (at
+// most 256 MR of them): the 8-bit digit passes start at the first byte where
+// the candidates differ, count into a shared histogram that one warp scans in
+// parallel, and read no global memory after the first load.
+constexpr int MR = 32;  // candidates per thread: 64 lists of 128
+__global__ void __launch_bounds__(256) k_knn_merge_reg(const uint64_t *lists, int64_t n_lists, int64_t list_stride,
+                                                       uint64_t *out) {
+    __shared__ int hist[256];
+    __shared__ uint64_t sel[KTOP];
+    __shared__ uint32_t red[2][8][2];
+    __shared__ int s_digit, s_need, s_count;
+    const int64_t q = blockIdx.x;
+    if (gridDim.y > 1) {
+        const int64_t per = (n_lists + gridDim.y - 1) / gridDim.y;
+        const int64_t l0 = blockIdx.y * per;
+        n_lists = l0 < n_lists ? (n_lists - l0 < per ? n_lists - l0 : per) : 0;
+        lists += l0 * list_stride;
+        out += static_cast<int64_t>(blockIdx.y) * gridDim.x * KTOP;
+    }
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int total = static_cast<int>(n_lists) * KTOP;
+    uint64_t v[MR];
+    uint64_t a = ~0ull, o = 0ull;
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        const int i = r * 256 + tid;
+        v[r] = i < total ? __ldg(lists + (i / KTOP) * list_stride + q * KTOP + (i % KTOP)) : 0ull;
+        if (v[r] != 0ull) {
+            a &= v[r];
+            o |= v[r];
+        }
+    }
+    // the bits every nonzero candidate shares
+    uint32_t r0 = __reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a)),
+             r1 = __reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a >> 32));
+    uint32_t r2 = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o)),
+             r3 = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o >> 32));
+    if (lane == 0) {
+        red[0][wid][0] = r0;
+        red[0][wid][1] = r1;
+        red[1][wid][0] = r2;
+        red[1][wid][1] = r3;
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int r = 0; r < MR; r++) cnt += v[r] != 0ull ? 1 : 0;
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    if (lane == 0) atomicAdd(&s_count, cnt);
+    uint64_t all = ~0ull, any = 0ull;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        all &= (static_cast<uint64_t>(red[0][w][1]) << 32) | red[0][w][0];
+        any |= (static_cast<uint64_t>(red[1][w][1]) << 32) | red[1][w][0];
+    }
+    __syncthreads();
+    const int n_nonzero = s_count;
+    __syncthreads();  // every thread has read the count before it is reused
+    uint64_t T;
+    if (n_nonzero <= KTOP) {
+        T = 1ull;  // every nonzero candidate
+    } else {
+        const uint64_t diff = all ^ any;  // nonzero: the candidates are distinct
+        const int top_byte = (63 - __clzll(static_cast<long long>(diff))) >> 3;
+        uint64_t mask = top_byte == 7 ? 0ull : ~0ull << (8 * (top_byte + 1));
+        uint64_t prefix = all & mask;
+        int need = KTOP;
+        for (int pass = top_byte; pass >= 0; --pass) {
+            hist[tid] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < MR; r++)
+                if (v[r] != 0ull && (v[r] & mask) == prefix) atomicAdd(&hist[(v[r] >> (8 * pass)) & 0xff], 1);
+            __syncthreads();
+            if (wid == 0) {
+                // lane l holds bins 255 - 8l .. 248 - 8l; counts at or above each bin, top down
+                int c[8], s8 = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    c[j] = hist[255 - 8 * lane - j];
+                    s8 += c[j];
+                }
+                int incl = s8;  // inclusive prefix over lanes (higher bins first)
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, incl, off);
+                    if (lane >= off) incl += t;
+                }
+                int acc = incl - s8;  // candidates in bins above this lane's
+                int d = -1, left = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    if (d < 0 && acc + c[j] >= need) {
+                        d = 255 - 8 * lane - j;
+                        left = need - acc;
+                    }
+                    acc += c[j];
+                }
+                const unsigned has = __ballot_sync(0xffffffffu, d >= 0);
+                const int src = __ffs(has) - 1;  // the highest bin reaching `need` is in the first such lane
+                if (lane == src) {
+                    s_digit = d;
+                    s_need = left;
+                }
+            }
+            __syncthreads();
+            prefix |= static_cast<uint64_t>(s_digit) << (8 * pass);
+            mask |= 0xffull << (8 * pass);
+            need = s_need;
+            __syncthreads();
+        }
+        T = prefix;
+    }
+    if (tid == 0) s_count = 0;
+    if (tid < KTOP) sel[tid] = 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        if (v[r] != 0ull && v[r] >= T) {
+            const int p = atomicAdd(&s_count, 1);
+            if (p < KTOP) sel[p] = v[r];
+        }
+    }
+    __syncthreads();
+    if (tid < KTOP) {
+        const uint64_t x = sel[tid];
+        int rank = 0;
+        for (int j = 0; j < KTOP; j++) rank += sel[j] > x ? 1 : 0;
+        if (x == 0ull) {
+            int zeros_before = 0;
+            for (int j = 0; j < tid; j++) zeros_before += sel[j] == 0ull ? 1 : 0;
+            rank += zeros_before;
+        }
+        out[q * KTOP + rank] = x;
+    }
+}
+
 // Keys -> (score, index).  DOT: q.k (EXACT divides out the query's 2^e);
 // L2: |q|^2 - (2 q.k - |k|^2), clamped at 0.  Empty slots: (-inf | +inf, -1).
 template <int MODE, int PREC>
@@ -1780,6 +1918,22 @@ __global__ void k_knn_seed(const uint64_t *keys, int nq, uint32_t *gthr) {
 // then one merge of the G partial lists.
 st_status merge_lists(st_handle *h, const uint64_t *lists, int64_t n_lists, int64_t list_stride, int64_t nq,
                       uint64_t *tmp, int groups, uint64_t *out) {
+    constexpr int64_t REG_LISTS = 256 * MR / KTOP;  // lists one k_knn_merge_reg block holds
+    if (n_lists > REG_LISTS && tmp && n_lists <= groups * REG_LISTS) {
+        // groups of at most REG_LISTS lists, then one merge of the groups
+        const int64_t gr = (n_lists + REG_LISTS - 1) / REG_LISTS;
+        k_knn_merge_reg<<<dim3(static_cast<unsigned>(nq), static_cast<unsigned>(gr)), 256, 0, h->stream>>>(
+            lists, n_lists, list_stride, tmp);
+        st_status s = st_after_launch(h, "k_knn_merge_reg");
+        if (s != ST_OK) return s;
+        lists = tmp;
+        n_lists = gr;
+        list_stride = nq * KTOP;
+    }
+    if (n_lists <= REG_LISTS) {
+        k_knn_merge_reg<<<static_cast<unsigned>(nq), 256, 0, h->stream>>>(lists, n_lists, list_stride, out);
+        return st_after_launch(h, "k_knn_merge_reg");
+    }
     if (n_lists > 2 * groups && tmp) {
         k_knn_merge<<<dim3(static_cast<unsigned>(nq), static_cast<unsigned>(groups)), 256, 0, h->stream>>>(
             lists, n_lists, list_stride, tmp);
@@ -1917,23 +2071,44 @@ __device__ __forceinline__ uint32_t tm_w_bits(float t, float mag) {
     return __half_as_ushort(__float2half_ru(-tl * 0.0009765625f));
 }
 
-// The exact stored score of one (key, query) pair, computed by the whole warp
-// (every lane calls it with the same arguments): key codes `codes` (64 bytes)
-// and scale s, query row qrow (f32) with p2e = 2^e.  Lane l takes dims 8l ..
-// 8l + 7 (its two code bytes, two float4 of the query); products and sums in
-// f64, rounded once: s sum (u - 1.5) q 2^e.
-__device__ __forceinline__ float tm_exact_warp(const uint8_t *codes, float s, const float *qrow, float p2e) {
+// The exact stored scores of up to TM_BATCH (key, query) pairs, computed by the
+// whole warp (every lane calls it with the same arguments; n warp-uniform,
+// entries from n on repeat pair 0 and are ignored): key codes `codes` (64
+// bytes) and scale s, query row qrow (f32) with p2e = 2^e.  Lane l takes dims
+// 8l .. 8l + 7 (its two code bytes, two float4 of the query); products and
+// sums in f64, rounded once: s sum (u - 1.5) q 2^e.  The loads of all pairs
+// are issued before any arithmetic and the shuffle reductions interleave, so
+// the pairs' L2 latencies overlap.
+constexpr int TM_BATCH = 2;  // kept pairs scored together (more spills the filter warps' registers)
+__device__ __forceinline__ void tm_exact_warp_batch(int n, const uint8_t *const (&codes)[TM_BATCH], const float (&s)[TM_BATCH],
+                                               const float *const (&qrow)[TM_BATCH], const float (&p2e)[TM_BATCH],
+                                               float (&out)[TM_BATCH]) {
     const int lane = threadIdx.x & 31;
-    const uint32_t cb = __ldg(reinterpret_cast<const uint16_t *>(codes) + lane);
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane);
-    const float4 b = __ldg(reinterpret_cast<const float4 *>(qrow) + 2 * lane + 1);
-    const float q[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    double acc = 0.0;
+    uint32_t cb[TM_BATCH];
+    float4 a[TM_BATCH], b[TM_BATCH];
 #pragma unroll
-    for (int i = 0; i < 8; i++) acc += (static_cast<double>((cb >> (2 * i)) & 3u) - 1.5) * static_cast<double>(q[i]);
+    for (int j = 0; j < TM_BATCH; j++) {
+        const uint8_t *cp = j < n ? codes[j] : codes[0];  // constant indices: no local-memory array
+        const float *qp = j < n ? qrow[j] : qrow[0];
+        cb[j] = __ldg(reinterpret_cast<const uint16_t *>(cp) + lane);
+        a[j] = __ldg(reinterpret_cast<const float4 *>(qp) + 2 * lane);
+        b[j] = __ldg(reinterpret_cast<const float4 *>(qp) + 2 * lane + 1);
+    }
+    double acc[TM_BATCH];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    return static_cast<float>(acc * static_cast<double>(s) * static_cast<double>(p2e));
+    for (int j = 0; j < TM_BATCH; j++) {
+        const float q[8] = {a[j].x, a[j].y, a[j].z, a[j].w, b[j].x, b[j].y, b[j].z, b[j].w};
+        double t = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) t += (static_cast<double>((cb[j] >> (2 * i)) & 3u) - 1.5) * static_cast<double>(q[i]);
+        acc[j] = t;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < TM_BATCH; j++) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+#pragma unroll
+    for (int j = 0; j < TM_BATCH; j++) out[j] = static_cast<float>(acc[j] * static_cast<double>(s[j]) * static_cast<double>(p2e[j]));
 }
 
 // r[i] for a warp-uniform runtime i (a select chain: indexing the register
@@ -2320,6 +2495,28 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         // list's owner lane if it reaches the threshold
                         const unsigned any = __ballot_sync(0xffffffffu, (pass[0] | pass[1] | pass[2] | pass[3]) != 0u);
                         if (any) {
+                            // kept pairs in (chunk, key lane, query) order, scored TM_BATCH at a time;
+                            // the owner lane of each query inserts in that order
+                            int np = 0, pq[TM_BATCH], pk[TM_BATCH];
+                            const uint8_t *pc_codes[TM_BATCH];
+                            const float *pc_q[TM_BATCH];
+                            float pc_s[TM_BATCH], pc_p[TM_BATCH], e4[TM_BATCH];
+                            auto flush = [&]() {
+                                tm_exact_warp_batch(np, pc_codes, pc_s, pc_q, pc_p, e4);
+#pragma unroll
+                                for (int j = 0; j < TM_BATCH; j++) {
+                                    if (j >= np) break;
+                                    const int qu = pq[j];
+                                    if (lane == (qu & 31) && e4[j] >= wthr[qu]) {
+                                        const int base = ocnt[qu];
+                                        bufs[static_cast<int64_t>(qu) * KCAP + base] =
+                                            make_key(e4[j], g.index_base + static_cast<uint32_t>(tb) +
+                                                                static_cast<uint32_t>(pk[j]));
+                                        ocnt[qu] = base + 1;
+                                    }
+                                }
+                                np = 0;
+                            };
 #pragma unroll 1
                             for (int c = 0; c < 4; c++) {
                                 const uint32_t pc = c == 0 ? pass[0] : c == 1 ? pass[1] : c == 2 ? pass[2] : pass[3];
@@ -2332,22 +2529,28 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                                     const float sL = __shfl_sync(0xffffffffu, scale, L);
                                     const int keyL = 32 * quad + L;
                                     const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
-                                    const uint32_t idxL =
-                                        g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(keyL);
                                     while (bits) {
                                         const int ib = __ffs(bits) - 1;
                                         bits &= bits - 1;
                                         const int qu = q0 + ib;
-                                        const float e = tm_exact_warp(
-                                            kcodes, sL, g.q + static_cast<int64_t>(qbase + qu) * 256, qc_p[qu]);
-                                        if (lane == 16 * (c & 1) + ib && e >= wthr[qu]) {
-                                            const int base = ocnt[qu];
-                                            bufs[static_cast<int64_t>(qu) * KCAP + base] = make_key(e, idxL);
-                                            ocnt[qu] = base + 1;
+                                        const float *qrow = g.q + static_cast<int64_t>(qbase + qu) * 256;
+                                        const float p2e = qc_p[qu];
+#pragma unroll
+                                        for (int j = 0; j < TM_BATCH; j++) {  // constant indices: registers
+                                            if (j == np) {
+                                                pq[j] = qu;
+                                                pk[j] = keyL;
+                                                pc_codes[j] = kcodes;
+                                                pc_q[j] = qrow;
+                                                pc_s[j] = sL;
+                                                pc_p[j] = p2e;
+                                            }
                                         }
+                                        if (++np == TM_BATCH) flush();
                                     }
                                 }
                             }
+                            if (np) flush();
                         }
                     } else {
                         // sample pass: acc' is a lower bound of the pair's score; a pair enters
