@@ -13,7 +13,11 @@
 //   lists (st_knn_merge_keys) and decodes them.  Exact: a query's global best k
 //   lie in the union of the shards' best k.  This is k_merge_parts
 //   (src/gpu_step/knn.rs:661-715) across GPUs instead of across one GPU's
-//   key parts.
+//   key parts.  The scans that seed their per-query thresholds from samples
+//   of the keys take the maximum of each seed over the ranks (two small
+//   ncclAllReduce MAX calls, nq x 4 bytes): any rank's 128th best over a sample
+//   bounds the global 128th best from below, so each rank filters as tightly
+//   as one GPU holding every key would.
 //
 // NCCL is resolved at run time (dlopen of libnccl.so.2, preferring a copy the
 // process has already loaded -- e.g. torch's -- so a communicator made by the
@@ -79,6 +83,28 @@ const NcclApi &nccl() {
 
 constexpr int64_t KLIST = 128;  // entries per query in a best-128 list
 
+// The handle's threshold exchange during a sharded scan: the per-query
+// published 128th-best scores (order-preserving u32) become their maximum over
+// the ranks, in place, on the handle's stream.
+st_status max_over_ranks(st_handle *h, uint32_t *gthr, int64_t nq, void *ctx) {
+    ST_CHECK_NCCL(h, nccl().all_reduce(gthr, gthr, static_cast<size_t>(nq), ncclUint32, ncclMax,
+                                       static_cast<ncclComm_t>(ctx), h->stream));
+    return ST_OK;
+}
+
+// Clears the handle's threshold exchange when the sharded call returns.
+struct ExchangeScope {
+    st_handle *h;
+    ExchangeScope(st_handle *hh, void *comm) : h(hh) {
+        h->thr_exchange = max_over_ranks;
+        h->thr_ctx = comm;
+    }
+    ~ExchangeScope() {
+        h->thr_exchange = nullptr;
+        h->thr_ctx = nullptr;
+    }
+};
+
 }  // namespace
 
 extern "C" st_status st_nccl_unique_id(uint8_t *out) {
@@ -143,18 +169,36 @@ extern "C" st_status st_knn_search_sharded(st_handle *h, const uint8_t *codes, c
     int world = 0;
     ST_CHECK_NCCL(h, api.comm_count(c, &world));
     const size_t list_bytes = sizeof(uint64_t) * static_cast<size_t>(nq) * KLIST;
-    uint8_t *buf = static_cast<uint8_t *>(st_scratch(h, SLOT_COMM, list_bytes * (world + 2)));
+    const size_t thr_bytes = (sizeof(uint32_t) * static_cast<size_t>(nq) + 255) & ~size_t(255);
+    uint8_t *buf = static_cast<uint8_t *>(st_scratch(h, SLOT_COMM, list_bytes * (world + 2) + thr_bytes));
     if (!buf) return ST_NO_MEMORY;
     uint64_t *local = reinterpret_cast<uint64_t *>(buf);
     uint64_t *gathered = reinterpret_cast<uint64_t *>(buf + list_bytes);
     uint64_t *merged = reinterpret_cast<uint64_t *>(buf + list_bytes * (world + 1));
     st_status s;
+    // The scans that seed their thresholds from samples share the seeds: every rank
+    // takes the same two exchanges (a rank with an empty shard contributes zeros,
+    // which rank below every published score).
+    const bool seeded = world > 1 && st_knn_seeded_route(dim, nq, mode, prec);
     if (n_local > 0) {
-        s = st_knn_topk_keys(h, codes, scales, n_local, dim, queries, nq, mode, prec, index_base, local);
+        if (seeded) {
+            ExchangeScope scope(h, comm);
+            s = st_knn_topk_keys(h, codes, scales, n_local, dim, queries, nq, mode, prec, index_base, local);
+        } else {
+            s = st_knn_topk_keys(h, codes, scales, n_local, dim, queries, nq, mode, prec, index_base, local);
+        }
         if (s != ST_OK) return s;
     } else {
         // an empty shard contributes empty lists (key 0 ranks below every real key)
         ST_CHECK_CUDA(h, cudaMemsetAsync(local, 0, list_bytes, h->stream));
+        if (seeded) {
+            uint32_t *thr = reinterpret_cast<uint32_t *>(buf + list_bytes * (world + 2));
+            ST_CHECK_CUDA(h, cudaMemsetAsync(thr, 0, sizeof(uint32_t) * nq, h->stream));
+            for (int stage = 0; stage < 2; stage++) {
+                s = max_over_ranks(h, thr, nq, comm);
+                if (s != ST_OK) return s;
+            }
+        }
     }
     ST_CHECK_NCCL(h, api.all_gather(local, gathered, static_cast<size_t>(nq) * KLIST, ncclUint64, c, h->stream));
     s = st_knn_merge_keys(h, gathered, world, nq * KLIST, nq, merged);

@@ -48,6 +48,11 @@ struct st_handle {
     size_t group_ctl_bytes = 0;
     void *mlp_ctl = nullptr;     // fused MLP step counters: where they were last zeroed, and how many bytes
     size_t mlp_ctl_bytes = 0;
+    // Set by the sharded kNN search for the duration of its local scan: after each of
+    // the two sampling stages the scan calls it on the per-query published 128th-best
+    // scores (nq order-preserving u32), which it replaces by their maximum over the ranks.
+    st_status (*thr_exchange)(st_handle *h, uint32_t *gthr, int64_t nq, void *ctx) = nullptr;
+    void *thr_ctx = nullptr;
 
     st_status fail(st_status s, const char *fmt, ...) {
         char buf[512];
@@ -83,3 +88,7 @@ bool st_make_map_4d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes,
                     uint64_t rows, uint64_t grp, uint64_t outer, uint64_t ld_elems, uint64_t inner_elems,
                     uint64_t stride_elems, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz,
                     std::string *why);
+
+// Whether a kNN scan of nq queries at this dim / mode / precision runs the two
+// threshold-seeding stages (and so calls h->thr_exchange exactly twice).
+bool st_knn_seeded_route(int32_t dim, int64_t nq, int32_t mode, int32_t prec);

@@ -1761,6 +1761,10 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                 const float scale = kf[f * NK + kk];
                 const float nrm = kn[f * NK + kk];
                 const bool klive = kk < nk;
+                // a scale that is not a positive finite number turns the filter's
+                // inequality around or into NaN: such a key takes the exact path for
+                // every query
+                const bool keep_all = !(scale > 0.0f && scale < INFINITY);
                 const float inv_s = rcp_approx(scale);
                 const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
 #pragma unroll
@@ -1803,7 +1807,7 @@ __global__ void __launch_bounds__(N_THREADS, 1) k_knn_narrow(const NarrowArgs g)
                             any |= v >= fmaf(t, inv_s, ca[i2]);
                         }
                     }
-                    any = any && klive;
+                    any = klive && (any || keep_all);
                     const bool slow = __any_sync(0xffffffffu, any);
                     if (!slow) {  // nothing more to read: the accumulator goes back to the MMA now
                         st::tc_fence_before();
@@ -2676,6 +2680,11 @@ st_status launch_tmem(st_handle *h, const NarrowArgs &g, int grid) {
 
 }  // namespace
 
+bool st_knn_seeded_route(int32_t dim, int64_t nq, int32_t mode, int32_t prec) {
+    // the keys-in-TMEM scan (> 32 EXACT dot-product queries) and the narrow scan (<= 32)
+    return dim == 256 && ((nq > NQ && prec == 0 && mode == 0) || nq <= NQ);
+}
+
 static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_keys, int32_t dim,
                            const float *queries, int64_t nq, int32_t mode, int32_t prec, int64_t index_base,
                            const int64_t *ranges, int64_t always, uint64_t *out_keys, const char *who) {
@@ -2759,15 +2768,24 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         };
         // two sample passes seed the thresholds (every 1024th, then every 16th tile):
         // a list's 128th best over a subset bounds the final 128th best from below
+        // With h->thr_exchange set (a key-sharded search), every stage ends with the
+        // maximum over the ranks: a rank's 128th best over its sample bounds the
+        // global 128th best from below too, and only keys reaching the global 128th
+        // best can be in the merged result.
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
-            if (sample * nqb < 4 * h->num_sms || sample >= tiles) continue;
-            s = pass(stride, 0, seed_keys);
-            if (s != ST_OK) return s;
-            k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
-                                                                                       static_cast<int>(nq), gthr);
-            s = st_after_launch(h, "k_knn_seed");
-            if (s != ST_OK) return s;
+            if (sample * nqb >= 4 * h->num_sms && sample < tiles) {
+                s = pass(stride, 0, seed_keys);
+                if (s != ST_OK) return s;
+                k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
+                                                                                           static_cast<int>(nq), gthr);
+                s = st_after_launch(h, "k_knn_seed");
+                if (s != ST_OK) return s;
+            }
+            if (h->thr_exchange) {
+                s = h->thr_exchange(h, gthr, nq, h->thr_ctx);
+                if (s != ST_OK) return s;
+            }
         }
         return pass(1, 1, out_keys);
     }
@@ -2838,23 +2856,31 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         // next pass starts from it instead of from its own first keys.  Two
         // levels: every 1024th tile seeds a pass over every 16th, which seeds the
         // full scan.
+        // (with h->thr_exchange set, each stage ends with the maximum over the ranks,
+        // as in the keys-in-TMEM scan above)
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
-            if (sample < 2 * h->num_sms) continue;
-            NarrowArgs gs = g;
-            const int64_t gsplits = std::min<int64_t>(sample_splits, sample);
-            gs.units = static_cast<int>(gsplits * nqb);
-            gs.unit_step = stride;
-            gs.tile_step = stride * gsplits;
-            gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
-            s = run(gs, static_cast<int>(std::min<int64_t>(gs.units, h->num_sms)));
-            if (s != ST_OK) return s;
-            s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS, seed_keys);
-            if (s != ST_OK) return s;
-            k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
-                                                                                       static_cast<int>(nq), gthr);
-            s = st_after_launch(h, "k_knn_seed");
-            if (s != ST_OK) return s;
+            if (sample >= 2 * h->num_sms) {
+                NarrowArgs gs = g;
+                const int64_t gsplits = std::min<int64_t>(sample_splits, sample);
+                gs.units = static_cast<int>(gsplits * nqb);
+                gs.unit_step = stride;
+                gs.tile_step = stride * gsplits;
+                gs.tiles_per_unit = (sample + gsplits - 1) / gsplits;
+                s = run(gs, static_cast<int>(std::min<int64_t>(gs.units, h->num_sms)));
+                if (s != ST_OK) return s;
+                s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS,
+                                seed_keys);
+                if (s != ST_OK) return s;
+                k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
+                                                                                           static_cast<int>(nq), gthr);
+                s = st_after_launch(h, "k_knn_seed");
+                if (s != ST_OK) return s;
+            }
+            if (h->thr_exchange) {
+                s = h->thr_exchange(h, gthr, nq, h->thr_ctx);
+                if (s != ST_OK) return s;
+            }
         }
         g.units = static_cast<int>(units);
         g.unit_step = tps;

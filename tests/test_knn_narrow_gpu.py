@@ -6,7 +6,7 @@ within the reference's 2e-3 (knn.rs:1099) and the exact ranking outside the
 query's f16 rounding bands.  Ragged tails (key counts that are
 not a multiple of the 128-key tile or of 4), one query, and a 33-query batch
 (the wide scan) agreeing with the same 32 queries run narrow; scans large
-enough to be seeded by the 1-in-64 tile sample."""
+enough to be seeded by the 1-in-16 tile sample; edge scales and queries."""
 import numpy as np
 import pytest
 import torch
@@ -88,3 +88,39 @@ def test_scales_off_a_16_byte_boundary(dev):
         assert s1.data_ptr() % 16 != 0
         s, i = K.search(c1, s1, torch.from_numpy(q).cuda(), k=64, mode="dot")
         _check_exact(q, c1.cpu().numpy(), s1.cpu().numpy(), s.cpu().numpy(), i.cpu().numpy(), 64, "dot")
+
+
+def test_narrow_edge_scales_and_queries(dev):
+    """The narrow dot-product scan with scales that are tiny, zero, negative
+    or huge, and queries that are all zero, tiny or huge.  A key whose scale is
+    not a positive finite number skips the filter and takes the exact path for
+    every query.  Bars as for the wide scan's edge cases: every returned score
+    within 2^-22 of the row's largest of its key's exact f64 score, and indices
+    identical to the oracle's outside such bands."""
+    import scratchtape_b200.knn as K
+    n, nq = 30_011, 20
+    codes, scales = K.synth_keys(n, 256, seed=21)
+    sc = scales.cpu().numpy().copy()
+    sc[:40] *= 1e-5
+    sc[40:50] = 0.0
+    sc[50:400] *= -1.0
+    sc[400:403] = [20000.0, -17000.0, 16384.0]
+    rng = np.random.default_rng(22)
+    q = rng.standard_normal((nq, 256)).astype(np.float32)
+    q[0] = 0.0
+    q[1] *= 1e-6
+    q[2] *= 1e6
+    q[19] = 0.0
+    got_s, got_i = K.search(codes, torch.from_numpy(sc).cuda(), torch.from_numpy(q).cuda(), k=128, mode="dot",
+                            prec="exact")
+    got_s, got_i = got_s.cpu().numpy(), got_i.cpu().numpy()
+    codes_h = codes.cpu().numpy()
+    want_s, want_i = oracle.knn_topk(codes_h, sc, q, 128, mode="dot", prec="exact")
+    for r in range(nq):
+        band = 2.0 ** -22 * np.abs(want_s[r]).max() + 1e-30
+        exact = oracle.knn_pair_dots(codes_h, sc, q, np.full(128, r), got_i[r])
+        assert np.all(np.abs(got_s[r] - exact) <= band), "row %d: scores off" % r
+        assert np.all(np.abs(exact - want_s[r]) <= 2 * band), "row %d: not the best keys" % r
+        ws = want_s[r]
+        tied = np.r_[False, np.abs(np.diff(ws)) <= 2 * band] | np.r_[np.abs(np.diff(ws)) <= 2 * band, False]
+        assert np.array_equal(got_i[r][~tied], want_i[r][~tied]), "row %d: indices differ outside ties" % r

@@ -9,6 +9,9 @@
 * the same search and average through the C ABI (st_knn_search_sharded,
   st_avg_params on a communicator made by st_nccl_comm_init): identical to
   the torch.distributed route.
+* a C-ABI search large enough for the sampling stages (the keys-in-TMEM scan
+  with 300 queries, the narrow scan with 20), whose seeds are exchanged as a
+  maximum over the ranks: identical, bit for bit, to one scan of all keys.
 """
 import os
 import socket
@@ -55,7 +58,16 @@ def _worker(rank, world, port, result_path):
     p_abi = p_torch.clone()
     shard.average_params(p_torch)
     shard.average_params(p_abi, comm=comm)
+    # 2.6 M keys per rank: both sampling stages' seeds cross the ranks
+    n2 = 5_200_001
+    lo2, hi2 = shard.shard_range(n2, world, rank)
+    c2, sc2 = K.synth_keys(hi2 - lo2, d, seed=13, first_key=lo2)
+    seeded = []
+    for nq2 in (300, 20):
+        q2 = torch.randn((nq2, d), device="cuda", generator=g)
+        seeded.append((q2, shard.knn_search_sharded(c2, sc2, q2, lo2, k=128, mode="dot", comm=comm)))
     torch.cuda.synchronize()
+    del c2, sc2
     comm.close()
     ok_abi = torch.equal(s_abi, s) and torch.equal(i_abi, i) and torch.equal(p_abi, p_torch)
     # heads: this rank's slice of 16 heads
@@ -72,8 +84,14 @@ def _worker(rank, world, port, result_path):
         ac, asc = K.synth_keys(n, d, seed=11)
         ws, wi = K.search(ac, asc, q, k=128, mode="dot")
         ok_knn = torch.equal(wi, i) and torch.equal(ws, s)
+        ac2, asc2 = K.synth_keys(n2, d, seed=13)
+        ok_seeded = True
+        for q2, (s2, i2) in seeded:
+            ws2, wi2 = K.search(ac2, asc2, q2, k=128, mode="dot")
+            ok_seeded = ok_seeded and torch.equal(wi2, i2) and torch.equal(ws2, s2)
         with open(result_path, "w") as f:
-            f.write("%d %d %d %d" % (int(ok_knn), int(oks[0].item()), int(oks[1].item()), int(oks[2].item())))
+            f.write("%d %d %d %d %d" % (int(ok_knn), int(oks[0].item()), int(oks[1].item()), int(oks[2].item()),
+                                        int(ok_seeded)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -83,8 +101,9 @@ def test_two_gpu_sharded_paths(tmp_path):
         pytest.skip("needs 2 GPUs")
     path = str(tmp_path / "res.txt")
     mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, start_method="spawn", join=True)
-    ok_knn, ok_heads, ok_avg, ok_abi = open(path).read().split()
+    ok_knn, ok_heads, ok_avg, ok_abi, ok_seeded = open(path).read().split()
     assert ok_knn == "1", "sharded kNN differs from the single-GPU scan"
     assert ok_heads == "1", "head-sharded attention differs"
     assert ok_avg == "1", "NCCL parameter average wrong"
     assert ok_abi == "1", "the C-ABI route (st_knn_search_sharded / st_avg_params) differs from the torch route"
+    assert ok_seeded == "1", "the sharded search with seeds shared across ranks differs from the single-GPU scan"
