@@ -696,13 +696,23 @@ def run_ours_c5(args):
         e[4].record()
     torch.cuda.synchronize()
     parts = [float(np.mean([e[j].elapsed_time(e[j + 1]) for e in evs])) for j in range(4)]
-    scan_ms, gather_ms, merge_ms, decode_ms = max_over_ranks(*parts)
+    alone_ms, gather_ms, merge_ms, decode_ms = max_over_ranks(*parts)
+    # at N > 1 the timed step's local scan also takes the seed thresholds' maximum over
+    # the ranks (inside st_knn_search_sharded); its share is the step less the rest
+    scan_ms = max(0.0, ms_per_step - gather_ms - merge_ms - decode_ms) if world > 1 else alone_ms
     split = {"scan_ms": scan_ms, "allgather_ms": gather_ms, "merge_ms": merge_ms, "decode_ms": decode_ms,
              "allgather_bytes_per_rank": nq * K.KMAX * 8,
              "limiter": "the local scan (%s): %.1f %% of a step" % (C5_KERNEL[args.prec].split(" ")[0],
                         100.0 * scan_ms / max(1e-9, scan_ms + gather_ms + merge_ms + decode_ms)),
-             "how": "the same step as separate calls (topk_keys, torch all_gather_into_tensor, merge_keys, decode) "
-                    "with CUDA events between them, mean of %d, max over ranks" % split_steps}
+             "how": ("the all-gather, merge and decode as separate calls (torch all_gather_into_tensor, merge_keys, "
+                     "decode) with CUDA events between them, mean of %d, max over ranks; scan_ms: the timed step "
+                     "(whose local scan shares the sampling stages' seeds across the ranks) less those; "
+                     "scan_ms_unshared: the local scan alone, seeds from this rank's keys only" % split_steps)
+                    if world > 1 else
+                    "the same step as separate calls (topk_keys, merge_keys, decode) with CUDA events between "
+                    "them, mean of %d" % split_steps}
+    if world > 1:
+        split["scan_ms_unshared"] = alone_ms
 
     # e2e through the public API: host queries in, host results out, every step
     hq = torch.from_numpy(qh).pin_memory()

@@ -1265,6 +1265,7 @@ struct NarrowArgs {
     // nslot lists per (query, quadrant) in unit_out
     int64_t flat_len, seg_len;
     int nslot;
+    int aligned;           // k_knn_tmem: 1 = CTA c takes part c / nqb of query block c % nqb (see tm_next)
     int *status;
 };
 
@@ -1345,13 +1346,15 @@ __device__ __forceinline__ bool narrow_tile(const NarrowArgs &g, int unit, int64
     return true;
 }
 
-// k_knn_tmem's work split: CTA c takes the flat range [c L / G, (c + 1) L / G) of
-// the pass's (query block, sample) sequence (L = g.flat_len, G = gridDim.x,
-// block-major, g.seg_len samples per block), so every CTA has the same number
-// of tiles and crosses at most a few block boundaries.  A piece is the part of
-// the range inside one query block; the CTAs that cover block b write their
-// lists to slots 0, 1, .. in range order (slot = c - the CTA holding b's first
-// sample).
+// k_knn_tmem's work split.  With at most one query block per SM (g.aligned),
+// the grid is nqb P CTAs and CTA c scans part c / nqb (of P equal parts) of
+// query block c % nqb, writing its lists to slot c / nqb.  Otherwise CTA c
+// takes the flat range [c L / G, (c + 1) L / G) of the pass's (query block,
+// sample) sequence (L = g.flat_len, G = gridDim.x, block-major, g.seg_len
+// samples per block), so every CTA has the same number of tiles and crosses at
+// most a few block boundaries; a piece is the part of the range inside one
+// query block, and the CTAs that cover block b write their lists to slots
+// 0, 1, .. in range order (slot = c - the CTA holding b's first sample).
 struct TPiece {
     int64_t pos, end;  // the CTA's remaining flat range
     int64_t j0, j1;    // the piece's samples of block qb
@@ -1361,11 +1364,23 @@ __device__ __forceinline__ int64_t tm_seg_start(const NarrowArgs &g, int64_t c) 
     return c * g.flat_len / gridDim.x;
 }
 __device__ __forceinline__ void tm_begin(const NarrowArgs &g, TPiece &p) {
-    p.pos = tm_seg_start(g, blockIdx.x);
-    p.end = tm_seg_start(g, blockIdx.x + 1);
+    p.pos = g.aligned ? 0 : tm_seg_start(g, blockIdx.x);
+    p.end = g.aligned ? 1 : tm_seg_start(g, blockIdx.x + 1);
 }
 __device__ __forceinline__ bool tm_next(const NarrowArgs &g, TPiece &p) {
     if (p.pos >= p.end) return false;
+    if (g.aligned) {
+        // gridDim.x = nqb P: the CTAs of part k of every query block scan the same tiles
+        // at the same time, so each tile comes from DRAM about once and from L2 for the
+        // other blocks
+        const int parts = gridDim.x / g.nqb, part = blockIdx.x / g.nqb;
+        p.pos = 1;
+        p.qb = blockIdx.x % g.nqb;
+        p.j0 = part * g.seg_len / parts;
+        p.j1 = (part + 1) * g.seg_len / parts;
+        p.slot = part;
+        return p.j1 > p.j0;
+    }
     const int64_t qb = p.pos / g.seg_len;
     p.qb = static_cast<int>(qb);
     p.j0 = p.pos - qb * g.seg_len;
@@ -2020,10 +2035,13 @@ constexpr int T_MMA_WARP = T_EPI + T_PROD;    // 12
 constexpr int T_TMA_WARP = T_MMA_WARP + 1;    // 13
 constexpr int T_THREADS = 32 * (T_TMA_WARP + 1);
 constexpr int T_STAGES = 6;
-constexpr int T_NACC = 2;
-constexpr int TO_Q = 0;                       // [2 steps][4 K chunks][128 rows x 128 B] f16, SW128
+constexpr int T_SN = 128;                     // queries per MMA step (N); 64 measured 1.41x slower
+constexpr int T_NST = TQ / T_SN;              // steps per tile
+constexpr int T_NACC = (512 - N_A * 128) / T_SN;  // accumulators: the TMEM the A buffers leave
+constexpr int T_R = T_SN / 64;                // a filter lane's queries per step
+constexpr int TO_Q = 0;                       // [2 query blocks of 128][4 K chunks][128 rows x 128 B] f16, SW128
 constexpr int TO_X = TO_Q + 2 * 4 * 16384;    // filter rows [128 x 128 B] SW128, K slice j (dims 16 j ..):
-                                              //   j = 0, 1 keys of A buffer j; j = 2, 3 queries of step j - 2
+                                              //   j = 0, 1 keys of A buffer j; j = 2, 3 queries of block j - 2
 constexpr int TO_RING = TO_X + 16384;
 constexpr int TO_KF = TO_RING + T_STAGES * N_STAGE_BYTES;   // [N_KF][128] scale
 constexpr int TO_QC = TO_KF + N_KF * NK * 4;                // [2 units][4][TQ]: E, 2^e, live, sum |hi|
@@ -2035,7 +2053,8 @@ constexpr int T_NBARS = 2 * T_STAGES + 2 * N_A + 2 * T_NACC + N_KF + 2 + 2 + 1 +
 constexpr int TO_MISC = TO_BAR + T_NBARS * 8;
 constexpr int TMEM_SMEM = TO_MISC + 16 + 1024;
 static_assert(TMEM_SMEM <= 232448, "keys-in-TMEM kNN scan shared memory exceeds the sm_100 limit");
-static_assert(N_A * 128 + T_NACC * 128 <= 512, "keys-in-TMEM kNN scan TMEM budget");
+static_assert(N_A * 128 + T_NACC * T_SN <= 512 && T_NACC >= 2, "keys-in-TMEM kNN scan TMEM budget");
+static_assert(T_SN == 64 || T_SN == 128, "keys-in-TMEM kNN scan step width");
 static_assert(TO_X % 1024 == 0 && TO_RING % 16 == 0 && N_STAGE_BYTES % 16 == 0, "keys-in-TMEM kNN scan alignment");
 constexpr float TM_SMALL = 1.220703125e-4f;   // 2^-13: smaller |s| expand as zeros (bound widened)
 constexpr float TM_BIG = 16384.0f;            // 2^14: larger |s| expand as zeros (every pair kept)
@@ -2113,6 +2132,12 @@ __device__ __forceinline__ void tm_exact_warp_batch(int n, const uint8_t *const 
         for (int j = 0; j < TM_BATCH; j++) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
 #pragma unroll
     for (int j = 0; j < TM_BATCH; j++) out[j] = static_cast<float>(acc[j] * static_cast<double>(s[j]) * static_cast<double>(p2e[j]));
+}
+
+// Slot sl (0..3) of filter lane `lane` in the warp of column half hw: the
+// query it owns, T_R per step of T_SN queries.
+__device__ __forceinline__ int tm_slot_query(int sl, int hw, int lane) {
+    return (sl / T_R) * T_SN + (T_SN / 2) * hw + 32 * (sl % T_R) + lane;
 }
 
 // r[i] for a warp-uniform runtime i (a select chain: indexing the register
@@ -2356,7 +2381,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
     } else if (warp == T_MMA_WARP) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, 128, 128);  // f32 <- f16 x f16
+            constexpr uint32_t idesc = st::idesc_make(1, 0, false, false, 128, T_SN);  // f32 <- f16 x f16
             const uint32_t qbuf = st::smem_u32(smem + TO_Q), xbuf = st::smem_u32(smem + TO_X);
             uint32_t gt = 0, gs = 0, uj = 0;
             bool ok = true;
@@ -2376,7 +2401,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     st::tc_fence_after();
                     const uint32_t abuf = tmem + b * 128u;
 #pragma unroll 1
-                    for (int step = 0; step < 2; step++, gs++) {
+                    for (int step = 0; step < T_NST; step++, gs++) {
                         const uint32_t a = gs % T_NACC;
                         if (gs >= T_NACC &&
                             !nwait(&acce[a], ((gs / T_NACC) - 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_EMPTY)) {
@@ -2384,16 +2409,19 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                             break;
                         }
                         st::tc_fence_after();
-                        const uint32_t acc = tmem + ACC_COL + a * 128u;
-                        const uint32_t qs = qbuf + step * 65536;
+                        const uint32_t acc = tmem + ACC_COL + a * T_SN;
+                        // queries T_SN step ..: 128-query block blk, from row rofs (8 KB per 64 rows,
+                        // a whole number of swizzle atoms)
+                        const uint32_t blk = (step * T_SN) >> 7, rofs = ((step * T_SN) & 127) * 128;
+                        const uint32_t qs = qbuf + blk * 65536 + rofs;
 #pragma unroll
                         for (int kk = 0; kk < 16; kk++)
                             st::umma_f16_ts(acc, abuf + 8 * kk,
                                             st::sdesc_sw128(qs + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), idesc,
                                             kk > 0 ? 1u : 0u);
-                        // the filter terms: K slice b of the keys' rows x slice 2 + step of the queries'
+                        // the filter terms: K slice b of the keys' rows x slice 2 + blk of the queries'
                         st::umma_f16(acc, st::sdesc_sw128(xbuf + b * 32, 16, 1024),
-                                     st::sdesc_sw128(xbuf + (2 + step) * 32, 16, 1024), idesc, 1u);
+                                     st::sdesc_sw128(xbuf + (2 + blk) * 32 + rofs, 16, 1024), idesc, 1u);
                         st::umma_commit(&accf[a]);
                     }
                     if (!ok) break;
@@ -2406,12 +2434,13 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        // Warp w: TMEM lanes 32 (w % 4) .. (keys), accumulator columns 64 (w / 4) .. + 63
-        // of each step (queries 128 step + 64 (w / 4) + c of the unit).  Lane l owns the
-        // candidate buffers of the unit's queries 128 (s / 2) + 64 (w / 4) + 32 (s % 2) + l
-        // (slots s = 0..3); the lists' counts, own 128th-best scores and effective
-        // thresholds live in shared memory, so that the loops over chunks and slots stay
-        // rolled (small code: the four roles share the SM's instruction cache).
+        // Warp w: TMEM lanes 32 (w % 4) .. (keys), accumulator columns T_SN / 2 (w / 4) ..
+        // of each step (queries T_SN step + T_SN / 2 (w / 4) + c of the unit).  Lane l owns
+        // the candidate buffers of the unit's queries tm_slot_query(s, w / 4, l), slots
+        // s = 0..3 (four queries of each step of T_SN); the lists' counts, own 128th-best
+        // scores and effective thresholds live in shared memory, so that the loops over
+        // chunks and slots stay rolled (small code: the four roles share the SM's
+        // instruction cache).
         const int quad = warp & 3, hw = warp >> 2;
         const unsigned lt = (1u << lane) - 1u;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * quad) << 16;
@@ -2427,12 +2456,12 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
         for (; ok && tm_next(g, pc); ++uj) {
             if (!nwait(&qready[uj & 1u], (uj >> 1) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_FULL)) break;
             const float *qc = qconst0 + (uj & 1u) * 4 * TQ;
-            const float *qc_p = qc + TQ, *qc_live = qc + 2 * TQ, *qc_mag = qc + 3 * TQ;
+            const float *qc_p = qc + TQ, *qc_mag = qc + 3 * TQ;
             const int qbase = pc.qb * TQ;
             const int nlive = g.nq - qbase;  // the unit's queries from nlive on are padding
 #pragma unroll 1
             for (int sl = 0; sl < 4; sl++) {
-                const int qu = 128 * (sl >> 1) + 64 * hw + 32 * (sl & 1) + lane;
+                const int qu = tm_slot_query(sl, hw, lane);
                 const bool live = qu < nlive;
                 ocnt[qu] = 0;
                 othr[qu] = live ? -INFINITY : INFINITY;
@@ -2457,25 +2486,27 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                 const bool klive = kk < nk;
                 const uint32_t idx = g.index_base + static_cast<uint32_t>(tb) + static_cast<uint32_t>(kk);
 #pragma unroll 1
-                for (int step = 0; step < 2; step++, gs++) {
+                for (int step = 0; step < T_NST; step++, gs++) {
                     const uint32_t a = gs % T_NACC;
                     if (!nwait(&accf[a], (gs / T_NACC) & 1u, abort_flag, g.status, st::DEV_TIMEOUT_ACC)) {
                         ok = false;
                         break;
                     }
                     st::tc_fence_after();
-                    const uint32_t acc = acc0 + a * 128u + 64u * hw;
-                    const int lim0 = nlive - (128 * step + 64 * hw);
+                    const int qw = step * T_SN + (T_SN / 2) * hw;  // this warp's first query of the step
+                    const uint32_t acc = acc0 + a * T_SN + (T_SN / 2) * hw;
+                    const int lim0 = nlive - qw;
+                    constexpr int NCH = T_SN / 32;  // this warp's 16-column chunks of a step
                     if (EXACT) {
                         // full pass: a pair is kept if its filtered accumulator is not negative
-                        uint32_t pass[4];  // per 16-query chunk, bit i: the pair was kept
+                        uint32_t pass[NCH];  // per 16-query chunk, bit i: the pair was kept
                         {
-                            uint32_t r[2][32];  // the warp's 64 columns, one wait
-                            st::tmem_ld32(acc, r[0]);
-                            st::tmem_ld32(acc + 32, r[1]);
+                            uint32_t r[NCH / 2][32];  // the warp's columns, one wait
+#pragma unroll
+                            for (int h2 = 0; h2 < NCH / 2; h2++) st::tmem_ld32(acc + 32 * h2, r[h2]);
                             st::tmem_ld_wait();
 #pragma unroll
-                            for (int hh = 0; hh < 4; hh++) {
+                            for (int hh = 0; hh < NCH; hh++) {
                                 const uint32_t *rc = r[hh >> 1] + 16 * (hh & 1);
                                 // all 16 negative <=> the AND of their sign bits is set
                                 const uint32_t a0 = rc[0] & rc[1] & rc[2] & rc[3], a1 = rc[4] & rc[5] & rc[6] & rc[7];
@@ -2497,7 +2528,10 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         if (lane == 0) st::mbar_arrive(&acce[a]);
                         // each kept pair's exact score, by the whole warp; inserted by the
                         // list's owner lane if it reaches the threshold
-                        const unsigned any = __ballot_sync(0xffffffffu, (pass[0] | pass[1] | pass[2] | pass[3]) != 0u);
+                        uint32_t pall = 0u;
+#pragma unroll
+                        for (int hh = 0; hh < NCH; hh++) pall |= pass[hh];
+                        const unsigned any = __ballot_sync(0xffffffffu, pall != 0u);
                         if (any) {
                             // kept pairs in (chunk, key lane, query) order, scored TM_BATCH at a time;
                             // the owner lane of each query inserts in that order
@@ -2522,14 +2556,16 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                                 np = 0;
                             };
 #pragma unroll 1
-                            for (int c = 0; c < 4; c++) {
-                                const uint32_t pc = c == 0 ? pass[0] : c == 1 ? pass[1] : c == 2 ? pass[2] : pass[3];
-                                unsigned lanes = __ballot_sync(0xffffffffu, pc != 0u);
-                                const int q0 = 128 * step + 64 * hw + 16 * c;
+                            for (int c = 0; c < NCH; c++) {
+                                uint32_t pcm = pass[0];  // pass[c] (a select chain keeps it in registers)
+#pragma unroll
+                                for (int hh = 1; hh < NCH; hh++) pcm = c == hh ? pass[hh] : pcm;
+                                unsigned lanes = __ballot_sync(0xffffffffu, pcm != 0u);
+                                const int q0 = qw + 16 * c;
                                 while (lanes) {
                                     const int L = __ffs(lanes) - 1;
                                     lanes &= lanes - 1;
-                                    uint32_t bits = __shfl_sync(0xffffffffu, pc, L);
+                                    uint32_t bits = __shfl_sync(0xffffffffu, pcm, L);
                                     const float sL = __shfl_sync(0xffffffffu, scale, L);
                                     const int keyL = 32 * quad + L;
                                     const uint8_t *kcodes = g.codes + (tb + keyL) * 64;
@@ -2560,11 +2596,11 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                         // sample pass: acc' is a lower bound of the pair's score; a pair enters
                         // its list, lowered by 2^-12, if the bound reaches the threshold
 #pragma unroll 1
-                        for (int c = 0; c < 4; c++) {
+                        for (int c = 0; c < NCH; c++) {
                             uint32_t r[16];
                             st::tmem_ld16(acc + 16 * c, r);
                             st::tmem_ld_wait();
-                            const int q0 = 128 * step + 64 * hw + 16 * c;
+                            const int q0 = qw + 16 * c;
                             uint32_t pm = 0u;
 #pragma unroll
                             for (int i4 = 0; i4 < 16; i4 += 4) {
@@ -2602,8 +2638,8 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
                     // 128th best, published, and the best any list of the query has published
                     if (i % TM_MAINT != TM_MAINT - 1) continue;
 #pragma unroll 1
-                    for (int sh = 0; sh < 2; sh++) {
-                        const int qu = 128 * step + 64 * hw + 32 * sh + lane;
+                    for (int sh = 0; sh < T_R; sh++) {
+                        const int qu = qw + 32 * sh + lane;
                         int cn = ocnt[qu];
                         float th = othr[qu];
                         const unsigned need = __ballot_sync(0xffffffffu, cn > KCAP - 32 * TM_MAINT);
@@ -2640,7 +2676,7 @@ __global__ void __launch_bounds__(T_THREADS, 1) k_knn_tmem(const NarrowArgs g) {
             }
 #pragma unroll 1
             for (int sl = 0; sl < 4; sl++) {
-                const int qu = 128 * (sl >> 1) + 64 * hw + 32 * (sl & 1) + lane;
+                const int qu = tm_slot_query(sl, hw, lane);
                 int cn = ocnt[qu];
                 float th = othr[qu];
                 uint64_t *my_out =
@@ -2703,20 +2739,29 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         const int64_t tiles = (n_keys + NK - 1) / NK;
         if (static_cast<int64_t>(nqb) * tiles > (1LL << 50)) return h->fail(ST_UNSUPPORTED_SHAPE, "%s: too many queries", who);
         // a pass over `samples` tiles per block: its grid and the slots its pieces need
-        auto plan = [&](int64_t samples, int &grid, int &nslot) {
+        auto plan = [&](int64_t samples, int &grid, int &nslot, int &aligned) {
+            if (nqb <= h->num_sms) {
+                // P aligned parts per query block, one per CTA
+                const int parts = static_cast<int>(std::min<int64_t>(h->num_sms / nqb, samples));
+                grid = nqb * parts;
+                nslot = parts;
+                aligned = 1;
+                return;
+            }
             const int64_t flat = static_cast<int64_t>(nqb) * samples;
             grid = static_cast<int>(std::min<int64_t>(flat, h->num_sms));
             const int64_t shortest = flat / grid;  // every CTA's range holds at least this many samples
             nslot = static_cast<int>((samples + shortest - 1) / shortest + 1);
+            aligned = 0;
         };
-        int grid_full, nslot_full;
-        plan(tiles, grid_full, nslot_full);
+        int grid_full, nslot_full, al;
+        plan(tiles, grid_full, nslot_full, al);
         int nslot_max = nslot_full;
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
             if (sample * nqb < 4 * h->num_sms || sample >= tiles) continue;
             int gr, ns;
-            plan(sample, gr, ns);
+            plan(sample, gr, ns, al);
             nslot_max = std::max(nslot_max, ns);
         }
         const int grid_cap = h->num_sms;
@@ -2751,9 +2796,10 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         // one pass over every stride-th tile: lists zeroed, scan, merge into `dst`
         auto pass = [&](int64_t stride, int exact, uint64_t *dst) -> st_status {
             const int64_t samples = (tiles + stride - 1) / stride;
-            int grid, nslot;
-            plan(samples, grid, nslot);
+            int grid, nslot, aligned;
+            plan(samples, grid, nslot, aligned);
             NarrowArgs a = g;
+            a.aligned = aligned;
             a.exact = exact;
             a.unit_step = stride;
             a.seg_len = samples;
