@@ -53,6 +53,10 @@ C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
 C3_TRAFFIC_PER_STEP = 6.326784e6 + 10.581504e6
 # DRAM bytes (read + write) of one k_mlp_step launch at C2, from one ncu capture
 C2_FUSED_TRAFFIC = 4.800256e6 + 5.820416e6
+# DRAM bytes of one k_knn_tmem full-pass launch, 4096 queries over 2^24 keys, from one ncu capture (the
+# capture-size rule keeps it below the full 2^27): reads 1.312 GB (the 1.14 GB of codes + scales once, the
+# rest L2 misses of the 16 query blocks' shared reads), writes 0.225 GB (per-block lists, candidate inserts)
+C5_TRAFFIC_READ_2P24, C5_TRAFFIC_WRITE_2P24 = 1.312352512e9, 0.224658176e9
 
 
 def parse_args():
@@ -795,11 +799,14 @@ def run_ours_c5(args):
                        "l2": "inputs (%.1f GB of codes + scales) far larger than L2; no flush needed"
                              % (n_total * (d / 4 + 4) / 1e9)},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": n_local * (d / 4 + 4) + nq * d * 4,
-                         "traffic_note": "algorithmic bytes per scan launch (codes + scales + queries); the ncu "
-                                         "capture's DRAM bytes are dominated by candidate-buffer inserts that grow "
-                                         "with the number of work units, not with the keys, so they do not scale "
-                                         "to a full launch",
+                         "frac": achieved / peak,
+                         "traffic": (C5_TRAFFIC_READ_2P24 * n_local / float(1 << 24) + C5_TRAFFIC_WRITE_2P24
+                                     if args.prec == "exact" else None),
+                         "traffic_note": "DRAM read + write of one k_knn_tmem full pass from an ncu capture at "
+                                         "2^24 keys x 4096 queries (1.312 GB read, 0.225 GB written), reads "
+                                         "scaled by this rank's keys / 2^24, writes (lists, candidate inserts) "
+                                         "as captured; algorithmic bytes (codes + scales + queries): %.3g"
+                                         % (n_local * (d / 4 + 4) + nq * d * 4),
                          "peak_source": peak_src + " (" + C5_PEAK_NOTE[args.prec] + ")",
                          "kernel": C5_KERNEL[args.prec],
                          "scan_ms": scan_ms, "algorithmic_tflop_per_scan": flops_alg / 1e12,
