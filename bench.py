@@ -739,6 +739,42 @@ def run_ours_c5(args):
     e_total, = max_over_ranks(float(sum(e_ms)))
     e2e_value = n_total / (e_total / e2e_steps / 1e3)
 
+    # the host link under the job's own concurrency: every rank copies 64 MiB from pinned
+    # host memory to its GPU and back at the same moment (after a barrier), one
+    # direction at a time and both at once; GB/s per rank, min and max over ranks --
+    # what bounds the e2e lines of the configs whose inputs are copied every step
+    link_n = 64 << 20
+    hbuf = torch.empty(link_n, dtype=torch.uint8).pin_memory()
+    hbuf2 = torch.empty(link_n, dtype=torch.uint8).pin_memory()
+    dbuf = torch.empty(link_n, dtype=torch.uint8, device=device)
+    dbuf2 = torch.empty(link_n, dtype=torch.uint8, device=device)
+    s_up, s_down = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def link_gbs(up, down, reps=3):
+        best = float("inf")
+        for _ in range(reps):
+            barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if up:
+                with torch.cuda.stream(s_up):
+                    dbuf.copy_(hbuf, non_blocking=True)
+            if down:
+                with torch.cuda.stream(s_down):
+                    hbuf2.copy_(dbuf2, non_blocking=True)
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        return link_n / best / 1e9
+
+    link = {}
+    for name, up, down in (("h2d", True, False), ("d2h", False, True), ("both_each_way", True, True)):
+        v = link_gbs(up, down)
+        neg_min, v_max = max_over_ranks(-v, v)
+        link[name + "_gbs_min_max"] = [-neg_min, v_max]
+    link["how"] = ("64 MiB pinned <-> device copies, all %d ranks at once after a barrier, wall clock around "
+                   "the copies (best of 3); both_each_way: the two directions on two streams together" % world)
+    del hbuf, hbuf2, dbuf, dbuf2
+
     # the small pass: 32 queries over the same keys, where the scan would be
     # HBM-bound if it ran at the tensor pipe's full rate (the ridge is ~33
     # queries per pass at 68 B/key); reported against the HBM roofline
@@ -813,6 +849,7 @@ def run_ours_c5(args):
                          "hbm_gbs": n_local * (d / 4 + 4) / (scan_ms / 1e3) / 1e9,
                          "small_pass": small_pass, "ivf_pass": ivf_pass},
             "time_split": split,
+            "host_link": link,
             "parity": parity,
             "e2e": {"value": e2e_value, "unit": C5_METRIC_UNIT, "h2d_bytes_per_step": int(hq.numel() * 4),
                     "d2h_bytes_per_step": int(hs.numel() * 4 + hi.numel() * 8), "ms_per_step": e_total / e2e_steps,
@@ -1325,6 +1362,73 @@ def large_gemm_probe(torch, device, peaks):
     return res
 
 
+def c4_gemm_breakdown(torch, device, peaks, cfg):
+    """Each TF32 GEMM shape of the C4 step at M = batch x seq = 8192 tokens (the
+    layer's QKV, output, FFN-in and FFN-out projections, forward NN, input-gradient
+    NT and weight-gradient TN) timed alone with CUDA events (10 back-to-back
+    launches replayed from one CUDA graph, as the step's are, after 3 eager
+    ones; operands resident), against the TF32 dense peak measured here (cuBLAS
+    through torch.matmul with TF32 allowed, 8192^3, best of 10) and against the
+    HBM time of its f32 operands and result: the bound of a GEMM is the larger
+    of flops / TF32 peak and bytes / HBM."""
+    import scratchtape_b200 as st
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    x = torch.randn((8192, 8192), device=device)
+    y = torch.randn((8192, 8192), device=device)
+    for _ in range(3):
+        torch.matmul(x, y)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(x, y)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del x, y
+    tf32_peak = 2.0 * 8192 ** 3 / (best / 1e3) / 1e12
+    hbm = float(peaks["hbm_gbs"]) * 1e9
+    m, d, f = cfg.batch * cfg.t, cfg.d, cfg.dff
+    shapes = [("qkv", d, 3 * d), ("out_proj", d, d), ("ffn_in", d, f), ("ffn_out", f, d)]
+    rows = []
+    for name, k, n in shapes:
+        for lay, (mm, kk, nn, ta, tb) in (("fwd NN", (m, k, n, False, False)), ("dX NT", (m, n, k, False, True)),
+                                          ("dW TN", (k, m, n, True, False))):
+            a = torch.randn((kk, mm) if ta else (mm, kk), device=device)
+            b = torch.randn((nn, kk) if tb else (kk, nn), device=device)
+            out = torch.empty((mm, nn), device=device)
+            side = torch.cuda.Stream(device)
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    st.mm(a, b, ta=ta, tb=tb, out=out)
+            torch.cuda.current_stream(device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(10):
+                    st.mm(a, b, ta=ta, tb=tb, out=out)
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            e1.synchronize()
+            del graph
+            us = e0.elapsed_time(e1) / 10 * 1e3
+            flops = 2.0 * mm * nn * kk
+            byts = 4.0 * (mm * kk + kk * nn + mm * nn)
+            bound_us = max(flops / (tf32_peak * 1e12), byts / hbm) * 1e6
+            rows.append({"gemm": "%s %s" % (name, lay), "m_k_n": [mm, kk, nn], "us": us,
+                         "tflops": flops / (us / 1e6) / 1e12, "frac_of_tf32_peak": flops / (us / 1e6) / 1e12 / tf32_peak,
+                         "bound": "hbm" if byts / hbm > flops / (tf32_peak * 1e12) else "tensor",
+                         "bound_us": bound_us, "frac_of_bound": bound_us / us})
+            del a, b, out
+    return {"tf32_peak_tflops": tf32_peak, "tf32_peak_how": "cuBLAS TF32 8192^3 via torch.matmul, best of 10",
+            "hbm_gbs": float(peaks["hbm_gbs"]), "gemms": rows}
+
+
 def run_ours_c4(args):
     import torch
     import torch.distributed as dist
@@ -1468,6 +1572,8 @@ def run_ours_c4(args):
             "clocks": sampler.summary(),
             "large_gemm": large_gemm_probe(torch, device, peaks),
         }
+        if world == 1:
+            line["gemm_breakdown"] = c4_gemm_breakdown(torch, device, peaks, cfg)
         if world == 1 and not args.no_cpu_baseline:
             el = cpu_baseline_c4(cfg)
             line["cpu_baseline"] = {"value": cfg.flops_per_step() / el / 1e12, "unit": "TFLOP/s", "cores": 1,
