@@ -160,82 +160,122 @@ __global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, 
 }
 
 // dx (+)= rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma.
-// Each block takes LN_ROWS consecutive rows (warp w: rows w, w + 8, ...) and
-// also writes its partial parameter gradients -- per column, sum over its rows
-// of dy * xhat and of dy, warps combined in warp order -- to
+// Each block takes LN_WARPS * RPW consecutive rows (warp w: rows w, w + 8,
+// ..., RPW of them, RPW * PER <= 32 so a warp's rows fit its registers); a
+// warp loads every row's dy, x (and dx) before any arithmetic, so its loads
+// are in flight together.  The block also writes its partial parameter
+// gradients -- per column, over its rows, sum of dy * xhat and of dy, rows
+// in order within a warp, warps combined in warp order -- to
 // part[block][2][d]; k_ln_params_sum adds the blocks in block order.
-constexpr int LN_WARPS = 8, LN_ROWS = 32, LN_MAXD = 512;  // LN_MAXD: widest row of the backward
+constexpr int LN_WARPS = 8, LN_MAXD = 512;  // LN_MAXD: widest row of the backward
+template <int PER, int RPW>
 __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const float *x, const float *gamma,
                                                           const float *mean, const float *rstd, float *dx, float *part,
-                                                          int64_t rows, int d, int accumulate) {
-    __shared__ float sh[LN_WARPS][2][LN_MAXD];
+                                                          int64_t rows, int accumulate) {
+    constexpr int D = 32 * PER;
+    __shared__ float sh[LN_WARPS][2][D];
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int per = d / 32;
-    float pg[LN_MAXD / 32], pb[LN_MAXD / 32];
+    const int64_t row0 = blockIdx.x * static_cast<int64_t>(LN_WARPS * RPW);
+    float dyv[RPW][PER], xv[RPW][PER], dxv[RPW][PER], mu[RPW], rs[RPW];
 #pragma unroll
-    for (int j = 0; j < LN_MAXD / 32; j++) pg[j] = pb[j] = 0.0f;
-    for (int i = warp; i < LN_ROWS; i += LN_WARPS) {
-        const int64_t r = blockIdx.x * static_cast<int64_t>(LN_ROWS) + i;
-        if (r >= rows) break;
-        const float mu = mean[r], rs = rstd[r];
-        float gv[LN_MAXD / 32], xh[LN_MAXD / 32];
-        float s1 = 0.0f, s2 = 0.0f;
+    for (int i = 0; i < RPW; i++) {
+        const int64_t r = row0 + warp + static_cast<int64_t>(LN_WARPS) * i;
+        const bool in = r < rows;
+        mu[i] = in ? mean[r] : 0.0f;
+        rs[i] = in ? rstd[r] : 0.0f;
 #pragma unroll
-        for (int j = 0; j < LN_MAXD / 32; j++)
-            if (j < per) {
-                const int c = lane + 32 * j;
-                const float dyv = dy[r * d + c];
-                xh[j] = (x[r * d + c] - mu) * rs;
-                gv[j] = dyv * gamma[c];
-                s1 += gv[j];
-                s2 += gv[j] * xh[j];
-                pg[j] += dyv * xh[j];
-                pb[j] += dyv;
-            }
-        const float m1 = warp_sum_f(s1) / static_cast<float>(d), m2 = warp_sum_f(s2) / static_cast<float>(d);
+        for (int j = 0; j < PER; j++) {
+            const int64_t e = r * D + lane + 32 * j;
+            dyv[i][j] = in ? dy[e] : 0.0f;
+            xv[i][j] = in ? x[e] : 0.0f;
+            dxv[i][j] = in && accumulate ? dx[e] : 0.0f;
+        }
+    }
+    float gam[PER], pg[PER], pb[PER];
 #pragma unroll
-        for (int j = 0; j < LN_MAXD / 32; j++)
-            if (j < per) {
-                const int64_t e = r * d + lane + 32 * j;
-                const float g = rs * (gv[j] - m1 - xh[j] * m2);
-                dx[e] = accumulate ? dx[e] + g : g;
-            }
+    for (int j = 0; j < PER; j++) {
+        gam[j] = gamma[lane + 32 * j];
+        pg[j] = pb[j] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < LN_MAXD / 32; j++)
-        if (j < per) {
-            sh[warp][0][lane + 32 * j] = pg[j];
-            sh[warp][1][lane + 32 * j] = pb[j];
+    for (int i = 0; i < RPW; i++) {
+        const int64_t r = row0 + warp + static_cast<int64_t>(LN_WARPS) * i;
+        float gv[PER], xh[PER];
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            xh[j] = (xv[i][j] - mu[i]) * rs[i];
+            gv[j] = dyv[i][j] * gam[j];
+            s1 += gv[j];
+            s2 += gv[j] * xh[j];
+            pg[j] += dyv[i][j] * xh[j];  // rows beyond the end add dy = 0
+            pb[j] += dyv[i][j];
         }
+        const float m1 = warp_sum_f(s1) / static_cast<float>(D), m2 = warp_sum_f(s2) / static_cast<float>(D);
+        if (r < rows) {
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const int64_t e = r * D + lane + 32 * j;
+                const float g = rs[i] * (gv[j] - m1 - xh[j] * m2);
+                dx[e] = accumulate ? dxv[i][j] + g : g;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        sh[warp][0][lane + 32 * j] = pg[j];
+        sh[warp][1][lane + 32 * j] = pb[j];
+    }
     __syncthreads();
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
         float sg = 0.0f, sb = 0.0f;
         for (int w = 0; w < LN_WARPS; w++) {
             sg += sh[w][0][c];
             sb += sh[w][1][c];
         }
-        part[(static_cast<int64_t>(blockIdx.x) * 2) * d + c] = sg;
-        part[(static_cast<int64_t>(blockIdx.x) * 2 + 1) * d + c] = sb;
+        part[(static_cast<int64_t>(blockIdx.x) * 2) * D + c] = sg;
+        part[(static_cast<int64_t>(blockIdx.x) * 2 + 1) * D + c] = sb;
     }
 }
 
 // dgamma[c] += sum of part[b][0][c], dbeta[c] += sum of part[b][1][c] over
-// blocks b: one warp per column, lanes take blocks lane, lane + 32, ...,
-// then a fixed butterfly.
-__global__ void k_ln_params_sum(const float *part, float *dgamma, float *dbeta, int d, int nblocks) {
-    const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (c >= d) return;
+// blocks b.  Block = 32 columns x 8 row groups: thread (g, c) adds blocks g,
+// g + 8, ... in order (32 consecutive columns per load: one 128-byte line),
+// then the 8 group sums are added in group order.
+__global__ void __launch_bounds__(256) k_ln_params_sum(const float *part, float *dgamma, float *dbeta, int d,
+                                                       int nblocks) {
+    __shared__ float sg_s[8][32], sb_s[8][32];
+    const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + cl;
     float sg = 0.0f, sb = 0.0f;
-    for (int b = lane; b < nblocks; b += 32) {
-        sg += part[(static_cast<int64_t>(b) * 2) * d + c];
-        sb += part[(static_cast<int64_t>(b) * 2 + 1) * d + c];
+    if (c < d) {
+        // eight blocks' values loaded before they are added (in block order)
+        for (int b0 = grp; b0 < nblocks; b0 += 64) {
+            float vg[8], vb[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int b = b0 + 8 * j;
+                vg[j] = b < nblocks ? part[(static_cast<int64_t>(b) * 2) * d + c] : 0.0f;
+                vb[j] = b < nblocks ? part[(static_cast<int64_t>(b) * 2 + 1) * d + c] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                sg += vg[j];
+                sb += vb[j];
+            }
+        }
     }
-    sg = warp_sum_f(sg);
-    sb = warp_sum_f(sb);
-    if (lane == 0) {
-        dgamma[c] += sg;
-        dbeta[c] += sb;
+    sg_s[grp][cl] = sg;
+    sb_s[grp][cl] = sb;
+    __syncthreads();
+    if (grp == 0 && c < d) {
+        float tg = 0.0f, tb = 0.0f;
+        for (int g = 0; g < 8; g++) {
+            tg += sg_s[g][cl];
+            tb += sb_s[g][cl];
+        }
+        dgamma[c] += tg;
+        dbeta[c] += tb;
     }
 }
 
@@ -406,17 +446,32 @@ extern "C" st_status st_layernorm_bwd(st_handle *h, const float *dy, const float
         d > LN_MAXD)
         return h->fail(ST_INVALID_ARG, "st_layernorm_bwd: bad arguments (d a multiple of 32 up to %d)", LN_MAXD);
     cudaSetDevice(h->device);
-    const int64_t nblocks = (rows + LN_ROWS - 1) / LN_ROWS;
+    // rows per warp: as many as fit 32 registers of each of dy, x, dx
+    const int per = static_cast<int>(d / 32), rpw = std::max(1, 32 / per);
+    const int64_t block_rows = static_cast<int64_t>(LN_WARPS) * rpw;
+    const int64_t nblocks = (rows + block_rows - 1) / block_rows;
     if (nblocks > (1LL << 31) - 1) return h->fail(ST_UNSUPPORTED_SHAPE, "st_layernorm_bwd: too many rows");
     float *part = static_cast<float *>(st_scratch(h, SLOT_STEP, sizeof(float) * 2 * nblocks * d));
     if (!part) return ST_NO_MEMORY;
-    k_ln_bwd<<<static_cast<unsigned>(nblocks), LN_WARPS * 32, 0, h->stream>>>(dy, x, gamma, mean, rstd, dx, part, rows,
-                                                                            static_cast<int>(d), accumulate);
+    const dim3 grid(static_cast<unsigned>(nblocks)), block(LN_WARPS * 32);
+    switch (per) {
+#define ST_LN_BWD(P)                                                                                     \
+    case P:                                                                                              \
+        k_ln_bwd<P, (32 / P > 1 ? 32 / P : 1)><<<grid, block, 0, h->stream>>>(dy, x, gamma, mean, rstd, dx, \
+                                                                              part, rows, accumulate);   \
+        break;
+        ST_LN_BWD(1) ST_LN_BWD(2) ST_LN_BWD(3) ST_LN_BWD(4) ST_LN_BWD(5) ST_LN_BWD(6) ST_LN_BWD(7) ST_LN_BWD(8)
+        ST_LN_BWD(9) ST_LN_BWD(10) ST_LN_BWD(11) ST_LN_BWD(12) ST_LN_BWD(13) ST_LN_BWD(14) ST_LN_BWD(15)
+        ST_LN_BWD(16)
+#undef ST_LN_BWD
+        default:
+            return h->fail(ST_INVALID_ARG, "st_layernorm_bwd: d = %lld", static_cast<long long>(d));
+    }
     st_status s = st_after_launch(h, "k_ln_bwd");
     if (s != ST_OK) return s;
-    k_ln_params_sum<<<static_cast<unsigned>((d + 7) / 8), 256, 0, h->stream>>>(part, dgamma, dbeta,
-                                                                              static_cast<int>(d),
-                                                                              static_cast<int>(nblocks));
+    k_ln_params_sum<<<static_cast<unsigned>((d + 31) / 32), 256, 0, h->stream>>>(part, dgamma, dbeta,
+                                                                                static_cast<int>(d),
+                                                                                static_cast<int>(nblocks));
     return st_after_launch(h, "k_ln_params_sum");
 }
 
