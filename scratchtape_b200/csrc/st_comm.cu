@@ -14,10 +14,10 @@
 //   lie in the union of the shards' best k.  This is k_merge_parts
 //   (src/gpu_step/knn.rs:661-715) across GPUs instead of across one GPU's
 //   key parts.  The scans that seed their per-query thresholds from samples
-//   of the keys take the maximum of each seed over the ranks (two small
-//   ncclAllReduce MAX calls, nq x 4 bytes): any rank's 128th best over a sample
-//   bounds the global 128th best from below, so each rank filters as tightly
-//   as one GPU holding every key would.
+//   of the keys share each sampling stage's lists (an ncclAllGather of nq x 128
+//   x 8 bytes per rank and a merge, twice): the 128th best of the union of the
+//   ranks' samples bounds the global 128th best from below, so each rank
+//   filters as tightly as one GPU holding every key would.
 //
 // NCCL is resolved at run time (dlopen of libnccl.so.2, preferring a copy the
 // process has already loaded -- e.g. torch's -- so a communicator made by the
@@ -83,25 +83,31 @@ const NcclApi &nccl() {
 
 constexpr int64_t KLIST = 128;  // entries per query in a best-128 list
 
-// The handle's threshold exchange during a sharded scan: the per-query
-// published 128th-best scores (order-preserving u32) become their maximum over
-// the ranks, in place, on the handle's stream.
-st_status max_over_ranks(st_handle *h, uint32_t *gthr, int64_t nq, void *ctx) {
-    ST_CHECK_NCCL(h, nccl().all_reduce(gthr, gthr, static_cast<size_t>(nq), ncclUint32, ncclMax,
-                                       static_cast<ncclComm_t>(ctx), h->stream));
-    return ST_OK;
+// The handle's seed exchange during a sharded scan: a sampling stage's merged
+// best-128 lists (nq x 128 sortable keys) are all-gathered and merged into the
+// best 128 of every rank's sample, in place, on the handle's stream.
+struct SeedExchange {
+    ncclComm_t comm;
+    int world;
+    uint64_t *gathered;  // [world][nq][128]
+};
+st_status merge_seeds(st_handle *h, uint64_t *seed_lists, int64_t nq, void *ctx) {
+    const SeedExchange *x = static_cast<const SeedExchange *>(ctx);
+    ST_CHECK_NCCL(h, nccl().all_gather(seed_lists, x->gathered, static_cast<size_t>(nq) * KLIST, ncclUint64, x->comm,
+                                       h->stream));
+    return st_knn_merge_keys(h, x->gathered, x->world, nq * KLIST, nq, seed_lists);
 }
 
-// Clears the handle's threshold exchange when the sharded call returns.
+// Clears the handle's seed exchange when the sharded call returns.
 struct ExchangeScope {
     st_handle *h;
-    ExchangeScope(st_handle *hh, void *comm) : h(hh) {
-        h->thr_exchange = max_over_ranks;
-        h->thr_ctx = comm;
+    ExchangeScope(st_handle *hh, SeedExchange *x) : h(hh) {
+        h->seed_exchange = merge_seeds;
+        h->seed_ctx = x;
     }
     ~ExchangeScope() {
-        h->thr_exchange = nullptr;
-        h->thr_ctx = nullptr;
+        h->seed_exchange = nullptr;
+        h->seed_ctx = nullptr;
     }
 };
 
@@ -169,33 +175,33 @@ extern "C" st_status st_knn_search_sharded(st_handle *h, const uint8_t *codes, c
     int world = 0;
     ST_CHECK_NCCL(h, api.comm_count(c, &world));
     const size_t list_bytes = sizeof(uint64_t) * static_cast<size_t>(nq) * KLIST;
-    const size_t thr_bytes = (sizeof(uint32_t) * static_cast<size_t>(nq) + 255) & ~size_t(255);
-    uint8_t *buf = static_cast<uint8_t *>(st_scratch(h, SLOT_COMM, list_bytes * (world + 2) + thr_bytes));
+    uint8_t *buf = static_cast<uint8_t *>(st_scratch(h, SLOT_COMM, list_bytes * (world + 3)));
     if (!buf) return ST_NO_MEMORY;
     uint64_t *local = reinterpret_cast<uint64_t *>(buf);
     uint64_t *gathered = reinterpret_cast<uint64_t *>(buf + list_bytes);
     uint64_t *merged = reinterpret_cast<uint64_t *>(buf + list_bytes * (world + 1));
     st_status s;
     // The scans that seed their thresholds from samples share the seeds: every rank
-    // takes the same two exchanges (a rank with an empty shard contributes zeros,
-    // which rank below every published score).
+    // takes the same two exchanges (the gathered buffer holds them while the local
+    // scan runs; a rank with an empty shard contributes empty lists -- key 0 ranks
+    // below every real key).
     const bool seeded = world > 1 && st_knn_seeded_route(dim, nq, mode, prec);
+    SeedExchange x{c, world, gathered};
     if (n_local > 0) {
         if (seeded) {
-            ExchangeScope scope(h, comm);
+            ExchangeScope scope(h, &x);
             s = st_knn_topk_keys(h, codes, scales, n_local, dim, queries, nq, mode, prec, index_base, local);
         } else {
             s = st_knn_topk_keys(h, codes, scales, n_local, dim, queries, nq, mode, prec, index_base, local);
         }
         if (s != ST_OK) return s;
     } else {
-        // an empty shard contributes empty lists (key 0 ranks below every real key)
         ST_CHECK_CUDA(h, cudaMemsetAsync(local, 0, list_bytes, h->stream));
         if (seeded) {
-            uint32_t *thr = reinterpret_cast<uint32_t *>(buf + list_bytes * (world + 2));
-            ST_CHECK_CUDA(h, cudaMemsetAsync(thr, 0, sizeof(uint32_t) * nq, h->stream));
+            uint64_t *seed = reinterpret_cast<uint64_t *>(buf + list_bytes * (world + 2));
             for (int stage = 0; stage < 2; stage++) {
-                s = max_over_ranks(h, thr, nq, comm);
+                ST_CHECK_CUDA(h, cudaMemsetAsync(seed, 0, list_bytes, h->stream));
+                s = merge_seeds(h, seed, nq, &x);
                 if (s != ST_OK) return s;
             }
         }

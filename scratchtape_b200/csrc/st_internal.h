@@ -49,10 +49,12 @@ struct st_handle {
     void *mlp_ctl = nullptr;     // fused MLP step counters: where they were last zeroed, and how many bytes
     size_t mlp_ctl_bytes = 0;
     // Set by the sharded kNN search for the duration of its local scan: after each of
-    // the two sampling stages the scan calls it on the per-query published 128th-best
-    // scores (nq order-preserving u32), which it replaces by their maximum over the ranks.
-    st_status (*thr_exchange)(st_handle *h, uint32_t *gthr, int64_t nq, void *ctx) = nullptr;
-    void *thr_ctx = nullptr;
+    // the two sampling stages the scan calls it on the stage's merged best-128 lists
+    // (nq rows of 128 sortable keys, zeros where the stage did not run on this rank),
+    // which it replaces by the merge of every rank's lists -- the best 128 of the union
+    // of the ranks' samples, from which the next stage's thresholds are seeded.
+    st_status (*seed_exchange)(st_handle *h, uint64_t *seed_lists, int64_t nq, void *ctx) = nullptr;
+    void *seed_ctx = nullptr;
 
     st_status fail(st_status s, const char *fmt, ...) {
         char buf[512];
@@ -90,5 +92,5 @@ bool st_make_map_4d(CUtensorMap *map, CUtensorMapDataType dtype, int elem_bytes,
                     std::string *why);
 
 // Whether a kNN scan of nq queries at this dim / mode / precision runs the two
-// threshold-seeding stages (and so calls h->thr_exchange exactly twice).
+// threshold-seeding stages (and so calls h->seed_exchange exactly twice).
 bool st_knn_seeded_route(int32_t dim, int64_t nq, int32_t mode, int32_t prec);

@@ -2814,22 +2814,26 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         };
         // two sample passes seed the thresholds (every 1024th, then every 16th tile):
         // a list's 128th best over a subset bounds the final 128th best from below
-        // With h->thr_exchange set (a key-sharded search), every stage ends with the
-        // maximum over the ranks: a rank's 128th best over its sample bounds the
-        // global 128th best from below too, and only keys reaching the global 128th
-        // best can be in the merged result.
+        // With h->seed_exchange set (a key-sharded search), every stage's lists are
+        // merged with the other ranks' before seeding: the 128th best of the union of
+        // the ranks' samples bounds the global 128th best from below, and only keys
+        // reaching the global 128th best can be in the merged result.
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
-            if (sample * nqb >= 4 * h->num_sms && sample < tiles) {
+            const bool run_stage = sample * nqb >= 4 * h->num_sms && sample < tiles;
+            if (run_stage) {
                 s = pass(stride, 0, seed_keys);
                 if (s != ST_OK) return s;
+            }
+            if (h->seed_exchange) {
+                if (!run_stage) ST_CHECK_CUDA(h, cudaMemsetAsync(seed_keys, 0, seed_bytes, h->stream));
+                s = h->seed_exchange(h, seed_keys, nq, h->seed_ctx);
+                if (s != ST_OK) return s;
+            }
+            if (run_stage || h->seed_exchange) {
                 k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
                                                                                            static_cast<int>(nq), gthr);
                 s = st_after_launch(h, "k_knn_seed");
-                if (s != ST_OK) return s;
-            }
-            if (h->thr_exchange) {
-                s = h->thr_exchange(h, gthr, nq, h->thr_ctx);
                 if (s != ST_OK) return s;
             }
         }
@@ -2902,11 +2906,12 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
         // next pass starts from it instead of from its own first keys.  Two
         // levels: every 1024th tile seeds a pass over every 16th, which seeds the
         // full scan.
-        // (with h->thr_exchange set, each stage ends with the maximum over the ranks,
-        // as in the keys-in-TMEM scan above)
+        // (with h->seed_exchange set, each stage's lists are merged with the other
+        // ranks' before seeding, as in the keys-in-TMEM scan above)
         for (int64_t stride : {int64_t(1024), int64_t(16)}) {
             const int64_t sample = (tiles + stride - 1) / stride;
-            if (sample >= 2 * h->num_sms) {
+            const bool run_stage = sample >= 2 * h->num_sms;
+            if (run_stage) {
                 NarrowArgs gs = g;
                 const int64_t gsplits = std::min<int64_t>(sample_splits, sample);
                 gs.units = static_cast<int>(gsplits * nqb);
@@ -2918,13 +2923,16 @@ static st_status topk_keys(st_handle *h, const uint8_t *codes, const float *scal
                 s = merge_lists(h, unit_out, gsplits * N_QUAD, nq_pad * KTOP, nq, merge_tmp, MERGE_GROUPS,
                                 seed_keys);
                 if (s != ST_OK) return s;
+            }
+            if (h->seed_exchange) {
+                if (!run_stage) ST_CHECK_CUDA(h, cudaMemsetAsync(seed_keys, 0, seed_bytes, h->stream));
+                s = h->seed_exchange(h, seed_keys, nq, h->seed_ctx);
+                if (s != ST_OK) return s;
+            }
+            if (run_stage || h->seed_exchange) {
                 k_knn_seed<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, h->stream>>>(seed_keys,
                                                                                            static_cast<int>(nq), gthr);
                 s = st_after_launch(h, "k_knn_seed");
-                if (s != ST_OK) return s;
-            }
-            if (h->thr_exchange) {
-                s = h->thr_exchange(h, gthr, nq, h->thr_ctx);
                 if (s != ST_OK) return s;
             }
         }

@@ -10,8 +10,9 @@
   st_avg_params on a communicator made by st_nccl_comm_init): identical to
   the torch.distributed route.
 * a C-ABI search large enough for the sampling stages (the keys-in-TMEM scan
-  with 300 queries, the narrow scan with 20), whose seeds are exchanged as a
-  maximum over the ranks: identical, bit for bit, to one scan of all keys.
+  with 300 queries, the narrow scan with 20), whose stages' best-128 lists
+  are merged across the ranks before seeding: identical, bit for bit, to one
+  scan of all keys.
 """
 import os
 import socket
