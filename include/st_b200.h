@@ -344,7 +344,12 @@ ST_API st_status st_avg_params(st_handle *h, float *p, int64_t n, void *comm);
  * scales as st_knn_search; n_local may be 0) and every rank passes the same
  * queries.  Each rank scans its shard, the per-query best-128 lists are
  * all-gathered over NCCL and merged, and every rank gets the global best k
- * (out_scores / out_ids as st_knn_search, ids global).  Replaces
+ * (out_scores / out_ids as st_knn_search, ids global).  Where the scan
+ * seeds its thresholds from samples of the keys (dim 256: up to 32 queries,
+ * or more than 32 EXACT dot-product queries), each sampling stage's lists
+ * are also all-gathered and merged, so every rank filters against the best
+ * 128 of all ranks' samples.  Every rank must call it with the same nq, dim,
+ * mode and prec (the collectives are the same on every rank).  Replaces
  * k_sort_lists + k_merge_parts (src/gpu_step/knn.rs:661-715) across GPUs. */
 ST_API st_status st_knn_search_sharded(st_handle *h, const uint8_t *codes, const float *scales, int64_t n_local,
                                        int32_t dim, const float *queries, int64_t nq, int32_t k, int32_t mode,
@@ -357,9 +362,12 @@ ST_API st_status st_knn_search_sharded(st_handle *h, const uint8_t *codes, const
  * DOT: q.k, largest first.  L2: |k|^2 - 2 q.k + |q|^2 clamped at 0,
  * smallest first.  Ties go to the lower key index. */
 typedef enum { ST_KNN_DOT = 0, ST_KNN_L2 = 1 } st_knn_mode;
-/* Arithmetic.  EXACT: the query is split into two f16 parts (power-of-two
- * prescaled), the codes c = 2u - 3 are exact, f32 accumulation on tcgen05:
- * error about 2^-22 of sum_i |q_i k_i|.  F16REF: the reference's numerics --
+/* Arithmetic.  EXACT: every returned score within about 2^-22 of
+ * sum_i |q_i k_i| of the exact score -- more than 32 dot-product queries at
+ * dim 256 are filtered on the tensor cores and rescored exactly in f64 (one
+ * rounding); up to 32 queries at dim 256 use a 30-bit fixed-point query with
+ * exact integer products; other shapes split the query into two f16 parts
+ * with f32 accumulation.  F16REF: the reference's numerics --
  * query and dequantised key (u - 1.5) * scale rounded to f16 before the
  * product (knn.rs:403-411, :630-643). */
 typedef enum { ST_KNN_EXACT = 0, ST_KNN_F16REF = 1 } st_knn_prec;
