@@ -258,7 +258,7 @@ struct FwdSmem {
 // and r + 128 share row r: each takes half of the row's key columns (warps w
 // and w + 4 read the same TMEM lanes); row reductions go through `red`.
 template <bool F32, int TK>
-__global__ void __launch_bounds__(ATHREADS, 1) k_attn_fwd(const AttnArgs g) {
+__global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const AttnArgs g) {
     using L = FwdSmem<TK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -632,16 +632,26 @@ st_status check(st_handle *h, const void *q, const void *k, const void *v, int64
     return ST_OK;
 }
 
+// The 128-key forward fits two CTAs per SM (82 KB of shared memory, 256 TMEM
+// columns, 128 registers a thread): with more CTAs than SMs every one is
+// resident in one wave.  With at most one per SM the launch asks for more than
+// half an SM's shared memory, so the CTAs spread over the SMs instead of
+// pairing up on half of them.
+constexpr int FWD_SPREAD_SMEM = 120 * 1024;
+
 template <bool F32, int TK>
 st_status launch_fwd_tk(st_handle *h, const AttnArgs &g) {
+    constexpr int spread = TK == 128 && FwdSmem<TK>::SIZE < FWD_SPREAD_SMEM ? FWD_SPREAD_SMEM : FwdSmem<TK>::SIZE;
     static bool attr = false;
     if (!attr) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<F32, TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              FwdSmem<TK>::SIZE));
+                                              spread));
         attr = true;
     }
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>((g.t + AT - 1) / AT));
-    k_attn_fwd<F32, TK><<<grid, ATHREADS, FwdSmem<TK>::SIZE, h->stream>>>(g);
+    const int64_t ctas = static_cast<int64_t>(grid.x) * grid.y;
+    const int smem = ctas > h->num_sms ? FwdSmem<TK>::SIZE : spread;
+    k_attn_fwd<F32, TK><<<grid, ATHREADS, smem, h->stream>>>(g);
     return st_after_launch(h, "k_attn_fwd");
 }
 
