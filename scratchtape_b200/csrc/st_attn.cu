@@ -57,7 +57,15 @@ struct AttnArgs {
     float scale;
     int causal;
     int one;  // softmax1 (forward): a phantom zero logit in every row's denominator
+    int tma;  // f16 per-head inputs: operand tiles by TMA (maps tq, tk, tv[, to, tdo]) instead of thread loads
     int *status;
+};
+
+// The tensor maps of the TMA-staged forward and backward: per-head f16
+// tensors [bh, t, 64] as {64 columns, t rows, bh heads}, boxes of 128 rows,
+// 128-byte swizzle (the layout the thread-loaded tiles use), zero fill past t.
+struct HeadMaps {
+    CUtensorMap q, k, v, o, dout;
 };
 
 // Bounded wait on a barrier that the MMA thread's commit completes.
@@ -73,39 +81,62 @@ __device__ __forceinline__ bool await(uint64_t *bar, uint32_t parity, int *statu
     }
 }
 
-// Rows [row0, row0 + nrows) of head z of a tensor (row map m) into a
-// 128-byte-swizzled [nrows x 64] f16 tile, zero rows at and beyond t.  Every
-// thread first loads all of its 16-byte pieces (up to nrows / 32 of them),
-// then stores them, so a thread's loads are in flight together; F32 sources
-// are rounded to f16 on the way.
-template <bool F32, int NROWS>
-__device__ __forceinline__ void stage_rows(uint8_t *dst, const void *base, const RowMap &m, int z, int heads,
-                                           int row0, int t) {
-    constexpr int PER = NROWS * 8 / ATHREADS;  // 16-byte f16 pieces per thread
-    uint4 v[PER];
+// Up to N [128 x 64] row ranges into 128-byte-swizzled f16 tiles: source i
+// is rows row0[i] .. row0[i] + 127 of head z of src[i] (row map map[i]) into
+// dst[i] (a null dst skips the source).  Every thread issues its loads of all
+// the sources before any store, so one global round trip covers them all;
+// rows at and beyond t are zero, and f32 sources are rounded to f16 on the way.
+template <int N>
+struct Tiles {
+    uint8_t *dst[N];
+    const void *src[N];
+    RowMap map[N];
+    int row0[N];
+};
+
+template <bool F32, int N>
+__device__ __forceinline__ void stage_tiles(const Tiles<N> &s, int z, int heads, int t) {
+    constexpr int PER = AT * 8 / ATHREADS;  // 16-byte f16 pieces per thread per tile
+    constexpr int W = F32 ? 2 : 1;          // 16-byte loads per piece
+    uint4 raw[N][PER][W];
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
-        const int gr = row0 + r;
-        v[i] = make_uint4(0u, 0u, 0u, 0u);
-        if (gr < t) {
-            const int64_t off = m.at(z, heads, gr) + 8 * c;
-            if (F32) {
-                const float4 *s = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off);
-                const float4 a = __ldg(s), b = __ldg(s + 1);
-                const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-                const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
-                v[i] = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
-                                  *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
-            } else {
-                v[i] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __half *>(base) + off));
+    for (int i = 0; i < N; i++) {
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int p = threadIdx.x + j * ATHREADS, r = p >> 3, c = p & 7;
+            const int gr = s.row0[i] + r;
+#pragma unroll
+            for (int w = 0; w < W; w++) raw[i][j][w] = make_uint4(0u, 0u, 0u, 0u);
+            if (s.dst[i] && gr < t) {
+                const int64_t off = s.map[i].at(z, heads, gr) + 8 * c;
+                if (F32) {
+                    const uint4 *q = reinterpret_cast<const uint4 *>(static_cast<const float *>(s.src[i]) + off);
+                    raw[i][j][0] = __ldg(q);
+                    raw[i][j][W - 1] = __ldg(q + (W - 1));
+                } else {
+                    raw[i][j][0] = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __half *>(s.src[i]) + off));
+                }
             }
         }
     }
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        const int p = threadIdx.x + i * ATHREADS, r = p >> 3, c = p & 7;
-        *reinterpret_cast<uint4 *>(dst + st::sw128_offset(r, c)) = v[i];
+    for (int i = 0; i < N; i++) {
+        if (!s.dst[i]) continue;
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int p = threadIdx.x + j * ATHREADS;
+            uint4 v = raw[i][j][0];
+            if (F32) {
+                const uint4 a = raw[i][j][0], b = raw[i][j][W - 1];
+                const __half2 h0 = __floats2half2_rn(__uint_as_float(a.x), __uint_as_float(a.y));
+                const __half2 h1 = __floats2half2_rn(__uint_as_float(a.z), __uint_as_float(a.w));
+                const __half2 h2 = __floats2half2_rn(__uint_as_float(b.x), __uint_as_float(b.y));
+                const __half2 h3 = __floats2half2_rn(__uint_as_float(b.z), __uint_as_float(b.w));
+                v = make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
+                               *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
+            }
+            *reinterpret_cast<uint4 *>(s.dst[i] + st::sw128_offset(p >> 3, p & 7)) = v;
+        }
     }
 }
 
@@ -258,7 +289,7 @@ struct FwdSmem {
 // and r + 128 share row r: each takes half of the row's key columns (warps w
 // and w + 4 read the same TMEM lanes); row reductions go through `red`.
 template <bool F32, int TK>
-__global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const AttnArgs g) {
+__global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
     using L = FwdSmem<TK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -274,16 +305,27 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
     const int64_t ro = g.mo.at(z, g.heads, gr < g.t ? gr : 0);
     const bool live = gr < g.t;
 
+    const bool tma = !F32 && g.tma;
     if (tid == 0) {
         st::mbar_init(&bar[0], 1);
         st::mbar_init(&bar[1], 1);
+        st::mbar_init(&bar[3], 1);
         st::fence_mbar_init();
+        if (tma) {  // Q, and K, V in 128-row boxes up to the last key this tile sees
+            const int nkb = (kc + AT - 1) / AT;
+            st::mbar_arrive_expect_tx(&bar[3], static_cast<uint32_t>(TILE * (1 + 2 * nkb)));
+            st::tma_load_4d(sQ, &tm.q, &bar[3], 0, q0, z, 0);
+            for (int b = 0; b < nkb; b++) {
+                st::tma_load_4d(sK + b * TILE, &tm.k, &bar[3], 0, b * AT, z, 0);
+                st::tma_load_4d(sV + b * TILE, &tm.v, &bar[3], 0, b * AT, z, 0);
+            }
+        }
     }
     if (warp == 0) {
         st::tmem_alloc(tslot, L::TMEM);
         st::tmem_relinquish();
     }
-    stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
+    if (!tma) stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
@@ -292,10 +334,12 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
     if (tid == 0) {  // S = Q K^T over kc16 keys
-        const uint32_t id = st::idesc_make(1, 0, false, false, AT, kc16);
-        const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK);
+        if (!tma || await(&bar[3], 0, g.status)) {
+            const uint32_t id = st::idesc_make(1, 0, false, false, AT, kc16);
+            const uint32_t q = st::smem_u32(sQ), k = st::smem_u32(sK);
 #pragma unroll
-        for (int kk = 0; kk < AD / 16; kk++) st::umma_f16(tS, kmaj(q, kk), kmaj(k, kk), id, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < AD / 16; kk++) st::umma_f16(tS, kmaj(q, kk), kmaj(k, kk), id, kk > 0 ? 1u : 0u);
+        }
         st::umma_commit(&bar[0]);
     }
     bool ok = await(&bar[0], 0, g.status);
@@ -408,20 +452,83 @@ constexpr int B_Q = 0, B_DO = TILE, B_K = 2 * TILE, B_V = 3 * TILE, B_P = 4 * TI
 constexpr int B_RED = B_S + PT, B_BAR = B_RED + 2 * AT * 4;
 constexpr int BWD_SMEM = B_BAR + 64 + 1024;
 
-// For query tile qt: D_r = sum_d dO[r,d] O[r,d] (both halves, the same order
-// on both threads of the row) and the row's log-sum-exp; Q and dO staged.
+// dot_half's sum for f16 rows held in 128-byte-swizzled tiles: row r,
+// columns 32 half .. 32 half + 31, in the same order (so the same bits).
+__device__ __forceinline__ float dot_half_tiles(const uint8_t *ta, const uint8_t *tb, int r, int half) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint4 x = *reinterpret_cast<const uint4 *>(ta + st::sw128_offset(r, 4 * half + c));
+        const uint4 y = *reinterpret_cast<const uint4 *>(tb + st::sw128_offset(r, 4 * half + c));
+        const uint32_t xv[4] = {x.x, x.y, x.z, x.w}, yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 fa = __half22float2(*reinterpret_cast<const __half2 *>(&xv[i]));
+            const float2 fb = __half22float2(*reinterpret_cast<const __half2 *>(&yv[i]));
+            acc = fmaf(fa.x, fb.x, acc);
+            acc = fmaf(fa.y, fb.y, acc);
+        }
+    }
+    return acc;
+}
+
+// Stages key tile kt (K, V; none when kt < 0) and query tile qt (Q, dO; none
+// when qt < 0), and for a query tile computes D_r = sum_d dO[r,d] O[r,d]
+// (both halves of the row, the same order on both threads) and the row's
+// log-sum-exp.  f16 inputs take one global round trip for everything: O is
+// staged too, into the P tile's space (free until bwd_scores writes P), and D
+// is read from shared memory; with g.tma the tiles come by TMA (one mbarrier,
+// `tbar`, phase `tph`).  f32 inputs take one round trip per pair of tiles (to
+// bound registers) and D from the f32 rows in memory.  False when the TMA
+// wait ran out (the status word says so).
 template <bool F32>
-__device__ __forceinline__ void bwd_stage_queries(const AttnArgs &g, uint8_t *smem, float *red, int z, int qt,
-                                                  float &dsum, float &lse) {
+__device__ __forceinline__ bool bwd_stage(const AttnArgs &g, const HeadMaps &tm, uint64_t *tbar, uint32_t &tph,
+                                          uint8_t *smem, float *red, int z, int qt, int kt, float &dsum, float &lse) {
     const int r = threadIdx.x & (AT - 1), half = threadIdx.x >> 7, gr = qt * AT + r;
-    stage_rows<F32, AT>(smem + B_Q, g.q, g.mq, z, g.heads, qt * AT, g.t);
-    stage_rows<F32, AT>(smem + B_DO, g.dout, g.mo, z, g.heads, qt * AT, g.t);
-    const float part = gr < g.t ? dot_half<F32>(g.o, g.dout, g.mo.at(z, g.heads, gr), half) : 0.0f;
+    const bool qrow = qt >= 0 && gr < g.t;
+    lse = qrow ? g.lse[static_cast<int64_t>(z) * g.t + gr] : 0.0f;
+    uint8_t *kd = kt >= 0 ? smem + B_K : nullptr, *vd = kt >= 0 ? smem + B_V : nullptr;
+    uint8_t *qd = qt >= 0 ? smem + B_Q : nullptr, *dd = qt >= 0 ? smem + B_DO : nullptr;
+    bool ok = true;
+    if (!F32 && g.tma) {
+        if (threadIdx.x == 0) {
+            st::mbar_arrive_expect_tx(tbar, static_cast<uint32_t>(TILE * ((kt >= 0 ? 2 : 0) + (qt >= 0 ? 3 : 0))));
+            if (kt >= 0) {
+                st::tma_load_4d(kd, &tm.k, tbar, 0, kt * AT, z, 0);
+                st::tma_load_4d(vd, &tm.v, tbar, 0, kt * AT, z, 0);
+            }
+            if (qt >= 0) {
+                st::tma_load_4d(qd, &tm.q, tbar, 0, qt * AT, z, 0);
+                st::tma_load_4d(dd, &tm.dout, tbar, 0, qt * AT, z, 0);
+                st::tma_load_4d(smem + B_P, &tm.o, tbar, 0, qt * AT, z, 0);
+            }
+        }
+        ok = await(tbar, tph, g.status);
+        tph ^= 1u;
+    } else if (F32) {
+        if (kt >= 0) stage_tiles<true, 2>(Tiles<2>{{kd, vd}, {g.k, g.v}, {g.mq, g.mq}, {kt * AT, kt * AT}}, z, g.heads, g.t);
+        if (qt >= 0)
+            stage_tiles<true, 2>(Tiles<2>{{qd, dd}, {g.q, g.dout}, {g.mq, g.mo}, {qt * AT, qt * AT}}, z, g.heads, g.t);
+    } else {
+        stage_tiles<false, 5>(Tiles<5>{{kd, vd, qd, dd, qt >= 0 ? smem + B_P : nullptr},
+                                       {g.k, g.v, g.q, g.dout, g.o},
+                                       {g.mq, g.mq, g.mq, g.mo, g.mo},
+                                       {kt * AT, kt * AT, qt * AT, qt * AT, qt * AT}},
+                              z, g.heads, g.t);
+    }
+    if (qt < 0) return ok;
+    float part;
+    if (F32) {
+        part = qrow ? dot_half<true>(g.o, g.dout, g.mo.at(z, g.heads, gr), half) : 0.0f;
+    } else {
+        __syncthreads();  // O and dO tiles complete
+        part = qrow ? dot_half_tiles(smem + B_P, smem + B_DO, r, half) : 0.0f;
+    }
     red[half * AT + r] = part;
-    lse = gr < g.t ? g.lse[static_cast<int64_t>(z) * g.t + gr] : 0.0f;
     __syncthreads();
     dsum = red[r] + red[AT + r];
-    __syncthreads();
+    __syncthreads();  // red and the staged O are read before either is reused
+    return ok;
 }
 
 // S = Q K^T and dP = dO V^T of one (query tile, key tile) pair, then P =
@@ -488,7 +595,7 @@ __device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uin
 // (D = rowsum(dO O) gives the softmax backward for softmax and softmax1
 // alike).  Every transposed operand is a shared-memory descriptor.
 template <bool F32>
-__global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
+__global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *red = reinterpret_cast<float *>(smem + B_RED);
@@ -502,6 +609,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     if (tid == 0) {
         st::mbar_init(&bar[0], 1);
         st::mbar_init(&bar[1], 1);
+        st::mbar_init(&bar[3], 1);
         st::fence_mbar_init();
     }
     if (warp == 0) {
@@ -514,16 +622,14 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     const uint32_t tmem = *tslot, tA = tmem + 256, tB = tmem + 320;  // dV / dQ, dK
     const uint32_t tQ = tmem + 384;                                   // dQ of a one-tile sequence
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t ph0 = 0, ph1 = 0;
+    uint32_t ph0 = 0, ph1 = 0, ph3 = 0;
     bool ok = true;
     if (key_role) {
         const int kt = tile;
-        stage_rows<F32, AT>(smem + B_K, g.k, g.mq, z, g.heads, kt * AT, g.t);
-        stage_rows<F32, AT>(smem + B_V, g.v, g.mq, z, g.heads, kt * AT, g.t);
         bool first = true;
         for (int qt = g.causal ? kt : 0; qt < ntile && ok; qt++) {
             float dsum, lse;
-            bwd_stage_queries<F32>(g, smem, red, z, qt, dsum, lse);
+            ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, qt, first ? kt : -1, dsum, lse) && ok;  // K, V too at first
             st::fence_proxy_async_smem();
             st::tc_fence_before();
             __syncthreads();
@@ -576,11 +682,13 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g) {
     } else {
         const int qt = tile;
         float dsum, lse;
-        bwd_stage_queries<F32>(g, smem, red, z, qt, dsum, lse);
+        ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, qt, 0, dsum, lse);  // the queries with key tile 0
         const int last = g.causal ? qt : ntile - 1;
         for (int kt = 0; kt <= last && ok; kt++) {
-            stage_rows<F32, AT>(smem + B_K, g.k, g.mq, z, g.heads, kt * AT, g.t);
-            stage_rows<F32, AT>(smem + B_V, g.v, g.mq, z, g.heads, kt * AT, g.t);
+            if (kt > 0) {
+                float unused0, unused1;
+                ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, -1, kt, unused0, unused1) && ok;
+            }
             st::fence_proxy_async_smem();
             st::tc_fence_before();
             __syncthreads();
@@ -640,7 +748,7 @@ st_status check(st_handle *h, const void *q, const void *k, const void *v, int64
 constexpr int FWD_SPREAD_SMEM = 120 * 1024;
 
 template <bool F32, int TK>
-st_status launch_fwd_tk(st_handle *h, const AttnArgs &g) {
+st_status launch_fwd_tk(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     constexpr int spread = TK == 128 && FwdSmem<TK>::SIZE < FWD_SPREAD_SMEM ? FWD_SPREAD_SMEM : FwdSmem<TK>::SIZE;
     static bool attr = false;
     if (!attr) {
@@ -651,17 +759,17 @@ st_status launch_fwd_tk(st_handle *h, const AttnArgs &g) {
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>((g.t + AT - 1) / AT));
     const int64_t ctas = static_cast<int64_t>(grid.x) * grid.y;
     const int smem = ctas > h->num_sms ? FwdSmem<TK>::SIZE : spread;
-    k_attn_fwd<F32, TK><<<grid, ATHREADS, smem, h->stream>>>(g);
+    k_attn_fwd<F32, TK><<<grid, ATHREADS, smem, h->stream>>>(g, tm);
     return st_after_launch(h, "k_attn_fwd");
 }
 
 template <bool F32>
-st_status launch_fwd(st_handle *h, const AttnArgs &g) {
-    return g.t <= AT ? launch_fwd_tk<F32, AT>(h, g) : launch_fwd_tk<F32, AMAXT>(h, g);
+st_status launch_fwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
+    return g.t <= AT ? launch_fwd_tk<F32, AT>(h, g, tm) : launch_fwd_tk<F32, AMAXT>(h, g, tm);
 }
 
 template <bool F32>
-st_status launch_bwd(st_handle *h, const AttnArgs &g) {
+st_status launch_bwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     static bool attr = false;
     if (!attr) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
@@ -669,11 +777,19 @@ st_status launch_bwd(st_handle *h, const AttnArgs &g) {
     }
     const int ntile = (g.t + AT - 1) / AT;
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(ntile == 1 ? 1 : 2 * ntile));
-    k_attn_bwd<F32><<<grid, ATHREADS, BWD_SMEM, h->stream>>>(g);
+    k_attn_bwd<F32><<<grid, ATHREADS, BWD_SMEM, h->stream>>>(g, tm);
     return st_after_launch(h, "k_attn_bwd");
 }
 
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The map of one per-head f16 tensor [bh, t, 64] (see HeadMaps); false when
+// the driver refuses it, and the kernels then stage with thread loads.
+bool head_map(CUtensorMap *m, const void *base, int64_t bh, int64_t t) {
+    return st_make_map_4d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, AD, static_cast<uint64_t>(t),
+                          static_cast<uint64_t>(bh), 1, AD, static_cast<uint64_t>(t * AD),
+                          static_cast<uint64_t>(bh * t * AD), AD, AT, CU_TENSOR_MAP_SWIZZLE_128B, nullptr);
+}
 
 }  // namespace
 
@@ -699,7 +815,9 @@ extern "C" st_status st_attn_fwd(st_handle *h, const void *q, const void *k, con
     g.causal = causal;
     g.one = one;
     g.status = h->d_status;
-    return launch_fwd<false>(h, g);
+    HeadMaps tm{};
+    g.tma = head_map(&tm.q, q, bh, t) && head_map(&tm.k, k, bh, t) && head_map(&tm.v, v, bh, t);
+    return launch_fwd<false>(h, g, tm);
 }
 
 extern "C" st_status st_attn_bwd(st_handle *h, const void *q, const void *k, const void *v, const void *o,
@@ -729,7 +847,10 @@ extern "C" st_status st_attn_bwd(st_handle *h, const void *q, const void *k, con
     g.scale = scale;
     g.causal = causal;
     g.status = h->d_status;
-    return launch_bwd<false>(h, g);
+    HeadMaps tm{};
+    g.tma = head_map(&tm.q, q, bh, t) && head_map(&tm.k, k, bh, t) && head_map(&tm.v, v, bh, t) &&
+            head_map(&tm.o, o, bh, t) && head_map(&tm.dout, dout, bh, t);
+    return launch_bwd<false>(h, g, tm);
 }
 
 extern "C" st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o, float *lse, int64_t batch,
@@ -757,7 +878,7 @@ extern "C" st_status st_attn_fwd_packed(st_handle *h, const float *qkv, float *o
     g.causal = causal;
     g.one = one;
     g.status = h->d_status;
-    return launch_fwd<true>(h, g);
+    return launch_fwd<true>(h, g, HeadMaps{});
 }
 
 extern "C" st_status st_attn_bwd_packed(st_handle *h, const float *qkv, const float *o, const float *dout,
@@ -789,5 +910,5 @@ extern "C" st_status st_attn_bwd_packed(st_handle *h, const float *qkv, const fl
     g.scale = scale;
     g.causal = causal;
     g.status = h->d_status;
-    return launch_bwd<true>(h, g);
+    return launch_bwd<true>(h, g, HeadMaps{});
 }
