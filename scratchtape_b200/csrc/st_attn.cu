@@ -311,6 +311,16 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
         st::mbar_init(&bar[1], 1);
         st::mbar_init(&bar[3], 1);
         st::fence_mbar_init();
+    }
+    if (warp == 0) {
+        st::tmem_alloc(tslot, L::TMEM);
+        st::tmem_relinquish();
+    }
+    // everything above overlaps the previous kernel's tail (programmatic dependent launch); no global
+    // memory is read before it has completed
+    st::grid_dep_wait();
+    st::grid_dep_launch();
+    if (tid == 0) {
         if (tma) {  // Q, and K, V in 128-row boxes up to the last key this tile sees
             const int nkb = (kc + AT - 1) / AT;
             st::mbar_arrive_expect_tx(&bar[3], static_cast<uint32_t>(TILE * (1 + 2 * nkb)));
@@ -320,10 +330,6 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
                 st::tma_load_4d(sV + b * TILE, &tm.v, &bar[3], 0, b * AT, z, 0);
             }
         }
-    }
-    if (warp == 0) {
-        st::tmem_alloc(tslot, L::TMEM);
-        st::tmem_relinquish();
     }
     if (!tma) stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
     st::fence_proxy_async_smem();
@@ -624,6 +630,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, cons
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t ph0 = 0, ph1 = 0, ph3 = 0;
     bool ok = true;
+    st::grid_dep_wait();  // the prologue above overlaps the previous kernel's tail
+    st::grid_dep_launch();
     if (key_role) {
         const int kt = tile;
         bool first = true;
@@ -740,6 +748,24 @@ st_status check(st_handle *h, const void *q, const void *k, const void *v, int64
     return ST_OK;
 }
 
+// Launches an attention kernel programmatically dependent on the previous
+// kernel of the stream: its prologue (barriers, TMEM) may run while that
+// kernel finishes; every global read follows griddepcontrol.wait.
+template <typename K>
+cudaError_t launch_dependent(st_handle *h, K kern, dim3 grid, int smem, const AttnArgs &g, const HeadMaps &tm) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(ATHREADS);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = h->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, g, tm);
+}
+
 // The 128-key forward fits two CTAs per SM (82 KB of shared memory, 256 TMEM
 // columns, 128 registers a thread): with more CTAs than SMs every one is
 // resident in one wave.  With at most one per SM the launch asks for more than
@@ -759,7 +785,7 @@ st_status launch_fwd_tk(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>((g.t + AT - 1) / AT));
     const int64_t ctas = static_cast<int64_t>(grid.x) * grid.y;
     const int smem = ctas > h->num_sms ? FwdSmem<TK>::SIZE : spread;
-    k_attn_fwd<F32, TK><<<grid, ATHREADS, smem, h->stream>>>(g, tm);
+    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_fwd<F32, TK>, grid, smem, g, tm));
     return st_after_launch(h, "k_attn_fwd");
 }
 
@@ -777,7 +803,7 @@ st_status launch_bwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     }
     const int ntile = (g.t + AT - 1) / AT;
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(ntile == 1 ? 1 : 2 * ntile));
-    k_attn_bwd<F32><<<grid, ATHREADS, BWD_SMEM, h->stream>>>(g, tm);
+    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd<F32>, grid, BWD_SMEM, g, tm));
     return st_after_launch(h, "k_attn_bwd");
 }
 
