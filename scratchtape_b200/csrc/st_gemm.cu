@@ -674,6 +674,8 @@ constexpr int COL_QUADS = 64, COL_GROUPS = 4, COL_UNROLL = 8;
 __global__ void __launch_bounds__(COL_QUADS *COL_GROUPS)
     k_col_sum_part4(const Operand B, int K, int N, int64_t rpc, float *part) {
     __shared__ float4 red[COL_GROUPS][COL_QUADS];
+    st::grid_dep_wait();  // launched programmatically dependent (st_launch_dependent)
+    st::grid_dep_launch();
     const int q = blockIdx.x * COL_QUADS + threadIdx.x;  // column quad
     const int g = threadIdx.y;
     const int chunk = blockIdx.y, z = blockIdx.z;
@@ -722,11 +724,14 @@ __global__ void __launch_bounds__(COL_QUADS *COL_GROUPS)
 
 // k_col_sum_fin over many chunks: block of COLF_WARPS warps per 32 columns
 // (lane = column, coalesced), warp w adds chunks w, w + COLF_WARPS, ... in
-// order, then the warps' sums are added in warp order.
-constexpr int COLF_WARPS = 16;
+// order with eight loads in flight (256 chunks: one round trip), then the
+// warps' sums are added in a fixed tree (warp w + h into w, h = 16, 8, .., 1).
+constexpr int COLF_WARPS = 32;
 __global__ void __launch_bounds__(COLF_WARPS * 32)
     k_col_sum_fin32(const float *part, int chunks, int N, float *dst, int64_t off, int64_t stride) {
     __shared__ float red[COLF_WARPS][32];
+    st::grid_dep_wait();  // launched programmatically dependent (st_launch_dependent)
+    st::grid_dep_launch();
     const int lane = threadIdx.x & 31, w = threadIdx.x / 32;
     const int col = blockIdx.x * 32 + lane, z = blockIdx.y;
     float s = 0.0f;
@@ -744,10 +749,14 @@ __global__ void __launch_bounds__(COLF_WARPS * 32)
     }
     red[w][lane] = s;
     __syncthreads();
+#pragma unroll
+    for (int h = COLF_WARPS / 2; h > 0; h >>= 1) {
+        if (w < h) red[w][lane] = __fadd_rn(red[w][lane], red[w + h][lane]);
+        __syncthreads();
+    }
     if (w == 0 && col < N) {
-        for (int j = 1; j < COLF_WARPS; j++) s = __fadd_rn(s, red[j][lane]);
         float *d = dst + off + static_cast<int64_t>(z) * stride + col;
-        *d = __fadd_rn(*d, s);
+        *d = __fadd_rn(*d, red[0][lane]);
     }
 }
 
@@ -872,12 +881,14 @@ st_status launch_col_sum(st_handle *h, const Operand &B, int64_t batch, int64_t 
         if (!part) return ST_NO_MEMORY;
         dim3 grid(static_cast<unsigned>((n / 4 + COL_QUADS - 1) / COL_QUADS), static_cast<unsigned>(chunks),
                   static_cast<unsigned>(batch));
-        k_col_sum_part4<<<grid, dim3(COL_QUADS, COL_GROUPS), 0, h->stream>>>(B, g.K, g.N, rpc, part);
+        ST_CHECK_CUDA(h, st_launch_dependent(h, k_col_sum_part4, grid, dim3(COL_QUADS, COL_GROUPS), 0, B, g.K, g.N,
+                                             rpc, part));
         st_status s = st_after_launch(h, "k_col_sum_part4");
         if (s != ST_OK) return s;
-        k_col_sum_fin32<<<dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(batch)),
-                          COLF_WARPS * 32, 0, h->stream>>>(part, static_cast<int>(chunks), g.N, e.col_sum,
-                                                           e.col_sum_off, e.col_sum_stride);
+        ST_CHECK_CUDA(h, st_launch_dependent(h, k_col_sum_fin32,
+                                             dim3(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>(batch)),
+                                             dim3(COLF_WARPS * 32), 0, part, static_cast<int>(chunks), g.N, e.col_sum,
+                                             e.col_sum_off, e.col_sum_stride));
         s = st_after_launch(h, "k_col_sum_fin32");
         if (s != ST_OK) return s;
     } else {

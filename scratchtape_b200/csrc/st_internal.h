@@ -76,6 +76,25 @@ struct st_handle {
 // Checks the launch that was just enqueued and counts it.
 st_status st_after_launch(st_handle *h, const char *what);
 
+// Launches `kern` on h's stream programmatically dependent on the previous
+// kernel there: the launch may overlap that kernel's tail, so `kern` must
+// execute griddepcontrol.wait before it touches global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t st_launch_dependent(st_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = h->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Returns a device buffer of at least `bytes` for `slot` (grows the slot;
 // growth synchronises the stream).  nullptr on failure (h->err set).
 void *st_scratch(st_handle *h, int slot, size_t bytes);

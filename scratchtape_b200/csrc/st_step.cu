@@ -14,8 +14,17 @@
 #include <algorithm>
 
 #include "st_internal.h"
+#include "st_ptx.cuh"
 
 namespace {
+
+// Every kernel below is launched programmatically dependent on the previous
+// kernel of the stream (st_launch_dependent) and begins with this: wait for
+// that kernel's results, then let the next kernel's launch begin.
+__device__ __forceinline__ void dep_enter() {
+    st::grid_dep_wait();
+    st::grid_dep_launch();
+}
 
 constexpr int MAXD = 1024;  // widest row the per-warp kernels take (32 lanes x 32)
 
@@ -33,6 +42,7 @@ __device__ __forceinline__ float warp_max_f(float v) {
 // x[r, :] = tok[ids[r], :] + pos[r % t, :]
 __global__ void k_embed_fwd(const int32_t *ids, const float *tok, const float *pos, float *x, int64_t rows, int t,
                             int d) {
+    dep_enter();
     const int64_t n4 = rows * d / 4;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -56,6 +66,7 @@ __global__ void __launch_bounds__(EMB_THREADS) k_embed_bwd_tok(const int32_t *id
                                                                int64_t rows, int d, int vocab, int accumulate) {
     __shared__ int64_t list[EMB_SEG];
     __shared__ int warp_n[EMB_THREADS / 32];
+    dep_enter();
     const int v = blockIdx.x;
     const int tid = threadIdx.x, warp = tid / 32, lane = tid & 31;
     constexpr int PER = MAXD / EMB_THREADS;
@@ -113,6 +124,7 @@ __global__ void __launch_bounds__(EMB_THREADS) k_embed_bwd_tok(const int32_t *id
 
 // dpos[i, c] (+)= sum over b ascending of dx[b*t + i, c]
 __global__ void k_embed_bwd_pos(const float *dx, float *dpos, int batch, int t, int d, int accumulate) {
+    dep_enter();
     const int64_t n = static_cast<int64_t>(t) * d;
     for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < n;
          e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -126,6 +138,7 @@ __global__ void k_embed_bwd_pos(const float *dx, float *dpos, int batch, int t, 
 // One warp per row; lane owns columns lane, lane + 32, ... (coalesced).
 __global__ void k_ln_fwd(const float *x, const float *gamma, const float *beta, float *y, float *mean, float *rstd,
                          int64_t rows, int d, float eps) {
+    dep_enter();
     const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
@@ -174,6 +187,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const
                                                           int64_t rows, int accumulate) {
     constexpr int D = 32 * PER;
     __shared__ float sh[LN_WARPS][2][D];
+    dep_enter();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int64_t row0 = blockIdx.x * static_cast<int64_t>(LN_WARPS * RPW);
     float dyv[RPW][PER], xv[RPW][PER], dxv[RPW][PER], mu[RPW], rs[RPW];
@@ -239,22 +253,25 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_bwd(const float *dy, const
 }
 
 // dgamma[c] += sum of part[b][0][c], dbeta[c] += sum of part[b][1][c] over
-// blocks b.  Block = 32 columns x 8 row groups: thread (g, c) adds blocks g,
-// g + 8, ... in order (32 consecutive columns per load: one 128-byte line),
-// then the 8 group sums are added in group order.
-__global__ void __launch_bounds__(256) k_ln_params_sum(const float *part, float *dgamma, float *dbeta, int d,
-                                                       int nblocks) {
-    __shared__ float sg_s[8][32], sb_s[8][32];
+// blocks b.  Block = 32 columns x 32 row groups: thread (g, c) adds blocks g,
+// g + 32, ... in order with eight loads in flight (a warp's load is 32
+// consecutive columns, one 128-byte line), so 256 blocks take one round trip;
+// the 32 group sums are then added in a fixed tree (group g + w into g for
+// w = 16, 8, 4, 2, 1).
+constexpr int LNP_GROUPS = 32;
+__global__ void __launch_bounds__(32 * LNP_GROUPS) k_ln_params_sum(const float *part, float *dgamma, float *dbeta,
+                                                                   int d, int nblocks) {
+    __shared__ float sg_s[LNP_GROUPS][32], sb_s[LNP_GROUPS][32];
+    dep_enter();
     const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + cl;
     float sg = 0.0f, sb = 0.0f;
     if (c < d) {
-        // eight blocks' values loaded before they are added (in block order)
-        for (int b0 = grp; b0 < nblocks; b0 += 64) {
+        for (int b0 = grp; b0 < nblocks; b0 += 8 * LNP_GROUPS) {
             float vg[8], vb[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int b = b0 + 8 * j;
+                const int b = b0 + LNP_GROUPS * j;
                 vg[j] = b < nblocks ? part[(static_cast<int64_t>(b) * 2) * d + c] : 0.0f;
                 vb[j] = b < nblocks ? part[(static_cast<int64_t>(b) * 2 + 1) * d + c] : 0.0f;
             }
@@ -268,14 +285,17 @@ __global__ void __launch_bounds__(256) k_ln_params_sum(const float *part, float 
     sg_s[grp][cl] = sg;
     sb_s[grp][cl] = sb;
     __syncthreads();
-    if (grp == 0 && c < d) {
-        float tg = 0.0f, tb = 0.0f;
-        for (int g = 0; g < 8; g++) {
-            tg += sg_s[g][cl];
-            tb += sb_s[g][cl];
+#pragma unroll
+    for (int w = LNP_GROUPS / 2; w > 0; w >>= 1) {
+        if (grp < w) {
+            sg_s[grp][cl] += sg_s[grp + w][cl];
+            sb_s[grp][cl] += sb_s[grp + w][cl];
         }
-        dgamma[c] += tg;
-        dbeta[c] += tb;
+        __syncthreads();
+    }
+    if (grp == 0 && c < d) {
+        dgamma[c] += sg_s[0][cl];
+        dbeta[c] += sb_s[0][cl];
     }
 }
 
@@ -283,6 +303,7 @@ __global__ void __launch_bounds__(256) k_ln_params_sum(const float *part, float 
 // dlogits = (softmax(x) - onehot(y)) * grad_scale.
 __global__ void k_ce(const float *logits, const int32_t *targets, float *loss_rows, float *dlogits, int64_t rows,
                      int vocab, float grad_scale) {
+    dep_enter();
     const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
@@ -319,6 +340,7 @@ __global__ void k_ce(const float *logits, const int32_t *targets, float *loss_ro
 // out[0] = mean of x[0..n): per-thread strided sums, then a fixed tree.
 __global__ void k_mean(const float *x, int64_t n, float *out) {
     __shared__ float sh[1024];
+    dep_enter();
     float s = 0.0f;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
     sh[threadIdx.x] = s;
@@ -349,7 +371,10 @@ __global__ void k_adam(float *p, const float *g, float *m, float *v, int64_t n, 
 }
 
 // The step counter lives on the device, so a captured step replays correctly.
-__global__ void k_step_inc(int32_t *step) { step[0] += 1; }
+__global__ void k_step_inc(int32_t *step) {
+    dep_enter();
+    step[0] += 1;
+}
 
 __device__ __forceinline__ float powi_dev(float a, int b) {  // the host powi_f32, op for op
     float r = 1.0f;
@@ -364,6 +389,7 @@ __device__ __forceinline__ float powi_dev(float a, int b) {  // the host powi_f3
 
 __global__ void k_adam_dev(float *p, const float *g, float *m, float *v, int64_t n, const int32_t *step, float lr,
                            float b1, float b2, float eps) {
+    dep_enter();
     const int t = step[0];
     const float i1 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b1, t)));
     const float i2 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b2, t)));
@@ -405,8 +431,8 @@ extern "C" st_status st_embed_fwd(st_handle *h, const int32_t *ids, const float 
         return h->fail(ST_INVALID_ARG, "st_embed_fwd: bad arguments");
     cudaSetDevice(h->device);
     const int64_t rows = batch * t;
-    k_embed_fwd<<<blocks_for(rows * d / 4, 256), 256, 0, h->stream>>>(ids, tok, pos, x, rows, static_cast<int>(t),
-                                                                     static_cast<int>(d));
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_embed_fwd, dim3(blocks_for(rows * d / 4, 256)), dim3(256), 0, ids, tok,
+                                         pos, x, rows, static_cast<int>(t), static_cast<int>(d)));
     return st_after_launch(h, "k_embed_fwd");
 }
 
@@ -417,12 +443,14 @@ extern "C" st_status st_embed_bwd(st_handle *h, const int32_t *ids, const float 
         vocab > (1LL << 30))
         return h->fail(ST_INVALID_ARG, "st_embed_bwd: bad arguments");
     cudaSetDevice(h->device);
-    k_embed_bwd_tok<<<static_cast<unsigned>(vocab), EMB_THREADS, 0, h->stream>>>(
-        ids, dx, dtok, batch * t, static_cast<int>(d), static_cast<int>(vocab), accumulate);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_embed_bwd_tok, dim3(static_cast<unsigned>(vocab)), dim3(EMB_THREADS), 0,
+                                         ids, dx, dtok, batch * t, static_cast<int>(d), static_cast<int>(vocab),
+                                         accumulate));
     st_status s = st_after_launch(h, "k_embed_bwd_tok");
     if (s != ST_OK) return s;
-    k_embed_bwd_pos<<<blocks_for(t * d, 256), 256, 0, h->stream>>>(dx, dpos, static_cast<int>(batch),
-                                                                   static_cast<int>(t), static_cast<int>(d), accumulate);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_embed_bwd_pos, dim3(blocks_for(t * d, 256)), dim3(256), 0, dx, dpos,
+                                         static_cast<int>(batch), static_cast<int>(t), static_cast<int>(d),
+                                         accumulate));
     return st_after_launch(h, "k_embed_bwd_pos");
 }
 
@@ -433,8 +461,9 @@ extern "C" st_status st_layernorm_fwd(st_handle *h, const float *x, const float 
         return h->fail(ST_INVALID_ARG, "st_layernorm_fwd: bad arguments (d a multiple of 32 up to %d)", MAXD);
     cudaSetDevice(h->device);
     const int wpb = 8;
-    k_ln_fwd<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(x, gamma, beta, y, mean, rstd,
-                                                                                        rows, static_cast<int>(d), eps);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_ln_fwd, dim3(static_cast<unsigned>((rows + wpb - 1) / wpb)),
+                                         dim3(32 * wpb), 0, x, gamma, beta, y, mean, rstd, rows, static_cast<int>(d),
+                                         eps));
     return st_after_launch(h, "k_ln_fwd");
 }
 
@@ -457,8 +486,8 @@ extern "C" st_status st_layernorm_bwd(st_handle *h, const float *dy, const float
     switch (per) {
 #define ST_LN_BWD(P)                                                                                     \
     case P:                                                                                              \
-        k_ln_bwd<P, (32 / P > 1 ? 32 / P : 1)><<<grid, block, 0, h->stream>>>(dy, x, gamma, mean, rstd, dx, \
-                                                                              part, rows, accumulate);   \
+        ST_CHECK_CUDA(h, st_launch_dependent(h, k_ln_bwd<P, (32 / P > 1 ? 32 / P : 1)>, grid, block, 0, dy, x, \
+                                             gamma, mean, rstd, dx, part, rows, accumulate));                 \
         break;
         ST_LN_BWD(1) ST_LN_BWD(2) ST_LN_BWD(3) ST_LN_BWD(4) ST_LN_BWD(5) ST_LN_BWD(6) ST_LN_BWD(7) ST_LN_BWD(8)
         ST_LN_BWD(9) ST_LN_BWD(10) ST_LN_BWD(11) ST_LN_BWD(12) ST_LN_BWD(13) ST_LN_BWD(14) ST_LN_BWD(15)
@@ -469,9 +498,9 @@ extern "C" st_status st_layernorm_bwd(st_handle *h, const float *dy, const float
     }
     st_status s = st_after_launch(h, "k_ln_bwd");
     if (s != ST_OK) return s;
-    k_ln_params_sum<<<static_cast<unsigned>((d + 31) / 32), 256, 0, h->stream>>>(part, dgamma, dbeta,
-                                                                                static_cast<int>(d),
-                                                                                static_cast<int>(nblocks));
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_ln_params_sum, dim3(static_cast<unsigned>((d + 31) / 32)),
+                                         dim3(32 * LNP_GROUPS), 0, part, dgamma, dbeta, static_cast<int>(d),
+                                         static_cast<int>(nblocks)));
     return st_after_launch(h, "k_ln_params_sum");
 }
 
@@ -484,11 +513,12 @@ extern "C" st_status st_cross_entropy(st_handle *h, const float *logits, const i
     float *loss_rows = static_cast<float *>(st_scratch(h, SLOT_STEP_ROWS, sizeof(float) * rows));
     if (!loss_rows) return ST_NO_MEMORY;
     const int wpb = 8;
-    k_ce<<<static_cast<unsigned>((rows + wpb - 1) / wpb), 32 * wpb, 0, h->stream>>>(
-        logits, targets, loss_rows, dlogits, rows, static_cast<int>(vocab), 1.0f / static_cast<float>(rows));
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_ce, dim3(static_cast<unsigned>((rows + wpb - 1) / wpb)), dim3(32 * wpb),
+                                         0, logits, targets, loss_rows, dlogits, rows, static_cast<int>(vocab),
+                                         1.0f / static_cast<float>(rows)));
     st_status s = st_after_launch(h, "k_ce");
     if (s != ST_OK) return s;
-    k_mean<<<1, 1024, 0, h->stream>>>(loss_rows, rows, loss);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_mean, dim3(1), dim3(1024), 0, loss_rows, rows, loss));
     return st_after_launch(h, "k_mean");
 }
 
@@ -507,9 +537,10 @@ extern "C" st_status st_adam_dev(st_handle *h, float *p, const float *g, float *
     if (!h) return ST_INVALID_ARG;
     if (!p || !g || !m || !v || !step || n < 1) return h->fail(ST_INVALID_ARG, "st_adam_dev: bad arguments");
     cudaSetDevice(h->device);
-    k_step_inc<<<1, 1, 0, h->stream>>>(step);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_step_inc, dim3(1), dim3(1), 0, step));
     st_status s = st_after_launch(h, "k_step_inc");
     if (s != ST_OK) return s;
-    k_adam_dev<<<blocks_for(n, 256), 256, 0, h->stream>>>(p, g, m, v, n, step, lr, beta1, beta2, eps);
+    ST_CHECK_CUDA(h, st_launch_dependent(h, k_adam_dev, dim3(blocks_for(n, 256)), dim3(256), 0, p, g, m, v, n, step,
+                                         lr, beta1, beta2, eps));
     return st_after_launch(h, "k_adam_dev");
 }
