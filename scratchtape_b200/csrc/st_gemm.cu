@@ -1110,10 +1110,11 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         const int kb_total = static_cast<int>((k + bke - 1) / bke);
         const int64_t tiles = m_tiles * ((n + BN - 1) / BN) * batch;
         // Split k only when the tiles fill less than half the GPU, keeping
-        // at least 4 k blocks (128) per split.
+        // at least 4 k blocks (128) per split; up to two CTAs per SM (one CTA
+        // streams operands at about half the rate two do).
         int splits = 1;
         if (tiles * 2 <= h->num_sms && kb_total >= 8) {
-            splits = static_cast<int>(std::min<int64_t>(std::min<int64_t>(h->num_sms / tiles, kb_total / 4), 16));
+            splits = static_cast<int>(std::min<int64_t>(std::min<int64_t>(2 * h->num_sms / tiles, kb_total / 4), 32));
             splits = std::max(splits, 1);
         }
         int kbps = (kb_total + splits - 1) / splits;
