@@ -33,7 +33,8 @@ constexpr int AMAXT = 256;            // longest sequence (the reference's MAX_S
 constexpr int AD = 64;                // head width
 constexpr int TILE = AT * AD * 2;     // one [128 x 64] f16 operand: 16 KB
 constexpr int PT = AT * AT * 2;       // one [128 x 128] f16 operand: 32 KB
-constexpr int ATHREADS = 256;  // two threads per row
+constexpr int ATHREADS = 256;  // two threads per row (thread-loaded operands, f32 layouts, many heads)
+constexpr int ATHREADS4 = 512;  // four threads per row (TMA-loaded f16 heads, at most one CTA per SM)
 
 // Where row r of head z of a tensor lives: element (z / heads) * bstride +
 // (z % heads) * hstride + r * rstride of its base.  Per-head tensors
@@ -276,8 +277,8 @@ __device__ __forceinline__ float fast_exp(float x) { return exp2f(x * 1.44269504
 template <int TK>
 struct FwdSmem {
     static constexpr int Q = 0, K = TILE, V = K + TK * 128, P = V + TK * 128;
-    static constexpr int RED = P + AT * TK * 2;  // [2][128] f32
-    static constexpr int BAR = RED + 2 * AT * 4;
+    static constexpr int RED = P + AT * TK * 2;  // [4][128] f32
+    static constexpr int BAR = RED + 4 * AT * 4;
     static constexpr int SIZE = BAR + 64 + 1024;
     static constexpr uint32_t TMEM = TK == 128 ? 256 : 512;  // S (TK columns) + O (64)
 };
@@ -285,11 +286,16 @@ struct FwdSmem {
 // Forward.  CTA = (head z = blockIdx.x, query tile blockIdx.y of 128 rows): S = Q K^T over every
 // key the tile sees (at most TK = 256 columns, so a row's scores fit one TMEM
 // row and need no online rescaling), the masked softmax (or softmax1) of
-// scale * S in registers, P as f16 into shared memory, O = P V.  Threads r
-// and r + 128 share row r: each takes half of the row's key columns (warps w
-// and w + 4 read the same TMEM lanes); row reductions go through `red`.
-template <bool F32, int TK>
-__global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
+// scale * S in registers, P as f16 into shared memory, O = P V.  The NTH / 128
+// threads r, r + 128, ... share row r: each takes an equal share of the row's
+// key columns (warps w, w + 4, ... read the same TMEM lanes); row reductions
+// go through `red`.  NTH = 512 (four threads per row) only with TMA-loaded
+// f16 operands and TK = 128.
+template <bool F32, int TK, int NTH = ATHREADS>
+__global__ void __launch_bounds__(NTH, (TK == 128 && NTH == ATHREADS) ? 2 : 1)
+    k_attn_fwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
+    static_assert(NTH == ATHREADS || (NTH == ATHREADS4 && TK == AT && !F32), "four threads per row: f16, TK 128");
+    constexpr int NG = NTH / AT;  // threads per row
     using L = FwdSmem<TK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int r = tid & (AT - 1), half = tid >> 7;
+    const int r = tid & (AT - 1), half = tid >> 7;  // half: this thread's share of the row (0 .. NG - 1)
     const int z = blockIdx.x, q0 = blockIdx.y * AT, gr = q0 + r;
     const int kc = g.causal ? min(g.t, q0 + AT) : g.t;  // keys this tile sees
     const int kc16 = (kc + 15) & ~15;                      // the MMAs' N / K extent over keys
@@ -331,7 +337,9 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
             }
         }
     }
-    if (!tma) stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
+    if constexpr (NTH == ATHREADS) {
+        if (!tma) stage_qkv<F32, TK>(sQ, sK, sV, g, z, q0, kc);
+    }
     st::fence_proxy_async_smem();
     st::tc_fence_before();
     __syncthreads();
@@ -353,23 +361,26 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
 
     const int lim = live ? (g.causal ? gr + 1 : g.t) : 0;  // columns < lim are visible
     float m = -INFINITY, l = 0.0f;
-    if (TK == AT) {
-        // up to 128 key columns: thread half h takes columns 64h .. 64h + 63 in
-        // registers (one TMEM read); columns at and past kc16 are masked
-        const int cbase = half * 64;
-        uint32_t x[64];
-        st::tmem_ld32(tS + lane_base + cbase, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-        st::tmem_ld32(tS + lane_base + cbase + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+    if constexpr (TK == AT) {
+        // up to 128 key columns: share h of the row takes columns CW h .. CW h + CW - 1
+        // in registers (one TMEM read); columns at and past kc16 are masked
+        constexpr int CW = AT / NG;
+        const int cbase = half * CW;
+        uint32_t x[CW];
+#pragma unroll
+        for (int c = 0; c < CW / 32; c++)
+            st::tmem_ld32(tS + lane_base + cbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&x[32 * c]));
         st::tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 64; j++)
+        for (int j = 0; j < CW; j++)
             if (cbase + j < lim) m = fmaxf(m, __uint_as_float(x[j]) * g.scale);
         red[half * AT + r] = m;
         __syncthreads();
-        m = fmaxf(m, red[(half ^ 1) * AT + r]);
+#pragma unroll
+        for (int o = 0; o < NG; o++) m = fmaxf(m, red[o * AT + r]);
         if (g.one) m = fmaxf(m, 0.0f);  // softmax1 shifts by max(row max, 0)
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < CW / 16; c++) {
             float p[16];
 #pragma unroll
             for (int j = 0; j < 16; j++) {
@@ -421,7 +432,9 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
     st::tc_fence_before();
     __syncthreads();
     st::tc_fence_after();
-    l += red[(half ^ 1) * AT + r];
+    l = 0.0f;  // the shares' sums in share order: the same value on every thread of the row
+#pragma unroll
+    for (int o = 0; o < NG; o++) l += red[o * AT + r];
     if (g.one && lim > 0) l += fast_exp(-m);  // softmax1's phantom zero logit
     if (half == 0 && live) g.lse[static_cast<int64_t>(z) * g.t + gr] = lim > 0 ? m + logf(l) : -INFINITY;
 
@@ -436,7 +449,7 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
     st::tc_fence_after();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll 1
-    for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+    for (int c0 = half * (AD / NG); c0 < (half + 1) * (AD / NG); c0 += 16) {
         uint32_t y16[16];
         st::tmem_ld16(tO + lane_base + c0, y16);
         st::tmem_ld_wait();
@@ -455,17 +468,19 @@ __global__ void __launch_bounds__(ATHREADS, TK == 128 ? 2 : 1) k_attn_fwd(const 
 
 // Backward shared memory: two [128 x 64] operand pairs and two [128 x 128] f16 tiles.
 constexpr int B_Q = 0, B_DO = TILE, B_K = 2 * TILE, B_V = 3 * TILE, B_P = 4 * TILE, B_S = B_P + PT;
-constexpr int B_RED = B_S + PT, B_BAR = B_RED + 2 * AT * 4;
+constexpr int B_RED = B_S + PT, B_BAR = B_RED + 4 * AT * 4;
 constexpr int BWD_SMEM = B_BAR + 64 + 1024;
 
-// dot_half's sum for f16 rows held in 128-byte-swizzled tiles: row r,
-// columns 32 half .. 32 half + 31, in the same order (so the same bits).
-__device__ __forceinline__ float dot_half_tiles(const uint8_t *ta, const uint8_t *tb, int r, int half) {
+// dot_half's sum for f16 rows held in 128-byte-swizzled tiles: row r, the
+// NP 8-column pieces from piece NP h on, in the same order as dot_half (so
+// with NP = 4 the same bits).
+template <int NP>
+__device__ __forceinline__ float dot_tiles(const uint8_t *ta, const uint8_t *tb, int r, int h) {
     float acc = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-        const uint4 x = *reinterpret_cast<const uint4 *>(ta + st::sw128_offset(r, 4 * half + c));
-        const uint4 y = *reinterpret_cast<const uint4 *>(tb + st::sw128_offset(r, 4 * half + c));
+    for (int c = 0; c < NP; c++) {
+        const uint4 x = *reinterpret_cast<const uint4 *>(ta + st::sw128_offset(r, NP * h + c));
+        const uint4 y = *reinterpret_cast<const uint4 *>(tb + st::sw128_offset(r, NP * h + c));
         const uint32_t xv[4] = {x.x, x.y, x.z, x.w}, yv[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -487,9 +502,10 @@ __device__ __forceinline__ float dot_half_tiles(const uint8_t *ta, const uint8_t
 // `tbar`, phase `tph`).  f32 inputs take one round trip per pair of tiles (to
 // bound registers) and D from the f32 rows in memory.  False when the TMA
 // wait ran out (the status word says so).
-template <bool F32>
+template <bool F32, int NTH>
 __device__ __forceinline__ bool bwd_stage(const AttnArgs &g, const HeadMaps &tm, uint64_t *tbar, uint32_t &tph,
                                           uint8_t *smem, float *red, int z, int qt, int kt, float &dsum, float &lse) {
+    constexpr int NG = NTH / AT;
     const int r = threadIdx.x & (AT - 1), half = threadIdx.x >> 7, gr = qt * AT + r;
     const bool qrow = qt >= 0 && gr < g.t;
     lse = qrow ? g.lse[static_cast<int64_t>(z) * g.t + gr] : 0.0f;
@@ -511,6 +527,8 @@ __device__ __forceinline__ bool bwd_stage(const AttnArgs &g, const HeadMaps &tm,
         }
         ok = await(tbar, tph, g.status);
         tph ^= 1u;
+    } else if constexpr (NTH != ATHREADS) {
+        // four threads per row is launched only with the tensor maps
     } else if (F32) {
         if (kt >= 0) stage_tiles<true, 2>(Tiles<2>{{kd, vd}, {g.k, g.v}, {g.mq, g.mq}, {kt * AT, kt * AT}}, z, g.heads, g.t);
         if (qt >= 0)
@@ -524,15 +542,17 @@ __device__ __forceinline__ bool bwd_stage(const AttnArgs &g, const HeadMaps &tm,
     }
     if (qt < 0) return ok;
     float part;
-    if (F32) {
+    if constexpr (F32) {
         part = qrow ? dot_half<true>(g.o, g.dout, g.mo.at(z, g.heads, gr), half) : 0.0f;
     } else {
         __syncthreads();  // O and dO tiles complete
-        part = qrow ? dot_half_tiles(smem + B_P, smem + B_DO, r, half) : 0.0f;
+        part = qrow ? dot_tiles<8 / NG>(smem + B_P, smem + B_DO, r, half) : 0.0f;
     }
     red[half * AT + r] = part;
     __syncthreads();
-    dsum = red[r] + red[AT + r];
+    dsum = 0.0f;  // the shares in share order: the same value on every thread of the row
+#pragma unroll
+    for (int o = 0; o < NG; o++) dsum += red[o * AT + r];
     __syncthreads();  // red and the staged O are read before either is reused
     return ok;
 }
@@ -540,7 +560,7 @@ __device__ __forceinline__ bool bwd_stage(const AttnArgs &g, const HeadMaps &tm,
 // S = Q K^T and dP = dO V^T of one (query tile, key tile) pair, then P =
 // exp(scale S - lse) and dS = scale P (dP - D) (masked entries 0) as f16
 // tiles in shared memory (P only when want_p).  Rows are queries.
-template <bool F32>
+template <bool F32, int NTH>
 __device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uint32_t tmem, uint64_t *bar,
                                            uint32_t &phase, int qt, int kt, float dsum, float lse, bool want_p) {
     const int tid = threadIdx.x, warp = tid >> 5, r = tid & (AT - 1), half = tid >> 7;
@@ -563,8 +583,9 @@ __device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uin
     const int gr = qt * AT + r;
     // key column c of this tile is key kt*128 + c; visible iff < t and (causal) <= gr
     const int lim = gr < g.t ? min(g.t, g.causal ? gr + 1 : g.t) - kt * AT : 0;
+    constexpr int CW = AT / (NTH / AT);  // this thread's share of the key columns
 #pragma unroll 1
-    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
+    for (int c0 = half * CW; c0 < half * CW + CW; c0 += 16) {
         uint32_t xs[16], xd[16];
         st::tmem_ld16(tS + lane_base + c0, xs);
         st::tmem_ld16(tdP + lane_base + c0, xd);
@@ -600,8 +621,10 @@ __device__ __forceinline__ bool bwd_scores(const AttnArgs &g, uint8_t *smem, uin
 // Both recompute S and dP from Q, K, V, dO and the forward's log-sum-exp
 // (D = rowsum(dO O) gives the softmax backward for softmax and softmax1
 // alike).  Every transposed operand is a shared-memory descriptor.
-template <bool F32>
-__global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
+template <bool F32, int NTH = ATHREADS>
+__global__ void __launch_bounds__(NTH, 1) k_attn_bwd(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
+    static_assert(NTH == ATHREADS || (NTH == ATHREADS4 && !F32), "four threads per row: f16 heads");
+    constexpr int NG = NTH / AT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *red = reinterpret_cast<float *>(smem + B_RED);
@@ -637,12 +660,12 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, cons
         bool first = true;
         for (int qt = g.causal ? kt : 0; qt < ntile && ok; qt++) {
             float dsum, lse;
-            ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, qt, first ? kt : -1, dsum, lse) && ok;  // K, V too at first
+            ok = bwd_stage<F32, NTH>(g, tm, &bar[3], ph3, smem, red, z, qt, first ? kt : -1, dsum, lse) && ok;
             st::fence_proxy_async_smem();
             st::tc_fence_before();
             __syncthreads();
             st::tc_fence_after();
-            ok = bwd_scores<F32>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, true) && ok;
+            ok = bwd_scores<F32, NTH>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, true) && ok;
             if (tid == 0) {
                 // dV += P^T dO, dK += dS^T Q: A = P^T / dS^T (stored [query][key]: MN-major, M = key),
                 // B = dO / Q (stored [query][d]: MN-major, N = d), K = the tile's 128 queries
@@ -677,7 +700,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, cons
             void *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
             const uint32_t src = w == 0 ? tA : w == 1 ? tB : tQ;
 #pragma unroll
-            for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+            for (int c0 = half * (AD / NG); c0 < (half + 1) * (AD / NG); c0 += 16) {
                 uint32_t x[16];
                 st::tmem_ld16(src + lane_base + c0, x);
                 st::tmem_ld_wait();
@@ -690,18 +713,18 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, cons
     } else {
         const int qt = tile;
         float dsum, lse;
-        ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, qt, 0, dsum, lse);  // the queries with key tile 0
+        ok = bwd_stage<F32, NTH>(g, tm, &bar[3], ph3, smem, red, z, qt, 0, dsum, lse);  // the queries with key tile 0
         const int last = g.causal ? qt : ntile - 1;
         for (int kt = 0; kt <= last && ok; kt++) {
             if (kt > 0) {
                 float unused0, unused1;
-                ok = bwd_stage<F32>(g, tm, &bar[3], ph3, smem, red, z, -1, kt, unused0, unused1) && ok;
+                ok = bwd_stage<F32, NTH>(g, tm, &bar[3], ph3, smem, red, z, -1, kt, unused0, unused1) && ok;
             }
             st::fence_proxy_async_smem();
             st::tc_fence_before();
             __syncthreads();
             st::tc_fence_after();
-            ok = bwd_scores<F32>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, false) && ok;
+            ok = bwd_scores<F32, NTH>(g, smem, tmem, bar, ph0, qt, kt, dsum, lse, false) && ok;
             if (tid == 0) {
                 // dQ += dS K: A = dS (K-major, K = key), B = K (stored [key][d]: MN-major, N = d)
                 constexpr uint32_t id_nt = st::idesc_make(1, 0, false, true, AT, AD);
@@ -718,7 +741,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) k_attn_bwd(const AttnArgs g, cons
         const int gq = qt * AT + r;
         const int64_t rq = g.mq.at(z, g.heads, gq < g.t ? gq : 0);
 #pragma unroll
-        for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+        for (int c0 = half * (AD / NG); c0 < (half + 1) * (AD / NG); c0 += 16) {
             uint32_t x[16];
             st::tmem_ld16(tA + lane_base + c0, x);
             st::tmem_ld_wait();
@@ -752,10 +775,11 @@ st_status check(st_handle *h, const void *q, const void *k, const void *v, int64
 // kernel of the stream: its prologue (barriers, TMEM) may run while that
 // kernel finishes; every global read follows griddepcontrol.wait.
 template <typename K>
-cudaError_t launch_dependent(st_handle *h, K kern, dim3 grid, int smem, const AttnArgs &g, const HeadMaps &tm) {
+cudaError_t launch_dependent(st_handle *h, K kern, dim3 grid, int threads, int smem, const AttnArgs &g,
+                             const HeadMaps &tm) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(ATHREADS);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = h->stream;
     cudaLaunchAttribute attr[1];
@@ -773,6 +797,8 @@ cudaError_t launch_dependent(st_handle *h, K kern, dim3 grid, int smem, const At
 // pairing up on half of them.
 constexpr int FWD_SPREAD_SMEM = 120 * 1024;
 
+// With at most one CTA per SM and TMA-loaded f16 heads of one tile, the
+// forward runs four threads per row (k_attn_fwd<false, 128, 512>).
 template <bool F32, int TK>
 st_status launch_fwd_tk(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     constexpr int spread = TK == 128 && FwdSmem<TK>::SIZE < FWD_SPREAD_SMEM ? FWD_SPREAD_SMEM : FwdSmem<TK>::SIZE;
@@ -780,12 +806,21 @@ st_status launch_fwd_tk(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     if (!attr) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<F32, TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               spread));
+        if constexpr (!F32 && TK == AT)
+            ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_fwd<false, AT, ATHREADS4>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, spread));
         attr = true;
     }
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>((g.t + AT - 1) / AT));
     const int64_t ctas = static_cast<int64_t>(grid.x) * grid.y;
     const int smem = ctas > h->num_sms ? FwdSmem<TK>::SIZE : spread;
-    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_fwd<F32, TK>, grid, smem, g, tm));
+    if constexpr (!F32 && TK == AT) {
+        if (g.tma && ctas <= h->num_sms) {
+            ST_CHECK_CUDA(h, launch_dependent(h, k_attn_fwd<false, AT, ATHREADS4>, grid, ATHREADS4, smem, g, tm));
+            return st_after_launch(h, "k_attn_fwd");
+        }
+    }
+    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_fwd<F32, TK>, grid, ATHREADS, smem, g, tm));
     return st_after_launch(h, "k_attn_fwd");
 }
 
@@ -794,16 +829,27 @@ st_status launch_fwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     return g.t <= AT ? launch_fwd_tk<F32, AT>(h, g, tm) : launch_fwd_tk<F32, AMAXT>(h, g, tm);
 }
 
+// With at most one CTA per SM and TMA-loaded f16 heads the backward runs
+// four threads per row (k_attn_bwd<false, 512>).
 template <bool F32>
 st_status launch_bwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     static bool attr = false;
     if (!attr) {
         ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+        if constexpr (!F32)
+            ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd<false, ATHREADS4>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
         attr = true;
     }
     const int ntile = (g.t + AT - 1) / AT;
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(ntile == 1 ? 1 : 2 * ntile));
-    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd<F32>, grid, BWD_SMEM, g, tm));
+    if constexpr (!F32) {
+        if (g.tma && static_cast<int64_t>(grid.x) * grid.y <= h->num_sms) {
+            ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd<false, ATHREADS4>, grid, ATHREADS4, BWD_SMEM, g, tm));
+            return st_after_launch(h, "k_attn_bwd");
+        }
+    }
+    ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd<F32>, grid, ATHREADS, BWD_SMEM, g, tm));
     return st_after_launch(h, "k_attn_bwd");
 }
 
