@@ -75,6 +75,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ivf", action="store_true", help="C5: skip the IVF search measurement")
     p.add_argument("--no-parity", action="store_true", help="C5: skip the full-size parity check against the oracle")
+    p.add_argument("--no-probes", action="store_true",
+                   help="C4: skip the large-GEMM and per-GEMM probes (the launches are then the step's alone)")
     p.add_argument("--c2-path", default="fused", choices=["fused", "gemms"],
                    help="C2: the fused one-kernel step, or six separate GEMM launches")
     a = p.parse_args()
@@ -1613,10 +1615,10 @@ def run_ours_c4(args):
                     "api": "scratchtape_b200.lm.TinyLM.capture_step graph replay (pinned host bytes in, loss out)"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
-            "large_gemm": large_gemm_probe(torch, device, peaks),
+            "large_gemm": None if args.no_probes else large_gemm_probe(torch, device, peaks),
         }
         if world == 1:
-            line["gemm_breakdown"] = c4_gemm_breakdown(torch, device, peaks, cfg)
+            line["gemm_breakdown"] = None if args.no_probes else c4_gemm_breakdown(torch, device, peaks, cfg)
         if world == 1 and not args.no_cpu_baseline:
             el = cpu_baseline_c4(cfg)
             line["cpu_baseline"] = {"value": cfg.flops_per_step() / el / 1e12, "unit": "TFLOP/s", "cores": 1,
