@@ -1081,6 +1081,10 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
     const int64_t m_tiles = (m + BM - 1) / BM;
     const int64_t tiles128 = m_tiles * ((n + 127) / 128) * batch;
     int BN = (n > 64 && (tiles128 >= h->num_sms || tiles128 * 8 <= h->num_sms)) ? 128 : 64;
+    // f32 operands: 256 wide when 128-wide tiles need more than one wave of two CTAs per SM and 256-wide ones
+    // fit in one (half the MMA instructions per flop; a 2-stage ring keeps two CTAs per SM)
+    const int64_t tiles256 = m_tiles * ((n + 255) / 256) * batch;
+    if (!ab && n > 256 && tiles128 > 2 * h->num_sms && tiles256 <= 2 * h->num_sms) BN = 256;
     if (use_tc) {
         // A: logical [m, k]; stored [m, k] (K-major) or [k, m] (MN-major).
         // K-major tiles: 128-byte swizzle.  MN-major tf32 tiles: 128-byte
@@ -1162,8 +1166,9 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             s = BN == 64 ? dispatch_tf32<64, 4, 2>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
                          : dispatch_tf32<128, 3, 2>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
         else
-            s = BN == 64 ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
-                         : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
+            s = BN == 64    ? dispatch_tf32<64, 4>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                : BN == 256 ? dispatch_tf32<256, 2>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid)
+                            : dispatch_tf32<128, 3>(h, a_mn, b_mn, ma, mb, mc, mm, mr, g, grid);
         if (s != ST_OK) return s;
         if (splits > 1) {
             const int groups = static_cast<int>((n + 3) / 4);

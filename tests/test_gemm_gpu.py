@@ -132,6 +132,11 @@ CASES_TC = [
     (1, 512, 4096, 128, True, False, False, False, False, False, False),
     (1, 4096, 512, 128, False, True, False, False, False, False, False),
     (1, 128, 4096, 512, True, False, False, False, False, False, False),
+    # 256-wide tiles (more than one wave of 128-wide ones, one wave of 256-wide): every layout, ragged N and K
+    (1, 8192, 64, 768, False, False, True, True, False, False, False),
+    (1, 8192, 64, 768, False, True, False, False, True, True, False),
+    (1, 8192, 40, 1000, True, False, True, False, False, False, True),
+    (1, 8192, 96, 1024, True, True, False, True, True, False, False),
 ]
 
 
