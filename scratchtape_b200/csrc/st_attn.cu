@@ -759,6 +759,142 @@ __global__ void __launch_bounds__(NTH, 1) k_attn_bwd(const AttnArgs g, const __g
     }
 }
 
+// Compact backward for one-tile sequences (t <= 128) when the heads are more
+// than the SMs: 98 KB of shared memory and 256 TMEM columns, so two CTAs fit
+// on an SM and the grid runs in one wave instead of two.  The same arithmetic
+// as k_attn_bwd (the same bits): after S = Q K^T and dP = dO V^T,
+//  1. dS = scale P (dP - D) -> the one [128 x 128] f16 tile X; dK = dS^T Q and
+//     dQ = dS K accumulate into dP's TMEM columns (dP is read by then);
+//  2. once those MMAs have read X, P = exp(scale S - lse) -> X (recomputed from
+//     S, which is still in TMEM); dV = P^T dO accumulates into S's columns.
+// Shared memory: Q, dO, K, V (16 KB each), X (32 KB, where the f16 path also
+// stages O for D), the row-reduction scratch and the barriers.
+constexpr int C_X = B_P, C_RED = C_X + PT, C_BAR = C_RED + 2 * AT * 4;
+constexpr int CBWD_SMEM = C_BAR + 64 + 1024;
+
+// One pass over this thread's 64 key columns of S (and dP): dS (want_ds) or
+// P as f16 into X, with k_attn_bwd's formulas.
+__device__ __forceinline__ void tile_pass(const AttnArgs &g, uint8_t *x, uint32_t tS, uint32_t tdP, int r, int half,
+                                          int lim, float dsum, float lse, bool want_ds) {
+    const uint32_t lane_base = static_cast<uint32_t>(r & ~31) << 16;
+#pragma unroll 1
+    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
+        uint32_t xs[16], xd[16];
+        st::tmem_ld16(tS + lane_base + c0, xs);
+        if (want_ds) st::tmem_ld16(tdP + lane_base + c0, xd);
+        st::tmem_ld_wait();
+        float p[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const bool vis = c0 + j < lim;
+            p[j] = vis ? fast_exp(__uint_as_float(xs[j]) * g.scale - lse) : 0.0f;
+            if (want_ds) p[j] = p[j] * (__uint_as_float(xd[j]) - dsum) * g.scale;
+        }
+        uint32_t o[8];
+        pack16(p, o);
+        put16(x, r, c0, o);
+    }
+    st::fence_proxy_async_smem();
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(ATHREADS, 2) k_attn_bwd1(const AttnArgs g, const __grid_constant__ HeadMaps tm) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *red = reinterpret_cast<float *>(smem + C_RED);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + C_BAR);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, r = tid & (AT - 1), half = tid >> 7;
+    const int z = blockIdx.x;
+    if (tid == 0) {
+        st::mbar_init(&bar[0], 1);
+        st::mbar_init(&bar[1], 1);
+        st::mbar_init(&bar[3], 1);
+        st::fence_mbar_init();
+    }
+    if (warp == 0) {
+        st::tmem_alloc(tslot, 256);
+        st::tmem_relinquish();
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t tmem = *tslot, tS = tmem, tdP = tmem + 128;
+    const uint32_t tdV = tmem, tdK = tmem + 128, tdQ = tmem + 192;  // into S's and dP's columns once they are read
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    st::grid_dep_wait();  // the prologue above overlaps the previous kernel's tail
+    st::grid_dep_launch();
+
+    uint32_t ph3 = 0;
+    float dsum, lse;
+    bool ok = bwd_stage<F32, ATHREADS>(g, tm, &bar[3], ph3, smem, red, z, 0, 0, dsum, lse);  // X holds O (f16)
+    st::fence_proxy_async_smem();
+    st::tc_fence_before();
+    __syncthreads();
+    st::tc_fence_after();
+    const uint32_t q = st::smem_u32(smem + B_Q), k = st::smem_u32(smem + B_K), v = st::smem_u32(smem + B_V),
+                   d = st::smem_u32(smem + B_DO), x = st::smem_u32(smem + C_X);
+    if (tid == 0) {  // S = Q K^T, dP = dO V^T
+        constexpr uint32_t id = st::idesc_make(1, 0, false, false, AT, AT);
+#pragma unroll
+        for (int kk = 0; kk < AD / 16; kk++) {
+            st::umma_f16(tS, kmaj(q, kk), kmaj(k, kk), id, kk > 0 ? 1u : 0u);
+            st::umma_f16(tdP, kmaj(d, kk), kmaj(v, kk), id, kk > 0 ? 1u : 0u);
+        }
+        st::umma_commit(&bar[0]);
+    }
+    ok = await(&bar[0], 0, g.status) && ok;
+    st::tc_fence_after();
+    const int lim = r < g.t ? min(g.t, g.causal ? r + 1 : g.t) : 0;
+    tile_pass(g, smem + C_X, tS, tdP, r, half, lim, dsum, lse, true);
+    if (tid == 0) {  // dK = dS^T Q, dQ = dS K
+        constexpr uint32_t id_tt = st::idesc_make(1, 0, true, true, AT, AD);
+        constexpr uint32_t id_nt = st::idesc_make(1, 0, false, true, AT, AD);
+#pragma unroll
+        for (int kk = 0; kk < AT / 16; kk++) {
+            st::umma_f16(tdK, mnmaj(x, kk, PT / 2), mnmaj(q, kk, TILE), id_tt, kk > 0 ? 1u : 0u);
+            st::umma_f16(tdQ, kmaj128(x, kk), mnmaj(k, kk, TILE), id_nt, kk > 0 ? 1u : 0u);
+        }
+        st::umma_commit(&bar[1]);
+    }
+    ok = await(&bar[1], 0, g.status) && ok;  // X is read: P may replace dS
+    st::tc_fence_after();
+    tile_pass(g, smem + C_X, tS, tdP, r, half, lim, dsum, lse, false);
+    if (tid == 0) {  // dV = P^T dO
+        constexpr uint32_t id_tt = st::idesc_make(1, 0, true, true, AT, AD);
+#pragma unroll
+        for (int kk = 0; kk < AT / 16; kk++)
+            st::umma_f16(tdV, mnmaj(x, kk, PT / 2), mnmaj(d, kk, TILE), id_tt, kk > 0 ? 1u : 0u);
+        st::umma_commit(&bar[0]);
+    }
+    ok = await(&bar[0], 1, g.status) && ok;
+    st::tc_fence_after();
+    const int64_t rk = g.mq.at(z, g.heads, r < g.t ? r : 0);
+    for (int w = 0; w < 3; w++) {
+        void *dst_t = w == 0 ? g.dv : w == 1 ? g.dk : g.dq;
+        const uint32_t src = w == 0 ? tdV : w == 1 ? tdK : tdQ;
+#pragma unroll
+        for (int c0 = half * (AD / 2); c0 < (half + 1) * (AD / 2); c0 += 16) {
+            uint32_t y16[16];
+            st::tmem_ld16(src + lane_base + c0, y16);
+            st::tmem_ld_wait();
+            float y[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) y[j] = __uint_as_float(y16[j]);
+            if (r < g.t && ok) store16<F32>(dst_t, rk + c0, y);
+        }
+    }
+    st::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        st::tc_fence_after();
+        st::tmem_dealloc(tmem, 256);
+    }
+}
+
 st_status check(st_handle *h, const void *q, const void *k, const void *v, int64_t bh, int64_t t, int64_t d,
                 const char *who) {
     if (!q || !k || !v) return h->fail(ST_INVALID_ARG, "%s: null buffer", who);
@@ -843,6 +979,16 @@ st_status launch_bwd(st_handle *h, const AttnArgs &g, const HeadMaps &tm) {
     }
     const int ntile = (g.t + AT - 1) / AT;
     const dim3 grid(static_cast<unsigned>(g.bh), static_cast<unsigned>(ntile == 1 ? 1 : 2 * ntile));
+    if (ntile == 1 && g.bh > h->num_sms) {  // one-tile heads beyond one per SM: the compact form, two per SM
+        static bool attr1 = false;
+        if (!attr1) {
+            ST_CHECK_CUDA(h, cudaFuncSetAttribute(k_attn_bwd1<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  CBWD_SMEM));
+            attr1 = true;
+        }
+        ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd1<F32>, grid, ATHREADS, CBWD_SMEM, g, tm));
+        return st_after_launch(h, "k_attn_bwd1");
+    }
     if constexpr (!F32) {
         if (g.tma && static_cast<int64_t>(grid.x) * grid.y <= h->num_sms) {
             ST_CHECK_CUDA(h, launch_dependent(h, k_attn_bwd<false, ATHREADS4>, grid, ATHREADS4, BWD_SMEM, g, tm));

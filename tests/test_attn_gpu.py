@@ -106,6 +106,34 @@ def test_packed_layout_matches_per_head_layout(dev, one):
         assert (got - want).abs().max().item() <= 5e-3 * want.abs().max().item()
 
 
+def test_compact_backward_matches_wide_backward(dev):
+    """More one-tile heads than SMs run the compact backward (two CTAs per SM:
+    dS and P share one tile, the gradients reuse S's and dP's TMEM columns);
+    its gradients of the first 100 heads equal the regular backward's on those
+    heads alone, per-head f16 and packed f32 layouts."""
+    from scratchtape_b200.attention import (attention_bwd, attention_bwd_packed, attention_fwd,
+                                            attention_fwd_packed)
+    bh, t = 160, 128
+    q, k, v, dout = _inputs(bh, t, 64, seed=21)
+    o, lse = attention_fwd(q, k, v, 0.125, True)
+    full = attention_bwd(q, k, v, o, dout, lse, 0.125, True)
+    part = attention_bwd(q[:100], k[:100], v[:100], o[:100], dout[:100], lse[:100], 0.125, True)
+    for a, b in zip(full, part):
+        x, y = a[:100].float(), b.float()
+        assert (x - y).abs().max().item() <= 5e-3 * y.abs().max().item()
+    b, h = 40, 4
+    g = torch.Generator(device="cuda").manual_seed(5)
+    qkv = (torch.randn((b * t, 3 * h * 64), generator=g, device="cuda") / 4).half().float()
+    do = torch.randn((b * t, h * 64), generator=g, device="cuda").half().float()
+    o2, lse2 = attention_fwd_packed(qkv, b, h, t, 0.125, True)
+    full2 = attention_bwd_packed(qkv, o2, do, lse2, b, h, t, 0.125, True)
+    rows = 25 * t  # the first 25 sequences: 100 heads
+    part2 = attention_bwd_packed(qkv[:rows].contiguous(), o2[:rows].contiguous(), do[:rows].contiguous(),
+                                 lse2[:100].contiguous(), 25, h, t, 0.125, True)
+    x, y = full2[:rows], part2
+    assert (x - y).abs().max().item() <= 5e-3 * y.abs().max().item()
+
+
 def test_deterministic(dev):
     from scratchtape_b200.attention import attention_bwd, attention_fwd
     q, k, v, dout = _inputs(16, 128, 64, seed=3)
