@@ -57,11 +57,12 @@ __global__ void k_embed_fwd(const int32_t *ids, const float *tok, const float *p
 
 // dtok[v, :] (+)= sum over rows r with ids[r] == v, in row order, of dx[r, :].
 // One block per vocabulary row.  The block walks the ids in segments of
-// EMB_SEG, compacts the matching row numbers into shared memory in row order
-// (warp ballots, warp offsets from a prefix over the warps), then every
-// thread adds those rows for its columns, EMB_UNROLL loads in flight, the
-// additions still in row order.
-constexpr int EMB_THREADS = 256, EMB_SEG = 2048, EMB_UNROLL = 4;
+// EMB_SEG (every thread loads its EMB_SEG / EMB_THREADS ids of a segment
+// before any test, so a segment costs one round trip), compacts the matching
+// row numbers into shared memory in row order (warp ballots, warp offsets from
+// a prefix over the warps), then every thread adds those rows for its
+// columns, EMB_UNROLL loads in flight, the additions still in row order.
+constexpr int EMB_THREADS = 256, EMB_SEG = 2048, EMB_UNROLL = 8;
 __global__ void __launch_bounds__(EMB_THREADS) k_embed_bwd_tok(const int32_t *ids, const float *dx, float *dtok,
                                                                int64_t rows, int d, int vocab, int accumulate) {
     __shared__ int64_t list[EMB_SEG];
@@ -74,10 +75,17 @@ __global__ void __launch_bounds__(EMB_THREADS) k_embed_bwd_tok(const int32_t *id
 #pragma unroll
     for (int j = 0; j < PER; j++) acc[j] = 0.0f;
     for (int64_t s0 = 0; s0 < rows; s0 += EMB_SEG) {
+        int32_t idv[EMB_SEG / EMB_THREADS];
+#pragma unroll
+        for (int i = 0; i < EMB_SEG / EMB_THREADS; i++) {
+            const int64_t r = s0 + i * EMB_THREADS + tid;
+            idv[i] = r < rows ? ids[r] : -1;  // ids are vocabulary rows, never negative
+        }
         int n = 0;  // rows listed so far in this segment (the same in every thread)
+#pragma unroll
         for (int i = 0; i < EMB_SEG; i += EMB_THREADS) {
             const int64_t r = s0 + i + tid;
-            const bool hit = r < rows && ids[r] == v;
+            const bool hit = idv[i / EMB_THREADS] == v;
             const unsigned m = __ballot_sync(0xffffffffu, hit);
             if (lane == 0) warp_n[warp] = __popc(m);
             __syncthreads();
