@@ -1442,10 +1442,11 @@ extern "C" st_status st_gemm_group(st_handle *h, const st_group_gemm *gemms, int
         G.n_tiles = static_cast<int>((n + G.bn - 1) / G.bn);
         const int tiles = G.m_tiles * G.n_tiles;
         const int kb_total = static_cast<int>((k + BK - 1) / BK);
-        // split k while the GEMM's tiles fill less than half the GPU, >= 4 k blocks per split
+        // split k as st_gemm does (while the tiles fill less than half the GPU, >= 4 k blocks per split, up to
+        // two CTAs per SM), so every GEMM's sums are the same, bit for bit
         int splits = 1;
         if (tiles * 2 <= h->num_sms && kb_total >= 8)
-            splits = std::max(1, std::min(std::min(h->num_sms / tiles, kb_total / 4), 16));
+            splits = std::max(1, std::min(std::min(2 * h->num_sms / tiles, kb_total / 4), 32));
         G.kb_per_split = (kb_total + splits - 1) / splits;
         G.splits = (kb_total + G.kb_per_split - 1) / G.kb_per_split;
         // a split GEMM's tiles are summed by red_parts reduction tasks each (row bands of 16 rows)
