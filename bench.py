@@ -50,7 +50,7 @@ C5_IVF = dict(keys=37_000_000, nlist=12288, nprobe=8, nq=16384, clusters=12288, 
 # capture: H = relu(X W1) 2.43 MB, Y = H W2 8.72 MB, dW2 = H^T dY 10.56 MB (writes stay in L2); the mean
 C2_TRAFFIC_PER_LAUNCH = (2.430208e6 + 8.721408e6 + 10.557184e6) / 3
 # DRAM bytes (read + write) of one k_attn_fwd + one k_attn_bwd launch at C3, from one ncu capture
-C3_TRAFFIC_PER_STEP = 6.339840e6 + 10.620928e6
+C3_TRAFFIC_PER_STEP = 6.320128e6 + 10.597888e6
 # DRAM bytes (read + write) of one k_mlp_step launch at C2, from one ncu capture
 C2_FUSED_TRAFFIC = 4.800256e6 + 5.820416e6
 # DRAM bytes of one k_knn_tmem full-pass launch, 4096 queries over 2^24 keys, from one ncu capture (the
