@@ -60,7 +60,8 @@ def _want_lse(q, k, scale, causal, one):
 @pytest.mark.parametrize("bh,t,causal", [(128, 128, True), (3, 77, True), (2, 1, True), (5, 100, False),
                                          (4, 128, False), (6, 33, True), (4, 256, True), (3, 200, True),
                                          (2, 129, True), (3, 256, False), (2, 181, False),
-                                         (160, 128, True)])  # more CTAs than SMs: two threads per row
+                                         (160, 128, True), (160, 77, False), (200, 100, True)])
+                                         # the last three: more heads than SMs (two threads per row, the compact backward)
 def test_forward_and_backward_match_oracle(dev, bh, t, causal, one):
     from scratchtape_b200.attention import attention_bwd, attention_fwd
     d, scale = 64, 1.0 / 8.0
