@@ -52,6 +52,9 @@ struct GemmArgs {
     int tma_aux;     // with tma_store: mask / residual tiles loaded by TMA (maps tmM / tmR)
     int c_outer;     // out has a batch stride (TMA batch coordinate z / c_grp)
     float *partial;  // split-k partials, [batch*splits][M][N]
+    float *cs_part;  // Epilogue::col_sum inside the GEMM: per-split column sums of b, [splits][N] (or null)
+    float *cs_dst;   // ... added into cs_dst[cs_off + col] by k_splitk_reduce
+    int64_t cs_off;
     int *status;
 };
 
@@ -397,11 +400,15 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap &tmA, const CUtensorM
     const int kb_total = (g.K + BKE - 1) / BKE;
     const int kb_begin = split * g.kb_per_split;
     const int nkb = max(0, min(kb_total, kb_begin + g.kb_per_split) - kb_begin);
+    // column sums of b (Epilogue::col_sum) by the epilogue warps of the first row of tiles, from the b tiles
+    // the ring stages anyway: row-major f32 b, 128 columns, one 32-column box per epilogue warp
+    constexpr bool CS_FORM = AB == 0 && B_MN && BN == 128;
+    const bool csum = CS_FORM && g.cs_part != nullptr && blockIdx.y == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             st::mbar_init(&full[s], 1);
-            st::mbar_init(&empty[s], 1);
+            st::mbar_init(&empty[s], csum ? 5 : 1);  // + one arrival per column-summing warp
         }
         st::mbar_init(acc_full, 1);
         for (int b = 0; b < 8; b++) st::mbar_init(&aux_bar[b], 1);
@@ -488,6 +495,22 @@ __device__ __forceinline__ void gemm_cta(const CUtensorMap &tmA, const CUtensorM
         }
     } else {  // warps 2..5: epilogue; warp w reads TMEM lanes 32*(w%4) ..
         const int q = warp & 3;
+        if (CS_FORM && csum) {
+            // this thread's column (box q, column lane) of every staged b tile, k ascending; the 32-byte
+            // atoms of box row r sit at atom (column / 8) ^ (r % 4) (the 32-byte-atom 128-byte swizzle)
+            float acc = 0.0f;
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (!st::mbar_wait(&full[s], (i / STAGES) & 1, g.status, st::DEV_TIMEOUT_FULL)) break;
+                const float *box = reinterpret_cast<const float *>(smem + s * C::STAGE_BYTES + C::A_BYTES + q * MNBOX);
+#pragma unroll 8
+                for (int r = 0; r < 32; r++) acc = __fadd_rn(acc, box[r * 32 + ((((lane >> 3) ^ (r & 3)) << 3) | (lane & 7))]);
+                __syncwarp();
+                if (lane == 0) st::mbar_arrive(&empty[s]);
+            }
+            const int col = n0 + q * 32 + lane;
+            if (col < g.N) g.cs_part[static_cast<int64_t>(split) * g.N + col] = acc;
+        }
         const bool ok = st::mbar_wait(acc_full, 0, g.status, st::DEV_TIMEOUT_ACC);
         st::tc_fence_after();
         st::grid_dep_launch();  // the MMAs are done: let the next kernel start its prologue
@@ -575,6 +598,17 @@ __global__ void k_splitk_reduce(const GemmArgs g) {
                 if (col >= g.N) break;
                 const int64_t oi = out_index(g, z, row, col);
                 g.c[oi] = epilogue(g, z, oi, col, s[j]);
+            }
+        }
+    }
+    if (g.cs_part && z == 0 && blockIdx.y == 0) {  // the GEMM's column sums of b, splits in order
+        for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += gridDim.x * blockDim.x) {
+            for (int j = 0; j < 4; j++) {
+                const int col = gi * 4 + j;
+                if (col >= g.N) break;
+                float s = 0.0f;
+                for (int sp = 0; sp < g.splits; sp++) s = __fadd_rn(s, __ldcg(g.cs_part + static_cast<int64_t>(sp) * g.N + col));
+                g.cs_dst[g.cs_off + col] = __fadd_rn(g.cs_dst[g.cs_off + col], s);
             }
         }
     }
@@ -1064,11 +1098,6 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
         g.vec = v ? 1 : 0;
     }
 
-    if (e.col_sum) {
-        const st_status s = launch_col_sum(h, B, batch, k, n, e);
-        if (s != ST_OK) return s;
-    }
-
     bool use_tc = (prec == ST_PREC_TF32 || prec == ST_PREC_F16) && k >= 1;
     const int bke = ab ? 64 : BK;  // elements per 128-byte k row
     const uint32_t mnw = ab ? 64 : 32;
@@ -1133,6 +1162,18 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             g.partial = static_cast<float *>(st_scratch(h, SLOT_SPLITK, sizeof(float) * batch * splits * m * n));
             if (!g.partial) return ST_NO_MEMORY;
         }
+        // Epilogue::col_sum: inside the GEMM when it splits k over 128-wide tiles of a row-major f32 b (the
+        // first row of tiles adds up the b tiles it stages; k_splitk_reduce adds the splits in order), else
+        // by its own two launches
+        if (e.col_sum && !ab && b_mn && splits > 1 && BN == 128 && batch == 1) {
+            g.cs_part = static_cast<float *>(st_scratch(h, SLOT_COLSUM, sizeof(float) * splits * n));
+            if (!g.cs_part) return ST_NO_MEMORY;
+            g.cs_dst = e.col_sum;
+            g.cs_off = e.col_sum_off;
+        } else if (e.col_sum) {
+            const st_status cs = launch_col_sum(h, B, batch, k, n, e);
+            if (cs != ST_OK) return cs;
+        }
         // epilogue through TMA stores when there is no split-k and out is
         // TMA-describable (16-byte aligned start and rows)
         CUtensorMap mc;
@@ -1180,6 +1221,10 @@ extern "C" st_status st_gemm(st_handle *h, const st_mat *a, const st_mat *b, con
             return st_after_launch(h, "k_splitk_reduce");
         }
         return ST_OK;
+    }
+    if (e.col_sum) {
+        const st_status cs = launch_col_sum(h, B, batch, k, n, e);
+        if (cs != ST_OK) return cs;
     }
     dim3 grid(static_cast<unsigned>((n + EX_T - 1) / EX_T), static_cast<unsigned>((m + EX_T - 1) / EX_T),
               static_cast<unsigned>(batch));
