@@ -603,12 +603,26 @@ __global__ void k_splitk_reduce(const GemmArgs g) {
     }
     if (g.cs_part && z == 0 && blockIdx.y == 0) {  // the GEMM's column sums of b, splits in order
         for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += gridDim.x * blockDim.x) {
+            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int sp0 = 0; sp0 < g.splits; sp0 += 8) {  // 32 loads in flight, then the additions in split order
+                float v[8][4];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        v[u][j] = (sp0 + u < g.splits && gi * 4 + j < g.N)
+                                      ? __ldcg(g.cs_part + static_cast<int64_t>(sp0 + u) * g.N + gi * 4 + j)
+                                      : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (sp0 + u < g.splits)
+#pragma unroll
+                        for (int j = 0; j < 4; j++) s[j] = __fadd_rn(s[j], v[u][j]);
+            }
             for (int j = 0; j < 4; j++) {
                 const int col = gi * 4 + j;
                 if (col >= g.N) break;
-                float s = 0.0f;
-                for (int sp = 0; sp < g.splits; sp++) s = __fadd_rn(s, __ldcg(g.cs_part + static_cast<int64_t>(sp) * g.N + col));
-                g.cs_dst[g.cs_off + col] = __fadd_rn(g.cs_dst[g.cs_off + col], s);
+                g.cs_dst[g.cs_off + col] = __fadd_rn(g.cs_dst[g.cs_off + col], s[j]);
             }
         }
     }
