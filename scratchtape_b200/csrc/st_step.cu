@@ -395,23 +395,44 @@ __device__ __forceinline__ float powi_dev(float a, int b) {  // the host powi_f3
     return r;
 }
 
+// One Adam element in the reference's operation order (the same bits as k_adam).
+struct AdamK {
+    float b1, b2, c1, c2, i1, i2, lr, eps;
+    __device__ __forceinline__ void operator()(float &p, float g, float &m, float &v) const {
+        m = __fadd_rn(__fmul_rn(m, b1), __fmul_rn(g, c1));
+        v = __fadd_rn(__fmul_rn(v, b2), __fmul_rn(__fmul_rn(g, g), c2));
+        const float mh = __fmul_rn(m, i1), vh = __fmul_rn(v, i2);
+        const float u = __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), lr);
+        p = __fsub_rn(p, u);
+    }
+};
+
+// VEC4: every pointer 16-byte aligned and n % 4 == 0, four elements per float4.
+template <bool VEC4>
 __global__ void k_adam_dev(float *p, const float *g, float *m, float *v, int64_t n, const int32_t *step, float lr,
                            float b1, float b2, float eps) {
     dep_enter();
     const int t = step[0];
-    const float i1 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b1, t)));
-    const float i2 = __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b2, t)));
-    const float c1 = __fsub_rn(1.0f, b1), c2 = __fsub_rn(1.0f, b2);
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float gi = g[i];
-        const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, c1));
-        const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), c2));
-        m[i] = mi;
-        v[i] = vi;
-        const float mh = __fmul_rn(mi, i1), vh = __fmul_rn(vi, i2);
-        const float u = __fmul_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), lr);
-        p[i] = __fsub_rn(p[i], u);
+    const AdamK a{b1, b2, __fsub_rn(1.0f, b1), __fsub_rn(1.0f, b2), __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b1, t))),
+                  __fdiv_rn(1.0f, __fsub_rn(1.0f, powi_dev(b2, t))), lr, eps};
+    if (VEC4) {
+        for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n / 4;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            float4 pi = reinterpret_cast<float4 *>(p)[i], mi = reinterpret_cast<float4 *>(m)[i];
+            float4 vi = reinterpret_cast<float4 *>(v)[i];
+            const float4 gi = reinterpret_cast<const float4 *>(g)[i];
+            a(pi.x, gi.x, mi.x, vi.x);
+            a(pi.y, gi.y, mi.y, vi.y);
+            a(pi.z, gi.z, mi.z, vi.z);
+            a(pi.w, gi.w, mi.w, vi.w);
+            reinterpret_cast<float4 *>(m)[i] = mi;
+            reinterpret_cast<float4 *>(v)[i] = vi;
+            reinterpret_cast<float4 *>(p)[i] = pi;
+        }
+    } else {
+        for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+            a(p[i], g[i], m[i], v[i]);
     }
 }
 
@@ -548,7 +569,13 @@ extern "C" st_status st_adam_dev(st_handle *h, float *p, const float *g, float *
     ST_CHECK_CUDA(h, st_launch_dependent(h, k_step_inc, dim3(1), dim3(1), 0, step));
     st_status s = st_after_launch(h, "k_step_inc");
     if (s != ST_OK) return s;
-    ST_CHECK_CUDA(h, st_launch_dependent(h, k_adam_dev, dim3(blocks_for(n, 256)), dim3(256), 0, p, g, m, v, n, step,
-                                         lr, beta1, beta2, eps));
+    const bool vec4 = n % 4 == 0 && ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                                      reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
+    if (vec4)
+        ST_CHECK_CUDA(h, st_launch_dependent(h, k_adam_dev<true>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, p, g, m,
+                                             v, n, step, lr, beta1, beta2, eps));
+    else
+        ST_CHECK_CUDA(h, st_launch_dependent(h, k_adam_dev<false>, dim3(blocks_for(n, 256)), dim3(256), 0, p, g, m, v,
+                                             n, step, lr, beta1, beta2, eps));
     return st_after_launch(h, "k_adam_dev");
 }

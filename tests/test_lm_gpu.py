@@ -170,6 +170,25 @@ def test_adam_bit_identical_to_oracle(dev):
         assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("n", [10007, 10008])  # scalar elements; four per float4 (aligned, n % 4 == 0)
+def test_device_adam_bit_identical_to_oracle(dev, n):
+    """st_adam_dev (the step count on the device, incremented before the update) gives the oracle's Adam bits."""
+    import scratchtape_b200.device as D
+    rng = np.random.default_rng(5)
+    p, g = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+    m, v = (rng.standard_normal(n) * 0.1).astype(np.float32), np.abs(rng.standard_normal(n) * 0.01).astype(np.float32)
+    tp, tg, tm, tv = (torch.from_numpy(x.copy()).cuda() for x in (p, g, m, v))
+    step = torch.zeros(1, dtype=torch.int32, device="cuda")
+    h = D.handle()
+    for s in (1, 2, 3):
+        h.call("st_adam_dev", D.ptr(tp), D.ptr(tg), D.ptr(tm), D.ptr(tv), n, D.ptr(step), 1e-3, 0.9, 0.999, 1e-8)
+        oracle.adam(p, g, m, v, s, 1e-3)
+    torch.cuda.synchronize()
+    assert step.item() == 3
+    for got, want in ((tp, p), (tm, m), (tv, v)):
+        assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
 def test_captured_step_replays_like_eager_steps(dev):
     from scratchtape_b200.lm import LmConfig, TinyLM
     c = LmConfig(d=128, heads=2, layers=2, dff=256, t=64, batch=4)
