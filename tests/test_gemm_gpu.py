@@ -132,6 +132,8 @@ CASES_TC = [
     (1, 512, 4096, 128, True, False, False, False, False, False, False),
     (1, 4096, 512, 128, False, True, False, False, False, False, False),
     (1, 128, 4096, 512, True, False, False, False, False, False, False),
+    # split k with the column sums inside the GEMM: ragged N and K
+    (1, 256, 2000, 200, True, False, True, False, False, False, True),
     # 256-wide tiles (more than one wave of 128-wide ones, one wave of 256-wide): every layout, ragged N and K
     (1, 8192, 64, 768, False, False, True, True, False, False, False),
     (1, 8192, 64, 768, False, True, False, False, True, True, False),
